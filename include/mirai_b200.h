@@ -1,0 +1,165 @@
+/*
+ * mirai_b200.h -- C ABI of the B200 (sm_100a) sparse-MoE expert FFN path.
+ *
+ * This library replaces the routed expert FFN of seruva19/mirai: fp32 router
+ * top-k, expert-contiguous token permute, SwiGLU gate/up and down grouped GEMMs
+ * over frozen bf16 / NF4 / INT8 expert weights, the weighted un-permute
+ * (combine), and the input-gradient (dX) path through the frozen experts.
+ *
+ * Conventions shared by every entry point:
+ *   - all data pointers are CUDA device pointers, except where noted;
+ *   - every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ *     default stream) and never synchronises the host;
+ *   - nothing in this library allocates device memory: callers pass outputs
+ *     and, where needed, a workspace sized by the matching *_workspace_bytes();
+ *   - the return value is MIRAI_OK (0) or a MIRAI_ERR_* code; the message of
+ *     the last failure on the calling thread is mirai_b200_last_error();
+ *   - kernels never trap.  A device-side bound check or a bounded wait that
+ *     gives up records a code that mirai_b200_device_status() returns.
+ *
+ * Weight layouts are the reference's (w1/w3 [E, I, H], w2 [E, H, I], out x in,
+ * transformer_lingbot_video.py:1143-1145), stored as the reference's
+ * CompressedGroupedExperts buffers (experts.py:998-1031, 1382-1470).
+ */
+#ifndef MIRAI_B200_H_
+#define MIRAI_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* mirai_stream_t; /* identical to cudaStream_t */
+
+enum {
+  MIRAI_OK = 0,
+  MIRAI_ERR_INVALID_ARG = 1,    /* bad pointer, size, dtype or alignment */
+  MIRAI_ERR_UNSUPPORTED = 2,    /* shape outside what the kernels tile */
+  MIRAI_ERR_CUDA = 3,           /* a CUDA runtime / driver call failed */
+  MIRAI_ERR_DEVICE_TIMEOUT = 4, /* a device-side wait reached its time limit */
+  MIRAI_ERR_DEVICE_BOUNDS = 5,  /* a device-side index check failed */
+  MIRAI_ERR_WORKSPACE = 6       /* workspace missing or too small */
+};
+
+/* Score function and renormalisation of mirai_route_topk. */
+enum { MIRAI_SCORE_SOFTMAX = 0, MIRAI_SCORE_SIGMOID = 1 };
+enum {
+  MIRAI_NORM_NONE = 0,  /* weights = gathered scores                                   */
+  MIRAI_NORM_CLAMP = 1, /* w / clamp_min(sum w, 1e-20)       (routers.py:248)          */
+  MIRAI_NORM_EPS = 2    /* w / (sum w + 1e-20) if k > 1, then * route_scale
+                           (transformer_lingbot_video.py:1031-1033)                   */
+};
+
+/* Output element type selector. */
+enum { MIRAI_DTYPE_BF16 = 0, MIRAI_DTYPE_F32 = 1 };
+
+/* Frozen NF4 expert tensor as stored by the reference for one key
+ * (CompressedGroupedExperts._store_nf4_grouped, experts.py:998-1031;
+ * load_nf4_packed_weight, experts.py:1424-1470).  Blocks of `blocksize`
+ * consecutive elements of each expert's row-major [out, in] matrix share one
+ * scale; two codes per byte, the first element in the high nibble. */
+typedef struct mirai_nf4_weight {
+  const uint8_t* packed;      /* {key}_nf4          [E, out*in/2]                     */
+  const uint8_t* absmax;      /* {key}_nf4_absmax   [E, out*in/blocksize] 8-bit codes */
+  const float* nested_absmax; /* {key}_nf4_nabsmax  [E, n_nested] fp32                */
+  const float* offset;        /* {key}_nf4_offset   [E] fp32                          */
+  const float* code;          /* {key}_nf4_code     [16] fp32 NF4 values              */
+  const float* nested_code;   /* {key}_nf4_ncode    [256] fp32 absmax code map         */
+  int32_t blocksize;          /* 64                                                   */
+  int32_t nested_blocksize;   /* 256                                                  */
+} mirai_nf4_weight;
+
+/* Frozen INT8 expert tensor (quant.py:189-235 with group_size = 0, i.e. plain
+ * per-output-channel symmetric; load_quantized_weight, experts.py:1382-1422). */
+typedef struct mirai_int8_weight {
+  const int8_t* q;    /* {key}_int8  [E, out, in]  */
+  const float* scale; /* {key}_scale [E, out, 1]   */
+} mirai_int8_weight;
+
+/* ----------------------------------------------------------------- library */
+const char* mirai_b200_last_error(void);
+int mirai_b200_version(void);
+/* Synchronises `stream`, then returns (and clears) the device error word:
+ * *code = 0 or a MIRAI_ERR_DEVICE_* code, *info = where it was raised. */
+int mirai_b200_device_status(mirai_stream_t stream, int* code, int* info);
+
+/* ------------------------------------------------------------ a1: router top-k
+ * Replaces TokenChoiceRouter.forward's selection (routers.py:241-249) and the
+ * LingBot router's (transformer_lingbot_video.py:1002-1033) on fp32 logits
+ * [T, E] (E <= 1024, 1 <= k <= min(E, 16)).  Choice scores are
+ * `score + choice_bias` (bias may be NULL); slots come out in descending choice
+ * order, ties to the lower expert id.  Weights are fp32 [T, k]. */
+int mirai_route_topk(const float* logits, int64_t num_tokens, int32_t num_experts, int32_t top_k,
+                     int32_t score_func, const float* choice_bias, int32_t norm_mode,
+                     float route_scale, int64_t* top_indices, float* top_weights,
+                     mirai_stream_t stream);
+
+/* -------------------------------------------------------- a2: dispatch plan
+ * Replaces build_dispatch_plan (dispatch_preprocess.py:128-179): stable sort of
+ * the flat [T*k] expert ids, bincount, cumsum, inverse permutation.  Outputs:
+ * counts/starts int64 [E], offsets int32 [E] (inclusive), sort_positions,
+ * sorted_token_indices, inverse_order int64 [T*k].  Deterministic. */
+size_t mirai_dispatch_plan_workspace_bytes(int64_t num_tokens, int32_t top_k, int32_t num_experts);
+int mirai_dispatch_plan(const int64_t* top_indices, int64_t num_tokens, int32_t top_k,
+                        int32_t num_experts, int64_t* counts, int64_t* starts, int32_t* offsets,
+                        int64_t* sort_positions, int64_t* sorted_token_indices,
+                        int64_t* inverse_order, void* workspace, size_t workspace_bytes,
+                        mirai_stream_t stream);
+
+/* ------------------------------------------------------------- a3: permute
+ * routed[s, :] = tokens[sorted_token_indices[s], :] for bf16 rows, tokens
+ * [num_tokens, hidden] (permute_routed_tokens, dispatch_ops.py:8-20;
+ * experts.py:2399-2421). */
+int mirai_permute_rows_bf16(const void* tokens, int64_t num_tokens, const int64_t* sorted_token_indices,
+                            int64_t num_rows, int32_t hidden, void* routed, mirai_stream_t stream);
+
+/* --------------------------------------- a6: gate/up grouped GEMM + SwiGLU
+ * For every expert segment of the expert-contiguous rows x_sorted [S, H]
+ * (segment e = rows [offsets[e-1], offsets[e])):
+ *   h = silu(x W1[e]^T) * (x W3[e]^T)                       -> h [S, I] bf16
+ * Replaces _FrozenDequantBatchedLinearPair.forward + silu*up (linear.py:166-189,
+ * experts.py:301-317).  `gate_up` (nullable) receives the pre-activation
+ * [S, 2I] bf16 (gate | up) that the dX path consumes.  Requires H % 64 == 0,
+ * I % 128 == 0. */
+int mirai_moe_gateup_swiglu_bf16(const void* x_sorted, const int32_t* offsets, int32_t num_experts,
+                                 int64_t num_rows, int32_t hidden, int32_t inter, const void* w1,
+                                 const void* w3, void* h, void* gate_up, mirai_stream_t stream);
+int mirai_moe_gateup_swiglu_nf4(const void* x_sorted, const int32_t* offsets, int32_t num_experts,
+                                int64_t num_rows, int32_t hidden, int32_t inter,
+                                const mirai_nf4_weight* w1, const mirai_nf4_weight* w3, void* h,
+                                void* gate_up, mirai_stream_t stream);
+int mirai_moe_gateup_swiglu_int8(const void* x_sorted, const int32_t* offsets, int32_t num_experts,
+                                 int64_t num_rows, int32_t hidden, int32_t inter,
+                                 const mirai_int8_weight* w1, const mirai_int8_weight* w3, void* h,
+                                 void* gate_up, mirai_stream_t stream);
+
+/* ------------------------------------------------- a7: down grouped GEMM
+ * y[s, :] = h[s, :] W2[e]^T for the rows of segment e -> y [S, H] bf16
+ * (_FrozenDequantBatchedLinear.forward, linear.py:95-114).  Requires
+ * I % 64 == 0, H % 256 == 0. */
+int mirai_moe_down_bf16(const void* h, const int32_t* offsets, int32_t num_experts,
+                        int64_t num_rows, int32_t inter, int32_t hidden, const void* w2, void* y,
+                        mirai_stream_t stream);
+int mirai_moe_down_nf4(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                       int32_t inter, int32_t hidden, const mirai_nf4_weight* w2, void* y,
+                       mirai_stream_t stream);
+int mirai_moe_down_int8(const void* h, const int32_t* offsets, int32_t num_experts,
+                        int64_t num_rows, int32_t inter, int32_t hidden,
+                        const mirai_int8_weight* w2, void* y, mirai_stream_t stream);
+
+/* ------------------------------------------------------------- a8: combine
+ * out[t, :] = sum_j top_weights[t, j] * y[inverse_order[t*k + j], :], summed in
+ * fp32 in ascending sorted position (the order of the reference's
+ * output.index_add_, experts.py:2433-2437), then cast to out_dtype.
+ * (combine_routed_tokens, dispatch_ops.py:23-44.) */
+int mirai_moe_combine(const void* y_sorted, const int64_t* inverse_order, const float* top_weights,
+                      int64_t num_tokens, int32_t top_k, int32_t hidden, void* out,
+                      int32_t out_dtype, mirai_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MIRAI_B200_H_ */

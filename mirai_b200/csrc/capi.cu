@@ -1,0 +1,101 @@
+// Library-wide state of the C ABI: last-error strings, the device error word,
+// SM count, and the tensor-map encoder obtained from the driver.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "tmap.h"
+
+namespace mirai {
+
+static thread_local char t_last_error[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return MIRAI_OK;
+}
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_bytes, const void* base,
+                 uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                 uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encoder();
+  if (!fn) return set_error(MIRAI_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return set_error(MIRAI_ERR_INVALID_ARG, "TMA base address %p is not 16-byte aligned", base);
+  if (row_stride_bytes % 16 != 0)
+    return set_error(MIRAI_ERR_INVALID_ARG, "TMA row stride %llu is not a multiple of 16 bytes",
+                     (unsigned long long)row_stride_bytes);
+  if ((uint64_t)box_inner * elem_bytes % 16 != 0)
+    return set_error(MIRAI_ERR_INVALID_ARG, "TMA box inner extent is not a multiple of 16 bytes");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(MIRAI_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for a [%llu x %llu] tensor", (int)r,
+                     (unsigned long long)outer, (unsigned long long)inner);
+  return MIRAI_OK;
+}
+
+}  // namespace mirai
+
+extern "C" {
+
+const char* mirai_b200_last_error(void) { return mirai::t_last_error; }
+
+int mirai_b200_version(void) { return 100; }
+
+int mirai_b200_device_status(mirai_stream_t stream, int* code, int* info) {
+  if (!code || !info) return mirai::set_error(MIRAI_ERR_INVALID_ARG, "device_status: null output pointer");
+  cudaError_t e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return mirai::set_error(MIRAI_ERR_CUDA, "device_status: %s", cudaGetErrorString(e));
+  int zero = 0;
+  e = cudaMemcpyFromSymbol(code, mirai::g_device_error, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(info, mirai::g_device_error_info, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(mirai::g_device_error, &zero, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(mirai::g_device_error_info, &zero, sizeof(int));
+  if (e != cudaSuccess) return mirai::set_error(MIRAI_ERR_CUDA, "device_status: %s", cudaGetErrorString(e));
+  return MIRAI_OK;
+}
+
+}  // extern "C"

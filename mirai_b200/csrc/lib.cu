@@ -1,0 +1,5 @@
+// Single translation unit of libmirai_b200.so: the device error word in
+// capi.cu is referenced by every kernel, so all parts compile together.
+#include "capi.cu"
+#include "routing.cu"
+#include "grouped_gemm.cu"

@@ -1,0 +1,193 @@
+"""Torch-facing wrappers of the sm_100a kernels (device memory + streams only).
+
+PyTorch is used here for allocation, streams and dtypes; every computation
+below is a call into ``libmirai_b200.so``.  Inputs must be CUDA tensors; there
+is no CPU path.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+SCORE_FUNCS = {"softmax": 0, "sigmoid": 1}
+NORM_MODES = {"none": 0, "clamp": 1, "eps": 2}
+
+
+def _ptr(t: torch.Tensor | None) -> _lib.c_vp:
+    return _lib.c_vp(0 if t is None else t.data_ptr())
+
+
+def _stream() -> _lib.c_vp:
+    return _lib.c_vp(torch.cuda.current_stream().cuda_stream)
+
+
+def _cuda(t: torch.Tensor, name: str, dtype: torch.dtype | None = None) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the B200 path has no CPU fallback)")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    return t.contiguous()
+
+
+def device_status() -> tuple[int, int]:
+    """Synchronise the current stream and return (and clear) the device error word."""
+    return _lib.device_status(torch.cuda.current_stream().cuda_stream)
+
+
+def check_device() -> None:
+    code, info = device_status()
+    if code:
+        raise _lib.MiraiError(code, f"raised on the device at site {info}")
+
+
+# ----------------------------------------------------------------------------- a1
+
+def route_topk(logits: torch.Tensor, top_k: int, *, score_func: str = "softmax",
+               choice_bias: torch.Tensor | None = None, norm: str = "clamp",
+               route_scale: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 top-k routing (routers.py:241-249; transformer_lingbot_video.py:1002-1033).
+
+    Returns (top_indices int64 [T, k], top_weights fp32 [T, k]); slots are in
+    descending choice order, ties to the lower expert id.
+    """
+    logits = _cuda(logits, "logits", torch.float32)
+    T, E = logits.shape
+    bias = None if choice_bias is None else _cuda(choice_bias, "choice_bias", torch.float32)
+    idx = torch.empty((T, top_k), dtype=torch.int64, device=logits.device)
+    w = torch.empty((T, top_k), dtype=torch.float32, device=logits.device)
+    _lib.call("mirai_route_topk", _ptr(logits), T, E, top_k, SCORE_FUNCS[score_func], _ptr(bias),
+              NORM_MODES[norm], float(route_scale), _ptr(idx), _ptr(w), _stream())
+    return idx, w
+
+
+# ----------------------------------------------------------------------------- a2
+
+@dataclass(frozen=True)
+class DispatchPlan:
+    """Device-resident routing layout (dispatch_preprocess.py:22-40)."""
+
+    counts: torch.Tensor                # [E] int64
+    starts: torch.Tensor                # [E] int64
+    offsets: torch.Tensor               # [E] int32 inclusive cumsum
+    sort_positions: torch.Tensor        # [S] int64
+    sorted_token_indices: torch.Tensor  # [S] int64
+    inverse_order: torch.Tensor         # [S] int64
+    total_slots: int
+    top_k: int
+
+
+def dispatch_plan(top_indices: torch.Tensor, num_experts: int,
+                  workspace: torch.Tensor | None = None) -> DispatchPlan:
+    top_indices = _cuda(top_indices, "top_indices", torch.int64)
+    T, k = top_indices.shape
+    S = T * k
+    dev = top_indices.device
+    counts = torch.empty(num_experts, dtype=torch.int64, device=dev)
+    starts = torch.empty(num_experts, dtype=torch.int64, device=dev)
+    offsets = torch.empty(num_experts, dtype=torch.int32, device=dev)
+    sp = torch.empty(S, dtype=torch.int64, device=dev)
+    st = torch.empty(S, dtype=torch.int64, device=dev)
+    inv = torch.empty(S, dtype=torch.int64, device=dev)
+    need = plan_workspace_bytes(T, k, num_experts)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    _lib.call("mirai_dispatch_plan", _ptr(top_indices), T, k, num_experts, _ptr(counts), _ptr(starts),
+              _ptr(offsets), _ptr(sp), _ptr(st), _ptr(inv), _ptr(workspace),
+              workspace.numel() * workspace.element_size(), _stream())
+    return DispatchPlan(counts, starts, offsets, sp, st, inv, S, k)
+
+
+def plan_workspace_bytes(num_tokens: int, top_k: int, num_experts: int) -> int:
+    return int(_lib.load().mirai_dispatch_plan_workspace_bytes(num_tokens, top_k, num_experts))
+
+
+# ----------------------------------------------------------------------------- a3
+
+def permute_rows(tokens: torch.Tensor, sorted_token_indices: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    tokens = _cuda(tokens, "tokens", torch.bfloat16)
+    idx = _cuda(sorted_token_indices, "sorted_token_indices", torch.int64)
+    S = idx.numel()
+    H = tokens.shape[1]
+    if out is None:
+        out = torch.empty((S, H), dtype=torch.bfloat16, device=tokens.device)
+    _lib.call("mirai_permute_rows_bf16", _ptr(tokens), tokens.shape[0], _ptr(idx), S, H, _ptr(out), _stream())
+    return out
+
+
+# ----------------------------------------------------------------------------- a6 / a7
+
+def gateup_swiglu(x_sorted: torch.Tensor, offsets: torch.Tensor, w1, w3, *, inter: int,
+                  save_gate_up: bool = False, out: torch.Tensor | None = None):
+    """h = silu(x W1^T) * (x W3^T) per expert segment.  ``w1``/``w3`` are bf16
+    tensors [E, I, H], or ``Nf4Weight`` / ``Int8Weight`` descriptors."""
+    x_sorted = _cuda(x_sorted, "x_sorted", torch.bfloat16)
+    offsets = _cuda(offsets, "offsets", torch.int32)
+    S, H = x_sorted.shape
+    E = offsets.numel()
+    h = out if out is not None else torch.empty((S, inter), dtype=torch.bfloat16, device=x_sorted.device)
+    gu = torch.empty((S, 2 * inter), dtype=torch.bfloat16, device=x_sorted.device) if save_gate_up else None
+    if isinstance(w1, torch.Tensor):
+        w1 = _cuda(w1, "w1", torch.bfloat16)
+        w3 = _cuda(w3, "w3", torch.bfloat16)
+        _lib.call("mirai_moe_gateup_swiglu_bf16", _ptr(x_sorted), _ptr(offsets), E, S, H, inter, _ptr(w1),
+                  _ptr(w3), _ptr(h), _ptr(gu), _stream())
+    elif isinstance(w1, _lib.Nf4Weight):
+        _lib.call("mirai_moe_gateup_swiglu_nf4", _ptr(x_sorted), _ptr(offsets), E, S, H, inter, w1, w3, _ptr(h),
+                  _ptr(gu), _stream())
+    elif isinstance(w1, _lib.Int8Weight):
+        _lib.call("mirai_moe_gateup_swiglu_int8", _ptr(x_sorted), _ptr(offsets), E, S, H, inter, w1, w3, _ptr(h),
+                  _ptr(gu), _stream())
+    else:
+        raise TypeError(f"unsupported weight type {type(w1)}")
+    return (h, gu) if save_gate_up else h
+
+
+def down(h: torch.Tensor, offsets: torch.Tensor, w2, *, hidden: int, out: torch.Tensor | None = None):
+    h = _cuda(h, "h", torch.bfloat16)
+    offsets = _cuda(offsets, "offsets", torch.int32)
+    S, I = h.shape
+    E = offsets.numel()
+    y = out if out is not None else torch.empty((S, hidden), dtype=torch.bfloat16, device=h.device)
+    if isinstance(w2, torch.Tensor):
+        w2 = _cuda(w2, "w2", torch.bfloat16)
+        _lib.call("mirai_moe_down_bf16", _ptr(h), _ptr(offsets), E, S, I, hidden, _ptr(w2), _ptr(y), _stream())
+    elif isinstance(w2, _lib.Nf4Weight):
+        _lib.call("mirai_moe_down_nf4", _ptr(h), _ptr(offsets), E, S, I, hidden, w2, _ptr(y), _stream())
+    elif isinstance(w2, _lib.Int8Weight):
+        _lib.call("mirai_moe_down_int8", _ptr(h), _ptr(offsets), E, S, I, hidden, w2, _ptr(y), _stream())
+    else:
+        raise TypeError(f"unsupported weight type {type(w2)}")
+    return y
+
+
+# ----------------------------------------------------------------------------- a8
+
+def combine(y_sorted: torch.Tensor, inverse_order: torch.Tensor, top_weights: torch.Tensor,
+            out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+    y_sorted = _cuda(y_sorted, "y_sorted", torch.bfloat16)
+    inv = _cuda(inverse_order, "inverse_order", torch.int64)
+    w = _cuda(top_weights.float(), "top_weights", torch.float32)
+    T, k = w.shape
+    H = y_sorted.shape[1]
+    if out is None:
+        out = torch.empty((T, H), dtype=out_dtype, device=y_sorted.device)
+    code = {torch.bfloat16: 0, torch.float32: 1}[out.dtype]
+    _lib.call("mirai_moe_combine", _ptr(y_sorted), _ptr(inv), _ptr(w), T, k, H, _ptr(out), code, _stream())
+    return out
+
+
+# ----------------------------------------------------------------------------- whole forward
+
+def moe_forward(tokens: torch.Tensor, top_indices: torch.Tensor, top_weights: torch.Tensor, w1, w3, w2, *,
+                num_experts: int, inter: int) -> torch.Tensor:
+    """Routed expert FFN forward: plan, permute, gate/up+SwiGLU, down, combine."""
+    plan = dispatch_plan(top_indices, num_experts)
+    xs = permute_rows(tokens, plan.sorted_token_indices)
+    h = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter)
+    y = down(h, plan.offsets, w2, hidden=tokens.shape[1])
+    return combine(y, plan.inverse_order, top_weights, out_dtype=tokens.dtype)

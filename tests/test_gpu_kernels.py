@@ -1,0 +1,210 @@
+"""Parity of the sm_100a kernels (called through the C ABI) against the CPU oracle.
+
+Integer outputs (routing index sets, dispatch plan, permutation) must be
+bit-exact; floating outputs are held to the north-star tolerance
+max|a - r| / max|r| <= 2e-2 (3e-2 for dX), computed against the oracle's
+restatement of the reference's dequantise-then-matmul path.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe as om
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+
+
+def _dev():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from mirai_b200.build import build
+    build()
+    return torch.device("cuda:0")
+
+
+def _bf16(t_np):
+    return torch.from_numpy(np.ascontiguousarray(t_np)).to(torch.bfloat16)
+
+
+def _f32(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _check(ops):
+    ops.check_device()
+
+
+# ----------------------------------------------------------------------------- a1
+
+@pytest.mark.parametrize("E,k", [(8, 2), (32, 2), (64, 4), (128, 8), (200, 3), (1000, 16)])
+@pytest.mark.parametrize("mode", ["softmax", "sigmoid_bias"])
+def test_route_topk_matches_oracle(E, k, mode):
+    dev = _dev()
+    from mirai_b200 import ops
+    rng = np.random.default_rng(E * 7 + k)
+    T = 777
+    logits = (rng.standard_normal((T, E)) * 1.3).astype(np.float32)
+    logits[5, :] = 0.25  # all-equal row: ties resolve to the lowest expert ids
+    if mode == "softmax":
+        kw = dict(score_func="softmax", norm="clamp")
+        okw = dict(score_func="softmax", norm="clamp")
+    else:
+        bias = (rng.standard_normal(E) * 0.1).astype(np.float32)
+        kw = dict(score_func="sigmoid", choice_bias=torch.from_numpy(bias).to(dev), norm="eps", route_scale=2.5)
+        okw = dict(score_func="sigmoid", bias=bias, norm="eps", route_scale=2.5)
+    idx, w = ops.route_topk(torch.from_numpy(logits).to(dev), k, **kw)
+    _check(ops)
+    ridx, rw = om.route_topk(logits, k, **okw)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ridx)  # same canonical slot order
+    np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("name", ["router_e8_k2", "router_e64_k4", "router_e128_k8"])
+def test_route_topk_matches_reference_golden(golden, name):
+    dev = _dev()
+    from mirai_b200 import ops
+    g = golden(name)
+    idx, w = ops.route_topk(torch.from_numpy(g["logits"]).to(dev), int(g["k"]))
+    ci, cw = om.canonical_slots(idx.cpu().numpy(), w.cpu().numpy())
+    ri, rw = om.canonical_slots(g["top_indices"], g["top_weights"])
+    np.testing.assert_array_equal(ci, ri)
+    np.testing.assert_allclose(cw, rw, rtol=1e-5, atol=1e-7)
+
+
+# ----------------------------------------------------------------------------- a2
+
+def _plan_cases():
+    rng = np.random.default_rng(3)
+    yield "uniform", rng.integers(0, 32, (5000, 2)), 32
+    yield "dups_and_empty", rng.integers(0, 4, (3001, 4)) * 3, 16
+    yield "single_expert", np.zeros((2049, 1), np.int64), 1
+    zipf = np.minimum(rng.zipf(1.2, (9000, 4)) - 1, 63)
+    yield "zipf", zipf, 64
+    yield "e1000", rng.integers(0, 1000, (4000, 8)), 1000
+    yield "tiny", np.array([[1, 0]]), 3
+
+
+@pytest.mark.parametrize("case", list(_plan_cases()), ids=lambda c: c[0])
+def test_dispatch_plan_bit_exact(case):
+    dev = _dev()
+    from mirai_b200 import ops
+    _, idx, E = case
+    idx = np.ascontiguousarray(idx, dtype=np.int64)
+    plan = ops.dispatch_plan(torch.from_numpy(idx).to(dev), E)
+    _check(ops)
+    ref = om.dispatch_plan(idx, E)
+    for f in ("counts", "starts", "offsets", "sort_positions", "sorted_token_indices", "inverse_order"):
+        np.testing.assert_array_equal(getattr(plan, f).cpu().numpy(), ref[f], err_msg=f)
+
+
+@pytest.mark.parametrize("name", ["plan_uniform", "plan_dups_empty", "plan_single", "plan_skew"])
+def test_dispatch_plan_matches_reference_golden(golden, name):
+    dev = _dev()
+    from mirai_b200 import ops
+    g = golden(name)
+    plan = ops.dispatch_plan(torch.from_numpy(g["top_indices"]).to(dev), int(g["num_experts"]))
+    for f in ("counts", "starts", "offsets", "sort_positions", "sorted_token_indices", "inverse_order"):
+        np.testing.assert_array_equal(getattr(plan, f).cpu().numpy(), g[f], err_msg=f)
+
+
+def test_dispatch_plan_rejects_bad_expert_ids_on_device():
+    dev = _dev()
+    from mirai_b200 import ops
+    idx = torch.tensor([[0, 1], [2, 7]], device=dev)  # 7 >= E
+    ops.dispatch_plan(idx, 4)
+    code, info = ops.device_status()
+    assert code == 5 and info == 100
+
+
+# ----------------------------------------------------------------------------- a3 / a8
+
+def test_permute_and_combine_exact():
+    dev = _dev()
+    from mirai_b200 import ops
+    rng = np.random.default_rng(5)
+    T, H, E, k = 301, 264, 16, 4
+    x = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    idx = rng.integers(0, E, (T, k))
+    plan = ops.dispatch_plan(torch.from_numpy(idx).to(dev), E)
+    xs = ops.permute_rows(_bf16(x).to(dev), plan.sorted_token_indices)
+    ref_plan = om.dispatch_plan(idx, E)
+    np.testing.assert_array_equal(_f32(xs), om.permute(x, ref_plan["sorted_token_indices"]))
+    y = oq.bf16_round(rng.standard_normal((T * k, H)).astype(np.float32))
+    w = rng.random((T, k)).astype(np.float32)
+    out = ops.combine(_bf16(y).to(dev), plan.inverse_order, torch.from_numpy(w).to(dev), out_dtype=torch.float32)
+    _check(ops)
+    ref = om.combine(y, w, ref_plan, T)
+    np.testing.assert_array_equal(_f32(out), ref)  # same fp32 order of additions
+    outb = ops.combine(_bf16(y).to(dev), plan.inverse_order, torch.from_numpy(w).to(dev))
+    np.testing.assert_array_equal(_f32(outb), oq.bf16_round(ref))
+
+
+# ----------------------------------------------------------------------------- a6 / a7 bf16
+
+def _segments(rng, E, total, skew=False):
+    if skew:
+        p = 1.0 / np.arange(1, E + 1) ** 1.2
+        p /= p.sum()
+        counts = rng.multinomial(total, p)
+    else:
+        counts = rng.multinomial(total, np.ones(E) / E)
+    counts[1 % E] = 0  # an empty expert
+    return counts
+
+
+@pytest.mark.parametrize("E,H,I,S,skew", [(4, 256, 256, 700, False), (8, 512, 384, 3000, True),
+                                          (3, 128, 128, 130, False), (16, 256, 512, 5000, True)])
+def test_gateup_and_down_bf16_match_oracle(E, H, I, S, skew):
+    dev = _dev()
+    from mirai_b200 import ops
+    rng = np.random.default_rng(S)
+    counts = _segments(rng, E, S, skew)
+    S = int(counts.sum())
+    offsets = np.cumsum(counts).astype(np.int32)
+    x = oq.bf16_round(rng.standard_normal((S, H)).astype(np.float32))
+    w1 = oq.bf16_round((rng.standard_normal((E, I, H)) * 0.05).astype(np.float32))
+    w3 = oq.bf16_round((rng.standard_normal((E, I, H)) * 0.05).astype(np.float32))
+    w2 = oq.bf16_round((rng.standard_normal((E, H, I)) * 0.05).astype(np.float32))
+    off = torch.from_numpy(offsets).to(dev)
+    h, gu = ops.gateup_swiglu(_bf16(x).to(dev), off, _bf16(w1).to(dev), _bf16(w3).to(dev), inter=I,
+                              save_gate_up=True)
+    y = ops.down(h, off, _bf16(w2).to(dev), hidden=H)
+    _check(ops)
+    ry, inter = om.expert_ffn_forward(x, offsets, w1, w3, w2, bf16=True, keep=True)
+    assert om.rel_max_err(_f32(gu[:, :I]), inter["gate"]) < TOL
+    assert om.rel_max_err(_f32(gu[:, I:]), inter["up"]) < TOL
+    assert om.rel_max_err(_f32(h), inter["h"]) < TOL
+    # the down GEMM checked on its own input
+    ry2 = om.expert_ffn_forward(x, offsets, w1, w3, w2, bf16=True)
+    assert om.rel_max_err(_f32(y), ry2) < TOL
+    hy = _f32(h)
+    ref_down = np.zeros((S, H), np.float32)
+    start = 0
+    for e in range(E):
+        end = offsets[e]
+        ref_down[start:end] = hy[start:end] @ w2[e].T
+        start = end
+    assert om.rel_max_err(_f32(y), ref_down) < 1e-2
+
+
+def test_moe_forward_bf16_end_to_end():
+    dev = _dev()
+    from mirai_b200 import ops
+    rng = np.random.default_rng(11)
+    T, H, E, k, I = 1024, 256, 8, 2, 512
+    x = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    logits = (x @ (rng.standard_normal((E, H)) * 0.02).T).astype(np.float32)
+    w1 = oq.bf16_round((rng.standard_normal((E, I, H)) * 0.02).astype(np.float32))
+    w3 = oq.bf16_round((rng.standard_normal((E, I, H)) * 0.02).astype(np.float32))
+    w2 = oq.bf16_round((rng.standard_normal((E, H, I)) * 0.02).astype(np.float32))
+    idx, w = ops.route_topk(torch.from_numpy(logits).to(dev), k)
+    out = ops.moe_forward(_bf16(x).to(dev), idx, w, _bf16(w1).to(dev), _bf16(w3).to(dev), _bf16(w2).to(dev),
+                          num_experts=E, inter=I)
+    _check(ops)
+    ridx, rw = om.route_topk(logits, k)
+    ref = om.moe_forward(x, ridx, rw, w1, w3, w2, bf16=True)
+    assert om.rel_max_err(_f32(out), ref) < TOL
