@@ -119,12 +119,61 @@ def permute_rows(tokens: torch.Tensor, sorted_token_indices: torch.Tensor,
     return out
 
 
+# ----------------------------------------------------------------------------- weight descriptors
+
+class NF4Tensor:
+    """Device buffers of one NF4 grouped-expert key, in the reference's layout
+    (experts.py:998-1031): ``packed`` uint8 [E, out*in/2(, 1)], ``absmax`` uint8
+    [E, out*in/64], ``nested_absmax`` fp32 [E, n], ``offset`` fp32 [E],
+    ``code`` fp32 [16], ``nested_code`` fp32 [256]."""
+
+    def __init__(self, packed, absmax, nested_absmax, offset, code, nested_code, shape,
+                 blocksize: int = 64, nested_blocksize: int = 256):
+        self.packed = _cuda(packed, "packed", torch.uint8)
+        self.absmax = _cuda(absmax, "absmax", torch.uint8)
+        self.nested_absmax = _cuda(nested_absmax, "nested_absmax", torch.float32)
+        self.offset = _cuda(offset.reshape(-1), "offset", torch.float32)
+        self.code = _cuda(code, "code", torch.float32)
+        self.nested_code = _cuda(nested_code, "nested_code", torch.float32)
+        self.shape = tuple(int(s) for s in shape)
+        self.blocksize = int(blocksize)
+        self.nested_blocksize = int(nested_blocksize)
+        self._struct = _lib.Nf4Weight(self.packed.data_ptr(), self.absmax.data_ptr(),
+                                      self.nested_absmax.data_ptr(), self.offset.data_ptr(),
+                                      self.code.data_ptr(), self.nested_code.data_ptr(),
+                                      self.blocksize, self.nested_blocksize)
+
+    def struct(self) -> _lib.Nf4Weight:
+        return self._struct
+
+
+class Int8Tensor:
+    """Device buffers of one INT8 grouped-expert key (group_size 0): ``q`` int8
+    [E, out, in] and ``scale`` fp32 [E, out, 1] (experts.py:1382-1422)."""
+
+    def __init__(self, q, scale):
+        self.q = _cuda(q, "int8 weight", torch.int8)
+        self.scale = _cuda(scale, "int8 scale", torch.float32)
+        self.shape = tuple(int(s) for s in self.q.shape)
+        self._struct = _lib.Int8Weight(self.q.data_ptr(), self.scale.data_ptr())
+
+    def struct(self) -> _lib.Int8Weight:
+        return self._struct
+
+
+def _as_weight(w):
+    if isinstance(w, (NF4Tensor, Int8Tensor)):
+        return w.struct()
+    return w
+
+
 # ----------------------------------------------------------------------------- a6 / a7
 
 def gateup_swiglu(x_sorted: torch.Tensor, offsets: torch.Tensor, w1, w3, *, inter: int,
                   save_gate_up: bool = False, out: torch.Tensor | None = None):
     """h = silu(x W1^T) * (x W3^T) per expert segment.  ``w1``/``w3`` are bf16
     tensors [E, I, H], or ``Nf4Weight`` / ``Int8Weight`` descriptors."""
+    w1, w3 = _as_weight(w1), _as_weight(w3)
     x_sorted = _cuda(x_sorted, "x_sorted", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
     S, H = x_sorted.shape
@@ -148,6 +197,7 @@ def gateup_swiglu(x_sorted: torch.Tensor, offsets: torch.Tensor, w1, w3, *, inte
 
 
 def down(h: torch.Tensor, offsets: torch.Tensor, w2, *, hidden: int, out: torch.Tensor | None = None):
+    w2 = _as_weight(w2)
     h = _cuda(h, "h", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
     S, I = h.shape

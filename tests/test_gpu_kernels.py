@@ -152,12 +152,14 @@ def _segments(rng, E, total, skew=False):
         counts = rng.multinomial(total, p)
     else:
         counts = rng.multinomial(total, np.ones(E) / E)
-    counts[1 % E] = 0  # an empty expert
+    if E > 1:
+        counts[1] = 0  # an empty expert
     return counts
 
 
 @pytest.mark.parametrize("E,H,I,S,skew", [(4, 256, 256, 700, False), (8, 512, 384, 3000, True),
-                                          (3, 128, 128, 130, False), (16, 256, 512, 5000, True)])
+                                          (3, 256, 128, 130, False), (16, 256, 512, 5000, True),
+                                          (1, 768, 128, 64, False)])
 def test_gateup_and_down_bf16_match_oracle(E, H, I, S, skew):
     dev = _dev()
     from mirai_b200 import ops
@@ -207,4 +209,76 @@ def test_moe_forward_bf16_end_to_end():
     _check(ops)
     ridx, rw = om.route_topk(logits, k)
     ref = om.moe_forward(x, ridx, rw, w1, w3, w2, bf16=True)
+    assert om.rel_max_err(_f32(out), ref) < TOL
+
+
+# ----------------------------------------------------------------------------- a4 / a5: fused NF4 / INT8 dequant
+
+def nf4_to_device(g, dev):
+    from mirai_b200 import ops
+    return ops.NF4Tensor(torch.from_numpy(g["nf4"]).to(dev), torch.from_numpy(g["absmax"]).to(dev),
+                         torch.from_numpy(g["nabsmax"]).to(dev), torch.from_numpy(g["offset"]).to(dev),
+                         torch.from_numpy(g["code"]).to(dev), torch.from_numpy(g["ncode"]).to(dev), g["shape"])
+
+
+def int8_to_device(q, s, dev):
+    from mirai_b200 import ops
+    return ops.Int8Tensor(torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev))
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "int8"])
+@pytest.mark.parametrize("E,H,I,S,skew", [(4, 256, 256, 700, False), (8, 512, 384, 3000, True),
+                                          (2, 1024, 1408, 400, False), (3, 3072, 1024, 500, True)])
+def test_quantized_gemms_match_dequant_then_matmul(fmt, E, H, I, S, skew):
+    dev = _dev()
+    from mirai_b200 import ops
+    rng = np.random.default_rng(S + len(fmt))
+    counts = _segments(rng, E, S, skew)
+    S = int(counts.sum())
+    offsets = np.cumsum(counts).astype(np.int32)
+    x = oq.bf16_round(rng.standard_normal((S, H)).astype(np.float32))
+    raw = [(rng.standard_normal(shape) * 0.05).astype(np.float32) for shape in ((E, I, H), (E, I, H), (E, H, I))]
+    if fmt == "nf4":
+        gs = [oq.nf4_quantize_grouped(w) for w in raw]
+        dense = [oq.nf4_dequantize_grouped(g) for g in gs]
+        dw = [nf4_to_device(g, dev) for g in gs]
+    else:
+        qs = [oq.int8_quantize(w, 0) for w in raw]
+        dense = [oq.bf16_round(oq.int8_dequantize(q, s, 0)) for q, s, _ in qs]
+        dw = [int8_to_device(q, s, dev) for q, s, _ in qs]
+    off = torch.from_numpy(offsets).to(dev)
+    h, gu = ops.gateup_swiglu(_bf16(x).to(dev), off, dw[0], dw[1], inter=I, save_gate_up=True)
+    y = ops.down(h, off, dw[2], hidden=H)
+    _check(ops)
+    _, inter = om.expert_ffn_forward(x, offsets, dense[0], dense[1], dense[2], bf16=True, keep=True)
+    assert om.rel_max_err(_f32(gu[:, :I]), inter["gate"]) < 1e-2
+    assert om.rel_max_err(_f32(gu[:, I:]), inter["up"]) < 1e-2
+    assert om.rel_max_err(_f32(h), inter["h"]) < TOL
+    hy = _f32(h)
+    ref_down = np.zeros((S, H), np.float32)
+    start = 0
+    for e in range(E):
+        end = offsets[e]
+        ref_down[start:end] = hy[start:end] @ dense[2][e].T
+        start = end
+    assert om.rel_max_err(_f32(y), ref_down) < 1e-2
+
+
+def test_nf4_moe_forward_end_to_end_config0_shape():
+    """Config-0 shape (T=512, H=256, E=8, k=2, I=512) with NF4 experts."""
+    dev = _dev()
+    from mirai_b200 import ops
+    rng = np.random.default_rng(0)
+    T, H, E, k, I = 512, 256, 8, 2, 512
+    x = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    logits = (x @ (rng.standard_normal((E, H)) * 0.02).T).astype(np.float32)
+    raw = [(rng.standard_normal(shape) * 0.02).astype(np.float32) for shape in ((E, I, H), (E, I, H), (E, H, I))]
+    gs = [oq.nf4_quantize_grouped(w) for w in raw]
+    dense = [oq.nf4_dequantize_grouped(g) for g in gs]
+    dw = [nf4_to_device(g, dev) for g in gs]
+    idx, w = ops.route_topk(torch.from_numpy(logits).to(dev), k)
+    out = ops.moe_forward(_bf16(x).to(dev), idx, w, dw[0], dw[1], dw[2], num_experts=E, inter=I)
+    _check(ops)
+    ridx, rw = om.route_topk(logits, k)
+    ref = om.moe_forward(x, ridx, rw, dense[0], dense[1], dense[2], bf16=True)
     assert om.rel_max_err(_f32(out), ref) < TOL
