@@ -1,0 +1,465 @@
+#!/usr/bin/env python
+"""MoE-FFN tokens/s (NF4 experts) on B200 -- the routed expert FFN of the
+seruva19/mirai denoiser, run through libmirai_b200.so.
+
+Default workload (BASELINE config 2 shape): 32768 tokens, hidden 2048,
+32 experts, top-2, SwiGLU intermediate 1408, NF4 blocksize-64 experts with
+double-quantised absmax.  One step = one pass of the path over the batch:
+fp32 router top-k on precomputed gate logits -> dispatch plan -> permute ->
+gate/up grouped GEMM + SwiGLU (fused NF4 dequant) -> down grouped GEMM (fused
+NF4 dequant) -> weighted combine.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank runs its own replica on its own tokens
+(experts replicated, no data-path collective): scaling "weak".
+``--impl reference`` times the CPU restatement of the reference's torch path
+(``oracle/``) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "c0": dict(T=512, H=256, E=8, k=2, I=512, fmt="nf4", zipf=None),
+    "c1": dict(T=32768, H=2048, E=32, k=2, I=1408, fmt="bf16", zipf=None),
+    "c2": dict(T=32768, H=2048, E=32, k=2, I=1408, fmt="nf4", zipf=None),
+    "c3": dict(T=8192, H=3072, E=64, k=4, I=1024, fmt="int8", zipf=1.2),
+}
+METRIC = "MoE-FFN tokens/s (NF4 experts) + % TC/HBM roofline at 1/2/4/8 B200"
+# Our kernels launched by one step: route 1, plan 4, permute 1, gate/up 1, down 1, combine 1.
+KERNELS_PER_STEP = 9
+# DRAM bytes (read + write) of one gate/up launch from an ncu capture, per
+# workload; see profiles/ for the capture and its command.  None until captured.
+NCU_TRAFFIC = {}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """Polls NVML (read-only) for SM clock and clock-event reasons."""
+
+    def __init__(self, index: int, period_s: float = 0.005):
+        self.index, self.period = index, period_s
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.ok = False
+
+    def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            names = {
+                "hw_slowdown": getattr(pynvml, "nvmlClocksEventReasonHwSlowdown", 0x8),
+                "hw_thermal_slowdown": getattr(pynvml, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+                "sw_thermal_slowdown": getattr(pynvml, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+                "sw_power_cap": getattr(pynvml, "nvmlClocksEventReasonSwPowerCap", 0x4),
+                "hw_power_brake_slowdown": getattr(pynvml, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+            }
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        except Exception as exc:  # NVML missing: report that, keep the run
+            self.error = str(exc)
+            return self
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    r = get_reasons(h)
+                    for n, bit in names.items():
+                        if r & bit:
+                            self.reasons.add(n)
+                except Exception:
+                    pass
+                time.sleep(self.period)
+
+        self.ok = True
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
+        return self
+
+    def stop(self):
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=1)
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": getattr(self, "error", "nvml")}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------- workload
+
+def make_workload(cfg, dev, seed):
+    import torch
+    from mirai_b200 import ops, tables
+
+    T, H, E, k, I = cfg["T"], cfg["H"], cfg["E"], cfg["k"], cfg["I"]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    gate = torch.randn(E, H, generator=g, device=dev) * 0.02
+    logits = x.float() @ gate.T
+    if cfg["zipf"]:
+        # Zipf(s) load over a seeded expert permutation: bias_e = c * log p_e,
+        # c chosen so the top expert gets about a quarter of the routes.
+        perm = torch.randperm(E, generator=torch.Generator().manual_seed(seed))
+        p = 1.0 / torch.arange(1, E + 1, dtype=torch.float64) ** cfg["zipf"]
+        p = (p / p.sum())[perm.argsort()].to(torch.float32).to(dev)
+        logits = logits + 2.0 * torch.log(p)[None, :]
+    ws = []
+    for shape in ((E, I, H), (E, I, H), (E, H, I)):
+        w = (torch.randn(shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        if cfg["fmt"] == "nf4":
+            w = ops.nf4_quantize(w, tables.nf4_code(dev), tables.dynamic_map(dev))
+        elif cfg["fmt"] == "int8":
+            w = ops.int8_quantize(w.float())
+        ws.append(w)
+    torch.cuda.synchronize()
+    return x, logits, ws
+
+
+def weight_bytes(cfg):
+    E, H, I = cfg["E"], cfg["H"], cfg["I"]
+    n = 3 * E * H * I
+    if cfg["fmt"] == "nf4":
+        return n // 2 + n // 64 + 4 * (n // 64 // 256 + E)
+    if cfg["fmt"] == "int8":
+        return n + 4 * E * (2 * I + H)
+    return 2 * n
+
+
+# ----------------------------------------------------------------------------- our arm
+
+def run_ours(args, cfg, rank, world, dev):
+    import torch
+    import torch.distributed as dist
+    from mirai_b200 import ops
+
+    T, H, E, k, I = cfg["T"], cfg["H"], cfg["E"], cfg["k"], cfg["I"]
+    x, logits, (w1, w3, w2) = make_workload(cfg, dev, seed=1234 + rank)
+    S = T * k
+
+    def step(xin, lin, out=None):
+        idx, tw = ops.route_topk(lin, k)
+        plan = ops.dispatch_plan(idx, E)
+        xs = ops.permute_rows(xin, plan.sorted_token_indices)
+        h = ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I)
+        y = ops.down(h, plan.offsets, w2, hidden=H)
+        return ops.combine(y, plan.inverse_order, tw, out=out)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-resident throughput (value)
+    for _ in range(args.warmup):
+        step(x, logits)
+    ops.check_device()
+    clocks = ClockSampler(torch.cuda.current_device()).start()
+    barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step(x, logits)
+    t1.record()
+    t1.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    ops.check_device()
+
+    # ---- dominant kernel alone: gate/up grouped GEMM (CUDA events on its stream)
+    idx, tw = ops.route_topk(logits, k)
+    plan = ops.dispatch_plan(idx, E)
+    xs = ops.permute_rows(x, plan.sorted_token_indices)
+    h = torch.empty((S, I), dtype=torch.bfloat16, device=dev)
+    y = torch.empty((S, H), dtype=torch.bfloat16, device=dev)
+    reps = max(5, min(50, args.steps))
+    for _ in range(3):
+        ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I, out=h)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in evs:
+        a.record()
+        ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I, out=h)
+        b.record()
+    torch.cuda.synchronize()
+    gu_ms = sum(a.elapsed_time(b) for a, b in evs) / reps
+    for a, b in evs:
+        a.record()
+        ops.down(h, plan.offsets, w2, hidden=H, out=y)
+        b.record()
+    torch.cuda.synchronize()
+    down_ms = sum(a.elapsed_time(b) for a, b in evs) / reps
+
+    # ---- end to end through the public API with host buffers
+    x_host = x.cpu().pin_memory()
+    l_host = logits.cpu().pin_memory()
+    o_host = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+    l_dev = torch.empty_like(logits)
+    o_dev = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        l_dev.copy_(l_host, non_blocking=True)
+        step(x_dev, l_dev, out=o_dev)
+        o_host.copy_(o_dev, non_blocking=True)
+
+    for _ in range(max(1, min(3, args.warmup))):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    e1.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    ops.check_device()
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+
+    peaks = load_peaks()
+    flops_gu = 4.0 * S * H * I
+    achieved = flops_gu / (gu_ms * 1e-3) / 1e12
+    traffic = NCU_TRAFFIC.get(f"{args.config}-gateup")
+    line = {
+        "metric": METRIC,
+        "value": world * T / (ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 activations x " + cfg["fmt"] + " weights, fp32 accumulate",
+        "data": "synthetic (seeded torch.randn; random-init experts quantised on the GPU)",
+        "config": {
+            "workload": f"{args.config}: one routed expert FFN layer forward, T={T} H={H} E={E} k={k} I={I} "
+                        f"{cfg['fmt']} experts" + (f", Zipf({cfg['zipf']}) load" if cfg["zipf"] else ""),
+            "tokens_per_gpu": T, "hidden": H, "experts": E, "top_k": k, "intermediate": I,
+            "weights": cfg["fmt"], "parallelism": f"dp{world} token-parallel replicas (experts replicated)",
+            "l2": f"no flush: inputs {(T * H * 2 + weight_bytes(cfg)) / 1e6:.0f} MB per step exceed the 126 MB L2",
+        },
+        "tflops": world * 6.0 * S * H * I / (ms * 1e-3) / 1e12,
+        "kernel_ms": {"gateup_swiglu": gu_ms, "down": down_ms},
+        "roofline": {
+            "kernel": f"gateup_swiglu_{cfg['fmt']}",
+            "bound": "tensor",
+            "achieved": achieved,
+            "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s",
+            "frac": achieved / peaks["bf16_tflops"],
+            "peak_source": f"{peaks['source']} bf16 dense (burst; kernel timed alone)",
+            "algorithmic": f"4*S*H*I = {flops_gu / 1e9:.1f} GFLOP per launch",
+            "traffic": traffic,
+        },
+        "e2e": {
+            "value": world * T / (e2e_ms * 1e-3),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": T * H * 2 + T * E * 4,
+            "d2h_bytes_per_step": T * H * 2,
+        },
+        "gpu_launches": KERNELS_PER_STEP * args.steps,
+        "clocks": clk,
+    }
+    return line
+
+
+# ----------------------------------------------------------------------------- CPU reference (oracle port)
+
+class CpuReference:
+    """The CPU restatement of the reference's torch path (oracle/), on host cores."""
+
+    def __init__(self, cfg, sample_tokens, seed=1234):
+        import numpy as np
+        from oracle import quant as oq
+
+        self.cfg = cfg
+        rng = np.random.default_rng(seed)
+        T, H, E, k, I = sample_tokens, cfg["H"], cfg["E"], cfg["k"], cfg["I"]
+        self.T = T
+        self.x = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+        gate = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+        self.logits = (self.x @ gate.T).astype(np.float32)
+        if cfg["zipf"]:
+            p = 1.0 / np.arange(1, E + 1) ** cfg["zipf"]
+            p = p / p.sum()
+            self.logits = (self.logits + 2.0 * np.log(p)[None, :]).astype(np.float32)
+        raw = [(rng.standard_normal(s) * 0.02).astype(np.float32) for s in ((E, I, H), (E, I, H), (E, H, I))]
+        self.threads = os.cpu_count() or 1
+        if cfg["fmt"] == "nf4":
+            from concurrent.futures import ThreadPoolExecutor
+            with ThreadPoolExecutor(self.threads) as pool:
+                per = list(pool.map(lambda a: oq.nf4_quantize_2d(raw[a[0]][a[1]]),
+                                    [(key, e) for key in range(3) for e in range(E)]))
+            self.store = []
+            for key in range(3):
+                p = per[key * E:(key + 1) * E]
+                self.store.append({"nf4": np.stack([q["packed"] for q in p]),
+                                   "absmax": np.stack([q["absmax"] for q in p]),
+                                   "nabsmax": np.stack([q["nested_absmax"] for q in p]),
+                                   "offset": np.stack([q["offset"] for q in p]),
+                                   "code": p[0]["code"], "ncode": p[0]["nested_code"],
+                                   "shape": raw[key].shape})
+        elif cfg["fmt"] == "int8":
+            self.store = [oq.int8_quantize(w, 0)[:2] for w in raw]
+        else:
+            self.store = [oq.bf16_round(w) for w in raw]
+
+    def _dequant(self):
+        from concurrent.futures import ThreadPoolExecutor
+        import numpy as np
+        from oracle import quant as oq
+
+        fmt = self.cfg["fmt"]
+        if fmt == "bf16":
+            return self.store
+
+        def one(args):
+            key, e = args
+            if fmt == "nf4":
+                g = self.store[key]
+                _, o, i = g["shape"]
+                return oq.nf4_dequantize_2d({"packed": g["nf4"][e], "absmax": g["absmax"][e],
+                                             "nested_absmax": g["nabsmax"][e], "offset": g["offset"][e],
+                                             "code": g["code"], "nested_code": g["ncode"]}, (o, i))
+            q, s = self.store[key]
+            return oq.bf16_round(oq.int8_dequantize(q[e], s[e], 0))
+
+        E = self.cfg["E"]
+        with ThreadPoolExecutor(self.threads) as pool:
+            flat = list(pool.map(one, [(key, e) for key in range(3) for e in range(E)]))
+        return [np.stack(flat[key * E:(key + 1) * E]) for key in range(3)]
+
+    def step(self):
+        from oracle import moe as om
+        idx, w = om.route_topk(self.logits, self.cfg["k"])
+        w1, w3, w2 = self._dequant()
+        return om.moe_forward(self.x, idx, w, w1, w3, w2, bf16=True)
+
+
+def cpu_sample_tokens(cfg):
+    return min(cfg["T"], 4096)
+
+
+def run_reference(args, cfg):
+    ref = CpuReference(cfg, cpu_sample_tokens(cfg))
+    for _ in range(args.warmup):
+        ref.step()
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        ref.step()
+    sec = (time.perf_counter() - t) / args.steps
+    value = ref.T / sec
+    sample = (f"{ref.T} of {cfg['T']} tokens per step, full dequantisation of all {cfg['E']} experts each step "
+              f"(as the reference's chunked_dequant path does every forward)")
+    return {
+        "metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 numpy with bf16 rounding points",
+        "data": "synthetic (seeded numpy)",
+        "config": {"workload": f"{args.config} (CPU sample)", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def cpu_baseline(cfg):
+    ref = CpuReference(cfg, cpu_sample_tokens(cfg))
+    ref.step()  # warm
+    t = time.perf_counter()
+    n = 0
+    while True:
+        ref.step()
+        n += 1
+        if time.perf_counter() - t > 10.0 or n >= 3:
+            break
+    sec = (time.perf_counter() - t) / n
+    return {"value": ref.T / sec, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
+            "sample": f"{n} forward(s) of {ref.T} tokens of the {cfg['T']}-token workload, dequantising all "
+                      f"experts each forward; oracle/ numpy restatement of the reference torch path"}
+
+
+# ----------------------------------------------------------------------------- main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args, cfg)), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        from mirai_b200 import _lib
+        _lib.load()
+        line = run_ours(args, cfg, rank, world, dev)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(cfg)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -158,6 +158,28 @@ int mirai_moe_combine(const void* y_sorted, const int64_t* inverse_order, const 
                       int64_t num_tokens, int32_t top_k, int32_t hidden, void* out,
                       int32_t out_dtype, mirai_stream_t stream);
 
+/* --------------------------------------------------- a4 / a5: weight ingest
+ * NF4 quantisation of a bf16 [E, out, in] expert stack into the reference's
+ * per-expert buffers (CompressedGroupedExperts._store_nf4_grouped,
+ * experts.py:998-1031, which calls bitsandbytes quantize_4bit with
+ * blocksize 64 and compress_statistics=True, quant.py:315-358):
+ * packed [E, out*in/2], absmax codes [E, out*in/64], nested_absmax
+ * [E, ceil(out*in/64/nested_blocksize)], offset [E].  `code` (16) and
+ * `nested_code` (256) are the NF4 and dynamic-map tables to quantise against.
+ * The workspace holds the fp32 block absmax (size from the query). */
+size_t mirai_nf4_quantize_workspace_bytes(int32_t num_experts, int64_t out_features, int64_t in_features);
+int mirai_nf4_quantize(const void* weight_bf16, int32_t num_experts, int64_t out_features, int64_t in_features,
+                       const float* code, const float* nested_code, int32_t blocksize, int32_t nested_blocksize,
+                       uint8_t* packed, uint8_t* absmax, float* nested_absmax, float* offset, void* workspace,
+                       size_t workspace_bytes, mirai_stream_t stream);
+
+/* Per-output-channel symmetric INT8 of `rows` rows of `in_features`
+ * (quant.py:189-235 with group_size 0): scale = max(amax/127, 1e-30),
+ * q = clamp(round_half_even(x / scale), -127, 127).  weight_dtype is
+ * MIRAI_DTYPE_F32 or MIRAI_DTYPE_BF16. */
+int mirai_int8_quantize_rows(const void* weight, int32_t weight_dtype, int64_t rows, int64_t in_features,
+                             int8_t* q, float* scale, mirai_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

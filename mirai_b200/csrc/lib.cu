@@ -3,3 +3,4 @@
 #include "capi.cu"
 #include "routing.cu"
 #include "grouped_gemm.cu"
+#include "quantize.cu"

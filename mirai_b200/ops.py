@@ -161,6 +161,41 @@ class Int8Tensor:
         return self._struct
 
 
+def nf4_quantize(weight: torch.Tensor, code: torch.Tensor, nested_code: torch.Tensor, *,
+                 blocksize: int = 64, nested_blocksize: int = 256) -> NF4Tensor:
+    """Quantise a [E, out, in] stack to NF4 on the GPU (experts.py:998-1031)."""
+    w = _cuda(weight.to(torch.bfloat16), "weight")
+    E, out_f, in_f = w.shape
+    dev = w.device
+    bpe = out_f * in_f // blocksize
+    n_nested = -(-bpe // nested_blocksize)
+    packed = torch.empty((E, out_f * in_f // 2, 1), dtype=torch.uint8, device=dev)
+    absmax = torch.empty((E, bpe), dtype=torch.uint8, device=dev)
+    nabs = torch.empty((E, n_nested), dtype=torch.float32, device=dev)
+    offset = torch.empty((E,), dtype=torch.float32, device=dev)
+    code = _cuda(code, "code", torch.float32)
+    nested_code = _cuda(nested_code, "nested_code", torch.float32)
+    need = int(_lib.load().mirai_nf4_quantize_workspace_bytes(E, out_f, in_f))
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    _lib.call("mirai_nf4_quantize", _ptr(w), E, out_f, in_f, _ptr(code), _ptr(nested_code), blocksize,
+              nested_blocksize, _ptr(packed), _ptr(absmax), _ptr(nabs), _ptr(offset), _ptr(ws), need, _stream())
+    return NF4Tensor(packed, absmax, nabs, offset, code, nested_code, (E, out_f, in_f), blocksize, nested_blocksize)
+
+
+def int8_quantize(weight: torch.Tensor) -> Int8Tensor:
+    """Per-output-channel symmetric INT8 of a [E, out, in] stack (quant.py:189-235, g = 0)."""
+    w = _cuda(weight, "weight")
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.float()
+    *lead, in_f = w.shape
+    rows = w.numel() // in_f
+    q = torch.empty(w.shape, dtype=torch.int8, device=w.device)
+    s = torch.empty((*lead, 1), dtype=torch.float32, device=w.device)
+    _lib.call("mirai_int8_quantize_rows", _ptr(w), 1 if w.dtype == torch.float32 else 0, rows, in_f, _ptr(q),
+              _ptr(s), _stream())
+    return Int8Tensor(q, s)
+
+
 def _as_weight(w):
     if isinstance(w, (NF4Tensor, Int8Tensor)):
         return w.struct()

@@ -282,3 +282,38 @@ def test_nf4_moe_forward_end_to_end_config0_shape():
     ridx, rw = om.route_topk(logits, k)
     ref = om.moe_forward(x, ridx, rw, dense[0], dense[1], dense[2], bf16=True)
     assert om.rel_max_err(_f32(out), ref) < TOL
+
+
+# ----------------------------------------------------------------------------- weight ingest
+
+@pytest.mark.parametrize("E,out_f,in_f", [(2, 128, 256), (3, 256, 1408), (1, 64, 64)])
+def test_nf4_quantizer_matches_oracle(E, out_f, in_f):
+    dev = _dev()
+    from mirai_b200 import ops, tables
+    rng = np.random.default_rng(out_f + in_f)
+    w = oq.bf16_round((rng.standard_normal((E, out_f, in_f)) * 0.05).astype(np.float32))
+    w[0, 3, :64] = 0.0  # an all-zero block
+    got = ops.nf4_quantize(_bf16(w).to(dev), tables.nf4_code(dev), tables.dynamic_map(dev))
+    _check(ops)
+    ref = oq.nf4_quantize_grouped(w)
+    np.testing.assert_array_equal(got.packed.cpu().numpy().reshape(E, -1), ref["nf4"].reshape(E, -1))
+    np.testing.assert_array_equal(got.absmax.cpu().numpy(), ref["absmax"])
+    np.testing.assert_array_equal(got.nested_absmax.cpu().numpy(), ref["nabsmax"])
+    np.testing.assert_array_equal(got.offset.cpu().numpy(), ref["offset"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_int8_quantizer_matches_reference_golden(golden, dtype):
+    dev = _dev()
+    from mirai_b200 import ops
+    g = golden("int8_quant")
+    w = torch.from_numpy(g["weight"]).to(dtype)
+    got = ops.int8_quantize(w.to(dev))
+    _check(ops)
+    if dtype == torch.float32:
+        np.testing.assert_array_equal(got.q.cpu().numpy(), g["q_g0"])
+        np.testing.assert_array_equal(got.scale.cpu().numpy(), g["s_g0"])
+    else:
+        q, s, _ = oq.int8_quantize(w.float().numpy(), 0)
+        np.testing.assert_array_equal(got.q.cpu().numpy(), q)
+        np.testing.assert_array_equal(got.scale.cpu().numpy(), s)
