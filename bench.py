@@ -37,7 +37,8 @@ CONFIGS = {
     "c3": dict(T=8192, H=3072, E=64, k=4, I=1024, fmt="int8", zipf=1.2),
 }
 METRIC = "MoE-FFN tokens/s (NF4 experts) + % TC/HBM roofline at 1/2/4/8 B200"
-# Our kernels launched by one step: route 1, plan 4, permute 1, gate/up 1, down 1, combine 1.
+# Our kernels launched by one forward step: route 1, plan 4, permute 1, gate/up 1, down 1,
+# combine 1; a train step adds combine-backward, down-dX, gate/up-dX and the un-permute sum.
 KERNELS_PER_STEP = 9
 # DRAM bytes (read + write) of one gate/up launch from an ncu capture, per
 # workload; see profiles/ for the capture and its command.  None until captured.
@@ -164,14 +165,25 @@ def run_ours(args, cfg, rank, world, dev):
     T, H, E, k, I = cfg["T"], cfg["H"], cfg["E"], cfg["k"], cfg["I"]
     x, logits, (w1, w3, w2) = make_workload(cfg, dev, seed=1234 + rank)
     S = T * k
+    train = args.mode == "train"
+    g_out = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(99 + rank)).to(
+        torch.bfloat16) if train else None
 
-    def step(xin, lin, out=None):
+    def step(xin, lin, out=None, gin=None, dx_out=None):
         idx, tw = ops.route_topk(lin, k)
-        plan = ops.dispatch_plan(idx, E)
-        xs = ops.permute_rows(xin, plan.sorted_token_indices)
-        h = ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I)
-        y = ops.down(h, plan.offsets, w2, hidden=H)
-        return ops.combine(y, plan.inverse_order, tw, out=out)
+        if not train:
+            plan = ops.dispatch_plan(idx, E)
+            xs = ops.permute_rows(xin, plan.sorted_token_indices)
+            h = ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I)
+            y = ops.down(h, plan.offsets, w2, hidden=H)
+            return ops.combine(y, plan.inverse_order, tw, out=out)
+        o, st = ops.moe_forward_train(xin, idx, tw, w1, w3, w2, num_experts=E, inter=I)
+        if out is not None:
+            out.copy_(o)
+        dx, _ = ops.moe_backward_dx(g_out if gin is None else gin, st, w1, w3, w2, inter=I)
+        if dx_out is not None:
+            dx_out.copy_(dx)
+        return o
 
     def barrier():
         if world > 1:
@@ -226,11 +238,21 @@ def run_ours(args, cfg, rank, world, dev):
     x_dev = torch.empty_like(x)
     l_dev = torch.empty_like(logits)
     o_dev = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    if train:
+        g_host = g_out.cpu().pin_memory()
+        dx_host = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+        g_dev = torch.empty_like(g_out)
+        dx_dev = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
 
     def e2e_step():
         x_dev.copy_(x_host, non_blocking=True)
         l_dev.copy_(l_host, non_blocking=True)
-        step(x_dev, l_dev, out=o_dev)
+        if train:
+            g_dev.copy_(g_host, non_blocking=True)
+            step(x_dev, l_dev, out=o_dev, gin=g_dev, dx_out=dx_dev)
+            dx_host.copy_(dx_dev, non_blocking=True)
+        else:
+            step(x_dev, l_dev, out=o_dev)
         o_host.copy_(o_dev, non_blocking=True)
 
     for _ in range(max(1, min(3, args.warmup))):
@@ -270,13 +292,14 @@ def run_ours(args, cfg, rank, world, dev):
         "dtype": "bf16 activations x " + cfg["fmt"] + " weights, fp32 accumulate",
         "data": "synthetic (seeded torch.randn; random-init experts quantised on the GPU)",
         "config": {
-            "workload": f"{args.config}: one routed expert FFN layer forward, T={T} H={H} E={E} k={k} I={I} "
+            "workload": f"{args.config}: one routed expert FFN layer "
+                        + ("forward + dX backward" if train else "forward") + f", T={T} H={H} E={E} k={k} I={I} "
                         f"{cfg['fmt']} experts" + (f", Zipf({cfg['zipf']}) load" if cfg["zipf"] else ""),
             "tokens_per_gpu": T, "hidden": H, "experts": E, "top_k": k, "intermediate": I,
             "weights": cfg["fmt"], "parallelism": f"dp{world} token-parallel replicas (experts replicated)",
             "l2": f"no flush: inputs {(T * H * 2 + weight_bytes(cfg)) / 1e6:.0f} MB per step exceed the 126 MB L2",
         },
-        "tflops": world * 6.0 * S * H * I / (ms * 1e-3) / 1e12,
+        "tflops": world * (12.0 if train else 6.0) * S * H * I / (ms * 1e-3) / 1e12,
         "kernel_ms": {"gateup_swiglu": gu_ms, "down": down_ms},
         "roofline": {
             "kernel": f"gateup_swiglu_{cfg['fmt']}",
@@ -292,10 +315,10 @@ def run_ours(args, cfg, rank, world, dev):
         "e2e": {
             "value": world * T / (e2e_ms * 1e-3),
             "unit": "tokens/s",
-            "h2d_bytes_per_step": T * H * 2 + T * E * 4,
-            "d2h_bytes_per_step": T * H * 2,
+            "h2d_bytes_per_step": T * H * 2 * (2 if train else 1) + T * E * 4,
+            "d2h_bytes_per_step": T * H * 2 * (2 if train else 1),
         },
-        "gpu_launches": KERNELS_PER_STEP * args.steps,
+        "gpu_launches": (KERNELS_PER_STEP + (4 if train else 0)) * args.steps,
         "clocks": clk,
     }
     return line
@@ -426,6 +449,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default="fwd", choices=["fwd", "train"],
+                    help="fwd: forward only; train: forward + dX backward through the frozen experts")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

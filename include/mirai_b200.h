@@ -153,10 +153,52 @@ int mirai_moe_down_int8(const void* h, const int32_t* offsets, int32_t num_exper
  * out[t, :] = sum_j top_weights[t, j] * y[inverse_order[t*k + j], :], summed in
  * fp32 in ascending sorted position (the order of the reference's
  * output.index_add_, experts.py:2433-2437), then cast to out_dtype.
- * (combine_routed_tokens, dispatch_ops.py:23-44.) */
+ * (combine_routed_tokens, dispatch_ops.py:23-44.)  With top_weights == NULL
+ * every weight is 1: the un-permute sum that is the permute backward
+ * (_PermuteRoutedTokens.backward, dispatch_ops.py:15-20). */
 int mirai_moe_combine(const void* y_sorted, const int64_t* inverse_order, const float* top_weights,
                       int64_t num_tokens, int32_t top_k, int32_t hidden, void* out,
                       int32_t out_dtype, mirai_stream_t stream);
+
+/* ---------------------------------------------------- a8 backward: combine
+ * _CombineRoutedTokens.backward (dispatch_ops.py:36-44) for the bf16 path:
+ *   grad_y[s, :]     = bf16( grad_out[t, :] * w[t, j] )     s = inverse_order[t*k + j]
+ *   grad_weights[t,j] = sum_h grad_out[t, h] * y[s, h]      (fp32)
+ * grad_out is bf16 [T, H]; y_sorted / grad_y_sorted bf16 [S, H]. */
+int mirai_moe_combine_backward(const void* grad_out, const void* y_sorted, const int64_t* inverse_order,
+                               const float* top_weights, int64_t num_tokens, int32_t top_k, int32_t hidden,
+                               void* grad_y_sorted, float* grad_weights, mirai_stream_t stream);
+
+/* ------------------------------------ a9: dX through the frozen experts
+ * Down projection backward fused with the SwiGLU backward
+ * (_FrozenDequantBatchedLinear.backward, linear.py:116-125, then autograd of
+ * silu(gate) * up, experts.py:301-317):
+ *   dh = bf16(grad_y W2[e])                                 (K = H, N = I)
+ *   dgate = bf16(silu'(gate) * bf16(dh * up)), dup = bf16(dh * bf16(silu(gate)))
+ * gate_up is the [S, 2I] bf16 (gate | up) saved by the forward; the result
+ * grad_gate_up is [S, 2I] bf16 (dgate | dup).  Requires H, I % 64 == 0. */
+int mirai_moe_down_dx_bf16(const void* grad_y, const int32_t* offsets, int32_t num_experts,
+                           int64_t num_rows, int32_t hidden, int32_t inter, const void* w2,
+                           const void* gate_up, void* grad_gate_up, mirai_stream_t stream);
+int mirai_moe_down_dx_nf4(const void* grad_y, const int32_t* offsets, int32_t num_experts,
+                          int64_t num_rows, int32_t hidden, int32_t inter, const mirai_nf4_weight* w2,
+                          const void* gate_up, void* grad_gate_up, mirai_stream_t stream);
+int mirai_moe_down_dx_int8(const void* grad_y, const int32_t* offsets, int32_t num_experts,
+                           int64_t num_rows, int32_t hidden, int32_t inter, const mirai_int8_weight* w2,
+                           const void* gate_up, void* grad_gate_up, mirai_stream_t stream);
+
+/* Gate/up projection backward (_FrozenDequantBatchedLinearPair.backward,
+ * linear.py:191-203): dx_sorted = dgate W1[e] + dup W3[e], one fp32
+ * accumulation over K = 2I, rounded once to bf16 [S, H]. */
+int mirai_moe_gateup_dx_bf16(const void* grad_gate_up, const int32_t* offsets, int32_t num_experts,
+                             int64_t num_rows, int32_t inter, int32_t hidden, const void* w1,
+                             const void* w3, void* dx_sorted, mirai_stream_t stream);
+int mirai_moe_gateup_dx_nf4(const void* grad_gate_up, const int32_t* offsets, int32_t num_experts,
+                            int64_t num_rows, int32_t inter, int32_t hidden, const mirai_nf4_weight* w1,
+                            const mirai_nf4_weight* w3, void* dx_sorted, mirai_stream_t stream);
+int mirai_moe_gateup_dx_int8(const void* grad_gate_up, const int32_t* offsets, int32_t num_experts,
+                             int64_t num_rows, int32_t inter, int32_t hidden, const mirai_int8_weight* w1,
+                             const mirai_int8_weight* w3, void* dx_sorted, mirai_stream_t stream);
 
 /* --------------------------------------------------- a4 / a5: weight ingest
  * NF4 quantisation of a bf16 [E, out, in] expert stack into the reference's

@@ -72,6 +72,18 @@ SIGNATURES = {
     "mirai_moe_down_int8": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, ctypes.POINTER(Int8Weight),
                                            c_vp, c_vp]),
     "mirai_moe_combine": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_i32, c_vp]),
+    "mirai_moe_combine_backward": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    "mirai_moe_down_dx_bf16": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp]),
+    "mirai_moe_down_dx_nf4": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, ctypes.POINTER(Nf4Weight),
+                                             c_vp, c_vp, c_vp]),
+    "mirai_moe_down_dx_int8": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, ctypes.POINTER(Int8Weight),
+                                              c_vp, c_vp, c_vp]),
+    "mirai_moe_gateup_dx_bf16": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp]),
+    "mirai_moe_gateup_dx_nf4": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, ctypes.POINTER(Nf4Weight),
+                                               ctypes.POINTER(Nf4Weight), c_vp, c_vp]),
+    "mirai_moe_gateup_dx_int8": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32,
+                                                ctypes.POINTER(Int8Weight), ctypes.POINTER(Int8Weight), c_vp,
+                                                c_vp]),
     "mirai_nf4_quantize_workspace_bytes": (c_size, [c_i32, c_i64, c_i64]),
     "mirai_nf4_quantize": (ctypes.c_int, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp,
                                           c_vp, c_vp, c_size, c_vp]),

@@ -1,24 +1,30 @@
-// a6 / a7: persistent grouped GEMMs over expert-contiguous row segments on
-// sm_100a tensor cores (tcgen05.mma, fp32 accumulators in TMEM), with the
+// a6 / a7 / a9: persistent grouped GEMMs over expert-contiguous row segments
+// on sm_100a tensor cores (tcgen05.mma, fp32 accumulators in TMEM), with the
 // frozen expert weights read as bf16, NF4 or INT8.
 //
-// One CTA per SM, warp-specialised:
-//   warp 0       TMA producer: A (routed activations) and, for bf16 weights,
-//                B; for NF4 / INT8 weights the raw codes of B
-//   warp 1       UMMA issuer (one elected thread) and TMEM owner
-//   warps 2..5   epilogue: TMEM -> registers -> SwiGLU / bf16 -> global
-//   warps 6..9   (NF4 / INT8 only) dequantisers: raw codes in shared memory ->
-//                exact bf16 weights written in the UMMA operand layout
-// An A/B ring of STAGES shared-memory slots carries the operand tiles; two
-// TMEM accumulators (2 x 256 fp32 columns) let the epilogue of tile i overlap
-// the main loop of tile i+1.  Tiles are (expert, 128-row block, column
-// block), enumerated expert-major with the column block fastest so that CTAs
-// running together share one expert's weights in L2.
+// Modes (one kernel template):
+//   GATEUP    h = silu(x W1^T) * (x W3^T)            B = W1/W3 rows  (K-major)
+//   DOWN      y = h W2^T                              B = W2 rows     (K-major)
+//   DXDOWN    dgu = swiglu_bwd(dy W2, gate, up)       B = W2 columns  (MN-major)
+//   DXGATEUP  dx = dgate W1 + dup W3                  B = W1;W3       (MN-major)
 //
-// Operand layouts (K-major, 128-byte swizzle, 8-row x 128-byte atoms):
-//   A tile  [128 rows][64 k]  = 16 KB
-//   B tile  [256 rows][64 k]  = 32 KB  (gate/up: 128 rows of W1 then 128 of W3;
-//                                        down: 256 rows of W2)
+// One CTA per SM, warp-specialised:
+//   warp 0        TMA producer: A tiles; B tiles (bf16) or raw codes (NF4/INT8)
+//   warp 1        UMMA issuer (one thread) and TMEM owner
+//   warps 2..5    epilogue: TMEM -> registers -> SwiGLU (+bwd) / bf16 -> global
+//   warps 6..13   (NF4 / INT8) dequantisers: raw codes in shared memory ->
+//                 exact bf16 weights in the UMMA operand layout
+// A/B ring of STAGES shared-memory slots; two TMEM accumulators (2 x 256
+// fp32 columns) overlap the epilogue of tile i with the main loop of tile
+// i+1.  Tiles are (expert, 128-row block, 256-column block), expert-major
+// with the column block fastest, so CTAs running together share one expert's
+// weights in L2.
+//
+// Operand layouts (128-byte swizzle):
+//   A  [128 rows][64 k] K-major = 16 KB
+//   B  K-major:  [256 rows][64 k]            (8-row x 128 B atoms, SBO 1 KB)
+//      MN-major: [4 x 64 n][64 k rows]       (atoms 8 k-rows x 64 n; LBO 8 KB
+//                                             between 64-n blocks, SBO 1 KB)
 // Dequantisation is bit-exact with the reference's dequantise-then-matmul:
 //   NF4  w = bf16( code[nibble] * (ncode[q] * nabsmax + offset) )  (quant.py:413-431)
 //   INT8 w = bf16( q * scale[row] )                                 (quant.py:238-260, g = 0)
@@ -35,40 +41,50 @@ constexpr int UMMA_K = 16;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 constexpr uint32_t B_BYTES = BN * BK * 2;
 constexpr int kEpiWarps = 4;
-constexpr int kDeqWarps = 4;
+constexpr int kDeqWarps = 8;
+constexpr int kDeqThreads = 32 * kDeqWarps;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr int kMaxExperts = 1024;
-constexpr int kMaxKBlocks = 64;  // K <= 4096 for the quantised formats
+constexpr int kMaxK = 4096;        // reduction length supported by the quantised formats
+constexpr int kMaxNested = 512;    // nested absmax entries per expert and key
 
-enum Mode { GATEUP = 0, DOWN = 1 };
+enum Mode { GATEUP = 0, DOWN = 1, DXDOWN = 2, DXGATEUP = 3 };
 enum WFmt { W_BF16 = 0, W_NF4 = 1, W_INT8 = 2 };
+
+template <int MODE> struct MCfg {
+  static constexpr bool MN = MODE == DXDOWN || MODE == DXGATEUP;  // B operand MN-major
+  static constexpr bool TWO_KEYS = MODE == GATEUP || MODE == DXGATEUP;
+};
 
 template <int WF> struct Cfg;
 template <> struct Cfg<W_BF16> {
   static constexpr int STAGES = 4;
   static constexpr uint32_t RAW_BYTES = 0;
   static constexpr int THREADS = 64 + 32 * kEpiWarps;
+  static constexpr int ROW_BYTES = 0;
 };
 template <> struct Cfg<W_NF4> {
   static constexpr int STAGES = 3;
   static constexpr uint32_t RAW_BYTES = BN * BK / 2;  // 8 KB of packed nibbles
   static constexpr int THREADS = 64 + 32 * (kEpiWarps + kDeqWarps);
+  static constexpr int ROW_BYTES = BK / 2;            // raw bytes of 64 elements
 };
 template <> struct Cfg<W_INT8> {
   static constexpr int STAGES = 3;
   static constexpr uint32_t RAW_BYTES = BN * BK;  // 16 KB of int8
   static constexpr int THREADS = 64 + 32 * (kEpiWarps + kDeqWarps);
+  static constexpr int ROW_BYTES = BK;
 };
 
-// One B half (128 weight rows) of a quantised key.
-struct QHalf {
+// One quantised key (W1, W3 or W2).
+struct QKey {
   const uint8_t* absmax;       // NF4: [E, out*in/64] codes
   const float* nested_absmax;  // NF4: [E, n_nested]
   const float* offset;         // NF4: [E]
   const float* code;           // NF4: [16]
   const float* nested_code;    // NF4: [256]
   const float* scale;          // INT8: [E, out]
-  int n_nested;                // per expert
+  int n_nested;                // NF4: per expert
 };
 
 struct Params {
@@ -76,12 +92,15 @@ struct Params {
   int E;
   int64_t S;               // total routed rows
   int K;                   // reduction length
-  int N;                   // rows of one expert's B matrix (I for gate/up, H for down)
+  int N;                   // output columns per row (I, H, I, H by mode)
   int n_tiles;             // column tiles per row block
-  __nv_bfloat16* out;      // h [S, I] (gate/up) or y [S, H] (down)
+  int krows;               // MN modes: K rows of one expert in one key (H for W2, I for W1/W3)
+  int kb_half;             // DXGATEUP: k-blocks taken from W1 before W3
+  int out_rows;            // K-major modes: rows of one expert's B matrix per key
+  __nv_bfloat16* out;      // h [S,I] | y [S,H] | dgu [S,2I] | dx [S,H]
   int64_t ldo;             // elements
-  __nv_bfloat16* gate_up;  // optional [S, 2I]
-  QHalf q[2];              // quantised B halves (gate/up: W1, W3; down: W2, W2)
+  __nv_bfloat16* gate_up;  // GATEUP: optional saved [S,2I] output; DXDOWN: saved input
+  QKey q[2];               // quantised keys (index 1 used by GATEUP / DXGATEUP)
   int nbs_shift;           // log2(nested_blocksize)
 };
 
@@ -99,12 +118,13 @@ struct Smem {
   int tile_prefix[kMaxExperts + 1];
 };
 
-// Extra shared memory of the dequantisers: per-tile absmax codes, the
-// byte -> (code[hi], code[lo]) table and the nested code map per B half.
+// Dequantiser scratch: per-tile absmax codes (or INT8 row scales), the
+// expert's nested absmax, and the code tables, per key.
 struct DeqSmem {
-  uint8_t absq[2][128 * kMaxKBlocks];
-  float2 lut[2][256];
+  uint8_t absq[16384];
+  float nested[2][kMaxNested];
   float ncode[2][256];
+  float code[2][16];
 };
 
 template <int WF>
@@ -138,10 +158,73 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
-// Weight row (within the [E * N] row space) of B half h for tile (e, n).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(s));
+  return d;
+}
+
+// ---------------------------------------------------------------------------
+// NF4 decode without memory lookups.  For one 64-element block the 16
+// possible outputs bf16(code[j] * scale) are formed once; their low and high
+// bytes are split into lo[4] / hi[4] (4 entries per register) so that PRMT
+// can select one entry per output byte from a 4-bit index.
+struct Nf4Tab {
+  uint32_t lo[4], hi[4];
+};
+
+__device__ __forceinline__ void nf4_table(const float* code, float scale, Nf4Tab& t) {
+  uint32_t q[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q[i] = pack_bf16x2(__fmul_rn(code[2 * i], scale), __fmul_rn(code[2 * i + 1], scale));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    t.lo[j] = prmt(q[2 * j], q[2 * j + 1], 0x6420);
+    t.hi[j] = prmt(q[2 * j], q[2 * j + 1], 0x7531);
+  }
+}
+
+// One packed word = 8 elements, the first element in the high nibble of
+// byte 0.  Produces 4 registers of bf16 pairs in element order.
+__device__ __forceinline__ void nf4_word(uint32_t w, const Nf4Tab& t, uint32_t (&o)[4]) {
+  const uint32_t sel = w & 0x77777777u;  // entry within the 8-entry half
+  const uint32_t selh = sel >> 16;
+  const uint32_t wsh = w << 4;
+  // byte masks: 0xFF where the nibble's bit 3 is set (entries 8..15), from the
+  // sign-replicating PRMT mode on the byte whose msb is that bit
+  const uint32_t m0 = prmt(w, wsh, 0x9D8C);
+  const uint32_t m1 = prmt(w, wsh, 0xBFAE);
+  const uint32_t lo0 = (prmt(t.lo[0], t.lo[1], sel) & ~m0) | (prmt(t.lo[2], t.lo[3], sel) & m0);
+  const uint32_t hi0 = (prmt(t.hi[0], t.hi[1], sel) & ~m0) | (prmt(t.hi[2], t.hi[3], sel) & m0);
+  const uint32_t lo1 = (prmt(t.lo[0], t.lo[1], selh) & ~m1) | (prmt(t.lo[2], t.lo[3], selh) & m1);
+  const uint32_t hi1 = (prmt(t.hi[0], t.hi[1], selh) & ~m1) | (prmt(t.hi[2], t.hi[3], selh) & m1);
+  // selector nibbles address [second, first, fourth, third] element of each byte pair
+  o[0] = prmt(lo0, hi0, 0x4051);
+  o[1] = prmt(lo0, hi0, 0x6273);
+  o[2] = prmt(lo1, hi1, 0x4051);
+  o[3] = prmt(lo1, hi1, 0x6273);
+}
+
+// 16 int8 (one uint4) -> 16 bf16(q * scale) as 8 registers.
+__device__ __forceinline__ void int8_x16(const uint4 r, float scale, uint32_t (&o)[8]) {
+  const uint32_t words[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const uint32_t biased = words[w] ^ 0x80808080u;  // q + 128 as unsigned bytes
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      // 0x4B0000uu is the float 2^23 + uu: subtracting 2^23 + 128 recovers q exactly
+      const float q0 = __uint_as_float(__byte_perm(biased, 0x4B000000u, 0x7540u + 2 * b)) - 8388736.f;
+      const float q1 = __uint_as_float(__byte_perm(biased, 0x4B000000u, 0x7541u + 2 * b)) - 8388736.f;
+      o[2 * w + b] = pack_bf16x2(__fmul_rn(q0, scale), __fmul_rn(q1, scale));
+    }
+  }
+}
+
+// K-major modes: weight row (within the [E * out_rows] row space) of B half h.
 template <int MODE>
-__device__ __forceinline__ int b_row(const Params& p, int e, int n, int h) {
-  return MODE == GATEUP ? e * p.N + n * (BN / 2) : e * p.N + n * BN + h * (BN / 2);
+__device__ __forceinline__ int kmajor_row(const Params& p, int e, int n, int h) {
+  return MODE == GATEUP ? e * p.out_rows + n * (BN / 2) : e * p.out_rows + n * BN + h * (BN / 2);
 }
 
 template <int MODE, int WF>
@@ -151,6 +234,7 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
   constexpr int STAGES = Cfg<WF>::STAGES;
   constexpr uint32_t RAW_BYTES = Cfg<WF>::RAW_BYTES;
   constexpr bool QUANT = WF != W_BF16;
+  constexpr bool MN = MCfg<MODE>::MN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = base;
@@ -215,15 +299,11 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
     prefetch_tmap(&tmap_b0);
     prefetch_tmap(&tmap_b1);
   }
-  if (QUANT && warp >= 2 + kEpiWarps) {
+  if (WF == W_NF4 && warp >= 2 + kEpiWarps) {
     const int d = threadIdx.x - 32 * (2 + kEpiWarps);
-    if (WF == W_NF4) {
-      for (int h = 0; h < 2; ++h) {
-        for (int i = d; i < 256; i += 32 * kDeqWarps) {
-          dq->lut[h][i] = make_float2(__ldg(p.q[h].code + (i >> 4)), __ldg(p.q[h].code + (i & 15)));
-          dq->ncode[h][i] = __ldg(p.q[h].nested_code + i);
-        }
-      }
+    for (int h = 0; h < 2; ++h) {
+      for (int i = d; i < 256; i += kDeqThreads) dq->ncode[h][i] = __ldg(p.q[h].nested_code + i);
+      if (d < 16) dq->code[h][d] = __ldg(p.q[h].code + d);
     }
   }
   tc_fence_before();
@@ -244,18 +324,27 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
         int e, m, n;
         decode_tile<WF>(t, sm, E, p.n_tiles, e, m, n);
         const int row0 = sm.row_start[e] + m * BM;
-        const int br0 = b_row<MODE>(p, e, n, 0);
-        const int br1 = b_row<MODE>(p, e, n, 1);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&sm.empty[stage], phase ^ 1, 10)) {
             *abort_flag = 1;
             break;
           }
+          // B source for this k-block
+          const bool key1 = MCfg<MODE>::TWO_KEYS && (MN ? kb >= p.kb_half : false);
+          const CUtensorMap* mb = key1 ? &tmap_b1 : &tmap_b0;
+          const int krow = MN ? e * p.krows + (kb - (key1 ? p.kb_half : 0)) * BK : 0;
           if (!QUANT) {
             mbar_arrive_expect_tx(&sm.full[stage], A_BYTES + B_BYTES);
             uint8_t* b_dst = sB + stage * B_BYTES;
-            tma_load_2d(b_dst, &tmap_b0, kb * BK, br0, &sm.full[stage]);
-            tma_load_2d(b_dst + B_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * BK, br1, &sm.full[stage]);
+            if (MN) {
+#pragma unroll
+              for (int nb = 0; nb < 4; ++nb)
+                tma_load_2d(b_dst + nb * (B_BYTES / 4), mb, n * BN + nb * 64, krow, &sm.full[stage]);
+            } else {
+              tma_load_2d(b_dst, &tmap_b0, kb * BK, kmajor_row<MODE>(p, e, n, 0), &sm.full[stage]);
+              tma_load_2d(b_dst + B_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * BK,
+                          kmajor_row<MODE>(p, e, n, 1), &sm.full[stage]);
+            }
           } else {
             mbar_arrive_expect_tx(&sm.full[stage], A_BYTES);
           }
@@ -267,10 +356,16 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
             }
             mbar_arrive_expect_tx(&sm.raw_full[stage], RAW_BYTES);
             uint8_t* r_dst = sRaw + stage * RAW_BYTES;
-            constexpr int kbx = WF == W_NF4 ? BK / 2 : BK;  // raw bytes of one row per k-block
-            tma_load_2d(r_dst, &tmap_b0, kb * kbx, br0, &sm.raw_full[stage]);
-            tma_load_2d(r_dst + RAW_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * kbx, br1,
-                        &sm.raw_full[stage]);
+            constexpr int RB = Cfg<WF>::ROW_BYTES;
+            if (MN) {
+#pragma unroll
+              for (int nb = 0; nb < 4; ++nb)
+                tma_load_2d(r_dst + nb * (RAW_BYTES / 4), mb, (n * BN + nb * 64) * RB / 64, krow, &sm.raw_full[stage]);
+            } else {
+              tma_load_2d(r_dst, &tmap_b0, kb * RB, kmajor_row<MODE>(p, e, n, 0), &sm.raw_full[stage]);
+              tma_load_2d(r_dst + RAW_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * RB,
+                          kmajor_row<MODE>(p, e, n, 1), &sm.raw_full[stage]);
+            }
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -282,7 +377,7 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
   } else if (warp == 1) {
     // ======================= UMMA issuer =======================
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(BM, BN);
+      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, false, MN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -307,7 +402,8 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
             const uint64_t ad = make_sdesc_sw128(a_addr + k * UMMA_K * 2, 16, 1024);
-            const uint64_t bd = make_sdesc_sw128(b_addr + k * UMMA_K * 2, 16, 1024);
+            const uint64_t bd = MN ? make_sdesc_sw128(b_addr + k * UMMA_K * 128, B_BYTES / 4, 1024)
+                                   : make_sdesc_sw128(b_addr + k * UMMA_K * 2, 16, 1024);
             umma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&sm.empty[stage]);
@@ -379,6 +475,52 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
             }
           }
         }
+      } else if (MODE == DXDOWN) {
+        // dgu = SwiGLU backward of the saved (gate, up) given dh = dy W2
+        // (autograd of experts.py:301-317 in bf16: mul, silu backward)
+        const int64_t ld2 = 2 * (int64_t)p.N;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          const int col = n * BN + c * 32;
+          uint32_t v32[32];
+          tmem_ld_32x32b_x32(tb + c * 32, v32);
+          tmem_ld_wait();
+          if (valid && col < p.N) {
+            const uint4* gs = reinterpret_cast<const uint4*>(p.gate_up + grow * ld2 + col);
+            const uint4* us = reinterpret_cast<const uint4*>(p.gate_up + grow * ld2 + p.N + col);
+            uint32_t gw[16], uw[16], dg[16], du[16];
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const uint4 a = gs[v], b = us[v];
+              gw[4 * v] = a.x, gw[4 * v + 1] = a.y, gw[4 * v + 2] = a.z, gw[4 * v + 3] = a.w;
+              uw[4 * v] = b.x, uw[4 * v + 1] = b.y, uw[4 * v + 2] = b.z, uw[4 * v + 3] = b.w;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float dgo[2], duo[2];
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                const float dh = bf16r(__uint_as_float(v32[2 * j + hh]));
+                const float gv = hh ? bf16_hi(gw[j]) : bf16_lo(gw[j]);
+                const float uv = hh ? bf16_hi(uw[j]) : bf16_lo(uw[j]);
+                const float sg = 1.f / (1.f + expf(-gv));
+                const float act = bf16r(gv * sg);
+                const float dact = bf16r(dh * uv);
+                duo[hh] = dh * act;
+                dgo[hh] = dact * sg * (1.f + gv * (1.f - sg));
+              }
+              dg[j] = pack_bf16x2(dgo[0], dgo[1]);
+              du[j] = pack_bf16x2(duo[0], duo[1]);
+            }
+            uint4* gd = reinterpret_cast<uint4*>(p.out + grow * ld2 + col);
+            uint4* ud = reinterpret_cast<uint4*>(p.out + grow * ld2 + p.N + col);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              gd[v] = make_uint4(dg[4 * v], dg[4 * v + 1], dg[4 * v + 2], dg[4 * v + 3]);
+              ud[v] = make_uint4(du[4 * v], du[4 * v + 1], du[4 * v + 2], du[4 * v + 3]);
+            }
+          }
+        }
       } else {
         const int col0 = n * BN;
 #pragma unroll 1
@@ -386,7 +528,7 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
           uint32_t v32[32];
           tmem_ld_32x32b_x32(tb + c * 32, v32);
           tmem_ld_wait();
-          if (valid) {
+          if (valid && col0 + c * 32 < p.N) {
             uint32_t yp[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) yp[j] = pack_bf16x2(__uint_as_float(v32[2 * j]), __uint_as_float(v32[2 * j + 1]));
@@ -402,33 +544,67 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
     }
   } else if (QUANT) {
     // ======================= dequantisers =======================
-    // Thread d owns B row d of each half (rows d and 128 + d of the tile).
+    // K-major: thread d owns B row (d & 127) of half (d >> 7).
+    // MN-major: thread d owns k-row (d & 63) of 64-column block (d >> 6).
     const int d = threadIdx.x - 32 * (2 + kEpiWarps);
     const int nkb = num_kb;
+    const int kh = MN ? 0 : d >> 7;       // key of this thread (K-major)
+    const int kr = MN ? d & 63 : d & 127;  // row index inside the stage
+    const int nbq = MN ? d >> 6 : 0;       // 64-column block (MN-major)
+    constexpr int RB = Cfg<WF>::ROW_BYTES;
+    const int nblk_row = p.N / 64;         // MN: NF4 blocks per weight row
     int stage = 0;
     uint32_t phase = 0;
+    float code[16];
     for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
       int e, m, n;
       decode_tile<WF>(t, sm, E, p.n_tiles, e, m, n);
-      int wrow[2];  // row inside the expert's [out, in] matrix
-      float s_off[2] = {0.f, 0.f};
-      float row_scale[2] = {0.f, 0.f};
-      const float* nab[2] = {nullptr, nullptr};
-      for (int h = 0; h < 2; ++h) wrow[h] = b_row<MODE>(p, e, n, h) - e * p.N + d;
+      // ---- stage this tile's scale inputs in shared memory
+      named_bar_sync(1, kDeqThreads);
       if (WF == W_NF4) {
-        // stage this tile's absmax codes: 128 rows x nkb bytes per half, contiguous
-        named_bar_sync(1, 32 * kDeqWarps);
-        for (int h = 0; h < 2; ++h) {
-          const uint4* src = reinterpret_cast<const uint4*>(p.q[h].absmax + (size_t)b_row<MODE>(p, e, n, h) * nkb);
-          uint4* dst = reinterpret_cast<uint4*>(dq->absq[h]);
-          for (int i = d; i < 8 * nkb; i += 32 * kDeqWarps) dst[i] = __ldg(src + i);
-          s_off[h] = __ldg(p.q[h].offset + e);
-          nab[h] = p.q[h].nested_absmax + (size_t)e * p.q[h].n_nested;
+        if (!MN) {
+          for (int h = 0; h < 2; ++h) {
+            if (kmajor_row<MODE>(p, e, n, h) - e * p.out_rows >= p.out_rows) continue;  // past the last row
+            const uint4* src =
+                reinterpret_cast<const uint4*>(p.q[h].absmax + (size_t)kmajor_row<MODE>(p, e, n, h) * nkb);
+            uint4* dst = reinterpret_cast<uint4*>(dq->absq + h * 128 * nkb);
+            for (int i = d; i < 8 * nkb; i += kDeqThreads) dst[i] = __ldg(src + i);
+          }
+        } else {
+          // absq[kk * 4 + j] = code of (k-row kk, column block n*4 + j)
+          for (int i = d; i < p.K * 4; i += kDeqThreads) {
+            const int kk = i >> 2, j = i & 3;
+            const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
+            const int wr = kk - key * p.krows;
+            const int nbg = n * 4 + j;
+            dq->absq[i] = nbg < nblk_row
+                              ? __ldg(p.q[key].absmax + ((size_t)e * p.krows + wr) * nblk_row + nbg) : (uint8_t)0;
+          }
         }
-        named_bar_sync(1, 32 * kDeqWarps);
-      } else {
-        for (int h = 0; h < 2; ++h) row_scale[h] = __ldg(p.q[h].scale + (size_t)e * p.N + wrow[h]);
+        for (int h = 0; h < (MCfg<MODE>::TWO_KEYS ? 2 : 1); ++h)
+          for (int i = d; i < p.q[h].n_nested; i += kDeqThreads)
+            dq->nested[h][i] = __ldg(p.q[h].nested_absmax + (size_t)e * p.q[h].n_nested + i);
+      } else if (MN) {
+        // INT8 MN-major: the scale belongs to the k-row (output channel of W)
+        float* srow = reinterpret_cast<float*>(dq->absq);
+        for (int kk = d; kk < p.K; kk += kDeqThreads) {
+          const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
+          srow[kk] = __ldg(p.q[key].scale + (size_t)e * p.krows + (kk - key * p.krows));
+        }
       }
+      named_bar_sync(1, kDeqThreads);
+      // K-major: is this thread's B row inside the expert's matrix?  (The last
+      // 256-row tile of a down projection with N % 256 == 128 is half empty.)
+      const bool row_live = MN || (kmajor_row<MODE>(p, e, n, kh) - e * p.out_rows + kr < p.out_rows);
+      float row_scale = 0.f;
+      if (WF == W_INT8 && !MN && row_live)
+        row_scale = __ldg(p.q[kh].scale + (size_t)kmajor_row<MODE>(p, e, n, kh) + kr);
+      float off[2] = {0.f, 0.f};
+      if (WF == W_NF4) {
+        off[0] = __ldg(p.q[0].offset + e);
+        off[1] = MCfg<MODE>::TWO_KEYS ? __ldg(p.q[1].offset + e) : off[0];
+      }
+      int cur_key = -1;
       for (int kb = 0; kb < nkb; ++kb) {
         bool ok = mbar_wait(&sm.raw_full[stage], phase, 40);
         ok = ok && mbar_wait(&sm.empty[stage], phase ^ 1, 41);
@@ -436,52 +612,56 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
           *abort_flag = 1;
           break;
         }
-        const uint8_t* raw = sRaw + stage * RAW_BYTES;
-        const uint32_t bst = smem_u32(sB + stage * B_BYTES);
+        const int key = MN ? ((MCfg<MODE>::TWO_KEYS && kb >= p.kb_half) ? 1 : 0)
+                           : (MCfg<MODE>::TWO_KEYS ? kh : 0);
+        const uint8_t* raw = sRaw + stage * RAW_BYTES +
+                             (MN ? nbq * (RAW_BYTES / 4) + kr * RB : kh * (RAW_BYTES / 2) + kr * RB);
+        const uint32_t row_addr = smem_u32(sB + stage * B_BYTES) +
+                                  (MN ? (uint32_t)nbq * (B_BYTES / 4) + (uint32_t)kr * 128u
+                                      : (uint32_t)(kh * 128 + kr) * 128u);
+        const int sw = kr & 7;
+        if (WF == W_NF4) {
+          if (key != cur_key) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t row_addr = bst + (uint32_t)(h * 128 + d) * 128u;
-          const int sw = d & 7;
-          if (WF == W_NF4) {
-            const uint32_t qcode = dq->absq[h][d * nkb + kb];
-            const int nidx = (wrow[h] * nkb + kb) >> p.nbs_shift;
-            const float scale = __fadd_rn(__fmul_rn(dq->ncode[h][qcode], __ldg(nab[h] + nidx)), s_off[h]);
-            const uint4* rp = reinterpret_cast<const uint4*>(raw + h * (RAW_BYTES / 2) + d * 32);
-            const uint4 r0 = rp[0], r1 = rp[1];
-            const uint32_t words[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-            const float2* lut = dq->lut[h];
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {  // 16-byte chunk c = elements 8c .. 8c+7 = raw bytes 4c .. 4c+3
-              uint32_t o[4];
-#pragma unroll
-              for (int b = 0; b < 4; ++b) {
-                const float2 f = lut[(words[c] >> (8 * b)) & 0xFFu];
-                o[b] = pack_bf16x2(__fmul_rn(f.x, scale), __fmul_rn(f.y, scale));
-              }
-              st_shared_v4(row_addr + (uint32_t)((c ^ sw) << 4), o[0], o[1], o[2], o[3]);
-            }
+            for (int i = 0; i < 16; ++i) code[i] = dq->code[key][i];
+            cur_key = key;
+          }
+          int blk;
+          uint32_t qcode;
+          bool live = row_live;
+          if (!MN) {
+            const int wrow = kmajor_row<MODE>(p, e, n, kh) - e * p.out_rows + kr;
+            blk = wrow * nkb + kb;
+            qcode = dq->absq[kh * 128 * nkb + kr * nkb + kb];
           } else {
-            const float scale = row_scale[h];
-            const uint4* rp = reinterpret_cast<const uint4*>(raw + h * (RAW_BYTES / 2) + d * 64);
+            const int kk = kb * BK + kr;                     // k-row across both keys
+            const int wr = kk - key * p.krows;               // k-row inside the key's matrix
+            const int nbg = n * 4 + nbq;
+            live = nbg < nblk_row;
+            blk = wr * nblk_row + nbg;
+            qcode = dq->absq[kk * 4 + nbq];
+          }
+          const float scale =
+              live ? __fadd_rn(__fmul_rn(dq->ncode[key][qcode], dq->nested[key][blk >> p.nbs_shift]), off[key]) : 0.f;
+          Nf4Tab tab;
+          nf4_table(code, scale, tab);
+          const uint4 r0 = reinterpret_cast<const uint4*>(raw)[0];
+          const uint4 r1 = reinterpret_cast<const uint4*>(raw)[1];
+          const uint32_t words[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {  // 16 int8 -> two 16-byte bf16 chunks
-              const uint4 r = rp[v];
-              const uint32_t words[4] = {r.x, r.y, r.z, r.w};
-              uint32_t o[8];
+          for (int c = 0; c < 8; ++c) {
+            uint32_t o[4];
+            nf4_word(words[c], tab, o);
+            st_shared_v4(row_addr + (uint32_t)((c ^ sw) << 4), o[0], o[1], o[2], o[3]);
+          }
+        } else {
+          const float scale = MN ? reinterpret_cast<const float*>(dq->absq)[kb * BK + kr] : row_scale;
 #pragma unroll
-              for (int w = 0; w < 4; ++w) {
-                const uint32_t biased = words[w] ^ 0x80808080u;  // q + 128 as unsigned bytes
-#pragma unroll
-                for (int b = 0; b < 2; ++b) {
-                  // 0x4B0000uu is the float 2^23 + uu: subtracting 2^23 + 128 recovers q exactly
-                  const float q0 = __uint_as_float(__byte_perm(biased, 0x4B000000u, 0x7540u + 2 * b)) - 8388736.f;
-                  const float q1 = __uint_as_float(__byte_perm(biased, 0x4B000000u, 0x7541u + 2 * b)) - 8388736.f;
-                  o[2 * w + b] = pack_bf16x2(__fmul_rn(q0, scale), __fmul_rn(q1, scale));
-                }
-              }
-              st_shared_v4(row_addr + (uint32_t)(((2 * v) ^ sw) << 4), o[0], o[1], o[2], o[3]);
-              st_shared_v4(row_addr + (uint32_t)(((2 * v + 1) ^ sw) << 4), o[4], o[5], o[6], o[7]);
-            }
+          for (int v = 0; v < 4; ++v) {
+            uint32_t o[8];
+            int8_x16(reinterpret_cast<const uint4*>(raw)[v], scale, o);
+            st_shared_v4(row_addr + (uint32_t)(((2 * v) ^ sw) << 4), o[0], o[1], o[2], o[3]);
+            st_shared_v4(row_addr + (uint32_t)(((2 * v + 1) ^ sw) << 4), o[4], o[5], o[6], o[7]);
           }
         }
         fence_proxy_async_smem();
@@ -521,60 +701,65 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1
   const int64_t max_tiles = ((p.S + BM - 1) / BM + p.E) * (int64_t)p.n_tiles;
   const int grid = (int)(max_tiles < sm_count() ? max_tiles : sm_count());
   kern<<<grid, Cfg<WF>::THREADS, smem, stream>>>(ta, tb0, tb1, p);
-  return check_launch(MODE == GATEUP ? "gateup_swiglu" : "down");
+  static const char* names[4] = {"gateup_swiglu", "down", "down_dx", "gateup_dx"};
+  return check_launch(names[MODE]);
 }
 
 static inline bool mis16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; }
 
-// Shared host-side checks and the A-operand tensor map.
+// Shared host-side checks, the A-operand tensor map and the mode geometry.
 template <int MODE>
 int prepare(const char* name, const void* a, const int32_t* offsets, int E, int64_t S, int K, int N, void* out,
             void* gate_up, Params& p, CUtensorMap& ta) {
   if (E <= 0 || E > kMaxExperts || S < 0 || K <= 0 || N <= 0)
     return set_error(MIRAI_ERR_INVALID_ARG, "%s: bad sizes (E=%d, S=%lld, K=%d, N=%d)", name, E, (long long)S, K, N);
-  const int ntile = MODE == GATEUP ? BN / 2 : BN;
+  const int ntile = MODE == GATEUP ? BN / 2 : (MODE == DOWN ? BN / 2 : 64);
   if (K % BK != 0 || N % ntile != 0)
     return set_error(MIRAI_ERR_UNSUPPORTED, "%s: needs K %% %d == 0 and N %% %d == 0 (K=%d, N=%d)", name, BK, ntile,
                      K, N);
   if (S >= (int64_t)1 << 31) return set_error(MIRAI_ERR_UNSUPPORTED, "%s: more than 2^31 routed rows", name);
   if (!a || !offsets || !out || mis16(out) || (gate_up && mis16(gate_up)))
     return set_error(MIRAI_ERR_INVALID_ARG, "%s: null or misaligned pointer", name);
+  if (MODE == DXDOWN && !gate_up) return set_error(MIRAI_ERR_INVALID_ARG, "%s: saved gate/up is required", name);
+  p = Params{};
   p.offsets = offsets;
   p.E = E;
   p.S = S;
   p.K = K;
   p.N = N;
-  p.n_tiles = N / ntile;
+  p.n_tiles = MODE == GATEUP ? N / (BN / 2) : (N + BN - 1) / BN;
+  p.krows = MODE == DXDOWN ? K : (MODE == DXGATEUP ? K / 2 : 0);
+  p.kb_half = MODE == DXGATEUP ? (K / 2) / BK : 0;
+  p.out_rows = N;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = N;
   p.gate_up = static_cast<__nv_bfloat16*>(gate_up);
   p.nbs_shift = 8;
-  p.q[0] = QHalf{};
-  p.q[1] = QHalf{};
   return make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, (uint64_t)K, (uint64_t)S, (uint64_t)K * 2, BK, BM,
                       CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-int bf16_weight_map(CUtensorMap& m, const void* w, int E, int N, int K) {
+// bf16 weight map.  K-major: [E*rows, cols] with boxes of 64 cols x 128 rows.
+// MN-major: the same matrix read as [E*rows (k), cols (n)] with 64 x 64 boxes.
+int bf16_weight_map(CUtensorMap& m, const void* w, int E, int rows, int cols, bool mn) {
   if (!w) return set_error(MIRAI_ERR_INVALID_ARG, "null weight pointer");
-  return make_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, (uint64_t)K, (uint64_t)E * N, (uint64_t)K * 2, BK,
-                      BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+  return make_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, (uint64_t)cols, (uint64_t)E * rows,
+                      (uint64_t)cols * 2, 64, mn ? 64 : BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-int nf4_half(CUtensorMap& m, QHalf& q, int& nbs_shift, const mirai_nf4_weight* w, int E, int N, int K) {
+int nf4_key(CUtensorMap& m, QKey& q, int& nbs_shift, const mirai_nf4_weight* w, int E, int rows, int cols, bool mn) {
   if (!w || !w->packed || !w->absmax || !w->nested_absmax || !w->offset || !w->code || !w->nested_code)
     return set_error(MIRAI_ERR_INVALID_ARG, "nf4 weight: null buffer");
-  if (w->blocksize != BK)
+  if (w->blocksize != 64)
     return set_error(MIRAI_ERR_UNSUPPORTED, "nf4 weight: blocksize %d (the fused kernel decodes blocksize 64)",
                      w->blocksize);
-  if (w->nested_blocksize <= 0 || (w->nested_blocksize & (w->nested_blocksize - 1)) != 0)
-    return set_error(MIRAI_ERR_UNSUPPORTED, "nf4 weight: nested blocksize %d is not a power of two",
+  if (w->nested_blocksize < 64 || (w->nested_blocksize & (w->nested_blocksize - 1)) != 0)
+    return set_error(MIRAI_ERR_UNSUPPORTED, "nf4 weight: nested blocksize %d is not a power of two >= 64",
                      w->nested_blocksize);
-  if (K / BK > kMaxKBlocks)
-    return set_error(MIRAI_ERR_UNSUPPORTED, "nf4 weight: in_features %d exceeds %d", K, BK * kMaxKBlocks);
+  if (cols % 64 != 0) return set_error(MIRAI_ERR_UNSUPPORTED, "nf4 weight: in_features %d %% 64 != 0", cols);
   if (mis16(w->absmax)) return set_error(MIRAI_ERR_INVALID_ARG, "nf4 weight: absmax codes not 16-byte aligned");
   nbs_shift = __builtin_ctz((unsigned)w->nested_blocksize);
-  const int64_t blocks_per_expert = (int64_t)N * K / BK;
+  const int64_t blocks_per_expert = (int64_t)rows * cols / 64;
   q.absmax = w->absmax;
   q.nested_absmax = w->nested_absmax;
   q.offset = w->offset;
@@ -582,107 +767,154 @@ int nf4_half(CUtensorMap& m, QHalf& q, int& nbs_shift, const mirai_nf4_weight* w
   q.nested_code = w->nested_code;
   q.scale = nullptr;
   q.n_nested = (int)((blocks_per_expert + w->nested_blocksize - 1) / w->nested_blocksize);
-  // packed nibbles as a [E*N rows, K/2 bytes] byte tensor; one box = 128 rows x 32 bytes
-  return make_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->packed, (uint64_t)K / 2, (uint64_t)E * N,
-                      (uint64_t)K / 2, BK / 2, BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (q.n_nested > kMaxNested)
+    return set_error(MIRAI_ERR_UNSUPPORTED, "nf4 weight: %d nested absmax blocks per expert (max %d)", q.n_nested,
+                     kMaxNested);
+  // packed nibbles as a [E*rows, cols/2] byte tensor; boxes of one 64-element
+  // block per row: 128 rows (K-major) or 64 rows (MN-major)
+  return make_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->packed, (uint64_t)cols / 2, (uint64_t)E * rows,
+                      (uint64_t)cols / 2, 32, mn ? 64 : BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-int int8_half(CUtensorMap& m, QHalf& q, const mirai_int8_weight* w, int E, int N, int K) {
+int int8_key(CUtensorMap& m, QKey& q, const mirai_int8_weight* w, int E, int rows, int cols, bool mn) {
   if (!w || !w->q || !w->scale) return set_error(MIRAI_ERR_INVALID_ARG, "int8 weight: null buffer");
-  q = QHalf{};
+  q = QKey{};
   q.scale = w->scale;
-  return make_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->q, (uint64_t)K, (uint64_t)E * N, (uint64_t)K, BK,
-                      BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+  return make_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->q, (uint64_t)cols, (uint64_t)E * rows, (uint64_t)cols,
+                      64, mn ? 64 : BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
+
+// Bind one weight key in any format.  rows x cols is one expert's matrix.
+struct WeightArg {
+  int fmt;
+  const void* bf16;
+  const mirai_nf4_weight* nf4;
+  const mirai_int8_weight* int8;
+};
+
+int bind_key(const WeightArg& w, CUtensorMap& m, QKey& q, int& shift, int E, int rows, int cols, bool mn) {
+  if (w.fmt == W_BF16) return bf16_weight_map(m, w.bf16, E, rows, cols, mn);
+  if (w.fmt == W_NF4) return nf4_key(m, q, shift, w.nf4, E, rows, cols, mn);
+  return int8_key(m, q, w.int8, E, rows, cols, mn);
+}
+
+template <int MODE>
+int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t S, int K, int N, void* out,
+        void* gate_up, const WeightArg& w0, const WeightArg& w1, int rows, int cols, mirai_stream_t stream) {
+  if (S == 0 && E > 0) return MIRAI_OK;
+  Params p;
+  CUtensorMap ta, t0, t1;
+  int rc = prepare<MODE>(name, a, offsets, E, S, K, N, out, gate_up, p, ta);
+  constexpr bool MN = MCfg<MODE>::MN;
+  if (!rc && MN && w0.fmt != W_BF16 && K > kMaxK)
+    rc = set_error(MIRAI_ERR_UNSUPPORTED, "%s: reduction length %d exceeds %d", name, K, kMaxK);
+  if (!rc && !MN && w0.fmt != W_BF16 && K > kMaxK)
+    rc = set_error(MIRAI_ERR_UNSUPPORTED, "%s: in_features %d exceeds %d", name, K, kMaxK);
+  int s0 = 8, s1 = 8;
+  if (!rc) rc = bind_key(w0, t0, p.q[0], s0, E, rows, cols, MN);
+  if (!rc && MCfg<MODE>::TWO_KEYS) rc = bind_key(w1, t1, p.q[1], s1, E, rows, cols, MN);
+  if (!rc && MCfg<MODE>::TWO_KEYS && s0 != s1)
+    rc = set_error(MIRAI_ERR_UNSUPPORTED, "%s: the two keys use different nested blocksizes", name);
+  if (rc) return rc;
+  if (!MCfg<MODE>::TWO_KEYS) {
+    t1 = t0;
+    p.q[1] = p.q[0];
+  }
+  p.nbs_shift = s0;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (w0.fmt) {
+    case W_BF16: return launch<MODE, W_BF16>(ta, t0, t1, p, st);
+    case W_NF4: return launch<MODE, W_NF4>(ta, t0, t1, p, st);
+    default: return launch<MODE, W_INT8>(ta, t0, t1, p, st);
+  }
+}
+
+inline WeightArg wb(const void* w) { return WeightArg{W_BF16, w, nullptr, nullptr}; }
+inline WeightArg wn(const mirai_nf4_weight* w) { return WeightArg{W_NF4, nullptr, w, nullptr}; }
+inline WeightArg wi(const mirai_int8_weight* w) { return WeightArg{W_INT8, nullptr, nullptr, w}; }
 
 }  // namespace gg
 }  // namespace mirai
 
-using namespace mirai;
 using namespace mirai::gg;
 
 extern "C" {
 
+// ---- forward: gate/up + SwiGLU.  B = W1/W3 [E, I, H]: rows I, cols H.
 int mirai_moe_gateup_swiglu_bf16(const void* x_sorted, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
                                  int32_t hidden, int32_t inter, const void* w1, const void* w3, void* h,
                                  void* gate_up, mirai_stream_t stream) {
-  Params p;
-  CUtensorMap ta, t0, t1;
-  if (num_rows == 0 && num_experts > 0) return MIRAI_OK;
-  int rc = prepare<GATEUP>("gateup_swiglu_bf16", x_sorted, offsets, num_experts, num_rows, hidden, inter, h, gate_up,
-                           p, ta);
-  if (!rc) rc = bf16_weight_map(t0, w1, num_experts, inter, hidden);
-  if (!rc) rc = bf16_weight_map(t1, w3, num_experts, inter, hidden);
-  if (rc) return rc;
-  return launch<GATEUP, W_BF16>(ta, t0, t1, p, reinterpret_cast<cudaStream_t>(stream));
+  return run<GATEUP>("gateup_swiglu_bf16", x_sorted, offsets, num_experts, num_rows, hidden, inter, h, gate_up,
+                     wb(w1), wb(w3), inter, hidden, stream);
 }
-
 int mirai_moe_gateup_swiglu_nf4(const void* x_sorted, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
                                 int32_t hidden, int32_t inter, const mirai_nf4_weight* w1, const mirai_nf4_weight* w3,
                                 void* h, void* gate_up, mirai_stream_t stream) {
-  Params p;
-  CUtensorMap ta, t0, t1;
-  if (num_rows == 0 && num_experts > 0) return MIRAI_OK;
-  int rc = prepare<GATEUP>("gateup_swiglu_nf4", x_sorted, offsets, num_experts, num_rows, hidden, inter, h, gate_up,
-                           p, ta);
-  int s0 = 8, s1 = 8;
-  if (!rc) rc = nf4_half(t0, p.q[0], s0, w1, num_experts, inter, hidden);
-  if (!rc) rc = nf4_half(t1, p.q[1], s1, w3, num_experts, inter, hidden);
-  if (!rc && s0 != s1) rc = set_error(MIRAI_ERR_UNSUPPORTED, "gateup_swiglu_nf4: w1/w3 nested blocksizes differ");
-  if (rc) return rc;
-  p.nbs_shift = s0;
-  return launch<GATEUP, W_NF4>(ta, t0, t1, p, reinterpret_cast<cudaStream_t>(stream));
+  return run<GATEUP>("gateup_swiglu_nf4", x_sorted, offsets, num_experts, num_rows, hidden, inter, h, gate_up,
+                     wn(w1), wn(w3), inter, hidden, stream);
 }
-
 int mirai_moe_gateup_swiglu_int8(const void* x_sorted, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
                                  int32_t hidden, int32_t inter, const mirai_int8_weight* w1,
                                  const mirai_int8_weight* w3, void* h, void* gate_up, mirai_stream_t stream) {
-  Params p;
-  CUtensorMap ta, t0, t1;
-  if (num_rows == 0 && num_experts > 0) return MIRAI_OK;
-  int rc = prepare<GATEUP>("gateup_swiglu_int8", x_sorted, offsets, num_experts, num_rows, hidden, inter, h, gate_up,
-                           p, ta);
-  if (!rc) rc = int8_half(t0, p.q[0], w1, num_experts, inter, hidden);
-  if (!rc) rc = int8_half(t1, p.q[1], w3, num_experts, inter, hidden);
-  if (rc) return rc;
-  return launch<GATEUP, W_INT8>(ta, t0, t1, p, reinterpret_cast<cudaStream_t>(stream));
+  return run<GATEUP>("gateup_swiglu_int8", x_sorted, offsets, num_experts, num_rows, hidden, inter, h, gate_up,
+                     wi(w1), wi(w3), inter, hidden, stream);
 }
 
+// ---- forward: down.  B = W2 [E, H, I]: rows H, cols I.
 int mirai_moe_down_bf16(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows, int32_t inter,
                         int32_t hidden, const void* w2, void* y, mirai_stream_t stream) {
-  Params p;
-  CUtensorMap ta, t0;
-  if (num_rows == 0 && num_experts > 0) return MIRAI_OK;
-  int rc = prepare<DOWN>("down_bf16", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, p, ta);
-  if (!rc) rc = bf16_weight_map(t0, w2, num_experts, hidden, inter);
-  if (rc) return rc;
-  return launch<DOWN, W_BF16>(ta, t0, t0, p, reinterpret_cast<cudaStream_t>(stream));
+  return run<DOWN>("down_bf16", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, wb(w2), wb(w2), hidden,
+                   inter, stream);
 }
-
 int mirai_moe_down_nf4(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows, int32_t inter,
                        int32_t hidden, const mirai_nf4_weight* w2, void* y, mirai_stream_t stream) {
-  Params p;
-  CUtensorMap ta, t0;
-  if (num_rows == 0 && num_experts > 0) return MIRAI_OK;
-  int rc = prepare<DOWN>("down_nf4", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, p, ta);
-  int s = 8;
-  if (!rc) rc = nf4_half(t0, p.q[0], s, w2, num_experts, hidden, inter);
-  if (rc) return rc;
-  p.q[1] = p.q[0];
-  p.nbs_shift = s;
-  return launch<DOWN, W_NF4>(ta, t0, t0, p, reinterpret_cast<cudaStream_t>(stream));
+  return run<DOWN>("down_nf4", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, wn(w2), wn(w2), hidden,
+                   inter, stream);
 }
-
 int mirai_moe_down_int8(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows, int32_t inter,
                         int32_t hidden, const mirai_int8_weight* w2, void* y, mirai_stream_t stream) {
-  Params p;
-  CUtensorMap ta, t0;
-  if (num_rows == 0 && num_experts > 0) return MIRAI_OK;
-  int rc = prepare<DOWN>("down_int8", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, p, ta);
-  if (!rc) rc = int8_half(t0, p.q[0], w2, num_experts, hidden, inter);
-  if (rc) return rc;
-  p.q[1] = p.q[0];
-  return launch<DOWN, W_INT8>(ta, t0, t0, p, reinterpret_cast<cudaStream_t>(stream));
+  return run<DOWN>("down_int8", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, wi(w2), wi(w2), hidden,
+                   inter, stream);
+}
+
+// ---- dX: down.  dh = dy W2 (K = H, N = I), SwiGLU backward fused.  B = W2 read MN-major.
+int mirai_moe_down_dx_bf16(const void* grad_y, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                           int32_t hidden, int32_t inter, const void* w2, const void* gate_up, void* grad_gate_up,
+                           mirai_stream_t stream) {
+  return run<DXDOWN>("down_dx_bf16", grad_y, offsets, num_experts, num_rows, hidden, inter, grad_gate_up,
+                     const_cast<void*>(gate_up), wb(w2), wb(w2), hidden, inter, stream);
+}
+int mirai_moe_down_dx_nf4(const void* grad_y, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                          int32_t hidden, int32_t inter, const mirai_nf4_weight* w2, const void* gate_up,
+                          void* grad_gate_up, mirai_stream_t stream) {
+  return run<DXDOWN>("down_dx_nf4", grad_y, offsets, num_experts, num_rows, hidden, inter, grad_gate_up,
+                     const_cast<void*>(gate_up), wn(w2), wn(w2), hidden, inter, stream);
+}
+int mirai_moe_down_dx_int8(const void* grad_y, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                           int32_t hidden, int32_t inter, const mirai_int8_weight* w2, const void* gate_up,
+                           void* grad_gate_up, mirai_stream_t stream) {
+  return run<DXDOWN>("down_dx_int8", grad_y, offsets, num_experts, num_rows, hidden, inter, grad_gate_up,
+                     const_cast<void*>(gate_up), wi(w2), wi(w2), hidden, inter, stream);
+}
+
+// ---- dX: gate/up.  dx = [dgate | dup] [W1 ; W3] (K = 2I, N = H).  B = W1/W3 read MN-major.
+int mirai_moe_gateup_dx_bf16(const void* grad_gate_up, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                             int32_t inter, int32_t hidden, const void* w1, const void* w3, void* dx_sorted,
+                             mirai_stream_t stream) {
+  return run<DXGATEUP>("gateup_dx_bf16", grad_gate_up, offsets, num_experts, num_rows, 2 * inter, hidden, dx_sorted,
+                       nullptr, wb(w1), wb(w3), inter, hidden, stream);
+}
+int mirai_moe_gateup_dx_nf4(const void* grad_gate_up, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                            int32_t inter, int32_t hidden, const mirai_nf4_weight* w1, const mirai_nf4_weight* w3,
+                            void* dx_sorted, mirai_stream_t stream) {
+  return run<DXGATEUP>("gateup_dx_nf4", grad_gate_up, offsets, num_experts, num_rows, 2 * inter, hidden, dx_sorted,
+                       nullptr, wn(w1), wn(w3), inter, hidden, stream);
+}
+int mirai_moe_gateup_dx_int8(const void* grad_gate_up, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                             int32_t inter, int32_t hidden, const mirai_int8_weight* w1, const mirai_int8_weight* w3,
+                             void* dx_sorted, mirai_stream_t stream) {
+  return run<DXGATEUP>("gateup_dx_int8", grad_gate_up, offsets, num_experts, num_rows, 2 * inter, hidden, dx_sorted,
+                       nullptr, wi(w1), wi(w3), inter, hidden, stream);
 }
 
 }  // extern "C"

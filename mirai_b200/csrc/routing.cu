@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint4* __restrict__ 
   float wt[kMaxTopK];
   for (int j = 0; j < k; ++j) {
     pos[j] = inv[t * k + j];
-    wt[j] = w[t * k + j];
+    wt[j] = w ? w[t * k + j] : 1.f;
     if (pos[j] < 0 || pos[j] >= S) {
       if (lane == 0) device_fail(MIRAI_ERR_DEVICE_BOUNDS, 800);
       return;
@@ -327,6 +327,48 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint4* __restrict__ 
       o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
       o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
+  }
+}
+
+// ============================================================================
+// a8 backward: one warp per token.  grad_y rows are written in place of the
+// token's routes; the score gradient is an fp32 dot product per route.
+// ============================================================================
+__global__ void __launch_bounds__(256) combine_backward_kernel(const uint4* __restrict__ g, const uint4* __restrict__ y,
+                                                               const int64_t* __restrict__ inv,
+                                                               const float* __restrict__ w, int64_t T, int k, int H,
+                                                               int64_t S, uint4* __restrict__ gy,
+                                                               float* __restrict__ gw) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const int vec_per_row = H / 8;
+  for (int j = 0; j < k; ++j) {
+    const int64_t pos = inv[t * k + j];
+    if (pos < 0 || pos >= S) {
+      if (lane == 0) device_fail(MIRAI_ERR_DEVICE_BOUNDS, 810);
+      return;
+    }
+    const float wt = w[t * k + j];
+    float dot = 0.f;
+    for (int v = lane; v < vec_per_row; v += 32) {
+      const uint4 gu = __ldg(g + t * vec_per_row + v);
+      const uint4 yu = __ldg(y + pos * vec_per_row + v);
+      const uint32_t gw4[4] = {gu.x, gu.y, gu.z, gu.w};
+      const uint32_t yw4[4] = {yu.x, yu.y, yu.z, yu.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float g0 = bf16_lo(gw4[q]), g1 = bf16_hi(gw4[q]);
+        dot = fmaf(g0, bf16_lo(yw4[q]), dot);
+        dot = fmaf(g1, bf16_hi(yw4[q]), dot);
+        o[q] = pack_bf16x2(g0 * wt, g1 * wt);
+      }
+      gy[pos * vec_per_row + v] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    if (lane == 0) gw[t * k + j] = dot;
   }
 }
 
@@ -429,13 +471,29 @@ int mirai_moe_combine(const void* y_sorted, const int64_t* inverse_order, const 
   if (out_dtype != MIRAI_DTYPE_BF16 && out_dtype != MIRAI_DTYPE_F32)
     return set_error(MIRAI_ERR_INVALID_ARG, "combine: unknown out_dtype %d", out_dtype);
   if (num_tokens == 0) return MIRAI_OK;
-  if (!y_sorted || !inverse_order || !top_weights || !out || misaligned16(y_sorted) || misaligned16(out))
+  if (!y_sorted || !inverse_order || !out || misaligned16(y_sorted) || misaligned16(out))
     return set_error(MIRAI_ERR_INVALID_ARG, "combine: null or misaligned pointer");
   const int blocks = (int)((num_tokens + 7) / 8);
   combine_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(y_sorted), inverse_order, top_weights, num_tokens, top_k, hidden,
       num_tokens * top_k, out, out_dtype);
   return check_launch("combine");
+}
+
+int mirai_moe_combine_backward(const void* grad_out, const void* y_sorted, const int64_t* inverse_order,
+                               const float* top_weights, int64_t num_tokens, int32_t top_k, int32_t hidden,
+                               void* grad_y_sorted, float* grad_weights, mirai_stream_t stream) {
+  if (num_tokens < 0 || top_k <= 0 || top_k > kMaxTopK || hidden <= 0 || hidden % 8 != 0)
+    return set_error(MIRAI_ERR_INVALID_ARG, "combine_backward: need 0 < k <= %d and hidden %% 8 == 0", kMaxTopK);
+  if (num_tokens == 0) return MIRAI_OK;
+  if (!grad_out || !y_sorted || !inverse_order || !top_weights || !grad_y_sorted || !grad_weights ||
+      misaligned16(grad_out) || misaligned16(y_sorted) || misaligned16(grad_y_sorted))
+    return set_error(MIRAI_ERR_INVALID_ARG, "combine_backward: null or misaligned pointer");
+  const int blocks = (int)((num_tokens + 7) / 8);
+  combine_backward_kernel<<<blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(grad_out), static_cast<const uint4*>(y_sorted), inverse_order, top_weights,
+      num_tokens, top_k, hidden, num_tokens * top_k, static_cast<uint4*>(grad_y_sorted), grad_weights);
+  return check_launch("combine_backward");
 }
 
 }  // extern "C"

@@ -252,18 +252,84 @@ def down(h: torch.Tensor, offsets: torch.Tensor, w2, *, hidden: int, out: torch.
 
 # ----------------------------------------------------------------------------- a8
 
-def combine(y_sorted: torch.Tensor, inverse_order: torch.Tensor, top_weights: torch.Tensor,
-            out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+def combine(y_sorted: torch.Tensor, inverse_order: torch.Tensor, top_weights: torch.Tensor | None,
+            out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None,
+            top_k: int | None = None) -> torch.Tensor:
+    """Weighted un-permute; ``top_weights=None`` sums the routes (permute backward)."""
     y_sorted = _cuda(y_sorted, "y_sorted", torch.bfloat16)
     inv = _cuda(inverse_order, "inverse_order", torch.int64)
-    w = _cuda(top_weights.float(), "top_weights", torch.float32)
-    T, k = w.shape
+    if top_weights is None:
+        k = int(top_k)
+        T = inv.numel() // k
+        w = None
+    else:
+        w = _cuda(top_weights.float(), "top_weights", torch.float32)
+        T, k = w.shape
     H = y_sorted.shape[1]
     if out is None:
         out = torch.empty((T, H), dtype=out_dtype, device=y_sorted.device)
     code = {torch.bfloat16: 0, torch.float32: 1}[out.dtype]
     _lib.call("mirai_moe_combine", _ptr(y_sorted), _ptr(inv), _ptr(w), T, k, H, _ptr(out), code, _stream())
     return out
+
+
+def combine_backward(grad_out: torch.Tensor, y_sorted: torch.Tensor, inverse_order: torch.Tensor,
+                     top_weights: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """(grad_y_sorted bf16 [S, H], grad_weights fp32 [T, k]) (dispatch_ops.py:36-44)."""
+    g = _cuda(grad_out.to(torch.bfloat16), "grad_out", torch.bfloat16)
+    y_sorted = _cuda(y_sorted, "y_sorted", torch.bfloat16)
+    inv = _cuda(inverse_order, "inverse_order", torch.int64)
+    w = _cuda(top_weights.float(), "top_weights", torch.float32)
+    T, k = w.shape
+    H = y_sorted.shape[1]
+    gy = torch.empty_like(y_sorted)
+    gw = torch.empty((T, k), dtype=torch.float32, device=y_sorted.device)
+    _lib.call("mirai_moe_combine_backward", _ptr(g), _ptr(y_sorted), _ptr(inv), _ptr(w), T, k, H, _ptr(gy),
+              _ptr(gw), _stream())
+    return gy, gw
+
+
+# ----------------------------------------------------------------------------- a9 dX
+
+def _fmt_suffix(w) -> str:
+    if isinstance(w, torch.Tensor):
+        return "bf16"
+    if isinstance(w, _lib.Nf4Weight):
+        return "nf4"
+    if isinstance(w, _lib.Int8Weight):
+        return "int8"
+    raise TypeError(f"unsupported weight type {type(w)}")
+
+
+def _wptr(w):
+    return _ptr(_cuda(w, "weight", torch.bfloat16)) if isinstance(w, torch.Tensor) else w
+
+
+def down_dx(grad_y: torch.Tensor, offsets: torch.Tensor, w2, gate_up: torch.Tensor, *, inter: int,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """grad_gate_up [S, 2I] = SwiGLU backward of (gate, up) given dh = grad_y W2."""
+    w2 = _as_weight(w2)
+    gy = _cuda(grad_y, "grad_y", torch.bfloat16)
+    offsets = _cuda(offsets, "offsets", torch.int32)
+    gu = _cuda(gate_up, "gate_up", torch.bfloat16)
+    S, H = gy.shape
+    dgu = out if out is not None else torch.empty((S, 2 * inter), dtype=torch.bfloat16, device=gy.device)
+    _lib.call(f"mirai_moe_down_dx_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), offsets.numel(), S, H, inter,
+              _wptr(w2), _ptr(gu), _ptr(dgu), _stream())
+    return dgu
+
+
+def gateup_dx(grad_gate_up: torch.Tensor, offsets: torch.Tensor, w1, w3, *, hidden: int,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """dx_sorted [S, H] = dgate W1 + dup W3 per expert segment."""
+    w1, w3 = _as_weight(w1), _as_weight(w3)
+    dgu = _cuda(grad_gate_up, "grad_gate_up", torch.bfloat16)
+    offsets = _cuda(offsets, "offsets", torch.int32)
+    S, I2 = dgu.shape
+    dxs = out if out is not None else torch.empty((S, hidden), dtype=torch.bfloat16, device=dgu.device)
+    _lib.call(f"mirai_moe_gateup_dx_{_fmt_suffix(w1)}", _ptr(dgu), _ptr(offsets), offsets.numel(), S, I2 // 2,
+              hidden, _wptr(w1), _wptr(w3), _ptr(dxs), _stream())
+    return dxs
 
 
 # ----------------------------------------------------------------------------- whole forward
@@ -276,3 +342,38 @@ def moe_forward(tokens: torch.Tensor, top_indices: torch.Tensor, top_weights: to
     h = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter)
     y = down(h, plan.offsets, w2, hidden=tokens.shape[1])
     return combine(y, plan.inverse_order, top_weights, out_dtype=tokens.dtype)
+
+
+@dataclass
+class ForwardState:
+    """What the dX pass needs from the forward (no dense weights are kept)."""
+
+    plan: DispatchPlan
+    y_sorted: torch.Tensor   # [S, H] bf16 expert outputs
+    gate_up: torch.Tensor    # [S, 2I] bf16 saved pre-activations
+    top_weights: torch.Tensor
+
+
+def moe_forward_train(tokens, top_indices, top_weights, w1, w3, w2, *, num_experts: int, inter: int,
+                      out_dtype: torch.dtype | None = None):
+    """Forward that also returns the state the dX pass consumes."""
+    plan = dispatch_plan(top_indices, num_experts)
+    xs = permute_rows(tokens, plan.sorted_token_indices)
+    h, gu = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter, save_gate_up=True)
+    y = down(h, plan.offsets, w2, hidden=tokens.shape[1])
+    out = combine(y, plan.inverse_order, top_weights, out_dtype=out_dtype or tokens.dtype)
+    return out, ForwardState(plan, y, gu, top_weights.float())
+
+
+def moe_backward_dx(grad_out: torch.Tensor, state: ForwardState, w1, w3, w2, *, inter: int,
+                    out_dtype: torch.dtype = torch.bfloat16):
+    """Input gradient through the frozen experts and the top-weight gradient.
+
+    grad_out [T, H] -> (dx [T, H], d_top_weights fp32 [T, k])."""
+    plan = state.plan
+    H = state.y_sorted.shape[1]
+    gy, gw = combine_backward(grad_out, state.y_sorted, plan.inverse_order, state.top_weights)
+    dgu = down_dx(gy, plan.offsets, w2, state.gate_up, inter=inter)
+    dxs = gateup_dx(dgu, plan.offsets, w1, w3, hidden=H)
+    dx = combine(dxs, plan.inverse_order, None, out_dtype=out_dtype, top_k=plan.top_k)
+    return dx, gw

@@ -228,7 +228,8 @@ def int8_to_device(q, s, dev):
 
 @pytest.mark.parametrize("fmt", ["nf4", "int8"])
 @pytest.mark.parametrize("E,H,I,S,skew", [(4, 256, 256, 700, False), (8, 512, 384, 3000, True),
-                                          (2, 1024, 1408, 400, False), (3, 3072, 1024, 500, True)])
+                                          (2, 1024, 1408, 400, False), (3, 3072, 1024, 500, True),
+                                          (3, 384, 256, 400, False)])
 def test_quantized_gemms_match_dequant_then_matmul(fmt, E, H, I, S, skew):
     dev = _dev()
     from mirai_b200 import ops
@@ -317,3 +318,60 @@ def test_int8_quantizer_matches_reference_golden(golden, dtype):
         q, s, _ = oq.int8_quantize(w.float().numpy(), 0)
         np.testing.assert_array_equal(got.q.cpu().numpy(), q)
         np.testing.assert_array_equal(got.scale.cpu().numpy(), s)
+
+
+# ----------------------------------------------------------------------------- a9: dX
+
+def _weights(fmt, rng, E, H, I, dev, std=0.05):
+    raw = [(rng.standard_normal(shape) * std).astype(np.float32) for shape in ((E, I, H), (E, I, H), (E, H, I))]
+    if fmt == "nf4":
+        gs = [oq.nf4_quantize_grouped(w) for w in raw]
+        return [oq.nf4_dequantize_grouped(g) for g in gs], [nf4_to_device(g, dev) for g in gs]
+    if fmt == "int8":
+        qs = [oq.int8_quantize(w, 0) for w in raw]
+        return ([oq.bf16_round(oq.int8_dequantize(q, s, 0)) for q, s, _ in qs],
+                [int8_to_device(q, s, dev) for q, s, _ in qs])
+    dense = [oq.bf16_round(w) for w in raw]
+    return dense, [_bf16(w).to(dev) for w in dense]
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "nf4", "int8"])
+@pytest.mark.parametrize("T,H,E,k,I", [(512, 256, 8, 2, 512), (300, 512, 6, 3, 1408), (700, 1024, 16, 4, 384)])
+def test_moe_forward_and_dx_match_oracle(fmt, T, H, E, k, I):
+    dev = _dev()
+    from mirai_b200 import ops
+    rng = np.random.default_rng(T + H + I)
+    x = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    logits = (rng.standard_normal((T, E)) * 1.5).astype(np.float32)
+    dense, dw = _weights(fmt, rng, E, H, I, dev)
+    g = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    idx, w = ops.route_topk(torch.from_numpy(logits).to(dev), k)
+    out, st = ops.moe_forward_train(_bf16(x).to(dev), idx, w, *dw, num_experts=E, inter=I)
+    dx, dwts = ops.moe_backward_dx(_bf16(g).to(dev), st, *dw, inter=I)
+    _check(ops)
+    ridx, rw = om.route_topk(logits, k)
+    ref = om.moe_forward(x, ridx, rw, *dense, bf16=True)
+    rdx, rdw = om.moe_backward_dx(x, ridx, rw, *dense, g, bf16=True)
+    assert om.rel_max_err(_f32(out), ref) < TOL
+    assert om.rel_max_err(_f32(dx), rdx) < 3e-2
+    assert om.rel_max_err(_f32(dwts), rdw) < 3e-2
+
+
+def test_dx_matches_reference_golden(golden):
+    """dX and top-score gradients against the reference's own autograd (bf16 experts)."""
+    dev = _dev()
+    from mirai_b200 import ops
+    g = golden("routed_dense_bf16")
+    x = oq.bf16_bits_to_f32(g["tokens"])
+    w1, w3, w2 = (oq.bf16_bits_to_f32(g[k]) for k in ("w1", "w3", "w2"))
+    scores = oq.bf16_bits_to_f32(g["top_scores"])
+    idx = torch.from_numpy(g["top_indices"]).to(dev)
+    E, I, H = w1.shape
+    out, st = ops.moe_forward_train(_bf16(x).to(dev), idx, torch.from_numpy(scores).to(dev),
+                                    _bf16(w1).to(dev), _bf16(w3).to(dev), _bf16(w2).to(dev), num_experts=E, inter=I)
+    dx, dws = ops.moe_backward_dx(_bf16(oq.bf16_bits_to_f32(g["grad"])).to(dev), st, _bf16(w1).to(dev),
+                                  _bf16(w3).to(dev), _bf16(w2).to(dev), inter=I)
+    _check(ops)
+    assert om.rel_max_err(_f32(out), oq.bf16_bits_to_f32(g["out"])) < TOL
+    assert om.rel_max_err(_f32(dx), oq.bf16_bits_to_f32(g["grad_tokens"])) < 3e-2
+    assert om.rel_max_err(_f32(dws), oq.bf16_bits_to_f32(g["grad_scores"])) < 3e-2
