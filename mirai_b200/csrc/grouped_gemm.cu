@@ -8,23 +8,29 @@
 //   DXDOWN    dgu = swiglu_bwd(dy W2, gate, up)       B = W2 columns  (MN-major)
 //   DXGATEUP  dx = dgate W1 + dup W3                  B = W1;W3       (MN-major)
 //
-// One CTA per SM, warp-specialised:
+// Warp roles in every CTA:
 //   warp 0        TMA producer: A tiles; B tiles (bf16) or raw codes (NF4/INT8)
 //   warp 1        UMMA issuer (one thread) and TMEM owner
 //   warps 2..5    epilogue: TMEM -> registers -> SwiGLU (+bwd) / bf16 -> global
 //   warps 6..13   (NF4 / INT8) dequantisers: raw codes in shared memory ->
 //                 exact bf16 weights in the UMMA operand layout
-// A/B ring of STAGES shared-memory slots; two TMEM accumulators (2 x 256
-// fp32 columns) overlap the epilogue of tile i with the main loop of tile
-// i+1.  Tiles are (expert, 128-row block, 256-column block), expert-major
-// with the column block fastest, so CTAs running together share one expert's
-// weights in L2.
+// Two TMEM accumulators (2 x 256 fp32 columns) overlap the epilogue of tile i
+// with the main loop of tile i+1.  Tiles are (expert, row block, 256-column
+// block), expert-major with the column block fastest so that the CTAs running
+// together share one expert's weights in L2.
 //
-// Operand layouts (128-byte swizzle):
+// PAIR = true runs each tile on a CTA pair (cluster of 2, tcgen05 cta_group::2):
+// a 256-row x 256-column tile whose A rows are split between the two SMs
+// (128 each) and whose B operand is split along N (128 columns each), so
+// each SM stages, and for NF4/INT8 decodes, only half of B.  The even CTA
+// issues the M=256 UMMAs; completion is multicast to both CTAs.  No TMA
+// multicast is used.  PAIR = false is the single-SM 128-row variant.
+//
+// Operand layouts (128-byte swizzle), per CTA:
 //   A  [128 rows][64 k] K-major = 16 KB
-//   B  K-major:  [256 rows][64 k]            (8-row x 128 B atoms, SBO 1 KB)
-//      MN-major: [4 x 64 n][64 k rows]       (atoms 8 k-rows x 64 n; LBO 8 KB
-//                                             between 64-n blocks, SBO 1 KB)
+//   B  K-major:  [B_ROWS rows][64 k]           (8-row x 128 B atoms, SBO 1 KB)
+//      MN-major: [B_ROWS/64 x 64 n][64 k rows] (atoms 8 k-rows x 64 n; LBO 8 KB
+//                                               between 64-n blocks, SBO 1 KB)
 // Dequantisation is bit-exact with the reference's dequantise-then-matmul:
 //   NF4  w = bf16( code[nibble] * (ncode[q] * nabsmax + offset) )  (quant.py:413-431)
 //   INT8 w = bf16( q * scale[row] )                                 (quant.py:238-260, g = 0)
@@ -34,12 +40,11 @@
 namespace mirai {
 namespace gg {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
+constexpr int BM = 128;  // rows of A per CTA
+constexpr int BN = 256;  // output columns per tile
 constexpr int BK = 64;
 constexpr int UMMA_K = 16;
 constexpr uint32_t A_BYTES = BM * BK * 2;
-constexpr uint32_t B_BYTES = BN * BK * 2;
 constexpr int kEpiWarps = 4;
 constexpr int kDeqWarps = 8;
 constexpr int kDeqThreads = 32 * kDeqWarps;
@@ -56,24 +61,17 @@ template <int MODE> struct MCfg {
   static constexpr bool TWO_KEYS = MODE == GATEUP || MODE == DXGATEUP;
 };
 
-template <int WF> struct Cfg;
-template <> struct Cfg<W_BF16> {
-  static constexpr int STAGES = 4;
-  static constexpr uint32_t RAW_BYTES = 0;
-  static constexpr int THREADS = 64 + 32 * kEpiWarps;
-  static constexpr int ROW_BYTES = 0;
-};
-template <> struct Cfg<W_NF4> {
-  static constexpr int STAGES = 3;
-  static constexpr uint32_t RAW_BYTES = BN * BK / 2;  // 8 KB of packed nibbles
-  static constexpr int THREADS = 64 + 32 * (kEpiWarps + kDeqWarps);
-  static constexpr int ROW_BYTES = BK / 2;            // raw bytes of 64 elements
-};
-template <> struct Cfg<W_INT8> {
-  static constexpr int STAGES = 3;
-  static constexpr uint32_t RAW_BYTES = BN * BK;  // 16 KB of int8
-  static constexpr int THREADS = 64 + 32 * (kEpiWarps + kDeqWarps);
-  static constexpr int ROW_BYTES = BK;
+// Per (format, pairing) geometry.
+template <int WF, bool PAIR> struct Cfg {
+  static constexpr int TILE_M = PAIR ? 2 * BM : BM;                      // rows per tile
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;                      // B rows / n-columns per CTA
+  static constexpr uint32_t B_BYTES = B_ROWS * BK * 2;                   // bf16 B per CTA per stage
+  static constexpr int ROW_BYTES = WF == W_NF4 ? BK / 2 : (WF == W_INT8 ? BK : 0);  // raw bytes / 64 elements
+  static constexpr uint32_t RAW_BYTES = B_ROWS * ROW_BYTES;
+  static constexpr int STAGES = WF == W_BF16 ? (PAIR ? 6 : 4) : (PAIR ? 4 : 3);
+  static constexpr int THREADS = 64 + 32 * kEpiWarps + (WF == W_BF16 ? 0 : kDeqThreads);
+  static constexpr int TPR = kDeqThreads / B_ROWS;                       // dequant threads per B row
+  static constexpr int ELEMS = BK / TPR;                                 // elements per dequant thread
 };
 
 // One quantised key (W1, W3 or W2).
@@ -104,12 +102,12 @@ struct Params {
   int nbs_shift;           // log2(nested_blocksize)
 };
 
-template <int WF>
+template <int WF, bool PAIR>
 struct Smem {
-  uint64_t full[Cfg<WF>::STAGES];
-  uint64_t empty[Cfg<WF>::STAGES];
-  uint64_t raw_full[Cfg<WF>::STAGES];
-  uint64_t raw_empty[Cfg<WF>::STAGES];
+  uint64_t full[Cfg<WF, PAIR>::STAGES];
+  uint64_t empty[Cfg<WF, PAIR>::STAGES];
+  uint64_t raw_full[Cfg<WF, PAIR>::STAGES];
+  uint64_t raw_empty[Cfg<WF, PAIR>::STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint32_t tmem_base;
@@ -127,14 +125,15 @@ struct DeqSmem {
   float code[2][16];
 };
 
-template <int WF>
+template <int WF, bool PAIR>
 constexpr size_t smem_bytes() {
-  return 1024 + Cfg<WF>::STAGES * (A_BYTES + B_BYTES + Cfg<WF>::RAW_BYTES) + sizeof(Smem<WF>) +
+  using C = Cfg<WF, PAIR>;
+  return 1024 + C::STAGES * (A_BYTES + C::B_BYTES + C::RAW_BYTES) + sizeof(Smem<WF, PAIR>) +
          (WF == W_BF16 ? 0 : sizeof(DeqSmem));
 }
 
-template <int WF>
-__device__ __forceinline__ void decode_tile(int t, const Smem<WF>& sm, int E, int n_tiles, int& e, int& m,
+template <int WF, bool PAIR>
+__device__ __forceinline__ void decode_tile(int t, const Smem<WF, PAIR>& sm, int E, int n_tiles, int& e, int& m,
                                             int& n) {
   const int mt = t / n_tiles;
   n = t - mt * n_tiles;
@@ -221,18 +220,23 @@ __device__ __forceinline__ void int8_x16(const uint4 r, float scale, uint32_t (&
   }
 }
 
-// K-major modes: weight row (within the [E * out_rows] row space) of B half h.
+// K-major modes: first weight row (within the [E * out_rows] row space) of the
+// 128-row B block `h` of tile (e, n): h = 0/1 are the two 128-row blocks of the
+// 256-column tile (gate/up: W1 and W3 rows n*128..; down: W2 rows n*256 + 128h..).
 template <int MODE>
 __device__ __forceinline__ int kmajor_row(const Params& p, int e, int n, int h) {
   return MODE == GATEUP ? e * p.out_rows + n * (BN / 2) : e * p.out_rows + n * BN + h * (BN / 2);
 }
 
-template <int MODE, int WF>
-__global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
+template <int MODE, int WF, bool PAIR>
+__global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b0,
                         const __grid_constant__ CUtensorMap tmap_b1, const Params p) {
-  constexpr int STAGES = Cfg<WF>::STAGES;
-  constexpr uint32_t RAW_BYTES = Cfg<WF>::RAW_BYTES;
+  using C = Cfg<WF, PAIR>;
+  constexpr int STAGES = C::STAGES;
+  constexpr uint32_t B_BYTES = C::B_BYTES;
+  constexpr uint32_t RAW_BYTES = C::RAW_BYTES;
+  constexpr int TILE_M = C::TILE_M;
   constexpr bool QUANT = WF != W_BF16;
   constexpr bool MN = MCfg<MODE>::MN;
   extern __shared__ uint8_t smem_raw[];
@@ -240,14 +244,22 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
   uint8_t* sA = base;
   uint8_t* sB = sA + STAGES * A_BYTES;
   uint8_t* sRaw = sB + STAGES * B_BYTES;
-  Smem<WF>& sm = *reinterpret_cast<Smem<WF>*>(sRaw + STAGES * RAW_BYTES);
-  DeqSmem* dq = reinterpret_cast<DeqSmem*>(reinterpret_cast<uint8_t*>(&sm) + sizeof(Smem<WF>));
+  Smem<WF, PAIR>& sm = *reinterpret_cast<Smem<WF, PAIR>*>(sRaw + STAGES * RAW_BYTES);
+  DeqSmem* dq = reinterpret_cast<DeqSmem*>(reinterpret_cast<uint8_t*>(&sm) + sizeof(Smem<WF, PAIR>));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int E = p.E;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // position in the CTA pair
+  const bool leader = rank == 0;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // tile-scheduling unit
+  const int num_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  // shared::cluster address of a barrier of this CTA as seen from the pair's leader
+  auto leader_addr = [&](uint64_t* bar) -> uint32_t {
+    return PAIR ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar);
+  };
 
-  // ---- segment table: row_start[e] and exclusive prefix of 128-row blocks
+  // ---- segment table: row_start[e] and exclusive prefix of TILE_M-row blocks
   if (warp == 0) {
     int carry = 0;
     for (int e0 = 0; e0 < E; e0 += 32) {
@@ -257,7 +269,7 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
         const int64_t end = p.offsets[e];
         const int64_t beg = e > 0 ? p.offsets[e - 1] : 0;
         const int64_t endc = end < p.S ? end : p.S;
-        cnt = endc > beg ? (int)((endc - beg + BM - 1) / BM) : 0;
+        cnt = endc > beg ? (int)((endc - beg + TILE_M - 1) / TILE_M) : 0;
         if (end < beg || end > p.S) device_fail(MIRAI_ERR_DEVICE_BOUNDS, 600 + MODE);
         sm.row_start[e] = (int)beg;
       }
@@ -277,22 +289,30 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
   }
   if (warp == 1) {
     if (lane == 0) {
+      const int pair_mult = PAIR ? 2 : 1;
       for (int s = 0; s < STAGES; ++s) {
-        mbar_init(&sm.full[s], QUANT ? 1 + kDeqWarps : 1);
+        // full: the leader's producer arrive (with the bytes of both CTAs) plus
+        // every dequantiser warp of the pair
+        mbar_init(&sm.full[s], 1 + (QUANT ? kDeqWarps * pair_mult : 0));
         mbar_init(&sm.empty[s], 1);
         mbar_init(&sm.raw_full[s], 1);
         mbar_init(&sm.raw_empty[s], kDeqWarps);
       }
       for (int a = 0; a < 2; ++a) {
         mbar_init(&sm.tfull[a], 1);
-        mbar_init(&sm.tempty[a], kEpiWarps);
+        mbar_init(&sm.tempty[a], kEpiWarps * pair_mult);
       }
       sm.abort_flag = 0;
       fence_mbar_init();
     }
     __syncwarp();
-    tmem_alloc(&sm.tmem_base, TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(&sm.tmem_base, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&sm.tmem_base, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_a);
@@ -308,6 +328,7 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA signal
   tc_fence_after();
 
   const uint32_t tmem_base = sm.tmem_base;
@@ -320,35 +341,46 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+      for (int t = unit; t < total_tiles && !*abort_flag; t += num_units) {
         int e, m, n;
-        decode_tile<WF>(t, sm, E, p.n_tiles, e, m, n);
-        const int row0 = sm.row_start[e] + m * BM;
+        decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
+        const int row0 = sm.row_start[e] + m * TILE_M + (int)rank * BM;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&sm.empty[stage], phase ^ 1, 10)) {
             *abort_flag = 1;
             break;
           }
+          const uint32_t full_addr = leader_addr(&sm.full[stage]);
           // B source for this k-block
-          const bool key1 = MCfg<MODE>::TWO_KEYS && (MN ? kb >= p.kb_half : false);
+          const bool key1 = MCfg<MODE>::TWO_KEYS && (MN ? kb >= p.kb_half : (PAIR && rank == 1));
           const CUtensorMap* mb = key1 ? &tmap_b1 : &tmap_b0;
-          const int krow = MN ? e * p.krows + (kb - (key1 ? p.kb_half : 0)) * BK : 0;
+          const int krow = MN ? e * p.krows + (kb - ((MN && key1) ? p.kb_half : 0)) * BK : 0;
+          const int pair_mult = PAIR ? 2 : 1;
+          if (leader) {
+            const uint32_t bytes = pair_mult * (A_BYTES + (QUANT ? 0u : B_BYTES));
+            if (PAIR) mbar_arrive_expect_tx_cluster(full_addr, bytes);
+            else mbar_arrive_expect_tx(&sm.full[stage], bytes);
+          }
+          auto load = [&](void* dst, const CUtensorMap* map, int x, int y) {
+            if (PAIR) tma_load_2d_pair(dst, map, x, y, full_addr);
+            else tma_load_2d(dst, map, x, y, &sm.full[stage]);
+          };
           if (!QUANT) {
-            mbar_arrive_expect_tx(&sm.full[stage], A_BYTES + B_BYTES);
             uint8_t* b_dst = sB + stage * B_BYTES;
             if (MN) {
+              // this CTA's columns: n*256 + rank*B_ROWS + 64*nb
 #pragma unroll
-              for (int nb = 0; nb < 4; ++nb)
-                tma_load_2d(b_dst + nb * (B_BYTES / 4), mb, n * BN + nb * 64, krow, &sm.full[stage]);
+              for (int nb = 0; nb < C::B_ROWS / 64; ++nb)
+                load(b_dst + nb * 8192, mb, n * BN + (int)rank * C::B_ROWS + nb * 64, krow);
+            } else if (PAIR) {
+              // 128 rows per CTA: gate/up -> rank 0 W1, rank 1 W3; down -> W2 rows block `rank`
+              load(b_dst, mb, kb * BK, kmajor_row<MODE>(p, e, n, (int)rank));
             } else {
-              tma_load_2d(b_dst, &tmap_b0, kb * BK, kmajor_row<MODE>(p, e, n, 0), &sm.full[stage]);
-              tma_load_2d(b_dst + B_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * BK,
-                          kmajor_row<MODE>(p, e, n, 1), &sm.full[stage]);
+              load(b_dst, &tmap_b0, kb * BK, kmajor_row<MODE>(p, e, n, 0));
+              load(b_dst + B_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * BK, kmajor_row<MODE>(p, e, n, 1));
             }
-          } else {
-            mbar_arrive_expect_tx(&sm.full[stage], A_BYTES);
           }
-          tma_load_2d(sA + stage * A_BYTES, &tmap_a, kb * BK, row0, &sm.full[stage]);
+          load(sA + stage * A_BYTES, &tmap_a, kb * BK, row0);
           if (QUANT) {
             if (!mbar_wait(&sm.raw_empty[stage], phase ^ 1, 11)) {
               *abort_flag = 1;
@@ -356,11 +388,14 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
             }
             mbar_arrive_expect_tx(&sm.raw_full[stage], RAW_BYTES);
             uint8_t* r_dst = sRaw + stage * RAW_BYTES;
-            constexpr int RB = Cfg<WF>::ROW_BYTES;
+            constexpr int RB = C::ROW_BYTES;
             if (MN) {
 #pragma unroll
-              for (int nb = 0; nb < 4; ++nb)
-                tma_load_2d(r_dst + nb * (RAW_BYTES / 4), mb, (n * BN + nb * 64) * RB / 64, krow, &sm.raw_full[stage]);
+              for (int nb = 0; nb < C::B_ROWS / 64; ++nb)
+                tma_load_2d(r_dst + nb * 64 * RB, mb, (n * BN + (int)rank * C::B_ROWS + nb * 64) * RB / 64, krow,
+                            &sm.raw_full[stage]);
+            } else if (PAIR) {
+              tma_load_2d(r_dst, mb, kb * RB, kmajor_row<MODE>(p, e, n, (int)rank), &sm.raw_full[stage]);
             } else {
               tma_load_2d(r_dst, &tmap_b0, kb * RB, kmajor_row<MODE>(p, e, n, 0), &sm.raw_full[stage]);
               tma_load_2d(r_dst + RAW_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * RB,
@@ -373,15 +408,24 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
           }
         }
       }
+      // tail: wait for the final MMA completion of every stage so that no
+      // commit from the pair's leader targets this CTA after it exits
+      for (int i = 0; i < STAGES; ++i) {
+        if (!mbar_wait(&sm.empty[stage], phase ^ 1, 12)) break;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
     }
   } else if (warp == 1) {
-    // ======================= UMMA issuer =======================
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, false, MN);
+    // ======================= UMMA issuer (the leader of a pair) =======================
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_bf16(TILE_M, BN, false, MN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x, ++it) {
+      for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++it) {
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&sm.tempty[acc], acc_phase ^ 1, 20)) {
@@ -402,11 +446,13 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
             const uint64_t ad = make_sdesc_sw128(a_addr + k * UMMA_K * 2, 16, 1024);
-            const uint64_t bd = MN ? make_sdesc_sw128(b_addr + k * UMMA_K * 128, B_BYTES / 4, 1024)
+            const uint64_t bd = MN ? make_sdesc_sw128(b_addr + k * UMMA_K * 128, 8192, 1024)
                                    : make_sdesc_sw128(b_addr + k * UMMA_K * 2, 16, 1024);
-            umma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            if (PAIR) umma_bf16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            else umma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          umma_commit(&sm.empty[stage]);
+          if (PAIR) umma_commit_pair(&sm.empty[stage], 0x3);
+          else umma_commit(&sm.empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -416,14 +462,16 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
           *abort_flag = 1;
           break;
         }
-        umma_commit(&sm.tfull[acc]);
+        if (PAIR) umma_commit_pair(&sm.tfull[acc], 0x3);
+        else umma_commit(&sm.tfull[acc]);
       }
     }
   } else if (warp < 2 + kEpiWarps) {
     // ======================= epilogue =======================
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t tempty_leader[2] = {leader_addr(&sm.tempty[0]), leader_addr(&sm.tempty[1])};
     int it = 0;
-    for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x, ++it) {
+    for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(&sm.tfull[acc], acc_phase, 30)) {
@@ -432,11 +480,11 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
       }
       tc_fence_after();
       int e, m, n;
-      decode_tile<WF>(t, sm, E, p.n_tiles, e, m, n);
-      const int r = q * 32 + lane;
+      decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
+      const int r = (int)rank * BM + q * 32 + lane;  // row inside the tile
       const int64_t seg_rows = (int64_t)sm.row_start[e + 1] - sm.row_start[e];
-      const bool valid = (int64_t)m * BM + r < seg_rows;
-      const int64_t grow = (int64_t)sm.row_start[e] + (int64_t)m * BM + r;
+      const bool valid = (int64_t)m * TILE_M + r < seg_rows;
+      const int64_t grow = (int64_t)sm.row_start[e] + (int64_t)m * TILE_M + r;
       const uint32_t tb = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
       if (MODE == GATEUP) {
         const int col0 = n * (BN / 2);
@@ -540,43 +588,60 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.tempty[acc]);
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_cluster(tempty_leader[acc]);
+        else mbar_arrive(&sm.tempty[acc]);
+      }
     }
   } else if (QUANT) {
     // ======================= dequantisers =======================
-    // K-major: thread d owns B row (d & 127) of half (d >> 7).
-    // MN-major: thread d owns k-row (d & 63) of 64-column block (d >> 6).
+    // This CTA's B block holds B_ROWS rows of 64 elements per stage (K-major:
+    // weight rows; MN-major: 64-element column blocks x 64 k-rows).  TPR
+    // threads share one row; thread d decodes ELEMS elements of row d / TPR.
+    constexpr int TPR = C::TPR;
+    constexpr int ELEMS = C::ELEMS;
+    constexpr int RB = C::ROW_BYTES;
     const int d = threadIdx.x - 32 * (2 + kEpiWarps);
+    const int row = d / TPR;            // B row inside the stage
+    const int part = d % TPR;           // which ELEMS-element slice of the row
     const int nkb = num_kb;
-    const int kh = MN ? 0 : d >> 7;       // key of this thread (K-major)
-    const int kr = MN ? d & 63 : d & 127;  // row index inside the stage
-    const int nbq = MN ? d >> 6 : 0;       // 64-column block (MN-major)
-    constexpr int RB = Cfg<WF>::ROW_BYTES;
-    const int nblk_row = p.N / 64;         // MN: NF4 blocks per weight row
+    // K-major: 128-row block and row in it; MN-major: 64-column block and k-row
+    const int kblk = MN ? 0 : (PAIR ? (int)rank : row >> 7);
+    const int kr = MN ? row & 63 : row & 127;
+    const int nbq = MN ? row >> 6 : 0;  // local 64-column block (MN)
+    const int nbase = MN ? (int)rank * C::B_ROWS / 64 : 0;  // first 64-column block of this CTA in the tile
+    const int nblk_row = p.N / 64;      // MN: NF4 blocks per weight row
     int stage = 0;
     uint32_t phase = 0;
     float code[16];
-    for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+    for (int t = unit; t < total_tiles && !*abort_flag; t += num_units) {
       int e, m, n;
-      decode_tile<WF>(t, sm, E, p.n_tiles, e, m, n);
+      decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
+      // key of this thread's rows (K-major) / of the k-block (MN)
+      const int row_key = MN ? 0 : (MCfg<MODE>::TWO_KEYS ? kblk : 0);
+      const int wrow_base = MN ? 0 : kmajor_row<MODE>(p, e, n, kblk) - e * p.out_rows;  // first weight row
       // ---- stage this tile's scale inputs in shared memory
       named_bar_sync(1, kDeqThreads);
       if (WF == W_NF4) {
         if (!MN) {
-          for (int h = 0; h < 2; ++h) {
-            if (kmajor_row<MODE>(p, e, n, h) - e * p.out_rows >= p.out_rows) continue;  // past the last row
+          const int nblk = PAIR ? 1 : 2;
+          for (int h = 0; h < nblk; ++h) {
+            const int blk = PAIR ? (int)rank : h;
+            if (kmajor_row<MODE>(p, e, n, blk) - e * p.out_rows >= p.out_rows) continue;  // past the last row
+            const int key = MCfg<MODE>::TWO_KEYS ? blk : 0;
             const uint4* src =
-                reinterpret_cast<const uint4*>(p.q[h].absmax + (size_t)kmajor_row<MODE>(p, e, n, h) * nkb);
+                reinterpret_cast<const uint4*>(p.q[key].absmax + (size_t)kmajor_row<MODE>(p, e, n, blk) * nkb);
             uint4* dst = reinterpret_cast<uint4*>(dq->absq + h * 128 * nkb);
             for (int i = d; i < 8 * nkb; i += kDeqThreads) dst[i] = __ldg(src + i);
           }
         } else {
-          // absq[kk * 4 + j] = code of (k-row kk, column block n*4 + j)
-          for (int i = d; i < p.K * 4; i += kDeqThreads) {
-            const int kk = i >> 2, j = i & 3;
+          // absq[kk * 4 + j] = code of (k-row kk, this CTA's column block j)
+          constexpr int NB = C::B_ROWS / 64;
+          for (int i = d; i < p.K * NB; i += kDeqThreads) {
+            const int kk = i / NB, j = i % NB;
             const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
             const int wr = kk - key * p.krows;
-            const int nbg = n * 4 + j;
+            const int nbg = n * 4 + nbase + j;
             dq->absq[i] = nbg < nblk_row
                               ? __ldg(p.q[key].absmax + ((size_t)e * p.krows + wr) * nblk_row + nbg) : (uint8_t)0;
           }
@@ -593,17 +658,18 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
         }
       }
       named_bar_sync(1, kDeqThreads);
-      // K-major: is this thread's B row inside the expert's matrix?  (The last
-      // 256-row tile of a down projection with N % 256 == 128 is half empty.)
-      const bool row_live = MN || (kmajor_row<MODE>(p, e, n, kh) - e * p.out_rows + kr < p.out_rows);
+      // K-major: is this thread's weight row inside the expert's matrix?  (The
+      // last 256-column tile of a down projection with N % 256 == 128 is half empty.)
+      const bool row_live = MN || (wrow_base + kr < p.out_rows);
       float row_scale = 0.f;
       if (WF == W_INT8 && !MN && row_live)
-        row_scale = __ldg(p.q[kh].scale + (size_t)kmajor_row<MODE>(p, e, n, kh) + kr);
+        row_scale = __ldg(p.q[row_key].scale + (size_t)e * p.out_rows + wrow_base + kr);
       float off[2] = {0.f, 0.f};
       if (WF == W_NF4) {
         off[0] = __ldg(p.q[0].offset + e);
         off[1] = MCfg<MODE>::TWO_KEYS ? __ldg(p.q[1].offset + e) : off[0];
       }
+      const int absq_row = PAIR ? 0 : kblk;  // absq block of this thread (K-major)
       int cur_key = -1;
       for (int kb = 0; kb < nkb; ++kb) {
         bool ok = mbar_wait(&sm.raw_full[stage], phase, 40);
@@ -612,14 +678,12 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
           *abort_flag = 1;
           break;
         }
-        const int key = MN ? ((MCfg<MODE>::TWO_KEYS && kb >= p.kb_half) ? 1 : 0)
-                           : (MCfg<MODE>::TWO_KEYS ? kh : 0);
-        const uint8_t* raw = sRaw + stage * RAW_BYTES +
-                             (MN ? nbq * (RAW_BYTES / 4) + kr * RB : kh * (RAW_BYTES / 2) + kr * RB);
-        const uint32_t row_addr = smem_u32(sB + stage * B_BYTES) +
-                                  (MN ? (uint32_t)nbq * (B_BYTES / 4) + (uint32_t)kr * 128u
-                                      : (uint32_t)(kh * 128 + kr) * 128u);
+        const int key = MN ? ((MCfg<MODE>::TWO_KEYS && kb >= p.kb_half) ? 1 : 0) : row_key;
+        const uint8_t* raw = sRaw + stage * RAW_BYTES + row * RB + part * (ELEMS * RB / 64);
+        const uint32_t row_addr = smem_u32(sB + stage * B_BYTES) + (uint32_t)row * 128u;
         const int sw = kr & 7;
+        constexpr int CH = ELEMS / 8;  // 16-byte chunks of this thread
+        const int c0 = part * CH;
         if (WF == W_NF4) {
           if (key != cur_key) {
 #pragma unroll
@@ -630,45 +694,48 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
           uint32_t qcode;
           bool live = row_live;
           if (!MN) {
-            const int wrow = kmajor_row<MODE>(p, e, n, kh) - e * p.out_rows + kr;
-            blk = wrow * nkb + kb;
-            qcode = dq->absq[kh * 128 * nkb + kr * nkb + kb];
+            blk = (wrow_base + kr) * nkb + kb;
+            qcode = dq->absq[absq_row * 128 * nkb + kr * nkb + kb];
           } else {
-            const int kk = kb * BK + kr;                     // k-row across both keys
-            const int wr = kk - key * p.krows;               // k-row inside the key's matrix
-            const int nbg = n * 4 + nbq;
+            const int kk = kb * BK + kr;        // k-row across both keys
+            const int wr = kk - key * p.krows;  // k-row inside the key's matrix
+            const int nbg = n * 4 + nbase + nbq;
             live = nbg < nblk_row;
             blk = wr * nblk_row + nbg;
-            qcode = dq->absq[kk * 4 + nbq];
+            qcode = dq->absq[kk * (C::B_ROWS / 64) + nbq];
           }
           const float scale =
               live ? __fadd_rn(__fmul_rn(dq->ncode[key][qcode], dq->nested[key][blk >> p.nbs_shift]), off[key]) : 0.f;
           Nf4Tab tab;
           nf4_table(code, scale, tab);
-          const uint4 r0 = reinterpret_cast<const uint4*>(raw)[0];
-          const uint4 r1 = reinterpret_cast<const uint4*>(raw)[1];
-          const uint32_t words[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+          uint32_t words[CH];
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
+          for (int v = 0; v < CH / 4; ++v) {
+            const uint4 r4 = reinterpret_cast<const uint4*>(raw)[v];
+            words[4 * v] = r4.x, words[4 * v + 1] = r4.y, words[4 * v + 2] = r4.z, words[4 * v + 3] = r4.w;
+          }
+#pragma unroll
+          for (int c = 0; c < CH; ++c) {
             uint32_t o[4];
             nf4_word(words[c], tab, o);
-            st_shared_v4(row_addr + (uint32_t)((c ^ sw) << 4), o[0], o[1], o[2], o[3]);
+            st_shared_v4(row_addr + (uint32_t)(((c0 + c) ^ sw) << 4), o[0], o[1], o[2], o[3]);
           }
         } else {
           const float scale = MN ? reinterpret_cast<const float*>(dq->absq)[kb * BK + kr] : row_scale;
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
+          for (int v = 0; v < CH / 2; ++v) {
             uint32_t o[8];
             int8_x16(reinterpret_cast<const uint4*>(raw)[v], scale, o);
-            st_shared_v4(row_addr + (uint32_t)(((2 * v) ^ sw) << 4), o[0], o[1], o[2], o[3]);
-            st_shared_v4(row_addr + (uint32_t)(((2 * v + 1) ^ sw) << 4), o[4], o[5], o[6], o[7]);
+            st_shared_v4(row_addr + (uint32_t)(((c0 + 2 * v) ^ sw) << 4), o[0], o[1], o[2], o[3]);
+            st_shared_v4(row_addr + (uint32_t)(((c0 + 2 * v + 1) ^ sw) << 4), o[4], o[5], o[6], o[7]);
           }
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&sm.raw_empty[stage]);
-          mbar_arrive(&sm.full[stage]);
+          if (PAIR) mbar_arrive_cluster(leader_addr(&sm.full[stage]));
+          else mbar_arrive(&sm.full[stage]);
         }
         if (++stage == STAGES) {
           stage = 0;
@@ -680,17 +747,30 @@ __global__ void __launch_bounds__(Cfg<WF>::THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
-template <int MODE, int WF>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const Params& p,
-           cudaStream_t stream) {
-  auto kern = grouped_gemm_kernel<MODE, WF>;
-  constexpr size_t smem = smem_bytes<WF>();
+// CTA pairs are used unless MIRAI_B200_CTA_PAIR=0 (kept for A/B measurement).
+static bool use_pairs() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("MIRAI_B200_CTA_PAIR");
+    v = (s && s[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+template <int MODE, int WF, bool PAIR>
+int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const Params& p,
+                cudaStream_t stream) {
+  using C = Cfg<WF, PAIR>;
+  auto kern = grouped_gemm_kernel<MODE, WF, PAIR>;
+  constexpr size_t smem = smem_bytes<WF, PAIR>();
   static_assert(smem <= 232448, "shared memory budget exceeded");
   static bool attr_set = false;
   if (!attr_set) {
@@ -698,11 +778,37 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1
     if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_set = true;
   }
-  const int64_t max_tiles = ((p.S + BM - 1) / BM + p.E) * (int64_t)p.n_tiles;
-  const int grid = (int)(max_tiles < sm_count() ? max_tiles : sm_count());
-  kern<<<grid, Cfg<WF>::THREADS, smem, stream>>>(ta, tb0, tb1, p);
+  const int64_t max_tiles = ((p.S + C::TILE_M - 1) / C::TILE_M + p.E) * (int64_t)p.n_tiles;
   static const char* names[4] = {"gateup_swiglu", "down", "down_dx", "gateup_dx"};
+  const int sms = sm_count();
+  if (!PAIR) {
+    const int grid = (int)(max_tiles < sms ? max_tiles : sms);
+    kern<<<grid, C::THREADS, smem, stream>>>(ta, tb0, tb1, p);
+    return check_launch(names[MODE]);
+  }
+  const int64_t units = max_tiles < sms / 2 ? max_tiles : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * units), 1, 1);
+  cfg.blockDim = dim3(C::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb0, tb1, p);
+  if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "%s: launch failed: %s", names[MODE], cudaGetErrorString(e));
   return check_launch(names[MODE]);
+}
+
+template <int MODE, int WF>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const Params& p,
+           cudaStream_t stream) {
+  return use_pairs() ? launch_impl<MODE, WF, true>(ta, tb0, tb1, p, stream)
+                     : launch_impl<MODE, WF, false>(ta, tb0, tb1, p, stream);
 }
 
 static inline bool mis16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; }
