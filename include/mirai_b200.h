@@ -200,6 +200,49 @@ int mirai_moe_gateup_dx_int8(const void* grad_gate_up, const int32_t* offsets, i
                              int64_t num_rows, int32_t inter, int32_t hidden, const mirai_int8_weight* w1,
                              const mirai_int8_weight* w3, void* dx_sorted, mirai_stream_t stream);
 
+/* ------------------------------------------- a10: LoRA on the down projection
+ * ActiveExpertLoRA.batched_subset_forward (active_expert_lora.py:434-478):
+ * y += scale * (h A_e^T) B_e^T with A [E, r, I], B [E, H, r] (r <= 32), fused
+ * into the down GEMMs as one extra 64-wide k-block.
+ *
+ * mirai_moe_lora_project writes the rank-block operand
+ *   out[s, j] = bf16(scale * sum_k x[s, k] * P_e[j, k])  (j < rank; 0 for j < 64)
+ * as [S, 64] bf16, where P_e[j, k] = proj[e*stride_e + j*stride_r + k*stride_k]
+ * (bf16): forward x = h, P = A (strides I*r, I, 1); dX x = grad_y, P = B read
+ * transposed (strides H*r, 1, r). */
+int mirai_moe_lora_project(const void* x, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                           int32_t k_dim, const void* proj, int64_t stride_e, int64_t stride_r, int64_t stride_k,
+                           int32_t rank, float scale, void* out, mirai_stream_t stream);
+
+/* Down GEMM plus the rank block: y = h W2^T + rank_a rank_b_e^T, with rank_a the
+ * [S, 64] projection of h and rank_b = B zero-padded to [E*H, 64] bf16. */
+int mirai_moe_down_lora_bf16(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                             int32_t inter, int32_t hidden, const void* w2, const void* rank_a,
+                             const void* rank_b, void* y, mirai_stream_t stream);
+int mirai_moe_down_lora_nf4(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                            int32_t inter, int32_t hidden, const mirai_nf4_weight* w2, const void* rank_a,
+                            const void* rank_b, void* y, mirai_stream_t stream);
+int mirai_moe_down_lora_int8(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                             int32_t inter, int32_t hidden, const mirai_int8_weight* w2, const void* rank_a,
+                             const void* rank_b, void* y, mirai_stream_t stream);
+
+/* Down dX plus the rank block: dh = grad_y W2 + rank_a rank_b_e, with rank_a the
+ * [S, 64] projection of grad_y through B (times scale) and rank_b = A
+ * zero-padded to [E*64, I] bf16; the SwiGLU backward is fused as in
+ * mirai_moe_down_dx_*. */
+int mirai_moe_down_dx_lora_bf16(const void* grad_y, const int32_t* offsets, int32_t num_experts,
+                                int64_t num_rows, int32_t hidden, int32_t inter, const void* w2,
+                                const void* gate_up, const void* rank_a, const void* rank_b,
+                                void* grad_gate_up, mirai_stream_t stream);
+int mirai_moe_down_dx_lora_nf4(const void* grad_y, const int32_t* offsets, int32_t num_experts,
+                               int64_t num_rows, int32_t hidden, int32_t inter, const mirai_nf4_weight* w2,
+                               const void* gate_up, const void* rank_a, const void* rank_b,
+                               void* grad_gate_up, mirai_stream_t stream);
+int mirai_moe_down_dx_lora_int8(const void* grad_y, const int32_t* offsets, int32_t num_experts,
+                                int64_t num_rows, int32_t hidden, int32_t inter, const mirai_int8_weight* w2,
+                                const void* gate_up, const void* rank_a, const void* rank_b,
+                                void* grad_gate_up, mirai_stream_t stream);
+
 /* --------------------------------------------------- a4 / a5: weight ingest
  * NF4 quantisation of a bf16 [E, out, in] expert stack into the reference's
  * per-expert buffers (CompressedGroupedExperts._store_nf4_grouped,

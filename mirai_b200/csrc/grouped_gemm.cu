@@ -100,6 +100,7 @@ struct Params {
   __nv_bfloat16* gate_up;  // GATEUP: optional saved [S,2I] output; DXDOWN: saved input
   QKey q[2];               // quantised keys (index 1 used by GATEUP / DXGATEUP)
   int nbs_shift;           // log2(nested_blocksize)
+  int has_ext;             // 1: one extra bf16 k-block (the LoRA rank block) from tmap_xa / tmap_xb
 };
 
 template <int WF, bool PAIR>
@@ -231,7 +232,8 @@ __device__ __forceinline__ int kmajor_row(const Params& p, int e, int n, int h) 
 template <int MODE, int WF, bool PAIR>
 __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b0,
-                        const __grid_constant__ CUtensorMap tmap_b1, const Params p) {
+                        const __grid_constant__ CUtensorMap tmap_b1, const __grid_constant__ CUtensorMap tmap_xa,
+                        const __grid_constant__ CUtensorMap tmap_xb, const Params p) {
   using C = Cfg<WF, PAIR>;
   constexpr int STAGES = C::STAGES;
   constexpr uint32_t B_BYTES = C::B_BYTES;
@@ -334,6 +336,9 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   const uint32_t tmem_base = sm.tmem_base;
   const int total_tiles = sm.tile_prefix[E] * p.n_tiles;
   const int num_kb = p.K / BK;
+  // the rank block of a fused LoRA adapter is one more k-block: A from tmap_xa
+  // ([S, 64] bf16), B from tmap_xb (bf16, the layout of this mode's B)
+  const int total_kb = num_kb + p.has_ext;
   volatile int* abort_flag = &sm.abort_flag;
 
   if (warp == 0) {
@@ -345,19 +350,20 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         int e, m, n;
         decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
         const int row0 = sm.row_start[e] + m * TILE_M + (int)rank * BM;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&sm.empty[stage], phase ^ 1, 10)) {
             *abort_flag = 1;
             break;
           }
           const uint32_t full_addr = leader_addr(&sm.full[stage]);
+          const bool ext = kb == num_kb;  // the fused rank block
           // B source for this k-block
           const bool key1 = MCfg<MODE>::TWO_KEYS && (MN ? kb >= p.kb_half : (PAIR && rank == 1));
           const CUtensorMap* mb = key1 ? &tmap_b1 : &tmap_b0;
           const int krow = MN ? e * p.krows + (kb - ((MN && key1) ? p.kb_half : 0)) * BK : 0;
           const int pair_mult = PAIR ? 2 : 1;
           if (leader) {
-            const uint32_t bytes = pair_mult * (A_BYTES + (QUANT ? 0u : B_BYTES));
+            const uint32_t bytes = pair_mult * (A_BYTES + ((QUANT && !ext) ? 0u : B_BYTES));
             if (PAIR) mbar_arrive_expect_tx_cluster(full_addr, bytes);
             else mbar_arrive_expect_tx(&sm.full[stage], bytes);
           }
@@ -365,7 +371,20 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             if (PAIR) tma_load_2d_pair(dst, map, x, y, full_addr);
             else tma_load_2d(dst, map, x, y, &sm.full[stage]);
           };
-          if (!QUANT) {
+          if (ext) {
+            uint8_t* b_dst = sB + stage * B_BYTES;
+            if (MN) {
+#pragma unroll
+              for (int nb = 0; nb < C::B_ROWS / 64; ++nb)
+                load(b_dst + nb * 8192, &tmap_xb, n * BN + (int)rank * C::B_ROWS + nb * 64, e * BK);
+            } else if (PAIR) {
+              load(b_dst, &tmap_xb, 0, kmajor_row<MODE>(p, e, n, (int)rank));
+            } else {
+              load(b_dst, &tmap_xb, 0, kmajor_row<MODE>(p, e, n, 0));
+              load(b_dst + B_BYTES / 2, &tmap_xb, 0, kmajor_row<MODE>(p, e, n, 1));
+            }
+            load(sA + stage * A_BYTES, &tmap_xa, 0, row0);
+          } else if (!QUANT) {
             uint8_t* b_dst = sB + stage * B_BYTES;
             if (MN) {
               // this CTA's columns: n*256 + rank*B_ROWS + 64*nb
@@ -380,13 +399,16 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
               load(b_dst + B_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * BK, kmajor_row<MODE>(p, e, n, 1));
             }
           }
-          load(sA + stage * A_BYTES, &tmap_a, kb * BK, row0);
+          if (!ext) load(sA + stage * A_BYTES, &tmap_a, kb * BK, row0);
           if (QUANT) {
             if (!mbar_wait(&sm.raw_empty[stage], phase ^ 1, 11)) {
               *abort_flag = 1;
               break;
             }
-            mbar_arrive_expect_tx(&sm.raw_full[stage], RAW_BYTES);
+            // the rank block has no raw codes: complete the raw stage empty
+            mbar_arrive_expect_tx(&sm.raw_full[stage], ext ? 0u : RAW_BYTES);
+          }
+          if (QUANT && !ext) {
             uint8_t* r_dst = sRaw + stage * RAW_BYTES;
             constexpr int RB = C::ROW_BYTES;
             if (MN) {
@@ -435,7 +457,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&sm.full[stage], phase, 21)) {
             ok = false;
             break;
@@ -671,12 +693,25 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       }
       const int absq_row = PAIR ? 0 : kblk;  // absq block of this thread (K-major)
       int cur_key = -1;
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = 0; kb < total_kb; ++kb) {
         bool ok = mbar_wait(&sm.raw_full[stage], phase, 40);
         ok = ok && mbar_wait(&sm.empty[stage], phase ^ 1, 41);
         if (!ok) {
           *abort_flag = 1;
           break;
+        }
+        if (kb == nkb) {  // rank block: B arrives by TMA, nothing to decode
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&sm.raw_empty[stage]);
+            if (PAIR) mbar_arrive_cluster(leader_addr(&sm.full[stage]));
+            else mbar_arrive(&sm.full[stage]);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+          continue;
         }
         const int key = MN ? ((MCfg<MODE>::TWO_KEYS && kb >= p.kb_half) ? 1 : 0) : row_key;
         const uint8_t* raw = sRaw + stage * RAW_BYTES + row * RB + part * (ELEMS * RB / 64);
@@ -766,7 +801,8 @@ static bool use_pairs() {
 }
 
 template <int MODE, int WF, bool PAIR>
-int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const Params& p,
+int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const CUtensorMap& txa,
+                const CUtensorMap& txb, const Params& p,
                 cudaStream_t stream) {
   using C = Cfg<WF, PAIR>;
   auto kern = grouped_gemm_kernel<MODE, WF, PAIR>;
@@ -783,12 +819,10 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
   const int sms = sm_count();
   if (!PAIR) {
     const int grid = (int)(max_tiles < sms ? max_tiles : sms);
-    kern<<<grid, C::THREADS, smem, stream>>>(ta, tb0, tb1, p);
+    kern<<<grid, C::THREADS, smem, stream>>>(ta, tb0, tb1, txa, txb, p);
     return check_launch(names[MODE]);
   }
-  const int64_t units = max_tiles < sms / 2 ? max_tiles : sms / 2;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(2 * units), 1, 1);
   cfg.blockDim = dim3(C::THREADS, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -799,16 +833,33 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb0, tb1, p);
+  // The kernel is persistent: launch no more pairs than can be resident at
+  // once (cluster placement can leave some SMs unpaired), else the surplus
+  // pairs run as a second wave.
+  static int resident_pairs = 0;
+  if (resident_pairs <= 0) {
+    cfg.gridDim = dim3((unsigned)(sms & ~1), 1, 1);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sms / 2;
+    }
+    resident_pairs = n;
+    if (getenv("MIRAI_B200_DEBUG")) fprintf(stderr, "[mirai_b200] %s: %d resident CTA pairs\n", names[MODE], n);
+  }
+  const int64_t units = max_tiles < resident_pairs ? max_tiles : resident_pairs;
+  cfg.gridDim = dim3((unsigned)(2 * units), 1, 1);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb0, tb1, txa, txb, p);
   if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "%s: launch failed: %s", names[MODE], cudaGetErrorString(e));
   return check_launch(names[MODE]);
 }
 
 template <int MODE, int WF>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const Params& p,
+int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const CUtensorMap& txa,
+           const CUtensorMap& txb, const Params& p,
            cudaStream_t stream) {
-  return use_pairs() ? launch_impl<MODE, WF, true>(ta, tb0, tb1, p, stream)
-                     : launch_impl<MODE, WF, false>(ta, tb0, tb1, p, stream);
+  return use_pairs() ? launch_impl<MODE, WF, true>(ta, tb0, tb1, txa, txb, p, stream)
+                     : launch_impl<MODE, WF, false>(ta, tb0, tb1, txa, txb, p, stream);
 }
 
 static inline bool mis16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; }
@@ -904,13 +955,37 @@ int bind_key(const WeightArg& w, CUtensorMap& m, QKey& q, int& shift, int E, int
   return int8_key(m, q, w.int8, E, rows, cols, mn);
 }
 
+// The optional rank block of a fused LoRA adapter: ext_a [S, 64] bf16 (one
+// k-block of A) and ext_b, bf16 in the layout of this mode's B:
+// down forward [E*H rows, 64] (K-major); down dX [E*64 rows, I] (MN-major).
+struct RankBlock {
+  const void* a;
+  const void* b;
+};
+
 template <int MODE>
 int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t S, int K, int N, void* out,
-        void* gate_up, const WeightArg& w0, const WeightArg& w1, int rows, int cols, mirai_stream_t stream) {
+        void* gate_up, const WeightArg& w0, const WeightArg& w1, int rows, int cols, mirai_stream_t stream,
+        const RankBlock* ext = nullptr) {
   if (S == 0 && E > 0) return MIRAI_OK;
   Params p;
-  CUtensorMap ta, t0, t1;
+  CUtensorMap ta, t0, t1, txa, txb;
   int rc = prepare<MODE>(name, a, offsets, E, S, K, N, out, gate_up, p, ta);
+  if (!rc && ext) {
+    if (!ext->a || !ext->b) rc = set_error(MIRAI_ERR_INVALID_ARG, "%s: null rank-block operand", name);
+    if (!rc)
+      rc = make_tmap_2d(&txa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ext->a, 64, (uint64_t)S, 128, BK, BM,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc) {
+      if (MCfg<MODE>::MN)  // [E*64 rank rows (k), N cols]
+        rc = make_tmap_2d(&txb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ext->b, (uint64_t)N, (uint64_t)E * BK,
+                          (uint64_t)N * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+      else  // [E*N rows, 64 rank cols (k)]
+        rc = make_tmap_2d(&txb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ext->b, 64, (uint64_t)E * N, 128, BK,
+                          BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    p.has_ext = 1;
+  }
   constexpr bool MN = MCfg<MODE>::MN;
   if (!rc && MN && w0.fmt != W_BF16 && K > kMaxK)
     rc = set_error(MIRAI_ERR_UNSUPPORTED, "%s: reduction length %d exceeds %d", name, K, kMaxK);
@@ -927,11 +1002,15 @@ int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t 
     p.q[1] = p.q[0];
   }
   p.nbs_shift = s0;
+  if (!ext) {
+    txa = ta;
+    txb = t0;
+  }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (w0.fmt) {
-    case W_BF16: return launch<MODE, W_BF16>(ta, t0, t1, p, st);
-    case W_NF4: return launch<MODE, W_NF4>(ta, t0, t1, p, st);
-    default: return launch<MODE, W_INT8>(ta, t0, t1, p, st);
+    case W_BF16: return launch<MODE, W_BF16>(ta, t0, t1, txa, txb, p, st);
+    case W_NF4: return launch<MODE, W_NF4>(ta, t0, t1, txa, txb, p, st);
+    default: return launch<MODE, W_INT8>(ta, t0, t1, txa, txb, p, st);
   }
 }
 
@@ -1001,6 +1080,50 @@ int mirai_moe_down_dx_int8(const void* grad_y, const int32_t* offsets, int32_t n
                            void* grad_gate_up, mirai_stream_t stream) {
   return run<DXDOWN>("down_dx_int8", grad_y, offsets, num_experts, num_rows, hidden, inter, grad_gate_up,
                      const_cast<void*>(gate_up), wi(w2), wi(w2), hidden, inter, stream);
+}
+
+// ---- LoRA on the down projection, fused as one extra k-block (a10).
+int mirai_moe_down_lora_bf16(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                             int32_t inter, int32_t hidden, const void* w2, const void* rank_a, const void* rank_b,
+                             void* y, mirai_stream_t stream) {
+  const RankBlock rb{rank_a, rank_b};
+  return run<DOWN>("down_lora_bf16", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, wb(w2), wb(w2),
+                   hidden, inter, stream, &rb);
+}
+int mirai_moe_down_lora_nf4(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                            int32_t inter, int32_t hidden, const mirai_nf4_weight* w2, const void* rank_a,
+                            const void* rank_b, void* y, mirai_stream_t stream) {
+  const RankBlock rb{rank_a, rank_b};
+  return run<DOWN>("down_lora_nf4", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, wn(w2), wn(w2),
+                   hidden, inter, stream, &rb);
+}
+int mirai_moe_down_lora_int8(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                             int32_t inter, int32_t hidden, const mirai_int8_weight* w2, const void* rank_a,
+                             const void* rank_b, void* y, mirai_stream_t stream) {
+  const RankBlock rb{rank_a, rank_b};
+  return run<DOWN>("down_lora_int8", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, wi(w2), wi(w2),
+                   hidden, inter, stream, &rb);
+}
+int mirai_moe_down_dx_lora_bf16(const void* grad_y, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                                int32_t hidden, int32_t inter, const void* w2, const void* gate_up,
+                                const void* rank_a, const void* rank_b, void* grad_gate_up, mirai_stream_t stream) {
+  const RankBlock rb{rank_a, rank_b};
+  return run<DXDOWN>("down_dx_lora_bf16", grad_y, offsets, num_experts, num_rows, hidden, inter, grad_gate_up,
+                     const_cast<void*>(gate_up), wb(w2), wb(w2), hidden, inter, stream, &rb);
+}
+int mirai_moe_down_dx_lora_nf4(const void* grad_y, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                               int32_t hidden, int32_t inter, const mirai_nf4_weight* w2, const void* gate_up,
+                               const void* rank_a, const void* rank_b, void* grad_gate_up, mirai_stream_t stream) {
+  const RankBlock rb{rank_a, rank_b};
+  return run<DXDOWN>("down_dx_lora_nf4", grad_y, offsets, num_experts, num_rows, hidden, inter, grad_gate_up,
+                     const_cast<void*>(gate_up), wn(w2), wn(w2), hidden, inter, stream, &rb);
+}
+int mirai_moe_down_dx_lora_int8(const void* grad_y, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                                int32_t hidden, int32_t inter, const mirai_int8_weight* w2, const void* gate_up,
+                                const void* rank_a, const void* rank_b, void* grad_gate_up, mirai_stream_t stream) {
+  const RankBlock rb{rank_a, rank_b};
+  return run<DXDOWN>("down_dx_lora_int8", grad_y, offsets, num_experts, num_rows, hidden, inter, grad_gate_up,
+                     const_cast<void*>(gate_up), wi(w2), wi(w2), hidden, inter, stream, &rb);
 }
 
 // ---- dX: gate/up.  dx = [dgate | dup] [W1 ; W3] (K = 2I, N = H).  B = W1/W3 read MN-major.

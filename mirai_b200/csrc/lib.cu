@@ -4,3 +4,4 @@
 #include "routing.cu"
 #include "grouped_gemm.cu"
 #include "quantize.cu"
+#include "lora.cu"

@@ -231,23 +231,71 @@ def gateup_swiglu(x_sorted: torch.Tensor, offsets: torch.Tensor, w1, w3, *, inte
     return (h, gu) if save_gate_up else h
 
 
-def down(h: torch.Tensor, offsets: torch.Tensor, w2, *, hidden: int, out: torch.Tensor | None = None):
+def down(h: torch.Tensor, offsets: torch.Tensor, w2, *, hidden: int, out: torch.Tensor | None = None,
+         lora: "DownLoRA | None" = None):
+    """y = h W2^T per expert segment (+ the fused LoRA rank block when ``lora``)."""
     w2 = _as_weight(w2)
     h = _cuda(h, "h", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
     S, I = h.shape
     E = offsets.numel()
     y = out if out is not None else torch.empty((S, hidden), dtype=torch.bfloat16, device=h.device)
-    if isinstance(w2, torch.Tensor):
-        w2 = _cuda(w2, "w2", torch.bfloat16)
-        _lib.call("mirai_moe_down_bf16", _ptr(h), _ptr(offsets), E, S, I, hidden, _ptr(w2), _ptr(y), _stream())
-    elif isinstance(w2, _lib.Nf4Weight):
-        _lib.call("mirai_moe_down_nf4", _ptr(h), _ptr(offsets), E, S, I, hidden, w2, _ptr(y), _stream())
-    elif isinstance(w2, _lib.Int8Weight):
-        _lib.call("mirai_moe_down_int8", _ptr(h), _ptr(offsets), E, S, I, hidden, w2, _ptr(y), _stream())
-    else:
-        raise TypeError(f"unsupported weight type {type(w2)}")
+    if lora is None:
+        _lib.call(f"mirai_moe_down_{_fmt_suffix(w2)}", _ptr(h), _ptr(offsets), E, S, I, hidden, _wptr(w2), _ptr(y),
+                  _stream())
+        return y
+    low = lora_project(h, offsets, lora.a, lora.a.stride(), lora.rank, lora.scale)
+    _lib.call(f"mirai_moe_down_lora_{_fmt_suffix(w2)}", _ptr(h), _ptr(offsets), E, S, I, hidden, _wptr(w2),
+              _ptr(low), _ptr(lora.b_pad()), _ptr(y), _stream())
     return y
+
+
+class DownLoRA:
+    """A LoRA adapter on the expert down projection (w2): y += scale (h A^T) B^T
+    with A [E, r, I] and B [E, H, r] (active_expert_lora.py:43-116, 434-478)."""
+
+    def __init__(self, a: torch.Tensor, b: torch.Tensor, scale: float):
+        self.a = _cuda(a.detach().to(torch.bfloat16), "lora_a")
+        self.b = _cuda(b.detach().to(torch.bfloat16), "lora_b")
+        E, r, I = self.a.shape
+        if tuple(self.b.shape[::2]) != (E, r) or r > 32:
+            raise ValueError(f"LoRA factors must be A [E, r, I] and B [E, H, r] with r <= 32, got "
+                             f"{tuple(self.a.shape)} and {tuple(self.b.shape)}")
+        self.rank = int(r)
+        self.scale = float(scale)
+        self._b_pad = None
+        self._a_pad = None
+
+    def b_pad(self) -> torch.Tensor:
+        """B zero-padded to [E*H, 64]: the K-major rank-block operand of the down GEMM."""
+        if self._b_pad is None:
+            E, H, r = self.b.shape
+            pad = torch.zeros((E, H, 64), dtype=torch.bfloat16, device=self.b.device)
+            pad[:, :, :r] = self.b
+            self._b_pad = pad.reshape(E * H, 64)
+        return self._b_pad
+
+    def a_pad(self) -> torch.Tensor:
+        """A zero-padded to [E*64, I]: the MN-major rank-block operand of the down dX GEMM."""
+        if self._a_pad is None:
+            E, r, I = self.a.shape
+            pad = torch.zeros((E, 64, I), dtype=torch.bfloat16, device=self.a.device)
+            pad[:, :r, :] = self.a
+            self._a_pad = pad.reshape(E * 64, I)
+        return self._a_pad
+
+
+def lora_project(x: torch.Tensor, offsets: torch.Tensor, proj: torch.Tensor, strides, rank: int,
+                 scale: float) -> torch.Tensor:
+    """[S, 64] bf16 rank-block operand: bf16(scale * x P_e^T), zero past ``rank``."""
+    x = _cuda(x, "x", torch.bfloat16)
+    offsets = _cuda(offsets, "offsets", torch.int32)
+    S, K = x.shape
+    out = torch.empty((S, 64), dtype=torch.bfloat16, device=x.device)
+    se, sr, sk = (int(v) for v in strides)
+    _lib.call("mirai_moe_lora_project", _ptr(x), _ptr(offsets), offsets.numel(), S, K, _ptr(proj), se, sr, sk,
+              int(rank), float(scale), _ptr(out), _stream())
+    return out
 
 
 # ----------------------------------------------------------------------------- a8
@@ -306,16 +354,23 @@ def _wptr(w):
 
 
 def down_dx(grad_y: torch.Tensor, offsets: torch.Tensor, w2, gate_up: torch.Tensor, *, inter: int,
-            out: torch.Tensor | None = None) -> torch.Tensor:
-    """grad_gate_up [S, 2I] = SwiGLU backward of (gate, up) given dh = grad_y W2."""
+            out: torch.Tensor | None = None, lora: DownLoRA | None = None) -> torch.Tensor:
+    """grad_gate_up [S, 2I] = SwiGLU backward of (gate, up) given dh = grad_y W2
+    (+ the LoRA path's input gradient when ``lora``)."""
     w2 = _as_weight(w2)
     gy = _cuda(grad_y, "grad_y", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
     gu = _cuda(gate_up, "gate_up", torch.bfloat16)
     S, H = gy.shape
     dgu = out if out is not None else torch.empty((S, 2 * inter), dtype=torch.bfloat16, device=gy.device)
-    _lib.call(f"mirai_moe_down_dx_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), offsets.numel(), S, H, inter,
-              _wptr(w2), _ptr(gu), _ptr(dgu), _stream())
+    if lora is None:
+        _lib.call(f"mirai_moe_down_dx_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), offsets.numel(), S, H, inter,
+                  _wptr(w2), _ptr(gu), _ptr(dgu), _stream())
+        return dgu
+    E, Hb, r = lora.b.shape
+    glow = lora_project(gy, offsets, lora.b, (Hb * r, 1, r), lora.rank, lora.scale)
+    _lib.call(f"mirai_moe_down_dx_lora_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), offsets.numel(), S, H, inter,
+              _wptr(w2), _ptr(gu), _ptr(glow), _ptr(lora.a_pad()), _ptr(dgu), _stream())
     return dgu
 
 
@@ -355,25 +410,25 @@ class ForwardState:
 
 
 def moe_forward_train(tokens, top_indices, top_weights, w1, w3, w2, *, num_experts: int, inter: int,
-                      out_dtype: torch.dtype | None = None):
+                      out_dtype: torch.dtype | None = None, lora: DownLoRA | None = None):
     """Forward that also returns the state the dX pass consumes."""
     plan = dispatch_plan(top_indices, num_experts)
     xs = permute_rows(tokens, plan.sorted_token_indices)
     h, gu = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter, save_gate_up=True)
-    y = down(h, plan.offsets, w2, hidden=tokens.shape[1])
+    y = down(h, plan.offsets, w2, hidden=tokens.shape[1], lora=lora)
     out = combine(y, plan.inverse_order, top_weights, out_dtype=out_dtype or tokens.dtype)
     return out, ForwardState(plan, y, gu, top_weights.float())
 
 
 def moe_backward_dx(grad_out: torch.Tensor, state: ForwardState, w1, w3, w2, *, inter: int,
-                    out_dtype: torch.dtype = torch.bfloat16):
+                    out_dtype: torch.dtype = torch.bfloat16, lora: DownLoRA | None = None):
     """Input gradient through the frozen experts and the top-weight gradient.
 
     grad_out [T, H] -> (dx [T, H], d_top_weights fp32 [T, k])."""
     plan = state.plan
     H = state.y_sorted.shape[1]
     gy, gw = combine_backward(grad_out, state.y_sorted, plan.inverse_order, state.top_weights)
-    dgu = down_dx(gy, plan.offsets, w2, state.gate_up, inter=inter)
+    dgu = down_dx(gy, plan.offsets, w2, state.gate_up, inter=inter, lora=lora)
     dxs = gateup_dx(dgu, plan.offsets, w1, w3, hidden=H)
     dx = combine(dxs, plan.inverse_order, None, out_dtype=out_dtype, top_k=plan.top_k)
     return dx, gw

@@ -375,3 +375,36 @@ def test_dx_matches_reference_golden(golden):
     assert om.rel_max_err(_f32(out), oq.bf16_bits_to_f32(g["out"])) < TOL
     assert om.rel_max_err(_f32(dx), oq.bf16_bits_to_f32(g["grad_tokens"])) < 3e-2
     assert om.rel_max_err(_f32(dws), oq.bf16_bits_to_f32(g["grad_scores"])) < 3e-2
+
+
+# ----------------------------------------------------------------------------- a10: LoRA on the down projection
+
+@pytest.mark.parametrize("fmt", ["bf16", "nf4"])
+@pytest.mark.parametrize("rank", [16, 4])
+def test_lora_on_down_forward_and_dx(fmt, rank):
+    dev = _dev()
+    from mirai_b200 import ops
+    T, H, E, k, I = 400, 256, 6, 2, 384
+    rng = np.random.default_rng(rank + len(fmt))
+    x = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    logits = (rng.standard_normal((T, E)) * 1.5).astype(np.float32)
+    dense, dw = _weights(fmt, rng, E, H, I, dev)
+    la = oq.bf16_round((rng.standard_normal((E, rank, I)) * 0.05).astype(np.float32))
+    lb = oq.bf16_round((rng.standard_normal((E, H, rank)) * 0.05).astype(np.float32))
+    scale = 16.0 / rank
+    lora = ops.DownLoRA(_bf16(la).to(dev), _bf16(lb).to(dev), scale)
+    g = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    idx, w = ops.route_topk(torch.from_numpy(logits).to(dev), k)
+    out, st = ops.moe_forward_train(_bf16(x).to(dev), idx, w, *dw, num_experts=E, inter=I, lora=lora)
+    dx, dwts = ops.moe_backward_dx(_bf16(g).to(dev), st, *dw, inter=I, lora=lora)
+    _check(ops)
+    ridx, rw = om.route_topk(logits, k)
+    ol = {"a": la, "b": lb, "scale": scale}
+    ref = om.moe_forward(x, ridx, rw, *dense, bf16=True, lora=ol)
+    rdx, rdw = om.moe_backward_dx(x, ridx, rw, *dense, g, bf16=True, lora=ol)
+    assert om.rel_max_err(_f32(out), ref) < TOL
+    assert om.rel_max_err(_f32(dx), rdx) < 3e-2
+    assert om.rel_max_err(_f32(dwts), rdw) < 3e-2
+    # the adapter matters: without it the forward differs by far more than the tolerance
+    ref0 = om.moe_forward(x, ridx, rw, *dense, bf16=True)
+    assert om.rel_max_err(ref0, ref) > 5 * om.rel_max_err(_f32(out), ref)
