@@ -214,6 +214,17 @@ int mirai_moe_lora_project(const void* x, const int32_t* offsets, int32_t num_ex
                            int32_t k_dim, const void* proj, int64_t stride_e, int64_t stride_r, int64_t stride_k,
                            int32_t rank, float scale, void* out, mirai_stream_t stream);
 
+/* Adapter-factor gradient (the LoRA weight gradients of bmm's backward in
+ * batched_subset_forward): grad[e][j][k] = sum over the rows s of segment e of
+ * g_rank[s, j] * x[s, k], fp32, rows summed in order (deterministic).
+ * g_rank is a [S, 64] bf16 rank-block operand (already scaled); grad element
+ * (e, j, k) is stored at grad[e*stride_e + j*stride_r + k*stride_k]:
+ * dA = lora_grad(h, grad-side rank block) into [E, r, I];
+ * dB = lora_grad(grad_y, forward rank block) into [E, H, r]. */
+int mirai_moe_lora_grad(const void* x, const void* g_rank, const int32_t* offsets, int32_t num_experts,
+                        int64_t num_rows, int32_t k_dim, int32_t rank, float* grad, int64_t stride_e,
+                        int64_t stride_r, int64_t stride_k, mirai_stream_t stream);
+
 /* Down GEMM plus the rank block: y = h W2^T + rank_a rank_b_e^T, with rank_a the
  * [S, 64] projection of h and rank_b = B zero-padded to [E*H, 64] bf16. */
 int mirai_moe_down_lora_bf16(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows,

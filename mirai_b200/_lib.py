@@ -86,6 +86,8 @@ SIGNATURES = {
                                                 c_vp]),
     "mirai_moe_lora_project": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_vp, c_i64, c_i64, c_i64, c_i32,
                                               c_f32, c_vp, c_vp]),
+    "mirai_moe_lora_grad": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i64, c_i64, c_i64,
+                                           c_vp]),
     "mirai_moe_down_lora_bf16": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,
                                                 c_vp]),
     "mirai_moe_down_lora_nf4": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, ctypes.POINTER(Nf4Weight),

@@ -260,6 +260,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   auto leader_addr = [&](uint64_t* bar) -> uint32_t {
     return PAIR ? mapa_shared(smem_u32(bar), 0) : smem_u32(bar);
   };
+  // the leader's `full` barriers as seen from this CTA (stage s at + 8 s)
+  const uint32_t full_leader0 = leader_addr(&sm.full[0]);
 
   // ---- segment table: row_start[e] and exclusive prefix of TILE_M-row blocks
   if (warp == 0) {
@@ -355,7 +357,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             *abort_flag = 1;
             break;
           }
-          const uint32_t full_addr = leader_addr(&sm.full[stage]);
+          const uint32_t full_addr = full_leader0 + 8u * stage;
           const bool ext = kb == num_kb;  // the fused rank block
           // B source for this k-block
           const bool key1 = MCfg<MODE>::TWO_KEYS && (MN ? kb >= p.kb_half : (PAIR && rank == 1));
@@ -364,8 +366,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           const int pair_mult = PAIR ? 2 : 1;
           if (leader) {
             const uint32_t bytes = pair_mult * (A_BYTES + ((QUANT && !ext) ? 0u : B_BYTES));
-            if (PAIR) mbar_arrive_expect_tx_cluster(full_addr, bytes);
-            else mbar_arrive_expect_tx(&sm.full[stage], bytes);
+            // the leader's own barrier: a CTA-local arrive carries the bytes of both CTAs
+            mbar_arrive_expect_tx(&sm.full[stage], bytes);
           }
           auto load = [&](void* dst, const CUtensorMap* map, int x, int y) {
             if (PAIR) tma_load_2d_pair(dst, map, x, y, full_addr);
@@ -704,7 +706,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           __syncwarp();
           if (lane == 0) {
             mbar_arrive(&sm.raw_empty[stage]);
-            if (PAIR) mbar_arrive_cluster(leader_addr(&sm.full[stage]));
+            if (PAIR) mbar_arrive_cluster(full_leader0 + 8u * stage);
             else mbar_arrive(&sm.full[stage]);
           }
           if (++stage == STAGES) {
@@ -769,7 +771,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&sm.raw_empty[stage]);
-          if (PAIR) mbar_arrive_cluster(leader_addr(&sm.full[stage]));
+          if (PAIR) mbar_arrive_cluster(full_leader0 + 8u * stage);
           else mbar_arrive(&sm.full[stage]);
         }
         if (++stage == STAGES) {

@@ -119,6 +119,45 @@ __global__ void __launch_bounds__(kThreads) lora_project_kernel(
   }
 }
 
+// Adapter-factor gradient over one expert's rows:
+//   grad[e][j][k] = sum_{s in segment e} g[s, j] * x[s, k]      (fp32, rows in order)
+// One block per (expert, 256 columns of K); each thread owns one column and R
+// accumulators; g rows are staged through shared memory 64 at a time.
+template <int R>
+__global__ void __launch_bounds__(256) lora_grad_kernel(const __nv_bfloat16* __restrict__ x,
+                                                        const __nv_bfloat16* __restrict__ g,
+                                                        const int32_t* __restrict__ offsets, int E, int K,
+                                                        int rank, float* __restrict__ grad, int64_t sE,
+                                                        int64_t sJ, int64_t sK) {
+  __shared__ float gs[64][R];
+  const int e = blockIdx.y;
+  const int col = blockIdx.x * 256 + threadIdx.x;
+  const int64_t beg = e > 0 ? offsets[e - 1] : 0;
+  const int64_t end = offsets[e];
+  float acc[R];
+#pragma unroll
+  for (int j = 0; j < R; ++j) acc[j] = 0.f;
+  for (int64_t s0 = beg; s0 < end; s0 += 64) {
+    const int n = (int)((end - s0) < 64 ? (end - s0) : 64);
+    __syncthreads();
+    for (int i = threadIdx.x; i < 64 * R; i += 256) {
+      const int rr = i / R, j = i % R;
+      gs[rr][j] = (rr < n && j < rank) ? __bfloat162float(g[(s0 + rr) * 64 + j]) : 0.f;
+    }
+    __syncthreads();
+    if (col < K) {
+      for (int rr = 0; rr < n; ++rr) {
+        const float xv = __bfloat162float(x[(s0 + rr) * K + col]);
+#pragma unroll
+        for (int j = 0; j < R; ++j) acc[j] = fmaf(gs[rr][j], xv, acc[j]);
+      }
+    }
+  }
+  if (col < K) {
+    for (int j = 0; j < rank && j < R; ++j) grad[e * sE + j * sJ + (int64_t)col * sK] = acc[j];
+  }
+}
+
 }  // namespace lr
 }  // namespace mirai
 
@@ -158,6 +197,30 @@ int mirai_moe_lora_project(const void* x, const int32_t* offsets, int32_t num_ex
   else MIRAI_LORA_LAUNCH(32);
 #undef MIRAI_LORA_LAUNCH
   return check_launch("lora_project");
+}
+
+int mirai_moe_lora_grad(const void* x, const void* g_rank, const int32_t* offsets, int32_t num_experts,
+                        int64_t num_rows, int32_t k_dim, int32_t rank, float* grad, int64_t stride_e,
+                        int64_t stride_r, int64_t stride_k, mirai_stream_t stream) {
+  if (num_experts <= 0 || num_experts > lr::kMaxExperts || num_rows < 0 || k_dim <= 0)
+    return set_error(MIRAI_ERR_INVALID_ARG, "lora_grad: bad sizes (E=%d, K=%d)", num_experts, k_dim);
+  if (rank <= 0 || rank > lr::kMaxRank)
+    return set_error(MIRAI_ERR_UNSUPPORTED, "lora_grad: rank %d outside 1..%d", rank, lr::kMaxRank);
+  if (!x || !g_rank || !offsets || !grad) return set_error(MIRAI_ERR_INVALID_ARG, "lora_grad: null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const dim3 grid((unsigned)((k_dim + 255) / 256), (unsigned)num_experts);
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  const __nv_bfloat16* gb = static_cast<const __nv_bfloat16*>(g_rank);
+  if (rank <= 8)
+    lr::lora_grad_kernel<8><<<grid, 256, 0, s>>>(xb, gb, offsets, num_experts, k_dim, rank, grad, stride_e,
+                                                 stride_r, stride_k);
+  else if (rank <= 16)
+    lr::lora_grad_kernel<16><<<grid, 256, 0, s>>>(xb, gb, offsets, num_experts, k_dim, rank, grad, stride_e,
+                                                  stride_r, stride_k);
+  else
+    lr::lora_grad_kernel<32><<<grid, 256, 0, s>>>(xb, gb, offsets, num_experts, k_dim, rank, grad, stride_e,
+                                                  stride_r, stride_k);
+  return check_launch("lora_grad");
 }
 
 }  // extern "C"

@@ -232,8 +232,9 @@ def gateup_swiglu(x_sorted: torch.Tensor, offsets: torch.Tensor, w1, w3, *, inte
 
 
 def down(h: torch.Tensor, offsets: torch.Tensor, w2, *, hidden: int, out: torch.Tensor | None = None,
-         lora: "DownLoRA | None" = None):
-    """y = h W2^T per expert segment (+ the fused LoRA rank block when ``lora``)."""
+         lora: "DownLoRA | None" = None, rank_a: torch.Tensor | None = None):
+    """y = h W2^T per expert segment (+ the fused LoRA rank block when ``lora``;
+    ``rank_a`` is its [S, 64] projection of h when the caller already has it)."""
     w2 = _as_weight(w2)
     h = _cuda(h, "h", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
@@ -244,7 +245,7 @@ def down(h: torch.Tensor, offsets: torch.Tensor, w2, *, hidden: int, out: torch.
         _lib.call(f"mirai_moe_down_{_fmt_suffix(w2)}", _ptr(h), _ptr(offsets), E, S, I, hidden, _wptr(w2), _ptr(y),
                   _stream())
         return y
-    low = lora_project(h, offsets, lora.a, lora.a.stride(), lora.rank, lora.scale)
+    low = rank_a if rank_a is not None else lora_project(h, offsets, lora.a, lora.a.stride(), lora.rank, lora.scale)
     _lib.call(f"mirai_moe_down_lora_{_fmt_suffix(w2)}", _ptr(h), _ptr(offsets), E, S, I, hidden, _wptr(w2),
               _ptr(low), _ptr(lora.b_pad()), _ptr(y), _stream())
     return y
@@ -254,9 +255,13 @@ class DownLoRA:
     """A LoRA adapter on the expert down projection (w2): y += scale (h A^T) B^T
     with A [E, r, I] and B [E, H, r] (active_expert_lora.py:43-116, 434-478)."""
 
-    def __init__(self, a: torch.Tensor, b: torch.Tensor, scale: float):
+    def __init__(self, a: torch.Tensor, b: torch.Tensor, scale: float, *, compute_grads: bool = False):
         self.a = _cuda(a.detach().to(torch.bfloat16), "lora_a")
         self.b = _cuda(b.detach().to(torch.bfloat16), "lora_b")
+        # when set, moe_backward_dx also fills grad_a [E, r, I] / grad_b [E, H, r] (fp32)
+        self.compute_grads = bool(compute_grads)
+        self.grad_a: torch.Tensor | None = None
+        self.grad_b: torch.Tensor | None = None
         E, r, I = self.a.shape
         if tuple(self.b.shape[::2]) != (E, r) or r > 32:
             raise ValueError(f"LoRA factors must be A [E, r, I] and B [E, H, r] with r <= 32, got "
@@ -354,7 +359,8 @@ def _wptr(w):
 
 
 def down_dx(grad_y: torch.Tensor, offsets: torch.Tensor, w2, gate_up: torch.Tensor, *, inter: int,
-            out: torch.Tensor | None = None, lora: DownLoRA | None = None) -> torch.Tensor:
+            out: torch.Tensor | None = None, lora: DownLoRA | None = None,
+            rank_a: torch.Tensor | None = None) -> torch.Tensor:
     """grad_gate_up [S, 2I] = SwiGLU backward of (gate, up) given dh = grad_y W2
     (+ the LoRA path's input gradient when ``lora``)."""
     w2 = _as_weight(w2)
@@ -368,10 +374,24 @@ def down_dx(grad_y: torch.Tensor, offsets: torch.Tensor, w2, gate_up: torch.Tens
                   _wptr(w2), _ptr(gu), _ptr(dgu), _stream())
         return dgu
     E, Hb, r = lora.b.shape
-    glow = lora_project(gy, offsets, lora.b, (Hb * r, 1, r), lora.rank, lora.scale)
+    glow = rank_a if rank_a is not None else lora_project(gy, offsets, lora.b, (Hb * r, 1, r), lora.rank,
+                                                          lora.scale)
     _lib.call(f"mirai_moe_down_dx_lora_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), offsets.numel(), S, H, inter,
               _wptr(w2), _ptr(gu), _ptr(glow), _ptr(lora.a_pad()), _ptr(dgu), _stream())
     return dgu
+
+
+def lora_grad(x: torch.Tensor, g_rank: torch.Tensor, offsets: torch.Tensor, rank: int, out: torch.Tensor,
+              strides) -> torch.Tensor:
+    """out[e][j][k] = sum over segment e of g_rank[s, j] * x[s, k] (fp32, by strides)."""
+    x = _cuda(x, "x", torch.bfloat16)
+    g = _cuda(g_rank, "g_rank", torch.bfloat16)
+    offsets = _cuda(offsets, "offsets", torch.int32)
+    S, K = x.shape
+    se, sr, sk = (int(v) for v in strides)
+    _lib.call("mirai_moe_lora_grad", _ptr(x), _ptr(g), _ptr(offsets), offsets.numel(), S, K, int(rank), _ptr(out),
+              se, sr, sk, _stream())
+    return out
 
 
 def gateup_dx(grad_gate_up: torch.Tensor, offsets: torch.Tensor, w1, w3, *, hidden: int,
@@ -407,6 +427,8 @@ class ForwardState:
     y_sorted: torch.Tensor   # [S, H] bf16 expert outputs
     gate_up: torch.Tensor    # [S, 2I] bf16 saved pre-activations
     top_weights: torch.Tensor
+    h: torch.Tensor | None = None         # [S, I] bf16, kept when LoRA factor grads are wanted
+    rank_a: torch.Tensor | None = None    # [S, 64] LoRA rank block of h (scaled)
 
 
 def moe_forward_train(tokens, top_indices, top_weights, w1, w3, w2, *, num_experts: int, inter: int,
@@ -415,9 +437,13 @@ def moe_forward_train(tokens, top_indices, top_weights, w1, w3, w2, *, num_exper
     plan = dispatch_plan(top_indices, num_experts)
     xs = permute_rows(tokens, plan.sorted_token_indices)
     h, gu = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter, save_gate_up=True)
-    y = down(h, plan.offsets, w2, hidden=tokens.shape[1], lora=lora)
+    low = None
+    if lora is not None:
+        low = lora_project(h, plan.offsets, lora.a, lora.a.stride(), lora.rank, lora.scale)
+    y = down(h, plan.offsets, w2, hidden=tokens.shape[1], lora=lora, rank_a=low)
     out = combine(y, plan.inverse_order, top_weights, out_dtype=out_dtype or tokens.dtype)
-    return out, ForwardState(plan, y, gu, top_weights.float())
+    keep = lora is not None and lora.compute_grads
+    return out, ForwardState(plan, y, gu, top_weights.float(), h if keep else None, low if keep else None)
 
 
 def moe_backward_dx(grad_out: torch.Tensor, state: ForwardState, w1, w3, w2, *, inter: int,
@@ -428,7 +454,19 @@ def moe_backward_dx(grad_out: torch.Tensor, state: ForwardState, w1, w3, w2, *, 
     plan = state.plan
     H = state.y_sorted.shape[1]
     gy, gw = combine_backward(grad_out, state.y_sorted, plan.inverse_order, state.top_weights)
-    dgu = down_dx(gy, plan.offsets, w2, state.gate_up, inter=inter, lora=lora)
+    glow = None
+    if lora is not None:
+        E, Hb, r = lora.b.shape
+        glow = lora_project(gy, plan.offsets, lora.b, (Hb * r, 1, r), lora.rank, lora.scale)
+        if lora.compute_grads:
+            if state.h is None or state.rank_a is None:
+                raise RuntimeError("LoRA factor gradients need the forward run with compute_grads=True")
+            Ia = lora.a.shape[2]
+            lora.grad_a = lora_grad(state.h, glow, plan.offsets, r,
+                                    torch.empty((E, r, Ia), dtype=torch.float32, device=gy.device), (r * Ia, Ia, 1))
+            lora.grad_b = lora_grad(gy, state.rank_a, plan.offsets, r,
+                                    torch.empty((E, Hb, r), dtype=torch.float32, device=gy.device), (Hb * r, 1, r))
+    dgu = down_dx(gy, plan.offsets, w2, state.gate_up, inter=inter, lora=lora, rank_a=glow)
     dxs = gateup_dx(dgu, plan.offsets, w1, w3, hidden=H)
     dx = combine(dxs, plan.inverse_order, None, out_dtype=out_dtype, top_k=plan.top_k)
     return dx, gw

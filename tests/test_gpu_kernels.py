@@ -408,3 +408,41 @@ def test_lora_on_down_forward_and_dx(fmt, rank):
     # the adapter matters: without it the forward differs by far more than the tolerance
     ref0 = om.moe_forward(x, ridx, rw, *dense, bf16=True)
     assert om.rel_max_err(ref0, ref) > 5 * om.rel_max_err(_f32(out), ref)
+
+
+def test_lora_factor_gradients():
+    """dA / dB of the down-projection adapter against the bmm backward formulas."""
+    dev = _dev()
+    from mirai_b200 import ops
+    T, H, E, k, I, r = 300, 256, 4, 2, 256, 8
+    rng = np.random.default_rng(17)
+    x = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    logits = (rng.standard_normal((T, E)) * 1.5).astype(np.float32)
+    dense, dw = _weights("bf16", rng, E, H, I, dev)
+    la = oq.bf16_round((rng.standard_normal((E, r, I)) * 0.05).astype(np.float32))
+    lb = oq.bf16_round((rng.standard_normal((E, H, r)) * 0.05).astype(np.float32))
+    scale = 2.0
+    g = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    lora = ops.DownLoRA(_bf16(la).to(dev), _bf16(lb).to(dev), scale, compute_grads=True)
+    idx, w = ops.route_topk(torch.from_numpy(logits).to(dev), k)
+    out, st = ops.moe_forward_train(_bf16(x).to(dev), idx, w, *dw, num_experts=E, inter=I, lora=lora)
+    ops.moe_backward_dx(_bf16(g).to(dev), st, *dw, inter=I, lora=lora)
+    _check(ops)
+    ridx, rw = om.route_topk(logits, k)
+    plan = om.dispatch_plan(ridx, E)
+    xs = om.permute(x, plan["sorted_token_indices"])
+    _, inter = om.expert_ffn_forward(xs, plan["offsets"], *dense, bf16=True,
+                                     lora={"a": la, "b": lb, "scale": scale}, keep=True)
+    sp = plan["sort_positions"]
+    gy = oq.bf16_round(g[sp // k] * rw.reshape(-1)[sp][:, None])
+    ga = np.zeros((E, r, I), np.float32)
+    gb = np.zeros((E, H, r), np.float32)
+    start = 0
+    for e in range(E):
+        end = plan["offsets"][e]
+        h_e, gy_e = inter["h"][start:end], gy[start:end]
+        gb[e] = scale * gy_e.T @ (h_e @ la[e].T)
+        ga[e] = scale * (gy_e @ lb[e]).T @ h_e
+        start = end
+    assert om.rel_max_err(lora.grad_a.cpu().numpy(), ga) < 3e-2
+    assert om.rel_max_err(lora.grad_b.cpu().numpy(), gb) < 3e-2
