@@ -45,7 +45,9 @@ constexpr int BN = 256;  // output columns per tile
 constexpr int BK = 64;
 constexpr int UMMA_K = 16;
 constexpr uint32_t A_BYTES = BM * BK * 2;
-constexpr int kEpiWarps = 4;
+// epilogue warps: 8 when the SM has no dequantisers (two per TMEM lane
+// quarter, splitting the columns), 4 otherwise
+constexpr int epi_warps(int wf) { return wf == 0 ? 8 : 4; }
 constexpr int kDeqWarps = 8;
 constexpr int kDeqThreads = 32 * kDeqWarps;
 constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -69,7 +71,10 @@ template <int WF, bool PAIR> struct Cfg {
   static constexpr int ROW_BYTES = WF == W_NF4 ? BK / 2 : (WF == W_INT8 ? BK : 0);  // raw bytes / 64 elements
   static constexpr uint32_t RAW_BYTES = B_ROWS * ROW_BYTES;
   static constexpr int STAGES = WF == W_BF16 ? (PAIR ? 6 : 4) : (PAIR ? 4 : 3);
-  static constexpr int THREADS = 64 + 32 * kEpiWarps + (WF == W_BF16 ? 0 : kDeqThreads);
+  // raw-code ring: its own producer warp runs ahead of the operand ring
+  static constexpr int RAW_STAGES = WF == W_BF16 ? 1 : (WF == W_NF4 ? (PAIR ? 8 : 6) : (PAIR ? 6 : 3));
+  static constexpr int EPI_WARPS = epi_warps(WF);
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS + (WF == W_BF16 ? 0 : kDeqThreads + 32);
   static constexpr int TPR = kDeqThreads / B_ROWS;                       // dequant threads per B row
   static constexpr int ELEMS = BK / TPR;                                 // elements per dequant thread
 };
@@ -107,8 +112,8 @@ template <int WF, bool PAIR>
 struct Smem {
   uint64_t full[Cfg<WF, PAIR>::STAGES];
   uint64_t empty[Cfg<WF, PAIR>::STAGES];
-  uint64_t raw_full[Cfg<WF, PAIR>::STAGES];
-  uint64_t raw_empty[Cfg<WF, PAIR>::STAGES];
+  uint64_t raw_full[Cfg<WF, PAIR>::RAW_STAGES];
+  uint64_t raw_empty[Cfg<WF, PAIR>::RAW_STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint32_t tmem_base;
@@ -129,7 +134,8 @@ struct DeqSmem {
 template <int WF, bool PAIR>
 constexpr size_t smem_bytes() {
   using C = Cfg<WF, PAIR>;
-  return 1024 + C::STAGES * (A_BYTES + C::B_BYTES + C::RAW_BYTES) + sizeof(Smem<WF, PAIR>) +
+  return 1024 + C::STAGES * (A_BYTES + C::B_BYTES) + (WF == W_BF16 ? 0 : C::RAW_STAGES * C::RAW_BYTES) +
+         sizeof(Smem<WF, PAIR>) +
          (WF == W_BF16 ? 0 : sizeof(DeqSmem));
 }
 
@@ -246,7 +252,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   uint8_t* sA = base;
   uint8_t* sB = sA + STAGES * A_BYTES;
   uint8_t* sRaw = sB + STAGES * B_BYTES;
-  Smem<WF, PAIR>& sm = *reinterpret_cast<Smem<WF, PAIR>*>(sRaw + STAGES * RAW_BYTES);
+  constexpr int RAW_STAGES = C::RAW_STAGES;
+  Smem<WF, PAIR>& sm = *reinterpret_cast<Smem<WF, PAIR>*>(sRaw + (QUANT ? RAW_STAGES * RAW_BYTES : 0));
   DeqSmem* dq = reinterpret_cast<DeqSmem*>(reinterpret_cast<uint8_t*>(&sm) + sizeof(Smem<WF, PAIR>));
 
   const int warp = threadIdx.x >> 5;
@@ -299,12 +306,14 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         // every dequantiser warp of the pair
         mbar_init(&sm.full[s], 1 + (QUANT ? kDeqWarps * pair_mult : 0));
         mbar_init(&sm.empty[s], 1);
+      }
+      for (int s = 0; s < RAW_STAGES; ++s) {
         mbar_init(&sm.raw_full[s], 1);
         mbar_init(&sm.raw_empty[s], kDeqWarps);
       }
       for (int a = 0; a < 2; ++a) {
         mbar_init(&sm.tfull[a], 1);
-        mbar_init(&sm.tempty[a], kEpiWarps * pair_mult);
+        mbar_init(&sm.tempty[a], C::EPI_WARPS * pair_mult);
       }
       sm.abort_flag = 0;
       fence_mbar_init();
@@ -323,8 +332,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     prefetch_tmap(&tmap_b0);
     prefetch_tmap(&tmap_b1);
   }
-  if (WF == W_NF4 && warp >= 2 + kEpiWarps) {
-    const int d = threadIdx.x - 32 * (2 + kEpiWarps);
+  if (WF == W_NF4 && warp >= 2 + C::EPI_WARPS) {
+    const int d = threadIdx.x - 32 * (2 + C::EPI_WARPS);
     for (int h = 0; h < 2; ++h) {
       for (int i = d; i < 256; i += kDeqThreads) dq->ncode[h][i] = __ldg(p.q[h].nested_code + i);
       if (d < 16) dq->code[h][d] = __ldg(p.q[h].code + d);
@@ -402,30 +411,6 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             }
           }
           if (!ext) load(sA + stage * A_BYTES, &tmap_a, kb * BK, row0);
-          if (QUANT) {
-            if (!mbar_wait(&sm.raw_empty[stage], phase ^ 1, 11)) {
-              *abort_flag = 1;
-              break;
-            }
-            // the rank block has no raw codes: complete the raw stage empty
-            mbar_arrive_expect_tx(&sm.raw_full[stage], ext ? 0u : RAW_BYTES);
-          }
-          if (QUANT && !ext) {
-            uint8_t* r_dst = sRaw + stage * RAW_BYTES;
-            constexpr int RB = C::ROW_BYTES;
-            if (MN) {
-#pragma unroll
-              for (int nb = 0; nb < C::B_ROWS / 64; ++nb)
-                tma_load_2d(r_dst + nb * 64 * RB, mb, (n * BN + (int)rank * C::B_ROWS + nb * 64) * RB / 64, krow,
-                            &sm.raw_full[stage]);
-            } else if (PAIR) {
-              tma_load_2d(r_dst, mb, kb * RB, kmajor_row<MODE>(p, e, n, (int)rank), &sm.raw_full[stage]);
-            } else {
-              tma_load_2d(r_dst, &tmap_b0, kb * RB, kmajor_row<MODE>(p, e, n, 0), &sm.raw_full[stage]);
-              tma_load_2d(r_dst + RAW_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * RB,
-                          kmajor_row<MODE>(p, e, n, 1), &sm.raw_full[stage]);
-            }
-          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -490,9 +475,12 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         else umma_commit(&sm.tfull[acc]);
       }
     }
-  } else if (warp < 2 + kEpiWarps) {
+  } else if (warp < 2 + C::EPI_WARPS) {
     // ======================= epilogue =======================
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // warps sharing a lane quarter split the 32-column chunks between them
+    constexpr int NSPLIT = C::EPI_WARPS / 4;
+    const int part = (warp - 2) / 4;
     const uint32_t tempty_leader[2] = {leader_addr(&sm.tempty[0]), leader_addr(&sm.tempty[1])};
     int it = 0;
     for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++it) {
@@ -513,7 +501,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       if (MODE == GATEUP) {
         const int col0 = n * (BN / 2);
 #pragma unroll 1
-        for (int c = 0; c < (BN / 2) / 32; ++c) {
+        for (int c = part * (4 / NSPLIT); c < (part + 1) * (4 / NSPLIT); ++c) {
           uint32_t g[32], u[32];
           tmem_ld_32x32b_x32(tb + c * 32, g);
           tmem_ld_32x32b_x32(tb + BN / 2 + c * 32, u);
@@ -526,8 +514,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
               // silu(gate), and the product (experts.py:301-317).
               const float g0 = bf16r(__uint_as_float(g[2 * j])), g1 = bf16r(__uint_as_float(g[2 * j + 1]));
               const float u0 = bf16r(__uint_as_float(u[2 * j])), u1 = bf16r(__uint_as_float(u[2 * j + 1]));
-              const float a0 = bf16r(g0 / (1.f + expf(-g0)));
-              const float a1 = bf16r(g1 / (1.f + expf(-g1)));
+              const float a0 = bf16r(__fdividef(g0, 1.f + __expf(-g0)));
+              const float a1 = bf16r(__fdividef(g1, 1.f + __expf(-g1)));
               hp[j] = pack_bf16x2(a0 * u0, a1 * u1);
               gp[j] = pack_bf16x2(g0, g1);
               up[j] = pack_bf16x2(u0, u1);
@@ -552,7 +540,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         // (autograd of experts.py:301-317 in bf16: mul, silu backward)
         const int64_t ld2 = 2 * (int64_t)p.N;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = part * (8 / NSPLIT); c < (part + 1) * (8 / NSPLIT); ++c) {
           const int col = n * BN + c * 32;
           uint32_t v32[32];
           tmem_ld_32x32b_x32(tb + c * 32, v32);
@@ -575,7 +563,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
                 const float dh = bf16r(__uint_as_float(v32[2 * j + hh]));
                 const float gv = hh ? bf16_hi(gw[j]) : bf16_lo(gw[j]);
                 const float uv = hh ? bf16_hi(uw[j]) : bf16_lo(uw[j]);
-                const float sg = 1.f / (1.f + expf(-gv));
+                const float sg = __fdividef(1.f, 1.f + __expf(-gv));
                 const float act = bf16r(gv * sg);
                 const float dact = bf16r(dh * uv);
                 duo[hh] = dh * act;
@@ -596,7 +584,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       } else {
         const int col0 = n * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = part * (8 / NSPLIT); c < (part + 1) * (8 / NSPLIT); ++c) {
           uint32_t v32[32];
           tmem_ld_32x32b_x32(tb + c * 32, v32);
           tmem_ld_wait();
@@ -617,6 +605,49 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         else mbar_arrive(&sm.tempty[acc]);
       }
     }
+  } else if (QUANT && warp == 2 + C::EPI_WARPS + kDeqWarps) {
+    // ======================= raw-code producer (NF4 / INT8) =======================
+    // Streams this CTA's share of the packed codes of every k-block into the
+    // raw ring, up to RAW_STAGES ahead of the dequantisers.
+    if (lane == 0) {
+      int rstage = 0;
+      uint32_t rphase = 0;
+      constexpr int RB = C::ROW_BYTES;
+      for (int t = unit; t < total_tiles && !*abort_flag; t += num_units) {
+        int e, m, n;
+        decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
+        for (int kb = 0; kb < total_kb; ++kb) {
+          if (!mbar_wait(&sm.raw_empty[rstage], rphase ^ 1, 11)) {
+            *abort_flag = 1;
+            break;
+          }
+          const bool ext = kb == num_kb;  // the rank block has no raw codes: an empty stage
+          mbar_arrive_expect_tx(&sm.raw_full[rstage], ext ? 0u : RAW_BYTES);
+          if (!ext) {
+            const bool key1 = MCfg<MODE>::TWO_KEYS && (MN ? kb >= p.kb_half : (PAIR && rank == 1));
+            const CUtensorMap* mb = key1 ? &tmap_b1 : &tmap_b0;
+            const int krow = MN ? e * p.krows + (kb - (key1 ? p.kb_half : 0)) * BK : 0;
+            uint8_t* r_dst = sRaw + rstage * RAW_BYTES;
+            if (MN) {
+#pragma unroll
+              for (int nb = 0; nb < C::B_ROWS / 64; ++nb)
+                tma_load_2d(r_dst + nb * 64 * RB, mb, (n * BN + (int)rank * C::B_ROWS + nb * 64) * RB / 64, krow,
+                            &sm.raw_full[rstage]);
+            } else if (PAIR) {
+              tma_load_2d(r_dst, mb, kb * RB, kmajor_row<MODE>(p, e, n, (int)rank), &sm.raw_full[rstage]);
+            } else {
+              tma_load_2d(r_dst, &tmap_b0, kb * RB, kmajor_row<MODE>(p, e, n, 0), &sm.raw_full[rstage]);
+              tma_load_2d(r_dst + RAW_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * RB,
+                          kmajor_row<MODE>(p, e, n, 1), &sm.raw_full[rstage]);
+            }
+          }
+          if (++rstage == RAW_STAGES) {
+            rstage = 0;
+            rphase ^= 1;
+          }
+        }
+      }
+    }
   } else if (QUANT) {
     // ======================= dequantisers =======================
     // This CTA's B block holds B_ROWS rows of 64 elements per stage (K-major:
@@ -625,7 +656,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     constexpr int TPR = C::TPR;
     constexpr int ELEMS = C::ELEMS;
     constexpr int RB = C::ROW_BYTES;
-    const int d = threadIdx.x - 32 * (2 + kEpiWarps);
+    const int d = threadIdx.x - 32 * (2 + C::EPI_WARPS);
     const int row = d / TPR;            // B row inside the stage
     const int part = d % TPR;           // which ELEMS-element slice of the row
     const int nkb = num_kb;
@@ -637,6 +668,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     const int nblk_row = p.N / 64;      // MN: NF4 blocks per weight row
     int stage = 0;
     uint32_t phase = 0;
+    int rstage = 0;  // raw ring position
+    uint32_t rphase = 0;
     float code[16];
     for (int t = unit; t < total_tiles && !*abort_flag; t += num_units) {
       int e, m, n;
@@ -696,7 +729,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       const int absq_row = PAIR ? 0 : kblk;  // absq block of this thread (K-major)
       int cur_key = -1;
       for (int kb = 0; kb < total_kb; ++kb) {
-        bool ok = mbar_wait(&sm.raw_full[stage], phase, 40);
+        bool ok = mbar_wait(&sm.raw_full[rstage], rphase, 40);
         ok = ok && mbar_wait(&sm.empty[stage], phase ^ 1, 41);
         if (!ok) {
           *abort_flag = 1;
@@ -705,7 +738,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         if (kb == nkb) {  // rank block: B arrives by TMA, nothing to decode
           __syncwarp();
           if (lane == 0) {
-            mbar_arrive(&sm.raw_empty[stage]);
+            mbar_arrive(&sm.raw_empty[rstage]);
             if (PAIR) mbar_arrive_cluster(full_leader0 + 8u * stage);
             else mbar_arrive(&sm.full[stage]);
           }
@@ -713,10 +746,14 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             stage = 0;
             phase ^= 1;
           }
+          if (++rstage == RAW_STAGES) {
+            rstage = 0;
+            rphase ^= 1;
+          }
           continue;
         }
         const int key = MN ? ((MCfg<MODE>::TWO_KEYS && kb >= p.kb_half) ? 1 : 0) : row_key;
-        const uint8_t* raw = sRaw + stage * RAW_BYTES + row * RB + part * (ELEMS * RB / 64);
+        const uint8_t* raw = sRaw + rstage * RAW_BYTES + row * RB + part * (ELEMS * RB / 64);
         const uint32_t row_addr = smem_u32(sB + stage * B_BYTES) + (uint32_t)row * 128u;
         const int sw = kr & 7;
         constexpr int CH = ELEMS / 8;  // 16-byte chunks of this thread
@@ -770,13 +807,17 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&sm.raw_empty[stage]);
+          mbar_arrive(&sm.raw_empty[rstage]);
           if (PAIR) mbar_arrive_cluster(full_leader0 + 8u * stage);
           else mbar_arrive(&sm.full[stage]);
         }
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
+        }
+        if (++rstage == RAW_STAGES) {
+          rstage = 0;
+          rphase ^= 1;
         }
       }
     }
