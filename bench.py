@@ -40,6 +40,10 @@ METRIC = "MoE-FFN tokens/s (NF4 experts) + % TC/HBM roofline at 1/2/4/8 B200"
 # Our kernels launched by one forward step: route 1, plan 4, permute 1, gate/up 1, down 1,
 # combine 1; a train step adds combine-backward, down-dX, gate/up-dX and the un-permute sum.
 KERNELS_PER_STEP = 9
+# train step: + combine-backward, down-dX, gate/up-dX, un-permute sum, and the
+# LoRA kernels (2 projections, 2 factor gradients)
+TRAIN_EXTRA_KERNELS = 8
+LORA_RANK = 16
 # DRAM bytes (read + write) of one gate/up launch from an ncu capture, per
 # workload; see profiles/ for the capture and its command.  None until captured.
 NCU_TRAFFIC = {}
@@ -166,8 +170,15 @@ def run_ours(args, cfg, rank, world, dev):
     x, logits, (w1, w3, w2) = make_workload(cfg, dev, seed=1234 + rank)
     S = T * k
     train = args.mode == "train"
-    g_out = torch.randn(T, H, device=dev, generator=torch.Generator(device=dev).manual_seed(99 + rank)).to(
-        torch.bfloat16) if train else None
+    gen = torch.Generator(device=dev).manual_seed(99 + rank)
+    g_out = torch.randn(T, H, device=dev, generator=gen).to(torch.bfloat16) if train else None
+    lora = None
+    if train:
+        # rank-16 LoRA on the down projection (alpha 16: scale alpha / rank = 1), lora_b perturbed
+        # away from its zero init as the reference's adapter tests do
+        la = torch.randn(E, LORA_RANK, I, device=dev, generator=gen) * (1.0 / I ** 0.5)
+        lb = torch.randn(E, H, LORA_RANK, device=dev, generator=gen) * 0.02
+        lora = ops.DownLoRA(la, lb, 16.0 / LORA_RANK, compute_grads=True)
 
     def step(xin, lin, out=None, gin=None, dx_out=None):
         idx, tw = ops.route_topk(lin, k)
@@ -177,10 +188,10 @@ def run_ours(args, cfg, rank, world, dev):
             h = ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I)
             y = ops.down(h, plan.offsets, w2, hidden=H)
             return ops.combine(y, plan.inverse_order, tw, out=out)
-        o, st = ops.moe_forward_train(xin, idx, tw, w1, w3, w2, num_experts=E, inter=I)
+        o, st = ops.moe_forward_train(xin, idx, tw, w1, w3, w2, num_experts=E, inter=I, lora=lora)
         if out is not None:
             out.copy_(o)
-        dx, _ = ops.moe_backward_dx(g_out if gin is None else gin, st, w1, w3, w2, inter=I)
+        dx, _ = ops.moe_backward_dx(g_out if gin is None else gin, st, w1, w3, w2, inter=I, lora=lora)
         if dx_out is not None:
             dx_out.copy_(dx)
         return o
@@ -293,13 +304,15 @@ def run_ours(args, cfg, rank, world, dev):
         "data": "synthetic (seeded torch.randn; random-init experts quantised on the GPU)",
         "config": {
             "workload": f"{args.config}: one routed expert FFN layer "
-                        + ("forward + dX backward" if train else "forward") + f", T={T} H={H} E={E} k={k} I={I} "
+                        + (f"forward + dX backward with a rank-{LORA_RANK} LoRA on w2 (adapter grads included)"
+                           if train else "forward") + f", T={T} H={H} E={E} k={k} I={I} "
                         f"{cfg['fmt']} experts" + (f", Zipf({cfg['zipf']}) load" if cfg["zipf"] else ""),
             "tokens_per_gpu": T, "hidden": H, "experts": E, "top_k": k, "intermediate": I,
             "weights": cfg["fmt"], "parallelism": f"dp{world} token-parallel replicas (experts replicated)",
             "l2": f"no flush: inputs {(T * H * 2 + weight_bytes(cfg)) / 1e6:.0f} MB per step exceed the 126 MB L2",
         },
-        "tflops": world * (12.0 if train else 6.0) * S * H * I / (ms * 1e-3) / 1e12,
+        "tflops": world * ((12.0 * S * H * I + 6.0 * S * LORA_RANK * (H + I)) if train else 6.0 * S * H * I)
+                  / (ms * 1e-3) / 1e12,
         "kernel_ms": {"gateup_swiglu": gu_ms, "down": down_ms},
         "roofline": {
             "kernel": f"gateup_swiglu_{cfg['fmt']}",
@@ -318,7 +331,7 @@ def run_ours(args, cfg, rank, world, dev):
             "h2d_bytes_per_step": T * H * 2 * (2 if train else 1) + T * E * 4,
             "d2h_bytes_per_step": T * H * 2 * (2 if train else 1),
         },
-        "gpu_launches": (KERNELS_PER_STEP + (4 if train else 0)) * args.steps,
+        "gpu_launches": (KERNELS_PER_STEP + (TRAIN_EXTRA_KERNELS if train else 0)) * args.steps,
         "clocks": clk,
     }
     return line

@@ -23,7 +23,7 @@ from typing import Any
 import torch
 
 from . import _lib
-from .experts import GroupedExpertWeights, run_routed
+from .experts import GroupedExpertWeights, down_lora_of, run_routed
 
 BACKEND_NAME = "b200"
 
@@ -64,9 +64,10 @@ class B200MoEKernelBackend:
     @staticmethod
     def module_reason(experts: Any) -> str | None:
         """Why this expert module cannot run here (None when it can)."""
-        lora = getattr(experts, "expert_lora", None)
-        if lora is not None and len(lora) > 0:
-            return "expert LoRA adapters are attached (not fused by this backend)"
+        try:
+            down_lora_of(experts)
+        except _lib.MiraiError as exc:
+            return str(exc)
         if callable(getattr(experts, "has_logical_expert_aliases", None)) and experts.has_logical_expert_aliases():
             return "logical expert aliases are not supported"
         return None
@@ -91,7 +92,7 @@ class B200MoEKernelBackend:
             if self.strict:
                 raise RuntimeError(f"memory.moe_kernel_backend='{BACKEND_NAME}' cannot run this layer: {reason}")
             return None
-        return run_routed(weights, tokens, top_scores, top_indices)
+        return run_routed(weights, tokens, top_scores, top_indices, lora=down_lora_of(experts))
 
 
 def build_moe_kernel_backend(value: str | None, *, direct_routed: bool = False):

@@ -728,97 +728,120 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       }
       const int absq_row = PAIR ? 0 : kblk;  // absq block of this thread (K-major)
       int cur_key = -1;
-      for (int kb = 0; kb < total_kb; ++kb) {
-        bool ok = mbar_wait(&sm.raw_full[rstage], rphase, 40);
-        ok = ok && mbar_wait(&sm.empty[stage], phase ^ 1, 41);
-        if (!ok) {
+      // Two k-blocks are in flight per iteration: both stages' codes, scales
+      // and tables are prepared before either is decoded, so the memory and
+      // table latencies of one block overlap the decode of the other, and one
+      // proxy fence covers both hand-offs.
+      constexpr int CH = ELEMS / 8;  // 16-byte chunks of this thread per k-block
+      const int c0 = part * CH;
+      const int sw = kr & 7;
+      bool failed = false;
+      for (int kb = 0; kb < total_kb && !failed; kb += 2) {
+        const int nk = total_kb - kb >= 2 ? 2 : 1;
+        int st[2], rst[2];
+        uint32_t ph[2], rph[2];
+        st[0] = stage, rst[0] = rstage, ph[0] = phase, rph[0] = rphase;
+        st[1] = stage + 1 == STAGES ? 0 : stage + 1;
+        ph[1] = stage + 1 == STAGES ? phase ^ 1 : phase;
+        rst[1] = rstage + 1 == RAW_STAGES ? 0 : rstage + 1;
+        rph[1] = rstage + 1 == RAW_STAGES ? rphase ^ 1 : rphase;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          if (i < nk && !failed) {
+            bool ok = mbar_wait(&sm.raw_full[rst[i]], rph[i], 40);
+            ok = ok && mbar_wait(&sm.empty[st[i]], ph[i] ^ 1, 41);
+            if (!ok) failed = true;
+          }
+        }
+        if (failed) {
           *abort_flag = 1;
           break;
         }
-        if (kb == nkb) {  // rank block: B arrives by TMA, nothing to decode
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&sm.raw_empty[rstage]);
-            if (PAIR) mbar_arrive_cluster(full_leader0 + 8u * stage);
-            else mbar_arrive(&sm.full[stage]);
-          }
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-          if (++rstage == RAW_STAGES) {
-            rstage = 0;
-            rphase ^= 1;
-          }
-          continue;
-        }
-        const int key = MN ? ((MCfg<MODE>::TWO_KEYS && kb >= p.kb_half) ? 1 : 0) : row_key;
-        const uint8_t* raw = sRaw + rstage * RAW_BYTES + row * RB + part * (ELEMS * RB / 64);
-        const uint32_t row_addr = smem_u32(sB + stage * B_BYTES) + (uint32_t)row * 128u;
-        const int sw = kr & 7;
-        constexpr int CH = ELEMS / 8;  // 16-byte chunks of this thread
-        const int c0 = part * CH;
-        if (WF == W_NF4) {
-          if (key != cur_key) {
+        // ---- prepare: raw words and (NF4) the block's 16-entry product table
+        constexpr int NW = WF == W_INT8 ? 2 * CH : CH;  // 32-bit words of raw codes per k-block
+        uint32_t words[2][NW];
+        Nf4Tab tab[2];
+        float iscale[2] = {0.f, 0.f};
+        bool dec[2] = {false, false};
 #pragma unroll
-            for (int i = 0; i < 16; ++i) code[i] = dq->code[key][i];
-            cur_key = key;
-          }
-          int blk;
-          uint32_t qcode;
-          bool live = row_live;
-          if (!MN) {
-            blk = (wrow_base + kr) * nkb + kb;
-            qcode = dq->absq[absq_row * 128 * nkb + kr * nkb + kb];
-          } else {
-            const int kk = kb * BK + kr;        // k-row across both keys
-            const int wr = kk - key * p.krows;  // k-row inside the key's matrix
-            const int nbg = n * 4 + nbase + nbq;
-            live = nbg < nblk_row;
-            blk = wr * nblk_row + nbg;
-            qcode = dq->absq[kk * (C::B_ROWS / 64) + nbq];
-          }
-          const float scale =
-              live ? __fadd_rn(__fmul_rn(dq->ncode[key][qcode], dq->nested[key][blk >> p.nbs_shift]), off[key]) : 0.f;
-          Nf4Tab tab;
-          nf4_table(code, scale, tab);
-          uint32_t words[CH];
+        for (int i = 0; i < 2; ++i) {
+          const int kbi = kb + i;
+          dec[i] = i < nk && kbi != nkb;  // the rank block arrives by TMA: nothing to decode
+          if (!dec[i]) continue;
+          const uint8_t* raw = sRaw + rst[i] * RAW_BYTES + row * RB + part * (ELEMS * RB / 64);
 #pragma unroll
-          for (int v = 0; v < CH / 4; ++v) {
+          for (int v = 0; v < NW / 4; ++v) {
             const uint4 r4 = reinterpret_cast<const uint4*>(raw)[v];
-            words[4 * v] = r4.x, words[4 * v + 1] = r4.y, words[4 * v + 2] = r4.z, words[4 * v + 3] = r4.w;
+            words[i][4 * v] = r4.x, words[i][4 * v + 1] = r4.y, words[i][4 * v + 2] = r4.z, words[i][4 * v + 3] = r4.w;
           }
+          const int key = MN ? ((MCfg<MODE>::TWO_KEYS && kbi >= p.kb_half) ? 1 : 0) : row_key;
+          if (WF == W_NF4) {
+            if (key != cur_key) {
 #pragma unroll
-          for (int c = 0; c < CH; ++c) {
-            uint32_t o[4];
-            nf4_word(words[c], tab, o);
-            st_shared_v4(row_addr + (uint32_t)(((c0 + c) ^ sw) << 4), o[0], o[1], o[2], o[3]);
+              for (int j = 0; j < 16; ++j) code[j] = dq->code[key][j];
+              cur_key = key;
+            }
+            int blk;
+            uint32_t qcode;
+            bool live = row_live;
+            if (!MN) {
+              blk = (wrow_base + kr) * nkb + kbi;
+              qcode = dq->absq[absq_row * 128 * nkb + kr * nkb + kbi];
+            } else {
+              const int kk = kbi * BK + kr;       // k-row across both keys
+              const int wr = kk - key * p.krows;  // k-row inside the key's matrix
+              const int nbg = n * 4 + nbase + nbq;
+              live = nbg < nblk_row;
+              blk = wr * nblk_row + nbg;
+              qcode = dq->absq[kk * (C::B_ROWS / 64) + nbq];
+            }
+            const float scale = live ? __fadd_rn(__fmul_rn(dq->ncode[key][qcode], dq->nested[key][blk >> p.nbs_shift]),
+                                                 off[key])
+                                     : 0.f;
+            nf4_table(code, scale, tab[i]);
+          } else {
+            iscale[i] = MN ? reinterpret_cast<const float*>(dq->absq)[kbi * BK + kr] : row_scale;
           }
-        } else {
-          const float scale = MN ? reinterpret_cast<const float*>(dq->absq)[kb * BK + kr] : row_scale;
+        }
+        // ---- decode into the swizzled operand rows
 #pragma unroll
-          for (int v = 0; v < CH / 2; ++v) {
-            uint32_t o[8];
-            int8_x16(reinterpret_cast<const uint4*>(raw)[v], scale, o);
-            st_shared_v4(row_addr + (uint32_t)(((c0 + 2 * v) ^ sw) << 4), o[0], o[1], o[2], o[3]);
-            st_shared_v4(row_addr + (uint32_t)(((c0 + 2 * v + 1) ^ sw) << 4), o[4], o[5], o[6], o[7]);
+        for (int i = 0; i < 2; ++i) {
+          if (!dec[i]) continue;
+          const uint32_t row_addr = smem_u32(sB + st[i] * B_BYTES) + (uint32_t)row * 128u;
+          if (WF == W_NF4) {
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+              uint32_t o[4];
+              nf4_word(words[i][c], tab[i], o);
+              st_shared_v4(row_addr + (uint32_t)(((c0 + c) ^ sw) << 4), o[0], o[1], o[2], o[3]);
+            }
+          } else {
+#pragma unroll
+            for (int v = 0; v < CH / 2; ++v) {
+              uint32_t o[8];
+              int8_x16(make_uint4(words[i][4 * v], words[i][4 * v + 1], words[i][4 * v + 2], words[i][4 * v + 3]),
+                       iscale[i], o);
+              st_shared_v4(row_addr + (uint32_t)(((c0 + 2 * v) ^ sw) << 4), o[0], o[1], o[2], o[3]);
+              st_shared_v4(row_addr + (uint32_t)(((c0 + 2 * v + 1) ^ sw) << 4), o[4], o[5], o[6], o[7]);
+            }
           }
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&sm.raw_empty[rstage]);
-          if (PAIR) mbar_arrive_cluster(full_leader0 + 8u * stage);
-          else mbar_arrive(&sm.full[stage]);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            if (i < nk) {
+              mbar_arrive(&sm.raw_empty[rst[i]]);
+              if (PAIR) mbar_arrive_cluster(full_leader0 + 8u * st[i]);
+              else mbar_arrive(&sm.full[st[i]]);
+            }
+          }
         }
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
-        if (++rstage == RAW_STAGES) {
-          rstage = 0;
-          rphase ^= 1;
-        }
+        stage = st[nk - 1] + 1 == STAGES ? 0 : st[nk - 1] + 1;
+        phase = st[nk - 1] + 1 == STAGES ? ph[nk - 1] ^ 1 : ph[nk - 1];
+        rstage = rst[nk - 1] + 1 == RAW_STAGES ? 0 : rst[nk - 1] + 1;
+        rphase = rst[nk - 1] + 1 == RAW_STAGES ? rph[nk - 1] ^ 1 : rph[nk - 1];
       }
     }
   }

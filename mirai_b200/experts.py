@@ -96,50 +96,108 @@ class GroupedExpertWeights:
 
 
 class _RoutedExpertsFunction(torch.autograd.Function):
-    """Forward through the fused kernels; backward = dX and top-score gradient."""
+    """Forward through the fused kernels; backward = dX, the top-score gradient
+    and, with a down-projection LoRA adapter, the adapter factor gradients."""
 
     @staticmethod
-    def forward(ctx, tokens, top_scores, top_indices, weights: GroupedExpertWeights):
+    def forward(ctx, tokens, top_scores, top_indices, weights: GroupedExpertWeights, lora_a, lora_b, lora_scale):
         x = tokens.to(torch.bfloat16).contiguous()
         out_dtype = tokens.dtype if tokens.dtype in (torch.bfloat16, torch.float32) else torch.float32
-        need_grad = ctx.needs_input_grad[0] or ctx.needs_input_grad[1]
+        need_grad = any(ctx.needs_input_grad[i] for i in (0, 1, 4, 5))
         w = top_scores.float().contiguous()
+        lora = None
+        if lora_a is not None:
+            lora = ops.DownLoRA(lora_a, lora_b, float(lora_scale),
+                                compute_grads=ctx.needs_input_grad[4] or ctx.needs_input_grad[5])
         if need_grad:
             out, state = ops.moe_forward_train(x, top_indices.contiguous(), w, weights.w1, weights.w3, weights.w2,
                                                num_experts=weights.num_experts, inter=weights.inter,
-                                               out_dtype=out_dtype)
+                                               out_dtype=out_dtype, lora=lora)
             ctx.state = state
             ctx.weights = weights
+            ctx.lora = lora
             ctx.token_dtype = tokens.dtype
             ctx.score_dtype = top_scores.dtype
+            ctx.factor_dtypes = (None if lora_a is None else lora_a.dtype, None if lora_b is None else lora_b.dtype)
         else:
             plan = ops.dispatch_plan(top_indices.contiguous(), weights.num_experts)
             xs = ops.permute_rows(x, plan.sorted_token_indices)
             h = ops.gateup_swiglu(xs, plan.offsets, weights.w1, weights.w3, inter=weights.inter)
-            y = ops.down(h, plan.offsets, weights.w2, hidden=weights.hidden)
+            y = ops.down(h, plan.offsets, weights.w2, hidden=weights.hidden, lora=lora)
             out = ops.combine(y, plan.inverse_order, w, out_dtype=out_dtype)
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
         wts = ctx.weights
+        lora = ctx.lora
         dx, dw = ops.moe_backward_dx(grad_out.to(torch.bfloat16).contiguous(), ctx.state, wts.w1, wts.w3, wts.w2,
-                                     inter=wts.inter,
+                                     inter=wts.inter, lora=lora,
                                      out_dtype=torch.float32 if ctx.token_dtype == torch.float32 else torch.bfloat16)
         ctx.state = None
-        return dx.to(ctx.token_dtype), dw.to(ctx.score_dtype), None, None
+        ga = gb = None
+        if lora is not None and lora.compute_grads:
+            ga = lora.grad_a.to(ctx.factor_dtypes[0])
+            gb = lora.grad_b.to(ctx.factor_dtypes[1])
+        return dx.to(ctx.token_dtype), dw.to(ctx.score_dtype), None, None, ga, gb, None
 
 
 def run_routed(weights: GroupedExpertWeights, tokens: torch.Tensor, top_scores: torch.Tensor,
-               top_indices: torch.Tensor) -> torch.Tensor:
-    """``run_direct_routed`` semantics on bound weights (experts.py:1749-1912)."""
+               top_indices: torch.Tensor, lora: tuple | None = None) -> torch.Tensor:
+    """``run_direct_routed`` semantics on bound weights (experts.py:1749-1912).
+
+    ``lora`` = (lora_a [E, r, I], lora_b [E, H, r], scale) adds a LoRA adapter
+    on the down projection (active_expert_lora.py:434-478); gradients flow to
+    both factors."""
     if top_scores.shape != top_indices.shape or top_indices.ndim != 2:
         raise ValueError("Direct routed execution requires matching [tokens, top_k] score and index tensors.")
     if int(top_indices.shape[0]) != int(tokens.shape[0]):
         raise ValueError("Direct routed expert indices do not match token count.")
     if not tokens.is_cuda:
         raise ValueError("the B200 expert path runs on CUDA tensors only (no CPU fallback)")
-    return _RoutedExpertsFunction.apply(tokens, top_scores, top_indices.to(torch.int64), weights)
+    la, lb, sc = lora if lora is not None else (None, None, 1.0)
+    return _RoutedExpertsFunction.apply(tokens, top_scores, top_indices.to(torch.int64), weights, la, lb, sc)
+
+
+def down_lora_of(experts: Any) -> tuple | None:
+    """(lora_a, lora_b, scale) of a plain ActiveExpertLoRA on ``w2``, or None.
+
+    The scale is the adapter's ``lora_scale(alpha, rank, rslora) * lora_scale *
+    rank_schedule_scale`` (active_expert_lora.py:461-466, lora_allocation.py:163-168).
+    Raises for adapters on other keys or with features the fused path does not
+    run (rank / parameter dropout in training, expert selection, timestep or
+    route gates, condenser)."""
+    adapters = getattr(experts, "expert_lora", None)
+    if adapters is None or len(adapters) == 0:
+        return None
+    keys = list(adapters.keys())
+    if keys != ["w2"]:
+        raise ops._lib.MiraiError(2, f"expert LoRA on {keys}: the fused path supports an adapter on w2 only")
+    ad = adapters["w2"]
+    training = bool(getattr(ad, "training", False))
+    unsupported = []
+    if training and float(getattr(ad, "_rank_dropout", 0.0)) > 0.0:
+        unsupported.append("rank dropout")
+    if training and float(getattr(ad, "_lora_parameter_dropout", 0.0)) > 0.0:
+        unsupported.append("parameter dropout")
+    if bool(getattr(ad, "_expert_selection_active", False)):
+        unsupported.append("expert selection mask")
+    if getattr(ad, "_timestep_mask_uniform", None) is not None or getattr(ad, "_tc_gate_hypernet", None) is not None:
+        unsupported.append("timestep / TC gate")
+    cond = getattr(ad, "_condenser", None)
+    if cond is not None and callable(getattr(cond, "delta", None)):
+        probe = getattr(cond, "enabled", None)
+        if probe is True:
+            unsupported.append("condenser")
+    if unsupported:
+        raise ops._lib.MiraiError(2, "expert LoRA features not fused: " + ", ".join(unsupported))
+    if not all(hasattr(ad, n) for n in ("rank", "lora_a", "lora_b")):
+        raise ops._lib.MiraiError(2, f"expert LoRA adapter {type(ad).__name__} on w2 is not an ActiveExpertLoRA")
+    rank = int(ad.rank)
+    alpha = float(ad._alpha()) if callable(getattr(ad, "_alpha", None)) else float(ad.lora_alpha)
+    denom = rank ** 0.5 if bool(getattr(ad, "use_rslora", False)) else float(rank)
+    scale = alpha / denom * float(getattr(ad, "_lora_scale", 1.0)) * float(getattr(ad, "_rank_schedule_scale", 1.0))
+    return ad.lora_a, ad.lora_b, scale
 
 
 class B200GroupedExperts(nn.Module):
@@ -177,6 +235,7 @@ class B200GroupedExperts(nn.Module):
         self.expert_dequant_chunk_size = int(chunk)
         self._loaded: set[str] = set()
         self._bound: GroupedExpertWeights | None = None
+        self.expert_lora = nn.ModuleDict()
 
     # ------------------------------------------------------------------ ingest
     def _set_buffer(self, name: str, value: torch.Tensor) -> None:
@@ -280,6 +339,44 @@ class B200GroupedExperts(nn.Module):
     def prefers_for_loop(self) -> bool:
         return True
 
+    def attach_expert_lora(self, *, tensor_name: str, adapter_name: str = "lora", rank: int, alpha: float,
+                           init: str = "kaiming", use_rslora: bool = False) -> None:
+        """A LoRA adapter on the down projection: lora_a [E, r, I] (kaiming-uniform),
+        lora_b [E, H, r] zeros, scale alpha / rank (or / sqrt(rank) for rsLoRA)."""
+        if tensor_name != "w2":
+            raise ValueError("the fused path supports an expert LoRA adapter on w2 only")
+        if not hasattr(self, "expert_lora"):
+            self.expert_lora = nn.ModuleDict()
+        _, H, I = self._shape_of("w2")
+        self.expert_lora["w2"] = _DownAdapter(self.num_experts, I, H, rank, alpha, use_rslora)
+
+    def _shape_of(self, key: str) -> tuple[int, int, int]:
+        if key in self._nf4_shapes:
+            return self._nf4_shapes[key]
+        for name in (f"{key}_int8", key):
+            t = self._buffers.get(name)
+            if t is not None:
+                return tuple(t.shape)
+        raise RuntimeError(f"{key} is not loaded")
+
     def run_direct_routed(self, tokens: torch.Tensor, top_scores: torch.Tensor,
                           top_indices: torch.Tensor) -> torch.Tensor:
-        return run_routed(self.bound_weights(), tokens, top_scores, top_indices)
+        return run_routed(self.bound_weights(), tokens, top_scores, top_indices, lora=down_lora_of(self))
+
+
+class _DownAdapter(nn.Module):
+    """Minimal expert LoRA on w2 with the reference adapter's parameter names."""
+
+    def __init__(self, num_experts: int, in_features: int, out_features: int, rank: int, alpha: float,
+                 use_rslora: bool):
+        super().__init__()
+        self.rank = int(rank)
+        self.use_rslora = bool(use_rslora)
+        self.lora_a = nn.Parameter(torch.empty(num_experts, self.rank, in_features))
+        self.lora_b = nn.Parameter(torch.zeros(num_experts, out_features, self.rank))
+        self.register_buffer("lora_alpha", torch.tensor(float(alpha)), persistent=True)
+        for e in range(num_experts):
+            nn.init.kaiming_uniform_(self.lora_a.data[e], a=5 ** 0.5)
+
+    def _alpha(self) -> float:
+        return float(self.lora_alpha.item())

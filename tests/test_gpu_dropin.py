@@ -1,0 +1,126 @@
+"""The drop-in layer on the GPU: the reference-compatible module, the
+``execute_direct`` backend and autograd, checked against the oracle."""
+
+import types
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe as om
+from oracle import quant as oq
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _dev():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from mirai_b200.build import build
+    build()
+    return torch.device("cuda:0")
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _nf4_dense_from_module(m, key):
+    E, out_f, in_f = m._nf4_shapes[key]
+    g = {"nf4": _np(getattr(m, f"{key}_nf4")).astype(np.uint8).reshape(E, -1),
+         "absmax": getattr(m, f"{key}_nf4_absmax").cpu().numpy(),
+         "nabsmax": getattr(m, f"{key}_nf4_nabsmax").cpu().numpy(),
+         "offset": getattr(m, f"{key}_nf4_offset").cpu().numpy(),
+         "code": getattr(m, f"{key}_nf4_code").cpu().numpy(),
+         "ncode": getattr(m, f"{key}_nf4_ncode").cpu().numpy(),
+         "shape": (E, out_f, in_f), "blocksize": 64, "nested_blocksize": 256}
+    g["nf4"] = getattr(m, f"{key}_nf4").cpu().numpy().reshape(E, -1)
+    return oq.nf4_dequantize_grouped(g)
+
+
+@pytest.mark.parametrize("token_dtype", [torch.bfloat16, torch.float32])
+def test_module_nf4_forward_and_autograd(token_dtype):
+    dev = _dev()
+    from mirai_b200.experts import B200GroupedExperts
+    T, H, E, k, I = 384, 256, 8, 2, 512
+    torch.manual_seed(0)
+    m = B200GroupedExperts.from_empty(num_experts=E, quant_format="nf4")
+    raw = {"w1": torch.randn(E, I, H) * 0.05, "w3": torch.randn(E, I, H) * 0.05, "w2": torch.randn(E, H, I) * 0.05}
+    for key, w in raw.items():
+        m.load_dense_weight(key, w.to(dev))
+    dense = [_nf4_dense_from_module(m, key) for key in ("w1", "w3", "w2")]
+    x = torch.randn(T, H).to(torch.bfloat16).to(token_dtype)
+    logits = torch.randn(T, E) * 1.5
+    sc, idx = torch.topk(torch.softmax(logits, -1), k)
+    sc = (sc / sc.sum(-1, keepdim=True)).to(token_dtype)
+    xt = x.to(dev).requires_grad_(True)
+    st = sc.to(dev).requires_grad_(True)
+    out = m.run_direct_routed(xt, st, idx.to(dev))
+    assert out.dtype == token_dtype
+    g = torch.randn(T, H).to(torch.bfloat16)
+    out.backward(g.to(dev).to(token_dtype))
+    xn, sn = _np(x), _np(sc)
+    ref = om.moe_forward(xn, idx.numpy(), sn, *dense, bf16=True)
+    rdx, rdw = om.moe_backward_dx(xn, idx.numpy(), sn, *dense, _np(g), bf16=True)
+    assert om.rel_max_err(_np(out), ref) < TOL
+    assert om.rel_max_err(_np(xt.grad), rdx) < 3e-2
+    assert om.rel_max_err(_np(st.grad), rdw) < 3e-2
+
+
+def test_backend_reads_reference_style_buffers_in_place():
+    """execute_direct on an object laid out like the reference's CompressedGroupedExperts."""
+    dev = _dev()
+    from mirai_b200 import ops
+    from mirai_b200.backend import B200MoEKernelBackend
+    T, H, E, k, I = 256, 256, 4, 2, 256
+    rng = np.random.default_rng(1)
+    ref_like = types.SimpleNamespace(_quant_format="nf4", num_experts=E, _nf4_shapes={}, expert_lora={},
+                                     _nf4_meta=types.SimpleNamespace(blocksize=64, nested_blocksize=256))
+    dense = []
+    for key, shape in (("w1", (E, I, H)), ("w3", (E, I, H)), ("w2", (E, H, I))):
+        gq = oq.nf4_quantize_grouped((rng.standard_normal(shape) * 0.05).astype(np.float32))
+        dense.append(oq.nf4_dequantize_grouped(gq))
+        setattr(ref_like, f"{key}_nf4", torch.from_numpy(gq["nf4"]).to(dev))
+        setattr(ref_like, f"{key}_nf4_absmax", torch.from_numpy(gq["absmax"]).to(dev))
+        setattr(ref_like, f"{key}_nf4_nabsmax", torch.from_numpy(gq["nabsmax"]).to(dev))
+        setattr(ref_like, f"{key}_nf4_offset", torch.from_numpy(gq["offset"]).to(dev))
+        setattr(ref_like, f"{key}_nf4_code", torch.from_numpy(gq["code"]).to(dev))
+        setattr(ref_like, f"{key}_nf4_ncode", torch.from_numpy(gq["ncode"]).to(dev))
+        ref_like._nf4_shapes[key] = shape
+    x = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    logits = (rng.standard_normal((T, E)) * 1.5).astype(np.float32)
+    idx, w = om.route_topk(logits, k)
+    backend = B200MoEKernelBackend()
+    out = backend.execute_direct(ref_like, torch.from_numpy(x).to(torch.bfloat16).to(dev),
+                                 torch.from_numpy(w).to(dev), torch.from_numpy(idx).to(dev))
+    ops.check_device()
+    assert out is not None
+    ref = om.moe_forward(x, idx, w, *dense, bf16=True)
+    assert om.rel_max_err(_np(out), ref) < TOL
+    # the binding is cached and re-used while the buffers stay put
+    assert backend.bind(ref_like) is backend.bind(ref_like)
+
+
+def test_module_with_lora_trains_adapter():
+    dev = _dev()
+    from mirai_b200.experts import B200GroupedExperts
+    T, H, E, k, I, r = 256, 256, 4, 2, 256, 8
+    torch.manual_seed(3)
+    m = B200GroupedExperts.from_empty(num_experts=E, quant_format="bf16")
+    ws = {"w1": torch.randn(E, I, H) * 0.05, "w3": torch.randn(E, I, H) * 0.05, "w2": torch.randn(E, H, I) * 0.05}
+    for key, w in ws.items():
+        m.load_dense_weight(key, w.to(dev))
+    m.attach_expert_lora(tensor_name="w2", rank=r, alpha=float(r))
+    m = m.to(dev)
+    with torch.no_grad():
+        m.expert_lora["w2"].lora_b.add_(0.02 * torch.randn_like(m.expert_lora["w2"].lora_b))
+    x = torch.randn(T, H, device=dev).to(torch.bfloat16).requires_grad_(True)
+    idx = torch.randint(0, E, (T, k), device=dev)
+    sc = torch.rand(T, k, device=dev) + 0.1
+    out = m.run_direct_routed(x, sc, idx)
+    out.float().pow(2).mean().backward()
+    ad = m.expert_lora["w2"]
+    assert ad.lora_a.grad is not None and ad.lora_b.grad is not None
+    assert float(ad.lora_a.grad.norm()) > 0 and float(ad.lora_b.grad.norm()) > 0
+    assert float(x.grad.norm()) > 0
