@@ -206,17 +206,24 @@ int mirai_moe_gateup_dx_int8(const void* grad_gate_up, const int32_t* offsets, i
  * into the down GEMMs as one extra 64-wide k-block.
  *
  * mirai_moe_lora_project writes the rank-block operand
- *   out[s, j] = bf16(scale * sum_k x[s, k] * P_e[j, k])  (j < rank; 0 for j < 64)
- * as [S, 64] bf16, where P_e[j, k] = proj[e*stride_e + j*stride_r + k*stride_k]
- * (bf16): forward x = h, P = A (strides I*r, I, 1); dX x = grad_y, P = B read
- * transposed (strides H*r, 1, r). */
+ *   out[s, j] = bf16(scale * sum_k x[s, k] * F_e[j, k])  (j < rank; 0 for rank <= j < 64)
+ * as [S, 64] bf16 for the rows s of every expert segment e, from the adapter
+ * factor zero-padded to 64 ranks (bf16) in one of two layouts:
+ *   MIRAI_LORA_FACTOR_ROWS: [E*64, K], F_e[j, k] at row e*64+j (A padded: the
+ *     forward projection, x = h, K = I);
+ *   MIRAI_LORA_FACTOR_COLS: [E*K, 64], F_e[j, k] at row e*K+k (B padded, the
+ *     operand mirai_moe_down_lora_* takes: the dX projection, x = grad_y, K = H).
+ * K % 8 == 0, out 16-byte aligned. */
+#define MIRAI_LORA_FACTOR_ROWS 0
+#define MIRAI_LORA_FACTOR_COLS 1
 int mirai_moe_lora_project(const void* x, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
-                           int32_t k_dim, const void* proj, int64_t stride_e, int64_t stride_r, int64_t stride_k,
-                           int32_t rank, float scale, void* out, mirai_stream_t stream);
+                           int32_t k_dim, const void* factor, int32_t factor_layout, int32_t rank, float scale,
+                           void* out, mirai_stream_t stream);
 
 /* Adapter-factor gradient (the LoRA weight gradients of bmm's backward in
  * batched_subset_forward): grad[e][j][k] = sum over the rows s of segment e of
- * g_rank[s, j] * x[s, k], fp32, rows summed in order (deterministic).
+ * g_rank[s, j] * x[s, k], fp32 (tensor cores, one accumulator per expert and
+ * 128 columns, rows summed in order: deterministic).
  * g_rank is a [S, 64] bf16 rank-block operand (already scaled); grad element
  * (e, j, k) is stored at grad[e*stride_e + j*stride_r + k*stride_k]:
  * dA = lora_grad(h, grad-side rank block) into [E, r, I];

@@ -84,8 +84,8 @@ SIGNATURES = {
     "mirai_moe_gateup_dx_int8": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32,
                                                 ctypes.POINTER(Int8Weight), ctypes.POINTER(Int8Weight), c_vp,
                                                 c_vp]),
-    "mirai_moe_lora_project": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_vp, c_i64, c_i64, c_i64, c_i32,
-                                              c_f32, c_vp, c_vp]),
+    "mirai_moe_lora_project": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_vp, c_i32, c_i32, c_f32, c_vp,
+                                              c_vp]),
     "mirai_moe_lora_grad": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i64, c_i64, c_i64,
                                            c_vp]),
     "mirai_moe_down_lora_bf16": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,

@@ -245,7 +245,7 @@ def down(h: torch.Tensor, offsets: torch.Tensor, w2, *, hidden: int, out: torch.
         _lib.call(f"mirai_moe_down_{_fmt_suffix(w2)}", _ptr(h), _ptr(offsets), E, S, I, hidden, _wptr(w2), _ptr(y),
                   _stream())
         return y
-    low = rank_a if rank_a is not None else lora_project(h, offsets, lora.a, lora.a.stride(), lora.rank, lora.scale)
+    low = rank_a if rank_a is not None else lora_project(h, offsets, lora, forward=True)
     _lib.call(f"mirai_moe_down_lora_{_fmt_suffix(w2)}", _ptr(h), _ptr(offsets), E, S, I, hidden, _wptr(w2),
               _ptr(low), _ptr(lora.b_pad()), _ptr(y), _stream())
     return y
@@ -290,16 +290,19 @@ class DownLoRA:
         return self._a_pad
 
 
-def lora_project(x: torch.Tensor, offsets: torch.Tensor, proj: torch.Tensor, strides, rank: int,
-                 scale: float) -> torch.Tensor:
-    """[S, 64] bf16 rank-block operand: bf16(scale * x P_e^T), zero past ``rank``."""
+LORA_FACTOR_ROWS, LORA_FACTOR_COLS = 0, 1
+
+
+def lora_project(x: torch.Tensor, offsets: torch.Tensor, lora: DownLoRA, *, forward: bool) -> torch.Tensor:
+    """[S, 64] bf16 rank-block operand bf16(scale * x F_e^T), zero past the rank:
+    F = A ([E, r, I], x = h) when ``forward``, else B^T ([E, H, r], x = grad_y)."""
     x = _cuda(x, "x", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
     S, K = x.shape
     out = torch.empty((S, 64), dtype=torch.bfloat16, device=x.device)
-    se, sr, sk = (int(v) for v in strides)
-    _lib.call("mirai_moe_lora_project", _ptr(x), _ptr(offsets), offsets.numel(), S, K, _ptr(proj), se, sr, sk,
-              int(rank), float(scale), _ptr(out), _stream())
+    factor, layout = (lora.a_pad(), LORA_FACTOR_ROWS) if forward else (lora.b_pad(), LORA_FACTOR_COLS)
+    _lib.call("mirai_moe_lora_project", _ptr(x), _ptr(offsets), offsets.numel(), S, K, _ptr(factor), layout,
+              int(lora.rank), float(lora.scale), _ptr(out), _stream())
     return out
 
 
@@ -373,9 +376,7 @@ def down_dx(grad_y: torch.Tensor, offsets: torch.Tensor, w2, gate_up: torch.Tens
         _lib.call(f"mirai_moe_down_dx_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), offsets.numel(), S, H, inter,
                   _wptr(w2), _ptr(gu), _ptr(dgu), _stream())
         return dgu
-    E, Hb, r = lora.b.shape
-    glow = rank_a if rank_a is not None else lora_project(gy, offsets, lora.b, (Hb * r, 1, r), lora.rank,
-                                                          lora.scale)
+    glow = rank_a if rank_a is not None else lora_project(gy, offsets, lora, forward=False)
     _lib.call(f"mirai_moe_down_dx_lora_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), offsets.numel(), S, H, inter,
               _wptr(w2), _ptr(gu), _ptr(glow), _ptr(lora.a_pad()), _ptr(dgu), _stream())
     return dgu
@@ -439,7 +440,7 @@ def moe_forward_train(tokens, top_indices, top_weights, w1, w3, w2, *, num_exper
     h, gu = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter, save_gate_up=True)
     low = None
     if lora is not None:
-        low = lora_project(h, plan.offsets, lora.a, lora.a.stride(), lora.rank, lora.scale)
+        low = lora_project(h, plan.offsets, lora, forward=True)
     y = down(h, plan.offsets, w2, hidden=tokens.shape[1], lora=lora, rank_a=low)
     out = combine(y, plan.inverse_order, top_weights, out_dtype=out_dtype or tokens.dtype)
     keep = lora is not None and lora.compute_grads
@@ -457,7 +458,7 @@ def moe_backward_dx(grad_out: torch.Tensor, state: ForwardState, w1, w3, w2, *, 
     glow = None
     if lora is not None:
         E, Hb, r = lora.b.shape
-        glow = lora_project(gy, plan.offsets, lora.b, (Hb * r, 1, r), lora.rank, lora.scale)
+        glow = lora_project(gy, plan.offsets, lora, forward=False)
         if lora.compute_grads:
             if state.h is None or state.rank_a is None:
                 raise RuntimeError("LoRA factor gradients need the forward run with compute_grads=True")

@@ -446,3 +446,49 @@ def test_lora_factor_gradients():
         start = end
     assert om.rel_max_err(lora.grad_a.cpu().numpy(), ga) < 3e-2
     assert om.rel_max_err(lora.grad_b.cpu().numpy(), gb) < 3e-2
+
+
+@pytest.mark.parametrize("K", [256, 200, 1408])
+@pytest.mark.parametrize("rank", [16, 5, 32])
+def test_lora_project_and_grad_ragged_segments(K, rank):
+    """The tensor-core rank-block kernels on ragged segments: an empty expert, a
+    one-row expert, partial 64/128-row blocks and K not a multiple of 128."""
+    dev = _dev()
+    from mirai_b200 import ops
+    counts = [0, 1, 130, 64, 300, 0]
+    E, H = len(counts), 192
+    offsets = np.cumsum(counts).astype(np.int32)
+    S = int(offsets[-1])
+    rng = np.random.default_rng(K + rank)
+    x = oq.bf16_round(rng.standard_normal((S, K)).astype(np.float32))
+    la = oq.bf16_round((rng.standard_normal((E, rank, K)) * 0.1).astype(np.float32))
+    lb = oq.bf16_round((rng.standard_normal((E, K, rank)) * 0.1).astype(np.float32))
+    g = np.zeros((S, 64), np.float32)
+    g[:, :rank] = oq.bf16_round(rng.standard_normal((S, rank)).astype(np.float32))
+    scale = 0.75
+    lora = ops.DownLoRA(_bf16(la).to(dev), _bf16(lb).to(dev), scale)
+    xd, od = _bf16(x).to(dev), torch.from_numpy(offsets).to(dev)
+    fwd = ops.lora_project(xd, od, lora, forward=True)
+    bwd = ops.lora_project(xd, od, lora, forward=False)
+    ga = ops.lora_grad(xd, _bf16(g).to(dev), od, rank, torch.full((E, rank, K), 7.0, device=dev),
+                       (rank * K, K, 1))
+    gb = ops.lora_grad(xd, _bf16(g).to(dev), od, rank, torch.full((E, K, rank), 7.0, device=dev),
+                       (K * rank, 1, rank))
+    _check(ops)
+    ref_f = np.zeros((S, 64), np.float32)
+    ref_b = np.zeros((S, 64), np.float32)
+    ref_ga = np.zeros((E, rank, K), np.float64)
+    start = 0
+    for e in range(E):
+        end = int(offsets[e])
+        xs = x[start:end].astype(np.float64)
+        ref_f[start:end, :rank] = scale * xs @ la[e].T
+        ref_b[start:end, :rank] = scale * xs @ lb[e]
+        ref_ga[e] = g[start:end, :rank].T.astype(np.float64) @ xs
+        start = end
+    assert om.rel_max_err(_f32(fwd), oq.bf16_round(ref_f)) < 1e-2
+    assert om.rel_max_err(_f32(bwd), oq.bf16_round(ref_b)) < 1e-2
+    assert np.all(_f32(fwd)[:, rank:] == 0) and np.all(_f32(bwd)[:, rank:] == 0)
+    assert om.rel_max_err(ga.cpu().numpy(), ref_ga) < 1e-4
+    assert om.rel_max_err(gb.cpu().numpy(), ref_ga.transpose(0, 2, 1)) < 1e-4
+    assert np.all(ga.cpu().numpy()[[0, 5]] == 0)
