@@ -55,6 +55,9 @@ SIGNATURES = {
     "mirai_b200_device_status": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "mirai_route_topk": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_i32, c_f32, c_vp, c_vp, c_vp]),
     "mirai_dispatch_plan_workspace_bytes": (c_size, [c_i64, c_i32, c_i32]),
+    "mirai_dispatch_plan_static_scratch_bytes": (c_size, []),
+    "mirai_dispatch_plan_static": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+                                                  c_vp]),
     "mirai_dispatch_plan": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                                            c_size, c_vp]),
     "mirai_permute_rows_bf16": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_i32, c_vp, c_vp]),

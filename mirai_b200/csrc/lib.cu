@@ -2,6 +2,7 @@
 // capi.cu is referenced by every kernel, so all parts compile together.
 #include "capi.cu"
 #include "routing.cu"
+#include "plan_static.cu"
 #include "grouped_gemm.cu"
 #include "quantize.cu"
 #include "lora.cu"
