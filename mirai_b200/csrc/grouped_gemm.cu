@@ -15,19 +15,25 @@
 //   warps 6..13   (NF4 / INT8) dequantisers: raw codes in shared memory ->
 //                 exact bf16 weights in the UMMA operand layout
 // Two TMEM accumulators (2 x 256 fp32 columns) overlap the epilogue of tile i
-// with the main loop of tile i+1.  Tiles are (expert, row block, 256-column
+// with the main loop of tile i+1.  Tiles are (expert, row block, column
 // block), expert-major with the column block fastest so that the CTAs running
 // together share one expert's weights in L2.
 //
 // PAIR = true runs each tile on a CTA pair (cluster of 2, tcgen05 cta_group::2):
-// a 256-row x 256-column tile whose A rows are split between the two SMs
-// (128 each) and whose B operand is split along N (128 columns each), so
-// each SM stages, and for NF4/INT8 decodes, only half of B.  The even CTA
-// issues the M=256 UMMAs; completion is multicast to both CTAs.  No TMA
-// multicast is used.  PAIR = false is the single-SM 128-row variant.
+// the A rows of every 256-row sub-tile are split between the two SMs (128
+// each) and the B operand is split along N, so each SM stages, and for
+// NF4/INT8 decodes, only half of B.  The even CTA issues the M=256 UMMAs;
+// completion is multicast to both CTAs.  No TMA multicast is used.
+// Every format uses one 256-row sub-tile x 256 columns per tile (RT = 1,
+// TN = 256).  The geometry also admits RT = 2 sub-tiles of 128 columns that
+// share one decoded B block (half the decode work per FLOP); on B200 that shape
+// measured slower for NF4 and bf16 alike (0.80 vs 0.73 ms, 0.75 vs 0.59 ms for
+// the c2 gate/up GEMM), because N = 128 UMMAs re-read A from shared memory twice
+// as often and shared-memory bandwidth, not decode, becomes the limit.
+// PAIR = false is the single-SM 128-row x 256-column variant.
 //
 // Operand layouts (128-byte swizzle), per CTA:
-//   A  [128 rows][64 k] K-major = 16 KB
+//   A  RT x [128 rows][64 k] K-major = RT x 16 KB
 //   B  K-major:  [B_ROWS rows][64 k]           (8-row x 128 B atoms, SBO 1 KB)
 //      MN-major: [B_ROWS/64 x 64 n][64 k rows] (atoms 8 k-rows x 64 n; LBO 8 KB
 //                                               between 64-n blocks, SBO 1 KB)
@@ -40,8 +46,8 @@
 namespace mirai {
 namespace gg {
 
-constexpr int BM = 128;  // rows of A per CTA
-constexpr int BN = 256;  // output columns per tile
+constexpr int BM = 128;  // rows of A per CTA and sub-tile
+constexpr int BN = 256;  // accumulator columns per tile (RT x TN)
 constexpr int BK = 64;
 constexpr int UMMA_K = 16;
 constexpr uint32_t A_BYTES = BM * BK * 2;
@@ -65,18 +71,27 @@ template <int MODE> struct MCfg {
 
 // Per (format, pairing) geometry.
 template <int WF, bool PAIR> struct Cfg {
-  static constexpr int TILE_M = PAIR ? 2 * BM : BM;                      // rows per tile
-  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;                      // B rows / n-columns per CTA
+  static constexpr bool QUANT = WF != W_BF16;
+  static constexpr int RT = 1;                                           // row sub-tiles per tile
+  static constexpr int TN = BN / RT;                                     // output columns per tile
+  static constexpr int SUB_M = PAIR ? 2 * BM : BM;                       // rows per sub-tile (UMMA M)
+  static constexpr int TILE_M = RT * SUB_M;                              // rows per tile
+  static constexpr uint32_t A_STAGE = RT * A_BYTES;                      // A per CTA per stage
+  static constexpr int B_ROWS = PAIR ? TN / 2 : TN;                      // B rows / n-columns per CTA
   static constexpr uint32_t B_BYTES = B_ROWS * BK * 2;                   // bf16 B per CTA per stage
   static constexpr int ROW_BYTES = WF == W_NF4 ? BK / 2 : (WF == W_INT8 ? BK : 0);  // raw bytes / 64 elements
   static constexpr uint32_t RAW_BYTES = B_ROWS * ROW_BYTES;
+  // Dequantisers: one thread per B row and k-block; KG groups of B_ROWS
+  // threads take the k-blocks in turn (group g: k-blocks g, g+KG, ...).
+  static constexpr int KG = QUANT ? kDeqThreads / B_ROWS : 1;
+  static constexpr int GROUP_WARPS = QUANT ? B_ROWS / 32 : 0;            // dequant warps per group
   static constexpr int STAGES = WF == W_BF16 ? (PAIR ? 6 : 4) : (PAIR ? 4 : 3);
   // raw-code ring: its own producer warp runs ahead of the operand ring
-  static constexpr int RAW_STAGES = WF == W_BF16 ? 1 : (WF == W_NF4 ? (PAIR ? 8 : 6) : (PAIR ? 6 : 3));
+  static constexpr int RAW_STAGES = WF == W_BF16 ? 1 : (PAIR ? 8 : (WF == W_NF4 ? 6 : 3));
   static constexpr int EPI_WARPS = epi_warps(WF);
   static constexpr int THREADS = 64 + 32 * EPI_WARPS + (WF == W_BF16 ? 0 : kDeqThreads + 32);
-  static constexpr int TPR = kDeqThreads / B_ROWS;                       // dequant threads per B row
-  static constexpr int ELEMS = BK / TPR;                                 // elements per dequant thread
+  static_assert(!QUANT || (kDeqThreads % B_ROWS == 0 && STAGES % KG == 0 && RAW_STAGES % KG == 0),
+                "each dequantiser group must own whole stages");
 };
 
 // One quantised key (W1, W3 or W2).
@@ -134,7 +149,7 @@ struct DeqSmem {
 template <int WF, bool PAIR>
 constexpr size_t smem_bytes() {
   using C = Cfg<WF, PAIR>;
-  return 1024 + C::STAGES * (A_BYTES + C::B_BYTES) + (WF == W_BF16 ? 0 : C::RAW_STAGES * C::RAW_BYTES) +
+  return 1024 + C::STAGES * (C::A_STAGE + C::B_BYTES) + (WF == W_BF16 ? 0 : C::RAW_STAGES * C::RAW_BYTES) +
          sizeof(Smem<WF, PAIR>) +
          (WF == W_BF16 ? 0 : sizeof(DeqSmem));
 }
@@ -228,11 +243,11 @@ __device__ __forceinline__ void int8_x16(const uint4 r, float scale, uint32_t (&
 }
 
 // K-major modes: first weight row (within the [E * out_rows] row space) of the
-// 128-row B block `h` of tile (e, n): h = 0/1 are the two 128-row blocks of the
-// 256-column tile (gate/up: W1 and W3 rows n*128..; down: W2 rows n*256 + 128h..).
-template <int MODE>
+// B block `h` (TN/2 rows) of tile (e, n): h = 0/1 are the two halves of the
+// TN-column tile (gate/up: W1 and W3 rows n*TN/2..; down: W2 rows n*TN + h*TN/2..).
+template <int MODE, int TN>
 __device__ __forceinline__ int kmajor_row(const Params& p, int e, int n, int h) {
-  return MODE == GATEUP ? e * p.out_rows + n * (BN / 2) : e * p.out_rows + n * BN + h * (BN / 2);
+  return MODE == GATEUP ? e * p.out_rows + n * (TN / 2) : e * p.out_rows + n * TN + h * (TN / 2);
 }
 
 template <int MODE, int WF, bool PAIR>
@@ -245,12 +260,16 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   constexpr uint32_t B_BYTES = C::B_BYTES;
   constexpr uint32_t RAW_BYTES = C::RAW_BYTES;
   constexpr int TILE_M = C::TILE_M;
+  constexpr int RT = C::RT;
+  constexpr int TN = C::TN;
+  constexpr int SUB_M = C::SUB_M;
+  constexpr uint32_t A_STAGE = C::A_STAGE;
   constexpr bool QUANT = WF != W_BF16;
   constexpr bool MN = MCfg<MODE>::MN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = base;
-  uint8_t* sB = sA + STAGES * A_BYTES;
+  uint8_t* sB = sA + STAGES * A_STAGE;
   uint8_t* sRaw = sB + STAGES * B_BYTES;
   constexpr int RAW_STAGES = C::RAW_STAGES;
   Smem<WF, PAIR>& sm = *reinterpret_cast<Smem<WF, PAIR>*>(sRaw + (QUANT ? RAW_STAGES * RAW_BYTES : 0));
@@ -304,12 +323,12 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       for (int s = 0; s < STAGES; ++s) {
         // full: the leader's producer arrive (with the bytes of both CTAs) plus
         // every dequantiser warp of the pair
-        mbar_init(&sm.full[s], 1 + (QUANT ? kDeqWarps * pair_mult : 0));
+        mbar_init(&sm.full[s], 1 + (QUANT ? C::GROUP_WARPS * pair_mult : 0));
         mbar_init(&sm.empty[s], 1);
       }
       for (int s = 0; s < RAW_STAGES; ++s) {
         mbar_init(&sm.raw_full[s], 1);
-        mbar_init(&sm.raw_empty[s], kDeqWarps);
+        mbar_init(&sm.raw_empty[s], C::GROUP_WARPS);
       }
       for (int a = 0; a < 2; ++a) {
         mbar_init(&sm.tfull[a], 1);
@@ -361,6 +380,9 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         int e, m, n;
         decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
         const int row0 = sm.row_start[e] + m * TILE_M + (int)rank * BM;
+        // sub-tiles holding rows of this expert (the first always does)
+        const int seg_rows = sm.row_start[e + 1] - sm.row_start[e];
+        const int n_live = (RT == 2 && m * TILE_M + SUB_M >= seg_rows) ? 1 : RT;
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&sm.empty[stage], phase ^ 1, 10)) {
             *abort_flag = 1;
@@ -374,7 +396,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           const int krow = MN ? e * p.krows + (kb - ((MN && key1) ? p.kb_half : 0)) * BK : 0;
           const int pair_mult = PAIR ? 2 : 1;
           if (leader) {
-            const uint32_t bytes = pair_mult * (A_BYTES + ((QUANT && !ext) ? 0u : B_BYTES));
+            const uint32_t bytes = pair_mult * (n_live * A_BYTES + ((QUANT && !ext) ? 0u : B_BYTES));
             // the leader's own barrier: a CTA-local arrive carries the bytes of both CTAs
             mbar_arrive_expect_tx(&sm.full[stage], bytes);
           }
@@ -387,30 +409,34 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             if (MN) {
 #pragma unroll
               for (int nb = 0; nb < C::B_ROWS / 64; ++nb)
-                load(b_dst + nb * 8192, &tmap_xb, n * BN + (int)rank * C::B_ROWS + nb * 64, e * BK);
+                load(b_dst + nb * 8192, &tmap_xb, n * TN + (int)rank * C::B_ROWS + nb * 64, e * BK);
             } else if (PAIR) {
-              load(b_dst, &tmap_xb, 0, kmajor_row<MODE>(p, e, n, (int)rank));
+              load(b_dst, &tmap_xb, 0, kmajor_row<MODE, TN>(p, e, n, (int)rank));
             } else {
-              load(b_dst, &tmap_xb, 0, kmajor_row<MODE>(p, e, n, 0));
-              load(b_dst + B_BYTES / 2, &tmap_xb, 0, kmajor_row<MODE>(p, e, n, 1));
+              load(b_dst, &tmap_xb, 0, kmajor_row<MODE, TN>(p, e, n, 0));
+              load(b_dst + B_BYTES / 2, &tmap_xb, 0, kmajor_row<MODE, TN>(p, e, n, 1));
             }
-            load(sA + stage * A_BYTES, &tmap_xa, 0, row0);
           } else if (!QUANT) {
             uint8_t* b_dst = sB + stage * B_BYTES;
             if (MN) {
-              // this CTA's columns: n*256 + rank*B_ROWS + 64*nb
+              // this CTA's columns: n*TN + rank*B_ROWS + 64*nb
 #pragma unroll
               for (int nb = 0; nb < C::B_ROWS / 64; ++nb)
-                load(b_dst + nb * 8192, mb, n * BN + (int)rank * C::B_ROWS + nb * 64, krow);
+                load(b_dst + nb * 8192, mb, n * TN + (int)rank * C::B_ROWS + nb * 64, krow);
             } else if (PAIR) {
-              // 128 rows per CTA: gate/up -> rank 0 W1, rank 1 W3; down -> W2 rows block `rank`
-              load(b_dst, mb, kb * BK, kmajor_row<MODE>(p, e, n, (int)rank));
+              // B_ROWS rows per CTA: gate/up -> rank 0 W1, rank 1 W3; down -> W2 rows block `rank`
+              load(b_dst, mb, kb * BK, kmajor_row<MODE, TN>(p, e, n, (int)rank));
             } else {
-              load(b_dst, &tmap_b0, kb * BK, kmajor_row<MODE>(p, e, n, 0));
-              load(b_dst + B_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * BK, kmajor_row<MODE>(p, e, n, 1));
+              load(b_dst, &tmap_b0, kb * BK, kmajor_row<MODE, TN>(p, e, n, 0));
+              load(b_dst + B_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * BK,
+                   kmajor_row<MODE, TN>(p, e, n, 1));
             }
           }
-          if (!ext) load(sA + stage * A_BYTES, &tmap_a, kb * BK, row0);
+          for (int sub = 0; sub < n_live; ++sub) {
+            uint8_t* a_dst = sA + stage * A_STAGE + sub * A_BYTES;
+            if (ext) load(a_dst, &tmap_xa, 0, row0 + sub * SUB_M);
+            else load(a_dst, &tmap_a, kb * BK, row0 + sub * SUB_M);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -430,7 +456,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   } else if (warp == 1) {
     // ======================= UMMA issuer (the leader of a pair) =======================
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = make_idesc_bf16(TILE_M, BN, false, MN);
+      constexpr uint32_t idesc = make_idesc_bf16(SUB_M, TN, false, MN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -442,6 +468,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           break;
         }
         tc_fence_after();
+        int e, m, n;
+        decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
+        const int seg_rows = sm.row_start[e + 1] - sm.row_start[e];
+        const int n_live = (RT == 2 && m * TILE_M + SUB_M >= seg_rows) ? 1 : RT;
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < total_kb; ++kb) {
@@ -450,15 +480,17 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
           const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          for (int sub = 0; sub < n_live; ++sub) {
+            const uint32_t a_addr = smem_u32(sA + stage * A_STAGE + sub * A_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k) {
-            const uint64_t ad = make_sdesc_sw128(a_addr + k * UMMA_K * 2, 16, 1024);
-            const uint64_t bd = MN ? make_sdesc_sw128(b_addr + k * UMMA_K * 128, 8192, 1024)
-                                   : make_sdesc_sw128(b_addr + k * UMMA_K * 2, 16, 1024);
-            if (PAIR) umma_bf16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-            else umma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < BK / UMMA_K; ++k) {
+              const uint64_t ad = make_sdesc_sw128(a_addr + k * UMMA_K * 2, 16, 1024);
+              const uint64_t bd = MN ? make_sdesc_sw128(b_addr + k * UMMA_K * 128, 8192, 1024)
+                                     : make_sdesc_sw128(b_addr + k * UMMA_K * 2, 16, 1024);
+              if (PAIR) umma_bf16_pair(d_tmem + sub * TN, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+              else umma_bf16(d_tmem + sub * TN, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
           }
           if (PAIR) umma_commit_pair(&sm.empty[stage], 0x3);
           else umma_commit(&sm.empty[stage]);
@@ -493,18 +525,21 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       tc_fence_after();
       int e, m, n;
       decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
-      const int r = (int)rank * BM + q * 32 + lane;  // row inside the tile
       const int64_t seg_rows = (int64_t)sm.row_start[e + 1] - sm.row_start[e];
+      for (int sub = 0; sub < RT; ++sub) {
+      if ((int64_t)m * TILE_M + sub * SUB_M >= seg_rows) break;  // no rows in this sub-tile (warp-uniform)
+      const int r = sub * SUB_M + (int)rank * BM + q * 32 + lane;  // row inside the tile
       const bool valid = (int64_t)m * TILE_M + r < seg_rows;
       const int64_t grow = (int64_t)sm.row_start[e] + (int64_t)m * TILE_M + r;
-      const uint32_t tb = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
+      const uint32_t tb = tmem_base + acc * BN + sub * TN + ((uint32_t)(q * 32) << 16);
       if (MODE == GATEUP) {
-        const int col0 = n * (BN / 2);
+        const int col0 = n * (TN / 2);
+        constexpr int NCH = TN / 64;  // 32-column chunks of gate (and of up)
 #pragma unroll 1
-        for (int c = part * (4 / NSPLIT); c < (part + 1) * (4 / NSPLIT); ++c) {
+        for (int c = part * (NCH / NSPLIT); c < (part + 1) * (NCH / NSPLIT); ++c) {
           uint32_t g[32], u[32];
           tmem_ld_32x32b_x32(tb + c * 32, g);
-          tmem_ld_32x32b_x32(tb + BN / 2 + c * 32, u);
+          tmem_ld_32x32b_x32(tb + TN / 2 + c * 32, u);
           tmem_ld_wait();
           if (valid) {
             uint32_t hp[16], gp[16], up[16];
@@ -539,9 +574,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         // dgu = SwiGLU backward of the saved (gate, up) given dh = dy W2
         // (autograd of experts.py:301-317 in bf16: mul, silu backward)
         const int64_t ld2 = 2 * (int64_t)p.N;
+        constexpr int NCH = TN / 32;
 #pragma unroll 1
-        for (int c = part * (8 / NSPLIT); c < (part + 1) * (8 / NSPLIT); ++c) {
-          const int col = n * BN + c * 32;
+        for (int c = part * (NCH / NSPLIT); c < (part + 1) * (NCH / NSPLIT); ++c) {
+          const int col = n * TN + c * 32;
           uint32_t v32[32];
           tmem_ld_32x32b_x32(tb + c * 32, v32);
           tmem_ld_wait();
@@ -582,9 +618,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           }
         }
       } else {
-        const int col0 = n * BN;
+        const int col0 = n * TN;
+        constexpr int NCH = TN / 32;
 #pragma unroll 1
-        for (int c = part * (8 / NSPLIT); c < (part + 1) * (8 / NSPLIT); ++c) {
+        for (int c = part * (NCH / NSPLIT); c < (part + 1) * (NCH / NSPLIT); ++c) {
           uint32_t v32[32];
           tmem_ld_32x32b_x32(tb + c * 32, v32);
           tmem_ld_wait();
@@ -598,6 +635,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           }
         }
       }
+      }  // sub-tiles
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -631,14 +669,14 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             if (MN) {
 #pragma unroll
               for (int nb = 0; nb < C::B_ROWS / 64; ++nb)
-                tma_load_2d(r_dst + nb * 64 * RB, mb, (n * BN + (int)rank * C::B_ROWS + nb * 64) * RB / 64, krow,
+                tma_load_2d(r_dst + nb * 64 * RB, mb, (n * TN + (int)rank * C::B_ROWS + nb * 64) * RB / 64, krow,
                             &sm.raw_full[rstage]);
             } else if (PAIR) {
-              tma_load_2d(r_dst, mb, kb * RB, kmajor_row<MODE>(p, e, n, (int)rank), &sm.raw_full[rstage]);
+              tma_load_2d(r_dst, mb, kb * RB, kmajor_row<MODE, TN>(p, e, n, (int)rank), &sm.raw_full[rstage]);
             } else {
-              tma_load_2d(r_dst, &tmap_b0, kb * RB, kmajor_row<MODE>(p, e, n, 0), &sm.raw_full[rstage]);
+              tma_load_2d(r_dst, &tmap_b0, kb * RB, kmajor_row<MODE, TN>(p, e, n, 0), &sm.raw_full[rstage]);
               tma_load_2d(r_dst + RAW_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * RB,
-                          kmajor_row<MODE>(p, e, n, 1), &sm.raw_full[rstage]);
+                          kmajor_row<MODE, TN>(p, e, n, 1), &sm.raw_full[rstage]);
             }
           }
           if (++rstage == RAW_STAGES) {
@@ -650,33 +688,34 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     }
   } else if (QUANT) {
     // ======================= dequantisers =======================
-    // This CTA's B block holds B_ROWS rows of 64 elements per stage (K-major:
-    // weight rows; MN-major: 64-element column blocks x 64 k-rows).  TPR
-    // threads share one row; thread d decodes ELEMS elements of row d / TPR.
-    constexpr int TPR = C::TPR;
-    constexpr int ELEMS = C::ELEMS;
+    // One thread per B row (K-major: a weight row; MN-major: one k-row of a
+    // 64-column block) and k-block: each thread decodes a whole 64-element
+    // block, i.e. one NF4 absmax block.  The KG groups of B_ROWS threads take
+    // the k-blocks of this CTA's sequence in turn (group g: g, g+KG, ...), so
+    // a group has KG main-loop steps to deliver each of its blocks.
     constexpr int RB = C::ROW_BYTES;
+    constexpr int KG = C::KG;
     const int d = threadIdx.x - 32 * (2 + C::EPI_WARPS);
-    const int row = d / TPR;            // B row inside the stage
-    const int part = d % TPR;           // which ELEMS-element slice of the row
+    const int grp = d / C::B_ROWS;
+    const int row = d % C::B_ROWS;      // B row inside the stage
     const int nkb = num_kb;
-    // K-major: 128-row block and row in it; MN-major: 64-column block and k-row
-    const int kblk = MN ? 0 : (PAIR ? (int)rank : row >> 7);
-    const int kr = MN ? row & 63 : row & 127;
+    // K-major: TN/2-row block and row in it; MN-major: 64-column block and k-row
+    const int kblk = MN ? 0 : (PAIR ? (int)rank : row / (TN / 2));
+    const int kr = MN ? row & 63 : row % (TN / 2);
     const int nbq = MN ? row >> 6 : 0;  // local 64-column block (MN)
     const int nbase = MN ? (int)rank * C::B_ROWS / 64 : 0;  // first 64-column block of this CTA in the tile
     const int nblk_row = p.N / 64;      // MN: NF4 blocks per weight row
-    int stage = 0;
-    uint32_t phase = 0;
-    int rstage = 0;  // raw ring position
-    uint32_t rphase = 0;
+    const int sw = row & 7;             // 128-byte swizzle phase of this operand row
     float code[16];
-    for (int t = unit; t < total_tiles && !*abort_flag; t += num_units) {
+    int cur_key = -1;
+    int gk = 0;  // position in this CTA's k-block sequence over all its tiles
+    bool failed = false;
+    for (int t = unit; t < total_tiles && !failed && !*abort_flag; t += num_units) {
       int e, m, n;
       decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
       // key of this thread's rows (K-major) / of the k-block (MN)
       const int row_key = MN ? 0 : (MCfg<MODE>::TWO_KEYS ? kblk : 0);
-      const int wrow_base = MN ? 0 : kmajor_row<MODE>(p, e, n, kblk) - e * p.out_rows;  // first weight row
+      const int wrow_base = MN ? 0 : kmajor_row<MODE, TN>(p, e, n, kblk) - e * p.out_rows;  // first weight row
       // ---- stage this tile's scale inputs in shared memory
       named_bar_sync(1, kDeqThreads);
       if (WF == W_NF4) {
@@ -684,21 +723,21 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           const int nblk = PAIR ? 1 : 2;
           for (int h = 0; h < nblk; ++h) {
             const int blk = PAIR ? (int)rank : h;
-            if (kmajor_row<MODE>(p, e, n, blk) - e * p.out_rows >= p.out_rows) continue;  // past the last row
+            if (kmajor_row<MODE, TN>(p, e, n, blk) - e * p.out_rows >= p.out_rows) continue;  // past the last row
             const int key = MCfg<MODE>::TWO_KEYS ? blk : 0;
-            const uint4* src =
-                reinterpret_cast<const uint4*>(p.q[key].absmax + (size_t)kmajor_row<MODE>(p, e, n, blk) * nkb);
-            uint4* dst = reinterpret_cast<uint4*>(dq->absq + h * 128 * nkb);
-            for (int i = d; i < 8 * nkb; i += kDeqThreads) dst[i] = __ldg(src + i);
+            const uint4* src = reinterpret_cast<const uint4*>(
+                p.q[key].absmax + (size_t)kmajor_row<MODE, TN>(p, e, n, blk) * nkb);
+            uint4* dst = reinterpret_cast<uint4*>(dq->absq + h * (TN / 2) * nkb);
+            for (int i = d; i < (TN / 2) * nkb / 16; i += kDeqThreads) dst[i] = __ldg(src + i);
           }
         } else {
-          // absq[kk * 4 + j] = code of (k-row kk, this CTA's column block j)
+          // absq[kk * NB + j] = code of (k-row kk, this CTA's column block j)
           constexpr int NB = C::B_ROWS / 64;
           for (int i = d; i < p.K * NB; i += kDeqThreads) {
             const int kk = i / NB, j = i % NB;
             const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
             const int wr = kk - key * p.krows;
-            const int nbg = n * 4 + nbase + j;
+            const int nbg = n * (TN / 64) + nbase + j;
             dq->absq[i] = nbg < nblk_row
                               ? __ldg(p.q[key].absmax + ((size_t)e * p.krows + wr) * nblk_row + nbg) : (uint8_t)0;
           }
@@ -716,7 +755,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       }
       named_bar_sync(1, kDeqThreads);
       // K-major: is this thread's weight row inside the expert's matrix?  (The
-      // last 256-column tile of a down projection with N % 256 == 128 is half empty.)
+      // last tile of a down projection whose N is not a multiple of TN is half empty.)
       const bool row_live = MN || (wrow_base + kr < p.out_rows);
       float row_scale = 0.f;
       if (WF == W_INT8 && !MN && row_live)
@@ -727,55 +766,28 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         off[1] = MCfg<MODE>::TWO_KEYS ? __ldg(p.q[1].offset + e) : off[0];
       }
       const int absq_row = PAIR ? 0 : kblk;  // absq block of this thread (K-major)
-      int cur_key = -1;
-      // Two k-blocks are in flight per iteration: both stages' codes, scales
-      // and tables are prepared before either is decoded, so the memory and
-      // table latencies of one block overlap the decode of the other, and one
-      // proxy fence covers both hand-offs.
-      constexpr int CH = ELEMS / 8;  // 16-byte chunks of this thread per k-block
-      const int c0 = part * CH;
-      const int sw = kr & 7;
-      bool failed = false;
-      for (int kb = 0; kb < total_kb && !failed; kb += 2) {
-        const int nk = total_kb - kb >= 2 ? 2 : 1;
-        int st[2], rst[2];
-        uint32_t ph[2], rph[2];
-        st[0] = stage, rst[0] = rstage, ph[0] = phase, rph[0] = rphase;
-        st[1] = stage + 1 == STAGES ? 0 : stage + 1;
-        ph[1] = stage + 1 == STAGES ? phase ^ 1 : phase;
-        rst[1] = rstage + 1 == RAW_STAGES ? 0 : rstage + 1;
-        rph[1] = rstage + 1 == RAW_STAGES ? rphase ^ 1 : rphase;
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          if (i < nk && !failed) {
-            bool ok = mbar_wait(&sm.raw_full[rst[i]], rph[i], 40);
-            ok = ok && mbar_wait(&sm.empty[st[i]], ph[i] ^ 1, 41);
-            if (!ok) failed = true;
-          }
-        }
-        if (failed) {
+      for (int kb = 0; kb < total_kb; ++kb, ++gk) {
+        if (gk % KG != grp) continue;
+        const int st = gk % STAGES, rst = gk % RAW_STAGES;
+        const uint32_t ph = (uint32_t)(gk / STAGES) & 1u, rph = (uint32_t)(gk / RAW_STAGES) & 1u;
+        bool ok = mbar_wait(&sm.raw_full[rst], rph, 40);
+        ok = ok && mbar_wait(&sm.empty[st], ph ^ 1, 41);
+        if (!ok) {
+          failed = true;
           *abort_flag = 1;
           break;
         }
-        // ---- prepare: raw words and (NF4) the block's 16-entry product table
-        constexpr int NW = WF == W_INT8 ? 2 * CH : CH;  // 32-bit words of raw codes per k-block
-        uint32_t words[2][NW];
-        Nf4Tab tab[2];
-        float iscale[2] = {0.f, 0.f};
-        bool dec[2] = {false, false};
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int kbi = kb + i;
-          dec[i] = i < nk && kbi != nkb;  // the rank block arrives by TMA: nothing to decode
-          if (!dec[i]) continue;
-          const uint8_t* raw = sRaw + rst[i] * RAW_BYTES + row * RB + part * (ELEMS * RB / 64);
-#pragma unroll
-          for (int v = 0; v < NW / 4; ++v) {
-            const uint4 r4 = reinterpret_cast<const uint4*>(raw)[v];
-            words[i][4 * v] = r4.x, words[i][4 * v + 1] = r4.y, words[i][4 * v + 2] = r4.z, words[i][4 * v + 3] = r4.w;
-          }
-          const int key = MN ? ((MCfg<MODE>::TWO_KEYS && kbi >= p.kb_half) ? 1 : 0) : row_key;
+        if (kb != nkb) {  // the rank block arrives by TMA: nothing to decode
+          const uint8_t* raw = sRaw + rst * RAW_BYTES + row * RB;
+          const uint32_t row_addr = smem_u32(sB + st * B_BYTES) + (uint32_t)row * 128u;
+          const int key = MN ? ((MCfg<MODE>::TWO_KEYS && kb >= p.kb_half) ? 1 : 0) : row_key;
           if (WF == W_NF4) {
+            uint32_t words[8];
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+              const uint4 r4 = reinterpret_cast<const uint4*>(raw)[v];
+              words[4 * v] = r4.x, words[4 * v + 1] = r4.y, words[4 * v + 2] = r4.z, words[4 * v + 3] = r4.w;
+            }
             if (key != cur_key) {
 #pragma unroll
               for (int j = 0; j < 16; ++j) code[j] = dq->code[key][j];
@@ -785,12 +797,12 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             uint32_t qcode;
             bool live = row_live;
             if (!MN) {
-              blk = (wrow_base + kr) * nkb + kbi;
-              qcode = dq->absq[absq_row * 128 * nkb + kr * nkb + kbi];
+              blk = (wrow_base + kr) * nkb + kb;
+              qcode = dq->absq[absq_row * (TN / 2) * nkb + kr * nkb + kb];
             } else {
-              const int kk = kbi * BK + kr;       // k-row across both keys
+              const int kk = kb * BK + kr;        // k-row across both keys
               const int wr = kk - key * p.krows;  // k-row inside the key's matrix
-              const int nbg = n * 4 + nbase + nbq;
+              const int nbg = n * (TN / 64) + nbase + nbq;
               live = nbg < nblk_row;
               blk = wr * nblk_row + nbg;
               qcode = dq->absq[kk * (C::B_ROWS / 64) + nbq];
@@ -798,50 +810,32 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             const float scale = live ? __fadd_rn(__fmul_rn(dq->ncode[key][qcode], dq->nested[key][blk >> p.nbs_shift]),
                                                  off[key])
                                      : 0.f;
-            nf4_table(code, scale, tab[i]);
-          } else {
-            iscale[i] = MN ? reinterpret_cast<const float*>(dq->absq)[kbi * BK + kr] : row_scale;
-          }
-        }
-        // ---- decode into the swizzled operand rows
+            Nf4Tab tab;
+            nf4_table(code, scale, tab);
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          if (!dec[i]) continue;
-          const uint32_t row_addr = smem_u32(sB + st[i] * B_BYTES) + (uint32_t)row * 128u;
-          if (WF == W_NF4) {
-#pragma unroll
-            for (int c = 0; c < CH; ++c) {
+            for (int c = 0; c < 8; ++c) {
               uint32_t o[4];
-              nf4_word(words[i][c], tab[i], o);
-              st_shared_v4(row_addr + (uint32_t)(((c0 + c) ^ sw) << 4), o[0], o[1], o[2], o[3]);
+              nf4_word(words[c], tab, o);
+              st_shared_v4(row_addr + (uint32_t)((c ^ sw) << 4), o[0], o[1], o[2], o[3]);
             }
           } else {
+            const float iscale = MN ? reinterpret_cast<const float*>(dq->absq)[kb * BK + kr] : row_scale;
 #pragma unroll
-            for (int v = 0; v < CH / 2; ++v) {
+            for (int v = 0; v < 4; ++v) {
               uint32_t o[8];
-              int8_x16(make_uint4(words[i][4 * v], words[i][4 * v + 1], words[i][4 * v + 2], words[i][4 * v + 3]),
-                       iscale[i], o);
-              st_shared_v4(row_addr + (uint32_t)(((c0 + 2 * v) ^ sw) << 4), o[0], o[1], o[2], o[3]);
-              st_shared_v4(row_addr + (uint32_t)(((c0 + 2 * v + 1) ^ sw) << 4), o[4], o[5], o[6], o[7]);
+              int8_x16(reinterpret_cast<const uint4*>(raw)[v], iscale, o);
+              st_shared_v4(row_addr + (uint32_t)(((2 * v) ^ sw) << 4), o[0], o[1], o[2], o[3]);
+              st_shared_v4(row_addr + (uint32_t)(((2 * v + 1) ^ sw) << 4), o[4], o[5], o[6], o[7]);
             }
           }
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            if (i < nk) {
-              mbar_arrive(&sm.raw_empty[rst[i]]);
-              if (PAIR) mbar_arrive_cluster(full_leader0 + 8u * st[i]);
-              else mbar_arrive(&sm.full[st[i]]);
-            }
-          }
+          mbar_arrive(&sm.raw_empty[rst]);
+          if (PAIR) mbar_arrive_cluster(full_leader0 + 8u * st);
+          else mbar_arrive(&sm.full[st]);
         }
-        stage = st[nk - 1] + 1 == STAGES ? 0 : st[nk - 1] + 1;
-        phase = st[nk - 1] + 1 == STAGES ? ph[nk - 1] ^ 1 : ph[nk - 1];
-        rstage = rst[nk - 1] + 1 == RAW_STAGES ? 0 : rst[nk - 1] + 1;
-        rphase = rst[nk - 1] + 1 == RAW_STAGES ? rph[nk - 1] ^ 1 : rph[nk - 1];
       }
     }
   }
@@ -880,12 +874,14 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
     if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     attr_set = true;
   }
-  const int64_t max_tiles = ((p.S + C::TILE_M - 1) / C::TILE_M + p.E) * (int64_t)p.n_tiles;
+  Params q = p;
+  q.n_tiles = MODE == GATEUP ? q.N / (C::TN / 2) : (q.N + C::TN - 1) / C::TN;
+  const int64_t max_tiles = ((q.S + C::TILE_M - 1) / C::TILE_M + q.E) * (int64_t)q.n_tiles;
   static const char* names[4] = {"gateup_swiglu", "down", "down_dx", "gateup_dx"};
   const int sms = sm_count();
   if (!PAIR) {
     const int grid = (int)(max_tiles < sms ? max_tiles : sms);
-    kern<<<grid, C::THREADS, smem, stream>>>(ta, tb0, tb1, txa, txb, p);
+    kern<<<grid, C::THREADS, smem, stream>>>(ta, tb0, tb1, txa, txb, q);
     return check_launch(names[MODE]);
   }
   cudaLaunchConfig_t cfg = {};
@@ -915,7 +911,7 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
   }
   const int64_t units = max_tiles < resident_pairs ? max_tiles : resident_pairs;
   cfg.gridDim = dim3((unsigned)(2 * units), 1, 1);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb0, tb1, txa, txb, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb0, tb1, txa, txb, q);
   if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "%s: launch failed: %s", names[MODE], cudaGetErrorString(e));
   return check_launch(names[MODE]);
 }
@@ -950,7 +946,7 @@ int prepare(const char* name, const void* a, const int32_t* offsets, int E, int6
   p.S = S;
   p.K = K;
   p.N = N;
-  p.n_tiles = MODE == GATEUP ? N / (BN / 2) : (N + BN - 1) / BN;
+  p.n_tiles = 0;  // set per tile geometry at launch
   p.krows = MODE == DXDOWN ? K : (MODE == DXGATEUP ? K / 2 : 0);
   p.kb_half = MODE == DXGATEUP ? (K / 2) / BK : 0;
   p.out_rows = N;
@@ -962,15 +958,16 @@ int prepare(const char* name, const void* a, const int32_t* offsets, int E, int6
                       CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-// bf16 weight map.  K-major: [E*rows, cols] with boxes of 64 cols x 128 rows.
+// bf16 weight map.  K-major: [E*rows, cols] with boxes of 64 cols x box_rows rows.
 // MN-major: the same matrix read as [E*rows (k), cols (n)] with 64 x 64 boxes.
-int bf16_weight_map(CUtensorMap& m, const void* w, int E, int rows, int cols, bool mn) {
+int bf16_weight_map(CUtensorMap& m, const void* w, int E, int rows, int cols, bool mn, int box_rows) {
   if (!w) return set_error(MIRAI_ERR_INVALID_ARG, "null weight pointer");
   return make_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, (uint64_t)cols, (uint64_t)E * rows,
-                      (uint64_t)cols * 2, 64, mn ? 64 : BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+                      (uint64_t)cols * 2, 64, mn ? 64 : box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-int nf4_key(CUtensorMap& m, QKey& q, int& nbs_shift, const mirai_nf4_weight* w, int E, int rows, int cols, bool mn) {
+int nf4_key(CUtensorMap& m, QKey& q, int& nbs_shift, const mirai_nf4_weight* w, int E, int rows, int cols, bool mn,
+            int box_rows) {
   if (!w || !w->packed || !w->absmax || !w->nested_absmax || !w->offset || !w->code || !w->nested_code)
     return set_error(MIRAI_ERR_INVALID_ARG, "nf4 weight: null buffer");
   if (w->blocksize != 64)
@@ -994,17 +991,17 @@ int nf4_key(CUtensorMap& m, QKey& q, int& nbs_shift, const mirai_nf4_weight* w, 
     return set_error(MIRAI_ERR_UNSUPPORTED, "nf4 weight: %d nested absmax blocks per expert (max %d)", q.n_nested,
                      kMaxNested);
   // packed nibbles as a [E*rows, cols/2] byte tensor; boxes of one 64-element
-  // block per row: 128 rows (K-major) or 64 rows (MN-major)
+  // block per row: box_rows rows (K-major) or 64 rows (MN-major)
   return make_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->packed, (uint64_t)cols / 2, (uint64_t)E * rows,
-                      (uint64_t)cols / 2, 32, mn ? 64 : BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+                      (uint64_t)cols / 2, 32, mn ? 64 : box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-int int8_key(CUtensorMap& m, QKey& q, const mirai_int8_weight* w, int E, int rows, int cols, bool mn) {
+int int8_key(CUtensorMap& m, QKey& q, const mirai_int8_weight* w, int E, int rows, int cols, bool mn, int box_rows) {
   if (!w || !w->q || !w->scale) return set_error(MIRAI_ERR_INVALID_ARG, "int8 weight: null buffer");
   q = QKey{};
   q.scale = w->scale;
   return make_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w->q, (uint64_t)cols, (uint64_t)E * rows, (uint64_t)cols,
-                      64, mn ? 64 : BN / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+                      64, mn ? 64 : box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 // Bind one weight key in any format.  rows x cols is one expert's matrix.
@@ -1015,10 +1012,20 @@ struct WeightArg {
   const mirai_int8_weight* int8;
 };
 
-int bind_key(const WeightArg& w, CUtensorMap& m, QKey& q, int& shift, int E, int rows, int cols, bool mn) {
-  if (w.fmt == W_BF16) return bf16_weight_map(m, w.bf16, E, rows, cols, mn);
-  if (w.fmt == W_NF4) return nf4_key(m, q, shift, w.nf4, E, rows, cols, mn);
-  return int8_key(m, q, w.int8, E, rows, cols, mn);
+int bind_key(const WeightArg& w, CUtensorMap& m, QKey& q, int& shift, int E, int rows, int cols, bool mn,
+             int box_rows) {
+  if (w.fmt == W_BF16) return bf16_weight_map(m, w.bf16, E, rows, cols, mn, box_rows);
+  if (w.fmt == W_NF4) return nf4_key(m, q, shift, w.nf4, E, rows, cols, mn, box_rows);
+  return int8_key(m, q, w.int8, E, rows, cols, mn, box_rows);
+}
+
+// Rows of one K-major B box (TN/2: the half of a tile's columns one CTA of a
+// pair holds, or one of the two boxes of a single-CTA tile).
+static int kmajor_box_rows(int fmt) {
+  static_assert(Cfg<W_BF16, true>::TN == Cfg<W_NF4, true>::TN && Cfg<W_NF4, true>::TN == Cfg<W_NF4, false>::TN,
+                "one column-tile width for every format");
+  (void)fmt;
+  return Cfg<W_BF16, true>::TN / 2;
 }
 
 // The optional rank block of a fused LoRA adapter: ext_a [S, 64] bf16 (one
@@ -1036,6 +1043,7 @@ int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t 
   if (S == 0 && E > 0) return MIRAI_OK;
   Params p;
   CUtensorMap ta, t0, t1, txa, txb;
+  const int box_rows = kmajor_box_rows(w0.fmt);
   int rc = prepare<MODE>(name, a, offsets, E, S, K, N, out, gate_up, p, ta);
   if (!rc && ext) {
     if (!ext->a || !ext->b) rc = set_error(MIRAI_ERR_INVALID_ARG, "%s: null rank-block operand", name);
@@ -1048,7 +1056,7 @@ int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t 
                           (uint64_t)N * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
       else  // [E*N rows, 64 rank cols (k)]
         rc = make_tmap_2d(&txb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ext->b, 64, (uint64_t)E * N, 128, BK,
-                          BN / 2, CU_TENSOR_MAP_SWIZZLE_128B);
+                          box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
     }
     p.has_ext = 1;
   }
@@ -1058,8 +1066,8 @@ int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t 
   if (!rc && !MN && w0.fmt != W_BF16 && K > kMaxK)
     rc = set_error(MIRAI_ERR_UNSUPPORTED, "%s: in_features %d exceeds %d", name, K, kMaxK);
   int s0 = 8, s1 = 8;
-  if (!rc) rc = bind_key(w0, t0, p.q[0], s0, E, rows, cols, MN);
-  if (!rc && MCfg<MODE>::TWO_KEYS) rc = bind_key(w1, t1, p.q[1], s1, E, rows, cols, MN);
+  if (!rc) rc = bind_key(w0, t0, p.q[0], s0, E, rows, cols, MN, box_rows);
+  if (!rc && MCfg<MODE>::TWO_KEYS) rc = bind_key(w1, t1, p.q[1], s1, E, rows, cols, MN, box_rows);
   if (!rc && MCfg<MODE>::TWO_KEYS && s0 != s1)
     rc = set_error(MIRAI_ERR_UNSUPPORTED, "%s: the two keys use different nested blocksizes", name);
   if (rc) return rc;

@@ -492,3 +492,50 @@ def test_lora_project_and_grad_ragged_segments(K, rank):
     assert om.rel_max_err(ga.cpu().numpy(), ref_ga) < 1e-4
     assert om.rel_max_err(gb.cpu().numpy(), ref_ga.transpose(0, 2, 1)) < 1e-4
     assert np.all(ga.cpu().numpy()[[0, 5]] == 0)
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "int8", "bf16"])
+def test_grouped_gemms_on_tile_edge_segments(fmt):
+    """All four grouped GEMMs on segments around the 256- and 512-row tile
+    edges (empty, 1, 255..257, 511..513 rows): a quantised CTA-pair tile holds
+    two 256-row sub-tiles, and a sub-tile past a segment's end is skipped."""
+    dev = _dev()
+    from mirai_b200 import ops
+    counts = np.array([0, 1, 255, 256, 257, 511, 512, 513, 0, 130])
+    E, H, I = len(counts), 256, 384
+    offsets = np.cumsum(counts).astype(np.int32)
+    S = int(offsets[-1])
+    rng = np.random.default_rng(7 + len(fmt))
+    x = oq.bf16_round(rng.standard_normal((S, H)).astype(np.float32))
+    gy = oq.bf16_round(rng.standard_normal((S, H)).astype(np.float32))
+    dense, dw = _weights(fmt, rng, E, H, I, dev)
+    off = torch.from_numpy(offsets).to(dev)
+    h, gu = ops.gateup_swiglu(_bf16(x).to(dev), off, dw[0], dw[1], inter=I, save_gate_up=True)
+    y = ops.down(h, off, dw[2], hidden=H)
+    dgu = ops.down_dx(_bf16(gy).to(dev), off, dw[2], gu, inter=I)
+    dxs = ops.gateup_dx(dgu, off, dw[0], dw[1], hidden=H)
+    _check(ops)
+    _, inter = om.expert_ffn_forward(x, offsets, dense[0], dense[1], dense[2], bf16=True, keep=True)
+    assert om.rel_max_err(_f32(gu[:, :I]), inter["gate"]) < 1e-2
+    assert om.rel_max_err(_f32(gu[:, I:]), inter["up"]) < 1e-2
+    assert om.rel_max_err(_f32(h), inter["h"]) < TOL
+    hk, guk, dguk = _f32(h), _f32(gu), _f32(dgu)
+    ref_y = np.zeros((S, H), np.float32)
+    ref_dgu = np.zeros((S, 2 * I), np.float32)
+    ref_dx = np.zeros((S, H), np.float32)
+    start = 0
+    for e in range(E):
+        end = int(offsets[e])
+        if end > start:
+            ref_y[start:end] = hk[start:end] @ dense[2][e].T
+            gate, up = guk[start:end, :I], guk[start:end, I:]
+            dh = oq.bf16_round(gy[start:end] @ dense[2][e])
+            act = oq.bf16_round(om.silu_f32(gate))
+            d_act = oq.bf16_round(dh * up)
+            ref_dgu[start:end, I:] = dh * act
+            ref_dgu[start:end, :I] = om.silu_backward_f32(d_act, gate)
+            ref_dx[start:end] = dguk[start:end, :I] @ dense[0][e] + dguk[start:end, I:] @ dense[1][e]
+        start = end
+    assert om.rel_max_err(_f32(y), ref_y) < TOL
+    assert om.rel_max_err(dguk, ref_dgu) < 3e-2
+    assert om.rel_max_err(_f32(dxs), ref_dx) < TOL
