@@ -11,8 +11,11 @@ NF4 dequant) -> weighted combine.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
 
-Under torchrun (N > 1) every rank runs its own replica on its own tokens
-(experts replicated, no data-path collective): scaling "weak".
+Under torchrun (N > 1) the layer runs expert-parallel (mirai_b200.expert_parallel):
+each rank owns E/N experts and routes its own tokens, with one NCCL all-to-all
+each way per layer.  c1-c3 keep their token count per rank (scaling "weak":
+per-GPU GEMM work is that of one GPU); c4 is BASELINE config 4, a 16-layer
+stack over 65536 tokens in total (scaling "strong").
 ``--impl reference`` times the CPU restatement of the reference's torch path
 (``oracle/``) on the host cores, rank 0 only.
 """
@@ -35,6 +38,9 @@ CONFIGS = {
     "c1": dict(T=32768, H=2048, E=32, k=2, I=1408, fmt="bf16", zipf=None),
     "c2": dict(T=32768, H=2048, E=32, k=2, I=1408, fmt="nf4", zipf=None),
     "c3": dict(T=8192, H=3072, E=64, k=4, I=1024, fmt="int8", zipf=1.2),
+    # expert-parallel stack: 16 layers, 65536 tokens split over the ranks, 128 experts
+    # (16 per GPU at 8); strong scaling
+    "c4": dict(T=65536, H=4096, E=128, k=8, I=1536, fmt="nf4", zipf=None, layers=16, ep="strong"),
 }
 METRIC = "MoE-FFN tokens/s (NF4 experts) + % TC/HBM roofline at 1/2/4/8 B200"
 # Our kernels launched by one forward step: route 1, plan 4, permute 1, gate/up 1, down 1,
@@ -47,7 +53,7 @@ LORA_RANK = 16
 # DRAM bytes (read + write) of one gate/up launch from an ncu capture of the
 # same kernel on the same workload (profiles/ holds the capture's summary and
 # its command).  Workloads not captured report null.
-NCU_TRAFFIC = {"c2-gateup": 363_836_416 + 163_019_776}
+NCU_TRAFFIC = {"c2-gateup": 363_971_840 + 163_746_560}
 
 
 def load_peaks():
@@ -162,6 +168,68 @@ def weight_bytes(cfg):
 
 # ----------------------------------------------------------------------------- our arm
 
+def measure_e2e(dev, host_in, n_out, out_shape, compute, args, barrier):
+    """ms per step through the public API with host buffers.  Every step copies
+    its inputs host -> device from pinned memory and its results device -> host.
+    Two buffer slots and two copy streams let step j's upload and step j-1's
+    download overlap the neighbouring steps' compute, as a serving loop would."""
+    import torch
+
+    comp = torch.cuda.current_stream()
+    up, down_s = torch.cuda.Stream(), torch.cuda.Stream()
+    slots = []
+    for _ in range(2):
+        slots.append({
+            "din": [torch.empty_like(t, device=dev) for t in host_in],
+            "dout": [torch.empty(out_shape, dtype=torch.bfloat16, device=dev) for _ in range(n_out)],
+            "hout": [torch.empty(out_shape, dtype=torch.bfloat16).pin_memory() for _ in range(n_out)],
+            "loaded": torch.cuda.Event(), "computed": torch.cuda.Event(), "saved": torch.cuda.Event(),
+            "used": False,
+        })
+
+    def e2e_step(j):
+        sl = slots[j % 2]
+        with torch.cuda.stream(up):
+            if sl["used"]:
+                up.wait_event(sl["computed"])  # the slot's previous step has read its inputs
+            for d, h in zip(sl["din"], host_in):
+                d.copy_(h, non_blocking=True)
+            sl["loaded"].record(up)
+        comp.wait_event(sl["loaded"])
+        if sl["used"]:
+            comp.wait_event(sl["saved"])  # the slot's previous result has been downloaded
+        compute(sl["din"], sl["dout"])
+        sl["computed"].record(comp)
+        with torch.cuda.stream(down_s):
+            down_s.wait_event(sl["computed"])
+            for h, d in zip(sl["hout"], sl["dout"]):
+                h.copy_(d, non_blocking=True)
+            sl["saved"].record(down_s)
+        sl["used"] = True
+
+    def drain():
+        for sl in slots:
+            if sl["used"]:
+                comp.wait_event(sl["saved"])
+
+    for j in range(max(1, min(3, args.warmup))):
+        e2e_step(j)
+    drain()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    up.wait_event(e0)
+    down_s.wait_event(e0)
+    for j in range(args.steps):
+        e2e_step(j)
+    drain()
+    e1.record(comp)
+    e1.synchronize()
+    barrier()
+    return e0.elapsed_time(e1) / args.steps
+
+
 def run_ours(args, cfg, rank, world, dev):
     import torch
     import torch.distributed as dist
@@ -227,6 +295,7 @@ def run_ours(args, cfg, rank, world, dev):
     h = torch.empty((S, I), dtype=torch.bfloat16, device=dev)
     y = torch.empty((S, H), dtype=torch.bfloat16, device=dev)
     reps = max(5, min(50, args.steps))
+    kclocks = ClockSampler(torch.cuda.current_device()).start()
     for _ in range(3):
         ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I, out=h)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
@@ -242,70 +311,18 @@ def run_ours(args, cfg, rank, world, dev):
         b.record()
     torch.cuda.synchronize()
     down_ms = sum(a.elapsed_time(b) for a, b in evs) / reps
+    kclk = kclocks.stop()
 
-    # ---- end to end through the public API with host buffers.  Every step copies its
-    # inputs host -> device from pinned memory and its result device -> host.  Two
-    # buffer slots and two copy streams let step j's input upload and step j-1's
-    # download overlap step j-1's / step j's compute, as a serving loop would.
-    comp = torch.cuda.current_stream()
-    up, down_s = torch.cuda.Stream(), torch.cuda.Stream()
+    # ---- end to end through the public API with host buffers
     host_in = [x.cpu().pin_memory(), logits.cpu().pin_memory()] + ([g_out.cpu().pin_memory()] if train else [])
-    n_out = 2 if train else 1
-    slots = []
-    for _ in range(2):
-        slots.append({
-            "din": [torch.empty_like(t, device=dev) for t in host_in],
-            "dout": [torch.empty((T, H), dtype=torch.bfloat16, device=dev) for _ in range(n_out)],
-            "hout": [torch.empty((T, H), dtype=torch.bfloat16).pin_memory() for _ in range(n_out)],
-            "loaded": torch.cuda.Event(), "computed": torch.cuda.Event(), "saved": torch.cuda.Event(),
-            "used": False,
-        })
 
-    def e2e_step(j):
-        sl = slots[j % 2]
-        with torch.cuda.stream(up):
-            if sl["used"]:
-                up.wait_event(sl["computed"])  # the slot's previous step has read its inputs
-            for d, h in zip(sl["din"], host_in):
-                d.copy_(h, non_blocking=True)
-            sl["loaded"].record(up)
-        comp.wait_event(sl["loaded"])
-        if sl["used"]:
-            comp.wait_event(sl["saved"])  # the slot's previous result has been downloaded
-        xin, lin = sl["din"][0], sl["din"][1]
+    def compute(din, dout):
         if train:
-            step(xin, lin, out=sl["dout"][0], gin=sl["din"][2], dx_out=sl["dout"][1])
+            step(din[0], din[1], out=dout[0], gin=din[2], dx_out=dout[1])
         else:
-            step(xin, lin, out=sl["dout"][0])
-        sl["computed"].record(comp)
-        with torch.cuda.stream(down_s):
-            down_s.wait_event(sl["computed"])
-            for h, d in zip(sl["hout"], sl["dout"]):
-                h.copy_(d, non_blocking=True)
-            sl["saved"].record(down_s)
-        sl["used"] = True
+            step(din[0], din[1], out=dout[0])
 
-    def drain():
-        for sl in slots:
-            if sl["used"]:
-                comp.wait_event(sl["saved"])
-
-    for j in range(max(1, min(3, args.warmup))):
-        e2e_step(j)
-    drain()
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(comp)
-    up.wait_event(e0)
-    down_s.wait_event(e0)
-    for j in range(args.steps):
-        e2e_step(j)
-    drain()
-    e1.record(comp)
-    e1.synchronize()
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
+    e2e_ms = measure_e2e(dev, host_in, 2 if train else 1, (T, H), compute, args, barrier)
     ops.check_device()
 
     if world > 1:
@@ -352,6 +369,7 @@ def run_ours(args, cfg, rank, world, dev):
             "peak_source": f"{peaks['source']} bf16 dense (burst; kernel timed alone)",
             "algorithmic": f"4*S*H*I = {flops_gu / 1e9:.1f} GFLOP per launch",
             "traffic": traffic,
+            "clocks": kclk,
         },
         "e2e": {
             "value": world * T / (e2e_ms * 1e-3),
@@ -364,6 +382,184 @@ def run_ours(args, cfg, rank, world, dev):
         "clocks": clk,
     }
     return line
+
+
+
+# ----------------------------------------------------------------------------- expert-parallel arm
+
+# per layer: route 1, plan 4, permute 1, local plan 4, local permute 1, gate/up 1, down 1,
+# un-permute 1, combine 1 (the NCCL all-to-alls are not counted)
+EP_KERNELS_PER_LAYER = 15
+
+
+def make_ep_workload(cfg, dev, rank, shard, tokens_local):
+    """This rank's tokens, layer-0 router logits and, per layer, the router gate
+    (identical on every rank) and this rank's E/N experts (seeded per rank)."""
+    import torch
+    from mirai_b200 import ops, tables
+
+    H, E, I = cfg["H"], cfg["E"], cfg["I"]
+    El = shard.local
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    x = torch.randn(tokens_local, H, generator=g, device=dev).to(torch.bfloat16)
+    stack = []
+    for layer in range(cfg.get("layers", 1)):
+        gate = (torch.randn(E, H, generator=torch.Generator(device=dev).manual_seed(77 + layer), device=dev)
+                * 0.02).to(torch.bfloat16)
+        wg = torch.Generator(device=dev).manual_seed(100003 * (layer + 1) + rank)
+        ws = []
+        for shape in ((El, I, H), (El, I, H), (El, H, I)):
+            w = (torch.randn(shape, generator=wg, device=dev) * 0.02).to(torch.bfloat16)
+            if cfg["fmt"] == "nf4":
+                w = ops.nf4_quantize(w, tables.nf4_code(dev), tables.dynamic_map(dev))
+            elif cfg["fmt"] == "int8":
+                w = ops.int8_quantize(w.float())
+            ws.append(w)
+        stack.append((gate, tuple(ws)))
+    x0 = x.float()
+    u0 = (x0 * torch.rsqrt(x0.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+    logits0 = ((u0 if cfg.get("layers", 1) > 1 else x) @ stack[0][0].T).float()
+    torch.cuda.synchronize()
+    return x, logits0, stack
+
+
+def run_ep(args, cfg, rank, world, dev):
+    import torch
+    import torch.distributed as dist
+    from mirai_b200 import ops
+    from mirai_b200.expert_parallel import CudaStepOps, ExpertShard, ep_moe_forward, shard_tokens
+
+    H, E, k, I = cfg["H"], cfg["E"], cfg["k"], cfg["I"]
+    layers = cfg.get("layers", 1)
+    strong = cfg.get("ep") == "strong"
+    T_total = cfg["T"] if strong else cfg["T"] * world
+    b, e = shard_tokens(T_total, world, rank)
+    T_r = e - b
+    shard = ExpertShard(E, world, rank)
+    x, logits0, stack = make_ep_workload(cfg, dev, rank, shard, T_r)
+    stepops = CudaStepOps()
+
+    def rms_norm(v):  # the block's pre-MoE norm (no learned scale): keeps the stack's activations bounded
+        vf = v.float()
+        return (vf * torch.rsqrt(vf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+
+    def step(xin, l0, out=None):
+        h = xin
+        for li, (gate, ws) in enumerate(stack):
+            if layers == 1:
+                h = ep_moe_forward(h, l0, ws, shard=shard, top_k=k, inter=I, ops=stepops)
+                continue
+            u = rms_norm(h)
+            lg = l0 if li == 0 else (u @ gate.T).float()
+            h = h + ep_moe_forward(u, lg, ws, shard=shard, top_k=k, inter=I, ops=stepops)  # residual
+        if out is not None:
+            out.copy_(h)
+        return h
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step(x, logits0)
+    ops.check_device()
+    clocks = ClockSampler(torch.cuda.current_device()).start()
+    barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step(x, logits0)
+    t1.record()
+    t1.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    ops.check_device()
+
+    # ---- dominant kernel alone: gate/up on this rank's expected share of rows
+    # (T_total * k / N routed rows spread evenly over its E/N experts)
+    R = T_total * k // world
+    offs = torch.tensor([(R * (j + 1)) // shard.local for j in range(shard.local)], dtype=torch.int32, device=dev)
+    xl = torch.randn(R, H, device=dev).to(torch.bfloat16)
+    hl = torch.empty((R, I), dtype=torch.bfloat16, device=dev)
+    w1, w3, _ = stack[0][1]
+    kclocks = ClockSampler(torch.cuda.current_device()).start()
+    for _ in range(3):
+        ops.gateup_swiglu(xl, offs, w1, w3, inter=I, out=hl)
+    reps = max(5, min(20, args.steps))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, bb in evs:
+        a.record()
+        ops.gateup_swiglu(xl, offs, w1, w3, inter=I, out=hl)
+        bb.record()
+    torch.cuda.synchronize()
+    gu_ms = sum(a.elapsed_time(bb) for a, bb in evs) / reps
+    kclk = kclocks.stop()
+    del xl, hl
+
+    # ---- end to end with host buffers (each rank: its tokens and layer-0 logits up, its output down)
+    host_in = [x.cpu().pin_memory(), logits0.cpu().pin_memory()]
+    e2e_ms = measure_e2e(dev, host_in, 1, (T_r, H), lambda din, dout: step(din[0], din[1], out=dout[0]),
+                         args, barrier)
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+    peaks = load_peaks()
+    flops_gu = 4.0 * R * H * I
+    achieved = flops_gu / (gu_ms * 1e-3) / 1e12
+    S_total = T_total * k
+    return {
+        "metric": METRIC,
+        "value": T_total / (ms * 1e-3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong" if strong else "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 activations x " + cfg["fmt"] + " weights, fp32 accumulate",
+        "data": "synthetic (seeded torch.randn tokens and router gates; random-init experts quantised on the GPU)",
+        "config": {
+            "workload": f"{args.config}: " + (f"a stack of {layers} routed expert FFN layers" if layers > 1 else
+                                              "one routed expert FFN layer") +
+                        f" forward, expert-parallel over {world} GPU(s), T={T_total} tokens in total "
+                        f"({T_r} on rank 0), H={H} E={E} ({shard.local} per GPU) k={k} I={I} {cfg['fmt']} experts",
+            "tokens_total": T_total, "hidden": H, "experts": E, "experts_per_gpu": shard.local, "top_k": k,
+            "intermediate": I, "layers": layers, "weights": cfg["fmt"],
+            "parallelism": f"ep{world}: experts sharded by contiguous blocks, tokens sharded by rank, "
+                           "NCCL all_to_all_single dispatch and return per layer",
+            "l2": "no flush: each layer's routed activations exceed the 126 MB L2",
+        },
+        "tflops": 6.0 * S_total * H * I * layers / (ms * 1e-3) / 1e12,
+        "roofline": {
+            "kernel": f"gateup_swiglu_{cfg['fmt']}",
+            "bound": "tensor",
+            "achieved": achieved,
+            "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s",
+            "frac": achieved / peaks["bf16_tflops"],
+            "peak_source": f"{peaks['source']} bf16 dense (burst; kernel timed alone)",
+            "algorithmic": f"4*R*H*I = {flops_gu / 1e9:.1f} GFLOP per launch, R = {R} rows of rank 0's share",
+            "traffic": None,
+            "clocks": kclk,
+        },
+        "e2e": {
+            "value": T_total / (e2e_ms * 1e-3),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": T_r * H * 2 + T_r * E * 4,
+            "d2h_bytes_per_step": T_r * H * 2,
+            "copies": "per rank: pinned host buffers; 2 slots, uploads and downloads on their own streams",
+        },
+        "gpu_launches": EP_KERNELS_PER_LAYER * layers * args.steps,
+        "gpu_launches_scope": "per rank",
+        "clocks": clk,
+    }
 
 
 # ----------------------------------------------------------------------------- CPU reference (oracle port)
@@ -440,10 +636,21 @@ class CpuReference:
 
 
 def cpu_sample_tokens(cfg):
-    return min(cfg["T"], 4096)
+    return min(cfg["T"], 4096 if not cfg.get("layers") else 1024)
+
+
+def cpu_sample_cfg(cfg):
+    """The CPU restatement runs one layer; for the expert-parallel stack it takes
+    one GPU's share of the experts (16 of 128) so the host holds a few GB, and
+    the rate is divided by the number of layers."""
+    if cfg.get("layers"):
+        return dict(cfg, E=16, layers=1), cfg["layers"], (f"one layer with 16 of {cfg['E']} experts, "
+                                                         f"rate divided by {cfg['layers']} layers")
+    return cfg, 1, ""
 
 
 def run_reference(args, cfg):
+    cfg, per, note = cpu_sample_cfg(cfg)
     ref = CpuReference(cfg, cpu_sample_tokens(cfg))
     for _ in range(args.warmup):
         ref.step()
@@ -451,9 +658,9 @@ def run_reference(args, cfg):
     for _ in range(args.steps):
         ref.step()
     sec = (time.perf_counter() - t) / args.steps
-    value = ref.T / sec
+    value = ref.T / sec / per
     sample = (f"{ref.T} of {cfg['T']} tokens per step, full dequantisation of all {cfg['E']} experts each step "
-              f"(as the reference's chunked_dequant path does every forward)")
+              f"(as the reference's chunked_dequant path does every forward)" + (f"; {note}" if note else ""))
     return {
         "metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": 0,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
@@ -467,6 +674,7 @@ def run_reference(args, cfg):
 
 
 def cpu_baseline(cfg):
+    cfg, per, note = cpu_sample_cfg(cfg)
     ref = CpuReference(cfg, cpu_sample_tokens(cfg))
     ref.step()  # warm
     t = time.perf_counter()
@@ -477,9 +685,10 @@ def cpu_baseline(cfg):
         if time.perf_counter() - t > 10.0 or n >= 3:
             break
     sec = (time.perf_counter() - t) / n
-    return {"value": ref.T / sec, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
+    return {"value": ref.T / sec / per, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
             "sample": f"{n} forward(s) of {ref.T} tokens of the {cfg['T']}-token workload, dequantising all "
-                      f"experts each forward; oracle/ numpy restatement of the reference torch path"}
+                      f"experts each forward; oracle/ numpy restatement of the reference torch path"
+                      + (f"; {note}" if note else "")}
 
 
 # ----------------------------------------------------------------------------- main
@@ -500,6 +709,8 @@ def main():
     cfg = CONFIGS[args.config]
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.mode == "train" and (world > 1 or cfg.get("layers")):
+        raise SystemExit("--mode train runs the single-GPU layer (c0-c3 on one GPU)")
 
     if args.impl == "reference":
         if rank == 0:
@@ -518,8 +729,9 @@ def main():
     try:
         from mirai_b200 import _lib
         _lib.load()
-        line = run_ours(args, cfg, rank, world, dev)
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line = run_ep(args, cfg, rank, world, dev) if (world > 1 or cfg.get("layers")) else \
+            run_ours(args, cfg, rank, world, dev)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the host-core baseline, N = 1 only
             line["cpu_baseline"] = cpu_baseline(cfg)
         if rank == 0:
             print(json.dumps(line), flush=True)

@@ -138,7 +138,7 @@ int mirai_moe_gateup_swiglu_int8(const void* x_sorted, const int32_t* offsets, i
 /* ------------------------------------------------- a7: down grouped GEMM
  * y[s, :] = h[s, :] W2[e]^T for the rows of segment e -> y [S, H] bf16
  * (_FrozenDequantBatchedLinear.forward, linear.py:95-114).  Requires
- * I % 64 == 0, H % 256 == 0. */
+ * I % 64 == 0, H % 64 == 0. */
 int mirai_moe_down_bf16(const void* h, const int32_t* offsets, int32_t num_experts,
                         int64_t num_rows, int32_t inter, int32_t hidden, const void* w2, void* y,
                         mirai_stream_t stream);

@@ -723,12 +723,15 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           const int nblk = PAIR ? 1 : 2;
           for (int h = 0; h < nblk; ++h) {
             const int blk = PAIR ? (int)rank : h;
-            if (kmajor_row<MODE, TN>(p, e, n, blk) - e * p.out_rows >= p.out_rows) continue;  // past the last row
+            // rows of this half inside the expert's matrix (a multiple of 64: N % 64 == 0)
+            const int first = kmajor_row<MODE, TN>(p, e, n, blk) - e * p.out_rows;
+            const int rows = min(TN / 2, p.out_rows - first);
+            if (rows <= 0) continue;  // past the last row
             const int key = MCfg<MODE>::TWO_KEYS ? blk : 0;
             const uint4* src = reinterpret_cast<const uint4*>(
                 p.q[key].absmax + (size_t)kmajor_row<MODE, TN>(p, e, n, blk) * nkb);
             uint4* dst = reinterpret_cast<uint4*>(dq->absq + h * (TN / 2) * nkb);
-            for (int i = d; i < (TN / 2) * nkb / 16; i += kDeqThreads) dst[i] = __ldg(src + i);
+            for (int i = d; i < rows * nkb / 16; i += kDeqThreads) dst[i] = __ldg(src + i);
           }
         } else {
           // absq[kk * NB + j] = code of (k-row kk, this CTA's column block j)
@@ -932,7 +935,10 @@ int prepare(const char* name, const void* a, const int32_t* offsets, int E, int6
             void* gate_up, Params& p, CUtensorMap& ta) {
   if (E <= 0 || E > kMaxExperts || S < 0 || K <= 0 || N <= 0)
     return set_error(MIRAI_ERR_INVALID_ARG, "%s: bad sizes (E=%d, S=%lld, K=%d, N=%d)", name, E, (long long)S, K, N);
-  const int ntile = MODE == GATEUP ? BN / 2 : (MODE == DOWN ? BN / 2 : 64);
+  // column granularity: gate/up tiles pair 128 W1 rows with 128 W3 rows; the
+  // other modes mask partial 256-column tiles in 32-column chunks (and, for
+  // NF4/INT8, by weight row), so they need N % 64 only
+  const int ntile = MODE == GATEUP ? BN / 2 : 64;
   if (K % BK != 0 || N % ntile != 0)
     return set_error(MIRAI_ERR_UNSUPPORTED, "%s: needs K %% %d == 0 and N %% %d == 0 (K=%d, N=%d)", name, BK, ntile,
                      K, N);

@@ -56,7 +56,9 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
     float c;
     if (bias) c = sc[i] + bias[e < E ? e : 0];
     else c = score_func == MIRAI_SCORE_SOFTMAX ? lg[i] : sc[i];
-    ch[i] = e < E ? c : -INFINITY;
+    // a NaN key ranks last (as -inf, lowest id first), so every slot gets a
+    // valid expert id even for a row of NaN logits
+    ch[i] = (e < E && !isnan(c)) ? c : -INFINITY;
   }
   float wsel[16];
   int isel[16];

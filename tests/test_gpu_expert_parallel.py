@@ -1,0 +1,86 @@
+"""Expert-parallel layer on 2+ GPUs over NCCL against the single-GPU layer.
+
+Each rank owns E/G experts (quantised separately; NF4 and INT8 buffers are
+per expert, so a block quantised alone equals the same block of the whole
+stack) and routes a contiguous shard of the tokens.  Rows of every expert
+segment arrive in the single-GPU order, so the outputs must be bit-identical.
+Skipped with fewer than two GPUs.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _weights(fmt, E, H, I, seed, dev):
+    from mirai_b200 import ops, tables
+    g = torch.Generator(device=dev).manual_seed(seed)
+    raw = [(torch.randn(s, generator=g, device=dev) * 0.02).to(torch.bfloat16) for s in ((E, I, H), (E, I, H), (E, H, I))]
+    return raw
+
+
+def _quant(fmt, w, dev):
+    from mirai_b200 import ops, tables
+    if fmt == "nf4":
+        return ops.nf4_quantize(w, tables.nf4_code(dev), tables.dynamic_map(dev))
+    if fmt == "int8":
+        return ops.int8_quantize(w.float())
+    return w.contiguous()
+
+
+def _rank_main(rank, world, port, cfg, results):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        from mirai_b200 import ops
+        from mirai_b200.expert_parallel import ExpertShard, ep_moe_forward, shard_tokens
+        T, H, E, k, I, fmt = cfg
+        g = torch.Generator(device=dev).manual_seed(11)
+        x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+        logits = torch.randn(T, E, generator=g, device=dev) * 1.5
+        raw = _weights(fmt, E, H, I, 5, dev)
+        shard = ExpertShard(E, world, rank)
+        lo, hi = shard.first, shard.first + shard.local
+        local = tuple(_quant(fmt, w[lo:hi].contiguous(), dev) for w in raw)
+        b, e = shard_tokens(T, world, rank)
+        out = ep_moe_forward(x[b:e].contiguous(), logits[b:e].contiguous(), local, shard=shard, top_k=k, inter=I)
+        code, info = ops.device_status()
+        full = tuple(_quant(fmt, w, dev) for w in raw)
+        idx, tw = ops.route_topk(logits, k)
+        ref = ops.moe_forward(x, idx, tw, *full, num_experts=E, inter=I)[b:e]
+        results[rank] = (code, bool(torch.equal(out, ref)), float((out.float() - ref.float()).abs().max()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "bf16", "int8"])
+def test_expert_parallel_equals_single_gpu_layer(fmt):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from mirai_b200.build import build
+    build()
+    world = 2
+    cfg = (3000, 256, 8, 2, 384, fmt)
+    with mp.Manager() as mgr:
+        results = mgr.dict()
+        mp.start_processes(_rank_main, args=(world, _free_port(), cfg, results), nprocs=world, start_method="spawn")
+        res = dict(results)
+    for r in range(world):
+        code, equal, maxdiff = res[r]
+        assert code == 0
+        assert equal, f"rank {r}: max |diff| {maxdiff}"

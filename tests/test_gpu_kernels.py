@@ -495,14 +495,15 @@ def test_lora_project_and_grad_ragged_segments(K, rank):
 
 
 @pytest.mark.parametrize("fmt", ["nf4", "int8", "bf16"])
-def test_grouped_gemms_on_tile_edge_segments(fmt):
-    """All four grouped GEMMs on segments around the 256- and 512-row tile
-    edges (empty, 1, 255..257, 511..513 rows): a quantised CTA-pair tile holds
-    two 256-row sub-tiles, and a sub-tile past a segment's end is skipped."""
+@pytest.mark.parametrize("H", [256, 320])
+def test_grouped_gemms_on_tile_edge_segments(fmt, H):
+    """All four grouped GEMMs on segments around the 256-row tile edges (empty,
+    1, 255..257, 511..513 rows), and with H = 320 a last 256-column tile of the
+    down GEMM that is three quarters empty (N % 256 == 64)."""
     dev = _dev()
     from mirai_b200 import ops
     counts = np.array([0, 1, 255, 256, 257, 511, 512, 513, 0, 130])
-    E, H, I = len(counts), 256, 384
+    E, I = len(counts), 384
     offsets = np.cumsum(counts).astype(np.int32)
     S = int(offsets[-1])
     rng = np.random.default_rng(7 + len(fmt))
@@ -539,3 +540,49 @@ def test_grouped_gemms_on_tile_edge_segments(fmt):
     assert om.rel_max_err(_f32(y), ref_y) < TOL
     assert om.rel_max_err(dguk, ref_dgu) < 3e-2
     assert om.rel_max_err(_f32(dxs), ref_dx) < TOL
+
+
+def test_lora_dx_matches_reference_golden(golden):
+    """Forward, dX and top-score gradients with a LoRA adapter on w2 against the
+    reference's own autograd (bf16 experts, ActiveExpertLoRA)."""
+    dev = _dev()
+    from mirai_b200 import ops
+    g = golden("routed_dense_bf16_lora")
+    x = oq.bf16_bits_to_f32(g["tokens"])
+    w1, w3, w2 = (oq.bf16_bits_to_f32(g[k]) for k in ("w1", "w3", "w2"))
+    la, lb = oq.bf16_round(g["lora_a"]), oq.bf16_round(g["lora_b"])  # stored as fp32 values
+    scores = oq.bf16_bits_to_f32(g["top_scores"])
+    idx = torch.from_numpy(g["top_indices"]).to(dev)
+    E, I, H = w1.shape
+    dw = [_bf16(w).to(dev) for w in (w1, w3, w2)]
+    lora = ops.DownLoRA(_bf16(la).to(dev), _bf16(lb).to(dev), float(g["lora_scale"]))
+    out, st = ops.moe_forward_train(_bf16(x).to(dev), idx, torch.from_numpy(scores).to(dev), *dw, num_experts=E,
+                                    inter=I, lora=lora)
+    dx, dws = ops.moe_backward_dx(_bf16(oq.bf16_bits_to_f32(g["grad"])).to(dev), st, *dw, inter=I, lora=lora)
+    _check(ops)
+    assert om.rel_max_err(_f32(out), oq.bf16_bits_to_f32(g["out"])) < TOL
+    assert om.rel_max_err(_f32(dx), oq.bf16_bits_to_f32(g["grad_tokens"])) < 3e-2
+    assert om.rel_max_err(_f32(dws), oq.bf16_bits_to_f32(g["grad_scores"])) < 3e-2
+
+
+def test_router_nan_rows_select_valid_experts():
+    """A row of NaN logits (a diverged activation upstream) must still yield k
+    distinct in-range expert ids, so the dispatch plan downstream stays valid;
+    NaN entries rank after every number."""
+    dev = _dev()
+    from mirai_b200 import ops
+    E, k = 128, 8
+    lg = torch.randn(6, E)
+    lg[0] = float("nan")
+    lg[1, ::2] = float("nan")
+    lg[2] = float("-inf")
+    idx, w = ops.route_topk(lg.to(dev), k)
+    plan = ops.dispatch_plan(idx, E)
+    _check(ops)
+    idx = idx.cpu()
+    assert int(idx.min()) >= 0 and int(idx.max()) < E
+    for row in idx:
+        assert len(set(row.tolist())) == k
+    assert sorted(idx[0].tolist()) == list(range(k))           # all NaN: lowest ids
+    assert all(e % 2 == 1 for e in idx[1].tolist())            # the numbers win over the NaNs
+    assert int(plan.counts.sum()) == 6 * k
