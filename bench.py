@@ -438,6 +438,13 @@ def run_ep(args, cfg, rank, world, dev):
     shard = ExpertShard(E, world, rank)
     x, logits0, stack = make_ep_workload(cfg, dev, rank, shard, T_r)
     stepops = CudaStepOps()
+    chunks = args.ep_chunks if world > 1 else 1
+    comm = torch.cuda.Stream() if chunks > 1 else None
+    if chunks > 1 and args.ep_free_sms > 0:
+        # leave SMs for NCCL's kernels so the exchanges overlap the GEMMs
+        ops.set_gemm_sm_limit(torch.cuda.get_device_properties(dev).multi_processor_count - args.ep_free_sms)
+    ep = lambda u, lg, ws: ep_moe_forward(u, lg, ws, shard=shard, top_k=k, inter=I, ops=stepops, chunks=chunks,
+                                          comm_stream=comm)
 
     def rms_norm(v):  # the block's pre-MoE norm (no learned scale): keeps the stack's activations bounded
         vf = v.float()
@@ -447,11 +454,11 @@ def run_ep(args, cfg, rank, world, dev):
         h = xin
         for li, (gate, ws) in enumerate(stack):
             if layers == 1:
-                h = ep_moe_forward(h, l0, ws, shard=shard, top_k=k, inter=I, ops=stepops)
+                h = ep(h, l0, ws)
                 continue
             u = rms_norm(h)
             lg = l0 if li == 0 else (u @ gate.T).float()
-            h = h + ep_moe_forward(u, lg, ws, shard=shard, top_k=k, inter=I, ops=stepops)  # residual
+            h = h + ep(u, lg, ws)  # residual
         if out is not None:
             out.copy_(h)
         return h
@@ -533,7 +540,10 @@ def run_ep(args, cfg, rank, world, dev):
             "tokens_total": T_total, "hidden": H, "experts": E, "experts_per_gpu": shard.local, "top_k": k,
             "intermediate": I, "layers": layers, "weights": cfg["fmt"],
             "parallelism": f"ep{world}: experts sharded by contiguous blocks, tokens sharded by rank, "
-                           "NCCL all_to_all_single dispatch and return per layer",
+                           "NCCL all_to_all_single dispatch and return per layer"
+                           + (f"; {chunks} chunks per layer, exchanges on a second stream overlapping the "
+                              f"GEMMs (GEMMs capped at {torch.cuda.get_device_properties(dev).multi_processor_count - args.ep_free_sms} SMs)"
+                              if chunks > 1 else ""),
             "l2": "no flush: each layer's routed activations exceed the 126 MB L2",
         },
         "tflops": 6.0 * S_total * H * I * layers / (ms * 1e-3) / 1e12,
@@ -703,6 +713,10 @@ def main():
     ap.add_argument("--mode", default="fwd", choices=["fwd", "train"],
                     help="fwd: forward only; train: forward + dX backward through the frozen experts")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-chunks", type=int, default=2,
+                    help="N > 1: token chunks per layer whose exchanges overlap the other chunks' GEMMs")
+    ap.add_argument("--ep-free-sms", type=int, default=16,
+                    help="N > 1 with chunks: SMs the GEMMs leave free for the communication kernels")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

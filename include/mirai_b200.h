@@ -84,6 +84,12 @@ int mirai_b200_version(void);
 /* Synchronises `stream`, then returns (and clears) the device error word:
  * *code = 0 or a MIRAI_ERR_DEVICE_* code, *info = where it was raised. */
 int mirai_b200_device_status(mirai_stream_t stream, int* code, int* info);
+/* Caps the SMs the persistent grouped GEMMs occupy (0 = all SMs, the default),
+ * process-wide, for launches made after the call.  A GEMM otherwise holds
+ * every SM for its whole duration; leaving a few free lets communication
+ * kernels on another stream (an expert-parallel all-to-all) run alongside it.
+ * No reference counterpart: the reference has no expert parallelism. */
+int mirai_b200_set_gemm_sm_limit(int32_t max_sms);
 
 /* ------------------------------------------------------------ a1: router top-k
  * Replaces TokenChoiceRouter.forward's selection (routers.py:241-249) and the
@@ -148,6 +154,36 @@ int mirai_moe_down_nf4(const void* h, const int32_t* offsets, int32_t num_expert
 int mirai_moe_down_int8(const void* h, const int32_t* offsets, int32_t num_experts,
                         int64_t num_rows, int32_t inter, int32_t hidden,
                         const mirai_int8_weight* w2, void* y, mirai_stream_t stream);
+
+/* --------------------------- a6 / a7 over source-major segments (expert parallel)
+ * The same two GEMMs when the rows of each expert come in num_sources separate
+ * runs, as an expert owner receives them from its peers: `offsets` holds the
+ * inclusive ends of num_sources * num_experts segments in memory order, segment
+ * s * num_experts + e being source s's rows for (weight) expert e.  Tiles visit
+ * the segments expert-major, so the weights of one expert stay hot in L2.  No
+ * reference counterpart (the reference has no expert parallelism); with
+ * num_sources = 1 these equal the entry points above. */
+int mirai_moe_gateup_swiglu_src_bf16(const void* x, const int32_t* offsets, int32_t num_sources,
+                                     int32_t num_experts, int64_t num_rows, int32_t hidden, int32_t inter,
+                                     const void* w1, const void* w3, void* h, void* gate_up,
+                                     mirai_stream_t stream);
+int mirai_moe_gateup_swiglu_src_nf4(const void* x, const int32_t* offsets, int32_t num_sources,
+                                    int32_t num_experts, int64_t num_rows, int32_t hidden, int32_t inter,
+                                    const mirai_nf4_weight* w1, const mirai_nf4_weight* w3, void* h,
+                                    void* gate_up, mirai_stream_t stream);
+int mirai_moe_gateup_swiglu_src_int8(const void* x, const int32_t* offsets, int32_t num_sources,
+                                     int32_t num_experts, int64_t num_rows, int32_t hidden, int32_t inter,
+                                     const mirai_int8_weight* w1, const mirai_int8_weight* w3, void* h,
+                                     void* gate_up, mirai_stream_t stream);
+int mirai_moe_down_src_bf16(const void* h, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                            int64_t num_rows, int32_t inter, int32_t hidden, const void* w2, void* y,
+                            mirai_stream_t stream);
+int mirai_moe_down_src_nf4(const void* h, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                           int64_t num_rows, int32_t inter, int32_t hidden, const mirai_nf4_weight* w2, void* y,
+                           mirai_stream_t stream);
+int mirai_moe_down_src_int8(const void* h, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                            int64_t num_rows, int32_t inter, int32_t hidden, const mirai_int8_weight* w2,
+                            void* y, mirai_stream_t stream);
 
 /* ------------------------------------------------------------- a8: combine
  * out[t, :] = sum_j top_weights[t, j] * y[inverse_order[t*k + j], :], summed in

@@ -54,6 +54,7 @@ SIGNATURES = {
     "mirai_b200_version": (ctypes.c_int, []),
     "mirai_b200_device_status": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "mirai_route_topk": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_i32, c_f32, c_vp, c_vp, c_vp]),
+    "mirai_b200_set_gemm_sm_limit": (ctypes.c_int, [c_i32]),
     "mirai_dispatch_plan_workspace_bytes": (c_size, [c_i64, c_i32, c_i32]),
     "mirai_dispatch_plan_static_scratch_bytes": (c_size, []),
     "mirai_dispatch_plan_static": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
@@ -74,6 +75,19 @@ SIGNATURES = {
                                           c_vp, c_vp]),
     "mirai_moe_down_int8": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, ctypes.POINTER(Int8Weight),
                                            c_vp, c_vp]),
+    "mirai_moe_gateup_swiglu_src_bf16": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_i32, c_vp,
+                                                        c_vp, c_vp, c_vp, c_vp]),
+    "mirai_moe_gateup_swiglu_src_nf4": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_i32,
+                                                       ctypes.POINTER(Nf4Weight), ctypes.POINTER(Nf4Weight), c_vp,
+                                                       c_vp, c_vp]),
+    "mirai_moe_gateup_swiglu_src_int8": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_i32,
+                                                        ctypes.POINTER(Int8Weight), ctypes.POINTER(Int8Weight), c_vp,
+                                                        c_vp, c_vp]),
+    "mirai_moe_down_src_bf16": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    "mirai_moe_down_src_nf4": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_i32,
+                                              ctypes.POINTER(Nf4Weight), c_vp, c_vp]),
+    "mirai_moe_down_src_int8": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_i32,
+                                               ctypes.POINTER(Int8Weight), c_vp, c_vp]),
     "mirai_moe_combine": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_i32, c_vp]),
     "mirai_moe_combine_backward": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp]),
     "mirai_moe_down_dx_bf16": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp]),

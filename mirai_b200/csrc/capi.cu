@@ -26,6 +26,12 @@ int check_launch(const char* what) {
   return MIRAI_OK;
 }
 
+// Upper bound on the SMs the persistent GEMMs occupy (0 = all).  Read at each
+// launch; set by mirai_b200_set_gemm_sm_limit.
+static int g_gemm_sm_limit = 0;
+
+int gemm_sm_limit() { return g_gemm_sm_limit; }
+
 int sm_count() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -84,6 +90,13 @@ extern "C" {
 const char* mirai_b200_last_error(void) { return mirai::t_last_error; }
 
 int mirai_b200_version(void) { return 100; }
+
+int mirai_b200_set_gemm_sm_limit(int32_t max_sms) {
+  if (max_sms < 0 || max_sms == 1)
+    return mirai::set_error(MIRAI_ERR_INVALID_ARG, "set_gemm_sm_limit: %d (use 0 for no limit, or >= 2)", max_sms);
+  mirai::g_gemm_sm_limit = max_sms;
+  return MIRAI_OK;
+}
 
 int mirai_b200_device_status(mirai_stream_t stream, int* code, int* info) {
   if (!code || !info) return mirai::set_error(MIRAI_ERR_INVALID_ARG, "device_status: null output pointer");

@@ -17,6 +17,7 @@ namespace mirai {
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
 int sm_count();
+int gemm_sm_limit();
 
 // Device-side error word.  Kernels never trap: a bounded wait that gives up,
 // or a bounds check that fails, records a code here and the kernel returns.

@@ -87,7 +87,7 @@ template <int WF, bool PAIR> struct Cfg {
   static constexpr int GROUP_WARPS = QUANT ? B_ROWS / 32 : 0;            // dequant warps per group
   static constexpr int STAGES = WF == W_BF16 ? (PAIR ? 6 : 4) : (PAIR ? 4 : 3);
   // raw-code ring: its own producer warp runs ahead of the operand ring
-  static constexpr int RAW_STAGES = WF == W_BF16 ? 1 : (PAIR ? 8 : (WF == W_NF4 ? 6 : 3));
+  static constexpr int RAW_STAGES = WF == W_BF16 ? 1 : (PAIR ? (WF == W_NF4 ? 8 : 6) : (WF == W_NF4 ? 4 : 2));
   static constexpr int EPI_WARPS = epi_warps(WF);
   static constexpr int THREADS = 64 + 32 * EPI_WARPS + (WF == W_BF16 ? 0 : kDeqThreads + 32);
   static_assert(!QUANT || (kDeqThreads % B_ROWS == 0 && STAGES % KG == 0 && RAW_STAGES % KG == 0),
@@ -121,10 +121,13 @@ struct Params {
   QKey q[2];               // quantised keys (index 1 used by GATEUP / DXGATEUP)
   int nbs_shift;           // log2(nested_blocksize)
   int has_ext;             // 1: one extra bf16 k-block (the LoRA rank block) from tmap_xa / tmap_xb
+  int nsrc;                // row sources: segment s*(E/nsrc) + w holds source s's rows for weight expert w
 };
 
+// Control block in shared memory.  16-byte aligned size: the dequantiser
+// scratch that follows it is written with 16-byte vector stores.
 template <int WF, bool PAIR>
-struct Smem {
+struct alignas(16) Smem {
   uint64_t full[Cfg<WF, PAIR>::STAGES];
   uint64_t empty[Cfg<WF, PAIR>::STAGES];
   uint64_t raw_full[Cfg<WF, PAIR>::RAW_STAGES];
@@ -133,13 +136,14 @@ struct Smem {
   uint64_t tempty[2];
   uint32_t tmem_base;
   int abort_flag;
-  int row_start[kMaxExperts + 1];
+  int row_start[kMaxExperts + 1];  // per segment, in tile order
+  int seg_rows[kMaxExperts + 1];
   int tile_prefix[kMaxExperts + 1];
 };
 
 // Dequantiser scratch: per-tile absmax codes (or INT8 row scales), the
 // expert's nested absmax, and the code tables, per key.
-struct DeqSmem {
+struct alignas(16) DeqSmem {
   uint8_t absq[16384];
   float nested[2][kMaxNested];
   float ncode[2][256];
@@ -149,14 +153,19 @@ struct DeqSmem {
 template <int WF, bool PAIR>
 constexpr size_t smem_bytes() {
   using C = Cfg<WF, PAIR>;
+  static_assert(sizeof(Smem<WF, PAIR>) % 16 == 0 && (C::RAW_STAGES * C::RAW_BYTES) % 16 == 0,
+                "the dequantiser scratch must start 16-byte aligned");
   return 1024 + C::STAGES * (C::A_STAGE + C::B_BYTES) + (WF == W_BF16 ? 0 : C::RAW_STAGES * C::RAW_BYTES) +
          sizeof(Smem<WF, PAIR>) +
          (WF == W_BF16 ? 0 : sizeof(DeqSmem));
 }
 
+// Tile t -> segment j (in tile order), weight expert e, row block m, column
+// block n.  Segments are visited weight-expert-major (all sources of expert 0,
+// then of expert 1, ...) so that concurrent tiles share one expert's weights.
 template <int WF, bool PAIR>
-__device__ __forceinline__ void decode_tile(int t, const Smem<WF, PAIR>& sm, int E, int n_tiles, int& e, int& m,
-                                            int& n) {
+__device__ __forceinline__ void decode_tile(int t, const Smem<WF, PAIR>& sm, int E, int nsrc, int n_tiles, int& j,
+                                            int& e, int& m, int& n) {
   const int mt = t / n_tiles;
   n = t - mt * n_tiles;
   int lo = 0, hi = E;
@@ -165,8 +174,9 @@ __device__ __forceinline__ void decode_tile(int t, const Smem<WF, PAIR>& sm, int
     if (sm.tile_prefix[mid] <= mt) lo = mid;
     else hi = mid;
   }
-  e = lo;
-  m = mt - sm.tile_prefix[e];
+  j = lo;
+  e = lo / nsrc;
+  m = mt - sm.tile_prefix[lo];
 }
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -289,19 +299,24 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   // the leader's `full` barriers as seen from this CTA (stage s at + 8 s)
   const uint32_t full_leader0 = leader_addr(&sm.full[0]);
 
-  // ---- segment table: row_start[e] and exclusive prefix of TILE_M-row blocks
+  // ---- segment table, in tile order j: row_start / seg_rows and the exclusive
+  // prefix of TILE_M-row blocks.  Tile-order segment j is memory segment
+  // g = (j % nsrc) * (E / nsrc) + j / nsrc (offsets are inclusive ends in memory order).
   if (warp == 0) {
+    const int nsrc = p.nsrc, wexp = E / nsrc;
     int carry = 0;
-    for (int e0 = 0; e0 < E; e0 += 32) {
-      const int e = e0 + lane;
+    for (int j0 = 0; j0 < E; j0 += 32) {
+      const int j = j0 + lane;
       int cnt = 0;
-      if (e < E) {
-        const int64_t end = p.offsets[e];
-        const int64_t beg = e > 0 ? p.offsets[e - 1] : 0;
+      if (j < E) {
+        const int g = (j % nsrc) * wexp + j / nsrc;
+        const int64_t end = p.offsets[g];
+        const int64_t beg = g > 0 ? p.offsets[g - 1] : 0;
         const int64_t endc = end < p.S ? end : p.S;
         cnt = endc > beg ? (int)((endc - beg + TILE_M - 1) / TILE_M) : 0;
         if (end < beg || end > p.S) device_fail(MIRAI_ERR_DEVICE_BOUNDS, 600 + MODE);
-        sm.row_start[e] = (int)beg;
+        sm.row_start[j] = (int)beg;
+        sm.seg_rows[j] = endc > beg ? (int)(endc - beg) : 0;
       }
       int incl = cnt;
 #pragma unroll
@@ -309,13 +324,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         const int v = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += v;
       }
-      if (e < E) sm.tile_prefix[e] = carry + incl - cnt;
+      if (j < E) sm.tile_prefix[j] = carry + incl - cnt;
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (lane == 0) {
-      sm.tile_prefix[E] = carry;
-      sm.row_start[E] = (int)(E > 0 ? p.offsets[E - 1] : 0);
-    }
+    if (lane == 0) sm.tile_prefix[E] = carry;
   }
   if (warp == 1) {
     if (lane == 0) {
@@ -377,11 +389,11 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int t = unit; t < total_tiles && !*abort_flag; t += num_units) {
-        int e, m, n;
-        decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
-        const int row0 = sm.row_start[e] + m * TILE_M + (int)rank * BM;
-        // sub-tiles holding rows of this expert (the first always does)
-        const int seg_rows = sm.row_start[e + 1] - sm.row_start[e];
+        int j, e, m, n;
+        decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
+        const int row0 = sm.row_start[j] + m * TILE_M + (int)rank * BM;
+        // sub-tiles holding rows of this segment (the first always does)
+        const int seg_rows = sm.seg_rows[j];
         const int n_live = (RT == 2 && m * TILE_M + SUB_M >= seg_rows) ? 1 : RT;
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&sm.empty[stage], phase ^ 1, 10)) {
@@ -468,9 +480,9 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           break;
         }
         tc_fence_after();
-        int e, m, n;
-        decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
-        const int seg_rows = sm.row_start[e + 1] - sm.row_start[e];
+        int j, e, m, n;
+        decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
+        const int seg_rows = sm.seg_rows[j];
         const int n_live = (RT == 2 && m * TILE_M + SUB_M >= seg_rows) ? 1 : RT;
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
@@ -523,14 +535,14 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         break;
       }
       tc_fence_after();
-      int e, m, n;
-      decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
-      const int64_t seg_rows = (int64_t)sm.row_start[e + 1] - sm.row_start[e];
+      int j, e, m, n;
+      decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
+      const int64_t seg_rows = sm.seg_rows[j];
       for (int sub = 0; sub < RT; ++sub) {
       if ((int64_t)m * TILE_M + sub * SUB_M >= seg_rows) break;  // no rows in this sub-tile (warp-uniform)
       const int r = sub * SUB_M + (int)rank * BM + q * 32 + lane;  // row inside the tile
       const bool valid = (int64_t)m * TILE_M + r < seg_rows;
-      const int64_t grow = (int64_t)sm.row_start[e] + (int64_t)m * TILE_M + r;
+      const int64_t grow = (int64_t)sm.row_start[j] + (int64_t)m * TILE_M + r;
       const uint32_t tb = tmem_base + acc * BN + sub * TN + ((uint32_t)(q * 32) << 16);
       if (MODE == GATEUP) {
         const int col0 = n * (TN / 2);
@@ -652,8 +664,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       uint32_t rphase = 0;
       constexpr int RB = C::ROW_BYTES;
       for (int t = unit; t < total_tiles && !*abort_flag; t += num_units) {
-        int e, m, n;
-        decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
+        int j, e, m, n;
+        decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&sm.raw_empty[rstage], rphase ^ 1, 11)) {
             *abort_flag = 1;
@@ -711,8 +723,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     int gk = 0;  // position in this CTA's k-block sequence over all its tiles
     bool failed = false;
     for (int t = unit; t < total_tiles && !failed && !*abort_flag; t += num_units) {
-      int e, m, n;
-      decode_tile<WF, PAIR>(t, sm, E, p.n_tiles, e, m, n);
+      int j, e, m, n;
+      decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
       // key of this thread's rows (K-major) / of the k-block (MN)
       const int row_key = MN ? 0 : (MCfg<MODE>::TWO_KEYS ? kblk : 0);
       const int wrow_base = MN ? 0 : kmajor_row<MODE, TN>(p, e, n, kblk) - e * p.out_rows;  // first weight row
@@ -881,7 +893,8 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
   q.n_tiles = MODE == GATEUP ? q.N / (C::TN / 2) : (q.N + C::TN - 1) / C::TN;
   const int64_t max_tiles = ((q.S + C::TILE_M - 1) / C::TILE_M + q.E) * (int64_t)q.n_tiles;
   static const char* names[4] = {"gateup_swiglu", "down", "down_dx", "gateup_dx"};
-  const int sms = sm_count();
+  const int limit = gemm_sm_limit();
+  const int sms = (limit > 0 && limit < sm_count()) ? limit : sm_count();
   if (!PAIR) {
     const int grid = (int)(max_tiles < sms ? max_tiles : sms);
     kern<<<grid, C::THREADS, smem, stream>>>(ta, tb0, tb1, txa, txb, q);
@@ -912,7 +925,8 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
     resident_pairs = n;
     if (getenv("MIRAI_B200_DEBUG")) fprintf(stderr, "[mirai_b200] %s: %d resident CTA pairs\n", names[MODE], n);
   }
-  const int64_t units = max_tiles < resident_pairs ? max_tiles : resident_pairs;
+  int64_t units = max_tiles < resident_pairs ? max_tiles : resident_pairs;
+  if (units > sms / 2) units = sms / 2;  // the SM limit, in pairs
   cfg.gridDim = dim3((unsigned)(2 * units), 1, 1);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb0, tb1, txa, txb, q);
   if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "%s: launch failed: %s", names[MODE], cudaGetErrorString(e));
@@ -960,6 +974,7 @@ int prepare(const char* name, const void* a, const int32_t* offsets, int E, int6
   p.ldo = N;
   p.gate_up = static_cast<__nv_bfloat16*>(gate_up);
   p.nbs_shift = 8;
+  p.nsrc = 1;
   return make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, (uint64_t)K, (uint64_t)S, (uint64_t)K * 2, BK, BM,
                       CU_TENSOR_MAP_SWIZZLE_128B);
 }
@@ -1042,15 +1057,21 @@ struct RankBlock {
   const void* b;
 };
 
+// E weight experts; nsrc > 1: `offsets` has nsrc * E segments, source-major
+// (segment s*E + e = rows of source s for expert e).
 template <int MODE>
 int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t S, int K, int N, void* out,
         void* gate_up, const WeightArg& w0, const WeightArg& w1, int rows, int cols, mirai_stream_t stream,
-        const RankBlock* ext = nullptr) {
-  if (S == 0 && E > 0) return MIRAI_OK;
+        const RankBlock* ext = nullptr, int nsrc = 1) {
+  if (nsrc <= 0 || E <= 0 || (int64_t)nsrc * E > kMaxExperts)
+    return set_error(MIRAI_ERR_INVALID_ARG, "%s: %d sources x %d experts outside 1..%d segments", name, nsrc, E,
+                     kMaxExperts);
+  if (S == 0) return MIRAI_OK;
   Params p;
   CUtensorMap ta, t0, t1, txa, txb;
   const int box_rows = kmajor_box_rows(w0.fmt);
-  int rc = prepare<MODE>(name, a, offsets, E, S, K, N, out, gate_up, p, ta);
+  int rc = prepare<MODE>(name, a, offsets, nsrc * E, S, K, N, out, gate_up, p, ta);
+  p.nsrc = nsrc;
   if (!rc && ext) {
     if (!ext->a || !ext->b) rc = set_error(MIRAI_ERR_INVALID_ARG, "%s: null rank-block operand", name);
     if (!rc)
@@ -1123,6 +1144,46 @@ int mirai_moe_gateup_swiglu_int8(const void* x_sorted, const int32_t* offsets, i
                                  const mirai_int8_weight* w3, void* h, void* gate_up, mirai_stream_t stream) {
   return run<GATEUP>("gateup_swiglu_int8", x_sorted, offsets, num_experts, num_rows, hidden, inter, h, gate_up,
                      wi(w1), wi(w3), inter, hidden, stream);
+}
+
+// ---- forward over source-major segments (expert-parallel receive buffers).
+int mirai_moe_gateup_swiglu_src_bf16(const void* x_sorted, const int32_t* offsets, int32_t num_sources,
+                                     int32_t num_experts, int64_t num_rows, int32_t hidden, int32_t inter,
+                                     const void* w1, const void* w3, void* h, void* gate_up, mirai_stream_t stream) {
+  return run<GATEUP>("gateup_swiglu_src_bf16", x_sorted, offsets, num_experts, num_rows, hidden, inter, h, gate_up,
+                     wb(w1), wb(w3), inter, hidden, stream, nullptr, num_sources);
+}
+int mirai_moe_gateup_swiglu_src_nf4(const void* x_sorted, const int32_t* offsets, int32_t num_sources,
+                                    int32_t num_experts, int64_t num_rows, int32_t hidden, int32_t inter,
+                                    const mirai_nf4_weight* w1, const mirai_nf4_weight* w3, void* h, void* gate_up,
+                                    mirai_stream_t stream) {
+  return run<GATEUP>("gateup_swiglu_src_nf4", x_sorted, offsets, num_experts, num_rows, hidden, inter, h, gate_up,
+                     wn(w1), wn(w3), inter, hidden, stream, nullptr, num_sources);
+}
+int mirai_moe_gateup_swiglu_src_int8(const void* x_sorted, const int32_t* offsets, int32_t num_sources,
+                                     int32_t num_experts, int64_t num_rows, int32_t hidden, int32_t inter,
+                                     const mirai_int8_weight* w1, const mirai_int8_weight* w3, void* h,
+                                     void* gate_up, mirai_stream_t stream) {
+  return run<GATEUP>("gateup_swiglu_src_int8", x_sorted, offsets, num_experts, num_rows, hidden, inter, h, gate_up,
+                     wi(w1), wi(w3), inter, hidden, stream, nullptr, num_sources);
+}
+int mirai_moe_down_src_bf16(const void* h, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                            int64_t num_rows, int32_t inter, int32_t hidden, const void* w2, void* y,
+                            mirai_stream_t stream) {
+  return run<DOWN>("down_src_bf16", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, wb(w2), wb(w2),
+                   hidden, inter, stream, nullptr, num_sources);
+}
+int mirai_moe_down_src_nf4(const void* h, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                           int64_t num_rows, int32_t inter, int32_t hidden, const mirai_nf4_weight* w2, void* y,
+                           mirai_stream_t stream) {
+  return run<DOWN>("down_src_nf4", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, wn(w2), wn(w2),
+                   hidden, inter, stream, nullptr, num_sources);
+}
+int mirai_moe_down_src_int8(const void* h, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                            int64_t num_rows, int32_t inter, int32_t hidden, const mirai_int8_weight* w2, void* y,
+                            mirai_stream_t stream) {
+  return run<DOWN>("down_src_int8", h, offsets, num_experts, num_rows, inter, hidden, y, nullptr, wi(w2), wi(w2),
+                   hidden, inter, stream, nullptr, num_sources);
 }
 
 // ---- forward: down.  B = W2 [E, H, I]: rows H, cols I.

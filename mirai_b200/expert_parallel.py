@@ -4,25 +4,27 @@ The layer shards by expert: rank r of G owns the contiguous experts
 [r*E/G, (r+1)*E/G) and routes its own shard of the tokens.  One layer is
 
   route (a1) -> global dispatch plan (a2) -> permute (a3)        on the token owner
-  all-to-all: rows (and their local expert ids) to the expert owners
-  local plan -> permute -> gate/up + down grouped GEMMs          on the expert owner
-  un-permute -> all-to-all back -> weighted combine (a8)          on the token owner
+  all-to-all: rows to the expert owners
+  gate/up + down grouped GEMMs over source-major segments         on the expert owner
+  all-to-all back -> weighted combine (a8)                        on the token owner
 
 Because experts are contiguous per rank, the rows of the global plan (sorted
-by expert id) are already grouped by destination rank, so the send buffer is
-the permuted activation itself.  The received rows arrive source-rank-major
-and, within a source, in expert order; the local plan re-sorts them stably by
-local expert, which reproduces the single-GPU row order of every expert
-segment when tokens are sharded contiguously by rank, so the result equals
-the single-GPU layer.  The reference runs MoE on one GPU (it has no expert
-parallelism); the exchange is this package's.  (Receiving each (rank, expert)
-block straight into an expert-major layout with grouped NCCL send/recv was
-measured slower on B200 than one all_to_all_single plus the local re-sort:
-18.8 vs 25.7 M tokens/s for c2 on 2 GPUs.)
+by expert id) are already grouped by destination rank and, inside, by
+expert, so the send buffer is the permuted activation itself.  The received
+rows arrive source-major, each source's rows in expert order; the grouped
+GEMMs take those G x E/G (source, expert) segments as they are (weight =
+expert, tiles visited expert-major), so the owner neither re-sorts nor
+restores the order, and its output goes back through the reverse all-to-all
+in the layout the token owner sent.  Per row the products are those of the
+single-GPU layer, so the result is identical to it.  The reference runs MoE
+on one GPU (it has no expert parallelism); the exchange is this package's.
+(Receiving each (rank, expert) block straight into an expert-major layout
+with grouped NCCL send/recv was measured slower on B200 than one
+all_to_all_single: 18.8 vs 25.7 M tokens/s for c2 on 2 GPUs.)
 
 Split sizes must be known on the host for NCCL's all-to-all, so each layer
-reads G counts back once (the reference's own host sync per layer,
-experts.py:2382, is of the same kind).
+reads the [G, chunks, E/G] count matrices back once (the reference's own host
+sync per layer, experts.py:2382, is of the same kind).
 
 `StepOps` names the per-rank steps.  The product path uses `CudaStepOps`
 (the sm_100a kernels); tests of the exchange logic on CPU ranks pass their own.
@@ -64,7 +66,8 @@ class StepOps(Protocol):
     def route(self, logits: torch.Tensor, top_k: int) -> tuple[torch.Tensor, torch.Tensor]: ...
     def plan(self, top_indices: torch.Tensor, num_experts: int) -> Any: ...
     def permute(self, x: torch.Tensor, sorted_token_indices: torch.Tensor) -> torch.Tensor: ...
-    def experts(self, x_sorted: torch.Tensor, offsets: torch.Tensor, weights: Any, inter: int) -> torch.Tensor: ...
+    def experts(self, x_sorted: torch.Tensor, offsets: torch.Tensor, weights: Any, inter: int,
+                sources: int = 1) -> torch.Tensor: ...
     def combine(self, y_sorted: torch.Tensor, inverse_order: torch.Tensor, top_weights: torch.Tensor | None,
                 top_k: int, out_dtype: torch.dtype) -> torch.Tensor: ...
 
@@ -85,10 +88,10 @@ class CudaStepOps:
     def permute(self, x, sorted_token_indices):
         return self.ops.permute_rows(x, sorted_token_indices)
 
-    def experts(self, x_sorted, offsets, weights, inter):
+    def experts(self, x_sorted, offsets, weights, inter, sources=1):
         w1, w3, w2 = weights
-        h = self.ops.gateup_swiglu(x_sorted, offsets, w1, w3, inter=inter)
-        return self.ops.down(h, offsets, w2, hidden=x_sorted.shape[1])
+        h = self.ops.gateup_swiglu(x_sorted, offsets, w1, w3, inter=inter, sources=sources)
+        return self.ops.down(h, offsets, w2, hidden=x_sorted.shape[1], sources=sources)
 
     def combine(self, y_sorted, inverse_order, top_weights, top_k, out_dtype):
         return self.ops.combine(y_sorted, inverse_order, top_weights, out_dtype=out_dtype, top_k=top_k)
@@ -99,52 +102,126 @@ def _a2a(out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits:
 
 
 def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: Any, *, shard: ExpertShard,
-                   top_k: int, inter: int, group=None, ops: StepOps | None = None) -> torch.Tensor:
+                   top_k: int, inter: int, group=None, ops: StepOps | None = None, chunks: int = 1,
+                   comm_stream: torch.cuda.Stream | None = None) -> torch.Tensor:
     """One expert-parallel routed FFN layer for this rank's tokens.
 
     tokens [T_r, H] bf16 and router logits [T_r, E] fp32 are this rank's token
     shard; ``local_weights`` = (w1, w3, w2) of this rank's E/G experts, in any
     format the GEMMs take.  Returns [T_r, H] in the tokens' dtype.  Every rank
-    must call it (the exchange is collective), with or without tokens."""
+    must call it (the exchange is collective) with the same ``chunks``, with or
+    without tokens.
+
+    ``chunks`` > 1 splits the tokens into that many contiguous chunks whose
+    exchanges run on ``comm_stream`` while the other chunks' GEMMs run on the
+    current stream (chunk i's rows travel while chunk i-1 computes, and its
+    results return while chunk i+1 computes).  The result is the same as with
+    one chunk.  For the overlap to happen the GEMMs must leave SMs free for the
+    communication kernels (``ops.set_gemm_sm_limit``)."""
     ops = ops or CudaStepOps()
     G, E, El = shard.world, shard.num_experts, shard.local
     T, H = tokens.shape
     dev = tokens.device
-    idx, tw = ops.route(logits, top_k)
-    plan = ops.plan(idx, E)
-    xs = ops.permute(tokens, plan.sorted_token_indices)
     if G == 1:  # one rank owns every expert: no exchange
+        idx, tw = ops.route(logits, top_k)
+        plan = ops.plan(idx, E)
+        xs = ops.permute(tokens, plan.sorted_token_indices)
         y = ops.experts(xs, plan.offsets, local_weights, inter)
         return ops.combine(y, plan.inverse_order, tw, top_k, tokens.dtype)
-    # rows per destination rank (experts are contiguous per rank) and, per row,
-    # the expert's index inside its owner's block
-    send_counts = plan.counts.view(G, El).sum(1)
-    recv_counts = torch.empty_like(send_counts)
-    dist.all_to_all_single(recv_counts, send_counts, group=group)
-    counts = torch.cat([send_counts, recv_counts]).tolist()  # the one host read per layer
-    sc, rc = counts[:G], counts[G:]
-    # expert of sorted row s = the segment containing s (offsets are inclusive ends)
-    S = xs.shape[0]
-    rows = torch.arange(S, device=dev, dtype=plan.offsets.dtype)
-    local_ids = (torch.searchsorted(plan.offsets, rows, right=True) % El).to(torch.int64)
-    R = sum(rc)
-    x_recv = torch.empty((R, H), dtype=xs.dtype, device=dev)
-    e_recv = torch.empty((R,), dtype=torch.int64, device=dev)
-    _a2a(x_recv, xs, rc, sc, group)
-    _a2a(e_recv, local_ids, rc, sc, group)
-    # expert owner: group the received rows by local expert, run the experts, restore the order
-    if R > 0:
-        lplan = ops.plan(e_recv.view(R, 1), El)
-        xl = ops.permute(x_recv, lplan.sorted_token_indices)
-        yl = ops.experts(xl, lplan.offsets, local_weights, inter)
-        y_recv = ops.combine(yl, lplan.inverse_order, None, 1, yl.dtype)
-    else:
-        y_recv = torch.empty((0, H), dtype=xs.dtype, device=dev)
-    y_back = torch.empty_like(xs)
-    _a2a(y_back, y_recv, sc, rc, group)
-    if T == 0:
-        return torch.empty((0, H), dtype=tokens.dtype, device=dev)
-    return ops.combine(y_back, plan.inverse_order, tw, top_k, tokens.dtype)
+    C = max(1, int(chunks))
+    bounds = [((T * c) // C, (T * (c + 1)) // C) for c in range(C)]
+    # ---- per chunk, on the current stream: route, plan, permute
+    prep = []
+    for b, e in bounds:
+        idx, tw = ops.route(logits[b:e], top_k)
+        plan = ops.plan(idx, E)
+        prep.append((tw, plan, ops.permute(tokens[b:e], plan.sorted_token_indices)))
+    # rows per (destination rank, chunk, local expert): experts are contiguous per
+    # rank, so chunk c's permuted rows for rank d are one run ordered by expert.
+    # One exchange of the count matrices and one host read for the whole layer.
+    send_mat = torch.stack([p[1].counts.view(G, El) for p in prep], dim=1).contiguous()  # [dest, chunk, expert]
+    recv_mat = torch.empty_like(send_mat)                                                 # [source, chunk, expert]
+    dist.all_to_all_single(recv_mat, send_mat, group=group)
+    flat = torch.cat([send_mat.reshape(-1), recv_mat.reshape(-1)]).tolist()
+    n = G * C * El
+    sm_ = [[flat[(d * C + c) * El:(d * C + c + 1) * El] for d in range(G)] for c in range(C)]
+    rm_ = [[flat[n + (s_ * C + c) * El:n + (s_ * C + c + 1) * El] for s_ in range(G)] for c in range(C)]
+    sc = [[sum(sm_[c][d]) for d in range(G)] for c in range(C)]
+    rc = [[sum(rm_[c][s_]) for s_ in range(G)] for c in range(C)]
+    # received rows of chunk c: source-major, each source's rows in expert order;
+    # the GEMMs take these G * El segments as they are (ends = running sum)
+    seg_ends = []
+    for c in range(C):
+        run, ends = 0, []
+        for s_ in range(G):
+            for e in range(El):
+                run += rm_[c][s_][e]
+                ends.append(run)
+        seg_ends.append(ends)
+    offs_dev = torch.tensor(seg_ends, dtype=torch.int32).to(dev, non_blocking=True) if tokens.is_cuda else \
+        torch.tensor(seg_ends, dtype=torch.int32)
+
+    comp = torch.cuda.current_stream(dev) if tokens.is_cuda else None
+    comm = comm_stream if (C > 1 and tokens.is_cuda) else None
+
+    def keep(t, stream):
+        # a tensor used on a stream other than its own is not reused before that stream is done with it
+        if stream is not None and t.is_cuda:
+            t.record_stream(stream)
+        return t
+
+    def on_comm(fn, after):
+        comm.wait_event(after)
+        with torch.cuda.stream(comm):
+            out = fn()
+            ev = torch.cuda.Event()
+            ev.record(comm)
+        return out, ev
+
+    def mark():
+        ev = torch.cuda.Event()
+        ev.record(comp)
+        return ev
+
+    def dispatch(c):
+        xs = keep(prep[c][2], comm)
+        x_recv = keep(torch.empty((sum(rc[c]), H), dtype=xs.dtype, device=dev), comp if comm is not None else None)
+        _a2a(x_recv, xs, rc[c], sc[c], group)
+        return x_recv
+
+    def compute(c, x_recv):
+        if x_recv.shape[0] == 0:
+            return torch.empty((0, H), dtype=x_recv.dtype, device=dev)
+        return ops.experts(x_recv, offs_dev[c], local_weights, inter, sources=G)
+
+    def give_back(c, y_recv):
+        keep(y_recv, comm)
+        y_back = keep(torch.empty_like(prep[c][2]), comp if comm is not None else None)
+        _a2a(y_back, y_recv, sc[c], rc[c], group)
+        return y_back
+
+    out = torch.empty((T, H), dtype=tokens.dtype, device=dev)
+    if comm is None:
+        for c, (b, e) in enumerate(bounds):
+            y_back = give_back(c, compute(c, dispatch(c)))
+            if e > b:
+                out[b:e] = ops.combine(y_back, prep[c][1].inverse_order, prep[c][0], top_k, tokens.dtype)
+        return out
+    # pipelined: dispatch c+1 and return c-1 on `comm` overlap compute c on the current stream
+    ready = mark()
+    sent = [on_comm(lambda c=c: dispatch(c), ready) for c in range(C)]
+    backs = []
+    for c in range(C):
+        x_recv, ev = sent[c]
+        comp.wait_event(ev)
+        y_recv = compute(c, x_recv)
+        backs.append(on_comm(lambda c=c, y=y_recv: give_back(c, y), mark()))
+    for c, (b, e) in enumerate(bounds):
+        y_back, ev = backs[c]
+        comp.wait_event(ev)
+        if e > b:
+            out[b:e] = ops.combine(y_back, prep[c][1].inverse_order, prep[c][0], top_k, tokens.dtype)
+    return out
 
 
 def shard_tokens(num_tokens: int, world: int, rank: int) -> tuple[int, int]:

@@ -44,6 +44,12 @@ def check_device() -> None:
         raise _lib.MiraiError(code, f"raised on the device at site {info}")
 
 
+def set_gemm_sm_limit(max_sms: int) -> None:
+    """Cap the SMs the persistent grouped GEMMs occupy (0 = all), process-wide,
+    so that communication kernels on another stream can run beside them."""
+    _lib.call("mirai_b200_set_gemm_sm_limit", int(max_sms))
+
+
 # ----------------------------------------------------------------------------- a1
 
 def route_topk(logits: torch.Tensor, top_k: int, *, score_func: str = "softmax",
@@ -205,16 +211,25 @@ def _as_weight(w):
 # ----------------------------------------------------------------------------- a6 / a7
 
 def gateup_swiglu(x_sorted: torch.Tensor, offsets: torch.Tensor, w1, w3, *, inter: int,
-                  save_gate_up: bool = False, out: torch.Tensor | None = None):
+                  save_gate_up: bool = False, out: torch.Tensor | None = None, sources: int = 1):
     """h = silu(x W1^T) * (x W3^T) per expert segment.  ``w1``/``w3`` are bf16
-    tensors [E, I, H], or ``Nf4Weight`` / ``Int8Weight`` descriptors."""
+    tensors [E, I, H], or ``Nf4Weight`` / ``Int8Weight`` descriptors.
+    ``sources`` > 1: ``offsets`` ends ``sources * E`` source-major segments
+    (segment s*E + e = source s's rows for expert e)."""
     w1, w3 = _as_weight(w1), _as_weight(w3)
     x_sorted = _cuda(x_sorted, "x_sorted", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
     S, H = x_sorted.shape
-    E = offsets.numel()
     h = out if out is not None else torch.empty((S, inter), dtype=torch.bfloat16, device=x_sorted.device)
     gu = torch.empty((S, 2 * inter), dtype=torch.bfloat16, device=x_sorted.device) if save_gate_up else None
+    if sources > 1:
+        if save_gate_up or offsets.numel() % sources:
+            raise ValueError("source-major segments: forward only, offsets a multiple of sources")
+        E = offsets.numel() // sources
+        _lib.call(f"mirai_moe_gateup_swiglu_src_{_fmt_suffix(w1)}", _ptr(x_sorted), _ptr(offsets), sources, E, S, H,
+                  inter, _wptr(w1), _wptr(w3), _ptr(h), None, _stream())
+        return h
+    E = offsets.numel()
     if isinstance(w1, torch.Tensor):
         w1 = _cuda(w1, "w1", torch.bfloat16)
         w3 = _cuda(w3, "w3", torch.bfloat16)
@@ -232,15 +247,22 @@ def gateup_swiglu(x_sorted: torch.Tensor, offsets: torch.Tensor, w1, w3, *, inte
 
 
 def down(h: torch.Tensor, offsets: torch.Tensor, w2, *, hidden: int, out: torch.Tensor | None = None,
-         lora: "DownLoRA | None" = None, rank_a: torch.Tensor | None = None):
+         lora: "DownLoRA | None" = None, rank_a: torch.Tensor | None = None, sources: int = 1):
     """y = h W2^T per expert segment (+ the fused LoRA rank block when ``lora``;
-    ``rank_a`` is its [S, 64] projection of h when the caller already has it)."""
+    ``rank_a`` is its [S, 64] projection of h when the caller already has it).
+    ``sources`` > 1: source-major segments as in ``gateup_swiglu``."""
     w2 = _as_weight(w2)
     h = _cuda(h, "h", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
     S, I = h.shape
-    E = offsets.numel()
     y = out if out is not None else torch.empty((S, hidden), dtype=torch.bfloat16, device=h.device)
+    if sources > 1:
+        if lora is not None or offsets.numel() % sources:
+            raise ValueError("source-major segments: no adapter, offsets a multiple of sources")
+        _lib.call(f"mirai_moe_down_src_{_fmt_suffix(w2)}", _ptr(h), _ptr(offsets), sources, offsets.numel() // sources,
+                  S, I, hidden, _wptr(w2), _ptr(y), _stream())
+        return y
+    E = offsets.numel()
     if lora is None:
         _lib.call(f"mirai_moe_down_{_fmt_suffix(w2)}", _ptr(h), _ptr(offsets), E, S, I, hidden, _wptr(w2), _ptr(y),
                   _stream())

@@ -1,8 +1,9 @@
 """Expert-parallel exchange on CPU ranks (gloo, world size 2 and 4).
 
-The exchange logic of mirai_b200.expert_parallel (split sizes, the two
-all-to-alls, local re-sort by expert, the return trip and the final weighted
-combine) runs for real over torch.distributed; the per-rank steps are the
+The exchange logic of mirai_b200.expert_parallel (count matrices and split
+sizes, the all-to-all to the expert owners, the source-major segments the
+owner's GEMMs take, the return trip and the final weighted combine) runs for
+real over torch.distributed; the per-rank steps are the
 oracle's (the CUDA kernels need a GPU).  The concatenated per-rank outputs
 must equal the single-process oracle layer, and ranks without tokens or
 experts without rows must not break the collective.
@@ -36,9 +37,20 @@ class OracleStepOps:
     def permute(self, x, sorted_token_indices):
         return torch.from_numpy(om.permute(x.numpy(), sorted_token_indices.numpy()))
 
-    def experts(self, x_sorted, offsets, weights, inter):
-        w1, w3, w2 = weights
-        return torch.from_numpy(om.expert_ffn_forward(x_sorted.numpy(), offsets.numpy(), w1, w3, w2, bf16=True))
+    def experts(self, x_sorted, offsets, weights, inter, sources=1):
+        # segment s*E + e holds source s's rows for expert e: gather each expert's
+        # rows in source order (one block per expert, as the single-process layer
+        # has them, so numpy's blocking and summation order match), run, scatter back
+        x, ends = x_sorted.numpy(), offsets.numpy().astype(np.int64)
+        E = ends.size // sources
+        starts = np.concatenate([[0], ends[:-1]])
+        order = [np.arange(starts[s_ * E + e], ends[s_ * E + e]) for e in range(E) for s_ in range(sources)]
+        perm = np.concatenate(order) if order else np.zeros(0, np.int64)
+        per_expert = np.cumsum([sum(ends[s_ * E + e] - starts[s_ * E + e] for s_ in range(sources)) for e in range(E)])
+        y = om.expert_ffn_forward(x[perm], per_expert, *weights, bf16=True)
+        out = np.empty_like(y)
+        out[perm] = y
+        return torch.from_numpy(out)
 
     def combine(self, y_sorted, inverse_order, top_weights, top_k, out_dtype):
         y = y_sorted.numpy()
@@ -65,13 +77,14 @@ def _rank_main(rank, world, port, cfg, results):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from mirai_b200.expert_parallel import ExpertShard, ep_moe_forward, shard_tokens
-        T, H, E, k, I, seed, token_split = cfg
+        T, H, E, k, I, seed, token_split, chunks = cfg
         x, logits, ws = _problem(T, H, E, k, I, seed)
         shard = ExpertShard(E, world, rank)
         b, e = token_split[rank] if token_split else shard_tokens(T, world, rank)
         lo, hi = shard.first, shard.first + shard.local
         out = ep_moe_forward(torch.from_numpy(x[b:e]), torch.from_numpy(logits[b:e]),
-                             tuple(w[lo:hi] for w in ws), shard=shard, top_k=k, inter=I, ops=OracleStepOps())
+                             tuple(w[lo:hi] for w in ws), shard=shard, top_k=k, inter=I, ops=OracleStepOps(),
+                             chunks=chunks)
         results[rank] = (b, e, out.numpy())
     finally:
         dist.destroy_process_group()
@@ -91,12 +104,14 @@ def _run(world, cfg):
 
 
 @pytest.mark.parametrize("world,cfg", [
-    (2, (96, 64, 8, 2, 128, 3, None)),
-    (4, (150, 64, 8, 3, 64, 5, None)),
-    (2, (80, 32, 4, 2, 64, 7, [(0, 0), (0, 80)])),  # rank 0 has no tokens
+    (2, (96, 64, 8, 2, 128, 3, None, 1)),
+    (4, (150, 64, 8, 3, 64, 5, None, 1)),
+    (2, (80, 32, 4, 2, 64, 7, [(0, 0), (0, 80)], 1)),  # rank 0 has no tokens
+    (2, (97, 64, 8, 2, 64, 9, None, 3)),               # three chunks per rank
+    (4, (60, 32, 8, 2, 64, 11, [(0, 40), (40, 41), (41, 41), (41, 60)], 2)),  # ragged shards and chunks
 ])
 def test_expert_parallel_matches_single_process_layer(world, cfg):
-    T, H, E, k, I, seed, _ = cfg
+    T, H, E, k, I, seed, _, _ = cfg
     res = _run(world, cfg)
     x, logits, ws = _problem(T, H, E, k, I, seed)
     idx, w = om.route_topk(logits, k)

@@ -43,7 +43,7 @@ def _rank_main(rank, world, port, cfg, results):
     try:
         from mirai_b200 import ops
         from mirai_b200.expert_parallel import ExpertShard, ep_moe_forward, shard_tokens
-        T, H, E, k, I, fmt = cfg
+        T, H, E, k, I, fmt, chunks = cfg
         g = torch.Generator(device=dev).manual_seed(11)
         x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
         logits = torch.randn(T, E, generator=g, device=dev) * 1.5
@@ -52,7 +52,12 @@ def _rank_main(rank, world, port, cfg, results):
         lo, hi = shard.first, shard.first + shard.local
         local = tuple(_quant(fmt, w[lo:hi].contiguous(), dev) for w in raw)
         b, e = shard_tokens(T, world, rank)
-        out = ep_moe_forward(x[b:e].contiguous(), logits[b:e].contiguous(), local, shard=shard, top_k=k, inter=I)
+        comm = torch.cuda.Stream() if chunks > 1 else None
+        if chunks > 1:
+            ops.set_gemm_sm_limit(torch.cuda.get_device_properties(dev).multi_processor_count - 16)
+        out = ep_moe_forward(x[b:e].contiguous(), logits[b:e].contiguous(), local, shard=shard, top_k=k, inter=I,
+                             chunks=chunks, comm_stream=comm)
+        ops.set_gemm_sm_limit(0)
         code, info = ops.device_status()
         full = tuple(_quant(fmt, w, dev) for w in raw)
         idx, tw = ops.route_topk(logits, k)
@@ -68,14 +73,16 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("fmt", ["nf4", "bf16", "int8"])
-def test_expert_parallel_equals_single_gpu_layer(fmt):
+@pytest.mark.parametrize("fmt,chunks", [("nf4", 1), ("bf16", 1), ("int8", 1), ("nf4", 3)])
+def test_expert_parallel_equals_single_gpu_layer(fmt, chunks):
+    """chunks = 3: the pipelined path, exchanges on a second stream and the GEMMs
+    capped below the SM count."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     from mirai_b200.build import build
     build()
     world = 2
-    cfg = (3000, 256, 8, 2, 384, fmt)
+    cfg = (3000, 256, 8, 2, 384, fmt, chunks)
     with mp.Manager() as mgr:
         results = mgr.dict()
         mp.start_processes(_rank_main, args=(world, _free_port(), cfg, results), nprocs=world, start_method="spawn")

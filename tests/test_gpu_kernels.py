@@ -586,3 +586,34 @@ def test_router_nan_rows_select_valid_experts():
     assert sorted(idx[0].tolist()) == list(range(k))           # all NaN: lowest ids
     assert all(e % 2 == 1 for e in idx[1].tolist())            # the numbers win over the NaNs
     assert int(plan.counts.sum()) == 6 * k
+
+
+@pytest.mark.parametrize("fmt", ["nf4", "int8", "bf16"])
+def test_source_major_segments_equal_expert_major(fmt):
+    """The GEMMs over G x E source-major segments (an expert owner's receive
+    buffer) give, row for row, exactly the results of the same rows grouped by
+    expert (the expert-parallel layer relies on it for bit-exactness)."""
+    dev = _dev()
+    from mirai_b200 import ops
+    G, E, H, I = 3, 5, 256, 384
+    rng = np.random.default_rng(21 + len(fmt))
+    counts = rng.integers(0, 300, size=(G, E))
+    counts[1, 2] = 0
+    counts[2, 4] = 513
+    R = int(counts.sum())
+    x = torch.randn(R, H).to(torch.bfloat16)
+    _, dw = _weights(fmt, rng, E, H, I, dev)
+    ends = np.cumsum(counts.reshape(-1)).astype(np.int32)
+    starts = np.concatenate([[0], ends[:-1]])
+    perm = np.concatenate([np.arange(starts[s * E + e], ends[s * E + e]) for e in range(E) for s in range(G)])
+    off_src = torch.from_numpy(ends).to(dev)
+    off_exp = torch.from_numpy(np.cumsum(counts.sum(0)).astype(np.int32)).to(dev)
+    xd = x.to(dev)
+    h_src = ops.gateup_swiglu(xd, off_src, dw[0], dw[1], inter=I, sources=G)
+    y_src = ops.down(h_src, off_src, dw[2], hidden=H, sources=G)
+    pd = torch.from_numpy(perm).to(dev)
+    h_exp = ops.gateup_swiglu(xd[pd], off_exp, dw[0], dw[1], inter=I)
+    y_exp = ops.down(h_exp, off_exp, dw[2], hidden=H)
+    _check(ops)
+    assert torch.equal(h_src[pd], h_exp)
+    assert torch.equal(y_src[pd], y_exp)
