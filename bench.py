@@ -427,7 +427,7 @@ def run_ep(args, cfg, rank, world, dev):
     import torch
     import torch.distributed as dist
     from mirai_b200 import ops
-    from mirai_b200.expert_parallel import CudaStepOps, ExpertShard, ep_moe_forward, shard_tokens
+    from mirai_b200.expert_parallel import CudaStepOps, ExpertParallelMoE, ExpertShard, ep_moe_forward, shard_tokens
 
     H, E, k, I = cfg["H"], cfg["E"], cfg["k"], cfg["I"]
     layers = cfg.get("layers", 1)
@@ -439,12 +439,20 @@ def run_ep(args, cfg, rank, world, dev):
     x, logits0, stack = make_ep_workload(cfg, dev, rank, shard, T_r)
     stepops = CudaStepOps()
     chunks = args.ep_chunks if world > 1 else 1
-    comm = torch.cuda.Stream() if chunks > 1 else None
-    if chunks > 1 and args.ep_free_sms > 0:
-        # leave SMs for NCCL's kernels so the exchanges overlap the GEMMs
-        ops.set_gemm_sm_limit(torch.cuda.get_device_properties(dev).multi_processor_count - args.ep_free_sms)
-    ep = lambda u, lg, ws: ep_moe_forward(u, lg, ws, shard=shard, top_k=k, inter=I, ops=stepops, chunks=chunks,
-                                          comm_stream=comm)
+    ipc = args.ep_transport == "ipc" and world > 1
+    free_sms = args.ep_free_sms if args.ep_free_sms is not None else (2 if ipc else 16)
+    if world > 1 and (chunks > 1 or ipc) and free_sms > 0:
+        # leave SMs for the communication kernels (NCCL's all-to-all; with ipc only the
+        # one-element arrival all-reduce) so the exchanges overlap the GEMMs
+        ops.set_gemm_sm_limit(torch.cuda.get_device_properties(dev).multi_processor_count - free_sms)
+    if ipc:
+        layer = ExpertParallelMoE(shard, top_k=k, inter=I, chunks=chunks, ops=stepops)
+        ep = layer.forward
+    else:
+        layer = None
+        comm = torch.cuda.Stream() if chunks > 1 else None
+        ep = lambda u, lg, ws: ep_moe_forward(u, lg, ws, shard=shard, top_k=k, inter=I, ops=stepops, chunks=chunks,
+                                              comm_stream=comm)
 
     def rms_norm(v):  # the block's pre-MoE norm (no learned scale): keeps the stack's activations bounded
         vf = v.float()
@@ -515,6 +523,9 @@ def run_ep(args, cfg, rank, world, dev):
         t = torch.tensor([ms, e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms = float(t[0]), float(t[1])
+    if layer is not None:
+        layer.close()
+    ops.set_gemm_sm_limit(0)
     peaks = load_peaks()
     flops_gu = 4.0 * R * H * I
     achieved = flops_gu / (gu_ms * 1e-3) / 1e12
@@ -539,11 +550,12 @@ def run_ep(args, cfg, rank, world, dev):
                         f"({T_r} on rank 0), H={H} E={E} ({shard.local} per GPU) k={k} I={I} {cfg['fmt']} experts",
             "tokens_total": T_total, "hidden": H, "experts": E, "experts_per_gpu": shard.local, "top_k": k,
             "intermediate": I, "layers": layers, "weights": cfg["fmt"],
-            "parallelism": f"ep{world}: experts sharded by contiguous blocks, tokens sharded by rank, "
-                           "NCCL all_to_all_single dispatch and return per layer"
-                           + (f"; {chunks} chunks per layer, exchanges on a second stream overlapping the "
-                              f"GEMMs (GEMMs capped at {torch.cuda.get_device_properties(dev).multi_processor_count - args.ep_free_sms} SMs)"
-                              if chunks > 1 else ""),
+            "parallelism": f"ep{world}: experts sharded by contiguous blocks, tokens sharded by rank, " + (
+                "copy-engine transfers into peer-mapped buffers (CUDA IPC over NVLink) with a one-element "
+                "NCCL all-reduce per chunk marking arrival" if ipc else "NCCL all_to_all_single dispatch and return")
+                + (f"; {chunks} chunks per layer, exchanges on a second stream overlapping the GEMMs"
+                   f" (GEMMs capped at {torch.cuda.get_device_properties(dev).multi_processor_count - free_sms} SMs)"
+                   if chunks > 1 and world > 1 else ""),
             "l2": "no flush: each layer's routed activations exceed the 126 MB L2",
         },
         "tflops": 6.0 * S_total * H * I * layers / (ms * 1e-3) / 1e12,
@@ -715,8 +727,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-chunks", type=int, default=2,
                     help="N > 1: token chunks per layer whose exchanges overlap the other chunks' GEMMs")
-    ap.add_argument("--ep-free-sms", type=int, default=16,
-                    help="N > 1 with chunks: SMs the GEMMs leave free for the communication kernels")
+    ap.add_argument("--ep-free-sms", type=int, default=None,
+                    help="N > 1: SMs the GEMMs leave free for communication kernels (default 2 ipc, 16 nccl)")
+    ap.add_argument("--ep-transport", default="ipc", choices=["ipc", "nccl"],
+                    help="N > 1: copy-engine transfers into peer-mapped buffers, or NCCL all_to_all_single")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

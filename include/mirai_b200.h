@@ -91,6 +91,19 @@ int mirai_b200_device_status(mirai_stream_t stream, int* code, int* info);
  * No reference counterpart: the reference has no expert parallelism. */
 int mirai_b200_set_gemm_sm_limit(int32_t max_sms);
 
+/* Peer buffers for the expert-parallel exchange (one process per GPU).  No
+ * reference counterpart.  mirai_ipc_export gives the 64-byte CUDA IPC handle of
+ * the allocation holding `ptr` and ptr's byte offset in it; another process
+ * maps it into its own device's context with mirai_ipc_import (peer access
+ * over NVLink, no context on the exporting GPU) and unmaps it with
+ * mirai_ipc_release(base).  mirai_copy_async is one cudaMemcpyAsync (a
+ * copy-engine transfer, also between a local and a mapped peer pointer) on
+ * `stream`.  The exporter keeps the memory alive while peers map it. */
+int mirai_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+int mirai_ipc_import(const void* handle, uint64_t offset, void** ptr, void** base);
+int mirai_ipc_release(void* base);
+int mirai_copy_async(void* dst, const void* src, uint64_t bytes, mirai_stream_t stream);
+
 /* ------------------------------------------------------------ a1: router top-k
  * Replaces TokenChoiceRouter.forward's selection (routers.py:241-249) and the
  * LingBot router's (transformer_lingbot_video.py:1002-1033) on fp32 logits

@@ -55,6 +55,10 @@ SIGNATURES = {
     "mirai_b200_device_status": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "mirai_route_topk": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_i32, c_f32, c_vp, c_vp, c_vp]),
     "mirai_b200_set_gemm_sm_limit": (ctypes.c_int, [c_i32]),
+    "mirai_ipc_export": (ctypes.c_int, [c_vp, c_vp, ctypes.POINTER(ctypes.c_uint64)]),
+    "mirai_ipc_import": (ctypes.c_int, [c_vp, ctypes.c_uint64, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp)]),
+    "mirai_ipc_release": (ctypes.c_int, [c_vp]),
+    "mirai_copy_async": (ctypes.c_int, [c_vp, c_vp, ctypes.c_uint64, c_vp]),
     "mirai_dispatch_plan_workspace_bytes": (c_size, [c_i64, c_i32, c_i32]),
     "mirai_dispatch_plan_static_scratch_bytes": (c_size, []),
     "mirai_dispatch_plan_static": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,

@@ -83,6 +83,21 @@ int make_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t elem_byte
   return MIRAI_OK;
 }
 
+typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static AddressRangeFn address_range() {
+  static AddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(p);
+  });
+  return fn;
+}
+
 }  // namespace mirai
 
 extern "C" {
@@ -90,6 +105,49 @@ extern "C" {
 const char* mirai_b200_last_error(void) { return mirai::t_last_error; }
 
 int mirai_b200_version(void) { return 100; }
+
+int mirai_ipc_export(const void* ptr, void* handle, uint64_t* offset) {
+  if (!ptr || !handle || !offset) return mirai::set_error(MIRAI_ERR_INVALID_ARG, "ipc_export: null pointer");
+  mirai::AddressRangeFn range = mirai::address_range();
+  if (!range) return mirai::set_error(MIRAI_ERR_CUDA, "ipc_export: cuMemGetAddressRange is not available");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return mirai::set_error(MIRAI_ERR_INVALID_ARG, "ipc_export: %p is not device memory", ptr);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return mirai::set_error(MIRAI_ERR_CUDA, "ipc_export: %s", cudaGetErrorString(e));
+  memcpy(handle, &h, sizeof(h));
+  *offset = (uint64_t)(reinterpret_cast<uintptr_t>(ptr) - (uintptr_t)base);
+  return MIRAI_OK;
+}
+
+int mirai_ipc_import(const void* handle, uint64_t offset, void** ptr, void** base) {
+  if (!handle || !ptr || !base) return mirai::set_error(MIRAI_ERR_INVALID_ARG, "ipc_import: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* b = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return mirai::set_error(MIRAI_ERR_CUDA, "ipc_import: %s", cudaGetErrorString(e));
+  *base = b;
+  *ptr = static_cast<uint8_t*>(b) + offset;
+  return MIRAI_OK;
+}
+
+int mirai_ipc_release(void* base) {
+  if (!base) return MIRAI_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return mirai::set_error(MIRAI_ERR_CUDA, "ipc_release: %s", cudaGetErrorString(e));
+  return MIRAI_OK;
+}
+
+int mirai_copy_async(void* dst, const void* src, uint64_t bytes, mirai_stream_t stream) {
+  if (bytes == 0) return MIRAI_OK;
+  if (!dst || !src) return mirai::set_error(MIRAI_ERR_INVALID_ARG, "copy_async: null pointer");
+  cudaError_t e = cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDefault, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return mirai::set_error(MIRAI_ERR_CUDA, "copy_async: %s", cudaGetErrorString(e));
+  return MIRAI_OK;
+}
 
 int mirai_b200_set_gemm_sm_limit(int32_t max_sms) {
   if (max_sms < 0 || max_sms == 1)

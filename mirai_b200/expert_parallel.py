@@ -229,3 +229,189 @@ def shard_tokens(num_tokens: int, world: int, rank: int) -> tuple[int, int]:
     base, extra = divmod(num_tokens, world)
     begin = rank * base + min(rank, extra)
     return begin, begin + base + (1 if rank < extra else 0)
+
+
+class PeerBuffers:
+    """One device buffer per rank of the group, mapped into every other rank
+    (CUDA IPC; one process per GPU), so a rank can write its blocks straight
+    into a peer's buffer with copy-engine transfers over NVLink.  `ensure` is
+    collective: every rank calls it with the same byte count (derived from data
+    all ranks hold) and the buffers are re-exported only when they must grow."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.local: torch.Tensor | None = None
+        self.ptrs: list[int] = []
+        self._bases: list[int | None] = []
+
+    def ensure(self, nbytes: int, dev: torch.device) -> list[int]:
+        if self.local is not None and self.local.numel() >= nbytes:
+            return self.ptrs
+        import ctypes
+        from . import _lib
+        self.release()
+        cap = (int(nbytes * 1.25) + (2 << 20) - 1) // (2 << 20) * (2 << 20)
+        self.local = torch.empty(cap, dtype=torch.uint8, device=dev)
+        handle = (ctypes.c_uint8 * 64)()
+        off = ctypes.c_uint64(0)
+        _lib.call("mirai_ipc_export", self.local.data_ptr(), handle, ctypes.byref(off))
+        infos: list = [None] * self.world
+        dist.all_gather_object(infos, (bytes(handle), off.value), group=self.group)
+        self.ptrs, self._bases = [], []
+        for r, (h, o) in enumerate(infos):
+            if r == self.rank:
+                self.ptrs.append(self.local.data_ptr())
+                self._bases.append(None)
+                continue
+            hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+            p, b = _lib.c_vp(0), _lib.c_vp(0)
+            _lib.call("mirai_ipc_import", hb, o, ctypes.byref(p), ctypes.byref(b))
+            self.ptrs.append(p.value)
+            self._bases.append(b.value)
+        return self.ptrs
+
+    def release(self) -> None:
+        """Collective: unmap the peers' buffers and drop this rank's."""
+        if self.local is None:
+            return
+        from . import _lib
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # nobody still writes into an old buffer
+        for b in self._bases:
+            if b:
+                _lib.call("mirai_ipc_release", _lib.c_vp(b))
+        dist.barrier(group=self.group)  # nobody still maps this rank's old buffer
+        self.local, self.ptrs, self._bases = None, [], []
+
+
+class ExpertParallelMoE:
+    """The expert-parallel layer with a copy-engine exchange (transport "ipc").
+
+    Same contract and result as ``ep_moe_forward``; the rows move differently:
+    every rank maps every other rank's exchange buffer (``PeerBuffers``), a
+    token owner copies each of its per-owner blocks straight into that owner's
+    receive region (source-major, the layout the source-major GEMMs take) with
+    one cudaMemcpyAsync (copy engines, no SMs), and the owner copies each
+    source's results straight back into the token owner's return region.  A
+    one-element NCCL all-reduce after the copies of a chunk, on the same
+    stream, tells every rank that all of that chunk's blocks have landed.  With
+    ``chunks`` > 1 the copies of one chunk run beside the GEMMs of another."""
+
+    def __init__(self, shard: ExpertShard, *, top_k: int, inter: int, group=None, chunks: int = 2,
+                 ops: StepOps | None = None):
+        self.shard, self.top_k, self.inter, self.group = shard, top_k, inter, group
+        self.chunks = max(1, int(chunks))
+        self.ops = ops or CudaStepOps()
+        self.buffers = PeerBuffers(group)
+        self.comm: torch.cuda.Stream | None = None
+        self._flag: torch.Tensor | None = None
+
+    def close(self) -> None:
+        self.buffers.release()
+
+    def _copy(self, dst: int, src: int, nbytes: int, stream) -> None:
+        from . import _lib
+        _lib.call("mirai_copy_async", _lib.c_vp(dst), _lib.c_vp(src), nbytes, _lib.c_vp(stream.cuda_stream))
+
+    def forward(self, tokens: torch.Tensor, logits: torch.Tensor, local_weights: Any) -> torch.Tensor:
+        ops, shard, k = self.ops, self.shard, self.top_k
+        G, E, El, me = shard.world, shard.num_experts, shard.local, shard.rank
+        T, H = tokens.shape
+        dev = tokens.device
+        if G == 1:
+            return ep_moe_forward(tokens, logits, local_weights, shard=shard, top_k=k, inter=self.inter, ops=ops)
+        if self.comm is None:
+            self.comm = torch.cuda.Stream(device=dev)
+            self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
+        comp, comm = torch.cuda.current_stream(dev), self.comm
+        C = self.chunks
+        bounds = [((T * c) // C, (T * (c + 1)) // C) for c in range(C)]
+        prep = []
+        for b, e in bounds:
+            idx, tw = ops.route(logits[b:e], k)
+            plan = ops.plan(idx, E)
+            prep.append((tw, plan, ops.permute(tokens[b:e], plan.sorted_token_indices)))
+        # every rank's rows per (destination, chunk, local expert): one gather, one host read
+        mine = torch.stack([p[1].counts.view(G, El) for p in prep], dim=1).contiguous()  # [dest, chunk, expert]
+        allm = torch.empty((G,) + tuple(mine.shape), dtype=mine.dtype, device=dev)      # [source, dest, chunk, expert]
+        dist.all_gather_into_tensor(allm, mine, group=self.group)
+        M = allm.cpu().numpy()
+        n = M.sum(axis=3)                                   # rows [source, dest, chunk]
+        R = n.sum(axis=0)                                   # rows each destination receives [dest, chunk]
+        S = n.sum(axis=1)                                   # rows each source sends [source, chunk]
+        row_bytes = H * tokens.element_size()
+        in_cap = int(R.sum(axis=1).max()) * row_bytes       # receive region, the same on every rank
+        ret_cap = int(S.sum(axis=1).max()) * row_bytes      # return region
+        in_cap = (in_cap + 255) // 256 * 256
+        ptrs = self.buffers.ensure(in_cap + ret_cap, dev)
+        local = self.buffers.local
+
+        def in_base(d, c):      # rows before chunk c in d's receive region
+            return int(R[d, :c].sum())
+
+        def src_off(d, c, s):   # rows of sources < s in d's chunk-c receive block
+            return int(n[:s, d, c].sum())
+
+        def send_off(s, d, c):  # rows for destinations < d in s's chunk-c send order
+            return int(n[s, :d, c].sum())
+
+        def ret_base(s, c):     # rows before chunk c in s's return region
+            return int(S[s, :c].sum())
+
+        x_in = local[:in_cap].view(tokens.dtype)[: int(R[me].sum()) * H].view(-1, H)
+        y_ret = local[in_cap:in_cap + ret_cap].view(tokens.dtype)[: int(S[me].sum()) * H].view(-1, H)
+        offs = []
+        for c in range(C):
+            ends, run = [], 0
+            for s in range(G):
+                for e in range(El):
+                    run += int(M[s, me, c, e])
+                    ends.append(run)
+            offs.append(ends)
+        offs_dev = torch.tensor(offs, dtype=torch.int32).to(dev, non_blocking=True)
+
+        def arrived(stream):
+            with torch.cuda.stream(stream):
+                dist.all_reduce(self._flag, group=self.group)
+                ev = torch.cuda.Event()
+                ev.record(stream)
+            return ev
+
+        ready = torch.cuda.Event()
+        ready.record(comp)
+        comm.wait_event(ready)
+        landed = []
+        for c in range(C):
+            xs = prep[c][2]
+            xs.record_stream(comm)
+            for d in range(G):
+                rows = int(n[me, d, c])
+                if rows:
+                    dst = ptrs[d] + (in_base(d, c) + src_off(d, c, me)) * row_bytes
+                    self._copy(dst, xs.data_ptr() + send_off(me, d, c) * row_bytes, rows * row_bytes, comm)
+            landed.append(arrived(comm))
+        returned = []
+        for c in range(C):
+            comp.wait_event(landed[c])
+            rows_c = int(R[me, c])
+            xc = x_in[in_base(me, c):in_base(me, c) + rows_c]
+            yc = ops.experts(xc, offs_dev[c], local_weights, self.inter, sources=G) if rows_c else xc
+            done = torch.cuda.Event()
+            done.record(comp)
+            comm.wait_event(done)
+            yc.record_stream(comm)
+            for s in range(G):
+                rows = int(n[s, me, c])
+                if rows:
+                    dst = ptrs[s] + in_cap + (ret_base(s, c) + send_off(s, me, c)) * row_bytes
+                    self._copy(dst, yc.data_ptr() + src_off(me, c, s) * row_bytes, rows * row_bytes, comm)
+            returned.append(arrived(comm))
+        out = torch.empty((T, H), dtype=tokens.dtype, device=dev)
+        for c, (b, e) in enumerate(bounds):
+            comp.wait_event(returned[c])
+            if e > b:
+                yb = y_ret[ret_base(me, c):ret_base(me, c) + int(S[me, c])]
+                out[b:e] = ops.combine(yb, prep[c][1].inverse_order, prep[c][0], k, tokens.dtype)
+        return out

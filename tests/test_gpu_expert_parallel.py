@@ -43,7 +43,7 @@ def _rank_main(rank, world, port, cfg, results):
     try:
         from mirai_b200 import ops
         from mirai_b200.expert_parallel import ExpertShard, ep_moe_forward, shard_tokens
-        T, H, E, k, I, fmt, chunks = cfg
+        T, H, E, k, I, fmt, chunks, transport = cfg
         g = torch.Generator(device=dev).manual_seed(11)
         x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
         logits = torch.randn(T, E, generator=g, device=dev) * 1.5
@@ -52,12 +52,20 @@ def _rank_main(rank, world, port, cfg, results):
         lo, hi = shard.first, shard.first + shard.local
         local = tuple(_quant(fmt, w[lo:hi].contiguous(), dev) for w in raw)
         b, e = shard_tokens(T, world, rank)
-        comm = torch.cuda.Stream() if chunks > 1 else None
-        if chunks > 1:
-            ops.set_gemm_sm_limit(torch.cuda.get_device_properties(dev).multi_processor_count - 16)
-        out = ep_moe_forward(x[b:e].contiguous(), logits[b:e].contiguous(), local, shard=shard, top_k=k, inter=I,
-                             chunks=chunks, comm_stream=comm)
-        ops.set_gemm_sm_limit(0)
+        xr, lr = x[b:e].contiguous(), logits[b:e].contiguous()
+        if transport == "ipc":
+            from mirai_b200.expert_parallel import ExpertParallelMoE
+            layer = ExpertParallelMoE(shard, top_k=k, inter=I, chunks=chunks)
+            out = layer.forward(xr, lr, local)
+            out2 = layer.forward(xr, lr, local)  # buffers reused
+            assert torch.equal(out, out2)
+            layer.close()
+        else:
+            comm = torch.cuda.Stream() if chunks > 1 else None
+            if chunks > 1:
+                ops.set_gemm_sm_limit(torch.cuda.get_device_properties(dev).multi_processor_count - 16)
+            out = ep_moe_forward(xr, lr, local, shard=shard, top_k=k, inter=I, chunks=chunks, comm_stream=comm)
+            ops.set_gemm_sm_limit(0)
         code, info = ops.device_status()
         full = tuple(_quant(fmt, w, dev) for w in raw)
         idx, tw = ops.route_topk(logits, k)
@@ -73,16 +81,20 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("fmt,chunks", [("nf4", 1), ("bf16", 1), ("int8", 1), ("nf4", 3)])
-def test_expert_parallel_equals_single_gpu_layer(fmt, chunks):
-    """chunks = 3: the pipelined path, exchanges on a second stream and the GEMMs
-    capped below the SM count."""
+@pytest.mark.parametrize("fmt,chunks,transport", [
+    ("nf4", 1, "nccl"), ("bf16", 1, "nccl"), ("int8", 1, "nccl"), ("nf4", 3, "nccl"),
+    ("nf4", 1, "ipc"), ("nf4", 3, "ipc"), ("int8", 2, "ipc"), ("bf16", 2, "ipc"),
+])
+def test_expert_parallel_equals_single_gpu_layer(fmt, chunks, transport):
+    """nccl, chunks = 3: the pipelined all-to-all path (exchanges on a second
+    stream, GEMMs capped below the SM count); ipc: copy-engine transfers into
+    peer-mapped buffers."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     from mirai_b200.build import build
     build()
     world = 2
-    cfg = (3000, 256, 8, 2, 384, fmt, chunks)
+    cfg = (3000, 256, 8, 2, 384, fmt, chunks, transport)
     with mp.Manager() as mgr:
         results = mgr.dict()
         mp.start_processes(_rank_main, args=(world, _free_port(), cfg, results), nprocs=world, start_method="spawn")
