@@ -1,0 +1,133 @@
+"""Measure the expert-parallel exchange on this machine (one process per GPU).
+
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
+        --master-port P -m mirai_b200.ep_probe bandwidth
+    python -m torch.distributed.run ... -m mirai_b200.ep_probe phases --config c2|c4
+
+``bandwidth``: bytes that cross NVLink per rank per second for NCCL's
+all_to_all_single and for copy-engine transfers into peer-mapped buffers (the
+layer's ``ipc`` transport), on equal-sized blocks.  ``phases``: CUDA-event
+times between the phases of one ``ExpertParallelMoE`` layer (1 chunk) on
+rank 0, averaged over 10 layers after 3 warm-up layers.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+
+def _bandwidth(dev, world, rank):
+    from . import _lib
+    from .expert_parallel import PeerBuffers
+    res = {}
+    for name, rows, H in (("c2-sized", 65536, 2048), ("c4-sized", 131072, 4096)):
+        n = rows * world
+        x = torch.randn(n, H, device=dev).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        remote = n * H * 2 * (world - 1) / world
+        for _ in range(3):
+            dist.all_to_all_single(y, x)
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(10):
+            dist.all_to_all_single(y, x)
+        b.record()
+        torch.cuda.synchronize()
+        nccl_ms = a.elapsed_time(b) / 10
+        # copy engines: block j of this rank's buffer goes to rank j's buffer at slot `rank`
+        pb = PeerBuffers()
+        ptrs = pb.ensure(x.numel() * 2, dev)
+        blk = rows * H * 2
+        stream = torch.cuda.current_stream()
+        flag = torch.zeros(1, device=dev)
+
+        def exchange():
+            for j in range(world):
+                _lib.call("mirai_copy_async", _lib.c_vp(ptrs[j] + rank * blk), _lib.c_vp(x.data_ptr() + j * blk),
+                          blk, _lib.c_vp(stream.cuda_stream))
+            dist.all_reduce(flag)
+
+        for _ in range(3):
+            exchange()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a.record()
+        for _ in range(10):
+            exchange()
+        b.record()
+        torch.cuda.synchronize()
+        ce_ms = a.elapsed_time(b) / 10
+        pb.release()
+        res[name] = {"bytes_per_rank_remote": int(remote),
+                     "nccl_all_to_all_ms": round(nccl_ms, 3), "nccl_GBps": round(remote / nccl_ms / 1e6, 1),
+                     "copy_engine_ms": round(ce_ms, 3), "copy_engine_GBps": round(remote / ce_ms / 1e6, 1)}
+        del x, y
+    return res
+
+
+def _phases(dev, world, rank, config):
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+    from .expert_parallel import ExpertParallelMoE, ExpertShard, shard_tokens
+    cfg = dict(bench.CONFIGS[config], layers=1)
+    strong = bench.CONFIGS[config].get("ep") == "strong"
+    T_total = cfg["T"] if strong else cfg["T"] * world
+    b, e = shard_tokens(T_total, world, rank)
+    shard = ExpertShard(cfg["E"], world, rank)
+    x, logits, stack = bench.make_ep_workload(cfg, dev, rank, shard, e - b)
+    layer = ExpertParallelMoE(shard, top_k=cfg["k"], inter=cfg["I"], chunks=1)
+    events = []
+
+    def hook(name, stream):  # records at its point in the stream
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        events.append((name, ev))
+
+    layer.on_phase = hook
+    for _ in range(3):
+        events.clear()
+        layer.forward(x, logits, stack[0][1])
+    torch.cuda.synchronize()
+    dist.barrier()
+    acc: dict[str, float] = {}
+    for _ in range(10):
+        events.clear()
+        layer.forward(x, logits, stack[0][1])
+        torch.cuda.synchronize()
+        for i in range(1, len(events)):
+            name = events[i][0]
+            acc[name] = acc.get(name, 0.0) + events[i - 1][1].elapsed_time(events[i][1]) / 10
+    layer.close()
+    return {"config": config, "world": world, "tokens_rank0": e - b,
+            "phases_ms": {k: round(v, 3) for k, v in acc.items()}, "layer_ms": round(sum(acc.values()), 3)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["bandwidth", "phases"])
+    ap.add_argument("--config", default="c2")
+    args = ap.parse_args()
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        res = _bandwidth(dev, world, rank) if args.what == "bandwidth" else _phases(dev, world, rank, args.config)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -307,6 +307,8 @@ class ExpertParallelMoE:
         self.buffers = PeerBuffers(group)
         self.comm: torch.cuda.Stream | None = None
         self._flag: torch.Tensor | None = None
+        # optional probe: called as on_phase(name, stream) at phase boundaries
+        self.on_phase = None
 
     def close(self) -> None:
         self.buffers.release()
@@ -326,6 +328,8 @@ class ExpertParallelMoE:
             self.comm = torch.cuda.Stream(device=dev)
             self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
         comp, comm = torch.cuda.current_stream(dev), self.comm
+        mark = self.on_phase or (lambda name, stream: None)
+        mark("start", comp)
         C = self.chunks
         bounds = [((T * c) // C, (T * (c + 1)) // C) for c in range(C)]
         prep = []
@@ -333,6 +337,7 @@ class ExpertParallelMoE:
             idx, tw = ops.route(logits[b:e], k)
             plan = ops.plan(idx, E)
             prep.append((tw, plan, ops.permute(tokens[b:e], plan.sorted_token_indices)))
+        mark("route+plan+permute", comp)
         # every rank's rows per (destination, chunk, local expert): one gather, one host read
         mine = torch.stack([p[1].counts.view(G, El) for p in prep], dim=1).contiguous()  # [dest, chunk, expert]
         allm = torch.empty((G,) + tuple(mine.shape), dtype=mine.dtype, device=dev)      # [source, dest, chunk, expert]
@@ -371,6 +376,7 @@ class ExpertParallelMoE:
                     ends.append(run)
             offs.append(ends)
         offs_dev = torch.tensor(offs, dtype=torch.int32).to(dev, non_blocking=True)
+        mark("count gather + host read", comp)
 
         def arrived(stream):
             with torch.cuda.stream(stream):
@@ -392,12 +398,14 @@ class ExpertParallelMoE:
                     dst = ptrs[d] + (in_base(d, c) + src_off(d, c, me)) * row_bytes
                     self._copy(dst, xs.data_ptr() + send_off(me, d, c) * row_bytes, rows * row_bytes, comm)
             landed.append(arrived(comm))
+            mark(f"dispatch copies + arrival, chunk {c}", comm)
         returned = []
         for c in range(C):
             comp.wait_event(landed[c])
             rows_c = int(R[me, c])
             xc = x_in[in_base(me, c):in_base(me, c) + rows_c]
             yc = ops.experts(xc, offs_dev[c], local_weights, self.inter, sources=G) if rows_c else xc
+            mark(f"gate/up + down GEMMs, chunk {c}", comp)
             done = torch.cuda.Event()
             done.record(comp)
             comm.wait_event(done)
@@ -408,10 +416,12 @@ class ExpertParallelMoE:
                     dst = ptrs[s] + in_cap + (ret_base(s, c) + send_off(s, me, c)) * row_bytes
                     self._copy(dst, yc.data_ptr() + src_off(me, c, s) * row_bytes, rows * row_bytes, comm)
             returned.append(arrived(comm))
+            mark(f"return copies + arrival, chunk {c}", comm)
         out = torch.empty((T, H), dtype=tokens.dtype, device=dev)
         for c, (b, e) in enumerate(bounds):
             comp.wait_event(returned[c])
             if e > b:
                 yb = y_ret[ret_base(me, c):ret_base(me, c) + int(S[me, c])]
                 out[b:e] = ops.combine(yb, prep[c][1].inverse_order, prep[c][0], k, tokens.dtype)
+        mark("combine", comp)
         return out
