@@ -103,6 +103,14 @@ int mirai_ipc_export(const void* ptr, void* handle, uint64_t* offset);
 int mirai_ipc_import(const void* handle, uint64_t offset, void** ptr, void** base);
 int mirai_ipc_release(void* base);
 int mirai_copy_async(void* dst, const void* src, uint64_t bytes, mirai_stream_t stream);
+/* Arrival flags of that exchange: mirai_ep_signal stores `epoch` (release,
+ * system scope) into each of `count` 8-byte slots given by device pointers
+ * (a rank's slot in every peer's flag array; NULL entries skipped), after the
+ * work already on `stream`; mirai_ep_wait holds `stream` until flags[i] >=
+ * epoch for every i < count except `skip`.  The wait gives up after 2 s and
+ * records MIRAI_ERR_DEVICE_TIMEOUT (mirai_b200_device_status). */
+int mirai_ep_signal(void* const* peer_slots, int32_t count, uint64_t epoch, mirai_stream_t stream);
+int mirai_ep_wait(const uint64_t* flags, int32_t count, int32_t skip, uint64_t epoch, mirai_stream_t stream);
 
 /* ------------------------------------------------------------ a1: router top-k
  * Replaces TokenChoiceRouter.forward's selection (routers.py:241-249) and the

@@ -134,6 +134,8 @@ struct alignas(16) Smem {
   uint64_t raw_empty[Cfg<WF, PAIR>::RAW_STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
+  uint64_t absq_full[2];   // NF4 pair K-major: the tile's absmax codes, prefetched
+  uint64_t absq_empty[2];
   uint32_t tmem_base;
   int abort_flag;
   int row_start[kMaxExperts + 1];  // per segment, in tile order
@@ -276,6 +278,11 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   constexpr uint32_t A_STAGE = C::A_STAGE;
   constexpr bool QUANT = WF != W_BF16;
   constexpr bool MN = MCfg<MODE>::MN;
+  // NF4 on CTA pairs, K-major: each tile's absmax codes (one contiguous run of
+  // B_ROWS x K/64 bytes) are bulk-copied by the raw-code producer into one of
+  // two buffers ahead of use, so the dequantisers never stop to stage them.
+  constexpr bool PREFETCH = WF == W_NF4 && PAIR && !MN;
+  constexpr int ABUF = 8192;  // bytes per prefetch buffer: B_ROWS x K/64 with K <= 4096
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = base;
@@ -343,6 +350,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         mbar_init(&sm.raw_empty[s], C::GROUP_WARPS);
       }
       for (int a = 0; a < 2; ++a) {
+        mbar_init(&sm.absq_full[a], 1);
+        mbar_init(&sm.absq_empty[a], kDeqWarps);
         mbar_init(&sm.tfull[a], 1);
         mbar_init(&sm.tempty[a], C::EPI_WARPS * pair_mult);
       }
@@ -663,9 +672,26 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       int rstage = 0;
       uint32_t rphase = 0;
       constexpr int RB = C::ROW_BYTES;
-      for (int t = unit; t < total_tiles && !*abort_flag; t += num_units) {
+      int tl = 0;  // tiles of this CTA so far
+      for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++tl) {
         int j, e, m, n;
         decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
+        if (PREFETCH) {
+          const int buf = tl & 1;
+          if (tl >= 2 && !mbar_wait(&sm.absq_empty[buf], ((tl >> 1) - 1) & 1, 13)) {
+            *abort_flag = 1;
+            break;
+          }
+          const int first = kmajor_row<MODE, TN>(p, e, n, (int)rank) - e * p.out_rows;
+          const int rows = min(TN / 2, p.out_rows - first);  // a multiple of 64 (N % 64 == 0)
+          const uint32_t bytes = rows > 0 ? (uint32_t)(rows * num_kb) : 0u;
+          mbar_arrive_expect_tx(&sm.absq_full[buf], bytes);
+          if (bytes) {
+            const int key = MCfg<MODE>::TWO_KEYS ? (int)rank : 0;
+            bulk_load_1d(dq->absq + buf * ABUF, p.q[key].absmax + (size_t)kmajor_row<MODE, TN>(p, e, n, (int)rank) * num_kb,
+                         bytes, &sm.absq_full[buf]);
+          }
+        }
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&sm.raw_empty[rstage], rphase ^ 1, 11)) {
             *abort_flag = 1;
@@ -722,15 +748,24 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     int cur_key = -1;
     int gk = 0;  // position in this CTA's k-block sequence over all its tiles
     bool failed = false;
-    for (int t = unit; t < total_tiles && !failed && !*abort_flag; t += num_units) {
+    int tl = 0;  // tiles of this CTA so far
+    // per-tile staging through shared memory (NF4 unless prefetched; INT8 MN-major)
+    constexpr bool STAGE = (WF == W_NF4 && !PREFETCH) || (WF == W_INT8 && MN);
+    for (int t = unit; t < total_tiles && !failed && !*abort_flag; t += num_units, ++tl) {
       int j, e, m, n;
       decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
       // key of this thread's rows (K-major) / of the k-block (MN)
       const int row_key = MN ? 0 : (MCfg<MODE>::TWO_KEYS ? kblk : 0);
       const int wrow_base = MN ? 0 : kmajor_row<MODE, TN>(p, e, n, kblk) - e * p.out_rows;  // first weight row
+      const int abuf = tl & 1;
+      if (PREFETCH && !mbar_wait(&sm.absq_full[abuf], (tl >> 1) & 1, 42)) {
+        failed = true;
+        *abort_flag = 1;
+        break;
+      }
       // ---- stage this tile's scale inputs in shared memory
-      named_bar_sync(1, kDeqThreads);
-      if (WF == W_NF4) {
+      if (STAGE) named_bar_sync(1, kDeqThreads);
+      if (WF == W_NF4 && !PREFETCH) {
         if (!MN) {
           const int nblk = PAIR ? 1 : 2;
           for (int h = 0; h < nblk; ++h) {
@@ -760,7 +795,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         for (int h = 0; h < (MCfg<MODE>::TWO_KEYS ? 2 : 1); ++h)
           for (int i = d; i < p.q[h].n_nested; i += kDeqThreads)
             dq->nested[h][i] = __ldg(p.q[h].nested_absmax + (size_t)e * p.q[h].n_nested + i);
-      } else if (MN) {
+      } else if (WF == W_INT8 && MN) {
         // INT8 MN-major: the scale belongs to the k-row (output channel of W)
         float* srow = reinterpret_cast<float*>(dq->absq);
         for (int kk = d; kk < p.K; kk += kDeqThreads) {
@@ -768,7 +803,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           srow[kk] = __ldg(p.q[key].scale + (size_t)e * p.krows + (kk - key * p.krows));
         }
       }
-      named_bar_sync(1, kDeqThreads);
+      if (STAGE) named_bar_sync(1, kDeqThreads);
       // K-major: is this thread's weight row inside the expert's matrix?  (The
       // last tile of a down projection whose N is not a multiple of TN is half empty.)
       const bool row_live = MN || (wrow_base + kr < p.out_rows);
@@ -813,7 +848,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             bool live = row_live;
             if (!MN) {
               blk = (wrow_base + kr) * nkb + kb;
-              qcode = dq->absq[absq_row * (TN / 2) * nkb + kr * nkb + kb];
+              qcode = PREFETCH ? dq->absq[abuf * ABUF + kr * nkb + kb]
+                               : dq->absq[absq_row * (TN / 2) * nkb + kr * nkb + kb];
             } else {
               const int kk = kb * BK + kr;        // k-row across both keys
               const int wr = kk - key * p.krows;  // k-row inside the key's matrix
@@ -822,9 +858,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
               blk = wr * nblk_row + nbg;
               qcode = dq->absq[kk * (C::B_ROWS / 64) + nbq];
             }
-            const float scale = live ? __fadd_rn(__fmul_rn(dq->ncode[key][qcode], dq->nested[key][blk >> p.nbs_shift]),
-                                                 off[key])
-                                     : 0.f;
+            const float nabs = PREFETCH ? __ldg(p.q[key].nested_absmax + (size_t)e * p.q[key].n_nested +
+                                                (blk >> p.nbs_shift))
+                                        : dq->nested[key][blk >> p.nbs_shift];
+            const float scale = live ? __fadd_rn(__fmul_rn(dq->ncode[key][qcode], nabs), off[key]) : 0.f;
             Nf4Tab tab;
             nf4_table(code, scale, tab);
 #pragma unroll
@@ -851,6 +888,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           if (PAIR) mbar_arrive_cluster(full_leader0 + 8u * st);
           else mbar_arrive(&sm.full[st]);
         }
+      }
+      if (PREFETCH && !failed) {  // this warp is done with the tile's absmax buffer
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.absq_empty[abuf]);
       }
     }
   }

@@ -6,3 +6,4 @@
 #include "grouped_gemm.cu"
 #include "quantize.cu"
 #include "lora.cu"
+#include "exchange.cu"

@@ -46,15 +46,19 @@ def _bandwidth(dev, world, rank):
         # copy engines: block j of this rank's buffer goes to rank j's buffer at slot `rank`
         pb = PeerBuffers()
         ptrs = pb.ensure(x.numel() * 2, dev)
+        data = [p + PeerBuffers.FLAG_BYTES for p in ptrs]
+        slots = (_lib.c_vp * world)(*[None if j == rank else ptrs[j] + 8 * rank for j in range(world)])
         blk = rows * H * 2
         stream = torch.cuda.current_stream()
-        flag = torch.zeros(1, device=dev)
+        epoch = [0]
 
-        def exchange():
+        def exchange():  # the layer's mechanism: copies, then arrival flags
             for j in range(world):
-                _lib.call("mirai_copy_async", _lib.c_vp(ptrs[j] + rank * blk), _lib.c_vp(x.data_ptr() + j * blk),
+                _lib.call("mirai_copy_async", _lib.c_vp(data[j] + rank * blk), _lib.c_vp(x.data_ptr() + j * blk),
                           blk, _lib.c_vp(stream.cuda_stream))
-            dist.all_reduce(flag)
+            epoch[0] += 1
+            _lib.call("mirai_ep_signal", slots, world, epoch[0], _lib.c_vp(stream.cuda_stream))
+            _lib.call("mirai_ep_wait", _lib.c_vp(ptrs[rank]), world, rank, epoch[0], _lib.c_vp(stream.cuda_stream))
 
         for _ in range(3):
             exchange()
@@ -66,6 +70,8 @@ def _bandwidth(dev, world, rank):
         b.record()
         torch.cuda.synchronize()
         ce_ms = a.elapsed_time(b) / 10
+        from .ops import check_device
+        check_device()
         pb.release()
         res[name] = {"bytes_per_rank_remote": int(remote),
                      "nccl_all_to_all_ms": round(nccl_ms, 3), "nccl_GBps": round(remote / nccl_ms / 1e6, 1),

@@ -234,9 +234,13 @@ def shard_tokens(num_tokens: int, world: int, rank: int) -> tuple[int, int]:
 class PeerBuffers:
     """One device buffer per rank of the group, mapped into every other rank
     (CUDA IPC; one process per GPU), so a rank can write its blocks straight
-    into a peer's buffer with copy-engine transfers over NVLink.  `ensure` is
-    collective: every rank calls it with the same byte count (derived from data
-    all ranks hold) and the buffers are re-exported only when they must grow."""
+    into a peer's buffer with copy-engine transfers over NVLink.  Each buffer
+    starts with FLAG_BYTES of arrival flags (one uint64 per rank, zeroed before
+    the buffer is shared); data regions follow.  `ensure` is collective: every
+    rank calls it with the same byte count (derived from data all ranks hold)
+    and the buffers are re-exported only when they must grow."""
+
+    FLAG_BYTES = 4096
 
     def __init__(self, group=None):
         self.group = group
@@ -247,13 +251,16 @@ class PeerBuffers:
         self._bases: list[int | None] = []
 
     def ensure(self, nbytes: int, dev: torch.device) -> list[int]:
-        if self.local is not None and self.local.numel() >= nbytes:
+        """Buffer pointers of every rank (data regions start FLAG_BYTES in)."""
+        if self.local is not None and self.local.numel() >= nbytes + self.FLAG_BYTES:
             return self.ptrs
         import ctypes
         from . import _lib
         self.release()
-        cap = (int(nbytes * 1.25) + (2 << 20) - 1) // (2 << 20) * (2 << 20)
+        cap = (int((nbytes + self.FLAG_BYTES) * 1.25) + (2 << 20) - 1) // (2 << 20) * (2 << 20)
         self.local = torch.empty(cap, dtype=torch.uint8, device=dev)
+        # flags start at zero; the handle exchange below orders this before any peer's signal
+        self.local[:self.FLAG_BYTES].zero_()
         handle = (ctypes.c_uint8 * 64)()
         off = ctypes.c_uint64(0)
         _lib.call("mirai_ipc_export", self.local.data_ptr(), handle, ctypes.byref(off))
@@ -297,7 +304,11 @@ class ExpertParallelMoE:
     source's results straight back into the token owner's return region.  A
     one-element NCCL all-reduce after the copies of a chunk, on the same
     stream, tells every rank that all of that chunk's blocks have landed.  With
-    ``chunks`` > 1 the copies of one chunk run beside the GEMMs of another."""
+    ``chunks`` > 1 the copies of one chunk run beside the GEMMs of another.
+    Arrival is signalled with flags in the peers' buffers: after a chunk's
+    copies a rank stores the exchange's epoch into its slot of every peer's
+    flag array, and a consumer's stream waits (bounded) for all its slots to
+    reach the epoch before the GEMMs or the combine read the data."""
 
     def __init__(self, shard: ExpertShard, *, top_k: int, inter: int, group=None, chunks: int = 2,
                  ops: StepOps | None = None):
@@ -306,7 +317,7 @@ class ExpertParallelMoE:
         self.ops = ops or CudaStepOps()
         self.buffers = PeerBuffers(group)
         self.comm: torch.cuda.Stream | None = None
-        self._flag: torch.Tensor | None = None
+        self.epoch = 0  # exchanges so far; the same sequence on every rank
         # optional probe: called as on_phase(name, stream) at phase boundaries
         self.on_phase = None
 
@@ -326,7 +337,6 @@ class ExpertParallelMoE:
             return ep_moe_forward(tokens, logits, local_weights, shard=shard, top_k=k, inter=self.inter, ops=ops)
         if self.comm is None:
             self.comm = torch.cuda.Stream(device=dev)
-            self._flag = torch.zeros(1, dtype=torch.float32, device=dev)
         comp, comm = torch.cuda.current_stream(dev), self.comm
         mark = self.on_phase or (lambda name, stream: None)
         mark("start", comp)
@@ -350,8 +360,10 @@ class ExpertParallelMoE:
         in_cap = int(R.sum(axis=1).max()) * row_bytes       # receive region, the same on every rank
         ret_cap = int(S.sum(axis=1).max()) * row_bytes      # return region
         in_cap = (in_cap + 255) // 256 * 256
+        F = PeerBuffers.FLAG_BYTES
         ptrs = self.buffers.ensure(in_cap + ret_cap, dev)
-        local = self.buffers.local
+        local = self.buffers.local[F:]
+        data = [p + F for p in ptrs]
 
         def in_base(d, c):      # rows before chunk c in d's receive region
             return int(R[d, :c].sum())
@@ -378,12 +390,21 @@ class ExpertParallelMoE:
         offs_dev = torch.tensor(offs, dtype=torch.int32).to(dev, non_blocking=True)
         mark("count gather + host read", comp)
 
+        from . import _lib
+        slots = (_lib.c_vp * G)(*[None if d == me else ptrs[d] + 8 * me for d in range(G)])
+
         def arrived(stream):
-            with torch.cuda.stream(stream):
-                dist.all_reduce(self._flag, group=self.group)
-                ev = torch.cuda.Event()
-                ev.record(stream)
-            return ev
+            """Signal this exchange to every peer; return (epoch, event after the local copy)."""
+            self.epoch += 1
+            _lib.call("mirai_ep_signal", slots, G, self.epoch, _lib.c_vp(stream.cuda_stream))
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            return self.epoch, ev
+
+        def wait(arrival):
+            epoch, ev = arrival
+            comp.wait_event(ev)  # this rank's own block
+            _lib.call("mirai_ep_wait", _lib.c_vp(ptrs[me]), G, me, epoch, _lib.c_vp(comp.cuda_stream))
 
         ready = torch.cuda.Event()
         ready.record(comp)
@@ -395,13 +416,13 @@ class ExpertParallelMoE:
             for d in range(G):
                 rows = int(n[me, d, c])
                 if rows:
-                    dst = ptrs[d] + (in_base(d, c) + src_off(d, c, me)) * row_bytes
+                    dst = data[d] + (in_base(d, c) + src_off(d, c, me)) * row_bytes
                     self._copy(dst, xs.data_ptr() + send_off(me, d, c) * row_bytes, rows * row_bytes, comm)
             landed.append(arrived(comm))
             mark(f"dispatch copies + arrival, chunk {c}", comm)
         returned = []
         for c in range(C):
-            comp.wait_event(landed[c])
+            wait(landed[c])
             rows_c = int(R[me, c])
             xc = x_in[in_base(me, c):in_base(me, c) + rows_c]
             yc = ops.experts(xc, offs_dev[c], local_weights, self.inter, sources=G) if rows_c else xc
@@ -413,13 +434,13 @@ class ExpertParallelMoE:
             for s in range(G):
                 rows = int(n[s, me, c])
                 if rows:
-                    dst = ptrs[s] + in_cap + (ret_base(s, c) + send_off(s, me, c)) * row_bytes
+                    dst = data[s] + in_cap + (ret_base(s, c) + send_off(s, me, c)) * row_bytes
                     self._copy(dst, yc.data_ptr() + src_off(me, c, s) * row_bytes, rows * row_bytes, comm)
             returned.append(arrived(comm))
             mark(f"return copies + arrival, chunk {c}", comm)
         out = torch.empty((T, H), dtype=tokens.dtype, device=dev)
         for c, (b, e) in enumerate(bounds):
-            comp.wait_event(returned[c])
+            wait(returned[c])
             if e > b:
                 yb = y_ret[ret_base(me, c):ret_base(me, c) + int(S[me, c])]
                 out[b:e] = ops.combine(yb, prep[c][1].inverse_order, prep[c][0], k, tokens.dtype)
