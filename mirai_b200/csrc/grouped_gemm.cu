@@ -9,11 +9,16 @@
 //   DXGATEUP  dx = dgate W1 + dup W3                  B = W1;W3       (MN-major)
 //
 // Warp roles in every CTA:
-//   warp 0        TMA producer: A tiles; B tiles (bf16) or raw codes (NF4/INT8)
-//   warp 1        UMMA issuer (one thread) and TMEM owner
-//   warps 2..5    epilogue: TMEM -> registers -> SwiGLU (+bwd) / bf16 -> global
-//   warps 6..13   (NF4 / INT8) dequantisers: raw codes in shared memory ->
-//                 exact bf16 weights in the UMMA operand layout
+//   TMA producer    A tiles; B tiles (bf16); the LoRA rank block
+//   UMMA issuer     one thread; owns the TMEM accumulators
+//   raw producer    (NF4 / INT8) packed codes into their own ring, and for NF4
+//                   pairs each tile's absmax codes by one bulk copy
+//   epilogue        TMEM -> registers -> SwiGLU (+bwd) / bf16 -> global
+//   dequantisers    (NF4 / INT8) raw codes -> exact bf16 weights in the UMMA
+//                   operand layout
+// NF4 on CTA pairs runs 16 dequantiser warps beside 4 epilogue warps (768
+// threads) with registers rebalanced per warpgroup by setmaxnreg; the other
+// variants run 8 (or none) with one register budget.
 // Two TMEM accumulators (2 x 256 fp32 columns) overlap the epilogue of tile i
 // with the main loop of tile i+1.  Tiles are (expert, row block, column
 // block), expert-major with the column block fastest so that the CTAs running
@@ -54,8 +59,6 @@ constexpr uint32_t A_BYTES = BM * BK * 2;
 // epilogue warps: 8 when the SM has no dequantisers (two per TMEM lane
 // quarter, splitting the columns), 4 otherwise
 constexpr int epi_warps(int wf) { return wf == 0 ? 8 : 4; }
-constexpr int kDeqWarps = 8;
-constexpr int kDeqThreads = 32 * kDeqWarps;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxK = 4096;        // reduction length supported by the quantised formats
@@ -81,16 +84,36 @@ template <int WF, bool PAIR> struct Cfg {
   static constexpr uint32_t B_BYTES = B_ROWS * BK * 2;                   // bf16 B per CTA per stage
   static constexpr int ROW_BYTES = WF == W_NF4 ? BK / 2 : (WF == W_INT8 ? BK : 0);  // raw bytes / 64 elements
   static constexpr uint32_t RAW_BYTES = B_ROWS * ROW_BYTES;
+  // WIDE (NF4 on CTA pairs): 16 dequantiser warps, with the registers split per
+  // warpgroup (setmaxnreg) so that they fit beside the epilogue.  Warps:
+  //   WIDE:  0 TMA producer, 1 MMA, 2 raw-code producer, 3 spare | 4..7 epilogue | 8..23 dequant
+  //   else:  0 TMA producer, 1 MMA, 2.. epilogue, then dequant (8 warps), then raw-code producer
+  static constexpr bool WIDE = WF == W_NF4 && PAIR;
+  static constexpr int DEQ_WARPS = WIDE ? 16 : (QUANT ? 8 : 0);
+  static constexpr int DEQ_THREADS = 32 * DEQ_WARPS;
   // Dequantisers: one thread per B row and k-block; KG groups of B_ROWS
   // threads take the k-blocks in turn (group g: k-blocks g, g+KG, ...).
-  static constexpr int KG = QUANT ? kDeqThreads / B_ROWS : 1;
+  static constexpr int KG = QUANT ? DEQ_THREADS / B_ROWS : 1;
   static constexpr int GROUP_WARPS = QUANT ? B_ROWS / 32 : 0;            // dequant warps per group
   static constexpr int STAGES = WF == W_BF16 ? (PAIR ? 6 : 4) : (PAIR ? 4 : 3);
   // raw-code ring: its own producer warp runs ahead of the operand ring
   static constexpr int RAW_STAGES = WF == W_BF16 ? 1 : (PAIR ? (WF == W_NF4 ? 8 : 6) : (WF == W_NF4 ? 4 : 2));
   static constexpr int EPI_WARPS = epi_warps(WF);
-  static constexpr int THREADS = 64 + 32 * EPI_WARPS + (WF == W_BF16 ? 0 : kDeqThreads + 32);
-  static_assert(!QUANT || (kDeqThreads % B_ROWS == 0 && STAGES % KG == 0 && RAW_STAGES % KG == 0),
+  static constexpr int EPI_FIRST = WIDE ? 4 : 2;
+  static constexpr int DEQ_FIRST = WIDE ? 8 : 2 + EPI_WARPS;
+  static constexpr int RAW_WARP = WIDE ? 2 : DEQ_FIRST + DEQ_WARPS;
+  static constexpr int THREADS = WIDE ? 32 * (DEQ_FIRST + DEQ_WARPS)
+                                      : 64 + 32 * EPI_WARPS + (WF == W_BF16 ? 0 : DEQ_THREADS + 32);
+  // WIDE register split: launched at 80 registers per thread (65536 / 768,
+  // rounded down to a multiple of 8), then producer warpgroup -> 48,
+  // epilogue -> 144, dequantisers -> 72: 128*48 + 128*144 + 512*72 = 61440 =
+  // 768 * 80, the launch allocation (setmaxnreg.inc draws only on registers
+  // the block was launched with; the host checks the compiled count).
+  static constexpr int LAUNCH_REGS = 80;
+  static constexpr int REG_WG0 = 48, REG_EPI = 144, REG_DEQ = 72;
+  static_assert(!WIDE || 128 * REG_WG0 + 128 * REG_EPI + DEQ_THREADS * REG_DEQ <= THREADS * LAUNCH_REGS,
+                "the register split must fit in the launch allocation");
+  static_assert(!QUANT || (DEQ_THREADS % B_ROWS == 0 && STAGES % KG == 0 && RAW_STAGES % KG == 0),
                 "each dequantiser group must own whole stages");
 };
 
@@ -182,6 +205,14 @@ __device__ __forceinline__ void decode_tile(int t, const Smem<WF, PAIR>& sm, int
 }
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Per-warpgroup register budget (all four warps of the group execute it).
+template <int N> __device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N> __device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -351,7 +382,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       }
       for (int a = 0; a < 2; ++a) {
         mbar_init(&sm.absq_full[a], 1);
-        mbar_init(&sm.absq_empty[a], kDeqWarps);
+        mbar_init(&sm.absq_empty[a], C::DEQ_WARPS);
         mbar_init(&sm.tfull[a], 1);
         mbar_init(&sm.tempty[a], C::EPI_WARPS * pair_mult);
       }
@@ -372,10 +403,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     prefetch_tmap(&tmap_b0);
     prefetch_tmap(&tmap_b1);
   }
-  if (WF == W_NF4 && warp >= 2 + C::EPI_WARPS) {
-    const int d = threadIdx.x - 32 * (2 + C::EPI_WARPS);
+  if (WF == W_NF4 && warp >= C::DEQ_FIRST && warp < C::DEQ_FIRST + C::DEQ_WARPS) {
+    const int d = threadIdx.x - 32 * C::DEQ_FIRST;
     for (int h = 0; h < 2; ++h) {
-      for (int i = d; i < 256; i += kDeqThreads) dq->ncode[h][i] = __ldg(p.q[h].nested_code + i);
+      for (int i = d; i < 256; i += C::DEQ_THREADS) dq->ncode[h][i] = __ldg(p.q[h].nested_code + i);
       if (d < 16) dq->code[h][d] = __ldg(p.q[h].code + d);
     }
   }
@@ -392,7 +423,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   const int total_kb = num_kb + p.has_ext;
   volatile int* abort_flag = &sm.abort_flag;
 
-  if (warp == 0) {
+  // Role bodies; dispatched below.
+  auto role_producer = [&]() {
     // ======================= TMA producer =======================
     if (lane == 0) {
       int stage = 0;
@@ -474,7 +506,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  };
+  auto role_mma = [&]() {
     // ======================= UMMA issuer (the leader of a pair) =======================
     if (lane == 0 && leader) {
       constexpr uint32_t idesc = make_idesc_bf16(SUB_M, TN, false, MN);
@@ -528,12 +561,13 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         else umma_commit(&sm.tfull[acc]);
       }
     }
-  } else if (warp < 2 + C::EPI_WARPS) {
+  };
+  auto role_epilogue = [&]() {
     // ======================= epilogue =======================
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     // warps sharing a lane quarter split the 32-column chunks between them
     constexpr int NSPLIT = C::EPI_WARPS / 4;
-    const int part = (warp - 2) / 4;
+    const int part = (warp - C::EPI_FIRST) / 4;
     const uint32_t tempty_leader[2] = {leader_addr(&sm.tempty[0]), leader_addr(&sm.tempty[1])};
     int it = 0;
     for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++it) {
@@ -664,7 +698,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         else mbar_arrive(&sm.tempty[acc]);
       }
     }
-  } else if (QUANT && warp == 2 + C::EPI_WARPS + kDeqWarps) {
+  };
+  auto role_raw = [&]() {
     // ======================= raw-code producer (NF4 / INT8) =======================
     // Streams this CTA's share of the packed codes of every k-block into the
     // raw ring, up to RAW_STAGES ahead of the dequantisers.
@@ -724,7 +759,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         }
       }
     }
-  } else if (QUANT) {
+  };
+  auto role_dequant = [&]() {
     // ======================= dequantisers =======================
     // One thread per B row (K-major: a weight row; MN-major: one k-row of a
     // 64-column block) and k-block: each thread decodes a whole 64-element
@@ -733,7 +769,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     // a group has KG main-loop steps to deliver each of its blocks.
     constexpr int RB = C::ROW_BYTES;
     constexpr int KG = C::KG;
-    const int d = threadIdx.x - 32 * (2 + C::EPI_WARPS);
+    const int d = threadIdx.x - 32 * C::DEQ_FIRST;
     const int grp = d / C::B_ROWS;
     const int row = d % C::B_ROWS;      // B row inside the stage
     const int nkb = num_kb;
@@ -764,7 +800,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         break;
       }
       // ---- stage this tile's scale inputs in shared memory
-      if (STAGE) named_bar_sync(1, kDeqThreads);
+      if (STAGE) named_bar_sync(1, C::DEQ_THREADS);
       if (WF == W_NF4 && !PREFETCH) {
         if (!MN) {
           const int nblk = PAIR ? 1 : 2;
@@ -778,12 +814,12 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             const uint4* src = reinterpret_cast<const uint4*>(
                 p.q[key].absmax + (size_t)kmajor_row<MODE, TN>(p, e, n, blk) * nkb);
             uint4* dst = reinterpret_cast<uint4*>(dq->absq + h * (TN / 2) * nkb);
-            for (int i = d; i < rows * nkb / 16; i += kDeqThreads) dst[i] = __ldg(src + i);
+            for (int i = d; i < rows * nkb / 16; i += C::DEQ_THREADS) dst[i] = __ldg(src + i);
           }
         } else {
           // absq[kk * NB + j] = code of (k-row kk, this CTA's column block j)
           constexpr int NB = C::B_ROWS / 64;
-          for (int i = d; i < p.K * NB; i += kDeqThreads) {
+          for (int i = d; i < p.K * NB; i += C::DEQ_THREADS) {
             const int kk = i / NB, j = i % NB;
             const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
             const int wr = kk - key * p.krows;
@@ -793,17 +829,17 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           }
         }
         for (int h = 0; h < (MCfg<MODE>::TWO_KEYS ? 2 : 1); ++h)
-          for (int i = d; i < p.q[h].n_nested; i += kDeqThreads)
+          for (int i = d; i < p.q[h].n_nested; i += C::DEQ_THREADS)
             dq->nested[h][i] = __ldg(p.q[h].nested_absmax + (size_t)e * p.q[h].n_nested + i);
       } else if (WF == W_INT8 && MN) {
         // INT8 MN-major: the scale belongs to the k-row (output channel of W)
         float* srow = reinterpret_cast<float*>(dq->absq);
-        for (int kk = d; kk < p.K; kk += kDeqThreads) {
+        for (int kk = d; kk < p.K; kk += C::DEQ_THREADS) {
           const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
           srow[kk] = __ldg(p.q[key].scale + (size_t)e * p.krows + (kk - key * p.krows));
         }
       }
-      if (STAGE) named_bar_sync(1, kDeqThreads);
+      if (STAGE) named_bar_sync(1, C::DEQ_THREADS);
       // K-major: is this thread's weight row inside the expert's matrix?  (The
       // last tile of a down projection whose N is not a multiple of TN is half empty.)
       const bool row_live = MN || (wrow_base + kr < p.out_rows);
@@ -894,6 +930,29 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         if (lane == 0) mbar_arrive(&sm.absq_empty[abuf]);
       }
     }
+  };
+
+  if (C::WIDE) {
+    // One register budget per warpgroup, set once at the top of its branch so
+    // that it covers all the code the group runs.
+    if (warp < 4) {
+      setmaxnreg_dec<C::REG_WG0>();
+      if (warp == 0) role_producer();
+      else if (warp == 1) role_mma();
+      else if (warp == C::RAW_WARP) role_raw();
+    } else if (warp < 8) {
+      setmaxnreg_inc<C::REG_EPI>();
+      role_epilogue();
+    } else {
+      setmaxnreg_dec<C::REG_DEQ>();
+      role_dequant();
+    }
+  } else {
+    if (warp == 0) role_producer();
+    else if (warp == 1) role_mma();
+    else if (warp >= C::EPI_FIRST && warp < C::EPI_FIRST + C::EPI_WARPS) role_epilogue();
+    else if (QUANT && warp == C::RAW_WARP) role_raw();
+    else if (QUANT && warp >= C::DEQ_FIRST) role_dequant();
   }
 
   tc_fence_before();
@@ -928,6 +987,15 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    if (C::WIDE) {
+      // the per-warpgroup register split needs the launch allocation it was sized for
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, kern);
+      if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+      if (fa.numRegs < C::LAUNCH_REGS)
+        return set_error(MIRAI_ERR_UNSUPPORTED, "grouped GEMM compiled with %d registers per thread; the register "
+                         "split needs %d", fa.numRegs, C::LAUNCH_REGS);
+    }
     attr_set = true;
   }
   Params q = p;
