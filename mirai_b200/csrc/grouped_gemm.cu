@@ -16,9 +16,9 @@
 //   epilogue        TMEM -> registers -> SwiGLU (+bwd) / bf16 -> global
 //   dequantisers    (NF4 / INT8) raw codes -> exact bf16 weights in the UMMA
 //                   operand layout
-// NF4 on CTA pairs runs 16 dequantiser warps beside 4 epilogue warps (768
-// threads) with registers rebalanced per warpgroup by setmaxnreg; the other
-// variants run 8 (or none) with one register budget.
+// NF4 / INT8 on CTA pairs run 16 dequantiser warps beside 4 epilogue warps
+// (768 threads) with registers rebalanced per warpgroup by setmaxnreg; the
+// single-CTA variants run 8 (or none) with one register budget.
 // Two TMEM accumulators (2 x 256 fp32 columns) overlap the epilogue of tile i
 // with the main loop of tile i+1.  Tiles are (expert, row block, column
 // block), expert-major with the column block fastest so that the CTAs running
@@ -84,11 +84,11 @@ template <int WF, bool PAIR> struct Cfg {
   static constexpr uint32_t B_BYTES = B_ROWS * BK * 2;                   // bf16 B per CTA per stage
   static constexpr int ROW_BYTES = WF == W_NF4 ? BK / 2 : (WF == W_INT8 ? BK : 0);  // raw bytes / 64 elements
   static constexpr uint32_t RAW_BYTES = B_ROWS * ROW_BYTES;
-  // WIDE (NF4 on CTA pairs): 16 dequantiser warps, with the registers split per
+  // WIDE (NF4 / INT8 on CTA pairs): 16 dequantiser warps, with the registers split per
   // warpgroup (setmaxnreg) so that they fit beside the epilogue.  Warps:
   //   WIDE:  0 TMA producer, 1 MMA, 2 raw-code producer, 3 spare | 4..7 epilogue | 8..23 dequant
   //   else:  0 TMA producer, 1 MMA, 2.. epilogue, then dequant (8 warps), then raw-code producer
-  static constexpr bool WIDE = WF == W_NF4 && PAIR;
+  static constexpr bool WIDE = QUANT && PAIR;
   static constexpr int DEQ_WARPS = WIDE ? 16 : (QUANT ? 8 : 0);
   static constexpr int DEQ_THREADS = 32 * DEQ_WARPS;
   // Dequantisers: one thread per B row and k-block; KG groups of B_ROWS
@@ -97,7 +97,7 @@ template <int WF, bool PAIR> struct Cfg {
   static constexpr int GROUP_WARPS = QUANT ? B_ROWS / 32 : 0;            // dequant warps per group
   static constexpr int STAGES = WF == W_BF16 ? (PAIR ? 6 : 4) : (PAIR ? 4 : 3);
   // raw-code ring: its own producer warp runs ahead of the operand ring
-  static constexpr int RAW_STAGES = WF == W_BF16 ? 1 : (PAIR ? (WF == W_NF4 ? 8 : 6) : (WF == W_NF4 ? 4 : 2));
+  static constexpr int RAW_STAGES = WF == W_BF16 ? 1 : (PAIR ? (WF == W_NF4 ? 8 : 4) : (WF == W_NF4 ? 4 : 2));
   static constexpr int EPI_WARPS = epi_warps(WF);
   static constexpr int EPI_FIRST = WIDE ? 4 : 2;
   static constexpr int DEQ_FIRST = WIDE ? 8 : 2 + EPI_WARPS;
