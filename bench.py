@@ -53,7 +53,7 @@ LORA_RANK = 16
 # DRAM bytes (read + write) of one gate/up launch from an ncu capture of the
 # same kernel on the same workload (profiles/ holds the capture's summary and
 # its command).  Workloads not captured report null.
-NCU_TRAFFIC = {"c2-gateup": 363_761_920 + 162_679_296}
+NCU_TRAFFIC = {"c2-gateup": 363_831_552 + 166_611_712}
 
 
 def load_peaks():
