@@ -51,3 +51,29 @@ def test_host_side_validation_without_gpu():
     assert lib.mirai_dispatch_plan_workspace_bytes(1000, 2, 8) == 8 * 4  # one 2048-route chunk
     with pytest.raises(_lib.MiraiError):
         _lib.call("mirai_moe_combine", None, None, None, 4, 0, 8, None, 0, None)
+
+
+def test_exchange_entry_points_validate_on_the_host():
+    """The expert-parallel exchange helpers reject bad arguments before any CUDA call."""
+    import ctypes
+
+    from mirai_b200 import _lib
+
+    lib = _lib.load()
+    off = ctypes.c_uint64(0)
+    handle = (ctypes.c_uint8 * 64)()
+    assert lib.mirai_ipc_export(None, handle, ctypes.byref(off)) == 1
+    assert lib.mirai_ipc_import(None, 0, None, None) == 1
+    assert lib.mirai_ipc_release(None) == 0                     # nothing to release
+    assert lib.mirai_copy_async(None, None, 0, None) == 0        # zero bytes: no copy
+    assert lib.mirai_copy_async(None, None, 16, None) == 1
+    slots = (_lib.c_vp * 2)()
+    assert lib.mirai_ep_signal(slots, 0, 1, None) == 1           # no slots
+    assert lib.mirai_ep_signal(slots, 65, 1, None) == 1          # more peers than supported
+    assert lib.mirai_ep_wait(None, 2, 0, 1, None) == 1
+    assert lib.mirai_ep_wait(_lib.c_vp(8 * 1024 + 4), 2, 0, 1, None) == 1  # flags not 8-byte aligned
+    assert lib.mirai_b200_set_gemm_sm_limit(1) == 1
+    assert lib.mirai_b200_set_gemm_sm_limit(-2) == 1
+    assert lib.mirai_b200_set_gemm_sm_limit(0) == 0
+    rc = lib.mirai_moe_gateup_swiglu_src_bf16(None, None, 0, 4, 128, 256, 256, None, None, None, None, None)
+    assert rc == 1 and b"sources" in lib.mirai_b200_last_error()
