@@ -9,13 +9,18 @@ fp32 router top-k on precomputed gate logits -> dispatch plan -> permute ->
 gate/up grouped GEMM + SwiGLU (fused NF4 dequant) -> down grouped GEMM (fused
 NF4 dequant) -> weighted combine.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c0..c4] [--mode fwd|train]
+                    [--impl ours|reference] [--ep-transport ipc|nccl] [--ep-chunks C]
 
-Under torchrun (N > 1) the layer runs expert-parallel (mirai_b200.expert_parallel):
-each rank owns E/N experts and routes its own tokens, with one NCCL all-to-all
-each way per layer.  c1-c3 keep their token count per rank (scaling "weak":
-per-GPU GEMM work is that of one GPU); c4 is BASELINE config 4, a 16-layer
-stack over 65536 tokens in total (scaling "strong").
+``--mode train`` (one GPU) runs BASELINE config 2's full step: forward, dX
+backward through the frozen experts and a rank-16 LoRA on w2 with its factor
+gradients.  Under torchrun (N > 1) the layer runs expert-parallel
+(mirai_b200.expert_parallel): each rank owns E/N experts and routes its own
+tokens; rows move by copy engines into peer-mapped buffers (``ipc``, default)
+or by NCCL all-to-all, in C chunks whose exchanges overlap the GEMMs.  c1-c3
+keep their token count per rank (scaling "weak": per-GPU GEMM work is that of
+one GPU); c4 is BASELINE config 4, a 16-layer stack over 65536 tokens in total
+(scaling "strong", also runnable on one GPU).
 ``--impl reference`` times the CPU restatement of the reference's torch path
 (``oracle/``) on the host cores, rank 0 only.
 """
