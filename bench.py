@@ -451,7 +451,9 @@ def run_ep(args, cfg, rank, world, dev):
         # one-element arrival all-reduce) so the exchanges overlap the GEMMs
         ops.set_gemm_sm_limit(torch.cuda.get_device_properties(dev).multi_processor_count - free_sms)
     if ipc:
-        layer = ExpertParallelMoE(shard, top_k=k, inter=I, chunks=chunks, ops=stepops)
+        layer = ExpertParallelMoE(shard, top_k=k, inter=I, chunks=chunks, ops=stepops,
+                                  copy_streams=args.ep_copy_streams, layout=args.ep_layout,
+                                  regroup=args.ep_regroup)
         ep = layer.forward
     else:
         layer = None
@@ -556,8 +558,9 @@ def run_ep(args, cfg, rank, world, dev):
             "tokens_total": T_total, "hidden": H, "experts": E, "experts_per_gpu": shard.local, "top_k": k,
             "intermediate": I, "layers": layers, "weights": cfg["fmt"],
             "parallelism": f"ep{world}: experts sharded by contiguous blocks, tokens sharded by rank, " + (
-                "copy-engine transfers into peer-mapped buffers (CUDA IPC over NVLink) with a one-element "
-                "NCCL all-reduce per chunk marking arrival" if ipc else "NCCL all_to_all_single dispatch and return")
+                f"copy-engine transfers into {args.ep_layout}-major peer-mapped receive buffers (CUDA IPC over "
+                f"NVLink, {args.ep_copy_streams} copy stream(s), regroup {args.ep_regroup}), arrival marked by "
+                "epoch flags in the peers' buffers" if ipc else "NCCL all_to_all_single dispatch and return (source-major segments)")
                 + (f"; {chunks} chunks per layer, exchanges on a second stream overlapping the GEMMs"
                    f" (GEMMs capped at {torch.cuda.get_device_properties(dev).multi_processor_count - free_sms} SMs)"
                    if chunks > 1 and world > 1 else ""),
@@ -734,6 +737,14 @@ def main():
                     help="N > 1: token chunks per layer whose exchanges overlap the other chunks' GEMMs")
     ap.add_argument("--ep-free-sms", type=int, default=None,
                     help="N > 1: SMs the GEMMs leave free for communication kernels (default 2 ipc, 16 nccl)")
+    ap.add_argument("--ep-layout", default="source", choices=["expert", "source"],
+                    help="ipc transport: receive rows expert-major (a copy per (peer, expert) block) or "
+                         "source-major (a copy per peer; G segments per expert in the GEMMs)")
+    ap.add_argument("--ep-regroup", default="auto", choices=["never", "auto", "always"],
+                    help="ipc transport, source-major layout: owners regroup received rows expert-major before "
+                         "the GEMMs where that saves more GEMM time than the two row gathers cost")
+    ap.add_argument("--ep-copy-streams", type=int, default=1,
+                    help="ipc transport: side streams a chunk's copy blocks are spread over (by peer)")
     ap.add_argument("--ep-transport", default="ipc", choices=["ipc", "nccl"],
                     help="N > 1: copy-engine transfers into peer-mapped buffers, or NCCL all_to_all_single")
     args = ap.parse_args()

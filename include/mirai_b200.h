@@ -103,6 +103,11 @@ int mirai_ipc_export(const void* ptr, void* handle, uint64_t* offset);
 int mirai_ipc_import(const void* handle, uint64_t offset, void** ptr, void** base);
 int mirai_ipc_release(void* base);
 int mirai_copy_async(void* dst, const void* src, uint64_t bytes, mirai_stream_t stream);
+/* `count` such copies, block i from src[i] to dst[i] of bytes[i] bytes (host
+ * arrays of device addresses), issued in order on `stream`, one
+ * cudaMemcpyAsync each; zero-byte blocks are skipped. */
+int mirai_copy_blocks(int32_t count, const uint64_t* dst, const uint64_t* src, const uint64_t* bytes,
+                      mirai_stream_t stream);
 /* Arrival flags of that exchange: mirai_ep_signal stores `epoch` (release,
  * system scope) into each of `count` 8-byte slots given by device pointers
  * (a rank's slot in every peer's flag array; NULL entries skipped), after the

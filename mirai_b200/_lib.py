@@ -59,6 +59,7 @@ SIGNATURES = {
     "mirai_ipc_import": (ctypes.c_int, [c_vp, ctypes.c_uint64, ctypes.POINTER(c_vp), ctypes.POINTER(c_vp)]),
     "mirai_ipc_release": (ctypes.c_int, [c_vp]),
     "mirai_copy_async": (ctypes.c_int, [c_vp, c_vp, ctypes.c_uint64, c_vp]),
+    "mirai_copy_blocks": (ctypes.c_int, [c_i32, c_vp, c_vp, c_vp, c_vp]),
     "mirai_ep_signal": (ctypes.c_int, [ctypes.POINTER(c_vp), c_i32, ctypes.c_uint64, c_vp]),
     "mirai_ep_wait": (ctypes.c_int, [c_vp, c_i32, c_i32, ctypes.c_uint64, c_vp]),
     "mirai_dispatch_plan_workspace_bytes": (c_size, [c_i64, c_i32, c_i32]),

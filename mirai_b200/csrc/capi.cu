@@ -149,6 +149,22 @@ int mirai_copy_async(void* dst, const void* src, uint64_t bytes, mirai_stream_t 
   return MIRAI_OK;
 }
 
+int mirai_copy_blocks(int32_t count, const uint64_t* dst, const uint64_t* src, const uint64_t* bytes,
+                      mirai_stream_t stream) {
+  if (count < 0 || (count > 0 && (!dst || !src || !bytes)))
+    return mirai::set_error(MIRAI_ERR_INVALID_ARG, "copy_blocks: bad block list");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (int32_t i = 0; i < count; ++i) {
+    if (bytes[i] == 0) continue;
+    if (!dst[i] || !src[i]) return mirai::set_error(MIRAI_ERR_INVALID_ARG, "copy_blocks: null address in block %d", i);
+    cudaError_t e = cudaMemcpyAsync(reinterpret_cast<void*>(dst[i]), reinterpret_cast<const void*>(src[i]),
+                                    (size_t)bytes[i], cudaMemcpyDefault, s);
+    if (e != cudaSuccess)
+      return mirai::set_error(MIRAI_ERR_CUDA, "copy_blocks: block %d: %s", i, cudaGetErrorString(e));
+  }
+  return MIRAI_OK;
+}
+
 int mirai_b200_set_gemm_sm_limit(int32_t max_sms) {
   if (max_sms < 0 || max_sms == 1)
     return mirai::set_error(MIRAI_ERR_INVALID_ARG, "set_gemm_sm_limit: %d (use 0 for no limit, or >= 2)", max_sms);

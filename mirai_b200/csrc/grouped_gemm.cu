@@ -309,11 +309,14 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   constexpr uint32_t A_STAGE = C::A_STAGE;
   constexpr bool QUANT = WF != W_BF16;
   constexpr bool MN = MCfg<MODE>::MN;
-  // NF4 on CTA pairs, K-major: each tile's absmax codes (one contiguous run of
-  // B_ROWS x K/64 bytes) are bulk-copied by the raw-code producer into one of
-  // two buffers ahead of use, so the dequantisers never stop to stage them.
-  constexpr bool PREFETCH = WF == W_NF4 && PAIR && !MN;
-  constexpr int ABUF = 8192;  // bytes per prefetch buffer: B_ROWS x K/64 with K <= 4096
+  // NF4 on CTA pairs: each tile's absmax codes reach one of two buffers a
+  // tile ahead of use, so the dequantisers never stop to stage them.  K-major,
+  // they are one contiguous run of B_ROWS x K/64 bytes, bulk-copied by the
+  // raw-code producer; MN-major, K rows of B_ROWS/64 bytes strided by the
+  // weight row, gathered by the spare warp of warpgroup 0.
+  constexpr bool PREFETCH = WF == W_NF4 && PAIR;
+  constexpr int ABUF = 8192;  // bytes per prefetch buffer: B_ROWS x K/64 or K x B_ROWS/64, K <= 4096
+  static_assert(!PREFETCH || (C::WIDE && C::RAW_WARP == 2), "the MN gatherer is warp 3 of the wide layout");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = base;
@@ -381,7 +384,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         mbar_init(&sm.raw_empty[s], C::GROUP_WARPS);
       }
       for (int a = 0; a < 2; ++a) {
-        mbar_init(&sm.absq_full[a], 1);
+        mbar_init(&sm.absq_full[a], MN ? 32 : 1);  // MN: every lane of the gathering warp
         mbar_init(&sm.absq_empty[a], C::DEQ_WARPS);
         mbar_init(&sm.tfull[a], 1);
         mbar_init(&sm.tempty[a], C::EPI_WARPS * pair_mult);
@@ -711,7 +714,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++tl) {
         int j, e, m, n;
         decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
-        if (PREFETCH) {
+        if (PREFETCH && !MN) {
           const int buf = tl & 1;
           if (tl >= 2 && !mbar_wait(&sm.absq_empty[buf], ((tl >> 1) - 1) & 1, 13)) {
             *abort_flag = 1;
@@ -758,6 +761,45 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           }
         }
       }
+    }
+  };
+  auto role_absq = [&]() {
+    // ======================= absmax gatherer (NF4 pair, MN-major) =======================
+    // buffer[kk * NB + j] = absmax code of (k-row kk, this CTA's column block j),
+    // filled a tile ahead of the dequantisers (buffers are released by them).
+    constexpr int NB = C::B_ROWS / 64;
+    const int nblk_row = p.N / 64;  // NF4 blocks per weight row
+    int tl = 0;
+    for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++tl) {
+      int j, e, m, n;
+      decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
+      const int buf = tl & 1;
+      if (tl >= 2 && !mbar_wait(&sm.absq_empty[buf], ((tl >> 1) - 1) & 1, 14)) {
+        *abort_flag = 1;
+        break;
+      }
+      uint8_t* dst = dq->absq + buf * ABUF;
+      const int nb0 = n * (TN / 64) + (int)rank * NB;  // first column block of this CTA (even)
+      static_assert(!(PREFETCH && MN) || NB == 2, "one 16-bit load covers this CTA's two column blocks");
+      if (NB == 2 && (nblk_row & 1) == 0 && nb0 + 1 < nblk_row) {
+        // both codes of a k-row in one aligned 16-bit load, four k-rows in flight per lane
+#pragma unroll 4
+        for (int kk = lane; kk < p.K; kk += 32) {
+          const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
+          const uint8_t* src = p.q[key].absmax + ((size_t)e * p.krows + (kk - key * p.krows)) * nblk_row + nb0;
+          reinterpret_cast<uint16_t*>(dst)[kk] = __ldg(reinterpret_cast<const uint16_t*>(src));
+        }
+      } else {
+#pragma unroll 1
+        for (int kk = lane; kk < p.K; kk += 32) {
+          const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
+          const uint8_t* src = p.q[key].absmax + ((size_t)e * p.krows + (kk - key * p.krows)) * nblk_row;
+#pragma unroll
+          for (int jj = 0; jj < NB; ++jj)
+            dst[kk * NB + jj] = nb0 + jj < nblk_row ? __ldg(src + nb0 + jj) : (uint8_t)0;
+        }
+      }
+      mbar_arrive(&sm.absq_full[buf]);  // release: this lane's stores are visible to the waiters
     }
   };
   auto role_dequant = [&]() {
@@ -892,7 +934,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
               const int nbg = n * (TN / 64) + nbase + nbq;
               live = nbg < nblk_row;
               blk = wr * nblk_row + nbg;
-              qcode = dq->absq[kk * (C::B_ROWS / 64) + nbq];
+              qcode = dq->absq[(PREFETCH ? abuf * ABUF : 0) + kk * (C::B_ROWS / 64) + nbq];
             }
             const float nabs = PREFETCH ? __ldg(p.q[key].nested_absmax + (size_t)e * p.q[key].n_nested +
                                                 (blk >> p.nbs_shift))
@@ -940,6 +982,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       if (warp == 0) role_producer();
       else if (warp == 1) role_mma();
       else if (warp == C::RAW_WARP) role_raw();
+      else if (PREFETCH && MN && warp == 3) role_absq();
     } else if (warp < 8) {
       setmaxnreg_inc<C::REG_EPI>();
       role_epilogue();

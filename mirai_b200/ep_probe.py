@@ -2,13 +2,17 @@
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
         --master-port P -m mirai_b200.ep_probe bandwidth
-    python -m torch.distributed.run ... -m mirai_b200.ep_probe phases --config c2|c4
+    python -m torch.distributed.run ... -m mirai_b200.ep_probe blocks
+    python -m torch.distributed.run ... -m mirai_b200.ep_probe phases --config c2|c4 [--layout expert|source]
 
 ``bandwidth``: bytes that cross NVLink per rank per second for NCCL's
 all_to_all_single and for copy-engine transfers into peer-mapped buffers (the
-layer's ``ipc`` transport), on equal-sized blocks.  ``phases``: CUDA-event
-times between the phases of one ``ExpertParallelMoE`` layer (1 chunk) on
-rank 0, averaged over 10 layers after 3 warm-up layers.
+layer's ``ipc`` transport), on equal-sized blocks.  ``blocks``: the same
+copy-engine exchange (128 MB per rank) split into 1 to 128 copies per peer, on
+one or two streams — the cost of a copy.  ``phases [--layout expert|source]
+[--copy-streams S] [--regroup never|auto|always]``: CUDA-event times between the phases of one
+``ExpertParallelMoE`` layer (1 chunk) on rank 0, averaged over 10 layers after
+3 warm-up layers.
 """
 
 from __future__ import annotations
@@ -80,7 +84,69 @@ def _bandwidth(dev, world, rank):
     return res
 
 
-def _phases(dev, world, rank, config):
+def _blocks(dev, world, rank):
+    """Copy-engine exchange of a fixed byte count per peer, split into n equal
+    blocks per peer (one cudaMemcpyAsync each), on 1 or 2 streams."""
+    import numpy as np
+    from . import _lib
+    from .expert_parallel import PeerBuffers
+    res = {}
+    blk = 134_217_728 // world          # bytes this rank sends each peer: 128 MB per rank in all
+    pb = PeerBuffers()
+    ptrs = pb.ensure(blk * world, dev)
+    data = [p + PeerBuffers.FLAG_BYTES for p in ptrs]
+    x = torch.empty(blk * world, dtype=torch.uint8, device=dev)
+    slots = (_lib.c_vp * world)(*[None if j == rank else ptrs[j] + 8 * rank for j in range(world)])
+    main = torch.cuda.current_stream()
+    sides = [torch.cuda.Stream() for _ in range(2)]
+    epoch = [0]
+    for nb in (1, 16, 64, 128):
+        piece = blk // nb
+        dst = np.array([data[j] + rank * blk + i * piece for j in range(world) for i in range(nb)], np.uint64)
+        src = np.array([x.data_ptr() + j * blk + i * piece for j in range(world) for i in range(nb)], np.uint64)
+        nbytes = np.full(len(dst), piece, np.uint64)
+        peer = np.repeat(np.arange(world), nb)
+        for ns in (1, 2):
+            def exchange():
+                start = torch.cuda.Event()
+                start.record(main)
+                for i in range(ns):
+                    sel = (peer % ns) == i
+                    st = sides[i] if ns > 1 else main
+                    if ns > 1:
+                        st.wait_event(start)
+                    d, s_, b = (np.ascontiguousarray(a[sel]) for a in (dst, src, nbytes))
+                    _lib.call("mirai_copy_blocks", len(b), d.ctypes.data, s_.ctypes.data, b.ctypes.data,
+                              _lib.c_vp(st.cuda_stream))
+                    if ns > 1:
+                        ev = torch.cuda.Event()
+                        ev.record(st)
+                        main.wait_event(ev)
+                epoch[0] += 1
+                _lib.call("mirai_ep_signal", slots, world, epoch[0], _lib.c_vp(main.cuda_stream))
+                _lib.call("mirai_ep_wait", _lib.c_vp(ptrs[rank]), world, rank, epoch[0], _lib.c_vp(main.cuda_stream))
+
+            for _ in range(3):
+                exchange()
+            torch.cuda.synchronize()
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(10):
+                exchange()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / 10
+            remote = blk * (world - 1)
+            res[f"{nb} blocks/peer, {ns} stream(s)"] = {"block_bytes": piece, "ms": round(ms, 3),
+                                                        "GBps": round(remote / ms / 1e6, 1)}
+    from .ops import check_device
+    check_device()
+    pb.release()
+    return res
+
+
+def _phases(dev, world, rank, config, layout="source", copy_streams=1, regroup="auto"):
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     import bench
     from .expert_parallel import ExpertParallelMoE, ExpertShard, shard_tokens
@@ -90,7 +156,8 @@ def _phases(dev, world, rank, config):
     b, e = shard_tokens(T_total, world, rank)
     shard = ExpertShard(cfg["E"], world, rank)
     x, logits, stack = bench.make_ep_workload(cfg, dev, rank, shard, e - b)
-    layer = ExpertParallelMoE(shard, top_k=cfg["k"], inter=cfg["I"], chunks=1)
+    layer = ExpertParallelMoE(shard, top_k=cfg["k"], inter=cfg["I"], chunks=1, layout=layout,
+                              copy_streams=copy_streams, regroup=regroup)
     events = []
 
     def hook(name, stream):  # records at its point in the stream
@@ -113,14 +180,18 @@ def _phases(dev, world, rank, config):
             name = events[i][0]
             acc[name] = acc.get(name, 0.0) + events[i - 1][1].elapsed_time(events[i][1]) / 10
     layer.close()
-    return {"config": config, "world": world, "tokens_rank0": e - b,
+    return {"config": config, "world": world, "tokens_rank0": e - b, "layout": layout, "copy_streams": copy_streams,
+            "regroup": regroup,
             "phases_ms": {k: round(v, 3) for k, v in acc.items()}, "layer_ms": round(sum(acc.values()), 3)}
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["bandwidth", "phases"])
+    ap.add_argument("what", choices=["bandwidth", "blocks", "phases"])
     ap.add_argument("--config", default="c2")
+    ap.add_argument("--layout", default="source", choices=["expert", "source"])
+    ap.add_argument("--copy-streams", type=int, default=1)
+    ap.add_argument("--regroup", default="auto", choices=["never", "auto", "always"])
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -128,7 +199,12 @@ def main():
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     try:
-        res = _bandwidth(dev, world, rank) if args.what == "bandwidth" else _phases(dev, world, rank, args.config)
+        if args.what == "bandwidth":
+            res = _bandwidth(dev, world, rank)
+        elif args.what == "blocks":
+            res = _blocks(dev, world, rank)
+        else:
+            res = _phases(dev, world, rank, args.config, args.layout, args.copy_streams, args.regroup)
         if rank == 0:
             print(json.dumps(res), flush=True)
     finally:

@@ -15,8 +15,10 @@ rows arrive source-major, each source's rows in expert order; the grouped
 GEMMs take those G x E/G (source, expert) segments as they are (weight =
 expert, tiles visited expert-major), so the owner neither re-sorts nor
 restores the order, and its output goes back through the reverse all-to-all
-in the layout the token owner sent.  Per row the products are those of the
-single-GPU layer, so the result is identical to it.  The reference runs MoE
+in the layout the token owner sent.  (``ExpertParallelMoE``, the copy-engine
+transport, places the blocks expert-major instead, so the GEMMs see one
+segment per expert.)  Per row the products are those of the single-GPU layer,
+so the result is identical to it.  The reference runs MoE
 on one GPU (it has no expert parallelism); the exchange is this package's.
 (Receiving each (rank, expert) block straight into an expert-major layout
 with grouped NCCL send/recv was measured slower on B200 than one
@@ -231,6 +233,149 @@ def shard_tokens(num_tokens: int, world: int, rank: int) -> tuple[int, int]:
     return begin, begin + base + (1 if rank < extra else 0)
 
 
+@dataclass
+class BlockPlan:
+    """Where every block of one rank's copy-engine exchange goes.
+
+    Rows are counted, not bytes.  A "dispatch" block moves this rank's rows of
+    one chunk for one (owner, local expert) from its permuted send rows to the
+    owner's receive region; a "return" block moves the owner's results for one
+    (source, local expert) of a chunk back to the source's return region.  Each
+    block list is four int64 arrays: peer rank, row in the peer's region, row
+    in this rank's chunk rows, row count."""
+
+    in_cap: int                   # receive region rows, the same on every rank
+    ret_cap: int                  # return region rows, the same on every rank
+    in_base: list[int]            # first row of chunk c in this rank's receive region
+    in_rows: list[int]            # rows this rank receives in chunk c
+    ret_base: list[int]           # first row of chunk c in this rank's return region
+    ret_rows: list[int]           # rows this rank sends (and gets back) in chunk c
+    gemm_ends: list[list[int]]    # [chunk][segment] running row ends of the receive rows
+    sources: int                  # segments per expert in gemm_ends (1: expert-major; G: source-major)
+    dispatch: list[tuple]         # per chunk: (peer, peer_row, my_row, rows)
+    give_back: list[tuple]        # per chunk: (peer, peer_row, my_row, rows)
+    # per chunk, source-major layout only: None, or the running ends of the
+    # expert segments when the owner regroups the chunk's received rows
+    # expert-major before its GEMMs (``regroup_order``)
+    regroup: list = None
+
+
+def _merge_runs(peer, peer_row, my_row, rows):
+    """Join consecutive blocks that continue each other on both sides."""
+    import numpy as np
+    if len(rows) < 2:
+        return peer, peer_row, my_row, rows
+    cont = (peer[1:] == peer[:-1]) & (peer_row[1:] == peer_row[:-1] + rows[:-1]) & \
+        (my_row[1:] == my_row[:-1] + rows[:-1])
+    start = np.concatenate([[True], ~cont])
+    idx = np.nonzero(start)[0]
+    return peer[idx], peer_row[idx], my_row[idx], np.add.reduceat(rows, idx)
+
+
+# Costs that decide whether an owner regroups a chunk's received rows (two row
+# gathers through HBM) to save the 256-row GEMM tiles that source boundaries
+# cut: measured on B200 for the NF4 grouped GEMMs and the row-gather kernel.
+GEMM_FLOPS_PER_S = 1.0e15
+GATHER_BYTES_PER_S = 6.0e12
+TILE_ROWS = 256
+
+
+def regroup_pays(L, hidden: int, inter: int, row_bytes: int) -> bool:
+    """L [sources, experts] rows of one received chunk, source-major.  True if
+    regrouping them expert-major (a gather of the rows there and one of the
+    results back) costs less than the GEMM tiles it saves."""
+    import numpy as np
+    L = np.asarray(L, dtype=np.int64)
+    tiles_src = int(((L + TILE_ROWS - 1) // TILE_ROWS).sum())
+    tiles_exp = int(((L.sum(axis=0) + TILE_ROWS - 1) // TILE_ROWS).sum())
+    saved = (tiles_src - tiles_exp) * 6.0 * TILE_ROWS * hidden * inter / GEMM_FLOPS_PER_S
+    cost = 2 * 2 * int(L.sum()) * row_bytes / GATHER_BYTES_PER_S  # two gathers, each a read and a write
+    return saved > cost
+
+
+def regroup_order(L: torch.Tensor, total: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(order, inverse) for the ``total`` rows of one chunk received
+    source-major with L [sources, experts] rows per segment (a tensor on the
+    rows' device, so no host round trip): rows ``order`` of the chunk are its
+    rows expert-major (source order inside an expert); ``inverse[order[i]] = i``."""
+    L = L.to(torch.int64)
+    flat = L.reshape(-1)
+    start = (torch.cumsum(flat, 0) - flat).view(L.shape)        # source-major start of each (s, e)
+    lens = L.t().reshape(-1)                                     # expert-major segment order (e, s)
+    starts = start.t().reshape(-1)
+    shift = starts - (torch.cumsum(lens, 0) - lens)
+    rows = torch.arange(total, dtype=torch.int64, device=L.device)
+    order = torch.repeat_interleave(shift, lens, output_size=total) + rows
+    inverse = torch.empty_like(order).scatter_(0, order, rows)
+    return order, inverse
+
+
+def exchange_blocks(M, rank: int, layout: str = "expert", *, regroup: str = "never", hidden: int = 0,
+                    inter: int = 0, row_bytes: int = 0) -> BlockPlan:
+    """Block plan of ``rank`` for the count tensor M [source, dest, chunk, local
+    expert] (rows every rank sends every owner, per chunk and owner's expert),
+    which every rank holds after the count gather.
+
+    ``layout`` "expert": receive regions are expert-major — chunk c of owner d
+    holds, for each of its experts in turn, that expert's rows from source 0,
+    1, ... in order, so the owner's grouped GEMMs see one contiguous segment
+    per expert (tiles are not split at source boundaries), at the price of one
+    copy per (peer, expert) block.  "source": source-major — each source's rows
+    of the chunk in one run, in expert order, one copy per peer and chunk; the
+    GEMMs then take G x E/G (source, expert) segments (``gemm_ends`` holds G*El
+    ends per chunk).  A source's send rows of a chunk are ordered by global
+    expert (the dispatch plan's order), i.e. by owner, then local expert; its
+    return region uses the same order, so the combine reads it like the
+    single-GPU layer's expert output.  Blocks that continue each other on both
+    sides are merged into one copy.
+
+    ``regroup`` ("never", "auto", "always"; source-major layout only): whether
+    the owner regroups a chunk's received rows expert-major before its GEMMs
+    (``BlockPlan.regroup``); "auto" does so where ``regroup_pays`` for the
+    layer's ``hidden``/``inter`` sizes and ``row_bytes``."""
+    import numpy as np
+    if layout not in ("expert", "source"):
+        raise ValueError(f"layout must be 'expert' or 'source', not {layout!r}")
+    M = np.asarray(M, dtype=np.int64)
+    G, _, C, El = M.shape
+    R = M.sum(axis=(0, 3))                    # rows each owner receives [dest, chunk]
+    S = M.sum(axis=(1, 3))                    # rows each source sends [source, chunk]
+    in_base = np.concatenate([np.zeros((G, 1), np.int64), np.cumsum(R, axis=1)[:, :-1]], axis=1)
+    ret_base = np.concatenate([np.zeros((G, 1), np.int64), np.cumsum(S, axis=1)[:, :-1]], axis=1)
+    # send position of block (s, d, c, e) in s's chunk-c rows: order (d, e)
+    flat = M.transpose(0, 2, 1, 3).reshape(G, C, G * El)
+    send_pos = (np.cumsum(flat, axis=2) - flat).reshape(G, C, G, El).transpose(0, 2, 1, 3)
+    if layout == "expert":
+        # receive position of block (s, d, c, e) in d's chunk-c rows: order (e, s)
+        flat = M.transpose(1, 2, 3, 0).reshape(G, C, El * G)
+        recv_pos = (np.cumsum(flat, axis=2) - flat).reshape(G, C, El, G).transpose(3, 0, 1, 2)
+    else:
+        # order (s, e)
+        flat = M.transpose(1, 2, 0, 3).reshape(G, C, G * El)
+        recv_pos = (np.cumsum(flat, axis=2) - flat).reshape(G, C, G, El).transpose(2, 0, 1, 3)
+    me = rank
+    dispatch, give_back, ends = [], [], []
+    for c in range(C):
+        d, e = np.nonzero(M[me, :, c, :])
+        dispatch.append(_merge_runs(d, in_base[d, c] + recv_pos[me, d, c, e], send_pos[me, d, c, e], M[me, d, c, e]))
+        s, e = np.nonzero(M[:, me, c, :])
+        give_back.append(_merge_runs(s, ret_base[s, c] + send_pos[s, me, c, e], recv_pos[s, me, c, e],
+                                     M[s, me, c, e]))
+        seg = M[:, me, c, :].sum(axis=0) if layout == "expert" else M[:, me, c, :].reshape(-1)
+        ends.append(np.cumsum(seg).tolist())
+    groups = [None] * C
+    if layout == "source" and regroup != "never":
+        for c in range(C):
+            L = M[:, me, c, :]
+            if L.sum() and (regroup == "always" or regroup_pays(L, hidden, inter, row_bytes)):
+                groups[c] = np.cumsum(L.sum(axis=0)).tolist()
+    return BlockPlan(in_cap=int(R.sum(axis=1).max()), ret_cap=int(S.sum(axis=1).max()),
+                     in_base=in_base[me].tolist(), in_rows=R[me].tolist(),
+                     ret_base=ret_base[me].tolist(), ret_rows=S[me].tolist(),
+                     gemm_ends=ends, sources=1 if layout == "expert" else G, dispatch=dispatch,
+                     give_back=give_back, regroup=groups)
+
+
 class PeerBuffers:
     """One device buffer per rank of the group, mapped into every other rank
     (CUDA IPC; one process per GPU), so a rank can write its blocks straight
@@ -298,25 +443,38 @@ class ExpertParallelMoE:
 
     Same contract and result as ``ep_moe_forward``; the rows move differently:
     every rank maps every other rank's exchange buffer (``PeerBuffers``), a
-    token owner copies each of its per-owner blocks straight into that owner's
-    receive region (source-major, the layout the source-major GEMMs take) with
-    one cudaMemcpyAsync (copy engines, no SMs), and the owner copies each
-    source's results straight back into the token owner's return region.  A
-    one-element NCCL all-reduce after the copies of a chunk, on the same
-    stream, tells every rank that all of that chunk's blocks have landed.  With
-    ``chunks`` > 1 the copies of one chunk run beside the GEMMs of another.
+    token owner copies each of its (owner, expert) blocks straight into that
+    owner's receive region with one cudaMemcpyAsync each (copy engines, no
+    SMs), at the place ``exchange_blocks`` gives it: expert-major, so the
+    owner's GEMMs run one segment per expert and no 256-row tile is cut at a
+    source boundary.  The owner copies each (source, expert) block of results
+    straight back into the token owner's return region, in the order the token
+    owner sent.  With ``chunks`` > 1 the copies of one chunk run beside the
+    GEMMs of another; ``copy_streams`` > 1 spreads a chunk's blocks over that
+    many side streams by peer, so several copies are in flight at once.
+    ``layout="source"`` keeps the receive rows source-major instead (one copy
+    per peer and chunk; the GEMMs take G segments per expert).
     Arrival is signalled with flags in the peers' buffers: after a chunk's
     copies a rank stores the exchange's epoch into its slot of every peer's
     flag array, and a consumer's stream waits (bounded) for all its slots to
     reach the epoch before the GEMMs or the combine read the data."""
 
     def __init__(self, shard: ExpertShard, *, top_k: int, inter: int, group=None, chunks: int = 2,
-                 ops: StepOps | None = None):
+                 ops: StepOps | None = None, copy_streams: int = 1, layout: str = "source",
+                 regroup: str = "auto"):
         self.shard, self.top_k, self.inter, self.group = shard, top_k, inter, group
         self.chunks = max(1, int(chunks))
         self.ops = ops or CudaStepOps()
         self.buffers = PeerBuffers(group)
         self.comm: torch.cuda.Stream | None = None
+        if layout not in ("expert", "source"):
+            raise ValueError(f"layout must be 'expert' or 'source', not {layout!r}")
+        self.layout = layout
+        if regroup not in ("never", "auto", "always"):
+            raise ValueError(f"regroup must be 'never', 'auto' or 'always', not {regroup!r}")
+        self.regroup = regroup
+        self.n_copy_streams = max(1, int(copy_streams))
+        self.copy_streams: list[torch.cuda.Stream] = []  # side streams when n_copy_streams > 1
         self.epoch = 0  # exchanges so far; the same sequence on every rank
         # optional probe: called as on_phase(name, stream) at phase boundaries
         self.on_phase = None
@@ -324,9 +482,36 @@ class ExpertParallelMoE:
     def close(self) -> None:
         self.buffers.release()
 
-    def _copy(self, dst: int, src: int, nbytes: int, stream) -> None:
+    def _copy_blocks(self, blocks, peer_base: list[int], my_base: int, row_bytes: int, stream) -> None:
+        """Issue one block list of a ``BlockPlan`` on ``stream`` (or spread over
+        the side copy streams by peer, joined back into ``stream``)."""
+        import numpy as np
         from . import _lib
-        _lib.call("mirai_copy_async", _lib.c_vp(dst), _lib.c_vp(src), nbytes, _lib.c_vp(stream.cuda_stream))
+        peer, peer_row, my_row, rows = blocks
+        if len(rows) == 0:
+            return
+        rb = np.uint64(row_bytes)
+        dst = np.asarray(peer_base, dtype=np.uint64)[peer] + peer_row.astype(np.uint64) * rb
+        src = np.uint64(my_base) + my_row.astype(np.uint64) * rb
+        nbytes = rows.astype(np.uint64) * rb
+        n = len(self.copy_streams)
+        if n == 0:
+            _lib.call("mirai_copy_blocks", len(rows), dst.ctypes.data, src.ctypes.data, nbytes.ctypes.data,
+                      _lib.c_vp(stream.cuda_stream))
+            return
+        start = torch.cuda.Event()
+        start.record(stream)
+        for i, side in enumerate(self.copy_streams):
+            sel = (peer % n) == i
+            if not sel.any():
+                continue
+            side.wait_event(start)
+            d, s_, b = (np.ascontiguousarray(a[sel]) for a in (dst, src, nbytes))
+            _lib.call("mirai_copy_blocks", len(b), d.ctypes.data, s_.ctypes.data, b.ctypes.data,
+                      _lib.c_vp(side.cuda_stream))
+            done = torch.cuda.Event()
+            done.record(side)
+            stream.wait_event(done)
 
     def forward(self, tokens: torch.Tensor, logits: torch.Tensor, local_weights: Any) -> torch.Tensor:
         ops, shard, k = self.ops, self.shard, self.top_k
@@ -337,6 +522,8 @@ class ExpertParallelMoE:
             return ep_moe_forward(tokens, logits, local_weights, shard=shard, top_k=k, inter=self.inter, ops=ops)
         if self.comm is None:
             self.comm = torch.cuda.Stream(device=dev)
+            if self.n_copy_streams > 1:
+                self.copy_streams = [torch.cuda.Stream(device=dev) for _ in range(self.n_copy_streams)]
         comp, comm = torch.cuda.current_stream(dev), self.comm
         mark = self.on_phase or (lambda name, stream: None)
         mark("start", comp)
@@ -352,42 +539,25 @@ class ExpertParallelMoE:
         mine = torch.stack([p[1].counts.view(G, El) for p in prep], dim=1).contiguous()  # [dest, chunk, expert]
         allm = torch.empty((G,) + tuple(mine.shape), dtype=mine.dtype, device=dev)      # [source, dest, chunk, expert]
         dist.all_gather_into_tensor(allm, mine, group=self.group)
-        M = allm.cpu().numpy()
-        n = M.sum(axis=3)                                   # rows [source, dest, chunk]
-        R = n.sum(axis=0)                                   # rows each destination receives [dest, chunk]
-        S = n.sum(axis=1)                                   # rows each source sends [source, chunk]
         row_bytes = H * tokens.element_size()
-        in_cap = int(R.sum(axis=1).max()) * row_bytes       # receive region, the same on every rank
-        ret_cap = int(S.sum(axis=1).max()) * row_bytes      # return region
-        in_cap = (in_cap + 255) // 256 * 256
+        plan = exchange_blocks(allm.cpu().numpy(), me, self.layout, regroup=self.regroup, hidden=H,
+                               inter=self.inter, row_bytes=row_bytes)
+        in_cap = (plan.in_cap * row_bytes + 255) // 256 * 256
+        ret_cap = plan.ret_cap * row_bytes
         F = PeerBuffers.FLAG_BYTES
         ptrs = self.buffers.ensure(in_cap + ret_cap, dev)
         local = self.buffers.local[F:]
         data = [p + F for p in ptrs]
-
-        def in_base(d, c):      # rows before chunk c in d's receive region
-            return int(R[d, :c].sum())
-
-        def src_off(d, c, s):   # rows of sources < s in d's chunk-c receive block
-            return int(n[:s, d, c].sum())
-
-        def send_off(s, d, c):  # rows for destinations < d in s's chunk-c send order
-            return int(n[s, :d, c].sum())
-
-        def ret_base(s, c):     # rows before chunk c in s's return region
-            return int(S[s, :c].sum())
-
-        x_in = local[:in_cap].view(tokens.dtype)[: int(R[me].sum()) * H].view(-1, H)
-        y_ret = local[in_cap:in_cap + ret_cap].view(tokens.dtype)[: int(S[me].sum()) * H].view(-1, H)
-        offs = []
-        for c in range(C):
-            ends, run = [], 0
-            for s in range(G):
-                for e in range(El):
-                    run += int(M[s, me, c, e])
-                    ends.append(run)
-            offs.append(ends)
-        offs_dev = torch.tensor(offs, dtype=torch.int32).to(dev, non_blocking=True)
+        ret = [p + in_cap for p in data]
+        x_in = local[:in_cap].view(tokens.dtype)[: sum(plan.in_rows) * H].view(-1, H)
+        y_ret = local[in_cap:in_cap + ret_cap].view(tokens.dtype)[: sum(plan.ret_rows) * H].view(-1, H)
+        # segment ends per chunk: the received layout's, or the regrouped experts'
+        seg_ends = [plan.gemm_ends[c] if plan.regroup[c] is None else plan.regroup[c] for c in range(C)]
+        flat_ends = torch.tensor([v for ends in seg_ends for v in ends], dtype=torch.int32).to(dev, non_blocking=True)
+        offs_dev, pos = [], 0
+        for ends in seg_ends:
+            offs_dev.append(flat_ends[pos:pos + len(ends)])
+            pos += len(ends)
         mark("count gather + host read", comp)
 
         from . import _lib
@@ -413,36 +583,36 @@ class ExpertParallelMoE:
         for c in range(C):
             xs = prep[c][2]
             xs.record_stream(comm)
-            for d in range(G):
-                rows = int(n[me, d, c])
-                if rows:
-                    dst = data[d] + (in_base(d, c) + src_off(d, c, me)) * row_bytes
-                    self._copy(dst, xs.data_ptr() + send_off(me, d, c) * row_bytes, rows * row_bytes, comm)
+            self._copy_blocks(plan.dispatch[c], data, xs.data_ptr(), row_bytes, comm)
             landed.append(arrived(comm))
             mark(f"dispatch copies + arrival, chunk {c}", comm)
         returned = []
         for c in range(C):
             wait(landed[c])
-            rows_c = int(R[me, c])
-            xc = x_in[in_base(me, c):in_base(me, c) + rows_c]
-            yc = ops.experts(xc, offs_dev[c], local_weights, self.inter, sources=G) if rows_c else xc
+            rows_c = plan.in_rows[c]
+            xc = x_in[plan.in_base[c]:plan.in_base[c] + rows_c]
+            if not rows_c:
+                yc = xc
+            elif plan.regroup[c] is None:
+                yc = ops.experts(xc, offs_dev[c], local_weights, self.inter, sources=plan.sources)
+            else:
+                # expert-major for the GEMMs (no tile cut at a source boundary), then back
+                order, inverse = regroup_order(allm[:, me, c, :], rows_c)
+                ye = ops.experts(ops.permute(xc, order), offs_dev[c], local_weights, self.inter)
+                yc = ops.permute(ye, inverse)
             mark(f"gate/up + down GEMMs, chunk {c}", comp)
             done = torch.cuda.Event()
             done.record(comp)
             comm.wait_event(done)
             yc.record_stream(comm)
-            for s in range(G):
-                rows = int(n[s, me, c])
-                if rows:
-                    dst = data[s] + in_cap + (ret_base(s, c) + send_off(s, me, c)) * row_bytes
-                    self._copy(dst, yc.data_ptr() + src_off(me, c, s) * row_bytes, rows * row_bytes, comm)
+            self._copy_blocks(plan.give_back[c], ret, yc.data_ptr(), row_bytes, comm)
             returned.append(arrived(comm))
             mark(f"return copies + arrival, chunk {c}", comm)
         out = torch.empty((T, H), dtype=tokens.dtype, device=dev)
         for c, (b, e) in enumerate(bounds):
             wait(returned[c])
             if e > b:
-                yb = y_ret[ret_base(me, c):ret_base(me, c) + int(S[me, c])]
+                yb = y_ret[plan.ret_base[c]:plan.ret_base[c] + plan.ret_rows[c]]
                 out[b:e] = ops.combine(yb, prep[c][1].inverse_order, prep[c][0], k, tokens.dtype)
         mark("combine", comp)
         return out

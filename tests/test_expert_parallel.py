@@ -130,3 +130,89 @@ def test_shard_arithmetic():
     assert (s.local, s.first) == (16, 48)
     with pytest.raises(ValueError):
         ExpertShard(10, 4, 0)
+
+
+@pytest.mark.parametrize("layout", ["expert", "source"])
+@pytest.mark.parametrize("G,C,El,seed", [(2, 1, 4, 0), (4, 2, 3, 1), (8, 2, 16, 2), (3, 3, 2, 3), (2, 2, 2, 4)])
+def test_exchange_blocks_round_trip(G, C, El, seed, layout):
+    """Every rank's dispatch and return block lists, run on simulated memory,
+    put each owner's receive rows expert-major (source order inside an expert)
+    or source-major (expert order inside a source), and bring every source's
+    rows back in its send order."""
+    from mirai_b200.expert_parallel import exchange_blocks
+    rng = np.random.default_rng(seed)
+    M = rng.integers(0, 6, size=(G, G, C, El))
+    M[0, :, 0, :] = 0             # a source with nothing in one chunk
+    M[:, G - 1, C - 1, 0] = 0     # an expert that gets nothing in one chunk
+    if seed == 4:
+        M[:] = 0                  # an empty layer
+    plans = [exchange_blocks(M, r, layout) for r in range(G)]
+    assert len({(p.in_cap, p.ret_cap) for p in plans}) == 1
+
+    def label(s, d, c, e, i):
+        return (((s * G + d) * C + c) * El + e) * 1000 + i
+
+    send = [[np.array([label(s, d, c, e, i) for d in range(G) for e in range(El) for i in range(M[s, d, c, e])],
+                      dtype=np.int64) for c in range(C)] for s in range(G)]
+    recv = [np.full(plans[0].in_cap, -1, np.int64) for _ in range(G)]
+    for s in range(G):
+        for c in range(C):
+            for peer, prow, mrow, rows in zip(*plans[s].dispatch[c]):
+                assert rows > 0
+                recv[peer][prow:prow + rows] = send[s][c][mrow:mrow + rows]
+    for d in range(G):
+        p = plans[d]
+        assert p.in_base == np.concatenate([[0], np.cumsum(p.in_rows)[:-1]]).tolist()
+        for c in range(C):
+            got = recv[d][p.in_base[c]:p.in_base[c] + p.in_rows[c]]
+            if layout == "expert":
+                want = [label(s, d, c, e, i) for e in range(El) for s in range(G) for i in range(M[s, d, c, e])]
+                assert p.gemm_ends[c] == np.cumsum(M[:, d, c, :].sum(axis=0)).tolist() and p.sources == 1
+            else:
+                want = [label(s, d, c, e, i) for s in range(G) for e in range(El) for i in range(M[s, d, c, e])]
+                assert p.gemm_ends[c] == np.cumsum(M[:, d, c, :].reshape(-1)).tolist() and p.sources == G
+                assert len(p.dispatch[c][0]) == len(set(p.dispatch[c][0].tolist()))  # one copy per peer
+            assert got.tolist() == want
+    ret = [np.full(plans[0].ret_cap, -1, np.int64) for _ in range(G)]
+    for d in range(G):
+        p = plans[d]
+        for c in range(C):
+            yc = recv[d][p.in_base[c]:p.in_base[c] + p.in_rows[c]]   # the owner's output rows, same order
+            for peer, prow, mrow, rows in zip(*p.give_back[c]):
+                ret[peer][prow:prow + rows] = yc[mrow:mrow + rows]
+    for s in range(G):
+        p = plans[s]
+        for c in range(C):
+            assert ret[s][p.ret_base[c]:p.ret_base[c] + p.ret_rows[c]].tolist() == send[s][c].tolist()
+
+
+@pytest.mark.parametrize("G,El,seed", [(2, 4, 0), (8, 16, 1), (3, 5, 2)])
+def test_regroup_order_is_expert_major(G, El, seed):
+    """Rows received source-major, taken in ``order``, are expert-major with
+    source order kept inside an expert; ``inverse`` restores the received order."""
+    from mirai_b200.expert_parallel import regroup_order
+    rng = np.random.default_rng(seed)
+    L = rng.integers(0, 7, size=(G, El))
+    L[0, :] = 0
+    L[:, El - 1] = 0
+    labels = np.array([s * 1000 * El + e * 1000 + i for s in range(G) for e in range(El) for i in range(L[s, e])])
+    order, inverse = regroup_order(torch.from_numpy(L).to(torch.int32), int(L.sum()))
+    got = labels[order.numpy()]
+    want = [s * 1000 * El + e * 1000 + i for e in range(El) for s in range(G) for i in range(L[s, e])]
+    assert got.tolist() == want
+    assert np.array_equal(got[inverse.numpy()], labels)
+
+
+def test_regroup_cost_rule():
+    """The owner regroups where cut tiles cost more than moving the rows twice:
+    c4's shapes at 8 GPUs (about 256 rows per source and expert), not at 2."""
+    from mirai_b200.expert_parallel import exchange_blocks, regroup_pays
+    rng = np.random.default_rng(0)
+    H, I = 4096, 1536
+    assert regroup_pays(256 + rng.integers(-16, 16, size=(8, 16)), H, I, 2 * H)
+    assert not regroup_pays(1024 + rng.integers(-32, 32, size=(2, 64)), H, I, 2 * H)
+    M = 256 + rng.integers(-16, 16, size=(8, 8, 2, 16))
+    p = exchange_blocks(M, 3, "source", regroup="auto", hidden=H, inter=I, row_bytes=2 * H)
+    assert all(r is not None for r in p.regroup)
+    assert p.regroup[1] == np.cumsum(M[:, 3, 1, :].sum(axis=0)).tolist()
+    assert all(r is None for r in exchange_blocks(M, 3, "source").regroup)

@@ -43,7 +43,7 @@ def _rank_main(rank, world, port, cfg, results):
     try:
         from mirai_b200 import ops
         from mirai_b200.expert_parallel import ExpertShard, ep_moe_forward, shard_tokens
-        T, H, E, k, I, fmt, chunks, transport = cfg
+        T, H, E, k, I, fmt, chunks, transport, copy_streams, regroup = cfg
         g = torch.Generator(device=dev).manual_seed(11)
         x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
         logits = torch.randn(T, E, generator=g, device=dev) * 1.5
@@ -55,7 +55,8 @@ def _rank_main(rank, world, port, cfg, results):
         xr, lr = x[b:e].contiguous(), logits[b:e].contiguous()
         if transport == "ipc":
             from mirai_b200.expert_parallel import ExpertParallelMoE
-            layer = ExpertParallelMoE(shard, top_k=k, inter=I, chunks=chunks)
+            layer = ExpertParallelMoE(shard, top_k=k, inter=I, chunks=chunks, copy_streams=copy_streams,
+                                      regroup=regroup)
             out = layer.forward(xr, lr, local)
             out2 = layer.forward(xr, lr, local)  # buffers reused
             assert torch.equal(out, out2)
@@ -81,20 +82,24 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("fmt,chunks,transport", [
-    ("nf4", 1, "nccl"), ("bf16", 1, "nccl"), ("int8", 1, "nccl"), ("nf4", 3, "nccl"),
-    ("nf4", 1, "ipc"), ("nf4", 3, "ipc"), ("int8", 2, "ipc"), ("bf16", 2, "ipc"),
+@pytest.mark.parametrize("fmt,chunks,transport,copy_streams,world,regroup", [
+    ("nf4", 1, "nccl", 1, 2, "never"), ("bf16", 1, "nccl", 1, 2, "never"), ("int8", 1, "nccl", 1, 2, "never"),
+    ("nf4", 3, "nccl", 1, 2, "never"),
+    ("nf4", 1, "ipc", 1, 2, "never"), ("nf4", 3, "ipc", 1, 2, "always"), ("int8", 2, "ipc", 1, 2, "always"),
+    ("bf16", 2, "ipc", 3, 2, "auto"),
+    ("nf4", 2, "ipc", 2, 4, "always"), ("nf4", 2, "nccl", 1, 4, "never"),
 ])
-def test_expert_parallel_equals_single_gpu_layer(fmt, chunks, transport):
-    """nccl, chunks = 3: the pipelined all-to-all path (exchanges on a second
+def test_expert_parallel_equals_single_gpu_layer(fmt, chunks, transport, copy_streams, world, regroup):
+    """nccl, chunks > 1: the pipelined all-to-all path (exchanges on a second
     stream, GEMMs capped below the SM count); ipc: copy-engine transfers into
-    peer-mapped buffers."""
-    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    source-major peer-mapped buffers, on one stream or spread over side
+    streams, with the owner regrouping received rows expert-major ("always")
+    or not ("never")."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from mirai_b200.build import build
     build()
-    world = 2
-    cfg = (3000, 256, 8, 2, 384, fmt, chunks, transport)
+    cfg = (3000, 256, 8, 2, 384, fmt, chunks, transport, copy_streams, regroup)
     with mp.Manager() as mgr:
         results = mgr.dict()
         mp.start_processes(_rank_main, args=(world, _free_port(), cfg, results), nprocs=world, start_method="spawn")
