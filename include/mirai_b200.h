@@ -185,8 +185,11 @@ int mirai_moe_down_int8(const void* h, const int32_t* offsets, int32_t num_exper
  * The same two GEMMs when the rows of each expert come in num_sources separate
  * runs, as an expert owner receives them from its peers: `offsets` holds the
  * inclusive ends of num_sources * num_experts segments in memory order, segment
- * s * num_experts + e being source s's rows for (weight) expert e.  Tiles visit
- * the segments expert-major, so the weights of one expert stay hot in L2.  No
+ * s * num_experts + e being source s's rows for (weight) expert e.  Each
+ * segment is cut into 128-row blocks and an expert's blocks, of any sources, are
+ * paired into 256-row tiles (one per SM of a CTA pair), so a source boundary
+ * wastes at most part of a block; tiles visit the experts in order, so the
+ * weights of one expert stay hot in L2.  No
  * reference counterpart (the reference has no expert parallelism); with
  * num_sources = 1 these equal the entry points above. */
 int mirai_moe_gateup_swiglu_src_bf16(const void* x, const int32_t* offsets, int32_t num_sources,

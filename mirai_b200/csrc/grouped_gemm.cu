@@ -189,19 +189,41 @@ constexpr size_t smem_bytes() {
 // block n.  Segments are visited weight-expert-major (all sources of expert 0,
 // then of expert 1, ...) so that concurrent tiles share one expert's weights.
 template <int WF, bool PAIR>
-__device__ __forceinline__ void decode_tile(int t, const Smem<WF, PAIR>& sm, int E, int nsrc, int n_tiles, int& j,
+__device__ __forceinline__ void decode_tile(int t, const Smem<WF, PAIR>& sm, int units, int n_tiles, int& j,
                                             int& e, int& m, int& n) {
+  // units: segments (one source: segment = expert), or experts (several sources)
   const int mt = t / n_tiles;
   n = t - mt * n_tiles;
-  int lo = 0, hi = E;
+  int lo = 0, hi = units;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (sm.tile_prefix[mid] <= mt) lo = mid;
     else hi = mid;
   }
   j = lo;
-  e = lo / nsrc;
+  e = lo;
   m = mt - sm.tile_prefix[lo];
+}
+
+// Several sources: an expert's rows are its nsrc segments e*nsrc + s (tile
+// order), cut into BM-row blocks segment by segment; tile m of the expert takes
+// blocks m*BPT .. m*BPT + BPT-1 (BPT = CTAs per tile), so a CTA pair can hold
+// blocks of two sources and no tile is cut at a source boundary beyond a
+// block.  Block q: first memory row and rows (0 past the expert's last block).
+template <int WF, bool PAIR>
+__device__ __forceinline__ void source_block(const Smem<WF, PAIR>& sm, int e, int nsrc, int q, int& row, int& rows) {
+  for (int s = 0; s < nsrc; ++s) {
+    const int len = sm.seg_rows[e * nsrc + s];
+    const int nb = (len + BM - 1) / BM;
+    if (q < nb) {
+      row = sm.row_start[e * nsrc + s] + q * BM;
+      rows = min(BM, len - q * BM);
+      return;
+    }
+    q -= nb;
+  }
+  row = 0;
+  rows = 0;
 }
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
@@ -369,6 +391,29 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
     if (lane == 0) sm.tile_prefix[E] = carry;
+    if (nsrc > 1) {
+      // several sources: tiles per expert = its BM-row blocks over all its
+      // segments, CTAs-per-tile at a time; the prefix is over experts instead
+      constexpr int BPT = PAIR ? 2 : 1;
+      __syncwarp();  // the segment table above is complete
+      carry = 0;
+      for (int e0 = 0; e0 < wexp; e0 += 32) {
+        const int e = e0 + lane;
+        int blocks = 0;
+        if (e < wexp)
+          for (int s = 0; s < nsrc; ++s) blocks += (sm.seg_rows[e * nsrc + s] + BM - 1) / BM;
+        const int cnt = (blocks + BPT - 1) / BPT;
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        if (e < wexp) sm.tile_prefix[e] = carry + incl - cnt;
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+      }
+      if (lane == 0) sm.tile_prefix[wexp] = carry;
+    }
   }
   if (warp == 1) {
     if (lane == 0) {
@@ -419,7 +464,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   tc_fence_after();
 
   const uint32_t tmem_base = sm.tmem_base;
-  const int total_tiles = sm.tile_prefix[E] * p.n_tiles;
+  const int units = p.nsrc > 1 ? E / p.nsrc : E;  // tile-order units: segments, or experts
+  const int total_tiles = sm.tile_prefix[units] * p.n_tiles;
+  constexpr int BPT = PAIR ? 2 : 1;               // BM-row blocks per tile
+  static_assert(RT == 1, "source blocks assume one row sub-tile per tile");
   const int num_kb = p.K / BK;
   // the rank block of a fused LoRA adapter is one more k-block: A from tmap_xa
   // ([S, 64] bf16), B from tmap_xb (bf16, the layout of this mode's B)
@@ -434,10 +482,14 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       uint32_t phase = 0;
       for (int t = unit; t < total_tiles && !*abort_flag; t += num_units) {
         int j, e, m, n;
-        decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
-        const int row0 = sm.row_start[j] + m * TILE_M + (int)rank * BM;
+        decode_tile<WF, PAIR>(t, sm, units, p.n_tiles, j, e, m, n);
+        int row0 = sm.row_start[j] + m * TILE_M + (int)rank * BM;
+        if (p.nsrc > 1) {  // this CTA's block (a past-the-end block loads rows 0..: never stored)
+          int rows;
+          source_block(sm, e, p.nsrc, m * BPT + (int)rank, row0, rows);
+        }
         // sub-tiles holding rows of this segment (the first always does)
-        const int seg_rows = sm.seg_rows[j];
+        const int seg_rows = p.nsrc > 1 ? TILE_M : sm.seg_rows[j];
         const int n_live = (RT == 2 && m * TILE_M + SUB_M >= seg_rows) ? 1 : RT;
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&sm.empty[stage], phase ^ 1, 10)) {
@@ -526,8 +578,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         }
         tc_fence_after();
         int j, e, m, n;
-        decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
-        const int seg_rows = sm.seg_rows[j];
+        decode_tile<WF, PAIR>(t, sm, units, p.n_tiles, j, e, m, n);
+        const int seg_rows = p.nsrc > 1 ? TILE_M : sm.seg_rows[j];
         const int n_live = (RT == 2 && m * TILE_M + SUB_M >= seg_rows) ? 1 : RT;
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
@@ -582,13 +634,17 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       }
       tc_fence_after();
       int j, e, m, n;
-      decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
+      decode_tile<WF, PAIR>(t, sm, units, p.n_tiles, j, e, m, n);
+      int blk_row = 0, blk_rows = 0;  // several sources: this CTA's block
+      if (p.nsrc > 1) source_block(sm, e, p.nsrc, m * BPT + (int)rank, blk_row, blk_rows);
       const int64_t seg_rows = sm.seg_rows[j];
       for (int sub = 0; sub < RT; ++sub) {
-      if ((int64_t)m * TILE_M + sub * SUB_M >= seg_rows) break;  // no rows in this sub-tile (warp-uniform)
+      // no rows in this sub-tile (warp-uniform; several sources: blocks say)
+      if (p.nsrc == 1 && (int64_t)m * TILE_M + sub * SUB_M >= seg_rows) break;
       const int r = sub * SUB_M + (int)rank * BM + q * 32 + lane;  // row inside the tile
-      const bool valid = (int64_t)m * TILE_M + r < seg_rows;
-      const int64_t grow = (int64_t)sm.row_start[j] + (int64_t)m * TILE_M + r;
+      const int lr = q * 32 + lane;                                 // row inside this CTA's block
+      const bool valid = p.nsrc > 1 ? lr < blk_rows : (int64_t)m * TILE_M + r < seg_rows;
+      const int64_t grow = p.nsrc > 1 ? (int64_t)blk_row + lr : (int64_t)sm.row_start[j] + (int64_t)m * TILE_M + r;
       const uint32_t tb = tmem_base + acc * BN + sub * TN + ((uint32_t)(q * 32) << 16);
       if (MODE == GATEUP) {
         const int col0 = n * (TN / 2);
@@ -713,7 +769,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       int tl = 0;  // tiles of this CTA so far
       for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++tl) {
         int j, e, m, n;
-        decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
+        decode_tile<WF, PAIR>(t, sm, units, p.n_tiles, j, e, m, n);
         if (PREFETCH && !MN) {
           const int buf = tl & 1;
           if (tl >= 2 && !mbar_wait(&sm.absq_empty[buf], ((tl >> 1) - 1) & 1, 13)) {
@@ -772,7 +828,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     int tl = 0;
     for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++tl) {
       int j, e, m, n;
-      decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
+      decode_tile<WF, PAIR>(t, sm, units, p.n_tiles, j, e, m, n);
       const int buf = tl & 1;
       if (tl >= 2 && !mbar_wait(&sm.absq_empty[buf], ((tl >> 1) - 1) & 1, 14)) {
         *abort_flag = 1;
@@ -831,7 +887,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     constexpr bool STAGE = (WF == W_NF4 && !PREFETCH) || (WF == W_INT8 && MN);
     for (int t = unit; t < total_tiles && !failed && !*abort_flag; t += num_units, ++tl) {
       int j, e, m, n;
-      decode_tile<WF, PAIR>(t, sm, E, p.nsrc, p.n_tiles, j, e, m, n);
+      decode_tile<WF, PAIR>(t, sm, units, p.n_tiles, j, e, m, n);
       // key of this thread's rows (K-major) / of the k-block (MN)
       const int row_key = MN ? 0 : (MCfg<MODE>::TWO_KEYS ? kblk : 0);
       const int wrow_base = MN ? 0 : kmajor_row<MODE, TN>(p, e, n, kblk) - e * p.out_rows;  // first weight row

@@ -13,7 +13,8 @@ by expert id) are already grouped by destination rank and, inside, by
 expert, so the send buffer is the permuted activation itself.  The received
 rows arrive source-major, each source's rows in expert order; the grouped
 GEMMs take those G x E/G (source, expert) segments as they are (weight =
-expert, tiles visited expert-major), so the owner neither re-sorts nor
+expert; each segment cut into 128-row blocks, an expert's blocks paired into
+256-row tiles, tiles visited expert-major), so the owner neither re-sorts nor
 restores the order, and its output goes back through the reverse all-to-all
 in the layout the token owner sent.  (``ExpertParallelMoE``, the copy-engine
 transport, places the blocks expert-major instead, so the GEMMs see one
@@ -273,9 +274,12 @@ def _merge_runs(peer, peer_row, my_row, rows):
 
 
 # Costs that decide whether an owner regroups a chunk's received rows (two row
-# gathers through HBM) to save the 256-row GEMM tiles that source boundaries
-# cut: measured on B200 for the NF4 grouped GEMMs and the row-gather kernel.
-GEMM_FLOPS_PER_S = 1.0e15
+# gathers through HBM) to save the GEMM tiles that source boundaries cut:
+# measured on B200 for the NF4 grouped GEMMs and the row-gather kernel.  The
+# GEMM rate is the marginal one of an extra 256-row tile (5.8 us at H=4096,
+# I=1536 on segment lengths near 256: a tile-equivalent 1.6 PFLOP/s; the
+# kernels' average rate is about 1.0 PFLOP/s).
+GEMM_FLOPS_PER_S = 1.6e15
 GATHER_BYTES_PER_S = 6.0e12
 TILE_ROWS = 256
 
@@ -283,10 +287,13 @@ TILE_ROWS = 256
 def regroup_pays(L, hidden: int, inter: int, row_bytes: int) -> bool:
     """L [sources, experts] rows of one received chunk, source-major.  True if
     regrouping them expert-major (a gather of the rows there and one of the
-    results back) costs less than the GEMM tiles it saves."""
+    results back) costs less than the GEMM tiles it saves.  On source-major
+    rows the GEMMs cut each segment into 128-row blocks and pair an expert's
+    blocks into 256-row tiles, so a segment wastes at most part of a block."""
     import numpy as np
     L = np.asarray(L, dtype=np.int64)
-    tiles_src = int(((L + TILE_ROWS - 1) // TILE_ROWS).sum())
+    half = TILE_ROWS // 2  # source-major segments are tiled in half-tile blocks, two per tile
+    tiles_src = int(((((L + half - 1) // half).sum(axis=0) + 1) // 2).sum())
     tiles_exp = int(((L.sum(axis=0) + TILE_ROWS - 1) // TILE_ROWS).sum())
     saved = (tiles_src - tiles_exp) * 6.0 * TILE_ROWS * hidden * inter / GEMM_FLOPS_PER_S
     cost = 2 * 2 * int(L.sum()) * row_bytes / GATHER_BYTES_PER_S  # two gathers, each a read and a write
@@ -442,18 +449,22 @@ class ExpertParallelMoE:
     """The expert-parallel layer with a copy-engine exchange (transport "ipc").
 
     Same contract and result as ``ep_moe_forward``; the rows move differently:
-    every rank maps every other rank's exchange buffer (``PeerBuffers``), a
-    token owner copies each of its (owner, expert) blocks straight into that
-    owner's receive region with one cudaMemcpyAsync each (copy engines, no
-    SMs), at the place ``exchange_blocks`` gives it: expert-major, so the
-    owner's GEMMs run one segment per expert and no 256-row tile is cut at a
-    source boundary.  The owner copies each (source, expert) block of results
-    straight back into the token owner's return region, in the order the token
-    owner sent.  With ``chunks`` > 1 the copies of one chunk run beside the
-    GEMMs of another; ``copy_streams`` > 1 spreads a chunk's blocks over that
-    many side streams by peer, so several copies are in flight at once.
-    ``layout="source"`` keeps the receive rows source-major instead (one copy
-    per peer and chunk; the GEMMs take G segments per expert).
+    every rank maps every other rank's exchange buffer (``PeerBuffers``) and a
+    token owner copies its rows straight into each owner's receive region
+    (copy engines, no SMs), at the places ``exchange_blocks`` gives them; the
+    owner copies the results straight back into the token owner's return
+    region, in the order the token owner sent.
+
+    ``layout="source"`` (default): one copy per peer and chunk; the owner's
+    GEMMs take the G source segments of each expert (128-row blocks paired
+    into tiles), or — where ``regroup_pays`` ("auto"; or "always"/"never") —
+    first gather the chunk's rows expert-major and the results back.
+    ``layout="expert"``: one copy per (peer, expert) block into an
+    expert-major region, so the GEMMs see one segment per expert; a copy
+    costs about 4 µs of copy-engine time, so this pays only with few blocks.
+    With ``chunks`` > 1 the copies of one chunk run beside the GEMMs of
+    another; ``copy_streams`` > 1 spreads a chunk's copies over that many side
+    streams by peer, so several are in flight at once.
     Arrival is signalled with flags in the peers' buffers: after a chunk's
     copies a rank stores the exchange's epoch into its slot of every peer's
     flag array, and a consumer's stream waits (bounded) for all its slots to

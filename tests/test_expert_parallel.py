@@ -205,13 +205,14 @@ def test_regroup_order_is_expert_major(G, El, seed):
 
 def test_regroup_cost_rule():
     """The owner regroups where cut tiles cost more than moving the rows twice:
-    c4's shapes at 8 GPUs (about 256 rows per source and expert), not at 2."""
+    ~64-row segments from each of 8 sources (paired 128-row blocks half
+    empty), not c4's shapes at 2 GPUs (~1024 rows per source and expert)."""
     from mirai_b200.expert_parallel import exchange_blocks, regroup_pays
     rng = np.random.default_rng(0)
     H, I = 4096, 1536
-    assert regroup_pays(256 + rng.integers(-16, 16, size=(8, 16)), H, I, 2 * H)
+    assert regroup_pays(64 + rng.integers(-16, 16, size=(8, 16)), H, I, 2 * H)
     assert not regroup_pays(1024 + rng.integers(-32, 32, size=(2, 64)), H, I, 2 * H)
-    M = 256 + rng.integers(-16, 16, size=(8, 8, 2, 16))
+    M = 64 + rng.integers(-16, 16, size=(8, 8, 2, 16))
     p = exchange_blocks(M, 3, "source", regroup="auto", hidden=H, inter=I, row_bytes=2 * H)
     assert all(r is not None for r in p.regroup)
     assert p.regroup[1] == np.cumsum(M[:, 3, 1, :].sum(axis=0)).tolist()
