@@ -67,6 +67,15 @@ def test_exchange_entry_points_validate_on_the_host():
     assert lib.mirai_ipc_release(None) == 0                     # nothing to release
     assert lib.mirai_copy_async(None, None, 0, None) == 0        # zero bytes: no copy
     assert lib.mirai_copy_async(None, None, 16, None) == 1
+    addrs = (ctypes.c_uint64 * 2)(0, 4096)
+    sizes = (ctypes.c_uint64 * 2)(0, 0)
+    assert lib.mirai_copy_blocks(0, None, None, None, None) == 0        # empty list
+    assert lib.mirai_copy_blocks(-1, addrs, addrs, sizes, None) == 1
+    assert lib.mirai_copy_blocks(2, None, addrs, sizes, None) == 1      # missing array
+    assert lib.mirai_copy_blocks(2, addrs, addrs, sizes, None) == 0     # zero-byte blocks are skipped
+    sizes[1] = 16
+    assert lib.mirai_copy_blocks(2, addrs, (ctypes.c_uint64 * 2)(0, 0), sizes, None) == 1  # null source
+    assert b"block 1" in lib.mirai_b200_last_error()
     slots = (_lib.c_vp * 2)()
     assert lib.mirai_ep_signal(slots, 0, 1, None) == 1           # no slots
     assert lib.mirai_ep_signal(slots, 65, 1, None) == 1          # more peers than supported
