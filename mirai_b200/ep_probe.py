@@ -56,8 +56,8 @@ def _bandwidth(dev, world, rank):
         stream = torch.cuda.current_stream()
         epoch = [0]
 
-        def exchange():  # the layer's mechanism: copies, then arrival flags
-            for j in range(world):
+        def exchange():  # the layer's mechanism: copies (rotated schedule), then arrival flags
+            for j in ((rank + i) % world for i in range(world)):
                 _lib.call("mirai_copy_async", _lib.c_vp(data[j] + rank * blk), _lib.c_vp(x.data_ptr() + j * blk),
                           blk, _lib.c_vp(stream.cuda_stream))
             epoch[0] += 1
@@ -102,10 +102,11 @@ def _blocks(dev, world, rank):
     epoch = [0]
     for nb in (1, 16, 64, 128):
         piece = blk // nb
-        dst = np.array([data[j] + rank * blk + i * piece for j in range(world) for i in range(nb)], np.uint64)
-        src = np.array([x.data_ptr() + j * blk + i * piece for j in range(world) for i in range(nb)], np.uint64)
+        peers = [(rank + i) % world for i in range(world)]  # rotated schedule, as the layer's
+        dst = np.array([data[j] + rank * blk + i * piece for j in peers for i in range(nb)], np.uint64)
+        src = np.array([x.data_ptr() + j * blk + i * piece for j in peers for i in range(nb)], np.uint64)
         nbytes = np.full(len(dst), piece, np.uint64)
-        peer = np.repeat(np.arange(world), nb)
+        peer = np.repeat(np.array(peers), nb)
         for ns in (1, 2):
             def exchange():
                 start = torch.cuda.Event()

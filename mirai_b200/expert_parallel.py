@@ -334,7 +334,9 @@ def exchange_blocks(M, rank: int, layout: str = "expert", *, regroup: str = "nev
     expert (the dispatch plan's order), i.e. by owner, then local expert; its
     return region uses the same order, so the combine reads it like the
     single-GPU layer's expert output.  Blocks that continue each other on both
-    sides are merged into one copy.
+    sides are merged into one copy, and each list visits the peers starting
+    from ``rank`` itself (a rotated schedule, so that the ranks' copies do not
+    all converge on one peer).
 
     ``regroup`` ("never", "auto", "always"; source-major layout only): whether
     the owner regroups a chunk's received rows expert-major before its GEMMs
@@ -361,13 +363,20 @@ def exchange_blocks(M, rank: int, layout: str = "expert", *, regroup: str = "nev
         flat = M.transpose(1, 2, 0, 3).reshape(G, C, G * El)
         recv_pos = (np.cumsum(flat, axis=2) - flat).reshape(G, C, G, El).transpose(2, 0, 1, 3)
     me = rank
+
+    def rotated(peer, *cols):
+        # peers in the order me, me+1, ... (mod G): at each step of the copy
+        # schedule every rank targets a different peer, so no peer's inbound
+        # links are shared by all senders at once
+        order = np.argsort((peer - me) % G, kind="stable")
+        return _merge_runs(peer[order], *(col[order] for col in cols))
+
     dispatch, give_back, ends = [], [], []
     for c in range(C):
         d, e = np.nonzero(M[me, :, c, :])
-        dispatch.append(_merge_runs(d, in_base[d, c] + recv_pos[me, d, c, e], send_pos[me, d, c, e], M[me, d, c, e]))
+        dispatch.append(rotated(d, in_base[d, c] + recv_pos[me, d, c, e], send_pos[me, d, c, e], M[me, d, c, e]))
         s, e = np.nonzero(M[:, me, c, :])
-        give_back.append(_merge_runs(s, ret_base[s, c] + send_pos[s, me, c, e], recv_pos[s, me, c, e],
-                                     M[s, me, c, e]))
+        give_back.append(rotated(s, ret_base[s, c] + send_pos[s, me, c, e], recv_pos[s, me, c, e], M[s, me, c, e]))
         seg = M[:, me, c, :].sum(axis=0) if layout == "expert" else M[:, me, c, :].reshape(-1)
         ends.append(np.cumsum(seg).tolist())
     groups = [None] * C

@@ -148,6 +148,10 @@ def test_exchange_blocks_round_trip(G, C, El, seed, layout):
         M[:] = 0                  # an empty layer
     plans = [exchange_blocks(M, r, layout) for r in range(G)]
     assert len({(p.in_cap, p.ret_cap) for p in plans}) == 1
+    for r, p in enumerate(plans):  # rotated schedule: peers visited from r upwards (mod G)
+        for blocks in p.dispatch + p.give_back:
+            steps = (blocks[0] - r) % G
+            assert np.all(np.diff(steps) >= 0)
 
     def label(s, d, c, e, i):
         return (((s * G + d) * C + c) * El + e) * 1000 + i
