@@ -291,13 +291,17 @@ def regroup_pays(L, hidden: int, inter: int, row_bytes: int) -> bool:
     rows the GEMMs cut each segment into 128-row blocks and pair an expert's
     blocks into 256-row tiles, so a segment wastes at most part of a block."""
     import numpy as np
-    L = np.asarray(L, dtype=np.int64)
+    return bool(_regroup_pays_chunks(np.asarray(L, dtype=np.int64)[:, None, :], hidden, inter, row_bytes)[0])
+
+
+def _regroup_pays_chunks(L, hidden: int, inter: int, row_bytes: int):
+    """``regroup_pays`` for every chunk at once: L [sources, chunks, experts]."""
     half = TILE_ROWS // 2  # source-major segments are tiled in half-tile blocks, two per tile
-    tiles_src = int(((((L + half - 1) // half).sum(axis=0) + 1) // 2).sum())
-    tiles_exp = int(((L.sum(axis=0) + TILE_ROWS - 1) // TILE_ROWS).sum())
-    saved = (tiles_src - tiles_exp) * 6.0 * TILE_ROWS * hidden * inter / GEMM_FLOPS_PER_S
-    cost = 2 * 2 * int(L.sum()) * row_bytes / GATHER_BYTES_PER_S  # two gathers, each a read and a write
-    return saved > cost
+    tiles_src = ((((L + half - 1) // half).sum(axis=0) + 1) // 2).sum(axis=1)
+    tiles_exp = ((L.sum(axis=0) + TILE_ROWS - 1) // TILE_ROWS).sum(axis=1)
+    saved = (tiles_src - tiles_exp) * (6.0 * TILE_ROWS * hidden * inter / GEMM_FLOPS_PER_S)
+    cost = L.sum(axis=(0, 2)) * (4.0 * row_bytes / GATHER_BYTES_PER_S)  # two gathers, each a read and a write
+    return (saved > cost) & (L.sum(axis=(0, 2)) > 0)
 
 
 def regroup_order(L: torch.Tensor, total: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -351,40 +355,52 @@ def exchange_blocks(M, rank: int, layout: str = "expert", *, regroup: str = "nev
     S = M.sum(axis=(1, 3))                    # rows each source sends [source, chunk]
     in_base = np.concatenate([np.zeros((G, 1), np.int64), np.cumsum(R, axis=1)[:, :-1]], axis=1)
     ret_base = np.concatenate([np.zeros((G, 1), np.int64), np.cumsum(S, axis=1)[:, :-1]], axis=1)
-    # send position of block (s, d, c, e) in s's chunk-c rows: order (d, e)
-    flat = M.transpose(0, 2, 1, 3).reshape(G, C, G * El)
-    send_pos = (np.cumsum(flat, axis=2) - flat).reshape(G, C, G, El).transpose(0, 2, 1, 3)
-    if layout == "expert":
+    me = rank
+    rot = (me + np.arange(G)) % G  # peers in the order me, me+1, ... (mod G): at each step of the
+    # copy schedule every rank targets a different peer, so no peer's inbound links are shared by all
+    # senders at once
+    dispatch, give_back, ends = [], [], []
+    if layout == "source":
+        # one block per (peer, chunk): a source's rows for an owner are one run on both sides
+        n = M.sum(axis=3)                                     # rows [source, dest, chunk]
+        src_off = np.cumsum(n, axis=0) - n                    # rows of lower sources in d's chunk block
+        send_off = np.cumsum(n, axis=1) - n                   # rows for lower owners in s's chunk rows
+        for c in range(C):
+            rows = n[me, rot, c]
+            keep = rows > 0
+            d = rot[keep]
+            dispatch.append((d, in_base[d, c] + src_off[me, d, c], send_off[me, d, c], rows[keep]))
+            rows = n[rot, me, c]
+            keep = rows > 0
+            s_ = rot[keep]
+            give_back.append((s_, ret_base[s_, c] + send_off[s_, me, c], src_off[s_, me, c], rows[keep]))
+            ends.append(np.cumsum(M[:, me, c, :].reshape(-1)).tolist())
+    else:
+        # send position of block (s, d, c, e) in s's chunk-c rows: order (d, e)
+        flat = M.transpose(0, 2, 1, 3).reshape(G, C, G * El)
+        send_pos = (np.cumsum(flat, axis=2) - flat).reshape(G, C, G, El).transpose(0, 2, 1, 3)
         # receive position of block (s, d, c, e) in d's chunk-c rows: order (e, s)
         flat = M.transpose(1, 2, 3, 0).reshape(G, C, El * G)
         recv_pos = (np.cumsum(flat, axis=2) - flat).reshape(G, C, El, G).transpose(3, 0, 1, 2)
-    else:
-        # order (s, e)
-        flat = M.transpose(1, 2, 0, 3).reshape(G, C, G * El)
-        recv_pos = (np.cumsum(flat, axis=2) - flat).reshape(G, C, G, El).transpose(2, 0, 1, 3)
-    me = rank
 
-    def rotated(peer, *cols):
-        # peers in the order me, me+1, ... (mod G): at each step of the copy
-        # schedule every rank targets a different peer, so no peer's inbound
-        # links are shared by all senders at once
-        order = np.argsort((peer - me) % G, kind="stable")
-        return _merge_runs(peer[order], *(col[order] for col in cols))
+        def rotated(peer, *cols):
+            order = np.argsort((peer - me) % G, kind="stable")
+            return _merge_runs(peer[order], *(col[order] for col in cols))
 
-    dispatch, give_back, ends = [], [], []
-    for c in range(C):
-        d, e = np.nonzero(M[me, :, c, :])
-        dispatch.append(rotated(d, in_base[d, c] + recv_pos[me, d, c, e], send_pos[me, d, c, e], M[me, d, c, e]))
-        s, e = np.nonzero(M[:, me, c, :])
-        give_back.append(rotated(s, ret_base[s, c] + send_pos[s, me, c, e], recv_pos[s, me, c, e], M[s, me, c, e]))
-        seg = M[:, me, c, :].sum(axis=0) if layout == "expert" else M[:, me, c, :].reshape(-1)
-        ends.append(np.cumsum(seg).tolist())
+        for c in range(C):
+            d, e = np.nonzero(M[me, :, c, :])
+            dispatch.append(rotated(d, in_base[d, c] + recv_pos[me, d, c, e], send_pos[me, d, c, e],
+                                    M[me, d, c, e]))
+            s_, e = np.nonzero(M[:, me, c, :])
+            give_back.append(rotated(s_, ret_base[s_, c] + send_pos[s_, me, c, e], recv_pos[s_, me, c, e],
+                                     M[s_, me, c, e]))
+            ends.append(np.cumsum(M[:, me, c, :].sum(axis=0)).tolist())
     groups = [None] * C
     if layout == "source" and regroup != "never":
-        for c in range(C):
-            L = M[:, me, c, :]
-            if L.sum() and (regroup == "always" or regroup_pays(L, hidden, inter, row_bytes)):
-                groups[c] = np.cumsum(L.sum(axis=0)).tolist()
+        L = M[:, me]                                          # [source, chunk, expert]
+        take = L.sum(axis=(0, 2)) > 0 if regroup == "always" else _regroup_pays_chunks(L, hidden, inter, row_bytes)
+        for c in np.nonzero(take)[0]:
+            groups[c] = np.cumsum(L[:, c, :].sum(axis=0)).tolist()
     return BlockPlan(in_cap=int(R.sum(axis=1).max()), ret_cap=int(S.sum(axis=1).max()),
                      in_base=in_base[me].tolist(), in_rows=R[me].tolist(),
                      ret_base=ret_base[me].tolist(), ret_rows=S[me].tolist(),
