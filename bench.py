@@ -11,6 +11,7 @@ NF4 dequant) -> weighted combine.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c0..c4] [--mode fwd|train]
                     [--impl ours|reference] [--ep-transport ipc|nccl] [--ep-chunks C]
+                    [--ep-layout source|expert] [--ep-regroup never|auto|always] [--ep-copy-streams S]
 
 ``--mode train`` (one GPU) runs BASELINE config 2's full step: forward, dX
 backward through the frozen experts and a rank-16 LoRA on w2 with its factor
