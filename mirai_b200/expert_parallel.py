@@ -147,6 +147,11 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
     dist.all_to_all_single(recv_mat, send_mat, group=group)
     flat = torch.cat([send_mat.reshape(-1), recv_mat.reshape(-1)]).tolist()
     n = G * C * El
+    # this rank's counts [1, dest, chunk, expert] and what it received; both must be sane
+    import numpy as np
+    check_counts(np.asarray(flat[:n]).reshape(1, G, C, El), 0, [p[2].shape[0] for p in prep])
+    if min(flat[n:], default=0) < 0:
+        raise ValueError("expert-parallel exchange: negative row count received")
     sm_ = [[flat[(d * C + c) * El:(d * C + c + 1) * El] for d in range(G)] for c in range(C)]
     rm_ = [[flat[n + (s_ * C + c) * El:n + (s_ * C + c + 1) * El] for s_ in range(G)] for c in range(C)]
     sc = [[sum(sm_[c][d]) for d in range(G)] for c in range(C)]
@@ -225,6 +230,23 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
         if e > b:
             out[b:e] = ops.combine(y_back, prep[c][1].inverse_order, prep[c][0], top_k, tokens.dtype)
     return out
+
+
+def check_counts(M, rank: int, sent_rows: list[int]) -> None:
+    """Reject an exchange whose gathered counts M [source, dest, chunk, local
+    expert] cannot be right before any row moves: a negative count anywhere,
+    or this rank's counts for a chunk not summing to the rows it permuted for
+    that chunk (a corrupted or foreign plan).  Raises ValueError; a peer that
+    goes on to the row exchange then ends in the process group's timeout."""
+    import numpy as np
+    M = np.asarray(M)
+    if (M < 0).any():
+        raise ValueError("expert-parallel exchange: negative row count in the gathered counts")
+    mine = M[rank].sum(axis=(0, 2))
+    for c, rows in enumerate(sent_rows):
+        if int(mine[c]) != int(rows):
+            raise ValueError(f"expert-parallel exchange: rank {rank} chunk {c} counts {int(mine[c])} routed rows "
+                             f"but permuted {int(rows)}")
 
 
 def shard_tokens(num_tokens: int, world: int, rank: int) -> tuple[int, int]:
@@ -350,6 +372,8 @@ def exchange_blocks(M, rank: int, layout: str = "expert", *, regroup: str = "nev
     if layout not in ("expert", "source"):
         raise ValueError(f"layout must be 'expert' or 'source', not {layout!r}")
     M = np.asarray(M, dtype=np.int64)
+    if (M < 0).any():
+        raise ValueError("exchange_blocks: negative row count")
     G, _, C, El = M.shape
     R = M.sum(axis=(0, 3))                    # rows each owner receives [dest, chunk]
     S = M.sum(axis=(1, 3))                    # rows each source sends [source, chunk]
@@ -576,7 +600,9 @@ class ExpertParallelMoE:
         allm = torch.empty((G,) + tuple(mine.shape), dtype=mine.dtype, device=dev)      # [source, dest, chunk, expert]
         dist.all_gather_into_tensor(allm, mine, group=self.group)
         row_bytes = H * tokens.element_size()
-        plan = exchange_blocks(allm.cpu().numpy(), me, self.layout, regroup=self.regroup, hidden=H,
+        counts = allm.cpu().numpy()
+        check_counts(counts, me, [p[2].shape[0] for p in prep])
+        plan = exchange_blocks(counts, me, self.layout, regroup=self.regroup, hidden=H,
                                inter=self.inter, row_bytes=row_bytes)
         in_cap = (plan.in_cap * row_bytes + 255) // 256 * 256
         ret_cap = plan.ret_cap * row_bytes

@@ -221,3 +221,87 @@ def test_regroup_cost_rule():
     assert all(r is not None for r in p.regroup)
     assert p.regroup[1] == np.cumsum(M[:, 3, 1, :].sum(axis=0)).tolist()
     assert all(r is None for r in exchange_blocks(M, 3, "source").regroup)
+
+
+class CorruptCountsOps(OracleStepOps):
+    """A rank whose dispatch plan reports one routed row more than it permuted."""
+
+    def plan(self, top_indices, num_experts):
+        p = super().plan(top_indices, num_experts)
+        p.counts = p.counts.clone()
+        p.counts[0] += 1
+        return p
+
+
+def _fault_rank_main(rank, world, port, mode, results):
+    import time
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    try:
+        from mirai_b200.expert_parallel import ExpertShard, ep_moe_forward, shard_tokens
+        T, H, E, k, I = 64, 32, 4, 2, 64
+        x, logits, ws = _problem(T, H, E, k, I, 3)
+        shard = ExpertShard(E, world, rank)
+        b, e = shard_tokens(T, world, rank)
+        lo, hi = shard.first, shard.first + shard.local
+        if mode == "absent" and rank == 1:
+            results[rank] = ("left", 0.0)  # this rank never joins the layer's collectives
+            return
+        ops = CorruptCountsOps() if (mode == "corrupt" and rank == 1) else OracleStepOps()
+        t0 = time.monotonic()
+        try:
+            ep_moe_forward(torch.from_numpy(x[b:e]), torch.from_numpy(logits[b:e]), tuple(w[lo:hi] for w in ws),
+                           shard=shard, top_k=k, inter=I, ops=ops)
+            outcome = "ok"
+        except ValueError:
+            outcome = "ValueError"
+        except Exception:  # the process group's timeout, or the peer's closed connection
+            outcome = "error"
+        results[rank] = (outcome, time.monotonic() - t0)
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _run_fault(mode):
+    with mp.Manager() as mgr:
+        results = mgr.dict()
+        mp.start_processes(_fault_rank_main, args=(2, _free_port(), mode, results), nprocs=2, start_method="spawn")
+        return dict(results)
+
+
+@pytest.mark.timeout(180)
+def test_rank_that_never_joins_ends_in_an_error_not_a_hang():
+    """Failure on the host: rank 1 leaves before the layer.  Rank 0's first
+    collective of the layer ends in an error within the process group's
+    timeout instead of waiting for ever."""
+    res = _run_fault("absent")
+    assert res[1][0] == "left"
+    outcome, seconds = res[0]
+    assert outcome == "error" and seconds < 60
+
+
+@pytest.mark.timeout(180)
+def test_corrupt_counts_are_rejected_before_rows_move():
+    """A rank whose plan disagrees with its permuted rows raises ValueError
+    after the count exchange, before the row exchange; its peer, waiting in the
+    row exchange, ends in an error within the timeout."""
+    res = _run_fault("corrupt")
+    assert res[1][0] == "ValueError"
+    outcome, seconds = res[0]
+    assert outcome == "error" and seconds < 60
+
+
+def test_check_counts():
+    from mirai_b200.expert_parallel import check_counts
+    M = np.ones((2, 2, 3, 4), np.int64)           # every rank sends 2 x 4 rows per chunk
+    check_counts(M, 1, [8, 8, 8])
+    with pytest.raises(ValueError, match="negative"):
+        bad = M.copy()
+        bad[0, 1, 2, 3] = -1
+        check_counts(bad, 1, [8, 8, 8])
+    with pytest.raises(ValueError, match="chunk 2"):
+        check_counts(M, 1, [8, 8, 7])

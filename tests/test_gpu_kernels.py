@@ -617,3 +617,30 @@ def test_source_major_segments_equal_expert_major(fmt):
     _check(ops)
     assert torch.equal(h_src[pd], h_exp)
     assert torch.equal(y_src[pd], y_exp)
+
+
+def test_exchange_wait_gives_up_and_reports_a_timeout():
+    """A peer that never signals (a flag nothing sets): the exchange's arrival
+    wait gives up after its 2 s limit, records MIRAI_ERR_DEVICE_TIMEOUT with the
+    silent peer's slot (site 700 + slot) and returns, so the host learns of it
+    and the context stays usable; a flag that has reached the epoch passes at once."""
+    import time
+
+    dev = _dev()
+    from mirai_b200 import _lib, ops
+    ops.device_status()  # start from a clear error word
+    flags = torch.zeros(2, dtype=torch.int64, device=dev)
+    stream = _lib.c_vp(torch.cuda.current_stream().cuda_stream)
+    t0 = time.monotonic()
+    _lib.call("mirai_ep_wait", _lib.c_vp(flags.data_ptr()), 2, 0, 1, stream)
+    code, info = ops.device_status()
+    waited = time.monotonic() - t0
+    assert (code, info) == (4, 701)  # MIRAI_ERR_DEVICE_TIMEOUT, slot 1
+    assert 1.5 < waited < 30
+    idx, _ = ops.route_topk(torch.randn(64, 8, device=dev), 2)  # the context still runs kernels
+    ops.check_device()
+    assert idx.shape == (64, 2)
+    flags[1] = 3
+    t0 = time.monotonic()
+    _lib.call("mirai_ep_wait", _lib.c_vp(flags.data_ptr()), 2, 0, 2, stream)
+    assert ops.device_status() == (0, 0) and time.monotonic() - t0 < 1.0
