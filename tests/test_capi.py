@@ -13,7 +13,8 @@ def declared_symbols():
     inc = os.path.join(ROOT, "include")
     for fn in sorted(os.listdir(inc)):
         if fn.endswith(".h"):
-            text = open(os.path.join(inc, fn)).read()
+            with open(os.path.join(inc, fn)) as f:
+                text = f.read()
             text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
             names += re.findall(r"^[A-Za-z_][\w \*]*?\b(mirai_\w+)\s*\(", text, flags=re.M)
     return sorted(set(names))

@@ -97,7 +97,7 @@ def _free_port():
 
 
 def _run(world, cfg):
-    with mp.Manager() as mgr:
+    with mp.get_context("spawn").Manager() as mgr:
         results = mgr.dict()
         mp.start_processes(_rank_main, args=(world, _free_port(), cfg, results), nprocs=world, start_method="spawn")
         return dict(results)
@@ -267,7 +267,7 @@ def _fault_rank_main(rank, world, port, mode, results):
 
 
 def _run_fault(mode):
-    with mp.Manager() as mgr:
+    with mp.get_context("spawn").Manager() as mgr:
         results = mgr.dict()
         mp.start_processes(_fault_rank_main, args=(2, _free_port(), mode, results), nprocs=2, start_method="spawn")
         return dict(results)
