@@ -3,13 +3,15 @@
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
         --master-port P -m mirai_b200.ep_probe bandwidth
     python -m torch.distributed.run ... -m mirai_b200.ep_probe blocks
+    python -m mirai_b200.ep_probe gemms          # one GPU
     python -m torch.distributed.run ... -m mirai_b200.ep_probe phases --config c2|c4 [--layout expert|source]
 
 ``bandwidth``: bytes that cross NVLink per rank per second for NCCL's
 all_to_all_single and for copy-engine transfers into peer-mapped buffers (the
 layer's ``ipc`` transport), on equal-sized blocks.  ``blocks``: the same
 copy-engine exchange (128 MB per rank) split into 1 to 128 copies per peer, on
-one or two streams — the cost of a copy.  ``phases [--layout expert|source]
+one or two streams — the cost of a copy.  ``gemms`` (one GPU): the owner's GEMMs on source-major rows against the same
+rows contiguous per expert.  ``phases [--layout expert|source]
 [--copy-streams S] [--regroup never|auto|always]``: CUDA-event times between the phases of one
 ``ExpertParallelMoE`` layer (1 chunk) on rank 0, averaged over 10 layers after
 3 warm-up layers.
@@ -186,14 +188,59 @@ def _phases(dev, world, rank, config, layout="source", copy_streams=1, regroup="
             "phases_ms": {k: round(v, 3) for k, v in acc.items()}, "layer_ms": round(sum(acc.values()), 3)}
 
 
+def _gemms(dev):
+    """The owner's GEMMs on rows received source-major (``sources`` = G) against
+    the same rows contiguous per expert, NF4, on one GPU: c2's segment sizes at 2
+    GPUs (~2048 rows per source and expert) and c4's at 8 (~256), ragged.  Min
+    and median of 7 alternating rounds of 20 launches each (ms)."""
+    import statistics
+    from . import ops, tables
+    res = {}
+    for case, (H, I, El, G, mean, spread) in {"c2 at 2 GPUs": (2048, 1408, 16, 2, 2048, 60),
+                                             "c4 at 8 GPUs": (4096, 1536, 16, 8, 256, 16)}.items():
+        g = torch.Generator(device=dev).manual_seed(1)
+        ws = [ops.nf4_quantize((torch.randn(sh, generator=g, device=dev) * 0.02).to(torch.bfloat16),
+                               tables.nf4_code(dev), tables.dynamic_map(dev))
+              for sh in ((El, I, H), (El, I, H), (El, H, I))]
+        cnt = mean + torch.randint(-spread, spread, (G * El,), generator=torch.Generator().manual_seed(5))
+        S = int(cnt.sum())
+        x = torch.randn(S, H, device=dev).to(torch.bfloat16)
+        offs_src = torch.cumsum(cnt, 0).to(torch.int32).to(dev)
+        offs_exp = torch.cumsum(cnt.view(G, El).sum(0), 0).to(torch.int32).to(dev)
+        h = torch.empty(S, I, device=dev, dtype=torch.bfloat16)
+        y = torch.empty(S, H, device=dev, dtype=torch.bfloat16)
+        runs = {"gateup_sources": lambda: ops.gateup_swiglu(x, offs_src, ws[0], ws[1], inter=I, out=h, sources=G),
+                "gateup_contiguous": lambda: ops.gateup_swiglu(x, offs_exp, ws[0], ws[1], inter=I, out=h),
+                "down_sources": lambda: ops.down(h, offs_src, ws[2], hidden=H, out=y, sources=G),
+                "down_contiguous": lambda: ops.down(h, offs_exp, ws[2], hidden=H, out=y)}
+        acc = {k: [] for k in runs}
+        for _ in range(7):
+            for name, fn in runs.items():
+                for _ in range(3):
+                    fn()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                for _ in range(20):
+                    fn()
+                b.record()
+                torch.cuda.synchronize()
+                acc[name].append(a.elapsed_time(b) / 20)
+        res[case] = {"rows": S, **{k: [round(min(v), 4), round(statistics.median(v), 4)] for k, v in acc.items()}}
+    ops.check_device()
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["bandwidth", "blocks", "phases"])
+    ap.add_argument("what", choices=["bandwidth", "blocks", "phases", "gemms"])
     ap.add_argument("--config", default="c2")
     ap.add_argument("--layout", default="source", choices=["expert", "source"])
     ap.add_argument("--copy-streams", type=int, default=1)
     ap.add_argument("--regroup", default="auto", choices=["never", "auto", "always"])
     args = ap.parse_args()
+    if args.what == "gemms":  # one GPU, no process group
+        print(json.dumps(_gemms(torch.device("cuda", 0))), flush=True)
+        return
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
