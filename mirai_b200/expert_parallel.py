@@ -17,9 +17,10 @@ expert; each segment cut into 128-row blocks, an expert's blocks paired into
 256-row tiles, tiles visited expert-major), so the owner neither re-sorts nor
 restores the order, and its output goes back through the reverse all-to-all
 in the layout the token owner sent.  (``ExpertParallelMoE``, the copy-engine
-transport, places the blocks expert-major instead, so the GEMMs see one
-segment per expert.)  Per row the products are those of the single-GPU layer,
-so the result is identical to it.  The reference runs MoE
+transport, receives source-major too by default; it can instead place the
+blocks expert-major, or regroup a chunk's rows expert-major before the GEMMs.)
+Per row the products are those of the single-GPU layer, so the result is
+identical to it.  The reference runs MoE
 on one GPU (it has no expert parallelism); the exchange is this package's.
 (Receiving each (rank, expert) block straight into an expert-major layout
 with grouped NCCL send/recv was measured slower on B200 than one
