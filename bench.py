@@ -2,20 +2,24 @@
 """MoE-FFN tokens/s (NF4 experts) on B200 -- the routed expert FFN of the
 seruva19/mirai denoiser, run through libmirai_b200.so.
 
-Default workload (BASELINE config 2 shape): 32768 tokens, hidden 2048,
-32 experts, top-2, SwiGLU intermediate 1408, NF4 blocksize-64 experts with
-double-quantised absmax.  One step = one pass of the path over the batch:
-fp32 router top-k on precomputed gate logits -> dispatch plan -> permute ->
-gate/up grouped GEMM + SwiGLU (fused NF4 dequant) -> down grouped GEMM (fused
-NF4 dequant) -> weighted combine.
+Default workload: BASELINE config 2 as it is defined -- 32768 tokens, hidden
+2048, 32 experts, top-2, SwiGLU intermediate 1408, NF4 blocksize-64 experts
+with double-quantised absmax, forward plus the dX backward through the frozen
+experts with a rank-16 LoRA on w2 (its factor gradients included).  One step
+= one pass of the path over the batch: fp32 router top-k on precomputed gate
+logits -> dispatch plan -> permute -> gate/up grouped GEMM + SwiGLU (fused
+NF4 dequant) -> LoRA rank projection -> down grouped GEMM with the rank block
+-> weighted combine; then combine backward -> down dX (SwiGLU backward fused)
+-> gate/up dX -> un-permute sum, and the LoRA factor gradients.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c0..c4] [--mode fwd|train]
-                    [--impl ours|reference] [--ep-transport ipc|nccl] [--ep-chunks C]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c0..c4] [--mode train|fwd]
+                    [--int8-rotation] [--impl ours|reference] [--ep-transport ipc|nccl] [--ep-chunks C]
                     [--ep-layout source|expert] [--ep-regroup never|auto|always] [--ep-copy-streams S]
 
-``--mode train`` (one GPU) runs BASELINE config 2's full step: forward, dX
-backward through the frozen experts and a rank-16 LoRA on w2 with its factor
-gradients.  Under torchrun (N > 1) the layer runs expert-parallel
+``--mode fwd`` times the forward layer alone (the line also carries the
+forward rate of a train run under ``forward``).  ``--int8-rotation`` runs
+c3 in the reference's default INT8 format (block-Hadamard groups of 256).
+Under torchrun (N > 1) the layer runs expert-parallel
 (mirai_b200.expert_parallel): each rank owns E/N experts and routes its own
 tokens; rows move by copy engines into peer-mapped buffers (``ipc``, default)
 or by NCCL all-to-all, in C chunks whose exchanges overlap the GEMMs.  c1-c3
@@ -56,10 +60,13 @@ KERNELS_PER_STEP = 9
 # LoRA kernels (2 projections, 2 factor gradients)
 TRAIN_EXTRA_KERNELS = 8
 LORA_RANK = 16
-# DRAM bytes (read + write) of one gate/up launch from an ncu capture of the
-# same kernel on the same workload (profiles/ holds the capture's summary and
-# its command).  Workloads not captured report null.
-NCU_TRAFFIC = {"c2-gateup": 363_831_552 + 166_611_712}
+# DRAM bytes (read + write) per launch of a grouped GEMM from an ncu capture of
+# the same kernel on the same workload, with the capture it came from (the
+# summary and its command are under profiles/).  A kernel changed since its
+# capture, or not captured, reports null.
+NCU_TRAFFIC = {
+    "c2-gateup_swiglu_nf4": (363_831_552 + 166_611_712, "profiles/grouped_gemm_nf4_c2.md"),
+}
 
 
 def load_peaks():
@@ -134,7 +141,7 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- workload
 
-def make_workload(cfg, dev, seed):
+def make_workload(cfg, dev, seed, rotation=False):
     import torch
     from mirai_b200 import ops, tables
 
@@ -156,7 +163,9 @@ def make_workload(cfg, dev, seed):
         if cfg["fmt"] == "nf4":
             w = ops.nf4_quantize(w, tables.nf4_code(dev), tables.dynamic_map(dev))
         elif cfg["fmt"] == "int8":
-            w = ops.int8_quantize(w.float())
+            # the reference's default format rotates groups of best_group_size(in) (quant.py:87-91)
+            g = (256 if shape[2] % 256 == 0 else 64 if shape[2] % 64 == 0 else 16) if rotation else 0
+            w = ops.int8_quantize(w.float(), group_size=g)
         ws.append(w)
     torch.cuda.synchronize()
     return x, logits, ws
@@ -236,13 +245,34 @@ def measure_e2e(dev, host_in, n_out, out_shape, compute, args, barrier):
     return e0.elapsed_time(e1) / args.steps
 
 
+def make_weights_fmt(cfg, args):
+    """Weight format label of the workload (INT8 with the rotation flag)."""
+    if cfg["fmt"] == "int8" and args.int8_rotation:
+        return "int8 block-Hadamard g=256"
+    return cfg["fmt"]
+
+
+def time_kernel(fn, reps):
+    """Mean ms of ``fn`` over ``reps`` launches, CUDA events on the current stream."""
+    import torch
+    for _ in range(3):
+        fn()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in evs:
+        a.record()
+        fn()
+        b.record()
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / reps
+
+
 def run_ours(args, cfg, rank, world, dev):
     import torch
     import torch.distributed as dist
     from mirai_b200 import ops
 
     T, H, E, k, I = cfg["T"], cfg["H"], cfg["E"], cfg["k"], cfg["I"]
-    x, logits, (w1, w3, w2) = make_workload(cfg, dev, seed=1234 + rank)
+    x, logits, (w1, w3, w2) = make_workload(cfg, dev, seed=1234 + rank, rotation=args.int8_rotation)
     S = T * k
     train = args.mode == "train"
     gen = torch.Generator(device=dev).manual_seed(99 + rank)
@@ -255,14 +285,17 @@ def run_ours(args, cfg, rank, world, dev):
         lb = torch.randn(E, H, LORA_RANK, device=dev, generator=gen) * 0.02
         lora = ops.DownLoRA(la, lb, 16.0 / LORA_RANK, compute_grads=True)
 
-    def step(xin, lin, out=None, gin=None, dx_out=None):
+    def forward(xin, lin, out=None):
         idx, tw = ops.route_topk(lin, k)
+        o = ops.moe_forward(xin, idx, tw, w1, w3, w2, num_experts=E, inter=I)
+        if out is not None:
+            out.copy_(o)
+        return o
+
+    def step(xin, lin, out=None, gin=None, dx_out=None):
         if not train:
-            plan = ops.dispatch_plan(idx, E)
-            xs = ops.permute_rows(xin, plan.sorted_token_indices)
-            h = ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I)
-            y = ops.down(h, plan.offsets, w2, hidden=H)
-            return ops.combine(y, plan.inverse_order, tw, out=out)
+            return forward(xin, lin, out)
+        idx, tw = ops.route_topk(lin, k)
         o, st = ops.moe_forward_train(xin, idx, tw, w1, w3, w2, num_experts=E, inter=I, lora=lora)
         if out is not None:
             out.copy_(o)
@@ -275,49 +308,53 @@ def run_ours(args, cfg, rank, world, dev):
         if world > 1:
             dist.barrier()
 
-    # ---- device-resident throughput (value)
-    for _ in range(args.warmup):
-        step(x, logits)
-    ops.check_device()
-    clocks = ClockSampler(torch.cuda.current_device()).start()
-    barrier()
-    torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(args.steps):
-        step(x, logits)
-    t1.record()
-    t1.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    ms = t0.elapsed_time(t1) / args.steps
-    ops.check_device()
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        ops.check_device()
+        clocks = ClockSampler(torch.cuda.current_device()).start()
+        barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(steps):
+            fn()
+        t1.record()
+        t1.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+        ops.check_device()
+        return t0.elapsed_time(t1) / steps, clk
 
-    # ---- dominant kernel alone: gate/up grouped GEMM (CUDA events on its stream)
+    # ---- device-resident throughput (value)
+    ms, clk = timed(lambda: step(x, logits), args.steps)
+    fwd_ms = timed(lambda: forward(x, logits), args.steps)[0] if train else ms
+
+    # ---- each grouped GEMM of the step alone (CUDA events on its stream)
     idx, tw = ops.route_topk(logits, k)
-    plan = ops.dispatch_plan(idx, E)
+    _, st = ops.moe_forward_train(x, idx, tw, w1, w3, w2, num_experts=E, inter=I, lora=lora)
+    plan = st.plan
     xs = ops.permute_rows(x, plan.sorted_token_indices)
     h = torch.empty((S, I), dtype=torch.bfloat16, device=dev)
     y = torch.empty((S, H), dtype=torch.bfloat16, device=dev)
     reps = max(5, min(50, args.steps))
     kclocks = ClockSampler(torch.cuda.current_device()).start()
-    for _ in range(3):
-        ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I, out=h)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-    for a, b in evs:
-        a.record()
-        ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I, out=h)
-        b.record()
-    torch.cuda.synchronize()
-    gu_ms = sum(a.elapsed_time(b) for a, b in evs) / reps
-    for a, b in evs:
-        a.record()
-        ops.down(h, plan.offsets, w2, hidden=H, out=y)
-        b.record()
-    torch.cuda.synchronize()
-    down_ms = sum(a.elapsed_time(b) for a, b in evs) / reps
+    kernels = {"gateup_swiglu": (4.0 * S * H * I, lambda: ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I, out=h)),
+               "down": (2.0 * S * H * I, lambda: ops.down(h, plan.offsets, w2, hidden=H, out=y))}
+    if train and not args.int8_rotation:
+        dgu = torch.empty((S, 2 * I), dtype=torch.bfloat16, device=dev)
+        dxs = torch.empty((S, H), dtype=torch.bfloat16, device=dev)
+        glow = ops.lora_project(y, plan.offsets, lora, forward=False)
+        kernels["down_dx"] = (2.0 * S * H * I, lambda: ops.down_dx(y, plan.offsets, w2, st.gate_up, inter=I,
+                                                                   out=dgu, lora=lora, rank_a=glow))
+        kernels["gateup_dx"] = (4.0 * S * H * I, lambda: ops.gateup_dx(dgu, plan.offsets, w1, w3, hidden=H,
+                                                                       out=dxs))
+    kernel_ms = {name: time_kernel(fn, reps) for name, (_, fn) in kernels.items()}
     kclk = kclocks.stop()
+    top = max(kernel_ms, key=kernel_ms.get)  # the step's dominant kernel
+    top_flops = kernels[top][0]
+    del h, y
 
     # ---- end to end through the public API with host buffers
     host_in = [x.cpu().pin_memory(), logits.cpu().pin_memory()] + ([g_out.cpu().pin_memory()] if train else [])
@@ -332,14 +369,17 @@ def run_ours(args, cfg, rank, world, dev):
     ops.check_device()
 
     if world > 1:
-        t = torch.tensor([ms, e2e_ms], device=dev)
+        t = torch.tensor([ms, e2e_ms, fwd_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0]), float(t[1])
+        ms, e2e_ms, fwd_ms = float(t[0]), float(t[1]), float(t[2])
 
     peaks = load_peaks()
-    flops_gu = 4.0 * S * H * I
-    achieved = flops_gu / (gu_ms * 1e-3) / 1e12
-    traffic = NCU_TRAFFIC.get(f"{args.config}-gateup")
+    achieved = top_flops / (kernel_ms[top] * 1e-3) / 1e12
+    fmt = make_weights_fmt(cfg, args)
+    kname = f"{top}_{cfg['fmt']}"
+    traffic = NCU_TRAFFIC.get(f"{args.config}-{kname}") if not args.int8_rotation else None
+    lora_flops = 6.0 * S * LORA_RANK * (H + I)  # rank projection + rank block, fwd and dX, and the factor grads
+    step_flops = (12.0 * S * H * I + lora_flops) if train else 6.0 * S * H * I
     line = {
         "metric": METRIC,
         "value": world * T / (ms * 1e-3),
@@ -351,31 +391,35 @@ def run_ours(args, cfg, rank, world, dev):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16 activations x " + cfg["fmt"] + " weights, fp32 accumulate",
+        "dtype": "bf16 activations x " + fmt + " weights, fp32 accumulate",
         "data": "synthetic (seeded torch.randn; random-init experts quantised on the GPU)",
         "config": {
             "workload": f"{args.config}: one routed expert FFN layer "
                         + (f"forward + dX backward with a rank-{LORA_RANK} LoRA on w2 (adapter grads included)"
                            if train else "forward") + f", T={T} H={H} E={E} k={k} I={I} "
-                        f"{cfg['fmt']} experts" + (f", Zipf({cfg['zipf']}) load" if cfg["zipf"] else ""),
+                        f"{fmt} experts" + (f", Zipf({cfg['zipf']}) load" if cfg["zipf"] else ""),
             "tokens_per_gpu": T, "hidden": H, "experts": E, "top_k": k, "intermediate": I,
-            "weights": cfg["fmt"], "parallelism": f"dp{world} token-parallel replicas (experts replicated)",
+            "weights": fmt, "parallelism": f"dp{world} token-parallel replicas (experts replicated)",
             "l2": f"no flush: inputs {(T * H * 2 + weight_bytes(cfg)) / 1e6:.0f} MB per step exceed the 126 MB L2",
         },
-        "tflops": world * ((12.0 * S * H * I + 6.0 * S * LORA_RANK * (H + I)) if train else 6.0 * S * H * I)
-                  / (ms * 1e-3) / 1e12,
-        "kernel_ms": {"gateup_swiglu": gu_ms, "down": down_ms},
+        "tflops": world * step_flops / (ms * 1e-3) / 1e12,
+        "forward": {"value": world * T / (fwd_ms * 1e-3), "unit": "tokens/s", "ms_per_step": fwd_ms,
+                    "tflops": world * 6.0 * S * H * I / (fwd_ms * 1e-3) / 1e12},
+        "kernel_ms": kernel_ms,
         "roofline": {
-            "kernel": f"gateup_swiglu_{cfg['fmt']}",
+            "kernel": kname,
             "bound": "tensor",
             "achieved": achieved,
             "peak": peaks["bf16_tflops"],
             "unit": "TFLOP/s",
             "frac": achieved / peaks["bf16_tflops"],
             "peak_source": f"{peaks['source']} bf16 dense (burst; kernel timed alone)",
-            "algorithmic": f"4*S*H*I = {flops_gu / 1e9:.1f} GFLOP per launch",
-            "traffic": traffic,
+            "algorithmic": f"{top_flops / (S * H * I):.0f}*S*H*I = {top_flops / 1e9:.1f} GFLOP per launch "
+                           f"(the step's longest kernel)",
+            "traffic": None if traffic is None else traffic[0],
+            "traffic_source": None if traffic is None else f"ncu dram__bytes_read+write, {traffic[1]}",
             "clocks": kclk,
+            "step_frac": (step_flops / (ms * 1e-3) / 1e12) / peaks["bf16_tflops"],
         },
         "e2e": {
             "value": world * T / (e2e_ms * 1e-3),
@@ -384,11 +428,19 @@ def run_ours(args, cfg, rank, world, dev):
             "d2h_bytes_per_step": T * H * 2 * (2 if train else 1),
             "copies": "pinned host buffers; 2 slots, uploads and downloads on their own streams overlap compute",
         },
-        "gpu_launches": (KERNELS_PER_STEP + (TRAIN_EXTRA_KERNELS if train else 0)) * args.steps,
+        "gpu_launches": (KERNELS_PER_STEP + (TRAIN_EXTRA_KERNELS if train else 0)
+                         + rotation_kernels(cfg, args, train)) * args.steps,
         "clocks": clk,
     }
     return line
 
+
+def rotation_kernels(cfg, args, train):
+    """Rotation launches per step in the block-Hadamard INT8 format: tokens and h
+    forward; dh (with the SwiGLU backward) and dx backward."""
+    if not (cfg["fmt"] == "int8" and args.int8_rotation):
+        return 0
+    return 4 if train else 2
 
 
 # ----------------------------------------------------------------------------- expert-parallel arm
@@ -566,6 +618,10 @@ def run_ep(args, cfg, rank, world, dev):
                    f" (GEMMs capped at {torch.cuda.get_device_properties(dev).multi_processor_count - free_sms} SMs)"
                    if chunks > 1 and world > 1 else ""),
             "l2": "no flush: each layer's routed activations exceed the 126 MB L2",
+            **({"timed_outside_path": "per layer after the first: an RMS norm and the router logits "
+                                      "(u @ gate.T) in torch/cuBLAS, and the residual add; they feed the "
+                                      "next layer's routing and are not part of the routed expert FFN"}
+               if layers > 1 else {}),
         },
         "tflops": 6.0 * S_total * H * I * layers / (ms * 1e-3) / 1e12,
         "roofline": {
@@ -596,13 +652,23 @@ def run_ep(args, cfg, rank, world, dev):
 # ----------------------------------------------------------------------------- CPU reference (oracle port)
 
 class CpuReference:
-    """The CPU restatement of the reference's torch path (oracle/), on host cores."""
+    """The CPU restatement of the reference's torch path (oracle/), on host cores.
 
-    def __init__(self, cfg, sample_tokens, seed=1234):
+    The reference's ``chunked_dequant`` runner (the default) dequantises every
+    expert chunk on every forward, and its frozen-linear autograd functions
+    dequantise again in backward (linear.py:116-125, 191-203).  One step of the
+    workload is therefore costed as: the full dequantisation of all experts
+    (once for a forward, twice for forward + dX), plus the routed compute of
+    all T tokens, measured on a ``sample``-token slice and scaled by
+    T / sample (the compute is linear in the tokens; the dequantisation is
+    not, so it is charged once per T tokens, never per sample)."""
+
+    def __init__(self, cfg, sample_tokens, seed=1234, train=False, rotation=False):
         import numpy as np
         from oracle import quant as oq
 
         self.cfg = cfg
+        self.train = train
         rng = np.random.default_rng(seed)
         T, H, E, k, I = sample_tokens, cfg["H"], cfg["E"], cfg["k"], cfg["I"]
         self.T = T
@@ -613,6 +679,12 @@ class CpuReference:
             p = 1.0 / np.arange(1, E + 1) ** cfg["zipf"]
             p = p / p.sum()
             self.logits = (self.logits + 2.0 * np.log(p)[None, :]).astype(np.float32)
+        self.g = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32)) if train else None
+        self.lora = None
+        if train:
+            self.lora = {"a": oq.bf16_round((rng.standard_normal((E, LORA_RANK, I)) / I ** 0.5).astype(np.float32)),
+                         "b": oq.bf16_round((rng.standard_normal((E, H, LORA_RANK)) * 0.02).astype(np.float32)),
+                         "scale": 16.0 / LORA_RANK}
         raw = [(rng.standard_normal(s) * 0.02).astype(np.float32) for s in ((E, I, H), (E, I, H), (E, H, I))]
         self.threads = os.cpu_count() or 1
         if cfg["fmt"] == "nf4":
@@ -630,11 +702,11 @@ class CpuReference:
                                    "code": p[0]["code"], "ncode": p[0]["nested_code"],
                                    "shape": raw[key].shape})
         elif cfg["fmt"] == "int8":
-            self.store = [oq.int8_quantize(w, 0)[:2] for w in raw]
+            self.store = [oq.int8_quantize(w, oq.best_group_size(w.shape[-1]) if rotation else 0) for w in raw]
         else:
             self.store = [oq.bf16_round(w) for w in raw]
 
-    def _dequant(self):
+    def dequant(self):
         from concurrent.futures import ThreadPoolExecutor
         import numpy as np
         from oracle import quant as oq
@@ -651,19 +723,40 @@ class CpuReference:
                 return oq.nf4_dequantize_2d({"packed": g["nf4"][e], "absmax": g["absmax"][e],
                                              "nested_absmax": g["nabsmax"][e], "offset": g["offset"][e],
                                              "code": g["code"], "nested_code": g["ncode"]}, (o, i))
-            q, s = self.store[key]
-            return oq.bf16_round(oq.int8_dequantize(q[e], s[e], 0))
+            q, s, gs = self.store[key]
+            return oq.bf16_round(oq.int8_dequantize(q[e], s[e], gs))
 
         E = self.cfg["E"]
         with ThreadPoolExecutor(self.threads) as pool:
             flat = list(pool.map(one, [(key, e) for key in range(3) for e in range(E)]))
         return [np.stack(flat[key * E:(key + 1) * E]) for key in range(3)]
 
-    def step(self):
+    def compute(self, dense):
+        """The routed compute on the sample: forward, or forward + dX (the
+        oracle's dX pass recomputes the expert forward it needs)."""
         from oracle import moe as om
         idx, w = om.route_topk(self.logits, self.cfg["k"])
-        w1, w3, w2 = self._dequant()
-        return om.moe_forward(self.x, idx, w, w1, w3, w2, bf16=True)
+        if self.train:
+            return om.moe_backward_dx(self.x, idx, w, *dense, self.g, bf16=True, lora=self.lora)
+        return om.moe_forward(self.x, idx, w, *dense, bf16=True)
+
+    def step_seconds(self):
+        """(seconds for one full-T step, dequantisation seconds, sample compute seconds)."""
+        t = time.perf_counter()
+        dense = self.dequant()
+        t_deq = time.perf_counter() - t
+        t = time.perf_counter()
+        self.compute(dense)
+        t_cmp = time.perf_counter() - t
+        passes = 2 if self.train else 1
+        return passes * t_deq + t_cmp * self.cfg["T"] / self.T, t_deq, t_cmp
+
+    def describe(self, n):
+        what = "forward + dX with a rank-16 LoRA on w2" if self.train else "forward"
+        passes = "twice (forward and backward)" if self.train else "once"
+        return (f"{n} step(s); each: the full dequantisation of all {self.cfg['E']} x 3 experts, charged {passes} "
+                f"per {self.cfg['T']}-token step, plus the routed {what} of a {self.T}-token sample scaled by "
+                f"{self.cfg['T']}/{self.T}; oracle/ numpy restatement of the reference torch path")
 
 
 def cpu_sample_tokens(cfg):
@@ -682,44 +775,44 @@ def cpu_sample_cfg(cfg):
 
 def run_reference(args, cfg):
     cfg, per, note = cpu_sample_cfg(cfg)
-    ref = CpuReference(cfg, cpu_sample_tokens(cfg))
+    train = args.mode == "train" and not cfg.get("layers")
+    ref = CpuReference(cfg, cpu_sample_tokens(cfg), train=train, rotation=args.int8_rotation)
     for _ in range(args.warmup):
-        ref.step()
-    t = time.perf_counter()
+        ref.step_seconds()
+    total = 0.0
     for _ in range(args.steps):
-        ref.step()
-    sec = (time.perf_counter() - t) / args.steps
-    value = ref.T / sec / per
-    sample = (f"{ref.T} of {cfg['T']} tokens per step, full dequantisation of all {cfg['E']} experts each step "
-              f"(as the reference's chunked_dequant path does every forward)" + (f"; {note}" if note else ""))
+        total += ref.step_seconds()[0]
+    sec = total / args.steps
+    value = cfg["T"] / sec / per
+    sample = ref.describe(args.steps) + (f"; {note}" if note else "")
     return {
         "metric": METRIC, "impl": "reference", "value": value, "unit": "tokens/s", "n_gpus": 0,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32 numpy with bf16 rounding points",
         "data": "synthetic (seeded numpy)",
-        "config": {"workload": f"{args.config} (CPU sample)", "sample": sample},
+        "config": {"workload": f"{args.config} " + ("forward + dX" if train else "forward") + " (CPU, projected "
+                   "to the full token count)", "sample": sample},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
-def cpu_baseline(cfg):
+def cpu_baseline(cfg, args):
     cfg, per, note = cpu_sample_cfg(cfg)
-    ref = CpuReference(cfg, cpu_sample_tokens(cfg))
-    ref.step()  # warm
+    train = args.mode == "train" and not cfg.get("layers")
+    ref = CpuReference(cfg, cpu_sample_tokens(cfg), train=train, rotation=args.int8_rotation)
+    ref.step_seconds()  # warm
     t = time.perf_counter()
-    n = 0
+    n, total = 0, 0.0
     while True:
-        ref.step()
+        total += ref.step_seconds()[0]
         n += 1
         if time.perf_counter() - t > 10.0 or n >= 3:
             break
-    sec = (time.perf_counter() - t) / n
-    return {"value": ref.T / sec / per, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
-            "sample": f"{n} forward(s) of {ref.T} tokens of the {cfg['T']}-token workload, dequantising all "
-                      f"experts each forward; oracle/ numpy restatement of the reference torch path"
-                      + (f"; {note}" if note else "")}
+    sec = total / n
+    return {"value": cfg["T"] / sec / per, "unit": "tokens/s", "cores": ref.threads, "kind": "port",
+            "sample": ref.describe(n) + (f"; {note}" if note else "")}
 
 
 # ----------------------------------------------------------------------------- main
@@ -731,8 +824,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="fwd", choices=["fwd", "train"],
-                    help="fwd: forward only; train: forward + dX backward through the frozen experts")
+    ap.add_argument("--mode", default=None, choices=["fwd", "train"],
+                    help="train (default for c0-c3 on one GPU: BASELINE config 2's step): forward + dX backward "
+                         "through the frozen experts with a rank-16 LoRA on w2; fwd: forward only (the default "
+                         "for the multi-GPU and c4 runs)")
+    ap.add_argument("--int8-rotation", action="store_true",
+                    help="c3: INT8 in the reference's default block-Hadamard format (groups of 256)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-chunks", type=int, default=2,
                     help="N > 1: token chunks per layer whose exchanges overlap the other chunks' GEMMs")
@@ -754,8 +851,12 @@ def main():
     cfg = CONFIGS[args.config]
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.mode is None:
+        args.mode = "fwd" if (world > 1 or cfg.get("layers")) else "train"
     if args.mode == "train" and (world > 1 or cfg.get("layers")):
         raise SystemExit("--mode train runs the single-GPU layer (c0-c3 on one GPU)")
+    if args.int8_rotation and cfg["fmt"] != "int8":
+        raise SystemExit("--int8-rotation applies to the INT8 workload (c3)")
 
     if args.impl == "reference":
         if rank == 0:
@@ -777,7 +878,7 @@ def main():
         line = run_ep(args, cfg, rank, world, dev) if (world > 1 or cfg.get("layers")) else \
             run_ours(args, cfg, rank, world, dev)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the host-core baseline, N = 1 only
-            line["cpu_baseline"] = cpu_baseline(cfg)
+            line["cpu_baseline"] = cpu_baseline(cfg, args)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

@@ -154,7 +154,7 @@ int mirai_permute_rows_bf16(const void* tokens, int64_t num_tokens, const int64_
  * Replaces _FrozenDequantBatchedLinearPair.forward + silu*up (linear.py:166-189,
  * experts.py:301-317).  `gate_up` (nullable) receives the pre-activation
  * [S, 2I] bf16 (gate | up) that the dX path consumes.  Requires H % 64 == 0,
- * I % 128 == 0. */
+ * I % 64 == 0. */
 int mirai_moe_gateup_swiglu_bf16(const void* x_sorted, const int32_t* offsets, int32_t num_experts,
                                  int64_t num_rows, int32_t hidden, int32_t inter, const void* w1,
                                  const void* w3, void* h, void* gate_up, mirai_stream_t stream);
@@ -344,9 +344,45 @@ int mirai_nf4_quantize(const void* weight_bf16, int32_t num_experts, int64_t out
 /* Per-output-channel symmetric INT8 of `rows` rows of `in_features`
  * (quant.py:189-235 with group_size 0): scale = max(amax/127, 1e-30),
  * q = clamp(round_half_even(x / scale), -127, 127).  weight_dtype is
- * MIRAI_DTYPE_F32 or MIRAI_DTYPE_BF16. */
+ * MIRAI_DTYPE_F32 or MIRAI_DTYPE_BF16.  The block-Hadamard format
+ * (group_size > 0) quantises rows rotated first by mirai_rotate_rows. */
 int mirai_int8_quantize_rows(const void* weight, int32_t weight_dtype, int64_t rows, int64_t in_features,
                              int8_t* q, float* scale, mirai_stream_t stream);
+
+/* ------------------------------------- a5: the block-Hadamard INT8 format
+ * The reference's default INT8 storage rotates each weight row's groups of g
+ * input features (g = 4^m, the largest of 256/64/16 dividing in_features,
+ * quant.py:87-91) by H = h4 (x) ... (x) h4 / sqrt(g) before quantising
+ * (quant.py:103-122, 189-235), so q * s = W H, and de-rotates the weight before
+ * each matmul (_dequantize_weight, quant.py:238-260).  H is symmetric and
+ * orthogonal, so this library rotates activations instead
+ * (rotated_int8.py:7-21) and runs the plain INT8 GEMMs on the stored codes:
+ *   forward  y  = (x H) (q s)^T         rotate x (and h, for w2) first
+ *   dX       dx = (dy (q s)) H          rotate the GEMM result after
+ *
+ * mirai_rotate_rows: out = in H along every g-wide group of the last dimension
+ * of a row-major [rows, cols] matrix (cols % g == 0, cols % 16 == 0, g a power
+ * of 4 in [4, 4096]), in fp32; in/out dtypes MIRAI_DTYPE_BF16 or _F32, 16-byte
+ * aligned; out may equal in.  Replaces _rotate_last_dim (quant.py:152-182). */
+int mirai_rotate_rows(const void* in, int32_t in_dtype, int64_t rows, int32_t cols, int32_t group, void* out,
+                      int32_t out_dtype, mirai_stream_t stream);
+
+/* The down projection's dX for the block-Hadamard format, in two steps:
+ * mirai_moe_down_dh_int8[_lora] computes dh_raw = bf16(grad_y (q s))
+ * [S, I] (+ rank_a rank_b_e, rank_b = A zero-padded to [E*64, I] AND rotated
+ * by H, so that rotating the sum gives the adapter's exact contribution); then
+ * mirai_swiglu_backward_rotated rotates dh_raw into dh = bf16(dh_raw H) and
+ * applies the SwiGLU backward of mirai_moe_down_dx_* to the saved gate_up,
+ * writing grad_gate_up [S, 2I].  (linear.py:116-125 with the de-rotated weight
+ * of quant.py:238-260, then experts.py:301-317 autograd.) */
+int mirai_moe_down_dh_int8(const void* grad_y, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                           int32_t hidden, int32_t inter, const mirai_int8_weight* w2, void* dh,
+                           mirai_stream_t stream);
+int mirai_moe_down_dh_lora_int8(const void* grad_y, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                                int32_t hidden, int32_t inter, const mirai_int8_weight* w2, const void* rank_a,
+                                const void* rank_b, void* dh, mirai_stream_t stream);
+int mirai_swiglu_backward_rotated(const void* dh, const void* gate_up, int64_t rows, int32_t inter, int32_t group,
+                                  void* grad_gate_up, mirai_stream_t stream);
 
 #ifdef __cplusplus
 }

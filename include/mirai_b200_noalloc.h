@@ -26,7 +26,13 @@
  *     on one stream are ordered and safe;
  *   - the first call on each device looks up the array's address
  *     (cudaGetSymbolAddress, which can load the module): make that first call
- *     outside any stream capture.
+ *     outside any stream capture;
+ *   - under lazy module loading (the CUDA default) the first call into this
+ *     library on a device loads its device image, the 1 MiB array included,
+ *     which can grow device memory once: make one library call on each device
+ *     before a memory-budget check that must hold until the launch;
+ *   - arguments are range-checked before any size is derived from them: a bad
+ *     T, k or E is MIRAI_ERR_INVALID_ARG, never MIRAI_ERR_WORKSPACE.
  */
 #ifndef MIRAI_B200_NOALLOC_H_
 #define MIRAI_B200_NOALLOC_H_

@@ -128,6 +128,12 @@ SIGNATURES = {
     "mirai_nf4_quantize": (ctypes.c_int, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp,
                                           c_vp, c_vp, c_size, c_vp]),
     "mirai_int8_quantize_rows": (ctypes.c_int, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp]),
+    "mirai_rotate_rows": (ctypes.c_int, [c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i32, c_vp]),
+    "mirai_swiglu_backward_rotated": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
+    "mirai_moe_down_dh_int8": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, ctypes.POINTER(Int8Weight),
+                                              c_vp, c_vp]),
+    "mirai_moe_down_dh_lora_int8": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32,
+                                                   ctypes.POINTER(Int8Weight), c_vp, c_vp, c_vp, c_vp]),
 }
 
 _lib = None

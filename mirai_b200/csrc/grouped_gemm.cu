@@ -655,7 +655,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           tmem_ld_32x32b_x32(tb + c * 32, g);
           tmem_ld_32x32b_x32(tb + TN / 2 + c * 32, u);
           tmem_ld_wait();
-          if (valid) {
+          if (valid && col0 + c * 32 < p.N) {  // the last tile of an I % 128 == 64 layer is half empty
             uint32_t hp[16], gp[16], up[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -684,8 +684,9 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             }
           }
         }
-      } else if (MODE == DXDOWN) {
+      } else if (MODE == DXDOWN && p.gate_up != nullptr) {
         // dgu = SwiGLU backward of the saved (gate, up) given dh = dy W2
+        // (without saved gate/up: dh itself, [S, I], by the plain epilogue below)
         // (autograd of experts.py:301-317 in bf16: mul, silu backward)
         const int64_t ld2 = 2 * (int64_t)p.N;
         constexpr int NCH = TN / 32;
@@ -992,9 +993,12 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
               blk = wr * nblk_row + nbg;
               qcode = dq->absq[(PREFETCH ? abuf * ABUF : 0) + kk * (C::B_ROWS / 64) + nbq];
             }
-            const float nabs = PREFETCH ? __ldg(p.q[key].nested_absmax + (size_t)e * p.q[key].n_nested +
-                                                (blk >> p.nbs_shift))
-                                        : dq->nested[key][blk >> p.nbs_shift];
+            // rows past the weight matrix (a partial last tile) read no scale: their block index
+            // lies beyond the expert's nested absmax
+            const float nabs = !live ? 0.f
+                               : PREFETCH ? __ldg(p.q[key].nested_absmax + (size_t)e * p.q[key].n_nested +
+                                                  (blk >> p.nbs_shift))
+                                          : dq->nested[key][blk >> p.nbs_shift];
             const float scale = live ? __fadd_rn(__fmul_rn(dq->ncode[key][qcode], nabs), off[key]) : 0.f;
             Nf4Tab tab;
             nf4_table(code, scale, tab);
@@ -1098,7 +1102,7 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
     attr_set = true;
   }
   Params q = p;
-  q.n_tiles = MODE == GATEUP ? q.N / (C::TN / 2) : (q.N + C::TN - 1) / C::TN;
+  q.n_tiles = MODE == GATEUP ? (q.N + C::TN / 2 - 1) / (C::TN / 2) : (q.N + C::TN - 1) / C::TN;
   const int64_t max_tiles = ((q.S + C::TILE_M - 1) / C::TILE_M + q.E) * (int64_t)q.n_tiles;
   static const char* names[4] = {"gateup_swiglu", "down", "down_dx", "gateup_dx"};
   const int limit = gemm_sm_limit();
@@ -1154,20 +1158,22 @@ static inline bool mis16(const void* ptr) { return (reinterpret_cast<uintptr_t>(
 // Shared host-side checks, the A-operand tensor map and the mode geometry.
 template <int MODE>
 int prepare(const char* name, const void* a, const int32_t* offsets, int E, int64_t S, int K, int N, void* out,
-            void* gate_up, Params& p, CUtensorMap& ta) {
+            void* gate_up, Params& p, CUtensorMap& ta, bool dh_only) {
   if (E <= 0 || E > kMaxExperts || S < 0 || K <= 0 || N <= 0)
     return set_error(MIRAI_ERR_INVALID_ARG, "%s: bad sizes (E=%d, S=%lld, K=%d, N=%d)", name, E, (long long)S, K, N);
-  // column granularity: gate/up tiles pair 128 W1 rows with 128 W3 rows; the
-  // other modes mask partial 256-column tiles in 32-column chunks (and, for
-  // NF4/INT8, by weight row), so they need N % 64 only
-  const int ntile = MODE == GATEUP ? BN / 2 : 64;
+  // column granularity: every mode masks a partial last tile (gate/up: 128 W1
+  // rows beside 128 W3 rows; the others: 256 columns) in 32-column chunks and,
+  // for NF4/INT8, by weight row, so N % 64 is enough
+  const int ntile = 64;
   if (K % BK != 0 || N % ntile != 0)
     return set_error(MIRAI_ERR_UNSUPPORTED, "%s: needs K %% %d == 0 and N %% %d == 0 (K=%d, N=%d)", name, BK, ntile,
                      K, N);
   if (S >= (int64_t)1 << 31) return set_error(MIRAI_ERR_UNSUPPORTED, "%s: more than 2^31 routed rows", name);
   if (!a || !offsets || !out || mis16(out) || (gate_up && mis16(gate_up)))
     return set_error(MIRAI_ERR_INVALID_ARG, "%s: null or misaligned pointer", name);
-  if (MODE == DXDOWN && !gate_up) return set_error(MIRAI_ERR_INVALID_ARG, "%s: saved gate/up is required", name);
+  if (MODE == DXDOWN && !gate_up && !dh_only)
+    return set_error(MIRAI_ERR_INVALID_ARG, "%s: saved gate/up is required", name);
+  if (dh_only) gate_up = nullptr;
   p = Params{};
   p.offsets = offsets;
   p.E = E;
@@ -1270,7 +1276,7 @@ struct RankBlock {
 template <int MODE>
 int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t S, int K, int N, void* out,
         void* gate_up, const WeightArg& w0, const WeightArg& w1, int rows, int cols, mirai_stream_t stream,
-        const RankBlock* ext = nullptr, int nsrc = 1) {
+        const RankBlock* ext = nullptr, int nsrc = 1, bool dh_only = false) {
   if (nsrc <= 0 || E <= 0 || (int64_t)nsrc * E > kMaxExperts)
     return set_error(MIRAI_ERR_INVALID_ARG, "%s: %d sources x %d experts outside 1..%d segments", name, nsrc, E,
                      kMaxExperts);
@@ -1278,7 +1284,7 @@ int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t 
   Params p;
   CUtensorMap ta, t0, t1, txa, txb;
   const int box_rows = kmajor_box_rows(w0.fmt);
-  int rc = prepare<MODE>(name, a, offsets, nsrc * E, S, K, N, out, gate_up, p, ta);
+  int rc = prepare<MODE>(name, a, offsets, nsrc * E, S, K, N, out, gate_up, p, ta, dh_only);
   p.nsrc = nsrc;
   if (!rc && ext) {
     if (!ext->a || !ext->b) rc = set_error(MIRAI_ERR_INVALID_ARG, "%s: null rank-block operand", name);
@@ -1473,6 +1479,22 @@ int mirai_moe_down_dx_lora_int8(const void* grad_y, const int32_t* offsets, int3
   const RankBlock rb{rank_a, rank_b};
   return run<DXDOWN>("down_dx_lora_int8", grad_y, offsets, num_experts, num_rows, hidden, inter, grad_gate_up,
                      const_cast<void*>(gate_up), wi(w2), wi(w2), hidden, inter, stream, &rb);
+}
+
+// ---- dX: down without the SwiGLU backward: dh = dy W2 [S, I] (+ the rank block).  The rotated
+// INT8 format rotates dh before the SwiGLU backward (mirai_swiglu_backward_rotated).
+int mirai_moe_down_dh_int8(const void* grad_y, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                           int32_t hidden, int32_t inter, const mirai_int8_weight* w2, void* dh,
+                           mirai_stream_t stream) {
+  return run<DXDOWN>("down_dh_int8", grad_y, offsets, num_experts, num_rows, hidden, inter, dh, nullptr, wi(w2),
+                     wi(w2), hidden, inter, stream, nullptr, 1, true);
+}
+int mirai_moe_down_dh_lora_int8(const void* grad_y, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                                int32_t hidden, int32_t inter, const mirai_int8_weight* w2, const void* rank_a,
+                                const void* rank_b, void* dh, mirai_stream_t stream) {
+  const RankBlock rb{rank_a, rank_b};
+  return run<DXDOWN>("down_dh_lora_int8", grad_y, offsets, num_experts, num_rows, hidden, inter, dh, nullptr,
+                     wi(w2), wi(w2), hidden, inter, stream, &rb, 1, true);
 }
 
 // ---- dX: gate/up.  dx = [dgate | dup] [W1 ; W3] (K = 2I, N = H).  B = W1/W3 read MN-major.

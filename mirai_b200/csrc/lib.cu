@@ -7,3 +7,4 @@
 #include "quantize.cu"
 #include "lora.cu"
 #include "exchange.cu"
+#include "rotate.cu"

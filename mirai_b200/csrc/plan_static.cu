@@ -19,7 +19,11 @@
 //    plans; calls on one stream are ordered and safe;
 //  * the first call on each device looks the array's address up
 //    (cudaGetSymbolAddress, which can load the module); make that first call
-//    outside any stream capture.
+//    outside any stream capture;
+//  * with lazy module loading (the CUDA default) the library's device image,
+//    this 1 MiB array included, is loaded by the first library call on a
+//    device, which can grow device memory once: make one library call on each
+//    device before a memory-budget check that must stay true until the launch.
 #include <mutex>
 
 #include "common.cuh"
@@ -65,6 +69,10 @@ size_t mirai_dispatch_plan_static_scratch_bytes(void) { return mirai::kPlanStati
 int mirai_dispatch_plan_static(const int64_t* top_indices, int64_t num_tokens, int32_t top_k, int32_t num_experts,
                                int64_t* counts, int64_t* starts, int32_t* offsets, int64_t* sort_positions,
                                int64_t* sorted_token_indices, int64_t* inverse_order, mirai_stream_t stream) {
+  // arguments first, so that an unusable plan is reported as such and not as a scratch shortfall
+  if (const char* why = mirai::plan_sizes_problem(num_tokens, top_k, num_experts))
+    return mirai::set_error(MIRAI_ERR_INVALID_ARG, "dispatch_plan_static: %s (T=%lld, k=%d, E=%d)", why,
+                            (long long)num_tokens, top_k, num_experts);
   const size_t need = mirai_dispatch_plan_workspace_bytes(num_tokens, top_k, num_experts);
   if (need > mirai::kPlanStaticScratchBytes)
     return mirai::set_error(MIRAI_ERR_WORKSPACE,

@@ -134,6 +134,18 @@ constexpr int kPlanRounds = 8;
 constexpr int kPlanChunk = kPlanThreads * kPlanRounds;  // 2048 routes per chunk
 constexpr int kPlanMaxExperts = 1024;
 
+// Range check shared by every dispatch-plan entry point, made before any size
+// is computed from the arguments: nullptr when they are usable, else why not.
+// T*k must fit the plan's int32 row offsets, so T is bounded by INT32_MAX / k
+// before the product is formed (no int64 overflow for any T).
+inline const char* plan_sizes_problem(int64_t num_tokens, int32_t top_k, int32_t num_experts) {
+  if (top_k <= 0) return "top_k must be positive";
+  if (num_experts <= 0 || num_experts > kPlanMaxExperts) return "expert count outside [1, 1024]";
+  if (num_tokens < 0) return "negative token count";
+  if (num_tokens > (int64_t)INT32_MAX / top_k) return "T*k exceeds the int32 range of the plan";
+  return nullptr;
+}
+
 __global__ void __launch_bounds__(kPlanThreads) plan_histogram_kernel(const int64_t* __restrict__ idx,
                                                                       int64_t S, int E,
                                                                       int* __restrict__ chunk_counts) {
@@ -413,7 +425,7 @@ int mirai_route_topk(const float* logits, int64_t num_tokens, int32_t num_expert
 }
 
 size_t mirai_dispatch_plan_workspace_bytes(int64_t num_tokens, int32_t top_k, int32_t num_experts) {
-  if (num_tokens <= 0 || top_k <= 0 || num_experts <= 0) return 0;
+  if (num_tokens <= 0 || mirai::plan_sizes_problem(num_tokens, top_k, num_experts) != nullptr) return 0;
   const int64_t S = num_tokens * top_k;
   const int64_t chunks = (S + kPlanChunk - 1) / kPlanChunk;
   return (size_t)(chunks * num_experts * sizeof(int));
@@ -423,10 +435,10 @@ int mirai_dispatch_plan(const int64_t* top_indices, int64_t num_tokens, int32_t 
                         int64_t* counts, int64_t* starts, int32_t* offsets, int64_t* sort_positions,
                         int64_t* sorted_token_indices, int64_t* inverse_order, void* workspace,
                         size_t workspace_bytes, mirai_stream_t stream) {
-  if (num_tokens < 0 || top_k <= 0 || num_experts <= 0 || num_experts > kPlanMaxExperts)
-    return set_error(MIRAI_ERR_INVALID_ARG, "dispatch_plan: need E in [1, %d], k > 0", kPlanMaxExperts);
+  if (const char* why = mirai::plan_sizes_problem(num_tokens, top_k, num_experts))
+    return set_error(MIRAI_ERR_INVALID_ARG, "dispatch_plan: %s (T=%lld, k=%d, E=%d)", why, (long long)num_tokens,
+                     top_k, num_experts);
   const int64_t S = num_tokens * top_k;
-  if (S >= (int64_t)1 << 31) return set_error(MIRAI_ERR_INVALID_ARG, "dispatch_plan: T*k exceeds int32 range");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (!counts || !starts || !offsets) return set_error(MIRAI_ERR_INVALID_ARG, "dispatch_plan: null pointer");
   if (S == 0) {

@@ -522,7 +522,7 @@ class ExpertParallelMoE:
 
     def __init__(self, shard: ExpertShard, *, top_k: int, inter: int, group=None, chunks: int = 2,
                  ops: StepOps | None = None, copy_streams: int = 1, layout: str = "source",
-                 regroup: str = "auto"):
+                 regroup: str = "auto", check_device: bool = True):
         self.shard, self.top_k, self.inter, self.group = shard, top_k, inter, group
         self.chunks = max(1, int(chunks))
         self.ops = ops or CudaStepOps()
@@ -537,11 +537,25 @@ class ExpertParallelMoE:
         self.n_copy_streams = max(1, int(copy_streams))
         self.copy_streams: list[torch.cuda.Stream] = []  # side streams when n_copy_streams > 1
         self.epoch = 0  # exchanges so far; the same sequence on every rank
+        # read the device error word at the host sync each call already makes (the count read)
+        self.check_device = bool(check_device)
         # optional probe: called as on_phase(name, stream) at phase boundaries
         self.on_phase = None
 
     def close(self) -> None:
         self.buffers.release()
+
+    def check(self) -> None:
+        """Raise ``MiraiError`` if a kernel or an arrival wait of this device
+        recorded an error since the last check (a wait gives up after 2 s and
+        leaves partly arrived rows behind it).  ``forward`` does this at the
+        start of every call (``check_device=True``); call it after the last
+        layer of a step, or call ``ops.check_device()``."""
+        from . import ops as _ops
+        code, info = _ops.device_status()
+        if code:
+            raise _ops._lib.MiraiError(code, f"expert-parallel layer on rank {self.shard.rank}: device error at "
+                                             f"site {info} (700 + peer slot: an arrival wait that gave up)")
 
     def _copy_blocks(self, blocks, peer_base: list[int], my_base: int, row_bytes: int, stream) -> None:
         """Issue one block list of a ``BlockPlan`` on ``stream`` (or spread over
@@ -602,6 +616,11 @@ class ExpertParallelMoE:
         dist.all_gather_into_tensor(allm, mine, group=self.group)
         row_bytes = H * tokens.element_size()
         counts = allm.cpu().numpy()
+        if self.check_device and tokens.is_cuda:
+            # The stream has just drained up to the count gather: an arrival wait of an earlier call
+            # that gave up (a peer more than 2 s late) or a failed kernel check is reported here,
+            # before this call moves any row.  The last call's status is read by check().
+            self.check()
         check_counts(counts, me, [p[2].shape[0] for p in prep])
         plan = exchange_blocks(counts, me, self.layout, regroup=self.regroup, hidden=H,
                                inter=self.inter, row_bytes=row_bytes)

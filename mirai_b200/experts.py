@@ -9,22 +9,32 @@ storage formats, reading the reference's own buffers in place:
 * NF4: ``{key}_nf4``, ``{key}_nf4_absmax``, ``{key}_nf4_nabsmax``,
   ``{key}_nf4_offset``, ``{key}_nf4_code``, ``{key}_nf4_ncode`` and the
   ``_Nf4Meta`` block sizes (experts.py:998-1031, 1424-1470);
-* INT8 (group size 0): ``{key}_int8`` and ``{key}_scale`` (experts.py:1382-1422);
+* INT8: ``{key}_int8`` and ``{key}_scale`` with ``{key}_group_size`` 0
+  (plain per-output-channel) or a power of 4 (block-Hadamard rotated,
+  quant.py:103-122, 189-260; experts.py:1382-1422);
 * bf16 dense tensors (the LingBot dense grouped experts).
 
 ``B200GroupedExperts`` is an ``nn.Module`` with the reference's construction
 and ingest API (``from_empty``, ``load_dense_weight``,
-``load_nf4_packed_weight``, ``load_quantized_weight``) and its direct-routed
-entry point ``run_direct_routed(tokens, top_scores, top_indices)``
-(experts.py:1749-1912), differentiable in ``tokens`` and ``top_scores``
-(the dX path through frozen experts; no dense weight is kept for backward,
-the invariant of linear.py:96-102).
+``load_nf4_packed_weight``, ``load_quantized_weight``, and the packed-state
+manifest entry of packed_state.py:441-449 through ``from_packed_state``) and
+its direct-routed entry point ``run_direct_routed(tokens, top_scores,
+top_indices)`` (experts.py:1749-1912), differentiable in ``tokens`` and
+``top_scores`` (the dX path through frozen experts; no dense weight is kept
+for backward, the invariant of linear.py:96-102).
+
+Ingest is described by one table, ``STORAGE``: for every format the buffers
+one weight key owns, their dtypes and their sizes as functions of the
+key's dense ``[E, out, in]`` shape.  Every loader (dense quantisation, NF4
+packed buffers, INT8 buffers, packed-state artifacts) checks its tensors
+against that table and reports every mismatch at once.
 """
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
-from typing import Any, Iterable
+from typing import Any, Callable, Iterable, Mapping
 
 import torch
 import torch.nn as nn
@@ -32,6 +42,7 @@ import torch.nn as nn
 from . import ops, tables
 
 KEYS = ("w1", "w3", "w2")  # gate, up, down (specs.py:129-230 canonical roles)
+DEFAULT_GROUP_SIZES = (256, 64, 16)  # quant.py:22
 
 
 @dataclass
@@ -44,22 +55,108 @@ class Nf4Meta:
     weight_dtype: torch.dtype = torch.bfloat16
 
 
-class GroupedExpertWeights:
-    """The three weight keys of one layer as kernel descriptors."""
+def best_group_size(in_features: int, group_sizes: Iterable[int] = DEFAULT_GROUP_SIZES) -> int:
+    """Largest configured rotation group dividing ``in_features``, else 0 (quant.py:87-91)."""
+    fits = [int(g) for g in group_sizes if int(g) > 0 and int(in_features) % int(g) == 0]
+    return max(fits) if fits else 0
 
-    def __init__(self, fmt: str, w1, w3, w2, num_experts: int, hidden: int, inter: int):
+
+def _is_power_of_four(g: int) -> bool:
+    return g >= 4 and (g & (g - 1)) == 0 and (g.bit_length() - 1) % 2 == 0
+
+
+# ----------------------------------------------------------------------------- storage table
+
+@dataclass(frozen=True)
+class BufferSlot:
+    """One buffer a weight key owns: ``{key}_{suffix}``.
+
+    ``per_expert(out, in, meta)`` is its element count per expert (the tensor
+    is ``[E, ...]``); ``fixed`` is the element count of a shared table (no
+    expert axis).  Exactly one of the two is set."""
+
+    suffix: str
+    dtype: torch.dtype
+    per_expert: Callable[[int, int, Any], int] | None = None
+    fixed: int | None = None
+
+
+STORAGE: dict[str, tuple[BufferSlot, ...]] = {
+    "nf4": (
+        BufferSlot("nf4", torch.uint8, per_expert=lambda o, i, m: o * i // 2),
+        BufferSlot("nf4_absmax", torch.uint8, per_expert=lambda o, i, m: o * i // m.blocksize),
+        BufferSlot("nf4_nabsmax", torch.float32,
+                   per_expert=lambda o, i, m: -(-(o * i // m.blocksize) // m.nested_blocksize)),
+        BufferSlot("nf4_offset", torch.float32, per_expert=lambda o, i, m: 1),
+        BufferSlot("nf4_code", torch.float32, fixed=16),
+        BufferSlot("nf4_ncode", torch.float32, fixed=256),
+    ),
+    "int8": (
+        BufferSlot("int8", torch.int8, per_expert=lambda o, i, m: o * i),
+        BufferSlot("scale", torch.float32, per_expert=lambda o, i, m: o),
+    ),
+}
+
+
+def storage_problems(fmt: str, key: str, num_experts: int, dense_shape: tuple[int, ...], meta: Any,
+                     tensors: Mapping[str, torch.Tensor]) -> list[str]:
+    """Every way ``tensors`` (suffix -> tensor) fails the ``STORAGE[fmt]`` entry
+    for one key of dense shape ``[E, out, in]``; empty when they fit."""
+    problems = []
+    if len(dense_shape) != 3 or dense_shape[0] != num_experts:
+        return [f"{key}: dense shape {tuple(dense_shape)} is not [{num_experts}, out, in]"]
+    _, out_f, in_f = dense_shape
+    if fmt == "nf4" and (in_f * out_f) % meta.blocksize:
+        problems.append(f"{key}: {out_f}x{in_f} elements are not whole blocks of {meta.blocksize}")
+    for slot in STORAGE[fmt]:
+        name = f"{key}_{slot.suffix}"
+        t = tensors.get(slot.suffix)
+        if not isinstance(t, torch.Tensor):
+            problems.append(f"{name}: missing")
+            continue
+        if t.dtype != slot.dtype:
+            problems.append(f"{name}: dtype {t.dtype}, the layout stores {slot.dtype}")
+        if slot.fixed is not None:
+            if t.numel() != slot.fixed:
+                problems.append(f"{name}: {t.numel()} entries, the table has {slot.fixed}")
+            continue
+        want = slot.per_expert(out_f, in_f, meta)
+        if t.ndim == 0 or int(t.shape[0]) != num_experts:
+            problems.append(f"{name}: leading axis of {tuple(t.shape)} is not the {num_experts} experts")
+        elif t.numel() != num_experts * want:
+            problems.append(f"{name}: {t.numel() // max(num_experts, 1)} entries per expert, "
+                            f"{out_f}x{in_f} needs {want}")
+    return problems
+
+
+def _require(problems: list[str], what: str) -> None:
+    if problems:
+        raise ValueError(f"{what} rejected: " + "; ".join(problems))
+
+
+class GroupedExpertWeights:
+    """The three weight keys of one layer as kernel descriptors.
+
+    ``rot_in`` / ``rot_mid``: block-Hadamard group sizes of the rotated INT8
+    format along the hidden (w1/w3 input) and intermediate (w2 input)
+    dimensions, 0 when not rotated."""
+
+    def __init__(self, fmt: str, w1, w3, w2, num_experts: int, hidden: int, inter: int, *,
+                 rot_in: int = 0, rot_mid: int = 0):
         self.fmt = fmt
         self.w1, self.w3, self.w2 = w1, w3, w2
         self.num_experts, self.hidden, self.inter = int(num_experts), int(hidden), int(inter)
+        self.rot_in, self.rot_mid = int(rot_in), int(rot_mid)
 
     @classmethod
     def from_module(cls, module: Any) -> "GroupedExpertWeights":
         """Bind the buffers of a reference-compatible grouped-expert module.
 
         Accepts the reference's ``CompressedGroupedExperts`` (NF4, or INT8
-        with group size 0), this package's ``B200GroupedExperts`` and dense
-        modules exposing ``w1``/``w2``/``w3`` tensors.  The buffers are used
-        in place (no copy); they must live on a CUDA device.
+        plain or with its fixed block-Hadamard rotation), this package's
+        ``B200GroupedExperts`` and dense modules exposing ``w1``/``w2``/``w3``
+        tensors.  The buffers are used in place (no copy); they must live on a
+        CUDA device.
         """
         fmt = str(getattr(module, "_quant_format", "")).lower()
         E = int(getattr(module, "num_experts"))
@@ -68,25 +165,37 @@ class GroupedExpertWeights:
             meta = getattr(module, "_nf4_meta")
             ws = {}
             for key in KEYS:
-                ws[key] = ops.NF4Tensor(
-                    getattr(module, f"{key}_nf4"), getattr(module, f"{key}_nf4_absmax"),
-                    getattr(module, f"{key}_nf4_nabsmax"), getattr(module, f"{key}_nf4_offset"),
-                    getattr(module, f"{key}_nf4_code"), getattr(module, f"{key}_nf4_ncode"),
-                    shapes[key], int(meta.blocksize), int(meta.nested_blocksize))
+                buf = {s.suffix: getattr(module, f"{key}_{s.suffix}", None) for s in STORAGE["nf4"]}
+                buf["nf4_offset"] = None if buf["nf4_offset"] is None else buf["nf4_offset"].reshape(E, 1)
+                problems = storage_problems("nf4", key, E, tuple(shapes.get(key, ())), meta, buf)
+                if problems:
+                    raise ops._lib.MiraiError(2, "NF4 expert buffers do not fit the kernel layout: "
+                                              + "; ".join(problems))
+                ws[key] = ops.NF4Tensor(buf["nf4"], buf["nf4_absmax"], buf["nf4_nabsmax"], buf["nf4_offset"],
+                                        buf["nf4_code"], buf["nf4_ncode"], shapes[key], int(meta.blocksize),
+                                        int(meta.nested_blocksize))
             _, inter, hidden = shapes["w1"]
             return cls("nf4", ws["w1"], ws["w3"], ws["w2"], E, hidden, inter)
         if fmt == "int8" and hasattr(module, "w1_int8"):
-            ws = {}
+            groups = {}
+            learned = getattr(module, "expert_rotation", None)
             for key in KEYS:
                 g = int(getattr(module, f"{key}_group_size", 0))
-                rot = getattr(module, "expert_rotation", None)
-                if g != 0 or (callable(rot) and rot(key) is not None):
-                    raise ops._lib.MiraiError(
-                        2, f"INT8 expert tensor {key} uses block rotation (group size {g}); the fused kernel "
-                           "reads plain per-output-channel INT8 (group_size=0)")
-                ws[key] = ops.Int8Tensor(getattr(module, f"{key}_int8"), getattr(module, f"{key}_scale"))
+                if callable(learned) and learned(key) is not None:
+                    raise ops._lib.MiraiError(2, f"INT8 expert tensor {key} carries a learned rotation matrix; "
+                                                 "the fused path applies the fixed block-Hadamard rotation only")
+                if g and not _is_power_of_four(g):
+                    raise ops._lib.MiraiError(2, f"INT8 expert tensor {key}: rotation group {g} is not a power "
+                                                 "of 4")
+                groups[key] = g
+            if groups["w1"] != groups["w3"]:
+                raise ops._lib.MiraiError(2, f"INT8 gate/up rotation groups differ ({groups['w1']} vs "
+                                             f"{groups['w3']}): one activation rotation feeds both")
+            ws = {key: ops.Int8Tensor(getattr(module, f"{key}_int8"), getattr(module, f"{key}_scale"),
+                                      group_size=groups[key]) for key in KEYS}
             _, inter, hidden = ws["w1"].shape
-            return cls("int8", ws["w1"], ws["w3"], ws["w2"], E, hidden, inter)
+            return cls("int8", ws["w1"], ws["w3"], ws["w2"], E, hidden, inter,
+                       rot_in=groups["w1"], rot_mid=groups["w2"])
         w1, w2, w3 = (getattr(module, k, None) for k in ("w1", "w2", "w3"))
         if all(isinstance(w, torch.Tensor) for w in (w1, w2, w3)):
             bf = [w.detach().to(torch.bfloat16).contiguous() for w in (w1, w3, w2)]
@@ -120,11 +229,9 @@ class _RoutedExpertsFunction(torch.autograd.Function):
             ctx.score_dtype = top_scores.dtype
             ctx.factor_dtypes = (None if lora_a is None else lora_a.dtype, None if lora_b is None else lora_b.dtype)
         else:
-            plan = ops.dispatch_plan(top_indices.contiguous(), weights.num_experts)
-            xs = ops.permute_rows(x, plan.sorted_token_indices)
-            h = ops.gateup_swiglu(xs, plan.offsets, weights.w1, weights.w3, inter=weights.inter)
-            y = ops.down(h, plan.offsets, weights.w2, hidden=weights.hidden, lora=lora)
-            out = ops.combine(y, plan.inverse_order, w, out_dtype=out_dtype)
+            out = ops.moe_forward(x, top_indices.contiguous(), w, weights.w1, weights.w3, weights.w2,
+                                  num_experts=weights.num_experts, inter=weights.inter, lora=lora,
+                                  out_dtype=out_dtype)
         return out
 
     @staticmethod
@@ -149,10 +256,11 @@ def run_routed(weights: GroupedExpertWeights, tokens: torch.Tensor, top_scores: 
     ``lora`` = (lora_a [E, r, I], lora_b [E, H, r], scale) adds a LoRA adapter
     on the down projection (active_expert_lora.py:434-478); gradients flow to
     both factors."""
-    if top_scores.shape != top_indices.shape or top_indices.ndim != 2:
-        raise ValueError("Direct routed execution requires matching [tokens, top_k] score and index tensors.")
-    if int(top_indices.shape[0]) != int(tokens.shape[0]):
-        raise ValueError("Direct routed expert indices do not match token count.")
+    if top_indices.ndim != 2 or tuple(top_scores.shape) != tuple(top_indices.shape):
+        raise ValueError(f"routed execution takes [tokens, top_k] scores and indices of one shape, got "
+                         f"{tuple(top_scores.shape)} and {tuple(top_indices.shape)}")
+    if tokens.ndim != 2 or tokens.shape[0] != top_indices.shape[0]:
+        raise ValueError(f"{tuple(tokens.shape)} tokens against routing for {int(top_indices.shape[0])} tokens")
     if not tokens.is_cuda:
         raise ValueError("the B200 expert path runs on CUDA tensors only (no CPU fallback)")
     la, lb, sc = lora if lora is not None else (None, None, 1.0)
@@ -200,6 +308,19 @@ def down_lora_of(experts: Any) -> tuple | None:
     return ad.lora_a, ad.lora_b, scale
 
 
+def _meta_from_spec(raw: Any) -> Nf4Meta:
+    """``nf4_meta`` of a packed-state manifest entry (packed_contract.py:58-78)."""
+    if not isinstance(raw, Mapping):
+        raise ValueError("packed NF4 expert entry carries no nf4_meta mapping")
+
+    def dtype(name, default):
+        value = getattr(torch, str(name or "").replace("torch.", ""), None)
+        return value if isinstance(value, torch.dtype) else default
+
+    return Nf4Meta(int(raw.get("blocksize", 64)), int(raw.get("nested_blocksize", 256)),
+                   dtype(raw.get("nested_dtype"), torch.float32), dtype(raw.get("weight_dtype"), torch.bfloat16))
+
+
 class B200GroupedExperts(nn.Module):
     """Frozen grouped experts with the reference's ingest API, run on sm_100a."""
 
@@ -208,7 +329,7 @@ class B200GroupedExperts(nn.Module):
                  expert_dequant_chunk_size: int = 0, group_sizes=None, execution_spec=None):
         super().__init__()
         self._init_empty(int(getattr(base, "num_experts", 0)) if base is not None else 0, quant_format,
-                         nf4_blocksize, expert_weight_access, expert_dequant_chunk_size)
+                         nf4_blocksize, expert_weight_access, expert_dequant_chunk_size, group_sizes)
         if base is not None:
             for key in ("w1", "w2", "w3"):
                 self.load_dense_weight(key, getattr(base, key))
@@ -219,18 +340,63 @@ class B200GroupedExperts(nn.Module):
                    group_sizes=None, execution_spec=None) -> "B200GroupedExperts":
         m = cls.__new__(cls)
         nn.Module.__init__(m)
-        m._init_empty(num_experts, quant_format, nf4_blocksize, expert_weight_access, expert_dequant_chunk_size)
+        m._init_empty(num_experts, quant_format, nf4_blocksize, expert_weight_access, expert_dequant_chunk_size,
+                      group_sizes)
         return m
 
-    def _init_empty(self, num_experts, quant_format, nf4_blocksize, access, chunk):
+    @classmethod
+    def from_packed_state(cls, spec: Mapping[str, Any], tensors: Mapping[str, torch.Tensor]) -> "B200GroupedExperts":
+        """Experts restored from one ``grouped_experts`` entry of a packed-state
+        manifest (packed_state.py:331-341, 441-449) and its tensor mapping
+        (safetensors names -> tensors, e.g. ``layers.3.ffn.experts.w1_nf4``).
+
+        NF4 and INT8 entries are read; ``spec["tensors"]`` maps each local
+        buffer name (``w1_nf4``, ``w1_nf4_absmax``, ... or ``w1_int8``,
+        ``w1_scale``) to its tensor key, ``spec["shapes"]`` gives each key's
+        dense shape, ``spec["group_sizes"]`` the INT8 rotation groups and
+        ``spec["nf4_meta"]`` the NF4 block sizes.  The tensors must already be
+        on the CUDA device that will run the layer (they are used in place)."""
+        if str(spec.get("kind")) != "grouped_experts":
+            raise ValueError(f"packed entry of kind {spec.get('kind')!r} is not grouped_experts")
+        fmt = str(spec.get("quant_format", "")).lower()
+        if fmt not in STORAGE:
+            raise ValueError(f"packed grouped experts in format {fmt!r}: the fused path reads nf4 and int8")
+        if spec.get("rotations"):
+            raise ValueError("packed grouped experts with learned rotations: the fused path applies the fixed "
+                             "block-Hadamard rotation only")
+        names = spec.get("tensors")
+        shapes = spec.get("shapes")
+        if not isinstance(names, Mapping) or not isinstance(shapes, Mapping):
+            raise ValueError("packed grouped-experts entry needs 'tensors' and 'shapes' mappings")
+        m = cls.from_empty(num_experts=int(spec["num_experts"]), quant_format=fmt)
+        meta = _meta_from_spec(spec.get("nf4_meta")) if fmt == "nf4" else None
+        groups = spec.get("group_sizes") or {}
+        missing = [f"{key}_{s.suffix}" for key in ("w1", "w2", "w3") for s in STORAGE[fmt]
+                   if str(names.get(f"{key}_{s.suffix}", "")) not in tensors]
+        if missing:
+            raise KeyError(f"packed grouped experts: tensors missing from the mapping: {missing}")
+        for key in ("w1", "w2", "w3"):
+            buf = {s.suffix: tensors[str(names[f"{key}_{s.suffix}"])] for s in STORAGE[fmt]}
+            shape = tuple(int(v) for v in shapes[key])
+            if fmt == "nf4":
+                m.load_nf4_packed_weight(key, packed=buf["nf4"], absmax=buf["nf4_absmax"],
+                                         nested_absmax=buf["nf4_nabsmax"], offset=buf["nf4_offset"],
+                                         code=buf["nf4_code"], nested_code=buf["nf4_ncode"], shape=shape, meta=meta)
+            else:
+                m.load_quantized_weight(key, weight_int8=buf["int8"], weight_scale=buf["scale"],
+                                        group_size=int(groups.get(key, 0)))
+        return m
+
+    def _init_empty(self, num_experts, quant_format, nf4_blocksize, access, chunk, group_sizes=None):
         fmt = str(quant_format or "nf4").lower()
         if fmt not in ("nf4", "int8", "bf16"):
-            raise ValueError("B200 grouped experts support quant_format 'nf4', 'int8' or 'bf16'.")
+            raise ValueError(f"quant_format {quant_format!r}: the B200 experts store nf4, int8 or bf16")
         self.num_experts = int(num_experts)
         self._quant_format = fmt
         self._nf4_blocksize = int(nf4_blocksize)
         self._nf4_meta: Nf4Meta | None = None
         self._nf4_shapes: dict[str, tuple[int, ...]] = {}
+        self._group_sizes = tuple(int(g) for g in (group_sizes or DEFAULT_GROUP_SIZES))
         self.expert_weight_access = access
         self.expert_dequant_chunk_size = int(chunk)
         self._loaded: set[str] = set()
@@ -238,85 +404,96 @@ class B200GroupedExperts(nn.Module):
         self.expert_lora = nn.ModuleDict()
 
     # ------------------------------------------------------------------ ingest
-    def _set_buffer(self, name: str, value: torch.Tensor) -> None:
-        if name in self._buffers:
-            self._buffers[name] = value
-        else:
-            self.register_buffer(name, value)
+    def _install(self, key: str, fmt: str, buffers: Mapping[str, torch.Tensor]) -> None:
+        """Register one key's buffers under the reference's names (``{key}_{suffix}``)."""
+        for suffix, value in buffers.items():
+            name = f"{key}_{suffix}" if suffix else key
+            if name in self._buffers:
+                self._buffers[name] = value
+            else:
+                self.register_buffer(name, value)
+        self._loaded.add(key)
         self._bound = None
 
-    def load_dense_weight(self, key: str, source: torch.Tensor, *, rotation=None) -> None:
-        """Quantise one [E, out, in] tensor on the GPU (experts.py:940-996)."""
+    def _check_key(self, key: str) -> None:
         if key not in ("w1", "w2", "w3"):
-            raise ValueError(f"Unknown grouped expert tensor '{key}'.")
+            raise ValueError(f"weight key {key!r}: grouped experts hold w1 (gate), w3 (up) and w2 (down)")
+
+    def load_dense_weight(self, key: str, source: torch.Tensor, *, rotation=None) -> None:
+        """Quantise one [E, out, in] tensor on the GPU (experts.py:940-996).
+
+        INT8 uses the rotation group ``best_group_size(in)`` of the module's
+        group sizes (quant.py:87-91, 189-235): rows are block-Hadamard rotated
+        in fp32 before the per-row amax/127 scale (0 = no rotation)."""
+        self._check_key(key)
         if source.ndim != 3 or int(source.shape[0]) != self.num_experts:
-            raise ValueError(f"grouped expert tensor {key} must be [E={self.num_experts}, out, in], "
-                             f"got {tuple(source.shape)}")
+            raise ValueError(f"dense {key} of shape {tuple(source.shape)}: expected [{self.num_experts}, out, in]")
         if rotation is not None:
-            raise ValueError("Learned expert rotations are not supported by the fused kernels.")
+            raise ValueError("learned rotation matrices are not applied by the fused kernels")
         src = source.detach()
         if not src.is_cuda:
-            raise ValueError("load_dense_weight needs the source on a CUDA device (quantisation runs on the GPU)")
+            raise ValueError("load_dense_weight quantises on the GPU: pass the source on a CUDA device")
         if self._quant_format == "nf4":
             dev = src.device
             t = ops.nf4_quantize(src, tables.nf4_code(dev), tables.dynamic_map(dev), blocksize=self._nf4_blocksize)
             self._nf4_meta = Nf4Meta(t.blocksize, t.nested_blocksize)
             self._nf4_shapes[key] = tuple(src.shape)
-            self._set_buffer(f"{key}_nf4", t.packed)
-            self._set_buffer(f"{key}_nf4_absmax", t.absmax)
-            self._set_buffer(f"{key}_nf4_nabsmax", t.nested_absmax)
-            self._set_buffer(f"{key}_nf4_offset", t.offset)
-            self._set_buffer(f"{key}_nf4_code", t.code)
-            self._set_buffer(f"{key}_nf4_ncode", t.nested_code)
+            self._install(key, "nf4", {"nf4": t.packed, "nf4_absmax": t.absmax, "nf4_nabsmax": t.nested_absmax,
+                                       "nf4_offset": t.offset, "nf4_code": t.code, "nf4_ncode": t.nested_code})
         elif self._quant_format == "int8":
-            t = ops.int8_quantize(src.float() if src.dtype not in (torch.float32, torch.bfloat16) else src)
-            self._set_buffer(f"{key}_int8", t.q)
-            self._set_buffer(f"{key}_scale", t.scale)
-            setattr(self, f"{key}_group_size", 0)
+            g = best_group_size(int(src.shape[-1]), self._group_sizes)
+            t = ops.int8_quantize(src.float() if src.dtype not in (torch.float32, torch.bfloat16) else src,
+                                  group_size=g)
+            self._install(key, "int8", {"int8": t.q, "scale": t.scale})
+            setattr(self, f"{key}_group_size", g)
         else:
-            self._set_buffer(key, src.to(torch.bfloat16).contiguous())
-        self._loaded.add(key)
+            self._install(key, "bf16", {"": src.to(torch.bfloat16).contiguous()})
 
     def load_nf4_packed_weight(self, key: str, *, packed, absmax, nested_absmax, offset, code, nested_code,
                                shape: Iterable[int], meta) -> None:
         """Restore one NF4 key from packed buffers (experts.py:1424-1470)."""
+        self._check_key(key)
         if self._quant_format != "nf4":
-            raise ValueError("NF4 packed state requires an NF4 grouped-expert wrapper.")
-        shape = tuple(int(d) for d in shape)
-        if len(shape) != 3 or shape[0] != self.num_experts:
-            raise ValueError(f"NF4 grouped expert tensor {key} has invalid dense shape {shape}.")
-        for name, t in {"packed": packed, "absmax": absmax, "nested_absmax": nested_absmax,
-                        "offset": offset}.items():
-            if t.ndim == 0 or int(t.shape[0]) != self.num_experts:
-                raise ValueError(f"NF4 grouped expert {key} {name} must have expert axis {self.num_experts}, "
-                                 f"got {tuple(t.shape)}.")
+            raise ValueError(f"NF4 buffers for {key} offered to {self._quant_format} experts")
         m = Nf4Meta(int(meta.blocksize), int(meta.nested_blocksize))
         if self._nf4_meta is not None and (self._nf4_meta.blocksize, self._nf4_meta.nested_blocksize) != (
                 m.blocksize, m.nested_blocksize):
-            raise ValueError("NF4 grouped expert tensors use inconsistent quantization metadata.")
+            raise ValueError(f"{key}: NF4 block sizes ({m.blocksize}, {m.nested_blocksize}) differ from the keys "
+                             f"already loaded ({self._nf4_meta.blocksize}, {self._nf4_meta.nested_blocksize})")
+        dense = tuple(int(d) for d in shape)
+        buf = {"nf4": packed, "nf4_absmax": absmax, "nf4_nabsmax": nested_absmax,
+               "nf4_offset": offset.reshape(offset.shape[0], -1) if offset.ndim else offset,
+               "nf4_code": code, "nf4_ncode": nested_code}
+        _require(storage_problems("nf4", key, self.num_experts, dense, m, buf), f"NF4 buffers for {key}")
         self._nf4_meta = m
-        self._nf4_shapes[key] = shape
-        self._set_buffer(f"{key}_nf4", packed.detach().contiguous())
-        self._set_buffer(f"{key}_nf4_absmax", absmax.detach().contiguous())
-        self._set_buffer(f"{key}_nf4_nabsmax", nested_absmax.detach().contiguous())
-        self._set_buffer(f"{key}_nf4_offset", offset.detach().contiguous())
-        self._set_buffer(f"{key}_nf4_code", code.detach().contiguous())
-        self._set_buffer(f"{key}_nf4_ncode", nested_code.detach().contiguous())
-        self._loaded.add(key)
+        self._nf4_shapes[key] = dense
+        self._install(key, "nf4", {"nf4": packed.detach().contiguous(), "nf4_absmax": absmax.detach().contiguous(),
+                                   "nf4_nabsmax": nested_absmax.detach().contiguous(),
+                                   "nf4_offset": offset.detach().reshape(-1).contiguous(),
+                                   "nf4_code": code.detach().contiguous(),
+                                   "nf4_ncode": nested_code.detach().contiguous()})
 
     def load_quantized_weight(self, key: str, *, weight_int8, weight_scale, group_size: int, rotation=None) -> None:
-        """Restore one INT8 key (experts.py:1382-1422); only group_size 0 is executable."""
-        if weight_int8.ndim != 3 or int(weight_int8.shape[0]) != self.num_experts:
-            raise ValueError(f"grouped expert tensor {key} must be 3D with {self.num_experts} experts.")
-        if tuple(weight_scale.shape) != (*tuple(weight_int8.shape[:-1]), 1):
-            raise ValueError(f"grouped expert scale {key} has shape {tuple(weight_scale.shape)}.")
-        if int(group_size) != 0 or rotation is not None:
-            raise ValueError("the fused INT8 kernels read per-output-channel INT8 (group_size=0, no rotation)")
+        """Restore one INT8 key (experts.py:1382-1422): group 0 is plain
+        per-output-channel INT8, a power of 4 the fixed block-Hadamard rotation."""
+        self._check_key(key)
+        g = int(group_size)
+        if rotation is not None:
+            raise ValueError(f"{key}: learned rotation matrices are not applied by the fused kernels")
+        if weight_int8.ndim != 3:
+            raise ValueError(f"INT8 {key} of shape {tuple(weight_int8.shape)}: expected [E, out, in]")
+        dense = tuple(int(d) for d in weight_int8.shape)
+        problems = storage_problems("int8", key, self.num_experts, dense, None,
+                                    {"int8": weight_int8.to(torch.int8), "scale": weight_scale.float()})
+        if tuple(weight_scale.shape) != (*dense[:-1], 1):
+            problems.append(f"{key}_scale: shape {tuple(weight_scale.shape)}, expected {(*dense[:-1], 1)}")
+        if g and (not _is_power_of_four(g) or dense[-1] % g):
+            problems.append(f"{key}: rotation group {g} is not a power of 4 dividing in_features {dense[-1]}")
+        _require(problems, f"INT8 buffers for {key}")
         self._quant_format = "int8"
-        self._set_buffer(f"{key}_int8", weight_int8.detach().to(torch.int8).contiguous())
-        self._set_buffer(f"{key}_scale", weight_scale.detach().float().contiguous())
-        setattr(self, f"{key}_group_size", 0)
-        self._loaded.add(key)
+        self._install(key, "int8", {"int8": weight_int8.detach().to(torch.int8).contiguous(),
+                                    "scale": weight_scale.detach().float().contiguous()})
+        setattr(self, f"{key}_group_size", g)
 
     def is_fully_loaded(self) -> bool:
         return self._loaded.issuperset({"w1", "w2", "w3"})
@@ -327,7 +504,7 @@ class B200GroupedExperts(nn.Module):
     # ------------------------------------------------------------------ execution
     def bound_weights(self) -> GroupedExpertWeights:
         if not self.is_fully_loaded():
-            raise RuntimeError("grouped experts are not fully loaded (need w1, w2, w3)")
+            raise RuntimeError(f"grouped experts are not fully loaded: have {sorted(self._loaded)}, need w1, w2, w3")
         if self._bound is None:
             self._bound = GroupedExpertWeights.from_module(self)
         return self._bound
@@ -376,7 +553,7 @@ class _DownAdapter(nn.Module):
         self.lora_b = nn.Parameter(torch.zeros(num_experts, out_features, self.rank))
         self.register_buffer("lora_alpha", torch.tensor(float(alpha)), persistent=True)
         for e in range(num_experts):
-            nn.init.kaiming_uniform_(self.lora_a.data[e], a=5 ** 0.5)
+            nn.init.kaiming_uniform_(self.lora_a.data[e], a=math.sqrt(5))
 
     def _alpha(self) -> float:
         return float(self.lora_alpha.item())

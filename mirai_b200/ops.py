@@ -154,13 +154,19 @@ class NF4Tensor:
 
 
 class Int8Tensor:
-    """Device buffers of one INT8 grouped-expert key (group_size 0): ``q`` int8
-    [E, out, in] and ``scale`` fp32 [E, out, 1] (experts.py:1382-1422)."""
+    """Device buffers of one INT8 grouped-expert key: ``q`` int8 [E, out, in]
+    and ``scale`` fp32 [E, out, 1] (experts.py:1382-1422).  ``group_size`` 0 is
+    plain per-output-channel INT8 (q * s = W); a power of 4 is the reference's
+    default block-Hadamard format (q * s = W H along groups of ``in``,
+    quant.py:189-235), run by rotating activations (``rotate_rows``)."""
 
-    def __init__(self, q, scale):
+    def __init__(self, q, scale, group_size: int = 0):
         self.q = _cuda(q, "int8 weight", torch.int8)
         self.scale = _cuda(scale, "int8 scale", torch.float32)
         self.shape = tuple(int(s) for s in self.q.shape)
+        self.group_size = int(group_size)
+        if self.group_size and self.shape[-1] % self.group_size:
+            raise ValueError(f"rotation group {self.group_size} does not divide in_features {self.shape[-1]}")
         self._struct = _lib.Int8Weight(self.q.data_ptr(), self.scale.data_ptr())
 
     def struct(self) -> _lib.Int8Weight:
@@ -188,18 +194,62 @@ def nf4_quantize(weight: torch.Tensor, code: torch.Tensor, nested_code: torch.Te
     return NF4Tensor(packed, absmax, nabs, offset, code, nested_code, (E, out_f, in_f), blocksize, nested_blocksize)
 
 
-def int8_quantize(weight: torch.Tensor) -> Int8Tensor:
-    """Per-output-channel symmetric INT8 of a [E, out, in] stack (quant.py:189-235, g = 0)."""
+def int8_quantize(weight: torch.Tensor, group_size: int = 0) -> Int8Tensor:
+    """Symmetric per-output-channel INT8 of a [E, out, in] stack (quant.py:189-235).
+
+    ``group_size`` > 0 first rotates each row's groups of that many input
+    features by the block-Hadamard matrix, in fp32 (the reference's default
+    format); codes can differ from the reference's by one step where the
+    rotated value lies on a rounding boundary (the rotation's fp32 sums are
+    ordered differently from a matrix product)."""
     w = _cuda(weight, "weight")
     if w.dtype not in (torch.float32, torch.bfloat16):
         w = w.float()
     *lead, in_f = w.shape
     rows = w.numel() // in_f
+    if group_size:
+        w = rotate_rows(w.float().reshape(rows, in_f), group_size, out_dtype=torch.float32).reshape(w.shape)
     q = torch.empty(w.shape, dtype=torch.int8, device=w.device)
     s = torch.empty((*lead, 1), dtype=torch.float32, device=w.device)
     _lib.call("mirai_int8_quantize_rows", _ptr(w), 1 if w.dtype == torch.float32 else 0, rows, in_f, _ptr(q),
               _ptr(s), _stream())
-    return Int8Tensor(q, s)
+    return Int8Tensor(q, s, group_size)
+
+
+_DTYPE_CODES = {torch.bfloat16: 0, torch.float32: 1}
+
+
+def rotate_rows(x: torch.Tensor, group: int, *, out: torch.Tensor | None = None,
+                out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """x H along every ``group``-wide block of the last dimension (H the
+    block-Hadamard matrix of quant.py:103-122; H = H^T = H^-1), computed in
+    fp32; bf16 or fp32 in and out.  ``out`` may be ``x`` itself."""
+    x = _cuda(x, "x")
+    if x.dtype not in _DTYPE_CODES:
+        raise TypeError(f"rotate_rows takes bf16 or fp32, got {x.dtype}")
+    cols = x.shape[-1]
+    rows = x.numel() // cols if cols else 0
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    _lib.call("mirai_rotate_rows", _ptr(x), _DTYPE_CODES[x.dtype], rows, cols, int(group), _ptr(out),
+              _DTYPE_CODES[out.dtype], _stream())
+    return out
+
+
+def swiglu_backward_rotated(dh_raw: torch.Tensor, gate_up: torch.Tensor, group: int) -> torch.Tensor:
+    """grad_gate_up [S, 2I] = SwiGLU backward of the saved (gate, up) given
+    dh = rotate(dh_raw): the down projection's input gradient in the rotated
+    INT8 format (dh_raw = grad_y (q s) from ``down_dh``)."""
+    dh_raw = _cuda(dh_raw, "dh", torch.bfloat16)
+    gate_up = _cuda(gate_up, "gate_up", torch.bfloat16)
+    S, I = dh_raw.shape
+    dgu = torch.empty((S, 2 * I), dtype=torch.bfloat16, device=dh_raw.device)
+    _lib.call("mirai_swiglu_backward_rotated", _ptr(dh_raw), _ptr(gate_up), S, I, int(group), _ptr(dgu), _stream())
+    return dgu
+
+
+def _group(w) -> int:
+    return int(getattr(w, "group_size", 0) or 0)
 
 
 def _as_weight(w):
@@ -291,7 +341,7 @@ class DownLoRA:
         self.rank = int(r)
         self.scale = float(scale)
         self._b_pad = None
-        self._a_pad = None
+        self._a_pad = {}  # rotation group -> padded (and, for a group, rotated) A
 
     def b_pad(self) -> torch.Tensor:
         """B zero-padded to [E*H, 64]: the K-major rank-block operand of the down GEMM."""
@@ -302,14 +352,21 @@ class DownLoRA:
             self._b_pad = pad.reshape(E * H, 64)
         return self._b_pad
 
-    def a_pad(self) -> torch.Tensor:
-        """A zero-padded to [E*64, I]: the MN-major rank-block operand of the down dX GEMM."""
-        if self._a_pad is None:
+    def a_pad(self, rotation: int = 0) -> torch.Tensor:
+        """A zero-padded to [E*64, I]: the MN-major rank-block operand of the
+        down dX GEMM; with ``rotation`` > 0 each row rotated by the
+        block-Hadamard matrix of that group size (A H), for the rotated INT8
+        format whose dh is rotated after the GEMM (H H = 1).  Built once per
+        adapter and group."""
+        if rotation not in self._a_pad:
             E, r, I = self.a.shape
             pad = torch.zeros((E, 64, I), dtype=torch.bfloat16, device=self.a.device)
             pad[:, :r, :] = self.a
-            self._a_pad = pad.reshape(E * 64, I)
-        return self._a_pad
+            pad = pad.reshape(E * 64, I)
+            if rotation:
+                pad = rotate_rows(pad, rotation)
+            self._a_pad[rotation] = pad
+        return self._a_pad[rotation]
 
 
 LORA_FACTOR_ROWS, LORA_FACTOR_COLS = 0, 1
@@ -404,6 +461,27 @@ def down_dx(grad_y: torch.Tensor, offsets: torch.Tensor, w2, gate_up: torch.Tens
     return dgu
 
 
+def down_dh(grad_y: torch.Tensor, offsets: torch.Tensor, w2: Int8Tensor, *, inter: int,
+            lora: DownLoRA | None = None, rank_a: torch.Tensor | None = None) -> torch.Tensor:
+    """dh_raw [S, I] = grad_y (q s) (+ the rank block with the LoRA A factor
+    rotated, so that rotating the sum gives the true dh): the INT8 down dX
+    without the SwiGLU backward, for the rotated format."""
+    if not isinstance(w2, Int8Tensor):
+        raise TypeError("down_dh reads INT8 experts")
+    gy = _cuda(grad_y, "grad_y", torch.bfloat16)
+    offsets = _cuda(offsets, "offsets", torch.int32)
+    S, H = gy.shape
+    dh = torch.empty((S, inter), dtype=torch.bfloat16, device=gy.device)
+    if lora is None:
+        _lib.call("mirai_moe_down_dh_int8", _ptr(gy), _ptr(offsets), offsets.numel(), S, H, inter, w2.struct(),
+                  _ptr(dh), _stream())
+        return dh
+    glow = rank_a if rank_a is not None else lora_project(gy, offsets, lora, forward=False)
+    _lib.call("mirai_moe_down_dh_lora_int8", _ptr(gy), _ptr(offsets), offsets.numel(), S, H, inter, w2.struct(),
+              _ptr(glow), _ptr(lora.a_pad(rotation=w2.group_size)), _ptr(dh), _stream())
+    return dh
+
+
 def lora_grad(x: torch.Tensor, g_rank: torch.Tensor, offsets: torch.Tensor, rank: int, out: torch.Tensor,
               strides) -> torch.Tensor:
     """out[e][j][k] = sum over segment e of g_rank[s, j] * x[s, k] (fp32, by strides)."""
@@ -432,14 +510,31 @@ def gateup_dx(grad_gate_up: torch.Tensor, offsets: torch.Tensor, w1, w3, *, hidd
 
 # ----------------------------------------------------------------------------- whole forward
 
+def _rotations(w1, w3, w2) -> tuple[int, int]:
+    """(input group, intermediate group) of a layer's weights: non-zero for the
+    rotated INT8 format (w1 and w3 share one activation rotation)."""
+    g1, g3 = _group(w1), _group(w3)
+    if g1 != g3:
+        raise ValueError(f"gate/up rotation groups differ ({g1} vs {g3})")
+    return g1, _group(w2)
+
+
 def moe_forward(tokens: torch.Tensor, top_indices: torch.Tensor, top_weights: torch.Tensor, w1, w3, w2, *,
-                num_experts: int, inter: int) -> torch.Tensor:
-    """Routed expert FFN forward: plan, permute, gate/up+SwiGLU, down, combine."""
+                num_experts: int, inter: int, lora: "DownLoRA | None" = None,
+                out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Routed expert FFN forward: plan, permute, gate/up+SwiGLU, down, combine.
+
+    Rotated INT8 weights: the tokens are rotated before the permute (T rows,
+    not S) and h before the down GEMM; the LoRA rank block is projected from
+    the unrotated h."""
+    g_in, g_mid = _rotations(w1, w3, w2)
     plan = dispatch_plan(top_indices, num_experts)
-    xs = permute_rows(tokens, plan.sorted_token_indices)
+    xs = permute_rows(rotate_rows(tokens, g_in) if g_in else tokens, plan.sorted_token_indices)
     h = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter)
-    y = down(h, plan.offsets, w2, hidden=tokens.shape[1])
-    return combine(y, plan.inverse_order, top_weights, out_dtype=tokens.dtype)
+    low = lora_project(h, plan.offsets, lora, forward=True) if lora is not None else None
+    y = down(rotate_rows(h, g_mid) if g_mid else h, plan.offsets, w2, hidden=tokens.shape[1], lora=lora,
+             rank_a=low)
+    return combine(y, plan.inverse_order, top_weights, out_dtype=out_dtype or tokens.dtype)
 
 
 @dataclass
@@ -457,13 +552,15 @@ class ForwardState:
 def moe_forward_train(tokens, top_indices, top_weights, w1, w3, w2, *, num_experts: int, inter: int,
                       out_dtype: torch.dtype | None = None, lora: DownLoRA | None = None):
     """Forward that also returns the state the dX pass consumes."""
+    g_in, g_mid = _rotations(w1, w3, w2)
     plan = dispatch_plan(top_indices, num_experts)
-    xs = permute_rows(tokens, plan.sorted_token_indices)
+    xs = permute_rows(rotate_rows(tokens, g_in) if g_in else tokens, plan.sorted_token_indices)
     h, gu = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter, save_gate_up=True)
     low = None
     if lora is not None:
         low = lora_project(h, plan.offsets, lora, forward=True)
-    y = down(h, plan.offsets, w2, hidden=tokens.shape[1], lora=lora, rank_a=low)
+    y = down(rotate_rows(h, g_mid) if g_mid else h, plan.offsets, w2, hidden=tokens.shape[1], lora=lora,
+             rank_a=low)
     out = combine(y, plan.inverse_order, top_weights, out_dtype=out_dtype or tokens.dtype)
     keep = lora is not None and lora.compute_grads
     return out, ForwardState(plan, y, gu, top_weights.float(), h if keep else None, low if keep else None)
@@ -489,7 +586,15 @@ def moe_backward_dx(grad_out: torch.Tensor, state: ForwardState, w1, w3, w2, *, 
                                     torch.empty((E, r, Ia), dtype=torch.float32, device=gy.device), (r * Ia, Ia, 1))
             lora.grad_b = lora_grad(gy, state.rank_a, plan.offsets, r,
                                     torch.empty((E, Hb, r), dtype=torch.float32, device=gy.device), (Hb * r, 1, r))
-    dgu = down_dx(gy, plan.offsets, w2, state.gate_up, inter=inter, lora=lora, rank_a=glow)
+    g_in, g_mid = _rotations(w1, w3, w2)
+    if g_mid:  # rotated INT8: dh = rotate(grad_y (q s)), then the SwiGLU backward
+        dh = down_dh(gy, plan.offsets, w2, inter=inter, lora=lora, rank_a=glow)
+        dgu = swiglu_backward_rotated(dh, state.gate_up, g_mid)
+    else:
+        dgu = down_dx(gy, plan.offsets, w2, state.gate_up, inter=inter, lora=lora, rank_a=glow)
     dxs = gateup_dx(dgu, plan.offsets, w1, w3, hidden=H)
+    if g_in:  # sum the routes in fp32, then rotate the token rows (T, not S)
+        dx32 = combine(dxs, plan.inverse_order, None, out_dtype=torch.float32, top_k=plan.top_k)
+        return rotate_rows(dx32, g_in, out_dtype=out_dtype), gw
     dx = combine(dxs, plan.inverse_order, None, out_dtype=out_dtype, top_k=plan.top_k)
     return dx, gw

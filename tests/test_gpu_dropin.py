@@ -124,3 +124,36 @@ def test_module_with_lora_trains_adapter():
     assert ad.lora_a.grad is not None and ad.lora_b.grad is not None
     assert float(ad.lora_a.grad.norm()) > 0 and float(ad.lora_b.grad.norm()) > 0
     assert float(x.grad.norm()) > 0
+
+
+@pytest.mark.parametrize("name", ["routed_int8_bf16", "routed_int8_fp32", "routed_int8_g16_fp32"])
+def test_module_int8_against_reference_goldens(golden, name):
+    """The reference's own INT8 routed execution (run_direct_routed under
+    chunked_dequant, forward and autograd; fixtures recorded from the
+    reference) against this module loaded from the same INT8 buffers: plain
+    per-channel INT8 with bf16 and fp32 tokens, and the block-Hadamard g=16
+    format.  The fp32 references are held to the bf16 tolerance (the kernels
+    compute in bf16 with fp32 accumulation)."""
+    dev = _dev()
+    from mirai_b200.experts import B200GroupedExperts
+    g = golden(name)
+
+    def act(key):
+        v = g[key]
+        return torch.from_numpy(oq.bf16_bits_to_f32(v) if v.dtype == np.uint16 else v.astype(np.float32))
+
+    tdtype = torch.bfloat16 if bool(g["bf16"]) else torch.float32
+    E = g["w1_int8"].shape[0]
+    m = B200GroupedExperts.from_empty(num_experts=E, quant_format="int8")
+    for key in ("w1", "w2", "w3"):
+        m.load_quantized_weight(key, weight_int8=torch.from_numpy(g[f"{key}_int8"]).to(dev),
+                                weight_scale=torch.from_numpy(g[f"{key}_scale"]).to(dev),
+                                group_size=int(g["group_size"]))
+    x = act("tokens").to(tdtype).to(dev).requires_grad_(True)
+    sc = act("top_scores").to(tdtype).to(dev).requires_grad_(True)
+    out = m.run_direct_routed(x, sc, torch.from_numpy(g["top_indices"]).to(dev))
+    out.backward(act("grad").to(tdtype).to(dev))
+    assert out.dtype == tdtype
+    assert om.rel_max_err(_np(out), act("out").numpy()) < TOL
+    assert om.rel_max_err(_np(x.grad), act("grad_tokens").numpy()) < 3e-2
+    assert om.rel_max_err(_np(sc.grad), act("grad_scores").numpy().reshape(sc.shape)) < 3e-2

@@ -43,7 +43,7 @@ def _rank_main(rank, world, port, cfg, results):
     try:
         from mirai_b200 import ops
         from mirai_b200.expert_parallel import ExpertShard, ep_moe_forward, shard_tokens
-        T, H, E, k, I, fmt, chunks, transport, copy_streams, regroup = cfg
+        T, H, E, k, I, fmt, chunks, transport, copy_streams, regroup, layout = cfg
         g = torch.Generator(device=dev).manual_seed(11)
         x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
         logits = torch.randn(T, E, generator=g, device=dev) * 1.5
@@ -56,8 +56,14 @@ def _rank_main(rank, world, port, cfg, results):
         if transport == "ipc":
             from mirai_b200.expert_parallel import ExpertParallelMoE
             layer = ExpertParallelMoE(shard, top_k=k, inter=I, chunks=chunks, copy_streams=copy_streams,
-                                      regroup=regroup)
+                                      regroup=regroup, layout=layout)
+            # a quarter of the tokens first: the second call needs larger exchange buffers, so every
+            # rank releases, re-exports and re-imports them (flags zeroed, the epoch still counting)
+            q = max(1, (e - b) // 4)
+            small = layer.forward(xr[:q].contiguous(), lr[:q].contiguous(), local)
+            grown_from = layer.buffers.local.numel()
             out = layer.forward(xr, lr, local)
+            grew = layer.buffers.local.numel() > grown_from
             out2 = layer.forward(xr, lr, local)  # buffers reused
             assert torch.equal(out, out2)
             layer.close()
@@ -71,7 +77,13 @@ def _rank_main(rank, world, port, cfg, results):
         full = tuple(_quant(fmt, w, dev) for w in raw)
         idx, tw = ops.route_topk(logits, k)
         ref = ops.moe_forward(x, idx, tw, *full, num_experts=E, inter=I)[b:e]
-        results[rank] = (code, bool(torch.equal(out, ref)), float((out.float() - ref.float()).abs().max()))
+        equal = bool(torch.equal(out, ref))
+        if transport == "ipc":
+            # the small call is the single-GPU layer on those tokens alone
+            ridx, rtw = ops.route_topk(lr[:q].contiguous(), k)
+            ours = ops.moe_forward(xr[:q].contiguous(), ridx, rtw, *full, num_experts=E, inter=I)
+            equal = equal and bool(torch.equal(small, ours)) and grew
+        results[rank] = (code, equal, float((out.float() - ref.float()).abs().max()))
     finally:
         dist.destroy_process_group()
 
@@ -82,24 +94,28 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("fmt,chunks,transport,copy_streams,world,regroup", [
-    ("nf4", 1, "nccl", 1, 2, "never"), ("bf16", 1, "nccl", 1, 2, "never"), ("int8", 1, "nccl", 1, 2, "never"),
-    ("nf4", 3, "nccl", 1, 2, "never"),
-    ("nf4", 1, "ipc", 1, 2, "never"), ("nf4", 3, "ipc", 1, 2, "always"), ("int8", 2, "ipc", 1, 2, "always"),
-    ("bf16", 2, "ipc", 3, 2, "auto"),
-    ("nf4", 2, "ipc", 2, 4, "always"), ("nf4", 2, "nccl", 1, 4, "never"),
+@pytest.mark.parametrize("fmt,chunks,transport,copy_streams,world,regroup,layout", [
+    ("nf4", 1, "nccl", 1, 2, "never", "source"), ("bf16", 1, "nccl", 1, 2, "never", "source"),
+    ("int8", 1, "nccl", 1, 2, "never", "source"), ("nf4", 3, "nccl", 1, 2, "never", "source"),
+    ("nf4", 1, "ipc", 1, 2, "never", "source"), ("nf4", 3, "ipc", 1, 2, "always", "source"),
+    ("int8", 2, "ipc", 1, 2, "always", "source"), ("bf16", 2, "ipc", 3, 2, "auto", "source"),
+    ("nf4", 2, "ipc", 1, 2, "never", "expert"), ("int8", 1, "ipc", 2, 2, "never", "expert"),
+    ("nf4", 2, "ipc", 2, 4, "always", "source"), ("nf4", 2, "ipc", 1, 4, "never", "expert"),
+    ("nf4", 2, "nccl", 1, 4, "never", "source"),
 ])
-def test_expert_parallel_equals_single_gpu_layer(fmt, chunks, transport, copy_streams, world, regroup):
+def test_expert_parallel_equals_single_gpu_layer(fmt, chunks, transport, copy_streams, world, regroup, layout):
     """nccl, chunks > 1: the pipelined all-to-all path (exchanges on a second
     stream, GEMMs capped below the SM count); ipc: copy-engine transfers into
-    source-major peer-mapped buffers, on one stream or spread over side
-    streams, with the owner regrouping received rows expert-major ("always")
-    or not ("never")."""
+    source-major peer-mapped buffers (owners regrouping received rows
+    expert-major "always" or not "never") or into expert-major buffers (one
+    copy per (peer, expert) block), on one stream or spread over side
+    streams.  The ipc layer is first called on a quarter of the tokens, so its
+    second call grows and re-shares the exchange buffers."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     from mirai_b200.build import build
     build()
-    cfg = (3000, 256, 8, 2, 384, fmt, chunks, transport, copy_streams, regroup)
+    cfg = (3000, 256, 8, 2, 384, fmt, chunks, transport, copy_streams, regroup, layout)
     with mp.Manager() as mgr:
         results = mgr.dict()
         mp.start_processes(_rank_main, args=(world, _free_port(), cfg, results), nprocs=world, start_method="spawn")

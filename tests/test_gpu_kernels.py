@@ -644,3 +644,104 @@ def test_exchange_wait_gives_up_and_reports_a_timeout():
     t0 = time.monotonic()
     _lib.call("mirai_ep_wait", _lib.c_vp(flags.data_ptr()), 2, 0, 2, stream)
     assert ops.device_status() == (0, 0) and time.monotonic() - t0 < 1.0
+
+
+# ----------------------------------------------------------------------------- a5: rotated INT8
+
+@pytest.mark.parametrize("group", [4, 16, 64, 256, 1024, 4096])
+@pytest.mark.parametrize("dtypes", [("bf16", "bf16"), ("f32", "f32"), ("f32", "bf16")])
+def test_rotate_rows_matches_the_hadamard_product(group, dtypes):
+    """Block-Hadamard rotation of rows (quant.py:150-182 restated in
+    oracle.quant.rotate_last_dim) in fp32: within fp32 rounding of the product,
+    and exactly its own inverse up to rounding."""
+    dev = _dev()
+    from mirai_b200 import ops
+    rng = np.random.default_rng(group)
+    rows, cols = 37, max(group, 64) * 3
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    tin = {"bf16": torch.bfloat16, "f32": torch.float32}[dtypes[0]]
+    tout = {"bf16": torch.bfloat16, "f32": torch.float32}[dtypes[1]]
+    xt = torch.from_numpy(x).to(dev).to(tin)
+    got = ops.rotate_rows(xt, group, out_dtype=tout)
+    _check(ops)
+    ref = oq.rotate_last_dim(_f32(xt), group, inverse=False)
+    tol = 1e-5 if tout == torch.float32 else 8e-3
+    assert np.abs(_f32(got) - ref).max() <= tol * np.abs(ref).max()
+    back = ops.rotate_rows(got.float(), group, out_dtype=torch.float32)
+    assert np.abs(_f32(back) - _f32(xt)).max() <= tol * 4 * np.abs(x).max()
+
+
+def test_rotate_rows_in_place_and_rejects_bad_groups():
+    dev = _dev()
+    from mirai_b200 import ops
+    from mirai_b200._lib import MiraiError
+    x = torch.randn(64, 512, device=dev)
+    ref = ops.rotate_rows(x, 64)
+    ops.rotate_rows(x, 64, out=x)
+    assert torch.equal(x, ref)
+    for bad in (8, 32, 3, 0, 8192):
+        with pytest.raises(MiraiError):
+            ops.rotate_rows(x, bad)
+
+
+@pytest.mark.parametrize("group", [16, 64, 256])
+def test_gpu_rotated_int8_quantiser_matches_the_reference_rule(group):
+    """Rotate in fp32, per-row amax/127, round half to even (quant.py:189-235):
+    identical codes except, rarely, one step where the rotated value sits on a
+    rounding boundary (the fast transform orders its fp32 sums differently)."""
+    dev = _dev()
+    from mirai_b200 import ops
+    rng = np.random.default_rng(group + 1)
+    w = (rng.standard_normal((3, 96, 1024)) * 0.02).astype(np.float32)
+    t = ops.int8_quantize(torch.from_numpy(w).to(dev), group_size=group)
+    _check(ops)
+    q, s, g = oq.int8_quantize(w, group)
+    assert g == group and t.group_size == group
+    gq = t.q.cpu().numpy().astype(np.int32)
+    assert np.abs(gq - q).max() <= 1 and (gq != q).mean() < 1e-3
+    np.testing.assert_allclose(t.scale.cpu().numpy(), s, rtol=1e-6)
+
+
+def _rotated_int8_weights(rng, E, H, I, g_in, g_mid, dev):
+    from mirai_b200 import ops
+    raw = [(rng.standard_normal(s) * 0.02).astype(np.float32) for s in ((E, I, H), (E, I, H), (E, H, I))]
+    groups = (g_in, g_in, g_mid)
+    qs = [oq.int8_quantize(w, g) for w, g in zip(raw, groups)]
+    dense = [oq.bf16_round(oq.int8_dequantize(q, s, g)) for q, s, g in qs]
+    dw = [ops.Int8Tensor(torch.from_numpy(q).to(dev), torch.from_numpy(s).to(dev), group_size=g) for q, s, g in qs]
+    return dense, dw
+
+
+@pytest.mark.parametrize("T,H,E,k,I,lora_rank", [(600, 1024, 8, 2, 1024, 0), (333, 256, 6, 3, 384, 8),
+                                                 (512, 3072, 4, 2, 1024, 16)])
+def test_rotated_int8_layer_forward_and_dx_match_oracle(T, H, E, k, I, lora_rank):
+    """The reference's default INT8 format (g = best of 256/64/16 per input
+    dimension), run as rotated activations into the INT8 GEMMs, against the
+    oracle's dequantise-then-matmul (weights de-rotated on the host)."""
+    dev = _dev()
+    from mirai_b200 import ops
+    rng = np.random.default_rng(T + I)
+    g_in, g_mid = oq.best_group_size(H), oq.best_group_size(I)
+    assert g_in and g_mid
+    dense, dw = _rotated_int8_weights(rng, E, H, I, g_in, g_mid, dev)
+    x = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    logits = (rng.standard_normal((T, E)) * 1.5).astype(np.float32)
+    g = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    lora, ol = None, None
+    if lora_rank:
+        la = oq.bf16_round((rng.standard_normal((E, lora_rank, I)) * 0.05).astype(np.float32))
+        lb = oq.bf16_round((rng.standard_normal((E, H, lora_rank)) * 0.05).astype(np.float32))
+        lora = ops.DownLoRA(_bf16(la).to(dev), _bf16(lb).to(dev), 2.0, compute_grads=True)
+        ol = {"a": la, "b": lb, "scale": 2.0}
+    idx, w = ops.route_topk(torch.from_numpy(logits).to(dev), k)
+    out, st = ops.moe_forward_train(_bf16(x).to(dev), idx, w, *dw, num_experts=E, inter=I, lora=lora)
+    dx, dwts = ops.moe_backward_dx(_bf16(g).to(dev), st, *dw, inter=I, lora=lora)
+    fwd = ops.moe_forward(_bf16(x).to(dev), idx, w, *dw, num_experts=E, inter=I, lora=lora)
+    _check(ops)
+    assert torch.equal(fwd, out)
+    ridx, rw = om.route_topk(logits, k)
+    ref = om.moe_forward(x, ridx, rw, *dense, bf16=True, lora=ol)
+    rdx, rdw = om.moe_backward_dx(x, ridx, rw, *dense, g, bf16=True, lora=ol)
+    assert om.rel_max_err(_f32(out), ref) < TOL
+    assert om.rel_max_err(_f32(dx), rdx) < 3e-2
+    assert om.rel_max_err(_f32(dwts), rdw) < 3e-2

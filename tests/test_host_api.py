@@ -61,30 +61,54 @@ def test_registry_hook():
         bk.build_moe_kernel_backend("b200", direct_routed=False)
 
 
-def test_rotated_int8_is_rejected_with_a_clear_error():
+def test_rotated_int8_binding_rules():
+    """The fixed block-Hadamard format binds (on CUDA buffers); what the fused
+    path cannot run is refused with the reason: a learned rotation matrix,
+    a group that is not a power of 4, gate/up groups that differ."""
     from mirai_b200._lib import MiraiError
     m = _fake_reference_int8(group=16)
-    with pytest.raises(MiraiError, match="group_size=0"):
+    m.expert_rotation = lambda key: torch.eye(16)
+    with pytest.raises(MiraiError, match="learned rotation"):
         ex.GroupedExpertWeights.from_module(m)
+    m = _fake_reference_int8(group=32)
+    with pytest.raises(MiraiError, match="power of 4"):
+        ex.GroupedExpertWeights.from_module(m)
+    m = _fake_reference_int8(group=16)
+    m.w3_group_size = 64
+    with pytest.raises(MiraiError, match="gate/up rotation groups differ"):
+        ex.GroupedExpertWeights.from_module(m)
+    # plain and rotated layers both reach the descriptor step (which needs CUDA tensors)
+    with pytest.raises(ValueError, match="CUDA"):
+        ex.GroupedExpertWeights.from_module(_fake_reference_int8(group=16))
+
+
+def test_best_group_size_follows_the_reference_rule():
+    assert ex.best_group_size(3072) == 256 and ex.best_group_size(1408) == 64 and ex.best_group_size(48) == 16
+    assert ex.best_group_size(40) == 0 and ex.best_group_size(1024, (64, 16)) == 64
 
 
 def test_module_ingest_validation_on_cpu():
     m = ex.B200GroupedExperts.from_empty(num_experts=4, quant_format="nf4")
-    with pytest.raises(ValueError, match="Unknown"):
+    with pytest.raises(ValueError, match="weight key"):
         m.load_dense_weight("w9", torch.zeros(4, 8, 8))
-    with pytest.raises(ValueError, match="must be"):
+    with pytest.raises(ValueError, match="expected \\[4, out, in\\]"):
         m.load_dense_weight("w1", torch.zeros(3, 8, 8))
     with pytest.raises(ValueError, match="CUDA"):
         m.load_dense_weight("w1", torch.zeros(4, 128, 64))
-    with pytest.raises(ValueError, match="NF4 grouped expert tensor"):
+    with pytest.raises(ValueError, match="dense shape"):
         m.load_nf4_packed_weight("w1", packed=torch.zeros(4, 1), absmax=torch.zeros(4, 1),
                                  nested_absmax=torch.zeros(4, 1), offset=torch.zeros(4), code=torch.zeros(16),
                                  nested_code=torch.zeros(256), shape=(3, 8, 8), meta=ex.Nf4Meta())
     q = ex.B200GroupedExperts.from_empty(num_experts=2, quant_format="int8")
-    with pytest.raises(ValueError, match="group_size=0"):
+    with pytest.raises(ValueError, match="not a power of 4"):
         q.load_quantized_weight("w1", weight_int8=torch.zeros(2, 4, 8, dtype=torch.int8),
-                                weight_scale=torch.ones(2, 4, 1), group_size=16)
-    assert not q.is_fully_loaded()
+                                weight_scale=torch.ones(2, 4, 1), group_size=8)
+    with pytest.raises(ValueError, match="w1_scale"):
+        q.load_quantized_weight("w1", weight_int8=torch.zeros(2, 4, 8, dtype=torch.int8),
+                                weight_scale=torch.ones(2, 5, 1), group_size=0)
+    q.load_quantized_weight("w1", weight_int8=torch.zeros(2, 4, 16, dtype=torch.int8),
+                            weight_scale=torch.ones(2, 4, 1), group_size=16)
+    assert q.w1_group_size == 16 and not q.is_fully_loaded()
     with pytest.raises(RuntimeError, match="not fully loaded"):
         q.bound_weights()
 

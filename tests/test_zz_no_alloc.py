@@ -53,6 +53,41 @@ def test_static_plan_matches_workspace_plan_on_consecutive_calls():
         assert int(got[0].sum()) == T * k
 
 
+def test_static_plan_allocates_nothing():
+    """After a first call on the device (which may load the library's device
+    image), a static-plan call leaves the device's free memory and torch's
+    allocations exactly as they were."""
+    dev, _lib, ops = _setup()
+    T, k, E = 20000, 4, 128
+    idx = torch.randint(0, E, (T, k), generator=torch.Generator().manual_seed(3)).to(dev)
+    out = [torch.empty(E, dtype=torch.int64, device=dev), torch.empty(E, dtype=torch.int64, device=dev),
+           torch.empty(E, dtype=torch.int32, device=dev)] + [torch.empty(T * k, dtype=torch.int64, device=dev)
+                                                             for _ in range(3)]
+    args = [ops._ptr(idx), T, k, E, *[ops._ptr(t) for t in out], ops._stream()]
+    _lib.call("mirai_dispatch_plan_static", *args)  # warm-up: module and symbol address
+    torch.cuda.synchronize()
+    free0, alloc0 = torch.cuda.mem_get_info(dev)[0], torch.cuda.memory_allocated(dev)
+    for _ in range(3):
+        _lib.call("mirai_dispatch_plan_static", *args)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(dev)[0] == free0
+    assert torch.cuda.memory_allocated(dev) == alloc0
+    ops.check_device()
+
+
+def test_static_plan_checks_arguments_before_sizing():
+    """An unusable expert count or token count is an argument error, not a
+    scratch shortfall, and nothing is launched."""
+    dev, _lib, ops = _setup()
+    idx = torch.zeros((4, 2), dtype=torch.int64, device=dev)
+    bufs = [torch.empty(8, dtype=torch.int64, device=dev) for _ in range(6)]
+    for T, k, E in [(4, 2, 2000), (2 ** 40, 2, 8), (4, 0, 8), (-1, 2, 8)]:
+        with pytest.raises(_lib.MiraiError) as err:
+            _lib.call("mirai_dispatch_plan_static", ops._ptr(idx), T, k, E, *[ops._ptr(t) for t in bufs],
+                      ops._stream())
+        assert err.value.code == 1, str(err.value)
+
+
 def test_static_plan_rejects_oversized_plans():
     dev, _lib, ops = _setup()
     limit = int(_lib.load().mirai_dispatch_plan_static_scratch_bytes())
