@@ -338,7 +338,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   // weight row, gathered by the spare warp of warpgroup 0.
   constexpr bool PREFETCH = WF == W_NF4 && PAIR;
   constexpr int ABUF = 8192;  // bytes per prefetch buffer: B_ROWS x K/64 or K x B_ROWS/64, K <= 4096
-  static_assert(!PREFETCH || (C::WIDE && C::RAW_WARP == 2), "the MN gatherer is warp 3 of the wide layout");
+  static_assert(!PREFETCH || (C::WIDE && C::RAW_WARP == 2), "the absmax gatherer is warp 3 of the wide layout");
+  static_assert(!PREFETCH || MN || C::B_ROWS * (kMaxK / BK) <= ABUF, "a K-major tile's codes fit one buffer");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = base;
@@ -429,7 +430,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         mbar_init(&sm.raw_empty[s], C::GROUP_WARPS);
       }
       for (int a = 0; a < 2; ++a) {
-        mbar_init(&sm.absq_full[a], MN ? 32 : 1);  // MN: every lane of the gathering warp
+        mbar_init(&sm.absq_full[a], 32);  // every lane of the gathering warp
         mbar_init(&sm.absq_empty[a], C::DEQ_WARPS);
         mbar_init(&sm.tfull[a], 1);
         mbar_init(&sm.tempty[a], C::EPI_WARPS * pair_mult);
@@ -767,26 +768,9 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       int rstage = 0;
       uint32_t rphase = 0;
       constexpr int RB = C::ROW_BYTES;
-      int tl = 0;  // tiles of this CTA so far
-      for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++tl) {
+      for (int t = unit; t < total_tiles && !*abort_flag; t += num_units) {
         int j, e, m, n;
         decode_tile<WF, PAIR>(t, sm, units, p.n_tiles, j, e, m, n);
-        if (PREFETCH && !MN) {
-          const int buf = tl & 1;
-          if (tl >= 2 && !mbar_wait(&sm.absq_empty[buf], ((tl >> 1) - 1) & 1, 13)) {
-            *abort_flag = 1;
-            break;
-          }
-          const int first = kmajor_row<MODE, TN>(p, e, n, (int)rank) - e * p.out_rows;
-          const int rows = min(TN / 2, p.out_rows - first);  // a multiple of 64 (N % 64 == 0)
-          const uint32_t bytes = rows > 0 ? (uint32_t)(rows * num_kb) : 0u;
-          mbar_arrive_expect_tx(&sm.absq_full[buf], bytes);
-          if (bytes) {
-            const int key = MCfg<MODE>::TWO_KEYS ? (int)rank : 0;
-            bulk_load_1d(dq->absq + buf * ABUF, p.q[key].absmax + (size_t)kmajor_row<MODE, TN>(p, e, n, (int)rank) * num_kb,
-                         bytes, &sm.absq_full[buf]);
-          }
-        }
         for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&sm.raw_empty[rstage], rphase ^ 1, 11)) {
             *abort_flag = 1;
@@ -821,11 +805,15 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     }
   };
   auto role_absq = [&]() {
-    // ======================= absmax gatherer (NF4 pair, MN-major) =======================
-    // buffer[kk * NB + j] = absmax code of (k-row kk, this CTA's column block j),
-    // filled a tile ahead of the dequantisers (buffers are released by them).
+    // ======================= absmax gatherer (NF4 pairs) =======================
+    // Fills one of two buffers with a tile's absmax codes a tile ahead of the
+    // dequantisers (which release them), laid out so that the 32 lanes of a
+    // dequantiser warp, reading the codes of 32 consecutive B rows for one
+    // k-block, read 32 consecutive bytes (one shared-memory wavefront):
+    //   K-major: buffer[kb * B_ROWS + r] = code of (this CTA's weight row r, k-block kb);
+    //   MN-major: buffer[kk * NB + j] = code of (k-row kk, this CTA's column block j).
     constexpr int NB = C::B_ROWS / 64;
-    const int nblk_row = p.N / 64;  // NF4 blocks per weight row
+    const int nblk_row = p.N / 64;  // NF4 blocks per weight row (MN-major)
     int tl = 0;
     for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++tl) {
       int j, e, m, n;
@@ -836,6 +824,29 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         break;
       }
       uint8_t* dst = dq->absq + buf * ABUF;
+      if (!MN) {
+        // this CTA's weight rows of the tile: `rows` x num_kb codes, contiguous in
+        // global memory (row-major, 16-byte aligned: rows is a multiple of 64)
+        const int first = kmajor_row<MODE, TN>(p, e, n, (int)rank) - e * p.out_rows;
+        const int rows = min(C::B_ROWS, p.out_rows - first);
+        const int key = MCfg<MODE>::TWO_KEYS ? (int)rank : 0;
+        const uint4* src = reinterpret_cast<const uint4*>(
+            p.q[key].absmax + (size_t)kmajor_row<MODE, TN>(p, e, n, (int)rank) * num_kb);
+        const int chunks = rows > 0 ? rows * num_kb / 16 : 0;
+#pragma unroll 1
+        for (int c = lane; c < chunks; c += 32) {
+          const uint4 v = __ldg(src + c);
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+          int r = (16 * c) / num_kb, kb = 16 * c - r * num_kb;
+#pragma unroll
+          for (int b = 0; b < 16; ++b) {
+            dst[kb * C::B_ROWS + r] = (uint8_t)(w[b >> 2] >> (8 * (b & 3)));
+            if (++kb == num_kb) kb = 0, ++r;
+          }
+        }
+        mbar_arrive(&sm.absq_full[buf]);  // release: this lane's stores are visible to the waiters
+        continue;
+      }
       const int nb0 = n * (TN / 64) + (int)rank * NB;  // first column block of this CTA (even)
       static_assert(!(PREFETCH && MN) || NB == 2, "one 16-bit load covers this CTA's two column blocks");
       if (NB == 2 && (nblk_row & 1) == 0 && nb0 + 1 < nblk_row) {
@@ -967,12 +978,13 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           const uint32_t row_addr = smem_u32(sB + st * B_BYTES) + (uint32_t)row * 128u;
           const int key = MN ? ((MCfg<MODE>::TWO_KEYS && kb >= p.kb_half) ? 1 : 0) : row_key;
           if (WF == W_NF4) {
-            uint32_t words[8];
-#pragma unroll
-            for (int v = 0; v < 2; ++v) {
-              const uint4 r4 = reinterpret_cast<const uint4*>(raw)[v];
-              words[4 * v] = r4.x, words[4 * v + 1] = r4.y, words[4 * v + 2] = r4.z, words[4 * v + 3] = r4.w;
-            }
+            // the row's 32 code bytes as two 16-byte loads; rows 4..7 of every 8 take the halves
+            // in the other order, so that each 8-lane phase of a load covers all 32 banks
+            const uint4* raw4 = reinterpret_cast<const uint4*>(raw);
+            const bool swap = (row & 4) != 0;
+            const uint4 ra = raw4[swap ? 1 : 0], rb = raw4[swap ? 0 : 1];
+            const uint4 r0 = swap ? rb : ra, r1 = swap ? ra : rb;
+            const uint32_t words[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
             if (key != cur_key) {
 #pragma unroll
               for (int j = 0; j < 16; ++j) code[j] = dq->code[key][j];
@@ -983,7 +995,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             bool live = row_live;
             if (!MN) {
               blk = (wrow_base + kr) * nkb + kb;
-              qcode = PREFETCH ? dq->absq[abuf * ABUF + kr * nkb + kb]
+              qcode = PREFETCH ? dq->absq[abuf * ABUF + kb * C::B_ROWS + kr]
                                : dq->absq[absq_row * (TN / 2) * nkb + kr * nkb + kb];
             } else {
               const int kk = kb * BK + kr;        // k-row across both keys
@@ -1042,7 +1054,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       if (warp == 0) role_producer();
       else if (warp == 1) role_mma();
       else if (warp == C::RAW_WARP) role_raw();
-      else if (PREFETCH && MN && warp == 3) role_absq();
+      else if (PREFETCH && warp == 3) role_absq();
     } else if (warp < 8) {
       setmaxnreg_inc<C::REG_EPI>();
       role_epilogue();

@@ -1,10 +1,9 @@
 """Generate the golden fixtures under tests/golden/ by running the reference.
 
 Run from the repository root in a container that has the seruva19/mirai
-reference checked out (default path: ``$MIRAI_REFERENCE`` or
-``/root/reference``):
+reference checked out, naming its root in ``MIRAI_REFERENCE``:
 
-    python tests/golden/make_golden.py
+    MIRAI_REFERENCE=<path to the mirai checkout> python tests/golden/make_golden.py
 
 It imports the reference's own code on the CPU and records inputs and
 outputs of:
@@ -33,7 +32,7 @@ from pathlib import Path
 
 import numpy as np
 
-REF = os.environ.get("MIRAI_REFERENCE", "/root/reference")
+REF = os.environ.get("MIRAI_REFERENCE", "")
 OUT = Path(__file__).resolve().parent
 
 
@@ -43,6 +42,8 @@ def _bf16_bits(t):
 
 
 def main() -> None:
+    if not REF or not os.path.isdir(os.path.join(REF, "mirai")):
+        raise SystemExit("set MIRAI_REFERENCE to the root of a seruva19/mirai checkout (the directory holding mirai/)")
     sys.path.insert(0, REF)
     import torch
     import torch.nn as nn

@@ -699,7 +699,7 @@ def test_gpu_rotated_int8_quantiser_matches_the_reference_rule(group):
     assert g == group and t.group_size == group
     gq = t.q.cpu().numpy().astype(np.int32)
     assert np.abs(gq - q).max() <= 1 and (gq != q).mean() < 1e-3
-    np.testing.assert_allclose(t.scale.cpu().numpy(), s, rtol=1e-6)
+    np.testing.assert_allclose(t.scale.cpu().numpy(), s, rtol=4e-6)  # a few fp32 ulps of the rotated amax
 
 
 def _rotated_int8_weights(rng, E, H, I, g_in, g_mid, dev):
