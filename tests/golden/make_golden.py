@@ -41,21 +41,81 @@ def _bf16_bits(t):
     return t.detach().to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
 
 
-def main() -> None:
+def lingbot_block() -> None:
+    """``LingBotVideoSparseMoeBlock`` (transformer_lingbot_video.py:1175-2377)
+    with a shared expert, sigmoid routing with a correction bias, top-k
+    renormalisation and route_scale 2.5, bf16 (router fp32), run by the
+    reference's built-in path: a training forward + backward, the same with a
+    48-token ``MoETokenChunkPolicy``, and an eval forward with a padding mask."""
+    import torch
+    from mirai.core.moe.runtime.token_chunking import MoETokenChunkPolicy
+    from mirai.vendors.lingbot_video.transformer_lingbot_video import LingBotVideoSparseMoeBlock
+
+    torch.manual_seed(21)
+    blk = LingBotVideoSparseMoeBlock(hidden_size=128, intermediate_size=256, num_experts=8, top_k=2,
+                                     moe_intermediate_size=128, score_func="sigmoid", norm_topk_prob=True,
+                                     n_group=None, topk_group=None, routed_scaling_factor=2.5, n_shared_experts=1)
+    with torch.no_grad():
+        for p in blk.parameters():
+            p.normal_(0.0, 0.05)
+        blk.router.e_score_correction_bias.normal_(0.0, 0.1)
+    blk = blk.to(torch.bfloat16)
+    blk.router.float()
+    B, S, H = 2, 64, 128
+    x = torch.randn(B, S, H).to(torch.bfloat16)
+    grad = torch.randn(B, S, H).to(torch.bfloat16)
+    res = {"x": _bf16_bits(x), "grad": _bf16_bits(grad), "top_k": np.int64(2), "route_scale": np.float32(2.5),
+           "router_weight": blk.router.weight.detach().float().numpy(),
+           "correction_bias": blk.router.e_score_correction_bias.detach().float().numpy()}
+    for key in ("w1", "w2", "w3"):
+        res[f"experts_{key}"] = _bf16_bits(getattr(blk.experts, key))
+    for name in ("gate_proj", "up_proj", "down_proj"):
+        res[f"shared_{name}"] = _bf16_bits(getattr(blk.shared_experts, name).weight)
+    with torch.no_grad():
+        idx, sc, *_ = blk.router(x.reshape(-1, H))
+    res["top_indices"], res["top_scores"] = idx.numpy().astype(np.int64), sc.float().numpy()
+    blk.train()
+    for tag, chunk in (("", 0), ("_chunked", 48)):
+        blk.set_token_chunk_policy(MoETokenChunkPolicy(token_chunk_size=chunk) if chunk else None)
+        xi = x.clone().requires_grad_(True)
+        out = blk(xi)
+        out.backward(grad)
+        res[f"out{tag}"], res[f"grad_x{tag}"] = _bf16_bits(out), _bf16_bits(xi.grad)
+    blk.set_token_chunk_policy(None)
+    blk.eval()
+    mask = torch.ones(B * S)
+    mask[S - 7:S] = 0  # the first sample's last 7 tokens are padding
+    with torch.no_grad():
+        res["padding_mask"] = mask.numpy()
+        res["out_masked"] = _bf16_bits(blk(x, padding_mask=mask))
+    np.savez_compressed(OUT / "lingbot_block.npz", **res)
+
+
+def main(only=None) -> None:
     if not REF or not os.path.isdir(os.path.join(REF, "mirai")):
         raise SystemExit("set MIRAI_REFERENCE to the root of a seruva19/mirai checkout (the directory holding mirai/)")
     sys.path.insert(0, REF)
     import torch
-    import torch.nn as nn
+
+    torch.set_num_threads(4)
+    only = set(only or {"basic", "routed", "lingbot_block"})
+    if "lingbot_block" in only:
+        lingbot_block()
+    if "basic" in only:
+        basic_fixtures()
+    if "routed" in only:
+        routed_fixtures()
+    print("golden fixtures written to", OUT)
+
+
+def basic_fixtures() -> None:
+    import torch
     from mirai.core.moe.routing.routers import TokenChoiceRouter
     from mirai.core.models.compressed_weights.execution.dispatch_preprocess import build_dispatch_plan
     from mirai.core.models.compressed_weights.execution.dispatch_ops import (
         combine_routed_tokens, permute_routed_tokens)
     from mirai.core.models.compressed_weights.quantization.quant import (
         _dequantize_weight, _quantize_weight)
-    from mirai.core.models.compressed_weights import CompressedGroupedExperts
-
-    torch.set_num_threads(4)
 
     # ------------------------------------------------------------------ router
     for name, (T, H, E, k, seed) in {
@@ -123,6 +183,14 @@ def main() -> None:
         res[f"deq_g{gsz}"] = deq.numpy()
         res[f"gres_g{gsz}"] = np.int64(gres)
     np.savez_compressed(OUT / "int8_quant.npz", **res)
+
+
+
+def routed_fixtures() -> None:
+    import torch
+    import torch.nn as nn
+    from mirai.core.models.compressed_weights.quantization.quant import _quantize_weight
+    from mirai.core.models.compressed_weights import CompressedGroupedExperts
 
     # ------------------------------------------------------------------ routed expert execution
     class _Base(nn.Module):
@@ -196,8 +264,9 @@ def main() -> None:
     routed_case("routed_dense_bf16", T=128, H=128, E=8, k=2, I=128, dtype=torch.bfloat16, fmt="dense", seed=4)
     routed_case("routed_dense_bf16_lora", T=96, H=64, E=4, k=2, I=128, dtype=torch.bfloat16, fmt="dense",
                 seed=5, lora_rank=4)
-    print("golden fixtures written to", OUT)
 
 
 if __name__ == "__main__":
-    main()
+    # no arguments: every fixture; otherwise any of "basic" (router, plan, permute/combine, INT8
+    # quantisation), "routed" (routed execution) and "lingbot_block"
+    main(set(sys.argv[1:]) or {"basic", "routed", "lingbot_block"})

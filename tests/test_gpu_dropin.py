@@ -1,6 +1,7 @@
 """The drop-in layer on the GPU: the reference-compatible module, the
 ``execute_direct`` backend and autograd, checked against the oracle."""
 
+import os
 import types
 
 import numpy as np
@@ -157,3 +158,102 @@ def test_module_int8_against_reference_goldens(golden, name):
     assert om.rel_max_err(_np(out), act("out").numpy()) < TOL
     assert om.rel_max_err(_np(x.grad), act("grad_tokens").numpy()) < 3e-2
     assert om.rel_max_err(_np(sc.grad), act("grad_scores").numpy().reshape(sc.shape)) < 3e-2
+
+
+def _block_from_golden(g, dev, chunk=0):
+    from mirai_b200.block import B200SparseMoeBlock, TokenChunkPolicy
+    bits = lambda key: torch.from_numpy(oq.bf16_bits_to_f32(g[key])).to(torch.bfloat16).to(dev)
+    state = {"router.weight": torch.from_numpy(g["router_weight"]).to(dev),
+             "router.e_score_correction_bias": torch.from_numpy(g["correction_bias"]).to(dev)}
+    for key in ("w1", "w2", "w3"):
+        state[f"experts.{key}"] = bits(f"experts_{key}")
+    for name in ("gate_proj", "up_proj", "down_proj"):
+        state[f"shared_experts.{name}.weight"] = bits(f"shared_{name}")
+    return B200SparseMoeBlock.from_state(state, top_k=int(g["top_k"]), score_func="sigmoid", norm_topk_prob=True,
+                                         route_scale=float(g["route_scale"]),
+                                         token_chunk_policy=TokenChunkPolicy(chunk) if chunk else None)
+
+
+@pytest.mark.parametrize("chunk", [0, 48])
+def test_lingbot_block_against_the_reference_block(golden, chunk):
+    """The reference's own LingBotVideoSparseMoeBlock (fixture recorded from it:
+    sigmoid router with correction bias, top-2 renormalised, route_scale 2.5,
+    8 bf16 experts, a shared expert; built-in routed path) against this block
+    on the same tensors: routed experts through B200MoEKernelBackend, shared
+    expert on the one-expert GEMMs, router selection in the router kernel.
+    Training forward + backward, without and with 48-token chunks
+    (MoETokenChunkPolicy, checkpointed), and an eval forward with a padding mask."""
+    dev = _dev()
+    from mirai_b200 import ops
+    from mirai_b200.block import route
+    g = golden("lingbot_block")
+    blk = _block_from_golden(g, dev, chunk)
+    x0 = torch.from_numpy(oq.bf16_bits_to_f32(g["x"])).to(torch.bfloat16).to(dev)
+    H = x0.shape[-1]
+    with torch.no_grad():
+        idx, sc = route(x0.reshape(-1, H), blk.router_weight, top_k=2, score_func="sigmoid",
+                        correction_bias=blk.e_score_correction_bias, route_scale=2.5)
+    ours_i, ours_w = om.canonical_slots(idx.cpu().numpy(), sc.float().cpu().numpy())
+    ref_i, ref_w = om.canonical_slots(g["top_indices"], g["top_scores"])
+    np.testing.assert_array_equal(ours_i, ref_i)
+    np.testing.assert_allclose(ours_w, ref_w, rtol=1e-2)  # bf16 route weights
+    blk.train()
+    x = x0.clone().requires_grad_(True)
+    out = blk(x)
+    out.backward(torch.from_numpy(oq.bf16_bits_to_f32(g["grad"])).to(torch.bfloat16).to(dev))
+    ops.check_device()
+    tag = "_chunked" if chunk else ""
+    assert om.rel_max_err(_np(out), oq.bf16_bits_to_f32(g[f"out{tag}"])) < TOL
+    assert om.rel_max_err(_np(x.grad), oq.bf16_bits_to_f32(g[f"grad_x{tag}"])) < 3e-2
+    assert blk.router_weight.grad is not None and torch.isfinite(blk.router_weight.grad).all()
+    blk.eval()
+    with torch.no_grad():
+        masked = blk(x0, padding_mask=torch.from_numpy(g["padding_mask"]).to(dev))
+    assert om.rel_max_err(_np(masked), oq.bf16_bits_to_f32(g["out_masked"])) < TOL
+
+
+def test_lingbot_block_chunks_change_nothing():
+    """Token chunks split the expert execution, not the routes: the chunked
+    block's output and input gradient equal the unchunked block's exactly."""
+    dev = _dev()
+    import numpy as _n
+    g = dict(_n.load(os.path.join(os.path.dirname(__file__), "golden", "lingbot_block.npz")))
+    x0 = torch.from_numpy(oq.bf16_bits_to_f32(g["x"])).to(torch.bfloat16).to(dev)
+    gr = torch.from_numpy(oq.bf16_bits_to_f32(g["grad"])).to(torch.bfloat16).to(dev)
+    res = []
+    for chunk in (0, 40):
+        blk = _block_from_golden(g, dev, chunk).train()
+        x = x0.clone().requires_grad_(True)
+        out = blk(x)
+        out.backward(gr)
+        res.append((out.detach(), x.grad))
+    assert torch.equal(res[0][0], res[1][0]) and torch.equal(res[0][1], res[1][1])
+
+
+def test_packed_state_nf4_experts_run_on_the_gpu():
+    """NF4 experts restored from a packed-state manifest entry (the reference's
+    names and layout) run through the fused kernels and match the oracle's
+    dequantise-then-matmul of the same buffers."""
+    dev = _dev()
+    from mirai_b200.experts import B200GroupedExperts
+    rng = np.random.default_rng(4)
+    T, H, E, k, I = 300, 256, 6, 2, 384
+    shapes = {"w1": (E, I, H), "w3": (E, I, H), "w2": (E, H, I)}
+    tensors, names, dense = {}, {}, {}
+    for key, shp in shapes.items():
+        g = oq.nf4_quantize_grouped((rng.standard_normal(shp) * 0.05).astype(np.float32))
+        dense[key] = oq.nf4_dequantize_grouped(g)
+        for suffix, arr in (("nf4", g["nf4"]), ("nf4_absmax", g["absmax"]), ("nf4_nabsmax", g["nabsmax"]),
+                            ("nf4_offset", g["offset"]), ("nf4_code", g["code"]), ("nf4_ncode", g["ncode"])):
+            names[f"{key}_{suffix}"] = f"layers.2.ffn.experts.{key}_{suffix}"
+            tensors[names[f"{key}_{suffix}"]] = torch.from_numpy(np.ascontiguousarray(arr)).to(dev)
+    spec = {"kind": "grouped_experts", "quant_format": "nf4", "num_experts": E, "shapes": shapes,
+            "group_sizes": {}, "tensors": names, "nf4_meta": {"blocksize": 64, "nested_blocksize": 256}}
+    m = B200GroupedExperts.from_packed_state(spec, tensors)
+    x = oq.bf16_round(rng.standard_normal((T, H)).astype(np.float32))
+    logits = (rng.standard_normal((T, E)) * 1.5).astype(np.float32)
+    ridx, rw = om.route_topk(logits, k)
+    out = m.run_direct_routed(torch.from_numpy(x).to(torch.bfloat16).to(dev), torch.from_numpy(rw).to(dev),
+                              torch.from_numpy(ridx).to(dev))
+    ref = om.moe_forward(x, ridx, rw, dense["w1"], dense["w3"], dense["w2"], bf16=True)
+    assert om.rel_max_err(_np(out), ref) < TOL

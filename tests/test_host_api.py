@@ -122,3 +122,103 @@ def test_tables_are_the_published_constructions():
     from oracle import quant as oq
     assert torch.equal(code, torch.from_numpy(oq.nf4_code_table()))
     assert torch.equal(dyn, torch.from_numpy(oq.dynamic_tree_map()))
+
+
+def test_token_chunk_policy_semantics():
+    """MoETokenChunkPolicy's rules (token_chunking.py:25-117): size 0 disables;
+    only training splits; chunks cover the tokens in order with their offsets;
+    checkpointed when gradients are enabled."""
+    from mirai_b200.block import TokenChunkPolicy
+    calls = []
+
+    def runner(t, s, i, off):
+        calls.append((off, t.shape[0]))
+        return t * 2
+
+    x = torch.arange(10.0).reshape(10, 1)
+    sc, idx = torch.ones(10, 2), torch.zeros(10, 2, dtype=torch.int64)
+    assert not TokenChunkPolicy(0).enabled and TokenChunkPolicy(0).chunk_count(10) == 1
+    assert TokenChunkPolicy(4).chunk_count(10) == 3
+    out = TokenChunkPolicy(4).execute(x, sc, idx, runner=runner, training=True)
+    assert calls == [(0, 4), (4, 4), (8, 2)] and torch.equal(out, x * 2)
+    calls.clear()
+    TokenChunkPolicy(4).execute(x, sc, idx, runner=runner, training=False)
+    assert calls == [(0, 10)]
+    calls.clear()
+    xg = x.clone().requires_grad_(True)
+    out = TokenChunkPolicy(3).execute(xg, sc, idx, runner=runner, training=True)
+    out.sum().backward()
+    assert torch.equal(xg.grad, torch.full_like(x, 2.0)) and len(calls) >= 4  # forward chunks (+ recompute)
+    with pytest.raises(ValueError):
+        TokenChunkPolicy(-1)
+    with pytest.raises(ValueError):
+        TokenChunkPolicy(4).execute(x, sc[:5], idx, runner=runner, training=True)
+
+
+def test_install_on_a_reference_like_block():
+    """install() puts the b200 backend on the block's kernel-backend seam and
+    moves the shared expert onto SharedExpertMLP with the same parameters."""
+    import torch.nn as nn
+    from mirai_b200.block import SharedExpertMLP, install
+
+    class _MLP(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.gate_proj = nn.Linear(8, 16, bias=False)
+            self.up_proj = nn.Linear(8, 16, bias=False)
+            self.down_proj = nn.Linear(16, 8, bias=False)
+
+    blk = types.SimpleNamespace(_mirai_moe_kernel_backend=None, shared_experts=_MLP())
+    ref = blk.shared_experts.state_dict()
+    install(blk)
+    assert isinstance(blk._mirai_moe_kernel_backend, bk.B200MoEKernelBackend)
+    assert blk._mirai_moe_kernel_backend.direct_only
+    assert isinstance(blk.shared_experts, SharedExpertMLP)
+    for k, v in blk.shared_experts.state_dict().items():
+        assert torch.equal(v, ref[k])
+
+
+def test_packed_state_entry_round_trip_on_cpu():
+    """A grouped-experts entry of the reference's packed-state manifest
+    (packed_state.py:331-341, 441-449): NF4 and INT8 buffers named as the
+    manifest names them load into B200GroupedExperts unchanged; a missing
+    tensor or a bad shape is refused with the reason."""
+    from oracle import quant as oq
+    E, I, H = 2, 128, 64
+    rng = __import__("numpy").random.default_rng(0)
+    tensors, names = {}, {}
+    shapes = {"w1": (E, I, H), "w3": (E, I, H), "w2": (E, H, I)}
+    for key, shp in shapes.items():
+        g = oq.nf4_quantize_grouped((rng.standard_normal(shp) * 0.05).astype("float32"))
+        for suffix, arr in (("nf4", g["nf4"]), ("nf4_absmax", g["absmax"]), ("nf4_nabsmax", g["nabsmax"]),
+                            ("nf4_offset", g["offset"]), ("nf4_code", g["code"]), ("nf4_ncode", g["ncode"])):
+            names[f"{key}_{suffix}"] = f"blocks.0.ffn.experts.{key}_{suffix}"
+            tensors[names[f"{key}_{suffix}"]] = torch.from_numpy(arr.copy())
+    spec = {"kind": "grouped_experts", "quant_format": "nf4", "num_experts": E, "shapes": shapes,
+            "group_sizes": {"w1": 0, "w2": 0, "w3": 0}, "tensors": names,
+            "nf4_meta": {"blocksize": 64, "nested_blocksize": 256, "nested_dtype": "float32",
+                         "weight_dtype": "bfloat16"}}
+    m = ex.B200GroupedExperts.from_packed_state(spec, tensors)
+    assert m.is_fully_loaded() and m._nf4_shapes["w2"] == (E, H, I)
+    for name, key in names.items():
+        assert torch.equal(getattr(m, name).reshape(-1), tensors[key].reshape(-1))
+    bad = dict(tensors)
+    del bad[names["w3_nf4_absmax"]]
+    with pytest.raises(KeyError, match="w3_nf4_absmax"):
+        ex.B200GroupedExperts.from_packed_state(spec, bad)
+    bad = dict(tensors)
+    bad[names["w1_nf4"]] = bad[names["w1_nf4"]][:, :-2]
+    with pytest.raises(ValueError, match="w1_nf4"):
+        ex.B200GroupedExperts.from_packed_state(spec, bad)
+    # INT8 (block-Hadamard g = 16)
+    names8, t8 = {}, {}
+    for key, shp in shapes.items():
+        q, s, gr = oq.int8_quantize((rng.standard_normal(shp) * 0.05).astype("float32"), 16)
+        names8[f"{key}_int8"], names8[f"{key}_scale"] = f"e.{key}_int8", f"e.{key}_scale"
+        t8[f"e.{key}_int8"], t8[f"e.{key}_scale"] = torch.from_numpy(q), torch.from_numpy(s)
+    spec8 = {"kind": "grouped_experts", "quant_format": "int8", "num_experts": E, "shapes": shapes,
+             "group_sizes": {"w1": 16, "w2": 16, "w3": 16}, "tensors": names8}
+    m8 = ex.B200GroupedExperts.from_packed_state(spec8, t8)
+    assert m8.w1_group_size == 16 and torch.equal(m8.w2_int8, t8["e.w2_int8"])
+    with pytest.raises(ValueError, match="learned rotations"):
+        ex.B200GroupedExperts.from_packed_state(dict(spec8, rotations={"w1": "r"}), t8)
