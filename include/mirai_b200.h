@@ -46,14 +46,30 @@ enum {
 /* Score function and renormalisation of mirai_route_topk. */
 enum { MIRAI_SCORE_SOFTMAX = 0, MIRAI_SCORE_SIGMOID = 1 };
 enum {
-  MIRAI_NORM_NONE = 0,  /* weights = gathered scores                                   */
+  MIRAI_NORM_NONE = 0,  /* weights = gathered scores * route_scale                     */
   MIRAI_NORM_CLAMP = 1, /* w / clamp_min(sum w, 1e-20)       (routers.py:248)          */
-  MIRAI_NORM_EPS = 2    /* w / (sum w + 1e-20) if k > 1, then * route_scale
+  MIRAI_NORM_EPS = 2,   /* w / (sum w + 1e-20) if k > 1, then * route_scale
                            (transformer_lingbot_video.py:1031-1033)                   */
+  MIRAI_NORM_L1 = 3     /* w / max(sum |w|, 1e-12), then * route_scale (MAGI-2:
+                           F.normalize(p=1), flash_mh_moe/route.py:144-145, and the
+                           route_scale of magi2_preview.py:2742)                      */
 };
 
-/* Output element type selector. */
-enum { MIRAI_DTYPE_BF16 = 0, MIRAI_DTYPE_F32 = 1 };
+/* Output element type selector.  MIRAI_COMBINE_BF16_ACCUM (combine only):
+ * bf16 output summed in bf16, out = bf16(out + bf16(y * bf16(w))) route by
+ * route in ascending sorted position -- MAGI-2's weighted index_add on bf16
+ * tensors (grouped_moe.py:751-756). */
+enum { MIRAI_DTYPE_BF16 = 0, MIRAI_DTYPE_F32 = 1, MIRAI_COMBINE_BF16_ACCUM = 2 };
+
+/* Expert weight layouts of the *_ex GEMMs: [G, out, in] (the compressed
+ * experts', w1/w3 [E, I, H], w2 [E, H, I]) or [G, in, out] (MAGI-2's W_gate /
+ * W_up [heads*E, d_head, d_expert], W_down [heads*E, d_expert, d_head],
+ * magi2_preview.py:2686-2709; NF4 blocks along each stored row). */
+enum { MIRAI_LAYOUT_OUT_IN = 0, MIRAI_LAYOUT_IN_OUT = 1 };
+/* Gate/up activations: SwiGLU silu(g) * u (experts.py:301-317), or MAGI-2's
+ * swiglu7 min(g,7) sigmoid(1.702 min(g,7)) (clamp(u,-7,7) + 1) computed in fp32
+ * on the bf16 gate/up (grouped_moe.py:287-335). */
+enum { MIRAI_ACT_SWIGLU = 0, MIRAI_ACT_SWIGLU7 = 1 };
 
 /* Frozen NF4 expert tensor as stored by the reference for one key
  * (CompressedGroupedExperts._store_nf4_grouped, experts.py:998-1031;
@@ -128,11 +144,21 @@ int mirai_route_topk(const float* logits, int64_t num_tokens, int32_t num_expert
                      float route_scale, int64_t* top_indices, float* top_weights,
                      mirai_stream_t stream);
 
+/* The same with one bias row per `bias_period` consecutive tokens: token t
+ * ranks score + bias_rows[(t / bias_period) * E + e].  MAGI-2 routes every
+ * head over its own experts with its own expert_bias row
+ * (compute_topk_probs_and_indices, flash_mh_moe/route.py:157-199; logits
+ * [heads, S, E] as heads * S rows, bias [heads, E], bias_period = S). */
+int mirai_route_topk_rows(const float* logits, int64_t num_tokens, int32_t num_experts, int32_t top_k,
+                          int32_t score_func, const float* bias_rows, int64_t bias_period, int32_t norm_mode,
+                          float route_scale, int64_t* top_indices, float* top_weights, mirai_stream_t stream);
+
 /* -------------------------------------------------------- a2: dispatch plan
  * Replaces build_dispatch_plan (dispatch_preprocess.py:128-179): stable sort of
  * the flat [T*k] expert ids, bincount, cumsum, inverse permutation.  Outputs:
  * counts/starts int64 [E], offsets int32 [E] (inclusive), sort_positions,
- * sorted_token_indices, inverse_order int64 [T*k].  Deterministic. */
+ * sorted_token_indices, inverse_order int64 [T*k].  Deterministic.
+ * E <= 4096 (MAGI-2's flattened heads x experts groups included). */
 size_t mirai_dispatch_plan_workspace_bytes(int64_t num_tokens, int32_t top_k, int32_t num_experts);
 int mirai_dispatch_plan(const int64_t* top_indices, int64_t num_tokens, int32_t top_k,
                         int32_t num_experts, int64_t* counts, int64_t* starts, int32_t* offsets,
@@ -325,6 +351,41 @@ int mirai_moe_down_dx_lora_int8(const void* grad_y, const int32_t* offsets, int3
                                 int64_t num_rows, int32_t hidden, int32_t inter, const mirai_int8_weight* w2,
                                 const void* gate_up, const void* rank_a, const void* rank_b,
                                 void* grad_gate_up, mirai_stream_t stream);
+
+/* ------------------------------- f4: any weight layout, activation, group count
+ * The four grouped GEMMs (gate/up + activation, down, down dX with the
+ * activation's backward, gate/up dX) for weights in either layout above and
+ * any number of groups (more than 1024 run as consecutive launches of 1024
+ * groups).  MAGI-2's multi-head grouped MoE (grouped_moe.py:583-757) flattens
+ * (head, expert) into heads * E groups over (token, head) rows of d_head
+ * features: hidden = d_head, inter = d_expert.  Replaces its grouped matmul
+ * roles (_grouped_linear / _grouped_linear_dx, grouped_moe.py:206-284, over
+ * gemm.py:359-367,433-482 segments) and the swiglu7 forward / backward.
+ * bf16 and NF4 weights; the [G, in, out] layout needs CTA pairs (the default). */
+int mirai_moe_gateup_ex_bf16(const void* x_sorted, const int32_t* offsets, int32_t num_groups, int64_t num_rows,
+                             int32_t hidden, int32_t inter, const void* w1, const void* w3, int32_t layout,
+                             int32_t activation, void* h, void* gate_up, mirai_stream_t stream);
+int mirai_moe_gateup_ex_nf4(const void* x_sorted, const int32_t* offsets, int32_t num_groups, int64_t num_rows,
+                            int32_t hidden, int32_t inter, const mirai_nf4_weight* w1, const mirai_nf4_weight* w3,
+                            int32_t layout, int32_t activation, void* h, void* gate_up, mirai_stream_t stream);
+int mirai_moe_down_ex_bf16(const void* h, const int32_t* offsets, int32_t num_groups, int64_t num_rows,
+                           int32_t inter, int32_t hidden, const void* w2, int32_t layout, void* y,
+                           mirai_stream_t stream);
+int mirai_moe_down_ex_nf4(const void* h, const int32_t* offsets, int32_t num_groups, int64_t num_rows,
+                          int32_t inter, int32_t hidden, const mirai_nf4_weight* w2, int32_t layout, void* y,
+                          mirai_stream_t stream);
+int mirai_moe_down_dx_ex_bf16(const void* grad_y, const int32_t* offsets, int32_t num_groups, int64_t num_rows,
+                              int32_t hidden, int32_t inter, const void* w2, int32_t layout, int32_t activation,
+                              const void* gate_up, void* grad_gate_up, mirai_stream_t stream);
+int mirai_moe_down_dx_ex_nf4(const void* grad_y, const int32_t* offsets, int32_t num_groups, int64_t num_rows,
+                             int32_t hidden, int32_t inter, const mirai_nf4_weight* w2, int32_t layout,
+                             int32_t activation, const void* gate_up, void* grad_gate_up, mirai_stream_t stream);
+int mirai_moe_gateup_dx_ex_bf16(const void* grad_gate_up, const int32_t* offsets, int32_t num_groups,
+                                int64_t num_rows, int32_t inter, int32_t hidden, const void* w1, const void* w3,
+                                int32_t layout, void* dx_sorted, mirai_stream_t stream);
+int mirai_moe_gateup_dx_ex_nf4(const void* grad_gate_up, const int32_t* offsets, int32_t num_groups,
+                               int64_t num_rows, int32_t inter, int32_t hidden, const mirai_nf4_weight* w1,
+                               const mirai_nf4_weight* w3, int32_t layout, void* dx_sorted, mirai_stream_t stream);
 
 /* --------------------------------------------------- a4 / a5: weight ingest
  * NF4 quantisation of a bf16 [E, out, in] expert stack into the reference's

@@ -129,6 +129,19 @@ SIGNATURES = {
                                           c_vp, c_vp, c_size, c_vp]),
     "mirai_int8_quantize_rows": (ctypes.c_int, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "mirai_rotate_rows": (ctypes.c_int, [c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i32, c_vp]),
+    "mirai_route_topk_rows": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_i64, c_i32, c_f32, c_vp,
+                                             c_vp, c_vp]),
+    **{f"mirai_moe_gateup_ex_{f}": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, t, t, c_i32, c_i32, c_vp,
+                                                   c_vp, c_vp])
+       for f, t in (("bf16", c_vp), ("nf4", ctypes.POINTER(Nf4Weight)))},
+    **{f"mirai_moe_down_ex_{f}": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, t, c_i32, c_vp, c_vp])
+       for f, t in (("bf16", c_vp), ("nf4", ctypes.POINTER(Nf4Weight)))},
+    **{f"mirai_moe_down_dx_ex_{f}": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, t, c_i32, c_i32, c_vp,
+                                                    c_vp, c_vp])
+       for f, t in (("bf16", c_vp), ("nf4", ctypes.POINTER(Nf4Weight)))},
+    **{f"mirai_moe_gateup_dx_ex_{f}": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, t, t, c_i32, c_vp,
+                                                      c_vp])
+       for f, t in (("bf16", c_vp), ("nf4", ctypes.POINTER(Nf4Weight)))},
     "mirai_swiglu_backward_rotated": (ctypes.c_int, [c_vp, c_vp, c_i64, c_i32, c_i32, c_vp, c_vp]),
     "mirai_moe_down_dh_int8": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, ctypes.POINTER(Int8Weight),
                                               c_vp, c_vp]),

@@ -173,9 +173,9 @@ def route(tokens: torch.Tensor, weight: torch.Tensor, *, top_k: int, score_func:
     if norm_topk_prob:  # w / (sum w + 1e-20) for k > 1, then * route_scale, in the kernel
         idx, w = ops.route_topk(lg, top_k, score_func=score_func, choice_bias=bias, norm="eps",
                                 route_scale=route_scale)
-    else:
-        idx, w = ops.route_topk(lg, top_k, score_func=score_func, choice_bias=bias, norm="none")
-        w = w * route_scale
+    else:  # the gathered scores times route_scale
+        idx, w = ops.route_topk(lg, top_k, score_func=score_func, choice_bias=bias, norm="none",
+                                route_scale=route_scale)
     if torch.is_grad_enabled() and logits.requires_grad:
         scores = torch.sigmoid(logits) if score_func == "sigmoid" else torch.softmax(logits, dim=-1)
         w = scores.gather(1, idx)

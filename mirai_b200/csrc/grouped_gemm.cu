@@ -67,10 +67,26 @@ constexpr int kMaxNested = 512;    // nested absmax entries per expert and key
 enum Mode { GATEUP = 0, DOWN = 1, DXDOWN = 2, DXGATEUP = 3 };
 enum WFmt { W_BF16 = 0, W_NF4 = 1, W_INT8 = 2 };
 
+// How a mode's two weight keys (if any) share a B tile: side by side along N
+// (gate/up: the gate columns, then the up columns of the same channels) or
+// one after the other along K (gate/up dX: K = [gate | up]).  Whether B is
+// read K-major or MN-major is a separate template flag of the kernel: the
+// reference's compressed experts store W as [E, out, in], so their forward
+// reads B K-major and their dX MN-major; MAGI-2's experts store W as
+// [E, in, out] (grouped_moe.py:109-154), the other way round.
 template <int MODE> struct MCfg {
-  static constexpr bool MN = MODE == DXDOWN || MODE == DXGATEUP;  // B operand MN-major
-  static constexpr bool TWO_KEYS = MODE == GATEUP || MODE == DXGATEUP;
+  static constexpr bool NSPLIT = MODE == GATEUP;
+  static constexpr bool KSPLIT = MODE == DXGATEUP;
+  static constexpr bool TWO_KEYS = NSPLIT || KSPLIT;
+  // B layout of the reference's compressed-expert layout ([E, out, in]) in this mode
+  static constexpr bool MN_NATIVE = MODE == DXDOWN || MODE == DXGATEUP;
 };
+
+// Gate/up activation applied by the GATEUP epilogue (and differentiated by the
+// DXDOWN epilogue): SwiGLU h = silu(g) * u (experts.py:301-317), or MAGI-2's
+// swiglu7 h = g' sigmoid(1.702 g') (u' + 1) with g' = min(g, 7) and
+// u' = clamp(u, -7, 7) (grouped_moe.py:287-335).
+enum Act { ACT_SWIGLU = 0, ACT_SWIGLU7 = 1 };
 
 // Per (format, pairing) geometry.
 template <int WF, bool PAIR> struct Cfg {
@@ -145,6 +161,8 @@ struct Params {
   int nbs_shift;           // log2(nested_blocksize)
   int has_ext;             // 1: one extra bf16 k-block (the LoRA rank block) from tmap_xa / tmap_xb
   int nsrc;                // row sources: segment s*(E/nsrc) + w holds source s's rows for weight expert w
+  int act;                 // Act of the gate/up epilogue (GATEUP) and of its backward (DXDOWN)
+  int prev_end;            // 1: segment 0 starts at offsets[-1] (a later chunk of > kMaxExperts groups)
 };
 
 // Control block in shared memory.  16-byte aligned size: the dequantiser
@@ -227,6 +245,24 @@ __device__ __forceinline__ void source_block(const Smem<WF, PAIR>& sm, int e, in
 }
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// MAGI-2's swiglu7 on bf16 gate / up values, in fp32 (grouped_moe.py:287-306):
+// g' = min(g, 7), u' = clamp(u, -7, 7), h = g' sigmoid(1.702 g') (u' + 1).
+__device__ __forceinline__ float swiglu7(float g, float u) {
+  const float gc = fminf(g, 7.f), uc = fminf(fmaxf(u, -7.f), 7.f);
+  const float sg = __fdividef(1.f, 1.f + __expf(-1.702f * gc));
+  return gc * sg * (uc + 1.f);
+}
+
+// Its backward (grouped_moe.py:309-335): given dh, the gradients of the
+// unclamped gate and up; the clamps pass no gradient outside their ranges.
+__device__ __forceinline__ void swiglu7_backward(float dh, float g, float u, float& dg, float& du) {
+  const float gc = fminf(g, 7.f), uc = fminf(fmaxf(u, -7.f), 7.f);
+  const float sg = __fdividef(1.f, 1.f + __expf(-1.702f * gc));
+  const float dgate = g <= 7.f ? sg + 1.702f * gc * sg * (1.f - sg) : 0.f;
+  dg = dh * dgate * (uc + 1.f);
+  du = (u >= -7.f && u <= 7.f) ? dh * (gc * sg) : 0.f;
+}
 
 // Per-warpgroup register budget (all four warps of the group execute it).
 template <int N> __device__ __forceinline__ void setmaxnreg_inc() {
@@ -315,7 +351,7 @@ __device__ __forceinline__ int kmajor_row(const Params& p, int e, int n, int h) 
   return MODE == GATEUP ? e * p.out_rows + n * (TN / 2) : e * p.out_rows + n * TN + h * (TN / 2);
 }
 
-template <int MODE, int WF, bool PAIR>
+template <int MODE, int WF, bool PAIR, bool BMN>
 __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b0,
                         const __grid_constant__ CUtensorMap tmap_b1, const __grid_constant__ CUtensorMap tmap_xa,
@@ -330,7 +366,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   constexpr int SUB_M = C::SUB_M;
   constexpr uint32_t A_STAGE = C::A_STAGE;
   constexpr bool QUANT = WF != W_BF16;
-  constexpr bool MN = MCfg<MODE>::MN;
+  constexpr bool MN = BMN;
+  using MC = MCfg<MODE>;
+  // B layouts other than the compressed-expert one run on CTA pairs only
+  static_assert(PAIR || MN == MC::MN_NATIVE, "the transposed weight layout runs on CTA pairs");
   // NF4 on CTA pairs: each tile's absmax codes reach one of two buffers a
   // tile ahead of use, so the dequantisers never stop to stage them.  K-major,
   // they are one contiguous run of B_ROWS x K/64 bytes, bulk-copied by the
@@ -353,6 +392,15 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int E = p.E;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // position in the CTA pair
+  // this CTA's key of an N-split tile, and the key / k-block-in-key of a k-block
+  auto key_of = [&](int kb) -> int {
+    return MC::KSPLIT ? (kb >= p.kb_half ? 1 : 0) : ((MC::NSPLIT && PAIR) ? (int)rank : 0);
+  };
+  auto kk_of = [&](int kb, int key) -> int { return (MC::KSPLIT && key) ? kb - p.kb_half : kb; };
+  // MN-major: first column (in the key's matrix) of 64-column block nb of this CTA's B
+  auto mn_col = [&](int n, int nb) -> int {
+    return MC::NSPLIT ? n * (C::TN / 2) + nb * 64 : n * C::TN + (int)rank * C::B_ROWS + nb * 64;
+  };
   const bool leader = rank == 0;
   const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // tile-scheduling unit
   const int num_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
@@ -375,7 +423,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       if (j < E) {
         const int g = (j % nsrc) * wexp + j / nsrc;
         const int64_t end = p.offsets[g];
-        const int64_t beg = g > 0 ? p.offsets[g - 1] : 0;
+        const int64_t beg = (g > 0 || p.prev_end) ? p.offsets[g - 1] : 0;
         const int64_t endc = end < p.S ? end : p.S;
         cnt = endc > beg ? (int)((endc - beg + TILE_M - 1) / TILE_M) : 0;
         if (end < beg || end > p.S) device_fail(MIRAI_ERR_DEVICE_BOUNDS, 600 + MODE);
@@ -499,10 +547,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           }
           const uint32_t full_addr = full_leader0 + 8u * stage;
           const bool ext = kb == num_kb;  // the fused rank block
-          // B source for this k-block
-          const bool key1 = MCfg<MODE>::TWO_KEYS && (MN ? kb >= p.kb_half : (PAIR && rank == 1));
-          const CUtensorMap* mb = key1 ? &tmap_b1 : &tmap_b0;
-          const int krow = MN ? e * p.krows + (kb - ((MN && key1) ? p.kb_half : 0)) * BK : 0;
+          // B source for this k-block: its key, the k-block inside the key
+          const int key = key_of(kb), kk = kk_of(kb, key);
+          const CUtensorMap* mb = key ? &tmap_b1 : &tmap_b0;
+          const int krow = MN ? e * p.krows + kk * BK : 0;
           const int pair_mult = PAIR ? 2 : 1;
           if (leader) {
             const uint32_t bytes = pair_mult * (n_live * A_BYTES + ((QUANT && !ext) ? 0u : B_BYTES));
@@ -528,17 +576,15 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           } else if (!QUANT) {
             uint8_t* b_dst = sB + stage * B_BYTES;
             if (MN) {
-              // this CTA's columns: n*TN + rank*B_ROWS + 64*nb
+              // this CTA's 64-column blocks of the key's [K, N] matrix
 #pragma unroll
-              for (int nb = 0; nb < C::B_ROWS / 64; ++nb)
-                load(b_dst + nb * 8192, mb, n * TN + (int)rank * C::B_ROWS + nb * 64, krow);
+              for (int nb = 0; nb < C::B_ROWS / 64; ++nb) load(b_dst + nb * 8192, mb, mn_col(n, nb), krow);
             } else if (PAIR) {
-              // B_ROWS rows per CTA: gate/up -> rank 0 W1, rank 1 W3; down -> W2 rows block `rank`
-              load(b_dst, mb, kb * BK, kmajor_row<MODE, TN>(p, e, n, (int)rank));
+              // B_ROWS rows per CTA: gate/up -> rank 0 W1, rank 1 W3; others -> rows block `rank`
+              load(b_dst, mb, kk * BK, kmajor_row<MODE, TN>(p, e, n, (int)rank));
             } else {
-              load(b_dst, &tmap_b0, kb * BK, kmajor_row<MODE, TN>(p, e, n, 0));
-              load(b_dst + B_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * BK,
-                   kmajor_row<MODE, TN>(p, e, n, 1));
+              load(b_dst, MODE == GATEUP ? &tmap_b0 : mb, kk * BK, kmajor_row<MODE, TN>(p, e, n, 0));
+              load(b_dst + B_BYTES / 2, MODE == GATEUP ? &tmap_b1 : mb, kk * BK, kmajor_row<MODE, TN>(p, e, n, 1));
             }
           }
           for (int sub = 0; sub < n_live; ++sub) {
@@ -660,13 +706,18 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             uint32_t hp[16], gp[16], up[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              // Round where the reference's bf16 tensors round: gate, up,
-              // silu(gate), and the product (experts.py:301-317).
+              // Round where the reference's bf16 tensors round: gate and up (the
+              // GEMM outputs), then SwiGLU's silu(gate) and product (experts.py:301-317)
+              // or swiglu7 in fp32 on the bf16 gate/up (grouped_moe.py:287-306).
               const float g0 = bf16r(__uint_as_float(g[2 * j])), g1 = bf16r(__uint_as_float(g[2 * j + 1]));
               const float u0 = bf16r(__uint_as_float(u[2 * j])), u1 = bf16r(__uint_as_float(u[2 * j + 1]));
-              const float a0 = bf16r(__fdividef(g0, 1.f + __expf(-g0)));
-              const float a1 = bf16r(__fdividef(g1, 1.f + __expf(-g1)));
-              hp[j] = pack_bf16x2(a0 * u0, a1 * u1);
+              if (p.act == ACT_SWIGLU7) {
+                hp[j] = pack_bf16x2(swiglu7(g0, u0), swiglu7(g1, u1));
+              } else {
+                const float a0 = bf16r(__fdividef(g0, 1.f + __expf(-g0)));
+                const float a1 = bf16r(__fdividef(g1, 1.f + __expf(-g1)));
+                hp[j] = pack_bf16x2(a0 * u0, a1 * u1);
+              }
               gp[j] = pack_bf16x2(g0, g1);
               up[j] = pack_bf16x2(u0, u1);
             }
@@ -715,6 +766,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
                 const float dh = bf16r(__uint_as_float(v32[2 * j + hh]));
                 const float gv = hh ? bf16_hi(gw[j]) : bf16_lo(gw[j]);
                 const float uv = hh ? bf16_hi(uw[j]) : bf16_lo(uw[j]);
+                if (p.act == ACT_SWIGLU7) {
+                  swiglu7_backward(dh, gv, uv, dgo[hh], duo[hh]);
+                  continue;
+                }
                 const float sg = __fdividef(1.f, 1.f + __expf(-gv));
                 const float act = bf16r(gv * sg);
                 const float dact = bf16r(dh * uv);
@@ -779,20 +834,20 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           const bool ext = kb == num_kb;  // the rank block has no raw codes: an empty stage
           mbar_arrive_expect_tx(&sm.raw_full[rstage], ext ? 0u : RAW_BYTES);
           if (!ext) {
-            const bool key1 = MCfg<MODE>::TWO_KEYS && (MN ? kb >= p.kb_half : (PAIR && rank == 1));
-            const CUtensorMap* mb = key1 ? &tmap_b1 : &tmap_b0;
-            const int krow = MN ? e * p.krows + (kb - (key1 ? p.kb_half : 0)) * BK : 0;
+            const int key = key_of(kb), kk = kk_of(kb, key);
+            const CUtensorMap* mb = key ? &tmap_b1 : &tmap_b0;
+            const int krow = MN ? e * p.krows + kk * BK : 0;
             uint8_t* r_dst = sRaw + rstage * RAW_BYTES;
             if (MN) {
 #pragma unroll
               for (int nb = 0; nb < C::B_ROWS / 64; ++nb)
-                tma_load_2d(r_dst + nb * 64 * RB, mb, (n * TN + (int)rank * C::B_ROWS + nb * 64) * RB / 64, krow,
-                            &sm.raw_full[rstage]);
+                tma_load_2d(r_dst + nb * 64 * RB, mb, mn_col(n, nb) * RB / 64, krow, &sm.raw_full[rstage]);
             } else if (PAIR) {
-              tma_load_2d(r_dst, mb, kb * RB, kmajor_row<MODE, TN>(p, e, n, (int)rank), &sm.raw_full[rstage]);
+              tma_load_2d(r_dst, mb, kk * RB, kmajor_row<MODE, TN>(p, e, n, (int)rank), &sm.raw_full[rstage]);
             } else {
-              tma_load_2d(r_dst, &tmap_b0, kb * RB, kmajor_row<MODE, TN>(p, e, n, 0), &sm.raw_full[rstage]);
-              tma_load_2d(r_dst + RAW_BYTES / 2, MODE == GATEUP ? &tmap_b1 : &tmap_b0, kb * RB,
+              tma_load_2d(r_dst, MODE == GATEUP ? &tmap_b0 : mb, kk * RB, kmajor_row<MODE, TN>(p, e, n, 0),
+                          &sm.raw_full[rstage]);
+              tma_load_2d(r_dst + RAW_BYTES / 2, MODE == GATEUP ? &tmap_b1 : mb, kk * RB,
                           kmajor_row<MODE, TN>(p, e, n, 1), &sm.raw_full[rstage]);
             }
           }
@@ -829,39 +884,46 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         // global memory (row-major, 16-byte aligned: rows is a multiple of 64)
         const int first = kmajor_row<MODE, TN>(p, e, n, (int)rank) - e * p.out_rows;
         const int rows = min(C::B_ROWS, p.out_rows - first);
-        const int key = MCfg<MODE>::TWO_KEYS ? (int)rank : 0;
-        const uint4* src = reinterpret_cast<const uint4*>(
-            p.q[key].absmax + (size_t)kmajor_row<MODE, TN>(p, e, n, (int)rank) * num_kb);
-        const int chunks = rows > 0 ? rows * num_kb / 16 : 0;
+        // k-blocks per weight row of one key: a K-split tile takes the first kb_half
+        // k-blocks from key 0 and the rest from key 1
+        const int nkbk = MC::KSPLIT ? p.kb_half : num_kb;
+        for (int kq = 0; kq < (MC::KSPLIT ? 2 : 1); ++kq) {
+          const int key = MC::KSPLIT ? kq : (MC::NSPLIT ? (int)rank : 0);
+          const uint4* src = reinterpret_cast<const uint4*>(
+              p.q[key].absmax + (size_t)kmajor_row<MODE, TN>(p, e, n, (int)rank) * nkbk);
+          const int chunks = rows > 0 ? rows * nkbk / 16 : 0;
 #pragma unroll 1
-        for (int c = lane; c < chunks; c += 32) {
-          const uint4 v = __ldg(src + c);
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-          int r = (16 * c) / num_kb, kb = 16 * c - r * num_kb;
+          for (int c = lane; c < chunks; c += 32) {
+            const uint4 v = __ldg(src + c);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            int r = (16 * c) / nkbk, kb = 16 * c - r * nkbk;
 #pragma unroll
-          for (int b = 0; b < 16; ++b) {
-            dst[kb * C::B_ROWS + r] = (uint8_t)(w[b >> 2] >> (8 * (b & 3)));
-            if (++kb == num_kb) kb = 0, ++r;
+            for (int b = 0; b < 16; ++b) {
+              dst[(kq * nkbk + kb) * C::B_ROWS + r] = (uint8_t)(w[b >> 2] >> (8 * (b & 3)));
+              if (++kb == nkbk) kb = 0, ++r;
+            }
           }
         }
         mbar_arrive(&sm.absq_full[buf]);  // release: this lane's stores are visible to the waiters
         continue;
       }
-      const int nb0 = n * (TN / 64) + (int)rank * NB;  // first column block of this CTA (even)
+      const int nb0 = mn_col(n, 0) / 64;  // first column block of this CTA in the key's rows (even)
       static_assert(!(PREFETCH && MN) || NB == 2, "one 16-bit load covers this CTA's two column blocks");
       if (NB == 2 && (nblk_row & 1) == 0 && nb0 + 1 < nblk_row) {
         // both codes of a k-row in one aligned 16-bit load, four k-rows in flight per lane
 #pragma unroll 4
         for (int kk = lane; kk < p.K; kk += 32) {
-          const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
-          const uint8_t* src = p.q[key].absmax + ((size_t)e * p.krows + (kk - key * p.krows)) * nblk_row + nb0;
+          const int key = MC::KSPLIT ? (kk >= p.krows ? 1 : 0) : (MC::NSPLIT ? (int)rank : 0);
+          const int wr = (MC::KSPLIT && key) ? kk - p.krows : kk;
+          const uint8_t* src = p.q[key].absmax + ((size_t)e * p.krows + wr) * nblk_row + nb0;
           reinterpret_cast<uint16_t*>(dst)[kk] = __ldg(reinterpret_cast<const uint16_t*>(src));
         }
       } else {
 #pragma unroll 1
         for (int kk = lane; kk < p.K; kk += 32) {
-          const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
-          const uint8_t* src = p.q[key].absmax + ((size_t)e * p.krows + (kk - key * p.krows)) * nblk_row;
+          const int key = MC::KSPLIT ? (kk >= p.krows ? 1 : 0) : (MC::NSPLIT ? (int)rank : 0);
+          const int wr = (MC::KSPLIT && key) ? kk - p.krows : kk;
+          const uint8_t* src = p.q[key].absmax + ((size_t)e * p.krows + wr) * nblk_row;
 #pragma unroll
           for (int jj = 0; jj < NB; ++jj)
             dst[kk * NB + jj] = nb0 + jj < nblk_row ? __ldg(src + nb0 + jj) : (uint8_t)0;
@@ -900,8 +962,8 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     for (int t = unit; t < total_tiles && !failed && !*abort_flag; t += num_units, ++tl) {
       int j, e, m, n;
       decode_tile<WF, PAIR>(t, sm, units, p.n_tiles, j, e, m, n);
-      // key of this thread's rows (K-major) / of the k-block (MN)
-      const int row_key = MN ? 0 : (MCfg<MODE>::TWO_KEYS ? kblk : 0);
+      // key of this thread's rows (K-major, N-split keys); K-split keys follow the k-block
+      const int row_key = (!MN && MC::NSPLIT) ? kblk : 0;
       const int wrow_base = MN ? 0 : kmajor_row<MODE, TN>(p, e, n, kblk) - e * p.out_rows;  // first weight row
       const int abuf = tl & 1;
       if (PREFETCH && !mbar_wait(&sm.absq_full[abuf], (tl >> 1) & 1, 42)) {
@@ -920,7 +982,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             const int first = kmajor_row<MODE, TN>(p, e, n, blk) - e * p.out_rows;
             const int rows = min(TN / 2, p.out_rows - first);
             if (rows <= 0) continue;  // past the last row
-            const int key = MCfg<MODE>::TWO_KEYS ? blk : 0;
+            const int key = MC::NSPLIT ? blk : 0;
             const uint4* src = reinterpret_cast<const uint4*>(
                 p.q[key].absmax + (size_t)kmajor_row<MODE, TN>(p, e, n, blk) * nkb);
             uint4* dst = reinterpret_cast<uint4*>(dq->absq + h * (TN / 2) * nkb);
@@ -931,21 +993,21 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           constexpr int NB = C::B_ROWS / 64;
           for (int i = d; i < p.K * NB; i += C::DEQ_THREADS) {
             const int kk = i / NB, j = i % NB;
-            const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
+            const int key = (MC::KSPLIT && kk >= p.krows) ? 1 : 0;
             const int wr = kk - key * p.krows;
             const int nbg = n * (TN / 64) + nbase + j;
             dq->absq[i] = nbg < nblk_row
                               ? __ldg(p.q[key].absmax + ((size_t)e * p.krows + wr) * nblk_row + nbg) : (uint8_t)0;
           }
         }
-        for (int h = 0; h < (MCfg<MODE>::TWO_KEYS ? 2 : 1); ++h)
+        for (int h = 0; h < (MC::TWO_KEYS ? 2 : 1); ++h)
           for (int i = d; i < p.q[h].n_nested; i += C::DEQ_THREADS)
             dq->nested[h][i] = __ldg(p.q[h].nested_absmax + (size_t)e * p.q[h].n_nested + i);
       } else if (WF == W_INT8 && MN) {
         // INT8 MN-major: the scale belongs to the k-row (output channel of W)
         float* srow = reinterpret_cast<float*>(dq->absq);
         for (int kk = d; kk < p.K; kk += C::DEQ_THREADS) {
-          const int key = (MCfg<MODE>::TWO_KEYS && kk >= p.krows) ? 1 : 0;
+          const int key = (MC::KSPLIT && kk >= p.krows) ? 1 : 0;
           srow[kk] = __ldg(p.q[key].scale + (size_t)e * p.krows + (kk - key * p.krows));
         }
       }
@@ -959,7 +1021,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       float off[2] = {0.f, 0.f};
       if (WF == W_NF4) {
         off[0] = __ldg(p.q[0].offset + e);
-        off[1] = MCfg<MODE>::TWO_KEYS ? __ldg(p.q[1].offset + e) : off[0];
+        off[1] = MC::TWO_KEYS ? __ldg(p.q[1].offset + e) : off[0];
       }
       const int absq_row = PAIR ? 0 : kblk;  // absq block of this thread (K-major)
       for (int kb = 0; kb < total_kb; ++kb, ++gk) {
@@ -976,7 +1038,9 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         if (kb != nkb) {  // the rank block arrives by TMA: nothing to decode
           const uint8_t* raw = sRaw + rst * RAW_BYTES + row * RB;
           const uint32_t row_addr = smem_u32(sB + st * B_BYTES) + (uint32_t)row * 128u;
-          const int key = MN ? ((MCfg<MODE>::TWO_KEYS && kb >= p.kb_half) ? 1 : 0) : row_key;
+          // the k-block's key: K-split by k-block, N-split by this CTA (pairs) or by row half
+          const int key = MC::KSPLIT ? (kb >= p.kb_half ? 1 : 0) : (MN ? key_of(kb) : row_key);
+          const int kk0 = kk_of(kb, key);  // k-block inside the key's matrix
           if (WF == W_NF4) {
             // the row's 32 code bytes as two 16-byte loads; rows 4..7 of every 8 take the halves
             // in the other order, so that each 8-lane phase of a load covers all 32 banks
@@ -994,13 +1058,13 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             uint32_t qcode;
             bool live = row_live;
             if (!MN) {
-              blk = (wrow_base + kr) * nkb + kb;
+              blk = (wrow_base + kr) * (MC::KSPLIT ? p.kb_half : nkb) + kk0;
               qcode = PREFETCH ? dq->absq[abuf * ABUF + kb * C::B_ROWS + kr]
                                : dq->absq[absq_row * (TN / 2) * nkb + kr * nkb + kb];
             } else {
-              const int kk = kb * BK + kr;        // k-row across both keys
-              const int wr = kk - key * p.krows;  // k-row inside the key's matrix
-              const int nbg = n * (TN / 64) + nbase + nbq;
+              const int kk = kb * BK + kr;                           // k-row across both keys
+              const int wr = (MC::KSPLIT && key) ? kk - p.krows : kk;  // k-row inside the key's matrix
+              const int nbg = mn_col(n, 0) / 64 + nbq;
               live = nbg < nblk_row;
               blk = wr * nblk_row + nbg;
               qcode = dq->absq[(PREFETCH ? abuf * ABUF : 0) + kk * (C::B_ROWS / 64) + nbq];
@@ -1090,12 +1154,12 @@ static bool use_pairs() {
   return v == 1;
 }
 
-template <int MODE, int WF, bool PAIR>
+template <int MODE, int WF, bool PAIR, bool BMN>
 int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const CUtensorMap& txa,
                 const CUtensorMap& txb, const Params& p,
                 cudaStream_t stream) {
   using C = Cfg<WF, PAIR>;
-  auto kern = grouped_gemm_kernel<MODE, WF, PAIR>;
+  auto kern = grouped_gemm_kernel<MODE, WF, PAIR, BMN>;
   constexpr size_t smem = smem_bytes<WF, PAIR>();
   static_assert(smem <= 232448, "shared memory budget exceeded");
   static bool attr_set = false;
@@ -1157,12 +1221,24 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
   return check_launch(names[MODE]);
 }
 
-template <int MODE, int WF>
+// BMN: B read MN-major.  The compressed-expert layout ([E, out, in]) has its
+// native B layout per mode (every format, single CTAs or pairs); the MAGI-2
+// layout ([E, in, out]) reads the other way round, for bf16 and NF4, on pairs.
+template <int MODE, int WF, bool BMN>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const CUtensorMap& txa,
            const CUtensorMap& txb, const Params& p,
            cudaStream_t stream) {
-  return use_pairs() ? launch_impl<MODE, WF, true>(ta, tb0, tb1, txa, txb, p, stream)
-                     : launch_impl<MODE, WF, false>(ta, tb0, tb1, txa, txb, p, stream);
+  if constexpr (BMN == MCfg<MODE>::MN_NATIVE) {
+    return use_pairs() ? launch_impl<MODE, WF, true, BMN>(ta, tb0, tb1, txa, txb, p, stream)
+                       : launch_impl<MODE, WF, false, BMN>(ta, tb0, tb1, txa, txb, p, stream);
+  } else if constexpr (WF == W_INT8) {
+    return set_error(MIRAI_ERR_UNSUPPORTED, "INT8 experts are read in the [E, out, in] layout only");
+  } else {
+    if (!use_pairs())
+      return set_error(MIRAI_ERR_UNSUPPORTED, "the [E, in, out] weight layout runs on CTA pairs "
+                       "(MIRAI_B200_CTA_PAIR=0 is set)");
+    return launch_impl<MODE, WF, true, BMN>(ta, tb0, tb1, txa, txb, p, stream);
+  }
 }
 
 static inline bool mis16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; }
@@ -1170,14 +1246,14 @@ static inline bool mis16(const void* ptr) { return (reinterpret_cast<uintptr_t>(
 // Shared host-side checks, the A-operand tensor map and the mode geometry.
 template <int MODE>
 int prepare(const char* name, const void* a, const int32_t* offsets, int E, int64_t S, int K, int N, void* out,
-            void* gate_up, Params& p, CUtensorMap& ta, bool dh_only) {
+            void* gate_up, Params& p, CUtensorMap& ta, bool dh_only, bool bmn) {
   if (E <= 0 || E > kMaxExperts || S < 0 || K <= 0 || N <= 0)
     return set_error(MIRAI_ERR_INVALID_ARG, "%s: bad sizes (E=%d, S=%lld, K=%d, N=%d)", name, E, (long long)S, K, N);
   // column granularity: every mode masks a partial last tile (gate/up: 128 W1
   // rows beside 128 W3 rows; the others: 256 columns) in 32-column chunks and,
   // for NF4/INT8, by weight row, so N % 64 is enough
   const int ntile = 64;
-  if (K % BK != 0 || N % ntile != 0)
+  if (K % BK != 0 || N % ntile != 0 || (MCfg<MODE>::KSPLIT && (K / 2) % BK != 0))
     return set_error(MIRAI_ERR_UNSUPPORTED, "%s: needs K %% %d == 0 and N %% %d == 0 (K=%d, N=%d)", name, BK, ntile,
                      K, N);
   if (S >= (int64_t)1 << 31) return set_error(MIRAI_ERR_UNSUPPORTED, "%s: more than 2^31 routed rows", name);
@@ -1193,8 +1269,8 @@ int prepare(const char* name, const void* a, const int32_t* offsets, int E, int6
   p.K = K;
   p.N = N;
   p.n_tiles = 0;  // set per tile geometry at launch
-  p.krows = MODE == DXDOWN ? K : (MODE == DXGATEUP ? K / 2 : 0);
-  p.kb_half = MODE == DXGATEUP ? (K / 2) / BK : 0;
+  p.krows = bmn ? (MCfg<MODE>::KSPLIT ? K / 2 : K) : 0;
+  p.kb_half = MCfg<MODE>::KSPLIT ? (K / 2) / BK : 0;
   p.out_rows = N;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = N;
@@ -1283,28 +1359,25 @@ struct RankBlock {
   const void* b;
 };
 
-// E weight experts; nsrc > 1: `offsets` has nsrc * E segments, source-major
-// (segment s*E + e = rows of source s for expert e).
+// One launch over at most kMaxExperts groups (see run).
 template <int MODE>
-int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t S, int K, int N, void* out,
-        void* gate_up, const WeightArg& w0, const WeightArg& w1, int rows, int cols, mirai_stream_t stream,
-        const RankBlock* ext = nullptr, int nsrc = 1, bool dh_only = false) {
-  if (nsrc <= 0 || E <= 0 || (int64_t)nsrc * E > kMaxExperts)
-    return set_error(MIRAI_ERR_INVALID_ARG, "%s: %d sources x %d experts outside 1..%d segments", name, nsrc, E,
-                     kMaxExperts);
-  if (S == 0) return MIRAI_OK;
+int run_groups(const char* name, const void* a, const int32_t* offsets, int E, int64_t S, int K, int N, void* out,
+               void* gate_up, const WeightArg& w0, const WeightArg& w1, int rows, int cols, mirai_stream_t stream,
+               const RankBlock* ext, int nsrc, bool dh_only, bool mn, int act, bool prev_end) {
   Params p;
   CUtensorMap ta, t0, t1, txa, txb;
   const int box_rows = kmajor_box_rows(w0.fmt);
-  int rc = prepare<MODE>(name, a, offsets, nsrc * E, S, K, N, out, gate_up, p, ta, dh_only);
+  int rc = prepare<MODE>(name, a, offsets, nsrc * E, S, K, N, out, gate_up, p, ta, dh_only, mn);
   p.nsrc = nsrc;
+  p.act = act;
+  p.prev_end = prev_end ? 1 : 0;
   if (!rc && ext) {
     if (!ext->a || !ext->b) rc = set_error(MIRAI_ERR_INVALID_ARG, "%s: null rank-block operand", name);
     if (!rc)
       rc = make_tmap_2d(&txa, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ext->a, 64, (uint64_t)S, 128, BK, BM,
                         CU_TENSOR_MAP_SWIZZLE_128B);
     if (!rc) {
-      if (MCfg<MODE>::MN)  // [E*64 rank rows (k), N cols]
+      if (mn)  // [E*64 rank rows (k), N cols]
         rc = make_tmap_2d(&txb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ext->b, (uint64_t)N, (uint64_t)E * BK,
                           (uint64_t)N * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
       else  // [E*N rows, 64 rank cols (k)]
@@ -1313,14 +1386,11 @@ int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t 
     }
     p.has_ext = 1;
   }
-  constexpr bool MN = MCfg<MODE>::MN;
-  if (!rc && MN && w0.fmt != W_BF16 && K > kMaxK)
+  if (!rc && w0.fmt != W_BF16 && K > kMaxK)
     rc = set_error(MIRAI_ERR_UNSUPPORTED, "%s: reduction length %d exceeds %d", name, K, kMaxK);
-  if (!rc && !MN && w0.fmt != W_BF16 && K > kMaxK)
-    rc = set_error(MIRAI_ERR_UNSUPPORTED, "%s: in_features %d exceeds %d", name, K, kMaxK);
   int s0 = 8, s1 = 8;
-  if (!rc) rc = bind_key(w0, t0, p.q[0], s0, E, rows, cols, MN, box_rows);
-  if (!rc && MCfg<MODE>::TWO_KEYS) rc = bind_key(w1, t1, p.q[1], s1, E, rows, cols, MN, box_rows);
+  if (!rc) rc = bind_key(w0, t0, p.q[0], s0, E, rows, cols, mn, box_rows);
+  if (!rc && MCfg<MODE>::TWO_KEYS) rc = bind_key(w1, t1, p.q[1], s1, E, rows, cols, mn, box_rows);
   if (!rc && MCfg<MODE>::TWO_KEYS && s0 != s1)
     rc = set_error(MIRAI_ERR_UNSUPPORTED, "%s: the two keys use different nested blocksizes", name);
   if (rc) return rc;
@@ -1334,11 +1404,79 @@ int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t 
     txb = t0;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  constexpr bool NAT = MCfg<MODE>::MN_NATIVE;
   switch (w0.fmt) {
-    case W_BF16: return launch<MODE, W_BF16>(ta, t0, t1, txa, txb, p, st);
-    case W_NF4: return launch<MODE, W_NF4>(ta, t0, t1, txa, txb, p, st);
-    default: return launch<MODE, W_INT8>(ta, t0, t1, txa, txb, p, st);
+    case W_BF16:
+      return mn == NAT ? launch<MODE, W_BF16, NAT>(ta, t0, t1, txa, txb, p, st)
+                       : launch<MODE, W_BF16, !NAT>(ta, t0, t1, txa, txb, p, st);
+    case W_NF4:
+      return mn == NAT ? launch<MODE, W_NF4, NAT>(ta, t0, t1, txa, txb, p, st)
+                       : launch<MODE, W_NF4, !NAT>(ta, t0, t1, txa, txb, p, st);
+    default:
+      return mn == NAT ? launch<MODE, W_INT8, NAT>(ta, t0, t1, txa, txb, p, st)
+                       : launch<MODE, W_INT8, !NAT>(ta, t0, t1, txa, txb, p, st);
   }
+}
+
+// One expert's share of each weight buffer, to start a chunk of groups at
+// group g0 (bf16 / NF4 / INT8 buffers are [E, rows, cols] in their encodings).
+struct KeyShift {
+  mirai_nf4_weight nf4;
+  mirai_int8_weight int8;
+};
+static WeightArg shift_weight(const WeightArg& w, int64_t g0, int rows, int cols, KeyShift& hold) {
+  const int64_t n = (int64_t)rows * cols;
+  WeightArg r = w;
+  if (w.fmt == W_BF16) {
+    r.bf16 = static_cast<const uint8_t*>(w.bf16) + g0 * n * 2;
+  } else if (w.fmt == W_NF4) {
+    hold.nf4 = *w.nf4;
+    const int64_t blocks = n / 64;
+    const int64_t nested = (blocks + w.nf4->nested_blocksize - 1) / w.nf4->nested_blocksize;
+    hold.nf4.packed += g0 * n / 2;
+    hold.nf4.absmax += g0 * blocks;
+    hold.nf4.nested_absmax += g0 * nested;
+    hold.nf4.offset += g0;
+    r.nf4 = &hold.nf4;
+  } else {
+    hold.int8 = *w.int8;
+    hold.int8.q += g0 * n;
+    hold.int8.scale += g0 * rows;
+    r.int8 = &hold.int8;
+  }
+  return r;
+}
+
+// E weight experts; nsrc > 1: `offsets` has nsrc * E segments, source-major
+// (segment s*E + e = rows of source s for expert e).  bmn: read B MN-major
+// (the native layout of the mode's compressed-expert weights, or the MAGI-2
+// [E, in, out] layout read the other way); act: the gate/up activation.
+// More than kMaxExperts groups (one source) run as consecutive launches over
+// chunks of kMaxExperts groups, each starting at the previous chunk's end.
+template <int MODE>
+int run(const char* name, const void* a, const int32_t* offsets, int E, int64_t S, int K, int N, void* out,
+        void* gate_up, const WeightArg& w0, const WeightArg& w1, int rows, int cols, mirai_stream_t stream,
+        const RankBlock* ext = nullptr, int nsrc = 1, bool dh_only = false, int bmn = -1, int act = ACT_SWIGLU) {
+  if (nsrc <= 0 || E <= 0 || (nsrc > 1 && (int64_t)nsrc * E > kMaxExperts))
+    return set_error(MIRAI_ERR_INVALID_ARG, "%s: %d sources x %d experts outside 1..%d segments", name, nsrc, E,
+                     kMaxExperts);
+  const bool mn = bmn < 0 ? MCfg<MODE>::MN_NATIVE : bmn != 0;
+  if (S == 0) return MIRAI_OK;
+  if (E > kMaxExperts) {
+    if (ext) return set_error(MIRAI_ERR_UNSUPPORTED, "%s: a rank block with more than %d groups", name, kMaxExperts);
+    for (int g0 = 0; g0 < E; g0 += kMaxExperts) {
+      const int Ec = E - g0 < kMaxExperts ? E - g0 : kMaxExperts;
+      KeyShift h0, h1;
+      const WeightArg c0 = shift_weight(w0, g0, rows, cols, h0);
+      const WeightArg c1 = MCfg<MODE>::TWO_KEYS ? shift_weight(w1, g0, rows, cols, h1) : c0;
+      const int rc = run_groups<MODE>(name, a, offsets + g0, Ec, S, K, N, out, gate_up, c0, c1, rows, cols,
+                                      stream, nullptr, 1, dh_only, mn, act, g0 > 0);
+      if (rc) return rc;
+    }
+    return MIRAI_OK;
+  }
+  return run_groups<MODE>(name, a, offsets, E, S, K, N, out, gate_up, w0, w1, rows, cols, stream, ext, nsrc, dh_only,
+                          mn, act, false);
 }
 
 inline WeightArg wb(const void* w) { return WeightArg{W_BF16, w, nullptr, nullptr}; }
@@ -1349,6 +1487,37 @@ inline WeightArg wi(const mirai_int8_weight* w) { return WeightArg{W_INT8, nullp
 }  // namespace mirai
 
 using namespace mirai::gg;
+
+// ---- any weight layout and activation (MAGI-2 multi-head grouped experts and
+// the compressed-expert layout alike), any number of groups.
+//   layout MIRAI_LAYOUT_OUT_IN: w1/w3 [G, I, H], w2 [G, H, I] (compressed experts)
+//          MIRAI_LAYOUT_IN_OUT: w1/w3 [G, H, I], w2 [G, I, H] (MAGI-2 W_gate/W_up/W_down)
+static int layout_ok(const char* name, int32_t layout, int32_t act) {
+  if (layout != MIRAI_LAYOUT_OUT_IN && layout != MIRAI_LAYOUT_IN_OUT)
+    return set_error(MIRAI_ERR_INVALID_ARG, "%s: unknown weight layout %d", name, layout);
+  if (act != MIRAI_ACT_SWIGLU && act != MIRAI_ACT_SWIGLU7)
+    return set_error(MIRAI_ERR_INVALID_ARG, "%s: unknown activation %d", name, act);
+  return MIRAI_OK;
+}
+
+template <int MODE>
+static int run_ex(const char* name, const void* a, const int32_t* offsets, int32_t groups, int64_t S, int K, int N,
+                  void* out, void* gate_up, const WeightArg& w0, const WeightArg& w1, int32_t layout, int32_t act,
+                  mirai_stream_t stream) {
+  if (int rc = layout_ok(name, layout, act)) return rc;
+  const bool in_out = layout == MIRAI_LAYOUT_IN_OUT;
+  // one key's [rows, cols] per group: OUT_IN stores [out, in], IN_OUT [in, out]
+  int rows, cols;
+  switch (MODE) {
+    case GATEUP: rows = in_out ? K : N, cols = in_out ? N : K; break;           // K = H, N = I
+    case DOWN: rows = in_out ? K : N, cols = in_out ? N : K; break;             // K = I, N = H
+    case DXDOWN: rows = in_out ? N : K, cols = in_out ? K : N; break;           // K = H, N = I
+    default: rows = in_out ? N : K / 2, cols = in_out ? K / 2 : N; break;      // K = 2I, N = H
+  }
+  const bool mn = in_out != MCfg<MODE>::MN_NATIVE;
+  return run<MODE>(name, a, offsets, groups, S, K, N, out, gate_up, w0, w1, rows, cols, stream, nullptr, 1,
+                   MODE == DXDOWN && gate_up == nullptr, mn ? 1 : 0, act);
+}
 
 extern "C" {
 
@@ -1528,5 +1697,37 @@ int mirai_moe_gateup_dx_int8(const void* grad_gate_up, const int32_t* offsets, i
   return run<DXGATEUP>("gateup_dx_int8", grad_gate_up, offsets, num_experts, num_rows, 2 * inter, hidden, dx_sorted,
                        nullptr, wi(w1), wi(w3), inter, hidden, stream);
 }
+
+#define MIRAI_EX_ENTRIES(SUF, WT, WRAP)                                                                          \
+  int mirai_moe_gateup_ex_##SUF(const void* x_sorted, const int32_t* offsets, int32_t num_groups,              \
+                                int64_t num_rows, int32_t hidden, int32_t inter, WT w1, WT w3, int32_t layout, \
+                                int32_t activation, void* h, void* gate_up, mirai_stream_t stream) {          \
+    return run_ex<GATEUP>("gateup_ex_" #SUF, x_sorted, offsets, num_groups, num_rows, hidden, inter, h,         \
+                          gate_up, WRAP(w1), WRAP(w3), layout, activation, stream);                             \
+  }                                                                                                              \
+  int mirai_moe_down_ex_##SUF(const void* h, const int32_t* offsets, int32_t num_groups, int64_t num_rows,     \
+                              int32_t inter, int32_t hidden, WT w2, int32_t layout, void* y,                    \
+                              mirai_stream_t stream) {                                                           \
+    return run_ex<DOWN>("down_ex_" #SUF, h, offsets, num_groups, num_rows, inter, hidden, y, nullptr, WRAP(w2), \
+                        WRAP(w2), layout, MIRAI_ACT_SWIGLU, stream);                                             \
+  }                                                                                                              \
+  int mirai_moe_down_dx_ex_##SUF(const void* grad_y, const int32_t* offsets, int32_t num_groups,               \
+                                 int64_t num_rows, int32_t hidden, int32_t inter, WT w2, int32_t layout,       \
+                                 int32_t activation, const void* gate_up, void* grad_gate_up,                  \
+                                 mirai_stream_t stream) {                                                        \
+    if (!gate_up) return set_error(MIRAI_ERR_INVALID_ARG, "down_dx_ex_" #SUF ": saved gate/up is required");   \
+    return run_ex<DXDOWN>("down_dx_ex_" #SUF, grad_y, offsets, num_groups, num_rows, hidden, inter,            \
+                          grad_gate_up, const_cast<void*>(gate_up), WRAP(w2), WRAP(w2), layout, activation,     \
+                          stream);                                                                               \
+  }                                                                                                              \
+  int mirai_moe_gateup_dx_ex_##SUF(const void* grad_gate_up, const int32_t* offsets, int32_t num_groups,       \
+                                   int64_t num_rows, int32_t inter, int32_t hidden, WT w1, WT w3,              \
+                                   int32_t layout, void* dx_sorted, mirai_stream_t stream) {                   \
+    return run_ex<DXGATEUP>("gateup_dx_ex_" #SUF, grad_gate_up, offsets, num_groups, num_rows, 2 * inter,      \
+                            hidden, dx_sorted, nullptr, WRAP(w1), WRAP(w3), layout, MIRAI_ACT_SWIGLU, stream); \
+  }
+MIRAI_EX_ENTRIES(bf16, const void*, wb)
+MIRAI_EX_ENTRIES(nf4, const mirai_nf4_weight*, wn)
+#undef MIRAI_EX_ENTRIES
 
 }  // extern "C"

@@ -14,13 +14,15 @@ constexpr int kRouteMaxPerLane = 32;  // E <= 1024
 template <int PER_LANE>
 __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict__ logits, int64_t T, int E,
                                                          int k, int score_func,
-                                                         const float* __restrict__ bias, int norm_mode,
-                                                         float route_scale, int64_t* __restrict__ out_idx,
-                                                         float* __restrict__ out_w) {
+                                                         const float* __restrict__ bias_rows, int64_t bias_period,
+                                                         int norm_mode, float route_scale,
+                                                         int64_t* __restrict__ out_idx, float* __restrict__ out_w) {
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (t >= T) return;
   const float* row = logits + t * E;
+  // bias row of this token: rows of `bias_period` tokens share one (MAGI-2: one per head)
+  const float* bias = bias_rows ? bias_rows + (t / bias_period) * E : nullptr;
   float lg[PER_LANE], sc[PER_LANE], ch[PER_LANE];
   float mx = -INFINITY;
 #pragma unroll
@@ -111,10 +113,18 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
         divide = true;
       }
       scale = route_scale;
+    } else if (norm_mode == MIRAI_NORM_L1) {
+      float asum = 0.f;  // F.normalize(p=1, eps=1e-12): w / max(sum |w|, eps)
+      for (int j = 0; j < k; ++j) asum += fabsf(wsel[j]);
+      den = fmaxf(asum, 1e-12f);
+      divide = true;
+      scale = route_scale;
+    } else {
+      scale = route_scale;  // MIRAI_NORM_NONE: the gathered scores times route_scale
     }
     for (int j = 0; j < k; ++j) {
       float w = divide ? wsel[j] / den : wsel[j];
-      if (norm_mode == MIRAI_NORM_EPS) w = w * scale;
+      if (norm_mode != MIRAI_NORM_CLAMP) w = w * scale;
       out_idx[t * k + j] = isel[j];
       out_w[t * k + j] = w;
     }
@@ -132,7 +142,12 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
 constexpr int kPlanThreads = 256;
 constexpr int kPlanRounds = 8;
 constexpr int kPlanChunk = kPlanThreads * kPlanRounds;  // 2048 routes per chunk
-constexpr int kPlanMaxExperts = 1024;
+// Up to 4096 groups (MAGI-2 flattens heads x experts: 12 x 256 = 3072).  The
+// per-chunk histograms live in dynamic shared memory sized by E.
+constexpr int kPlanMaxExperts = 4096;
+constexpr int kPlanWarps = 8;  // kPlanThreads / 32
+inline size_t plan_hist_smem(int E) { return (size_t)E * sizeof(int); }
+inline size_t plan_scatter_smem(int E) { return (size_t)(1 + kPlanWarps) * E * sizeof(int); }
 
 // Range check shared by every dispatch-plan entry point, made before any size
 // is computed from the arguments: nullptr when they are usable, else why not.
@@ -140,7 +155,7 @@ constexpr int kPlanMaxExperts = 1024;
 // before the product is formed (no int64 overflow for any T).
 inline const char* plan_sizes_problem(int64_t num_tokens, int32_t top_k, int32_t num_experts) {
   if (top_k <= 0) return "top_k must be positive";
-  if (num_experts <= 0 || num_experts > kPlanMaxExperts) return "expert count outside [1, 1024]";
+  if (num_experts <= 0 || num_experts > kPlanMaxExperts) return "expert count outside [1, 4096]";
   if (num_tokens < 0) return "negative token count";
   if (num_tokens > (int64_t)INT32_MAX / top_k) return "T*k exceeds the int32 range of the plan";
   return nullptr;
@@ -149,7 +164,7 @@ inline const char* plan_sizes_problem(int64_t num_tokens, int32_t top_k, int32_t
 __global__ void __launch_bounds__(kPlanThreads) plan_histogram_kernel(const int64_t* __restrict__ idx,
                                                                       int64_t S, int E,
                                                                       int* __restrict__ chunk_counts) {
-  __shared__ int hist[kPlanMaxExperts];
+  extern __shared__ int hist[];  // [E]
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
   const int64_t base = (int64_t)blockIdx.x * kPlanChunk;
@@ -188,13 +203,17 @@ __global__ void __launch_bounds__(256) plan_chunk_scan_kernel(int* __restrict__ 
 }
 
 // (2b) one block: exclusive scan of the expert totals -> starts, offsets.
+// Thread i owns experts [i*PER, (i+1)*PER) (PER = ceil(E / 1024) <= 4).
 __global__ void __launch_bounds__(1024) plan_expert_scan_kernel(const int64_t* __restrict__ counts, int E,
                                                                 int64_t* __restrict__ starts,
                                                                 int32_t* __restrict__ offsets) {
   __shared__ int64_t warp_sums[32];
-  const int e = threadIdx.x;
+  const int per = (E + 1023) / 1024;
+  const int e0 = threadIdx.x * per;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t v = (e < E) ? counts[e] : 0;
+  int64_t v = 0;
+  for (int i = 0; i < per; ++i)
+    if (e0 + i < E) v += counts[e0 + i];
   int64_t incl = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -213,10 +232,13 @@ __global__ void __launch_bounds__(1024) plan_expert_scan_kernel(const int64_t* _
     warp_sums[lane] = ws;
   }
   __syncthreads();
-  const int64_t excl = (warp > 0 ? warp_sums[warp - 1] : 0) + incl - v;
-  if (e < E) {
-    starts[e] = excl;
-    offsets[e] = (int32_t)(excl + v);
+  int64_t run = (warp > 0 ? warp_sums[warp - 1] : 0) + incl - v;
+  for (int i = 0; i < per; ++i) {
+    const int e = e0 + i;
+    if (e >= E) break;
+    starts[e] = run;
+    run += counts[e];
+    offsets[e] = (int32_t)run;
   }
 }
 
@@ -224,15 +246,17 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter_kernel(
     const int64_t* __restrict__ idx, int64_t S, int E, int k, const int* __restrict__ chunk_base,
     const int64_t* __restrict__ starts,
     int64_t* __restrict__ sort_positions, int64_t* __restrict__ sorted_tok, int64_t* __restrict__ inverse) {
-  constexpr int kWarps = kPlanThreads / 32;
-  __shared__ int running[kPlanMaxExperts];
-  __shared__ int warp_hist[kWarps][kPlanMaxExperts];
+  constexpr int kWarps = kPlanWarps;
+  static_assert(kWarps * 32 == kPlanThreads, "one histogram row per warp");
+  extern __shared__ int plan_smem[];  // running [E], then kWarps rows of [E]
+  int* running = plan_smem;
+  auto warp_hist = [&](int w, int e) -> int& { return plan_smem[(1 + w) * E + e]; };
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int e = threadIdx.x; e < E; e += blockDim.x)
     running[e] = (int)starts[e] + chunk_base[(int64_t)blockIdx.x * E + e];
   const int64_t base = (int64_t)blockIdx.x * kPlanChunk;
   for (int r = 0; r < kPlanRounds; ++r) {
-    for (int i = threadIdx.x; i < kWarps * E; i += blockDim.x) warp_hist[i / E][i % E] = 0;
+    for (int i = threadIdx.x; i < kWarps * E; i += blockDim.x) plan_smem[E + i] = 0;
     __syncthreads();
     const int64_t p = base + r * kPlanThreads + threadIdx.x;
     const bool valid = p < S;
@@ -241,11 +265,11 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter_kernel(
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int rank_in_warp = __popc(peers & ((1u << lane) - 1u));
     const int leader = __ffs(peers) - 1;
-    if (e >= 0 && lane == leader) warp_hist[warp][e] = __popc(peers);
+    if (e >= 0 && lane == leader) warp_hist(warp, e) = __popc(peers);
     __syncthreads();
     if (e >= 0) {
       int pos = running[e] + rank_in_warp;
-      for (int w = 0; w < warp; ++w) pos += warp_hist[w][e];
+      for (int w = 0; w < warp; ++w) pos += warp_hist(w, e);
       sort_positions[pos] = p;
       sorted_tok[pos] = p / k;
       inverse[p] = pos;
@@ -253,7 +277,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_scatter_kernel(
     __syncthreads();
     for (int ee = threadIdx.x; ee < E; ee += blockDim.x) {
       int add = 0;
-      for (int w = 0; w < kWarps; ++w) add += warp_hist[w][ee];
+      for (int w = 0; w < kWarps; ++w) add += warp_hist(w, ee);
       running[ee] += add;
     }
     __syncthreads();
@@ -285,6 +309,8 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const uint4* __restri
 // ascending sorted position, then a single rounding to the output type.
 // ============================================================================
 constexpr int kMaxTopK = 16;
+
+__device__ __forceinline__ float bf16r_(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
 __global__ void __launch_bounds__(256) combine_kernel(const uint4* __restrict__ y, const int64_t* __restrict__ inv,
                                                       const float* __restrict__ w, int64_t T, int k, int H,
@@ -323,13 +349,23 @@ __global__ void __launch_bounds__(256) combine_kernel(const uint4* __restrict__ 
     for (int j = 0; j < k; ++j) {
       const uint4 u = __ldg(y + pos[j] * vec_per_row + v);
       const uint32_t wd[4] = {u.x, u.y, u.z, u.w};
+      if (out_dtype == MIRAI_COMBINE_BF16_ACCUM) {
+        // bf16 tensors throughout: bf16(y * bf16(w)) added into a bf16 running sum
+        const float wb = bf16r_(wt[j]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[2 * q] = bf16r_(acc[2 * q] + bf16r_(bf16_lo(wd[q]) * wb));
+          acc[2 * q + 1] = bf16r_(acc[2 * q + 1] + bf16r_(bf16_hi(wd[q]) * wb));
+        }
+        continue;
+      }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         acc[2 * q] = __fadd_rn(acc[2 * q], __fmul_rn(bf16_lo(wd[q]), wt[j]));
         acc[2 * q + 1] = __fadd_rn(acc[2 * q + 1], __fmul_rn(bf16_hi(wd[q]), wt[j]));
       }
     }
-    if (out_dtype == MIRAI_DTYPE_BF16) {
+    if (out_dtype != MIRAI_DTYPE_F32) {
       uint4 o;
       o.x = pack_bf16x2(acc[0], acc[1]);
       o.y = pack_bf16x2(acc[2], acc[3]);
@@ -394,25 +430,27 @@ static inline bool misaligned16(const void* p) { return (reinterpret_cast<uintpt
 
 extern "C" {
 
-int mirai_route_topk(const float* logits, int64_t num_tokens, int32_t num_experts, int32_t top_k,
-                     int32_t score_func, const float* choice_bias, int32_t norm_mode, float route_scale,
-                     int64_t* top_indices, float* top_weights, mirai_stream_t stream) {
+static int route_topk_impl(const char* name, const float* logits, int64_t num_tokens, int32_t num_experts,
+                           int32_t top_k, int32_t score_func, const float* bias, int64_t bias_period,
+                           int32_t norm_mode, float route_scale, int64_t* top_indices, float* top_weights,
+                           mirai_stream_t stream) {
   if (num_tokens < 0 || num_experts <= 0 || num_experts > 1024 || top_k <= 0 || top_k > num_experts ||
       top_k > 16)
-    return set_error(MIRAI_ERR_INVALID_ARG, "route_topk: need 0 < k <= min(E, 16), E <= 1024 (E=%d, k=%d)",
+    return set_error(MIRAI_ERR_INVALID_ARG, "%s: need 0 < k <= min(E, 16), E <= 1024 (E=%d, k=%d)", name,
                      num_experts, top_k);
   if (score_func != MIRAI_SCORE_SOFTMAX && score_func != MIRAI_SCORE_SIGMOID)
-    return set_error(MIRAI_ERR_INVALID_ARG, "route_topk: unknown score_func %d", score_func);
-  if (norm_mode < MIRAI_NORM_NONE || norm_mode > MIRAI_NORM_EPS)
-    return set_error(MIRAI_ERR_INVALID_ARG, "route_topk: unknown norm_mode %d", norm_mode);
+    return set_error(MIRAI_ERR_INVALID_ARG, "%s: unknown score_func %d", name, score_func);
+  if (norm_mode < MIRAI_NORM_NONE || norm_mode > MIRAI_NORM_L1)
+    return set_error(MIRAI_ERR_INVALID_ARG, "%s: unknown norm_mode %d", name, norm_mode);
+  if (bias && bias_period <= 0) return set_error(MIRAI_ERR_INVALID_ARG, "%s: bias period must be positive", name);
   if (num_tokens == 0) return MIRAI_OK;
-  if (!logits || !top_indices || !top_weights)
-    return set_error(MIRAI_ERR_INVALID_ARG, "route_topk: null pointer");
+  if (!logits || !top_indices || !top_weights) return set_error(MIRAI_ERR_INVALID_ARG, "%s: null pointer", name);
   const int blocks = (int)((num_tokens + 7) / 8);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int per_lane = (num_experts + 31) / 32;
-#define MIRAI_ROUTE_LAUNCH(P)                                                                              \
-  route_topk_kernel<P><<<blocks, 256, 0, s>>>(logits, num_tokens, num_experts, top_k, score_func, choice_bias, \
+  const int64_t period = bias ? bias_period : 1;
+#define MIRAI_ROUTE_LAUNCH(P)                                                                                  \
+  route_topk_kernel<P><<<blocks, 256, 0, s>>>(logits, num_tokens, num_experts, top_k, score_func, bias, period, \
                                               norm_mode, route_scale, top_indices, top_weights)
   if (per_lane <= 1) MIRAI_ROUTE_LAUNCH(1);
   else if (per_lane <= 2) MIRAI_ROUTE_LAUNCH(2);
@@ -421,7 +459,21 @@ int mirai_route_topk(const float* logits, int64_t num_tokens, int32_t num_expert
   else if (per_lane <= 16) MIRAI_ROUTE_LAUNCH(16);
   else MIRAI_ROUTE_LAUNCH(32);
 #undef MIRAI_ROUTE_LAUNCH
-  return check_launch("route_topk");
+  return check_launch(name);
+}
+
+int mirai_route_topk(const float* logits, int64_t num_tokens, int32_t num_experts, int32_t top_k,
+                     int32_t score_func, const float* choice_bias, int32_t norm_mode, float route_scale,
+                     int64_t* top_indices, float* top_weights, mirai_stream_t stream) {
+  return route_topk_impl("route_topk", logits, num_tokens, num_experts, top_k, score_func, choice_bias,
+                         num_tokens > 0 ? num_tokens : 1, norm_mode, route_scale, top_indices, top_weights, stream);
+}
+
+int mirai_route_topk_rows(const float* logits, int64_t num_tokens, int32_t num_experts, int32_t top_k,
+                          int32_t score_func, const float* bias_rows, int64_t bias_period, int32_t norm_mode,
+                          float route_scale, int64_t* top_indices, float* top_weights, mirai_stream_t stream) {
+  return route_topk_impl("route_topk_rows", logits, num_tokens, num_experts, top_k, score_func, bias_rows,
+                         bias_period, norm_mode, route_scale, top_indices, top_weights, stream);
 }
 
 size_t mirai_dispatch_plan_workspace_bytes(int64_t num_tokens, int32_t top_k, int32_t num_experts) {
@@ -455,11 +507,18 @@ int mirai_dispatch_plan(const int64_t* top_indices, int64_t num_tokens, int32_t 
                      workspace_bytes);
   const int chunks = (int)((S + kPlanChunk - 1) / kPlanChunk);
   int* cc = static_cast<int*>(workspace);
-  plan_histogram_kernel<<<chunks, kPlanThreads, 0, s>>>(top_indices, S, num_experts, cc);
+  static bool smem_attr = false;  // the scatter's histograms exceed 48 KB above 1365 experts
+  if (!smem_attr) {
+    cudaError_t e = cudaFuncSetAttribute(plan_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)plan_scatter_smem(kPlanMaxExperts));
+    if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "dispatch_plan: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    smem_attr = true;
+  }
+  plan_histogram_kernel<<<chunks, kPlanThreads, plan_hist_smem(num_experts), s>>>(top_indices, S, num_experts, cc);
   plan_chunk_scan_kernel<<<(num_experts + 7) / 8, 256, 0, s>>>(cc, chunks, num_experts, counts);
   plan_expert_scan_kernel<<<1, 1024, 0, s>>>(counts, num_experts, starts, offsets);
-  plan_scatter_kernel<<<chunks, kPlanThreads, 0, s>>>(top_indices, S, num_experts, top_k, cc, starts,
-                                                      sort_positions, sorted_token_indices, inverse_order);
+  plan_scatter_kernel<<<chunks, kPlanThreads, plan_scatter_smem(num_experts), s>>>(
+      top_indices, S, num_experts, top_k, cc, starts, sort_positions, sorted_token_indices, inverse_order);
   return check_launch("dispatch_plan");
 }
 
@@ -482,7 +541,7 @@ int mirai_moe_combine(const void* y_sorted, const int64_t* inverse_order, const 
                       mirai_stream_t stream) {
   if (num_tokens < 0 || top_k <= 0 || top_k > kMaxTopK || hidden <= 0 || hidden % 8 != 0)
     return set_error(MIRAI_ERR_INVALID_ARG, "combine: need 0 < k <= %d and hidden %% 8 == 0", kMaxTopK);
-  if (out_dtype != MIRAI_DTYPE_BF16 && out_dtype != MIRAI_DTYPE_F32)
+  if (out_dtype != MIRAI_DTYPE_BF16 && out_dtype != MIRAI_DTYPE_F32 && out_dtype != MIRAI_COMBINE_BF16_ACCUM)
     return set_error(MIRAI_ERR_INVALID_ARG, "combine: unknown out_dtype %d", out_dtype);
   if (num_tokens == 0) return MIRAI_OK;
   if (!y_sorted || !inverse_order || !out || misaligned16(y_sorted) || misaligned16(out))

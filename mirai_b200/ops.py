@@ -14,7 +14,10 @@ import torch
 from . import _lib
 
 SCORE_FUNCS = {"softmax": 0, "sigmoid": 1}
-NORM_MODES = {"none": 0, "clamp": 1, "eps": 2}
+NORM_MODES = {"none": 0, "clamp": 1, "eps": 2, "l1": 3}
+LAYOUTS = {"out_in": 0, "in_out": 1}      # [G, out, in] (compressed experts) / [G, in, out] (MAGI-2)
+ACTIVATIONS = {"swiglu": 0, "swiglu7": 1}
+COMBINE_BF16_ACCUM = 2
 
 
 def _ptr(t: torch.Tensor | None) -> _lib.c_vp:
@@ -65,6 +68,13 @@ def route_topk(logits: torch.Tensor, top_k: int, *, score_func: str = "softmax",
     bias = None if choice_bias is None else _cuda(choice_bias, "choice_bias", torch.float32)
     idx = torch.empty((T, top_k), dtype=torch.int64, device=logits.device)
     w = torch.empty((T, top_k), dtype=torch.float32, device=logits.device)
+    if bias is not None and bias.ndim == 2:  # one bias row per T / rows tokens (per head)
+        period = T // bias.shape[0] if bias.shape[0] else 0
+        if period * bias.shape[0] != T:
+            raise ValueError(f"{bias.shape[0]} bias rows do not split {T} tokens evenly")
+        _lib.call("mirai_route_topk_rows", _ptr(logits), T, E, top_k, SCORE_FUNCS[score_func], _ptr(bias), period,
+                  NORM_MODES[norm], float(route_scale), _ptr(idx), _ptr(w), _stream())
+        return idx, w
     _lib.call("mirai_route_topk", _ptr(logits), T, E, top_k, SCORE_FUNCS[score_func], _ptr(bias),
               NORM_MODES[norm], float(route_scale), _ptr(idx), _ptr(w), _stream())
     return idx, w
@@ -389,8 +399,10 @@ def lora_project(x: torch.Tensor, offsets: torch.Tensor, lora: DownLoRA, *, forw
 
 def combine(y_sorted: torch.Tensor, inverse_order: torch.Tensor, top_weights: torch.Tensor | None,
             out_dtype: torch.dtype = torch.bfloat16, out: torch.Tensor | None = None,
-            top_k: int | None = None) -> torch.Tensor:
-    """Weighted un-permute; ``top_weights=None`` sums the routes (permute backward)."""
+            top_k: int | None = None, bf16_accumulate: bool = False) -> torch.Tensor:
+    """Weighted un-permute; ``top_weights=None`` sums the routes (permute backward).
+    ``bf16_accumulate``: bf16 products summed in bf16, route by route (MAGI-2's
+    index_add on bf16 tensors) instead of one fp32 sum."""
     y_sorted = _cuda(y_sorted, "y_sorted", torch.bfloat16)
     inv = _cuda(inverse_order, "inverse_order", torch.int64)
     if top_weights is None:
@@ -404,6 +416,10 @@ def combine(y_sorted: torch.Tensor, inverse_order: torch.Tensor, top_weights: to
     if out is None:
         out = torch.empty((T, H), dtype=out_dtype, device=y_sorted.device)
     code = {torch.bfloat16: 0, torch.float32: 1}[out.dtype]
+    if bf16_accumulate:
+        if out.dtype != torch.bfloat16:
+            raise TypeError("bf16 accumulation writes a bf16 output")
+        code = COMBINE_BF16_ACCUM
     _lib.call("mirai_moe_combine", _ptr(y_sorted), _ptr(inv), _ptr(w), T, k, H, _ptr(out), code, _stream())
     return out
 
@@ -505,6 +521,64 @@ def gateup_dx(grad_gate_up: torch.Tensor, offsets: torch.Tensor, w1, w3, *, hidd
     dxs = out if out is not None else torch.empty((S, hidden), dtype=torch.bfloat16, device=dgu.device)
     _lib.call(f"mirai_moe_gateup_dx_{_fmt_suffix(w1)}", _ptr(dgu), _ptr(offsets), offsets.numel(), S, I2 // 2,
               hidden, _wptr(w1), _wptr(w3), _ptr(dxs), _stream())
+    return dxs
+
+
+# ----------------------------------------------------------------------------- any layout / activation / group count
+
+def _ex_suffix(w) -> str:
+    if isinstance(w, torch.Tensor):
+        return "bf16"
+    if isinstance(w, _lib.Nf4Weight):
+        return "nf4"
+    raise TypeError(f"the *_ex GEMMs read bf16 or NF4 weights, not {type(w)}")
+
+
+def gateup_ex(x_sorted, offsets, w1, w3, *, inter: int, layout: str, activation: str, save_gate_up: bool = False):
+    """gate/up + activation over any number of groups, weights in ``layout``
+    ("out_in" [G, I, H] or "in_out" [G, H, I]); returns h (and gate_up)."""
+    w1, w3 = _as_weight(w1), _as_weight(w3)
+    x_sorted = _cuda(x_sorted, "x_sorted", torch.bfloat16)
+    offsets = _cuda(offsets, "offsets", torch.int32)
+    S, H = x_sorted.shape
+    h = torch.empty((S, inter), dtype=torch.bfloat16, device=x_sorted.device)
+    gu = torch.empty((S, 2 * inter), dtype=torch.bfloat16, device=x_sorted.device) if save_gate_up else None
+    _lib.call(f"mirai_moe_gateup_ex_{_ex_suffix(w1)}", _ptr(x_sorted), _ptr(offsets), offsets.numel(), S, H, inter,
+              _wptr(w1), _wptr(w3), LAYOUTS[layout], ACTIVATIONS[activation], _ptr(h), _ptr(gu), _stream())
+    return (h, gu) if save_gate_up else h
+
+
+def down_ex(h, offsets, w2, *, hidden: int, layout: str):
+    w2 = _as_weight(w2)
+    h = _cuda(h, "h", torch.bfloat16)
+    offsets = _cuda(offsets, "offsets", torch.int32)
+    S, I = h.shape
+    y = torch.empty((S, hidden), dtype=torch.bfloat16, device=h.device)
+    _lib.call(f"mirai_moe_down_ex_{_ex_suffix(w2)}", _ptr(h), _ptr(offsets), offsets.numel(), S, I, hidden,
+              _wptr(w2), LAYOUTS[layout], _ptr(y), _stream())
+    return y
+
+
+def down_dx_ex(grad_y, offsets, w2, gate_up, *, inter: int, layout: str, activation: str):
+    w2 = _as_weight(w2)
+    gy = _cuda(grad_y, "grad_y", torch.bfloat16)
+    offsets = _cuda(offsets, "offsets", torch.int32)
+    gu = _cuda(gate_up, "gate_up", torch.bfloat16)
+    S, H = gy.shape
+    dgu = torch.empty((S, 2 * inter), dtype=torch.bfloat16, device=gy.device)
+    _lib.call(f"mirai_moe_down_dx_ex_{_ex_suffix(w2)}", _ptr(gy), _ptr(offsets), offsets.numel(), S, H, inter,
+              _wptr(w2), LAYOUTS[layout], ACTIVATIONS[activation], _ptr(gu), _ptr(dgu), _stream())
+    return dgu
+
+
+def gateup_dx_ex(grad_gate_up, offsets, w1, w3, *, hidden: int, layout: str):
+    w1, w3 = _as_weight(w1), _as_weight(w3)
+    dgu = _cuda(grad_gate_up, "grad_gate_up", torch.bfloat16)
+    offsets = _cuda(offsets, "offsets", torch.int32)
+    S, I2 = dgu.shape
+    dxs = torch.empty((S, hidden), dtype=torch.bfloat16, device=dgu.device)
+    _lib.call(f"mirai_moe_gateup_dx_ex_{_ex_suffix(w1)}", _ptr(dgu), _ptr(offsets), offsets.numel(), S, I2 // 2,
+              hidden, _wptr(w1), _wptr(w3), LAYOUTS[layout], _ptr(dxs), _stream())
     return dxs
 
 

@@ -245,3 +245,90 @@ def rel_max_err(a: np.ndarray, r: np.ndarray) -> float:
     r = np.asarray(r, dtype=np.float64)
     den = np.abs(r).max()
     return float(np.abs(a - r).max() / den) if den > 0 else float(np.abs(a - r).max())
+
+
+# ----------------------------------------------------------------------------- f4: MAGI-2 multi-head grouped MoE
+
+def magi2_route(x_heads: np.ndarray, gate: np.ndarray, expert_bias: np.ndarray | None, *, experts: int,
+                top_k: int, score_func: str = "sigmoid", route_norm: bool = True, route_scale: float = 1.0):
+    """MAGI-2 router (magi2_preview.py:2727-2744; flash_mh_moe/route.py:28-154,
+    torch path without virtual groups): per head h, logits = x_heads[:, h] @
+    gate[h]^T in fp32, sigmoid / softmax scores, top-k of score +
+    expert_bias[h] (descending, ties to the lower id), weights gathered from
+    the unbiased scores, F.normalize(p=1, eps=1e-12) when route_norm, times
+    route_scale.  Returns (probs [H, S, k], indices [H, S, k])."""
+    S, H, d = x_heads.shape
+    g = np.asarray(gate, dtype=np.float32).reshape(H, experts, d)
+    logits = np.einsum("shd,hed->hse", np.asarray(x_heads, dtype=np.float32), g).astype(np.float32)
+    scores = sigmoid_f32(logits) if score_func == "sigmoid" else softmax_f32(logits)
+    choice = scores if expert_bias is None else (scores + np.asarray(expert_bias, np.float32).reshape(H, 1, experts))
+    order = np.argsort(-choice, axis=-1, kind="stable")[..., :top_k]
+    w = np.take_along_axis(scores, order, axis=-1).astype(np.float32)
+    if route_norm:
+        w = (w / np.maximum(np.abs(w).sum(-1, keepdims=True, dtype=np.float32), np.float32(1e-12))).astype(np.float32)
+    return (w * np.float32(route_scale)).astype(np.float32), order.astype(np.int64)
+
+
+def swiglu7_f32(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """grouped_moe.py:287-306 on fp32 copies of bf16 gate / up."""
+    g = np.minimum(np.asarray(gate, np.float32), np.float32(7.0))
+    u = np.clip(np.asarray(up, np.float32), np.float32(-7.0), np.float32(7.0))
+    return (g * sigmoid_f32(np.float32(1.702) * g) * (u + np.float32(1.0))).astype(np.float32)
+
+
+def swiglu7_backward_f32(grad: np.ndarray, gate: np.ndarray, up: np.ndarray):
+    """grouped_moe.py:309-335 (the same as autograd of the clamps and products)."""
+    gr = np.asarray(gate, np.float32)
+    ur = np.asarray(up, np.float32)
+    g = np.minimum(gr, np.float32(7.0))
+    u = np.clip(ur, np.float32(-7.0), np.float32(7.0))
+    s = sigmoid_f32(np.float32(1.702) * g)
+    dgate = (s + np.float32(1.702) * g * s * (np.float32(1.0) - s)) * (gr <= 7.0)
+    d_g = (grad * dgate * (u + np.float32(1.0))).astype(np.float32)
+    d_u = (grad * (g * s) * ((ur >= -7.0) & (ur <= 7.0))).astype(np.float32)
+    return d_g, d_u
+
+
+def magi2_experts(x_heads: np.ndarray, probs: np.ndarray, idx: np.ndarray, w_gate: np.ndarray, w_up: np.ndarray,
+                  w_down: np.ndarray, grad_out: np.ndarray | None = None):
+    """``CoreMultiHeadMoE._torch_forward`` (magi2_preview.py:2770-2793) in bf16,
+    and, with ``grad_out``, its autograd: per head, per expert (ascending), the
+    selected tokens' gate = bf16(x W_gate[g]), up = bf16(x W_up[g]), h =
+    bf16(swiglu7), y = bf16(h W_down[g]), added as bf16(y * bf16(w)) into a bf16
+    output.  Weights are [G, in, out] with G = heads * experts.
+    Returns out [S, H, d] (and dx [S, H, d], dprobs [H, S, k])."""
+    S, H, d = x_heads.shape
+    E = w_gate.shape[0] // H
+    x = bf16_round(np.asarray(x_heads, np.float32))
+    out = np.zeros((S, H, d), np.float32)
+    dx = np.zeros((S, H, d), np.float32)
+    dprobs = np.zeros(idx.shape, np.float32)
+    for h in range(H):
+        for e in range(E):
+            tok, slot = np.nonzero(idx[h] == e)
+            if tok.size == 0:
+                continue
+            gidx = h * E + e
+            xs = x[tok, h]
+            gate = bf16_round(xs @ w_gate[gidx])
+            up = bf16_round(xs @ w_up[gidx])
+            hid = bf16_round(swiglu7_f32(gate, up))
+            y = bf16_round(hid @ w_down[gidx])
+            wb = bf16_round(probs[h, tok, slot])
+            contrib = bf16_round(y * wb[:, None])
+            for r, t in enumerate(tok):  # index_add_: rows in order, bf16 running sum
+                out[t, h] = bf16_round(out[t, h] + contrib[r])
+            if grad_out is None:
+                continue
+            g = bf16_round(np.asarray(grad_out, np.float32)[tok, h])
+            dy = bf16_round(g * wb[:, None])
+            dprobs[h, tok, slot] = bf16_round((g * y).sum(axis=1, dtype=np.float32))
+            dh = bf16_round(dy @ w_down[gidx].T)
+            d_g, d_u = swiglu7_backward_f32(dh, gate, up)
+            d_g, d_u = bf16_round(d_g), bf16_round(d_u)
+            dxs = bf16_round(bf16_round(d_g @ w_gate[gidx].T) + bf16_round(d_u @ w_up[gidx].T))
+            for r, t in enumerate(tok):
+                dx[t, h] = bf16_round(dx[t, h] + dxs[r])
+    if grad_out is None:
+        return out
+    return out, dx, dprobs

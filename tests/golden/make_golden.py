@@ -91,6 +91,46 @@ def lingbot_block() -> None:
     np.savez_compressed(OUT / "lingbot_block.npz", **res)
 
 
+def magi2_moe() -> None:
+    """MAGI-2's ``CoreMultiHeadMoE`` (magi2_preview.py:2630-2829), vendored
+    reference path (``_torch_forward``, swiglu7, bf16 index_add combine): 4
+    heads of d_head 64, 4 experts per head (16 groups), top-2, d_expert 64,
+    sigmoid routing with a per-head expert bias, L1 route norm, route_scale
+    4.9, bf16.  Records the router's routes, the layer output, and the experts'
+    forward and autograd given those routes (x_heads and topk_probs gradients)."""
+    import torch
+    from mirai.vendors.magi2_preview.model.magi2_preview import CoreMultiHeadMoE, CoreMultiHeadMoEConfig
+
+    torch.manual_seed(31)
+    cfg = CoreMultiHeadMoEConfig(hidden_size=256, num_heads=4, num_experts=4, top_k=2, expert_intermediate_size=64,
+                                 num_layers=1, params_dtype=torch.bfloat16, score_func="sigmoid", route_norm=True,
+                                 route_scale=4.9)
+    m = CoreMultiHeadMoE(cfg)
+    with torch.no_grad():
+        m.gate.normal_(0.0, 0.05)
+        for key in ("W_gate", "W_up", "W_down"):
+            getattr(m, key).normal_(0.0, 0.05)
+        m.router.expert_bias.normal_(0.0, 0.1)
+    S = 96
+    x = torch.randn(S, 256).to(torch.bfloat16)
+    x_heads = x.view(S, 4, 64)
+    with torch.no_grad():
+        probs, idx = m._route(x_heads)
+        out = m._forward_impl(x)
+    xh = x_heads.clone().requires_grad_(True)
+    pr = probs.clone().requires_grad_(True)
+    eo = m._torch_forward(xh, pr, idx)
+    grad = torch.randn_like(eo)
+    eo.backward(grad)
+    np.savez_compressed(
+        OUT / "magi2_moe.npz", x=_bf16_bits(x), gate=m.gate.detach().float().numpy(),
+        expert_bias=m.router.expert_bias.float().numpy(), W_gate=_bf16_bits(m.W_gate), W_up=_bf16_bits(m.W_up),
+        W_down=_bf16_bits(m.W_down), heads=np.int64(4), experts=np.int64(4), top_k=np.int64(2),
+        route_scale=np.float32(4.9), topk_probs=probs.float().numpy(), topk_indices=idx.numpy().astype(np.int64),
+        out=_bf16_bits(out), experts_out=_bf16_bits(eo), grad=_bf16_bits(grad), grad_x_heads=_bf16_bits(xh.grad),
+        grad_probs=pr.grad.float().numpy())
+
+
 def main(only=None) -> None:
     if not REF or not os.path.isdir(os.path.join(REF, "mirai")):
         raise SystemExit("set MIRAI_REFERENCE to the root of a seruva19/mirai checkout (the directory holding mirai/)")
@@ -98,9 +138,11 @@ def main(only=None) -> None:
     import torch
 
     torch.set_num_threads(4)
-    only = set(only or {"basic", "routed", "lingbot_block"})
+    only = set(only or {"basic", "routed", "lingbot_block", "magi2_moe"})
     if "lingbot_block" in only:
         lingbot_block()
+    if "magi2_moe" in only:
+        magi2_moe()
     if "basic" in only:
         basic_fixtures()
     if "routed" in only:
@@ -268,5 +310,5 @@ def routed_fixtures() -> None:
 
 if __name__ == "__main__":
     # no arguments: every fixture; otherwise any of "basic" (router, plan, permute/combine, INT8
-    # quantisation), "routed" (routed execution) and "lingbot_block"
-    main(set(sys.argv[1:]) or {"basic", "routed", "lingbot_block"})
+    # quantisation), "routed" (routed execution), "lingbot_block" and "magi2_moe"
+    main(set(sys.argv[1:]) or {"basic", "routed", "lingbot_block", "magi2_moe"})

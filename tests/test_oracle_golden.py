@@ -116,3 +116,47 @@ def test_nf4_roundtrip_properties():
     assert code[0] == -1.0 and code[-1] == 1.0 and code[7] == 0.0 and np.all(np.diff(code) > 0)
     ncode = oq.dynamic_tree_map()
     assert ncode.shape == (256,) and ncode[-1] == 1.0 and np.all(np.diff(ncode) >= 0)
+
+
+def test_magi2_oracle_matches_the_reference_layer(golden):
+    """The numpy restatement of MAGI-2's multi-head MoE (oracle.moe.magi2_*)
+    against the reference's CoreMultiHeadMoE (fixture recorded from it):
+    routes bit-exact as index sets, forward and autograd within bf16
+    matmul-ordering differences."""
+    g = golden("magi2_moe")
+    b = lambda k: oq.bf16_bits_to_f32(g[k])
+    H, E, k = int(g["heads"]), int(g["experts"]), int(g["top_k"])
+    x = b("x")
+    S = x.shape[0]
+    xh = x.reshape(S, H, -1)
+    p, i = om.magi2_route(xh, g["gate"], g["expert_bias"], experts=E, top_k=k, route_scale=float(g["route_scale"]))
+    ci, cw = om.canonical_slots(i.reshape(-1, k), p.reshape(-1, k))
+    ri, rw = om.canonical_slots(g["topk_indices"].reshape(-1, k), g["topk_probs"].reshape(-1, k))
+    np.testing.assert_array_equal(ci, ri)
+    np.testing.assert_allclose(cw, rw, rtol=1e-5, atol=1e-6)
+    out, dx, dp = om.magi2_experts(xh, g["topk_probs"], g["topk_indices"], b("W_gate"), b("W_up"), b("W_down"),
+                                   b("grad").reshape(xh.shape))
+    assert om.rel_max_err(out.reshape(S, -1), b("out")) < 2e-3
+    assert om.rel_max_err(dx, b("grad_x_heads")) < 5e-3
+    assert om.rel_max_err(dp, g["grad_probs"]) < 1e-2
+
+
+def test_magi2_flat_routes_follow_the_reference_order():
+    """(token, head) rows with flat group ids head * E + expert: a stable sort
+    of them lists each group's tokens in ascending order, the order of the
+    reference's argsort over (head, token, k) (grouped_moe.py:660-666)."""
+    import torch
+    from mirai_b200.magi2 import _flat_routes
+    rng = np.random.default_rng(0)
+    H, S, k, E = 3, 7, 2, 5
+    idx = np.stack([np.stack([rng.permutation(E)[:k] for _ in range(S)]) for _ in range(H)])
+    probs = rng.random((H, S, k)).astype(np.float32)
+    flat, pr = _flat_routes(torch.from_numpy(probs), torch.from_numpy(idx), E)
+    assert flat.shape == (S * H, k) and torch.equal(flat[1 * H + 2], torch.from_numpy(idx[2, 1] + 2 * E))
+    assert torch.equal(pr[1 * H + 2], torch.from_numpy(probs[2, 1]))
+    ours = np.argsort(flat.numpy().reshape(-1), kind="stable")
+    rows_ours = ours // k  # row = token * H + head
+    ref_flat = (idx + (np.arange(H) * E)[:, None, None]).reshape(-1)
+    ref_order = np.argsort(ref_flat, kind="stable")
+    ref_rows = ((ref_order % (S * k)) // k) * H + ref_order // (S * k)
+    np.testing.assert_array_equal(rows_ours, ref_rows)

@@ -81,7 +81,7 @@ def test_static_plan_checks_arguments_before_sizing():
     dev, _lib, ops = _setup()
     idx = torch.zeros((4, 2), dtype=torch.int64, device=dev)
     bufs = [torch.empty(8, dtype=torch.int64, device=dev) for _ in range(6)]
-    for T, k, E in [(4, 2, 2000), (2 ** 40, 2, 8), (4, 0, 8), (-1, 2, 8)]:
+    for T, k, E in [(4, 2, 5000), (2 ** 40, 2, 8), (4, 0, 8), (-1, 2, 8)]:
         with pytest.raises(_lib.MiraiError) as err:
             _lib.call("mirai_dispatch_plan_static", ops._ptr(idx), T, k, E, *[ops._ptr(t) for t in bufs],
                       ops._stream())
