@@ -240,6 +240,31 @@ int mirai_moe_down_src_int8(const void* h, const int32_t* offsets, int32_t num_s
                             int64_t num_rows, int32_t inter, int32_t hidden, const mirai_int8_weight* w2,
                             void* y, mirai_stream_t stream);
 
+/* The dX GEMMs over source-major segments (an expert owner's share of the
+ * expert-parallel backward: gradient rows arrive as the forward's rows did).
+ * down_dx_src with gate_up == NULL writes dh = dy W2 [S, I] (no SwiGLU
+ * backward; the block-Hadamard INT8 format rotates dh first). */
+int mirai_moe_down_dx_src_bf16(const void* grad_y, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                               int64_t num_rows, int32_t hidden, int32_t inter, const void* w2, const void* gate_up,
+                               void* grad_gate_up, mirai_stream_t stream);
+int mirai_moe_down_dx_src_nf4(const void* grad_y, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                              int64_t num_rows, int32_t hidden, int32_t inter, const mirai_nf4_weight* w2,
+                              const void* gate_up, void* grad_gate_up, mirai_stream_t stream);
+int mirai_moe_down_dx_src_int8(const void* grad_y, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                               int64_t num_rows, int32_t hidden, int32_t inter, const mirai_int8_weight* w2,
+                               const void* gate_up, void* grad_gate_up, mirai_stream_t stream);
+int mirai_moe_gateup_dx_src_bf16(const void* grad_gate_up, const int32_t* offsets, int32_t num_sources,
+                                 int32_t num_experts, int64_t num_rows, int32_t inter, int32_t hidden,
+                                 const void* w1, const void* w3, void* dx_sorted, mirai_stream_t stream);
+int mirai_moe_gateup_dx_src_nf4(const void* grad_gate_up, const int32_t* offsets, int32_t num_sources,
+                                int32_t num_experts, int64_t num_rows, int32_t inter, int32_t hidden,
+                                const mirai_nf4_weight* w1, const mirai_nf4_weight* w3, void* dx_sorted,
+                                mirai_stream_t stream);
+int mirai_moe_gateup_dx_src_int8(const void* grad_gate_up, const int32_t* offsets, int32_t num_sources,
+                                 int32_t num_experts, int64_t num_rows, int32_t inter, int32_t hidden,
+                                 const mirai_int8_weight* w1, const mirai_int8_weight* w3, void* dx_sorted,
+                                 mirai_stream_t stream);
+
 /* ------------------------------------------------------------- a8: combine
  * out[t, :] = sum_j top_weights[t, j] * y[inverse_order[t*k + j], :], summed in
  * fp32 in ascending sorted position (the order of the reference's

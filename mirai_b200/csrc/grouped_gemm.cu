@@ -1618,6 +1618,29 @@ int mirai_moe_down_dx_int8(const void* grad_y, const int32_t* offsets, int32_t n
                      const_cast<void*>(gate_up), wi(w2), wi(w2), hidden, inter, stream);
 }
 
+// ---- dX over source-major segments (the expert-parallel backward on an expert
+// owner; num_sources = 1 equals the entry points above).  down_dx_src with
+// gate_up == NULL writes dh = dy W2 [S, I] without the SwiGLU backward.
+#define MIRAI_DX_SRC(SUF, WT, WRAP)                                                                            \
+  int mirai_moe_down_dx_src_##SUF(const void* grad_y, const int32_t* offsets, int32_t num_sources,          \
+                                  int32_t num_experts, int64_t num_rows, int32_t hidden, int32_t inter, WT w2, \
+                                  const void* gate_up, void* grad_gate_up, mirai_stream_t stream) {           \
+    return run<DXDOWN>("down_dx_src_" #SUF, grad_y, offsets, num_experts, num_rows, hidden, inter,            \
+                       grad_gate_up, const_cast<void*>(gate_up), WRAP(w2), WRAP(w2), hidden, inter, stream,   \
+                       nullptr, num_sources, gate_up == nullptr);                                              \
+  }                                                                                                            \
+  int mirai_moe_gateup_dx_src_##SUF(const void* grad_gate_up, const int32_t* offsets, int32_t num_sources,  \
+                                    int32_t num_experts, int64_t num_rows, int32_t inter, int32_t hidden,    \
+                                    WT w1, WT w3, void* dx_sorted, mirai_stream_t stream) {                    \
+    return run<DXGATEUP>("gateup_dx_src_" #SUF, grad_gate_up, offsets, num_experts, num_rows, 2 * inter,     \
+                         hidden, dx_sorted, nullptr, WRAP(w1), WRAP(w3), inter, hidden, stream, nullptr,     \
+                         num_sources);                                                                         \
+  }
+MIRAI_DX_SRC(bf16, const void*, wb)
+MIRAI_DX_SRC(nf4, const mirai_nf4_weight*, wn)
+MIRAI_DX_SRC(int8, const mirai_int8_weight*, wi)
+#undef MIRAI_DX_SRC
+
 // ---- LoRA on the down projection, fused as one extra k-block (a10).
 int mirai_moe_down_lora_bf16(const void* h, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
                              int32_t inter, int32_t hidden, const void* w2, const void* rank_a, const void* rank_b,

@@ -283,12 +283,12 @@ def gateup_swiglu(x_sorted: torch.Tensor, offsets: torch.Tensor, w1, w3, *, inte
     h = out if out is not None else torch.empty((S, inter), dtype=torch.bfloat16, device=x_sorted.device)
     gu = torch.empty((S, 2 * inter), dtype=torch.bfloat16, device=x_sorted.device) if save_gate_up else None
     if sources > 1:
-        if save_gate_up or offsets.numel() % sources:
-            raise ValueError("source-major segments: forward only, offsets a multiple of sources")
+        if offsets.numel() % sources:
+            raise ValueError("source-major segments: offsets must be a multiple of sources")
         E = offsets.numel() // sources
         _lib.call(f"mirai_moe_gateup_swiglu_src_{_fmt_suffix(w1)}", _ptr(x_sorted), _ptr(offsets), sources, E, S, H,
-                  inter, _wptr(w1), _wptr(w3), _ptr(h), None, _stream())
-        return h
+                  inter, _wptr(w1), _wptr(w3), _ptr(h), _ptr(gu), _stream())
+        return (h, gu) if save_gate_up else h
     E = offsets.numel()
     if isinstance(w1, torch.Tensor):
         w1 = _cuda(w1, "w1", torch.bfloat16)
@@ -456,16 +456,27 @@ def _wptr(w):
     return _ptr(_cuda(w, "weight", torch.bfloat16)) if isinstance(w, torch.Tensor) else w
 
 
-def down_dx(grad_y: torch.Tensor, offsets: torch.Tensor, w2, gate_up: torch.Tensor, *, inter: int,
+def down_dx(grad_y: torch.Tensor, offsets: torch.Tensor, w2, gate_up: torch.Tensor | None, *, inter: int,
             out: torch.Tensor | None = None, lora: DownLoRA | None = None,
-            rank_a: torch.Tensor | None = None) -> torch.Tensor:
+            rank_a: torch.Tensor | None = None, sources: int = 1) -> torch.Tensor:
     """grad_gate_up [S, 2I] = SwiGLU backward of (gate, up) given dh = grad_y W2
-    (+ the LoRA path's input gradient when ``lora``)."""
+    (+ the LoRA path's input gradient when ``lora``).  ``sources`` > 1:
+    source-major segments (an expert owner's rows); there ``gate_up=None``
+    returns dh [S, I] itself."""
     w2 = _as_weight(w2)
     gy = _cuda(grad_y, "grad_y", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
-    gu = _cuda(gate_up, "gate_up", torch.bfloat16)
     S, H = gy.shape
+    if sources > 1:
+        if lora is not None or offsets.numel() % sources:
+            raise ValueError("source-major segments: no adapter, offsets a multiple of sources")
+        gu = None if gate_up is None else _cuda(gate_up, "gate_up", torch.bfloat16)
+        width = inter if gu is None else 2 * inter
+        dgu = out if out is not None else torch.empty((S, width), dtype=torch.bfloat16, device=gy.device)
+        _lib.call(f"mirai_moe_down_dx_src_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), sources,
+                  offsets.numel() // sources, S, H, inter, _wptr(w2), _ptr(gu), _ptr(dgu), _stream())
+        return dgu
+    gu = _cuda(gate_up, "gate_up", torch.bfloat16)
     dgu = out if out is not None else torch.empty((S, 2 * inter), dtype=torch.bfloat16, device=gy.device)
     if lora is None:
         _lib.call(f"mirai_moe_down_dx_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), offsets.numel(), S, H, inter,
@@ -512,13 +523,20 @@ def lora_grad(x: torch.Tensor, g_rank: torch.Tensor, offsets: torch.Tensor, rank
 
 
 def gateup_dx(grad_gate_up: torch.Tensor, offsets: torch.Tensor, w1, w3, *, hidden: int,
-              out: torch.Tensor | None = None) -> torch.Tensor:
-    """dx_sorted [S, H] = dgate W1 + dup W3 per expert segment."""
+              out: torch.Tensor | None = None, sources: int = 1) -> torch.Tensor:
+    """dx_sorted [S, H] = dgate W1 + dup W3 per expert segment (``sources`` > 1:
+    source-major segments)."""
     w1, w3 = _as_weight(w1), _as_weight(w3)
     dgu = _cuda(grad_gate_up, "grad_gate_up", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
     S, I2 = dgu.shape
     dxs = out if out is not None else torch.empty((S, hidden), dtype=torch.bfloat16, device=dgu.device)
+    if sources > 1:
+        if offsets.numel() % sources:
+            raise ValueError("source-major segments: offsets must be a multiple of sources")
+        _lib.call(f"mirai_moe_gateup_dx_src_{_fmt_suffix(w1)}", _ptr(dgu), _ptr(offsets), sources,
+                  offsets.numel() // sources, S, I2 // 2, hidden, _wptr(w1), _wptr(w3), _ptr(dxs), _stream())
+        return dxs
     _lib.call(f"mirai_moe_gateup_dx_{_fmt_suffix(w1)}", _ptr(dgu), _ptr(offsets), offsets.numel(), S, I2 // 2,
               hidden, _wptr(w1), _wptr(w3), _ptr(dxs), _stream())
     return dxs
