@@ -448,6 +448,9 @@ def rotation_kernels(cfg, args, train):
 # per layer: route 1, plan 4, permute 1, local plan 4, local permute 1, gate/up 1, down 1,
 # un-permute 1, combine 1 (the NCCL all-to-alls are not counted)
 EP_KERNELS_PER_LAYER = 15
+# training adds: combine backward, down dX, gate/up dX, un-permute sum, the LoRA rank projections (2) and
+# factor gradients (2), and the owners' regrouping gathers (4)
+EP_TRAIN_EXTRA_KERNELS = 12
 
 
 def make_ep_workload(cfg, dev, rank, shard, tokens_local):
@@ -485,7 +488,8 @@ def run_ep(args, cfg, rank, world, dev):
     import torch
     import torch.distributed as dist
     from mirai_b200 import ops
-    from mirai_b200.expert_parallel import CudaStepOps, ExpertParallelMoE, ExpertShard, ep_moe_forward, shard_tokens
+    from mirai_b200.expert_parallel import (CudaStepOps, ExpertParallelMoE, ExpertShard, ep_moe_backward,
+                                            ep_moe_forward, shard_tokens)
 
     H, E, k, I = cfg["H"], cfg["E"], cfg["k"], cfg["I"]
     layers = cfg.get("layers", 1)
@@ -496,8 +500,18 @@ def run_ep(args, cfg, rank, world, dev):
     shard = ExpertShard(E, world, rank)
     x, logits0, stack = make_ep_workload(cfg, dev, rank, shard, T_r)
     stepops = CudaStepOps()
+    train = args.mode == "train"
+    if train and layers > 1:
+        raise SystemExit("--mode train runs single-layer workloads (c0-c3)")
+    gen = torch.Generator(device=dev).manual_seed(99 + rank)
+    g_out = torch.randn(T_r, cfg["H"], device=dev, generator=gen).to(torch.bfloat16) if train else None
+    lora = None
+    if train:  # the rank-16 LoRA on w2 of this rank's experts, as in the single-GPU step
+        la = torch.randn(shard.local, LORA_RANK, cfg["I"], device=dev, generator=gen) * (1.0 / cfg["I"] ** 0.5)
+        lb = torch.randn(shard.local, cfg["H"], LORA_RANK, device=dev, generator=gen) * 0.02
+        lora = ops.DownLoRA(la, lb, 16.0 / LORA_RANK, compute_grads=True)
     chunks = args.ep_chunks if world > 1 else 1
-    ipc = args.ep_transport == "ipc" and world > 1
+    ipc = args.ep_transport == "ipc" and world > 1 and not train  # training runs on the NCCL transport
     free_sms = args.ep_free_sms if args.ep_free_sms is not None else (2 if ipc else 16)
     if world > 1 and (chunks > 1 or ipc) and free_sms > 0:
         # leave SMs for the communication kernels (NCCL's all-to-all; with ipc only the
@@ -518,7 +532,17 @@ def run_ep(args, cfg, rank, world, dev):
         vf = v.float()
         return (vf * torch.rsqrt(vf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
 
-    def step(xin, l0, out=None):
+    def step(xin, l0, out=None, gin=None, dx_out=None):
+        if train:  # one layer: forward keeping the owners' gate/up, then the dX exchange and GEMMs
+            o, st = ep_moe_forward(xin, l0, stack[0][1], shard=shard, top_k=k, inter=I, ops=stepops, chunks=chunks,
+                                   train=True, lora=lora)
+            dx, _ = ep_moe_backward(g_out if gin is None else gin, st, stack[0][1], shard=shard, inter=I,
+                                    ops=stepops, lora=lora)
+            if out is not None:
+                out.copy_(o)
+            if dx_out is not None:
+                dx_out.copy_(dx)
+            return o
         h = xin
         for li, (gate, ws) in enumerate(stack):
             if layers == 1:
@@ -575,9 +599,10 @@ def run_ep(args, cfg, rank, world, dev):
     del xl, hl
 
     # ---- end to end with host buffers (each rank: its tokens and layer-0 logits up, its output down)
-    host_in = [x.cpu().pin_memory(), logits0.cpu().pin_memory()]
-    e2e_ms = measure_e2e(dev, host_in, 1, (T_r, H), lambda din, dout: step(din[0], din[1], out=dout[0]),
-                         args, barrier)
+    host_in = [x.cpu().pin_memory(), logits0.cpu().pin_memory()] + ([g_out.cpu().pin_memory()] if train else [])
+    e2e_ms = measure_e2e(dev, host_in, 2 if train else 1, (T_r, H),
+                         lambda din, dout: step(din[0], din[1], out=dout[0], gin=din[2] if train else None,
+                                                dx_out=dout[1] if train else None), args, barrier)
 
     if world > 1:
         t = torch.tensor([ms, e2e_ms], device=dev)
@@ -606,7 +631,8 @@ def run_ep(args, cfg, rank, world, dev):
         "config": {
             "workload": f"{args.config}: " + (f"a stack of {layers} routed expert FFN layers" if layers > 1 else
                                               "one routed expert FFN layer") +
-                        f" forward, expert-parallel over {world} GPU(s), T={T_total} tokens in total "
+                        (f" forward + dX backward with a rank-{LORA_RANK} LoRA on w2 (adapter grads included)"
+                         if train else " forward") + f", expert-parallel over {world} GPU(s), T={T_total} tokens in total "
                         f"({T_r} on rank 0), H={H} E={E} ({shard.local} per GPU) k={k} I={I} {cfg['fmt']} experts",
             "tokens_total": T_total, "hidden": H, "experts": E, "experts_per_gpu": shard.local, "top_k": k,
             "intermediate": I, "layers": layers, "weights": cfg["fmt"],
@@ -623,7 +649,7 @@ def run_ep(args, cfg, rank, world, dev):
                                       "next layer's routing and are not part of the routed expert FFN"}
                if layers > 1 else {}),
         },
-        "tflops": 6.0 * S_total * H * I * layers / (ms * 1e-3) / 1e12,
+        "tflops": (12.0 if train else 6.0) * S_total * H * I * layers / (ms * 1e-3) / 1e12,
         "roofline": {
             "kernel": f"gateup_swiglu_{cfg['fmt']}",
             "bound": "tensor",
@@ -639,11 +665,11 @@ def run_ep(args, cfg, rank, world, dev):
         "e2e": {
             "value": T_total / (e2e_ms * 1e-3),
             "unit": "tokens/s",
-            "h2d_bytes_per_step": T_r * H * 2 + T_r * E * 4,
-            "d2h_bytes_per_step": T_r * H * 2,
+            "h2d_bytes_per_step": T_r * H * 2 * (2 if train else 1) + T_r * E * 4,
+            "d2h_bytes_per_step": T_r * H * 2 * (2 if train else 1),
             "copies": "per rank: pinned host buffers; 2 slots, uploads and downloads on their own streams",
         },
-        "gpu_launches": EP_KERNELS_PER_LAYER * layers * args.steps,
+        "gpu_launches": (EP_KERNELS_PER_LAYER + (EP_TRAIN_EXTRA_KERNELS if train else 0)) * layers * args.steps,
         "gpu_launches_scope": "per rank",
         "clocks": clk,
     }
@@ -1071,9 +1097,9 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default=None, choices=["fwd", "train"],
-                    help="train (default for c0-c3 on one GPU: BASELINE config 2's step): forward + dX backward "
-                         "through the frozen experts with a rank-16 LoRA on w2; fwd: forward only (the default "
-                         "for the multi-GPU and c4 runs)")
+                    help="train (default for c0-c3, at every GPU count: BASELINE config 2's step): forward + dX "
+                         "backward through the frozen experts with a rank-16 LoRA on w2; fwd: forward only (the "
+                         "default for the c4 stack)")
     ap.add_argument("--int8-rotation", action="store_true",
                     help="c3: INT8 in the reference's default block-Hadamard format (groups of 256)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1104,10 +1130,10 @@ def main():
     cfg = CONFIGS[args.config] if args.tokens is None else dict(CONFIGS[args.config], T=int(args.tokens))
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.mode is None:
-        args.mode = "fwd" if (world > 1 or cfg.get("layers")) else "train"
-    if args.mode == "train" and (world > 1 or cfg.get("layers")):
-        raise SystemExit("--mode train runs the single-GPU layer (c0-c3 on one GPU)")
+    if args.mode is None:  # BASELINE config 2's step at every GPU count; the c4 stack runs forward
+        args.mode = "fwd" if cfg.get("layers") else "train"
+    if args.mode == "train" and cfg.get("layers"):
+        raise SystemExit("--mode train runs single-layer workloads (c0-c3)")
     if args.int8_rotation and cfg["fmt"] != "int8":
         raise SystemExit("--int8-rotation applies to the INT8 workload (c3)")
 

@@ -74,6 +74,13 @@ class StepOps(Protocol):
                 sources: int = 1) -> torch.Tensor: ...
     def combine(self, y_sorted: torch.Tensor, inverse_order: torch.Tensor, top_weights: torch.Tensor | None,
                 top_k: int, out_dtype: torch.dtype) -> torch.Tensor: ...
+    # training (the dX pass through frozen experts)
+    def experts_train(self, x_sorted: torch.Tensor, offsets: torch.Tensor, weights: Any, inter: int,
+                      sources: int = 1) -> tuple[torch.Tensor, Any]: ...
+    def experts_backward(self, grad_y: torch.Tensor, offsets: torch.Tensor, weights: Any, inter: int,
+                         sources: int, saved: Any) -> torch.Tensor: ...
+    def combine_backward(self, grad_out: torch.Tensor, y_sorted: torch.Tensor, inverse_order: torch.Tensor,
+                         top_weights: torch.Tensor, top_k: int) -> tuple[torch.Tensor, torch.Tensor]: ...
 
 
 class CudaStepOps:
@@ -93,21 +100,97 @@ class CudaStepOps:
         return self.ops.permute_rows(x, sorted_token_indices)
 
     def experts(self, x_sorted, offsets, weights, inter, sources=1):
+        return self.experts_train(x_sorted, offsets, weights, inter, sources, save=False)[0]
+
+    @staticmethod
+    def _regroup(offsets, sources, total):
+        """Expert-major order of ``total`` source-major rows, from the segment
+        ends on the device (no host read): (order, inverse, expert-major ends)."""
+        E = offsets.numel() // sources
+        ends = offsets.to(torch.int64)
+        L = (ends - torch.cat([ends.new_zeros(1), ends[:-1]])).view(sources, E)
+        order, inverse = regroup_order(L, total)
+        return order, inverse, torch.cumsum(L.sum(0), 0).to(torch.int32)
+
+    def experts_train(self, x_sorted, offsets, weights, inter, sources=1, save=True, lora=None):
+        """The owner's GEMMs; the block-Hadamard INT8 format rotates the received
+        rows and h here (a row's rotation does not depend on where it runs).
+        With a LoRA adapter on w2 (this rank's experts' factors) the received
+        rows are regrouped expert-major first, so the rank-block kernels see one
+        segment per expert; the rows, and so the products, are unchanged."""
+        if lora is not None and sources > 1:
+            order, inverse, ends = self._regroup(offsets, sources, x_sorted.shape[0])
+            y, saved = self.experts_train(self.ops.permute_rows(x_sorted, order), ends, weights, inter, 1, save,
+                                          lora)
+            return self.ops.permute_rows(y, inverse), ("regrouped", order, inverse, ends, saved)
         w1, w3, w2 = weights
-        h = self.ops.gateup_swiglu(x_sorted, offsets, w1, w3, inter=inter, sources=sources)
-        return self.ops.down(h, offsets, w2, hidden=x_sorted.shape[1], sources=sources)
+        g_in, g_mid = self.ops._rotations(w1, w3, w2)
+        x = self.ops.rotate_rows(x_sorted, g_in) if g_in else x_sorted
+        res = self.ops.gateup_swiglu(x, offsets, w1, w3, inter=inter, sources=sources, save_gate_up=save)
+        h, gu = res if save else (res, None)
+        low = self.ops.lora_project(h, offsets, lora, forward=True) if lora is not None else None
+        y = self.ops.down(self.ops.rotate_rows(h, g_mid) if g_mid else h, offsets, w2, hidden=x_sorted.shape[1],
+                          sources=sources, lora=lora, rank_a=low)
+        keep = lora is not None and lora.compute_grads
+        return y, (gu, h if keep else None, low if keep else None)
+
+    def experts_backward(self, grad_y, offsets, weights, inter, sources, saved, lora=None):
+        if isinstance(saved, tuple) and saved and isinstance(saved[0], str):
+            _, order, inverse, ends, inner = saved
+            dxs = self.experts_backward(self.ops.permute_rows(grad_y, order), ends, weights, inter, 1, inner, lora)
+            return self.ops.permute_rows(dxs, inverse)
+        gu, h, low = saved
+        w1, w3, w2 = weights
+        g_in, g_mid = self.ops._rotations(w1, w3, w2)
+        glow = None
+        if lora is not None:
+            glow = self.ops.lora_project(grad_y, offsets, lora, forward=False)
+            if lora.compute_grads:  # this chunk's share of the factor gradients, added up over chunks
+                E, Hb, r = lora.b.shape
+                Ia = lora.a.shape[2]
+                ga = self.ops.lora_grad(h, glow, offsets, r, torch.empty((E, r, Ia), dtype=torch.float32,
+                                                                         device=grad_y.device), (r * Ia, Ia, 1))
+                gb = self.ops.lora_grad(grad_y, low, offsets, r, torch.empty((E, Hb, r), dtype=torch.float32,
+                                                                             device=grad_y.device), (Hb * r, 1, r))
+                lora.grad_a = ga if lora.grad_a is None else lora.grad_a + ga
+                lora.grad_b = gb if lora.grad_b is None else lora.grad_b + gb
+        if g_mid:
+            dh = (self.ops.down_dx(grad_y, offsets, w2, None, inter=inter, sources=sources) if sources > 1
+                  else self.ops.down_dh(grad_y, offsets, w2, inter=inter, lora=lora, rank_a=glow))
+            dgu = self.ops.swiglu_backward_rotated(dh, gu, g_mid)
+        else:
+            dgu = self.ops.down_dx(grad_y, offsets, w2, gu, inter=inter, sources=sources, lora=lora, rank_a=glow)
+        dxs = self.ops.gateup_dx(dgu, offsets, w1, w3, hidden=grad_y.shape[1], sources=sources)
+        return self.ops.rotate_rows(dxs, g_in) if g_in else dxs
 
     def combine(self, y_sorted, inverse_order, top_weights, top_k, out_dtype):
         return self.ops.combine(y_sorted, inverse_order, top_weights, out_dtype=out_dtype, top_k=top_k)
+
+    def combine_backward(self, grad_out, y_sorted, inverse_order, top_weights, top_k):
+        return self.ops.combine_backward(grad_out, y_sorted, inverse_order, top_weights)
 
 
 def _a2a(out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int], group) -> None:
     dist.all_to_all_single(out, inp, out_splits, in_splits, group=group)
 
 
+@dataclass
+class EPTrainState:
+    """What ``ep_moe_backward`` needs from a training forward, per chunk: the
+    token-owner side (route weights, plan, the returned expert outputs, split
+    sizes) and the expert-owner side (segment ends, the saved gate/up of the
+    rows it received)."""
+
+    bounds: list            # [(begin, end)] token range of each chunk
+    chunks: list            # per chunk: dict(tw, plan, y_back, sc, rc, offs, saved)
+    top_k: int
+    hidden: int
+    dtype: torch.dtype
+
+
 def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: Any, *, shard: ExpertShard,
                    top_k: int, inter: int, group=None, ops: StepOps | None = None, chunks: int = 1,
-                   comm_stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+                   comm_stream: torch.cuda.Stream | None = None, train: bool = False, lora=None):
     """One expert-parallel routed FFN layer for this rank's tokens.
 
     tokens [T_r, H] bf16 and router logits [T_r, E] fp32 are this rank's token
@@ -121,7 +204,16 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
     current stream (chunk i's rows travel while chunk i-1 computes, and its
     results return while chunk i+1 computes).  The result is the same as with
     one chunk.  For the overlap to happen the GEMMs must leave SMs free for the
-    communication kernels (``ops.set_gemm_sm_limit``)."""
+    communication kernels (``ops.set_gemm_sm_limit``).
+
+    ``train=True`` returns ``(out, state)``: the owners keep the gate/up
+    pre-activations of the rows they received, the token owners the expert
+    outputs that came back, for ``ep_moe_backward`` (chunks then run one after
+    another, on the current stream).  ``lora`` (``ops.DownLoRA`` over this
+    rank's experts) adds a LoRA adapter on w2 (training only); its factor
+    gradients are this rank's experts' and come out of ``ep_moe_backward``."""
+    if lora is not None and not train:
+        raise ValueError("the expert-parallel forward takes a LoRA adapter in training (train=True)")
     ops = ops or CudaStepOps()
     G, E, El = shard.world, shard.num_experts, shard.local
     T, H = tokens.shape
@@ -130,8 +222,13 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
         idx, tw = ops.route(logits, top_k)
         plan = ops.plan(idx, E)
         xs = ops.permute(tokens, plan.sorted_token_indices)
-        y = ops.experts(xs, plan.offsets, local_weights, inter)
-        return ops.combine(y, plan.inverse_order, tw, top_k, tokens.dtype)
+        if not train:
+            y = ops.experts(xs, plan.offsets, local_weights, inter)
+            return ops.combine(y, plan.inverse_order, tw, top_k, tokens.dtype)
+        y, saved = ops.experts_train(xs, plan.offsets, local_weights, inter, **({"lora": lora} if lora else {}))
+        out = ops.combine(y, plan.inverse_order, tw, top_k, tokens.dtype)
+        return out, EPTrainState([(0, T)], [dict(tw=tw, plan=plan, y_back=y, sc=None, rc=None, offs=plan.offsets,
+                                                 saved=saved)], top_k, H, tokens.dtype)
     C = max(1, int(chunks))
     bounds = [((T * c) // C, (T * (c + 1)) // C) for c in range(C)]
     # ---- per chunk, on the current stream: route, plan, permute
@@ -171,7 +268,7 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
         torch.tensor(seg_ends, dtype=torch.int32)
 
     comp = torch.cuda.current_stream(dev) if tokens.is_cuda else None
-    comm = comm_stream if (C > 1 and tokens.is_cuda) else None
+    comm = comm_stream if (C > 1 and tokens.is_cuda and not train) else None
 
     def keep(t, stream):
         # a tensor used on a stream other than its own is not reused before that stream is done with it
@@ -210,6 +307,21 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
         return y_back
 
     out = torch.empty((T, H), dtype=tokens.dtype, device=dev)
+    if train:
+        state = []
+        for c, (b, e) in enumerate(bounds):
+            x_recv = dispatch(c)
+            if x_recv.shape[0]:
+                y_recv, saved = ops.experts_train(x_recv, offs_dev[c], local_weights, inter, sources=G,
+                                                  **({"lora": lora} if lora else {}))
+            else:
+                y_recv, saved = torch.empty((0, H), dtype=x_recv.dtype, device=dev), None
+            y_back = give_back(c, y_recv)
+            if e > b:
+                out[b:e] = ops.combine(y_back, prep[c][1].inverse_order, prep[c][0], top_k, tokens.dtype)
+            state.append(dict(tw=prep[c][0], plan=prep[c][1], y_back=y_back, sc=sc[c], rc=rc[c], offs=offs_dev[c],
+                              saved=saved))
+        return out, EPTrainState(bounds, state, top_k, H, tokens.dtype)
     if comm is None:
         for c, (b, e) in enumerate(bounds):
             y_back = give_back(c, compute(c, dispatch(c)))
@@ -231,6 +343,53 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
         if e > b:
             out[b:e] = ops.combine(y_back, prep[c][1].inverse_order, prep[c][0], top_k, tokens.dtype)
     return out
+
+
+def ep_moe_backward(grad_out: torch.Tensor, state: EPTrainState, local_weights: Any, *, shard: ExpertShard,
+                    inter: int, group=None, ops: StepOps | None = None, lora=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """dX of ``ep_moe_forward(train=True)`` through the frozen experts:
+    grad_out [T_r, H] -> (dx [T_r, H] in the tokens' dtype, d_top_weights fp32
+    [T_r, k]).  Collective, like the forward (every rank calls it).
+
+    Per chunk, mirroring the forward: the combine backward on the token owner
+    (linear.py's frozen-linear backward inputs, dispatch_ops.py:36-44); the
+    gradient rows travel to the expert owners with the forward's split sizes;
+    the owner's down dX (SwiGLU backward fused, on the gate/up it kept) and
+    gate/up dX run over the same source-major segments; dX rows travel back
+    and the token owner sums each token's routes (the permute backward,
+    dispatch_ops.py:15-20).  Every row's products are those of the single-GPU
+    backward, so the result equals it."""
+    ops = ops or CudaStepOps()
+    G = shard.world
+    k, H = state.top_k, state.hidden
+    kw = {"lora": lora} if lora is not None else {}
+    if lora is not None and lora.compute_grads:
+        lora.grad_a = lora.grad_b = None  # summed over this call's chunks
+    T = grad_out.shape[0]
+    dev = grad_out.device
+    dx = torch.empty((T, H), dtype=state.dtype, device=dev)
+    dw = torch.empty((T, k), dtype=torch.float32, device=dev)
+    for (b, e), st in zip(state.bounds, state.chunks):
+        plan = st["plan"]
+        if e > b:
+            gy, gw = ops.combine_backward(grad_out[b:e], st["y_back"], plan.inverse_order, st["tw"], k)
+            dw[b:e] = gw
+        else:  # no tokens here: an empty block of the gradient rows' dtype (the collectives need one dtype)
+            gy = torch.empty((0, H), dtype=st["y_back"].dtype, device=dev)
+        if G == 1:
+            dxs = ops.experts_backward(gy, st["offs"], local_weights, inter, 1, st["saved"], **kw)
+        else:
+            gy_recv = torch.empty((sum(st["rc"]), H), dtype=gy.dtype, device=dev)
+            _a2a(gy_recv, gy.contiguous(), st["rc"], st["sc"], group)
+            if gy_recv.shape[0]:
+                dx_recv = ops.experts_backward(gy_recv, st["offs"], local_weights, inter, G, st["saved"], **kw)
+            else:
+                dx_recv = torch.empty((0, H), dtype=gy.dtype, device=dev)
+            dxs = torch.empty((sum(st["sc"]), H), dtype=dx_recv.dtype, device=dev)
+            _a2a(dxs, dx_recv.contiguous(), st["sc"], st["rc"], group)
+        if e > b:
+            dx[b:e] = ops.combine(dxs, plan.inverse_order, None, k, state.dtype)
+    return dx, dw
 
 
 def check_counts(M, rank: int, sent_rows: list[int]) -> None:

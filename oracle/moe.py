@@ -191,6 +191,34 @@ def silu_backward_f32(grad: np.ndarray, x: np.ndarray) -> np.ndarray:
     return (grad * sig * (np.float32(1.0) + x * (np.float32(1.0) - sig))).astype(np.float32)
 
 
+def expert_ffn_backward(grad_y: np.ndarray, offsets: np.ndarray, w1, w3, w2, inter: dict, *, bf16: bool = True,
+                        lora: dict | None = None) -> np.ndarray:
+    """Per-expert input gradient of the SwiGLU MLP over expert-contiguous rows
+    (linear.py:116-125, 191-203 and autograd of experts.py:301-317), given the
+    forward's ``gate`` / ``up`` intermediates (``expert_ffn_forward(keep=True)``)."""
+    E = w1.shape[0]
+    dxs = np.zeros((grad_y.shape[0], w1.shape[2]), dtype=np.float32)
+    start = 0
+    for e in range(E):
+        end = int(offsets[e])
+        if end > start:
+            gy = grad_y[start:end]
+            gate = inter["gate"][start:end]
+            up = inter["up"][start:end]
+            dh = _r(gy @ w2[e], bf16)
+            if lora is not None:
+                dlow_out = _r(gy * np.float32(lora["scale"]), bf16)
+                dlow = _r(dlow_out @ lora["b"][e], bf16)
+                dh = _r(dh + _r(dlow @ lora["a"][e], bf16), bf16)
+            act = _r(silu_f32(gate), bf16)
+            d_act = _r(dh * up, bf16)
+            d_up = _r(dh * act, bf16)
+            d_gate = _r(silu_backward_f32(d_act, gate), bf16)
+            dxs[start:end] = _r(_r(d_gate @ w1[e], bf16) + _r(d_up @ w3[e], bf16), bf16)
+        start = end
+    return dxs
+
+
 def moe_backward_dx(x: np.ndarray, top_idx: np.ndarray, top_w: np.ndarray, w1, w3, w2,
                     grad_out: np.ndarray, *, bf16: bool = True, lora: dict | None = None):
     """Input gradient through frozen experts (linear.py:116-125, 191-203;
@@ -208,25 +236,7 @@ def moe_backward_dx(x: np.ndarray, top_idx: np.ndarray, top_w: np.ndarray, w1, w
     grad_w_sorted = (g * y).sum(axis=1, dtype=np.float32)
     grad_w = np.zeros(T * k, dtype=np.float32)
     grad_w[sp] = grad_w_sorted
-    dxs = np.zeros_like(xs, dtype=np.float32)
-    start = 0
-    for e in range(E):
-        end = int(plan["offsets"][e])
-        if end > start:
-            gy = grad_y[start:end]
-            gate = inter["gate"][start:end]
-            up = inter["up"][start:end]
-            dh = _r(gy @ w2[e], bf16)
-            if lora is not None:
-                dlow_out = _r(gy * np.float32(lora["scale"]), bf16)
-                dlow = _r(dlow_out @ lora["b"][e], bf16)
-                dh = _r(dh + _r(dlow @ lora["a"][e], bf16), bf16)
-            act = _r(silu_f32(gate), bf16)
-            d_act = _r(dh * up, bf16)
-            d_up = _r(dh * act, bf16)
-            d_gate = _r(silu_backward_f32(d_act, gate), bf16)
-            dxs[start:end] = _r(_r(d_gate @ w1[e], bf16) + _r(d_up @ w3[e], bf16), bf16)
-        start = end
+    dxs = expert_ffn_backward(grad_y, plan["offsets"], w1, w3, w2, inter, bf16=bf16, lora=lora)
     dx = np.zeros((T, x.shape[1]), dtype=np.float32)
     if bf16:
         # permute backward accumulates in the activation dtype, sequentially in

@@ -52,6 +52,43 @@ class OracleStepOps:
         out[perm] = y
         return torch.from_numpy(out)
 
+    def _by_expert(self, offsets, sources):
+        ends = offsets.numpy().astype(np.int64)
+        E = ends.size // sources
+        starts = np.concatenate([[0], ends[:-1]])
+        order = [np.arange(starts[s_ * E + e], ends[s_ * E + e]) for e in range(E) for s_ in range(sources)]
+        perm = np.concatenate(order) if order else np.zeros(0, np.int64)
+        per_expert = np.cumsum([sum(ends[s_ * E + e] - starts[s_ * E + e] for s_ in range(sources))
+                                for e in range(E)])
+        return perm, per_expert
+
+    def experts_train(self, x_sorted, offsets, weights, inter, sources=1):
+        perm, per_expert = self._by_expert(offsets, sources)
+        y, mids = om.expert_ffn_forward(x_sorted.numpy()[perm], per_expert, *weights, bf16=True, keep=True)
+        out = np.empty_like(y)
+        out[perm] = y
+        return torch.from_numpy(out), (perm, per_expert, mids)
+
+    def experts_backward(self, grad_y, offsets, weights, inter, sources, saved):
+        perm, per_expert, mids = saved
+        dxs = om.expert_ffn_backward(grad_y.numpy()[perm], per_expert, *weights, mids, bf16=True)
+        out = np.empty_like(dxs)
+        out[perm] = dxs
+        return torch.from_numpy(out)
+
+    def combine_backward(self, grad_out, y_sorted, inverse_order, top_weights, top_k):
+        """dispatch_ops.py:36-44 for bf16 tensors: grad_y = bf16(g * w), grad_w = <g, y> (fp32)."""
+        g, y = grad_out.numpy(), y_sorted.numpy()
+        inv = inverse_order.numpy().reshape(-1, top_k)
+        w = top_weights.numpy()
+        gy = np.zeros_like(y)
+        gw = np.zeros(w.shape, np.float32)
+        for t in range(inv.shape[0]):
+            for j in range(top_k):
+                gy[inv[t, j]] = oq.bf16_round(g[t] * w[t, j])
+                gw[t, j] = np.dot(g[t].astype(np.float64), y[inv[t, j]].astype(np.float64))
+        return torch.from_numpy(gy), torch.from_numpy(gw)
+
     def combine(self, y_sorted, inverse_order, top_weights, top_k, out_dtype):
         y = y_sorted.numpy()
         inv = inverse_order.numpy().reshape(-1, top_k)
@@ -305,3 +342,63 @@ def test_check_counts():
         check_counts(bad, 1, [8, 8, 8])
     with pytest.raises(ValueError, match="chunk 2"):
         check_counts(M, 1, [8, 8, 7])
+
+
+def _bwd_rank_main(rank, world, port, cfg, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from mirai_b200.expert_parallel import ExpertShard, ep_moe_backward, ep_moe_forward, shard_tokens
+        T, H, E, k, I, seed, token_split, chunks = cfg
+        x, logits, ws = _problem(T, H, E, k, I, seed)
+        g = oq.bf16_round(np.random.default_rng(seed + 100).standard_normal((T, H)).astype(np.float32))
+        shard = ExpertShard(E, world, rank)
+        b, e = token_split[rank] if token_split else shard_tokens(T, world, rank)
+        local = tuple(w[shard.first:shard.first + shard.local] for w in ws)
+        ops = OracleStepOps()
+        out, st = ep_moe_forward(torch.from_numpy(x[b:e]), torch.from_numpy(logits[b:e]), local, shard=shard,
+                                 top_k=k, inter=I, ops=ops, chunks=chunks, train=True)
+        dx, dw = ep_moe_backward(torch.from_numpy(g[b:e]), st, local, shard=shard, inter=I, ops=ops)
+        results[rank] = (b, e, out.numpy(), dx.numpy(), dw.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_bwd(world, cfg):
+    with mp.get_context("spawn").Manager() as mgr:
+        results = mgr.dict()
+        mp.start_processes(_bwd_rank_main, args=(world, _free_port(), cfg, results), nprocs=world,
+                           start_method="spawn")
+        return dict(results)
+
+
+@pytest.mark.parametrize("world,cfg", [
+    (2, (96, 64, 8, 2, 128, 3, None, 1)),
+    (4, (150, 64, 8, 3, 64, 5, None, 2)),
+    (2, (80, 32, 4, 2, 64, 7, [(0, 0), (0, 80)], 1)),  # rank 0 has no tokens
+])
+def test_expert_parallel_backward_equals_one_rank(world, cfg):
+    """dX through the frozen experts across ranks (training forward keeps the
+    owners' gate/up; gradient rows travel to the owners and dX rows back):
+    the concatenated dX and route-weight gradients of world ranks equal the
+    world-1 run of the same steps exactly, and the oracle's single-process
+    backward within the bf16 tolerance (its un-permute sum rounds to bf16 after
+    every route, as the reference's bf16 index_add does)."""
+    res = _run_bwd(world, cfg)
+    one = _run_bwd(1, cfg[:6] + (None, 1))
+    T, H, E, k, I, seed = cfg[:6]
+    dx = np.zeros((T, H), np.float32)
+    dw = np.zeros((T, k), np.float32)
+    out = np.zeros((T, H), np.float32)
+    for r in range(world):
+        b, e, o, d, w = res[r]
+        out[b:e], dx[b:e], dw[b:e] = o, d, w
+    np.testing.assert_array_equal(out, one[0][2])
+    np.testing.assert_array_equal(dx, one[0][3])
+    np.testing.assert_array_equal(dw, one[0][4])
+    x, logits, ws = _problem(T, H, E, k, I, seed)
+    g = oq.bf16_round(np.random.default_rng(seed + 100).standard_normal((T, H)).astype(np.float32))
+    ridx, rw = om.route_topk(logits, k)
+    rdx, rdw = om.moe_backward_dx(x, ridx, rw, *ws, g, bf16=True)
+    assert om.rel_max_err(dx, rdx) < 2e-2
+    assert om.rel_max_err(dw, rdw) < 1e-5

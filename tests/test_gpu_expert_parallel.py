@@ -124,3 +124,83 @@ def test_expert_parallel_equals_single_gpu_layer(fmt, chunks, transport, copy_st
         code, equal, maxdiff = res[r]
         assert code == 0
         assert equal, f"rank {r}: max |diff| {maxdiff}"
+
+
+def _train_rank_main(rank, world, port, cfg, results):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        from mirai_b200 import ops
+        from mirai_b200.expert_parallel import ExpertShard, ep_moe_backward, ep_moe_forward, shard_tokens
+        T, H, E, k, I, fmt, chunks, rotated, lora_rank = cfg
+        g = torch.Generator(device=dev).manual_seed(13)
+        x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+        logits = torch.randn(T, E, generator=g, device=dev) * 1.5
+        gout = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+        raw = _weights(fmt, E, H, I, 5, dev)
+
+        def quant(w, key_in):
+            if fmt == "int8" and rotated:
+                return ops.int8_quantize(w.float(), group_size=64 if key_in % 64 == 0 else 16)
+            return _quant(fmt, w, dev)
+
+        shard = ExpertShard(E, world, rank)
+        lo, hi = shard.first, shard.first + shard.local
+        local = tuple(quant(w[lo:hi].contiguous(), w.shape[2]) for w in raw)
+        full = tuple(quant(w, w.shape[2]) for w in raw)
+        b, e = shard_tokens(T, world, rank)
+        lora = lora_full = None
+        if lora_rank:
+            la = torch.randn(E, lora_rank, I, generator=g, device=dev) * 0.05
+            lb = torch.randn(E, H, lora_rank, generator=g, device=dev) * 0.05
+            lora = ops.DownLoRA(la[lo:hi], lb[lo:hi], 2.0, compute_grads=True)
+            lora_full = ops.DownLoRA(la, lb, 2.0, compute_grads=True)
+        out, st = ep_moe_forward(x[b:e].contiguous(), logits[b:e].contiguous(), local, shard=shard, top_k=k,
+                                 inter=I, chunks=chunks, train=True, lora=lora)
+        dx, dw = ep_moe_backward(gout[b:e].contiguous(), st, local, shard=shard, inter=I, lora=lora)
+        code, info = ops.device_status()
+        idx, tw = ops.route_topk(logits, k)
+        ref, rst = ops.moe_forward_train(x, idx, tw, *full, num_experts=E, inter=I, lora=lora_full)
+        rdx, rdw = ops.moe_backward_dx(gout, rst, *full, inter=I, lora=lora_full)
+        same = bool(torch.equal(out, ref[b:e])) and bool(torch.equal(dw, rdw[b:e]))
+        if lora_rank:  # this rank's experts' factor gradients (partial sums per chunk: the bf16 tolerance)
+            for got, want in ((lora.grad_a, lora_full.grad_a[lo:hi]), (lora.grad_b, lora_full.grad_b[lo:hi])):
+                same = same and float((got - want).abs().max() / want.abs().max()) < 1e-3
+        dx_exact = bool(torch.equal(dx, rdx[b:e]))
+        rel = float((dx.float() - rdx[b:e].float()).abs().max() / rdx.float().abs().max())
+        results[rank] = (code, same, dx_exact, rel)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fmt,chunks,world,rotated,lora_rank", [
+    ("nf4", 1, 2, False, 0), ("bf16", 2, 2, False, 0), ("int8", 1, 2, False, 0), ("int8", 2, 2, True, 0),
+    ("nf4", 2, 2, False, 16), ("nf4", 2, 4, False, 16),
+])
+def test_expert_parallel_backward_equals_single_gpu(fmt, chunks, world, rotated, lora_rank):
+    """Training through the expert-parallel layer (NCCL transport): the
+    forward output and the route-weight gradients equal the single-GPU
+    layer's exactly, and so does dX (the rows' products and each token's
+    ascending-position sum are the single-GPU ones); the block-Hadamard INT8
+    format rotates dX rows on the owners before the route sum, so there dX is
+    held to the bf16 tolerance instead.  With a rank-16 LoRA on w2 the owners
+    regroup their rows expert-major; the adapter's factor gradients of each
+    rank's experts match the single-GPU ones (summed per chunk)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from mirai_b200.build import build
+    build()
+    cfg = (2000, 256, 8, 2, 384, fmt, chunks, rotated, lora_rank)
+    with mp.Manager() as mgr:
+        results = mgr.dict()
+        mp.start_processes(_train_rank_main, args=(world, _free_port(), cfg, results), nprocs=world,
+                           start_method="spawn")
+        res = dict(results)
+    for r in range(world):
+        code, same, dx_exact, rel = res[r]
+        assert code == 0 and same
+        assert dx_exact or (rotated and rel < 3e-2), f"rank {r}: dx rel err {rel}"
