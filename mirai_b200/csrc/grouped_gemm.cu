@@ -193,6 +193,16 @@ struct alignas(16) DeqSmem {
   float code[2][16];
 };
 
+// Staged epilogue (NF4 / INT8): each epilogue warp writes 32 rows x 32 bf16
+// columns of an output into one of STG_BUFS shared-memory boxes (64-byte TMA
+// swizzle) and a TMA store writes the box to global memory, instead of every
+// lane storing its own row (32 cache lines per warp store, whose wavefronts
+// share the shared-memory port with the dequantisers).
+constexpr int STG_BUFS = 3;
+constexpr uint32_t STG_BOX = 32 * 64;  // bytes: 32 rows x 32 bf16
+// (CTA pairs only: the single-CTA variants, kept for A/B measurement, have no room left)
+template <int WF, bool PAIR> __host__ __device__ constexpr bool staged_epilogue() { return WF != W_BF16 && PAIR; }
+
 template <int WF, bool PAIR>
 constexpr size_t smem_bytes() {
   using C = Cfg<WF, PAIR>;
@@ -200,7 +210,8 @@ constexpr size_t smem_bytes() {
                 "the dequantiser scratch must start 16-byte aligned");
   return 1024 + C::STAGES * (C::A_STAGE + C::B_BYTES) + (WF == W_BF16 ? 0 : C::RAW_STAGES * C::RAW_BYTES) +
          sizeof(Smem<WF, PAIR>) +
-         (WF == W_BF16 ? 0 : sizeof(DeqSmem));
+         (WF == W_BF16 ? 0 : sizeof(DeqSmem)) +
+         (staged_epilogue<WF, PAIR>() ? 1024 + (size_t)C::EPI_WARPS * STG_BUFS * STG_BOX : 0);
 }
 
 // Tile t -> segment j (in tile order), weight expert e, row block m, column
@@ -355,7 +366,9 @@ template <int MODE, int WF, bool PAIR, bool BMN>
 __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b0,
                         const __grid_constant__ CUtensorMap tmap_b1, const __grid_constant__ CUtensorMap tmap_xa,
-                        const __grid_constant__ CUtensorMap tmap_xb, const Params p) {
+                        const __grid_constant__ CUtensorMap tmap_xb, const __grid_constant__ CUtensorMap tmap_o0,
+                        const __grid_constant__ CUtensorMap tmap_o1, const __grid_constant__ CUtensorMap tmap_o2,
+                        const Params p) {
   using C = Cfg<WF, PAIR>;
   constexpr int STAGES = C::STAGES;
   constexpr uint32_t B_BYTES = C::B_BYTES;
@@ -387,6 +400,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
   constexpr int RAW_STAGES = C::RAW_STAGES;
   Smem<WF, PAIR>& sm = *reinterpret_cast<Smem<WF, PAIR>*>(sRaw + (QUANT ? RAW_STAGES * RAW_BYTES : 0));
   DeqSmem* dq = reinterpret_cast<DeqSmem*>(reinterpret_cast<uint8_t*>(&sm) + sizeof(Smem<WF, PAIR>));
+  constexpr bool STAGED = staged_epilogue<WF, PAIR>();
+  // staging boxes of the epilogue warps (1024-byte aligned: the swizzle pattern repeats every 512 bytes)
+  uint8_t* sStage = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(dq) + (QUANT ? sizeof(DeqSmem) : 0) + 1023) & ~uintptr_t(1023));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -671,6 +688,26 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     constexpr int NSPLIT = C::EPI_WARPS / 4;
     const int part = (warp - C::EPI_FIRST) / 4;
     const uint32_t tempty_leader[2] = {leader_addr(&sm.tempty[0]), leader_addr(&sm.tempty[1])};
+    int stg = 0;  // the next staging box of this warp
+    // Write one 32 x 32 bf16 block (this lane's row: 16 packed words) through a
+    // staging box to `map` at (col, row0): the whole warp, rows row0..row0+31 all valid.
+    auto stage_store = [&](const CUtensorMap* map, int col, int64_t row0, const uint32_t (&w)[16]) {
+      uint8_t* box = sStage + ((warp - C::EPI_FIRST) * STG_BUFS + stg) * STG_BOX;
+      if (lane == 0) bulk_wait_group_read<STG_BUFS - 1>();  // the box's previous store has read it
+      __syncwarp();
+      const uint32_t rowaddr = smem_u32(box) + (uint32_t)lane * 64u;
+      const uint32_t sw = (uint32_t)(lane >> 1) & 3u;  // 64-byte swizzle: 16-byte chunk ^= row bits 1..2
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        st_shared_v4(rowaddr + (((uint32_t)v ^ sw) << 4), w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(map, box, col, (int)row0);
+        bulk_commit_group();
+      }
+      stg = stg + 1 == STG_BUFS ? 0 : stg + 1;
+    };
     int it = 0;
     for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++it) {
       const int acc = it & 1;
@@ -693,6 +730,9 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       const bool valid = p.nsrc > 1 ? lr < blk_rows : (int64_t)m * TILE_M + r < seg_rows;
       const int64_t grow = p.nsrc > 1 ? (int64_t)blk_row + lr : (int64_t)sm.row_start[j] + (int64_t)m * TILE_M + r;
       const uint32_t tb = tmem_base + acc * BN + sub * TN + ((uint32_t)(q * 32) << 16);
+      // all 32 rows of this warp belong to the segment: stores go through TMA boxes
+      const bool boxed = STAGED && __all_sync(0xffffffffu, valid);
+      const int64_t row0 = __shfl_sync(0xffffffffu, grow, 0);
       if (MODE == GATEUP) {
         const int col0 = n * (TN / 2);
         constexpr int NCH = TN / 64;  // 32-column chunks of gate (and of up)
@@ -720,6 +760,14 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
               }
               gp[j] = pack_bf16x2(g0, g1);
               up[j] = pack_bf16x2(u0, u1);
+            }
+            if (boxed) {
+              stage_store(&tmap_o0, col0 + c * 32, row0, hp);
+              if (p.gate_up != nullptr) {
+                stage_store(&tmap_o1, col0 + c * 32, row0, gp);
+                stage_store(&tmap_o2, col0 + c * 32, row0, up);
+              }
+              continue;
             }
             uint4* dst = reinterpret_cast<uint4*>(p.out + grow * p.ldo + col0 + c * 32);
 #pragma unroll
@@ -779,6 +827,11 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
               dg[j] = pack_bf16x2(dgo[0], dgo[1]);
               du[j] = pack_bf16x2(duo[0], duo[1]);
             }
+            if (boxed) {
+              stage_store(&tmap_o0, col, row0, dg);  // the gate half of dgu
+              stage_store(&tmap_o1, col, row0, du);  // the up half
+              continue;
+            }
             uint4* gd = reinterpret_cast<uint4*>(p.out + grow * ld2 + col);
             uint4* ud = reinterpret_cast<uint4*>(p.out + grow * ld2 + p.N + col);
 #pragma unroll
@@ -800,6 +853,10 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
             uint32_t yp[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) yp[j] = pack_bf16x2(__uint_as_float(v32[2 * j]), __uint_as_float(v32[2 * j + 1]));
+            if (boxed) {
+              stage_store(&tmap_o0, col0 + c * 32, row0, yp);
+              continue;
+            }
             uint4* dst = reinterpret_cast<uint4*>(p.out + grow * p.ldo + col0 + c * 32);
 #pragma unroll
             for (int v = 0; v < 4; ++v) dst[v] = make_uint4(yp[4 * v], yp[4 * v + 1], yp[4 * v + 2], yp[4 * v + 3]);
@@ -814,6 +871,9 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         else mbar_arrive(&sm.tempty[acc]);
       }
     }
+    // this warp's TMA stores have written global memory (and read their boxes) before the CTA exits
+    if (STAGED && lane == 0) bulk_wait_group_all();
+    __syncwarp();
   };
   auto role_raw = [&]() {
     // ======================= raw-code producer (NF4 / INT8) =======================
@@ -1156,7 +1216,7 @@ static bool use_pairs() {
 
 template <int MODE, int WF, bool PAIR, bool BMN>
 int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const CUtensorMap& txa,
-                const CUtensorMap& txb, const Params& p,
+                const CUtensorMap& txb, const CUtensorMap* to, const Params& p,
                 cudaStream_t stream) {
   using C = Cfg<WF, PAIR>;
   auto kern = grouped_gemm_kernel<MODE, WF, PAIR, BMN>;
@@ -1185,7 +1245,7 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
   const int sms = (limit > 0 && limit < sm_count()) ? limit : sm_count();
   if (!PAIR) {
     const int grid = (int)(max_tiles < sms ? max_tiles : sms);
-    kern<<<grid, C::THREADS, smem, stream>>>(ta, tb0, tb1, txa, txb, q);
+    kern<<<grid, C::THREADS, smem, stream>>>(ta, tb0, tb1, txa, txb, to[0], to[1], to[2], q);
     return check_launch(names[MODE]);
   }
   cudaLaunchConfig_t cfg = {};
@@ -1216,7 +1276,7 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
   int64_t units = max_tiles < resident_pairs ? max_tiles : resident_pairs;
   if (units > sms / 2) units = sms / 2;  // the SM limit, in pairs
   cfg.gridDim = dim3((unsigned)(2 * units), 1, 1);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb0, tb1, txa, txb, q);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb0, tb1, txa, txb, to[0], to[1], to[2], q);
   if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "%s: launch failed: %s", names[MODE], cudaGetErrorString(e));
   return check_launch(names[MODE]);
 }
@@ -1226,18 +1286,18 @@ int launch_impl(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap
 // layout ([E, in, out]) reads the other way round, for bf16 and NF4, on pairs.
 template <int MODE, int WF, bool BMN>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1, const CUtensorMap& txa,
-           const CUtensorMap& txb, const Params& p,
+           const CUtensorMap& txb, const CUtensorMap* to, const Params& p,
            cudaStream_t stream) {
   if constexpr (BMN == MCfg<MODE>::MN_NATIVE) {
-    return use_pairs() ? launch_impl<MODE, WF, true, BMN>(ta, tb0, tb1, txa, txb, p, stream)
-                       : launch_impl<MODE, WF, false, BMN>(ta, tb0, tb1, txa, txb, p, stream);
+    return use_pairs() ? launch_impl<MODE, WF, true, BMN>(ta, tb0, tb1, txa, txb, to, p, stream)
+                       : launch_impl<MODE, WF, false, BMN>(ta, tb0, tb1, txa, txb, to, p, stream);
   } else if constexpr (WF == W_INT8) {
     return set_error(MIRAI_ERR_UNSUPPORTED, "INT8 experts are read in the [E, out, in] layout only");
   } else {
     if (!use_pairs())
       return set_error(MIRAI_ERR_UNSUPPORTED, "the [E, in, out] weight layout runs on CTA pairs "
                        "(MIRAI_B200_CTA_PAIR=0 is set)");
-    return launch_impl<MODE, WF, true, BMN>(ta, tb0, tb1, txa, txb, p, stream);
+    return launch_impl<MODE, WF, true, BMN>(ta, tb0, tb1, txa, txb, to, p, stream);
   }
 }
 
@@ -1403,18 +1463,43 @@ int run_groups(const char* name, const void* a, const int32_t* offsets, int E, i
     txa = ta;
     txb = t0;
   }
+  // output maps of the staged epilogue (32 x 32 bf16 boxes, 64-byte swizzle); a map that
+  // a mode does not store through is a copy of another (never used)
+  CUtensorMap to[3];
+  if (w0.fmt != W_BF16) {
+    const bool dgu = MODE == DXDOWN && p.gate_up != nullptr;  // [S, 2N]: gate half, then up half
+    const uint64_t ld = dgu ? 2 * (uint64_t)N : (uint64_t)N;
+    char* o = static_cast<char*>(out);
+    rc = make_tmap_2d(&to[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, o, (uint64_t)N, (uint64_t)S, ld * 2, 32, 32,
+                      CU_TENSOR_MAP_SWIZZLE_64B);
+    if (!rc)
+      rc = dgu ? make_tmap_2d(&to[1], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, o + (size_t)N * 2, (uint64_t)N,
+                              (uint64_t)S, ld * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+         : (MODE == GATEUP && gate_up)
+             ? make_tmap_2d(&to[1], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gate_up, (uint64_t)N, (uint64_t)S,
+                            4 * (uint64_t)N, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+             : (to[1] = to[0], MIRAI_OK);
+    if (!rc)
+      rc = (MODE == GATEUP && gate_up)
+               ? make_tmap_2d(&to[2], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<char*>(gate_up) + (size_t)N * 2,
+                              (uint64_t)N, (uint64_t)S, 4 * (uint64_t)N, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+               : (to[2] = to[0], MIRAI_OK);
+    if (rc) return rc;
+  } else {
+    to[0] = to[1] = to[2] = ta;
+  }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   constexpr bool NAT = MCfg<MODE>::MN_NATIVE;
   switch (w0.fmt) {
     case W_BF16:
-      return mn == NAT ? launch<MODE, W_BF16, NAT>(ta, t0, t1, txa, txb, p, st)
-                       : launch<MODE, W_BF16, !NAT>(ta, t0, t1, txa, txb, p, st);
+      return mn == NAT ? launch<MODE, W_BF16, NAT>(ta, t0, t1, txa, txb, to, p, st)
+                       : launch<MODE, W_BF16, !NAT>(ta, t0, t1, txa, txb, to, p, st);
     case W_NF4:
-      return mn == NAT ? launch<MODE, W_NF4, NAT>(ta, t0, t1, txa, txb, p, st)
-                       : launch<MODE, W_NF4, !NAT>(ta, t0, t1, txa, txb, p, st);
+      return mn == NAT ? launch<MODE, W_NF4, NAT>(ta, t0, t1, txa, txb, to, p, st)
+                       : launch<MODE, W_NF4, !NAT>(ta, t0, t1, txa, txb, to, p, st);
     default:
-      return mn == NAT ? launch<MODE, W_INT8, NAT>(ta, t0, t1, txa, txb, p, st)
-                       : launch<MODE, W_INT8, !NAT>(ta, t0, t1, txa, txb, p, st);
+      return mn == NAT ? launch<MODE, W_INT8, NAT>(ta, t0, t1, txa, txb, to, p, st)
+                       : launch<MODE, W_INT8, !NAT>(ta, t0, t1, txa, txb, to, p, st);
   }
 }
 
