@@ -333,11 +333,31 @@ def down(h: torch.Tensor, offsets: torch.Tensor, w2, *, hidden: int, out: torch.
     return y
 
 
+_PAD_ATTR = "_mirai_lora_pads"
+
+
+def _factor_pads(src: torch.Tensor) -> dict:
+    """The padded kernel operands built from one adapter factor, kept on the
+    factor tensor itself (the caller's parameter) so that they are built once
+    per binding and rebuilt only when the factor changes: a moved version
+    counter (an in-place optimizer step) or new storage drops them."""
+    tag = (src._version, src.data_ptr())
+    held = getattr(src, _PAD_ATTR, None)
+    if held is None or held[0] != tag:
+        held = (tag, {})
+        try:
+            setattr(src, _PAD_ATTR, held)
+        except (AttributeError, RuntimeError):
+            pass  # a tensor that takes no attributes gets pads for this call only
+    return held[1]
+
+
 class DownLoRA:
     """A LoRA adapter on the expert down projection (w2): y += scale (h A^T) B^T
     with A [E, r, I] and B [E, H, r] (active_expert_lora.py:43-116, 434-478)."""
 
     def __init__(self, a: torch.Tensor, b: torch.Tensor, scale: float, *, compute_grads: bool = False):
+        self._src_a, self._src_b = a, b
         self.a = _cuda(a.detach().to(torch.bfloat16), "lora_a")
         self.b = _cuda(b.detach().to(torch.bfloat16), "lora_b")
         # when set, moe_backward_dx also fills grad_a [E, r, I] / grad_b [E, H, r] (fp32)
@@ -350,33 +370,35 @@ class DownLoRA:
                              f"{tuple(self.a.shape)} and {tuple(self.b.shape)}")
         self.rank = int(r)
         self.scale = float(scale)
-        self._b_pad = None
-        self._a_pad = {}  # rotation group -> padded (and, for a group, rotated) A
 
     def b_pad(self) -> torch.Tensor:
-        """B zero-padded to [E*H, 64]: the K-major rank-block operand of the down GEMM."""
-        if self._b_pad is None:
+        """B zero-padded to [E*H, 64]: the K-major rank-block operand of the
+        down GEMM.  Built once per value of the factor."""
+        pads = _factor_pads(self._src_b)
+        if "b" not in pads:
             E, H, r = self.b.shape
             pad = torch.zeros((E, H, 64), dtype=torch.bfloat16, device=self.b.device)
             pad[:, :, :r] = self.b
-            self._b_pad = pad.reshape(E * H, 64)
-        return self._b_pad
+            pads["b"] = pad.reshape(E * H, 64)
+        return pads["b"]
 
     def a_pad(self, rotation: int = 0) -> torch.Tensor:
         """A zero-padded to [E*64, I]: the MN-major rank-block operand of the
         down dX GEMM; with ``rotation`` > 0 each row rotated by the
         block-Hadamard matrix of that group size (A H), for the rotated INT8
         format whose dh is rotated after the GEMM (H H = 1).  Built once per
-        adapter and group."""
-        if rotation not in self._a_pad:
+        value of the factor and group."""
+        pads = _factor_pads(self._src_a)
+        key = ("a", int(rotation))
+        if key not in pads:
             E, r, I = self.a.shape
             pad = torch.zeros((E, 64, I), dtype=torch.bfloat16, device=self.a.device)
             pad[:, :r, :] = self.a
             pad = pad.reshape(E * 64, I)
             if rotation:
                 pad = rotate_rows(pad, rotation)
-            self._a_pad[rotation] = pad
-        return self._a_pad[rotation]
+            pads[key] = pad
+        return pads[key]
 
 
 LORA_FACTOR_ROWS, LORA_FACTOR_COLS = 0, 1

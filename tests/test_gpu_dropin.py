@@ -127,6 +127,41 @@ def test_module_with_lora_trains_adapter():
     assert float(x.grad.norm()) > 0
 
 
+def test_lora_operands_follow_optimizer_steps():
+    """The padded adapter operands are built once per value of the factors:
+    after each optimizer step the module's outputs and gradients equal those
+    of freshly made factor tensors with the same values."""
+    dev = _dev()
+    from mirai_b200.experts import B200GroupedExperts, down_lora_of, run_routed
+    T, H, E, k, I, r = 384, 256, 4, 2, 256, 16
+    torch.manual_seed(5)
+    m = B200GroupedExperts.from_empty(num_experts=E, quant_format="bf16")
+    for key, shp in (("w1", (E, I, H)), ("w3", (E, I, H)), ("w2", (E, H, I))):
+        m.load_dense_weight(key, (torch.randn(*shp) * 0.05).to(dev))
+    m.attach_expert_lora(tensor_name="w2", rank=r, alpha=float(r))
+    m = m.to(dev)
+    ad = m.expert_lora["w2"]
+    opt = torch.optim.SGD(ad.parameters(), lr=2.0)
+    idx = torch.randint(0, E, (T, k), device=dev)
+    sc = torch.rand(T, k, device=dev) + 0.1
+    for _ in range(3):
+        x = torch.randn(T, H, device=dev).to(torch.bfloat16)
+        xa = x.clone().requires_grad_(True)
+        out = m.run_direct_routed(xa, sc, idx)
+        out.float().pow(2).mean().backward()
+        a, b, scale = down_lora_of(m)
+        fa = a.detach().clone().requires_grad_(True)
+        fb = b.detach().clone().requires_grad_(True)
+        xb = x.clone().requires_grad_(True)
+        ref = run_routed(m.bound_weights(), xb, sc, idx, lora=(fa, fb, scale))
+        ref.float().pow(2).mean().backward()
+        assert torch.equal(out, ref)
+        assert torch.equal(xa.grad, xb.grad)
+        assert torch.equal(ad.lora_a.grad, fa.grad) and torch.equal(ad.lora_b.grad, fb.grad)
+        opt.step()
+        opt.zero_grad()
+
+
 @pytest.mark.parametrize("name", ["routed_int8_bf16", "routed_int8_fp32", "routed_int8_g16_fp32"])
 def test_module_int8_against_reference_goldens(golden, name):
     """The reference's own INT8 routed execution (run_direct_routed under

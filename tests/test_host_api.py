@@ -222,3 +222,20 @@ def test_packed_state_entry_round_trip_on_cpu():
     assert m8.w1_group_size == 16 and torch.equal(m8.w2_int8, t8["e.w2_int8"])
     with pytest.raises(ValueError, match="learned rotations"):
         ex.B200GroupedExperts.from_packed_state(dict(spec8, rotations={"w1": "r"}), t8)
+
+
+def test_lora_factor_pads_are_kept_until_the_factor_changes():
+    """Padded adapter operands live on the factor tensor and are rebuilt only
+    after the factor changes (in-place update or new storage)."""
+    from mirai_b200 import ops
+
+    p = torch.nn.Parameter(torch.randn(2, 4, 8))
+    pads = ops._factor_pads(p)
+    pads["b"] = "built"
+    assert ops._factor_pads(p)["b"] == "built"
+    with torch.no_grad():
+        p.add_(1.0)  # an optimizer step
+    assert "b" not in ops._factor_pads(p)
+    ops._factor_pads(p)["b"] = "rebuilt"
+    p.data = torch.zeros(2, 4, 8)  # new storage
+    assert "b" not in ops._factor_pads(p)
