@@ -53,12 +53,6 @@ CONFIGS = {
     "c4": dict(T=65536, H=4096, E=128, k=8, I=1536, fmt="nf4", zipf=None, layers=16, ep="strong"),
 }
 METRIC = "MoE-FFN tokens/s (NF4 experts) + % TC/HBM roofline at 1/2/4/8 B200"
-# Our kernels launched by one forward step: route 1, plan 4, permute 1, gate/up 1, down 1,
-# combine 1; a train step adds combine-backward, down-dX, gate/up-dX and the un-permute sum.
-KERNELS_PER_STEP = 9
-# train step: + combine-backward, down-dX, gate/up-dX, un-permute sum, and the
-# LoRA kernels (2 projections, 2 factor gradients)
-TRAIN_EXTRA_KERNELS = 8
 LORA_RANK = 16
 # DRAM bytes (read + write) per launch of a grouped GEMM from an ncu capture of
 # the same kernel on the same workload, with the capture it came from (the
@@ -316,19 +310,21 @@ def run_ours(args, cfg, rank, world, dev):
         barrier()
         torch.cuda.synchronize()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0 = ops.launch_count()
         t0.record()
         for _ in range(steps):
             fn()
         t1.record()
+        n1 = ops.launch_count()
         t1.synchronize()
         barrier()
         torch.cuda.synchronize()
         clk = clocks.stop()
         ops.check_device()
-        return t0.elapsed_time(t1) / steps, clk
+        return t0.elapsed_time(t1) / steps, clk, n1 - n0
 
     # ---- device-resident throughput (value)
-    ms, clk = timed(lambda: step(x, logits), args.steps)
+    ms, clk, launches = timed(lambda: step(x, logits), args.steps)
     fwd_ms = timed(lambda: forward(x, logits), args.steps)[0] if train else ms
 
     # ---- each grouped GEMM of the step alone (CUDA events on its stream)
@@ -428,30 +424,15 @@ def run_ours(args, cfg, rank, world, dev):
             "d2h_bytes_per_step": T * H * 2 * (2 if train else 1),
             "copies": "pinned host buffers; 2 slots, uploads and downloads on their own streams overlap compute",
         },
-        "gpu_launches": (KERNELS_PER_STEP + (TRAIN_EXTRA_KERNELS if train else 0)
-                         + rotation_kernels(cfg, args, train)) * args.steps,
+        "gpu_launches": launches,
+        "gpu_launches_source": "libmirai_b200's own count of the kernels its entry points enqueued in the timed "
+                               "region (mirai_b200_launch_count)",
         "clocks": clk,
     }
     return line
 
 
-def rotation_kernels(cfg, args, train):
-    """Rotation launches per step in the block-Hadamard INT8 format: tokens and h
-    forward; dh (with the SwiGLU backward) and dx backward."""
-    if not (cfg["fmt"] == "int8" and args.int8_rotation):
-        return 0
-    return 4 if train else 2
-
-
 # ----------------------------------------------------------------------------- expert-parallel arm
-
-# per layer: route 1, plan 4, permute 1, local plan 4, local permute 1, gate/up 1, down 1,
-# un-permute 1, combine 1 (the NCCL all-to-alls are not counted)
-EP_KERNELS_PER_LAYER = 15
-# training adds: combine backward, down dX, gate/up dX, un-permute sum, the LoRA rank projections (2) and
-# factor gradients (2), and the owners' regrouping gathers (4)
-EP_TRAIN_EXTRA_KERNELS = 12
-
 
 def make_ep_workload(cfg, dev, rank, shard, tokens_local):
     """This rank's tokens, layer-0 router logits and, per layer, the router gate
@@ -511,7 +492,7 @@ def run_ep(args, cfg, rank, world, dev):
         lb = torch.randn(shard.local, cfg["H"], LORA_RANK, device=dev, generator=gen) * 0.02
         lora = ops.DownLoRA(la, lb, 16.0 / LORA_RANK, compute_grads=True)
     chunks = args.ep_chunks if world > 1 else 1
-    ipc = args.ep_transport == "ipc" and world > 1 and not train  # training runs on the NCCL transport
+    ipc = args.ep_transport == "ipc" and world > 1
     free_sms = args.ep_free_sms if args.ep_free_sms is not None else (2 if ipc else 16)
     if world > 1 and (chunks > 1 or ipc) and free_sms > 0:
         # leave SMs for the communication kernels (NCCL's all-to-all; with ipc only the
@@ -534,10 +515,14 @@ def run_ep(args, cfg, rank, world, dev):
 
     def step(xin, l0, out=None, gin=None, dx_out=None):
         if train:  # one layer: forward keeping the owners' gate/up, then the dX exchange and GEMMs
-            o, st = ep_moe_forward(xin, l0, stack[0][1], shard=shard, top_k=k, inter=I, ops=stepops, chunks=chunks,
-                                   train=True, lora=lora)
-            dx, _ = ep_moe_backward(g_out if gin is None else gin, st, stack[0][1], shard=shard, inter=I,
-                                    ops=stepops, lora=lora)
+            g = g_out if gin is None else gin
+            if layer is not None:
+                o, st = layer.forward(xin, l0, stack[0][1], train=True, lora=lora)
+                dx, _ = layer.backward(g, st, stack[0][1], lora=lora)
+            else:
+                o, st = ep_moe_forward(xin, l0, stack[0][1], shard=shard, top_k=k, inter=I, ops=stepops,
+                                       chunks=chunks, train=True, lora=lora)
+                dx, _ = ep_moe_backward(g, st, stack[0][1], shard=shard, inter=I, ops=stepops, lora=lora)
             if out is not None:
                 out.copy_(o)
             if dx_out is not None:
@@ -566,10 +551,12 @@ def run_ep(args, cfg, rank, world, dev):
     barrier()
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = ops.launch_count()
     t0.record()
     for _ in range(args.steps):
         step(x, logits0)
     t1.record()
+    launches = ops.launch_count() - n0
     t1.synchronize()
     barrier()
     torch.cuda.synchronize()
@@ -669,8 +656,10 @@ def run_ep(args, cfg, rank, world, dev):
             "d2h_bytes_per_step": T_r * H * 2 * (2 if train else 1),
             "copies": "per rank: pinned host buffers; 2 slots, uploads and downloads on their own streams",
         },
-        "gpu_launches": (EP_KERNELS_PER_LAYER + (EP_TRAIN_EXTRA_KERNELS if train else 0)) * layers * args.steps,
-        "gpu_launches_scope": "per rank",
+        "gpu_launches": launches,
+        "gpu_launches_scope": "rank 0 (every rank launches its own)",
+        "gpu_launches_source": "libmirai_b200's own count of the kernels its entry points enqueued in the timed "
+                               "region (mirai_b200_launch_count)",
         "clocks": clk,
     }
 

@@ -97,6 +97,9 @@ typedef struct mirai_int8_weight {
 /* ----------------------------------------------------------------- library */
 const char* mirai_b200_last_error(void);
 int mirai_b200_version(void);
+/* Kernels this library has enqueued since it was loaded (every entry point,
+ * all devices and streams): lets a caller count the launches of a region. */
+uint64_t mirai_b200_launch_count(void);
 /* Synchronises `stream`, then returns (and clears) the device error word:
  * *code = 0 or a MIRAI_ERR_DEVICE_* code, *info = where it was raised. */
 int mirai_b200_device_status(mirai_stream_t stream, int* code, int* info);

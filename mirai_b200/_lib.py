@@ -52,6 +52,7 @@ class Int8Weight(ctypes.Structure):
 SIGNATURES = {
     "mirai_b200_last_error": (ctypes.c_char_p, []),
     "mirai_b200_version": (ctypes.c_int, []),
+    "mirai_b200_launch_count": (ctypes.c_uint64, []),
     "mirai_b200_device_status": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "mirai_route_topk": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_i32, c_f32, c_vp, c_vp, c_vp]),
     "mirai_b200_set_gemm_sm_limit": (ctypes.c_int, [c_i32]),
@@ -191,6 +192,10 @@ def call(name: str, *args) -> None:
     if rc != MIRAI_OK:
         msg = lib.mirai_b200_last_error()
         raise MiraiError(rc, msg.decode() if msg else "")
+
+
+def launch_count() -> int:
+    return int(load().mirai_b200_launch_count())
 
 
 def device_status(stream_handle: int) -> tuple[int, int]:

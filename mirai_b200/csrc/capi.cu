@@ -1,5 +1,6 @@
 // Library-wide state of the C ABI: last-error strings, the device error word,
 // SM count, and the tensor-map encoder obtained from the driver.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -20,9 +21,13 @@ int set_error(int code, const char* fmt, ...) {
   return code;
 }
 
-int check_launch(const char* what) {
+// Kernels this library has enqueued since it was loaded (all devices and streams).
+static std::atomic<unsigned long long> g_launches{0};
+
+int check_launch(const char* what, int kernels) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  g_launches.fetch_add((unsigned long long)kernels, std::memory_order_relaxed);
   return MIRAI_OK;
 }
 
@@ -105,6 +110,8 @@ extern "C" {
 const char* mirai_b200_last_error(void) { return mirai::t_last_error; }
 
 int mirai_b200_version(void) { return 100; }
+
+uint64_t mirai_b200_launch_count(void) { return mirai::g_launches.load(std::memory_order_relaxed); }
 
 int mirai_ipc_export(const void* ptr, void* handle, uint64_t* offset) {
   if (!ptr || !handle || !offset) return mirai::set_error(MIRAI_ERR_INVALID_ARG, "ipc_export: null pointer");

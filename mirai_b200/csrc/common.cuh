@@ -15,7 +15,9 @@ namespace mirai {
 // ----------------------------------------------------------------------------
 // host-side error state (defined in capi.cu)
 int set_error(int code, const char* fmt, ...);
-int check_launch(const char* what);
+// Reads the launch status of the `kernels` kernels just enqueued and, on success,
+// adds them to the count mirai_b200_launch_count() reports.
+int check_launch(const char* what, int kernels = 1);
 int sm_count();
 int gemm_sm_limit();
 
@@ -127,6 +129,12 @@ __device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, ui
           smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Bring `bytes` (a multiple of 16) at the 16-byte aligned global address `p` into L2 (TMA unit).
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
+               : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {

@@ -687,7 +687,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     // warps sharing a lane quarter split the 32-column chunks between them
     constexpr int NSPLIT = C::EPI_WARPS / 4;
     const int part = (warp - C::EPI_FIRST) / 4;
-    const uint32_t tempty_leader[2] = {leader_addr(&sm.tempty[0]), leader_addr(&sm.tempty[1])};
+    const uint32_t tempty_leader0 = leader_addr(&sm.tempty[0]), tempty_leader1 = leader_addr(&sm.tempty[1]);
     int stg = 0;  // the next staging box of this warp
     // Write one 32 x 32 bf16 block (this lane's row: 16 packed words) through a
     // staging box to `map` at (col, row0): the whole warp, rows row0..row0+31 all valid.
@@ -712,16 +712,32 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
     for (int t = unit; t < total_tiles && !*abort_flag; t += num_units, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait(&sm.tfull[acc], acc_phase, 30)) {
-        *abort_flag = 1;
-        break;
-      }
-      tc_fence_after();
       int j, e, m, n;
       decode_tile<WF, PAIR>(t, sm, units, p.n_tiles, j, e, m, n);
       int blk_row = 0, blk_rows = 0;  // several sources: this CTA's block
       if (p.nsrc > 1) source_block(sm, e, p.nsrc, m * BPT + (int)rank, blk_row, blk_rows);
       const int64_t seg_rows = sm.seg_rows[j];
+      if (MODE == DXDOWN && p.gate_up != nullptr) {
+        // The SwiGLU backward reads this tile's saved gate and up columns: start
+        // bringing this thread's row of both into L2 while the accumulator fills.
+        const int col0 = n * TN;
+        const int cols = min(TN, p.N - col0);
+        for (int sub = 0; sub < RT && cols > 0; ++sub) {
+          const int lr = q * 32 + lane;
+          const int r = sub * SUB_M + (int)rank * BM + lr;
+          const bool live = p.nsrc > 1 ? lr < blk_rows : (int64_t)m * TILE_M + r < seg_rows;
+          if (!live || part != 0) continue;
+          const int64_t grow = p.nsrc > 1 ? (int64_t)blk_row + lr : (int64_t)sm.row_start[j] + (int64_t)m * TILE_M + r;
+          const __nv_bfloat16* base = p.gate_up + grow * 2 * (int64_t)p.N + col0;
+          prefetch_l2_bulk(base, (uint32_t)cols * 2u);
+          prefetch_l2_bulk(base + p.N, (uint32_t)cols * 2u);
+        }
+      }
+      if (!mbar_wait(&sm.tfull[acc], acc_phase, 30)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
       for (int sub = 0; sub < RT; ++sub) {
       // no rows in this sub-tile (warp-uniform; several sources: blocks say)
       if (p.nsrc == 1 && (int64_t)m * TILE_M + sub * SUB_M >= seg_rows) break;
@@ -790,22 +806,34 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         // (autograd of experts.py:301-317 in bf16: mul, silu backward)
         const int64_t ld2 = 2 * (int64_t)p.N;
         constexpr int NCH = TN / 32;
-#pragma unroll 1
-        for (int c = part * (NCH / NSPLIT); c < (part + 1) * (NCH / NSPLIT); ++c) {
+        const int c_first = part * (NCH / NSPLIT), c_end = (part + 1) * (NCH / NSPLIT);
+        // the saved gate/up of the next chunk are loaded while this chunk computes
+        uint4 gnext[4], unext[4];
+        auto load_gu = [&](int c) {
           const int col = n * TN + c * 32;
+          if (valid && col < p.N) {
+            const uint4* gs = reinterpret_cast<const uint4*>(p.gate_up + grow * ld2 + col);
+            const uint4* us = reinterpret_cast<const uint4*>(p.gate_up + grow * ld2 + p.N + col);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) gnext[v] = gs[v], unext[v] = us[v];
+          }
+        };
+        load_gu(c_first);
+#pragma unroll 1
+        for (int c = c_first; c < c_end; ++c) {
+          const int col = n * TN + c * 32;
+          uint32_t gw[16], uw[16];
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            gw[4 * v] = gnext[v].x, gw[4 * v + 1] = gnext[v].y, gw[4 * v + 2] = gnext[v].z, gw[4 * v + 3] = gnext[v].w;
+            uw[4 * v] = unext[v].x, uw[4 * v + 1] = unext[v].y, uw[4 * v + 2] = unext[v].z, uw[4 * v + 3] = unext[v].w;
+          }
+          if (c + 1 < c_end) load_gu(c + 1);
           uint32_t v32[32];
           tmem_ld_32x32b_x32(tb + c * 32, v32);
           tmem_ld_wait();
           if (valid && col < p.N) {
-            const uint4* gs = reinterpret_cast<const uint4*>(p.gate_up + grow * ld2 + col);
-            const uint4* us = reinterpret_cast<const uint4*>(p.gate_up + grow * ld2 + p.N + col);
-            uint32_t gw[16], uw[16], dg[16], du[16];
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              const uint4 a = gs[v], b = us[v];
-              gw[4 * v] = a.x, gw[4 * v + 1] = a.y, gw[4 * v + 2] = a.z, gw[4 * v + 3] = a.w;
-              uw[4 * v] = b.x, uw[4 * v + 1] = b.y, uw[4 * v + 2] = b.z, uw[4 * v + 3] = b.w;
-            }
+            uint32_t dg[16], du[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               float dgo[2], duo[2];
@@ -867,7 +895,7 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        if (PAIR) mbar_arrive_cluster(tempty_leader[acc]);
+        if (PAIR) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
         else mbar_arrive(&sm.tempty[acc]);
       }
     }

@@ -161,7 +161,7 @@ int mirai_nf4_quantize(const void* weight_bf16, int32_t num_experts, int64_t out
   const int n_nested = (int)((bpe + nested_blocksize - 1) / nested_blocksize);
   qz::nf4_nested_kernel<<<num_experts, 1024, 0, s>>>(am, bpe, nested_blocksize, n_nested, nested_code, absmax,
                                                       nested_absmax, offset);
-  return check_launch("nf4_quantize");
+  return check_launch("nf4_quantize", 2);
 }
 
 int mirai_int8_quantize_rows(const void* weight, int32_t weight_dtype, int64_t rows, int64_t in_features, int8_t* q,

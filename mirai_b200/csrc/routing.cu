@@ -497,7 +497,7 @@ int mirai_dispatch_plan(const int64_t* top_indices, int64_t num_tokens, int32_t 
     cudaMemsetAsync(counts, 0, sizeof(int64_t) * num_experts, s);
     cudaMemsetAsync(starts, 0, sizeof(int64_t) * num_experts, s);
     cudaMemsetAsync(offsets, 0, sizeof(int32_t) * num_experts, s);
-    return check_launch("dispatch_plan(empty)");
+    return check_launch("dispatch_plan(empty)", 0);  // memsets only
   }
   if (!top_indices || !sort_positions || !sorted_token_indices || !inverse_order)
     return set_error(MIRAI_ERR_INVALID_ARG, "dispatch_plan: null pointer");
@@ -519,7 +519,7 @@ int mirai_dispatch_plan(const int64_t* top_indices, int64_t num_tokens, int32_t 
   plan_expert_scan_kernel<<<1, 1024, 0, s>>>(counts, num_experts, starts, offsets);
   plan_scatter_kernel<<<chunks, kPlanThreads, plan_scatter_smem(num_experts), s>>>(
       top_indices, S, num_experts, top_k, cc, starts, sort_positions, sorted_token_indices, inverse_order);
-  return check_launch("dispatch_plan");
+  return check_launch("dispatch_plan", 4);
 }
 
 int mirai_permute_rows_bf16(const void* tokens, int64_t num_tokens, const int64_t* sorted_token_indices,

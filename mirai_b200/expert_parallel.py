@@ -696,6 +696,7 @@ class ExpertParallelMoE:
         self.n_copy_streams = max(1, int(copy_streams))
         self.copy_streams: list[torch.cuda.Stream] = []  # side streams when n_copy_streams > 1
         self.epoch = 0  # exchanges so far; the same sequence on every rank
+        self._gen = 0   # forwards so far (a training state is valid until the next one)
         # read the device error word at the host sync each call already makes (the count read)
         self.check_device = bool(check_device)
         # optional probe: called as on_phase(name, stream) at phase boundaries
@@ -747,13 +748,27 @@ class ExpertParallelMoE:
             done.record(side)
             stream.wait_event(done)
 
-    def forward(self, tokens: torch.Tensor, logits: torch.Tensor, local_weights: Any) -> torch.Tensor:
+    def forward(self, tokens: torch.Tensor, logits: torch.Tensor, local_weights: Any, *, train: bool = False,
+                lora=None):
+        """The layer for this rank's tokens (``ep_moe_forward``'s contract).
+
+        ``train=True`` returns ``(out, state)`` for ``backward``: the owners
+        keep the gate/up of the rows they received, and the expert outputs
+        stay where they came back, in this rank's exchange buffer, so one
+        instance serves one layer of a training step (a second forward on the
+        same instance before ``backward`` makes ``backward`` refuse the state).
+        ``lora`` (``ops.DownLoRA`` over this rank's experts) adds the adapter
+        on w2 (training only)."""
+        if lora is not None and not train:
+            raise ValueError("the expert-parallel forward takes a LoRA adapter in training (train=True)")
         ops, shard, k = self.ops, self.shard, self.top_k
         G, E, El, me = shard.world, shard.num_experts, shard.local, shard.rank
         T, H = tokens.shape
         dev = tokens.device
         if G == 1:
-            return ep_moe_forward(tokens, logits, local_weights, shard=shard, top_k=k, inter=self.inter, ops=ops)
+            return ep_moe_forward(tokens, logits, local_weights, shard=shard, top_k=k, inter=self.inter, ops=ops,
+                                  train=train, lora=lora)
+        self._gen += 1
         if self.comm is None:
             self.comm = torch.cuda.Stream(device=dev)
             if self.n_copy_streams > 1:
@@ -784,9 +799,10 @@ class ExpertParallelMoE:
         plan = exchange_blocks(counts, me, self.layout, regroup=self.regroup, hidden=H,
                                inter=self.inter, row_bytes=row_bytes)
         in_cap = (plan.in_cap * row_bytes + 255) // 256 * 256
-        ret_cap = plan.ret_cap * row_bytes
+        ret_cap = (plan.ret_cap * row_bytes + 255) // 256 * 256
         F = PeerBuffers.FLAG_BYTES
-        ptrs = self.buffers.ensure(in_cap + ret_cap, dev)
+        # regions: received rows | returned expert outputs | (training) returned dX rows
+        ptrs = self.buffers.ensure(in_cap + ret_cap * (2 if train else 1), dev)
         local = self.buffers.local[F:]
         data = [p + F for p in ptrs]
         ret = [p + in_cap for p in data]
@@ -801,22 +817,7 @@ class ExpertParallelMoE:
             pos += len(ends)
         mark("count gather + host read", comp)
 
-        from . import _lib
-        slots = (_lib.c_vp * G)(*[None if d == me else ptrs[d] + 8 * me for d in range(G)])
-
-        def arrived(stream):
-            """Signal this exchange to every peer; return (epoch, event after the local copy)."""
-            self.epoch += 1
-            _lib.call("mirai_ep_signal", slots, G, self.epoch, _lib.c_vp(stream.cuda_stream))
-            ev = torch.cuda.Event()
-            ev.record(stream)
-            return self.epoch, ev
-
-        def wait(arrival):
-            epoch, ev = arrival
-            comp.wait_event(ev)  # this rank's own block
-            _lib.call("mirai_ep_wait", _lib.c_vp(ptrs[me]), G, me, epoch, _lib.c_vp(comp.cuda_stream))
-
+        ex = _Exchange(self, ptrs, comp)
         ready = torch.cuda.Event()
         ready.record(comp)
         comm.wait_event(ready)
@@ -825,35 +826,173 @@ class ExpertParallelMoE:
             xs = prep[c][2]
             xs.record_stream(comm)
             self._copy_blocks(plan.dispatch[c], data, xs.data_ptr(), row_bytes, comm)
-            landed.append(arrived(comm))
+            landed.append(ex.arrived(comm))
             mark(f"dispatch copies + arrival, chunk {c}", comm)
-        returned = []
+        returned, saved = [], []
+        kw = {"lora": lora} if lora is not None else {}
         for c in range(C):
-            wait(landed[c])
+            ex.wait(landed[c])
             rows_c = plan.in_rows[c]
             xc = x_in[plan.in_base[c]:plan.in_base[c] + rows_c]
+            sv = None
             if not rows_c:
                 yc = xc
             elif plan.regroup[c] is None:
-                yc = ops.experts(xc, offs_dev[c], local_weights, self.inter, sources=plan.sources)
+                if train:
+                    yc, sv = ops.experts_train(xc, offs_dev[c], local_weights, self.inter, sources=plan.sources, **kw)
+                else:
+                    yc = ops.experts(xc, offs_dev[c], local_weights, self.inter, sources=plan.sources)
             else:
                 # expert-major for the GEMMs (no tile cut at a source boundary), then back
                 order, inverse = regroup_order(allm[:, me, c, :], rows_c)
-                ye = ops.experts(ops.permute(xc, order), offs_dev[c], local_weights, self.inter)
+                xe = ops.permute(xc, order)
+                if train:
+                    ye, inner = ops.experts_train(xe, offs_dev[c], local_weights, self.inter, **kw)
+                    sv = ("regrouped", order, inverse, offs_dev[c], inner)
+                else:
+                    ye = ops.experts(xe, offs_dev[c], local_weights, self.inter)
                 yc = ops.permute(ye, inverse)
+            saved.append(sv)
             mark(f"gate/up + down GEMMs, chunk {c}", comp)
             done = torch.cuda.Event()
             done.record(comp)
             comm.wait_event(done)
             yc.record_stream(comm)
             self._copy_blocks(plan.give_back[c], ret, yc.data_ptr(), row_bytes, comm)
-            returned.append(arrived(comm))
+            returned.append(ex.arrived(comm))
             mark(f"return copies + arrival, chunk {c}", comm)
         out = torch.empty((T, H), dtype=tokens.dtype, device=dev)
+        y_back = []
         for c, (b, e) in enumerate(bounds):
-            wait(returned[c])
+            ex.wait(returned[c])
+            yb = y_ret[plan.ret_base[c]:plan.ret_base[c] + plan.ret_rows[c]]
+            y_back.append(yb)
             if e > b:
-                yb = y_ret[plan.ret_base[c]:plan.ret_base[c] + plan.ret_rows[c]]
                 out[b:e] = ops.combine(yb, prep[c][1].inverse_order, prep[c][0], k, tokens.dtype)
         mark("combine", comp)
-        return out
+        if not train:
+            return out
+        dx_ret = local[in_cap + ret_cap:in_cap + 2 * ret_cap].view(tokens.dtype)[: sum(plan.ret_rows) * H].view(-1, H)
+        return out, IPCTrainState(gen=self._gen, bounds=bounds, prep=[(p[0], p[1]) for p in prep], plan=plan,
+                                  offs=offs_dev, saved=saved, y_back=y_back, x_in=x_in, dx_ret=dx_ret,
+                                  ptrs=list(ptrs), data=data, ret2=[p + in_cap + ret_cap for p in data],
+                                  row_bytes=row_bytes, top_k=k, hidden=H, dtype=tokens.dtype)
+
+    def backward(self, grad_out: torch.Tensor, state: "IPCTrainState", local_weights: Any, *,
+                 lora=None) -> tuple[torch.Tensor, torch.Tensor]:
+        """dX of ``forward(train=True)``: grad_out [T_r, H] -> (dx [T_r, H],
+        d_top_weights fp32 [T_r, k]), with the rank's adapter gradients in
+        ``lora``.  Collective.  Per chunk, as ``ep_moe_backward`` does, over
+        the copy-engine exchange: the combine backward here; the gradient rows
+        copied into the owners' receive regions (the forward's rows are no
+        longer needed there: every owner finished its GEMMs on them before the
+        last expert outputs came back); the owner's dX GEMMs on the gate/up it
+        kept; dX rows copied back into the third region of the token owner's
+        buffer; the permute backward sums each token's routes."""
+        ops, shard = self.ops, self.shard
+        if shard.world == 1:
+            return ep_moe_backward(grad_out, state, local_weights, shard=shard, inter=self.inter, ops=ops, lora=lora)
+        if not isinstance(state, IPCTrainState) or state.gen != self._gen:
+            raise RuntimeError("expert-parallel backward: this layer's exchange buffers were used by another forward "
+                               "since the training forward (use one ExpertParallelMoE per layer in training)")
+        if lora is not None and lora.compute_grads:
+            lora.grad_a = lora.grad_b = None  # summed over this call's chunks
+        dev = grad_out.device
+        comp, comm = torch.cuda.current_stream(dev), self.comm
+        mark = self.on_phase or (lambda name, stream: None)
+        plan, k, H = state.plan, state.top_k, state.hidden
+        T = grad_out.shape[0]
+        ex = _Exchange(self, state.ptrs, comp)
+        dx = torch.empty((T, H), dtype=state.dtype, device=dev)
+        dw = torch.empty((T, k), dtype=torch.float32, device=dev)
+        sent = []
+        for c, (b, e) in enumerate(state.bounds):
+            tw, dplan = state.prep[c]
+            if e > b:
+                gy, gw = ops.combine_backward(grad_out[b:e], state.y_back[c], dplan.inverse_order, tw, k)
+                dw[b:e] = gw
+            else:
+                gy = torch.empty((0, H), dtype=state.y_back[c].dtype, device=dev)
+            done = torch.cuda.Event()
+            done.record(comp)
+            comm.wait_event(done)
+            gy.record_stream(comm)
+            self._copy_blocks(plan.dispatch[c], state.data, gy.data_ptr(), state.row_bytes, comm)
+            sent.append(ex.arrived(comm))
+            mark(f"combine backward + gradient copies, chunk {c}", comm)
+        kw = {"lora": lora} if lora is not None else {}
+        returned = []
+        for c in range(len(state.bounds)):
+            ex.wait(sent[c])
+            rows_c = plan.in_rows[c]
+            gc = state.x_in[plan.in_base[c]:plan.in_base[c] + rows_c]
+            if rows_c:
+                dc = ops.experts_backward(gc, state.offs[c], local_weights, self.inter, plan.sources,
+                                          state.saved[c], **kw)
+            else:
+                dc = gc
+            mark(f"dX GEMMs, chunk {c}", comp)
+            done = torch.cuda.Event()
+            done.record(comp)
+            comm.wait_event(done)
+            dc.record_stream(comm)
+            self._copy_blocks(plan.give_back[c], state.ret2, dc.data_ptr(), state.row_bytes, comm)
+            returned.append(ex.arrived(comm))
+        for c, (b, e) in enumerate(state.bounds):
+            ex.wait(returned[c])
+            if e > b:
+                rows = state.dx_ret[plan.ret_base[c]:plan.ret_base[c] + plan.ret_rows[c]]
+                dx[b:e] = ops.combine(rows, state.prep[c][1].inverse_order, None, k, state.dtype)
+        mark("dX un-permute", comp)
+        return dx, dw
+
+
+class _Exchange:
+    """Arrival signalling of one layer's copy-engine exchanges: ``arrived``
+    stores the next epoch into this rank's slot of every peer's flags after a
+    block list's copies; ``wait`` holds the compute stream (bounded, 2 s)
+    until every peer's slot in this rank's flags reaches an epoch."""
+
+    def __init__(self, layer: "ExpertParallelMoE", ptrs: list[int], comp):
+        from . import _lib
+        self.layer, self.ptrs, self.comp, self._lib = layer, ptrs, comp, _lib
+        G, me = layer.shard.world, layer.shard.rank
+        self.slots = (_lib.c_vp * G)(*[None if d == me else ptrs[d] + 8 * me for d in range(G)])
+
+    def arrived(self, stream):
+        """Signal this exchange to every peer; return (epoch, event after the local copy)."""
+        lay = self.layer
+        lay.epoch += 1
+        self._lib.call("mirai_ep_signal", self.slots, lay.shard.world, lay.epoch, self._lib.c_vp(stream.cuda_stream))
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        return lay.epoch, ev
+
+    def wait(self, arrival):
+        epoch, ev = arrival
+        self.comp.wait_event(ev)  # this rank's own block
+        lay = self.layer
+        self._lib.call("mirai_ep_wait", self._lib.c_vp(self.ptrs[lay.shard.rank]), lay.shard.world, lay.shard.rank,
+                       epoch, self._lib.c_vp(self.comp.cuda_stream))
+
+
+@dataclass
+class IPCTrainState:
+    """What ``ExpertParallelMoE.backward`` needs from ``forward(train=True)``."""
+
+    gen: int                 # the layer's forward count when this state was made
+    bounds: list             # [(begin, end)] token range of each chunk
+    prep: list               # per chunk: (route weights, dispatch plan)
+    plan: "BlockPlan"
+    offs: list               # per chunk: segment ends of the owner's GEMMs (device)
+    saved: list              # per chunk: what the owner's GEMMs kept (None without rows)
+    y_back: list             # per chunk: the expert outputs that came back (views of the buffer)
+    x_in: torch.Tensor       # this rank's receive region (the gradient rows land here)
+    dx_ret: torch.Tensor     # this rank's dX return region
+    ptrs: list               # every rank's buffer (flags first)
+    data: list               # every rank's receive region
+    ret2: list               # every rank's dX return region
+    row_bytes: int
+    top_k: int
+    hidden: int
+    dtype: torch.dtype

@@ -41,6 +41,12 @@ def device_status() -> tuple[int, int]:
     return _lib.device_status(torch.cuda.current_stream().cuda_stream)
 
 
+def launch_count() -> int:
+    """Kernels libmirai_b200 has enqueued since it was loaded (host-side count:
+    every kernel an entry point launched, on any stream)."""
+    return _lib.launch_count()
+
+
 def check_device() -> None:
     code, info = device_status()
     if code:

@@ -135,8 +135,9 @@ def _train_rank_main(rank, world, port, cfg, results):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     try:
         from mirai_b200 import ops
-        from mirai_b200.expert_parallel import ExpertShard, ep_moe_backward, ep_moe_forward, shard_tokens
-        T, H, E, k, I, fmt, chunks, rotated, lora_rank = cfg
+        from mirai_b200.expert_parallel import (ExpertParallelMoE, ExpertShard, ep_moe_backward, ep_moe_forward,
+                                                shard_tokens)
+        T, H, E, k, I, fmt, chunks, rotated, lora_rank, transport, regroup = cfg
         g = torch.Generator(device=dev).manual_seed(13)
         x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
         logits = torch.randn(T, E, generator=g, device=dev) * 1.5
@@ -159,14 +160,33 @@ def _train_rank_main(rank, world, port, cfg, results):
             lb = torch.randn(E, H, lora_rank, generator=g, device=dev) * 0.05
             lora = ops.DownLoRA(la[lo:hi], lb[lo:hi], 2.0, compute_grads=True)
             lora_full = ops.DownLoRA(la, lb, 2.0, compute_grads=True)
-        out, st = ep_moe_forward(x[b:e].contiguous(), logits[b:e].contiguous(), local, shard=shard, top_k=k,
-                                 inter=I, chunks=chunks, train=True, lora=lora)
-        dx, dw = ep_moe_backward(gout[b:e].contiguous(), st, local, shard=shard, inter=I, lora=lora)
+        xr, lr_, gr = x[b:e].contiguous(), logits[b:e].contiguous(), gout[b:e].contiguous()
+        stale_refused = True
+        if transport == "ipc":
+            layer = ExpertParallelMoE(shard, top_k=k, inter=I, chunks=chunks, regroup=regroup)
+            try:
+                # a training state is refused once another forward has used the layer's buffers
+                _, old = layer.forward(xr, lr_, local, train=True, lora=lora)
+                layer.forward(xr, lr_, local)
+                try:
+                    layer.backward(gr, old, local, lora=lora)
+                    stale_refused = False
+                except RuntimeError:
+                    pass
+                out, st = layer.forward(xr, lr_, local, train=True, lora=lora)
+                dx, dw = layer.backward(gr, st, local, lora=lora)
+                torch.cuda.synchronize()
+            finally:
+                layer.close()
+        else:
+            out, st = ep_moe_forward(xr, lr_, local, shard=shard, top_k=k, inter=I, chunks=chunks, train=True,
+                                     lora=lora)
+            dx, dw = ep_moe_backward(gr, st, local, shard=shard, inter=I, lora=lora)
         code, info = ops.device_status()
         idx, tw = ops.route_topk(logits, k)
         ref, rst = ops.moe_forward_train(x, idx, tw, *full, num_experts=E, inter=I, lora=lora_full)
         rdx, rdw = ops.moe_backward_dx(gout, rst, *full, inter=I, lora=lora_full)
-        same = bool(torch.equal(out, ref[b:e])) and bool(torch.equal(dw, rdw[b:e]))
+        same = stale_refused and bool(torch.equal(out, ref[b:e])) and bool(torch.equal(dw, rdw[b:e]))
         if lora_rank:  # this rank's experts' factor gradients (partial sums per chunk: the bf16 tolerance)
             for got, want in ((lora.grad_a, lora_full.grad_a[lo:hi]), (lora.grad_b, lora_full.grad_b[lo:hi])):
                 same = same and float((got - want).abs().max() / want.abs().max()) < 1e-3
@@ -177,24 +197,31 @@ def _train_rank_main(rank, world, port, cfg, results):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fmt,chunks,world,rotated,lora_rank", [
-    ("nf4", 1, 2, False, 0), ("bf16", 2, 2, False, 0), ("int8", 1, 2, False, 0), ("int8", 2, 2, True, 0),
-    ("nf4", 2, 2, False, 16), ("nf4", 2, 4, False, 16),
+@pytest.mark.parametrize("fmt,chunks,world,rotated,lora_rank,transport,regroup", [
+    ("nf4", 1, 2, False, 0, "nccl", "never"), ("bf16", 2, 2, False, 0, "nccl", "never"),
+    ("int8", 1, 2, False, 0, "nccl", "never"), ("int8", 2, 2, True, 0, "nccl", "never"),
+    ("nf4", 2, 2, False, 16, "nccl", "never"), ("nf4", 2, 4, False, 16, "nccl", "never"),
+    ("nf4", 2, 2, False, 16, "ipc", "never"), ("bf16", 1, 2, False, 0, "ipc", "always"),
+    ("int8", 2, 2, True, 16, "ipc", "auto"), ("nf4", 2, 4, False, 16, "ipc", "always"),
 ])
-def test_expert_parallel_backward_equals_single_gpu(fmt, chunks, world, rotated, lora_rank):
-    """Training through the expert-parallel layer (NCCL transport): the
+def test_expert_parallel_backward_equals_single_gpu(fmt, chunks, world, rotated, lora_rank, transport, regroup):
+    """Training through the expert-parallel layer (NCCL all-to-all, or the
+    copy-engine exchange of ``ExpertParallelMoE`` with and without the
+    owners' expert-major regrouping): the
     forward output and the route-weight gradients equal the single-GPU
     layer's exactly, and so does dX (the rows' products and each token's
     ascending-position sum are the single-GPU ones); the block-Hadamard INT8
     format rotates dX rows on the owners before the route sum, so there dX is
     held to the bf16 tolerance instead.  With a rank-16 LoRA on w2 the owners
     regroup their rows expert-major; the adapter's factor gradients of each
-    rank's experts match the single-GPU ones (summed per chunk)."""
+    rank's experts match the single-GPU ones (summed per chunk).  The
+    copy-engine layer refuses a training state once another forward has
+    reused its buffers."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     from mirai_b200.build import build
     build()
-    cfg = (2000, 256, 8, 2, 384, fmt, chunks, rotated, lora_rank)
+    cfg = (2000, 256, 8, 2, 384, fmt, chunks, rotated, lora_rank, transport, regroup)
     with mp.Manager() as mgr:
         results = mgr.dict()
         mp.start_processes(_train_rank_main, args=(world, _free_port(), cfg, results), nprocs=world,
