@@ -336,19 +336,26 @@ def run_ours(args, cfg, rank, world, dev):
     y = torch.empty((S, H), dtype=torch.bfloat16, device=dev)
     reps = max(5, min(50, args.steps))
     kclocks = ClockSampler(torch.cuda.current_device()).start()
-    kernels = {"gateup_swiglu": (4.0 * S * H * I, lambda: ops.gateup_swiglu(xs, plan.offsets, w1, w3, inter=I, out=h)),
-               "down": (2.0 * S * H * I, lambda: ops.down(h, plan.offsets, w2, hidden=H, out=y))}
+    # the weights the step's GEMMs multiply: NF4 decoded once per pass to bf16 where staging pays
+    sw1, sw3, sw2 = ops.stage_nf4((w1, w3, w2), S, E, training=train)
+    staged = sw1 is not w1
+    kernels = {"gateup_swiglu": (4.0 * S * H * I, lambda: ops.gateup_swiglu(xs, plan.offsets, sw1, sw3, inter=I,
+                                                                             out=h)),
+               "down": (2.0 * S * H * I, lambda: ops.down(h, plan.offsets, sw2, hidden=H, out=y))}
     if train and not args.int8_rotation:
         dgu = torch.empty((S, 2 * I), dtype=torch.bfloat16, device=dev)
         dxs = torch.empty((S, H), dtype=torch.bfloat16, device=dev)
         glow = ops.lora_project(y, plan.offsets, lora, forward=False)
-        kernels["down_dx"] = (2.0 * S * H * I, lambda: ops.down_dx(y, plan.offsets, w2, st.gate_up, inter=I,
+        kernels["down_dx"] = (2.0 * S * H * I, lambda: ops.down_dx(y, plan.offsets, sw2, st.gate_up, inter=I,
                                                                    out=dgu, lora=lora, rank_a=glow))
-        kernels["gateup_dx"] = (4.0 * S * H * I, lambda: ops.gateup_dx(dgu, plan.offsets, w1, w3, hidden=H,
+        kernels["gateup_dx"] = (4.0 * S * H * I, lambda: ops.gateup_dx(dgu, plan.offsets, sw1, sw3, hidden=H,
                                                                        out=dxs))
     kernel_ms = {name: time_kernel(fn, reps) for name, (_, fn) in kernels.items()}
+    if staged:  # the decode pass itself: HBM-bound, the three keys one after another
+        kernel_ms["nf4_dequantize_x3"] = time_kernel(
+            lambda: [ops.nf4_dequantize(w, out=o) for w, o in ((w1, sw1), (w3, sw3), (w2, sw2))], reps)
     kclk = kclocks.stop()
-    top = max(kernel_ms, key=kernel_ms.get)  # the step's dominant kernel
+    top = max(kernels, key=kernel_ms.get)  # the step's dominant GEMM
     top_flops = kernels[top][0]
     del h, y
 
@@ -372,7 +379,7 @@ def run_ours(args, cfg, rank, world, dev):
     peaks = load_peaks()
     achieved = top_flops / (kernel_ms[top] * 1e-3) / 1e12
     fmt = make_weights_fmt(cfg, args)
-    kname = f"{top}_{cfg['fmt']}"
+    kname = f"{top}_{'bf16 (NF4 staged)' if staged else cfg['fmt']}"
     traffic = NCU_TRAFFIC.get(f"{args.config}-{kname}") if not args.int8_rotation else None
     lora_flops = 6.0 * S * LORA_RANK * (H + I)  # rank projection + rank block, fwd and dX, and the factor grads
     step_flops = (12.0 * S * H * I + lora_flops) if train else 6.0 * S * H * I
@@ -396,6 +403,10 @@ def run_ours(args, cfg, rank, world, dev):
                         f"{fmt} experts" + (f", Zipf({cfg['zipf']}) load" if cfg["zipf"] else ""),
             "tokens_per_gpu": T, "hidden": H, "experts": E, "top_k": k, "intermediate": I,
             "weights": fmt, "parallelism": f"dp{world} token-parallel replicas (experts replicated)",
+            **({"nf4_decode": "once per pass into bf16 copies, then the bf16 GEMMs (staging "
+                              f"{args.nf4_staging})" if staged else
+                              f"inside the GEMMs' main loops (staging {args.nf4_staging})"}
+               if cfg["fmt"] == "nf4" else {}),
             "l2": f"no flush: inputs {(T * H * 2 + weight_bytes(cfg)) / 1e6:.0f} MB per step exceed the 126 MB L2",
         },
         "tflops": world * step_flops / (ms * 1e-3) / 1e12,
@@ -1092,6 +1103,10 @@ def main():
     ap.add_argument("--int8-rotation", action="store_true",
                     help="c3: INT8 in the reference's default block-Hadamard format (groups of 256)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nf4-staging", default="auto", choices=["auto", "always", "never"],
+                    help="NF4 experts: decode each key once per pass into bf16 copies for the bf16 GEMMs "
+                         "(always), decode inside the GEMMs (never), or stage training passes with many rows "
+                         "per expert (auto)")
     ap.add_argument("--ep-chunks", type=int, default=2,
                     help="N > 1: token chunks per layer whose exchanges overlap the other chunks' GEMMs")
     ap.add_argument("--ep-free-sms", type=int, default=None,
@@ -1141,8 +1156,9 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     try:
-        from mirai_b200 import _lib
+        from mirai_b200 import _lib, ops
         _lib.load()
+        ops.set_nf4_staging(args.nf4_staging)
         line = run_ep(args, cfg, rank, world, dev) if (world > 1 or cfg.get("layers")) else \
             run_ours(args, cfg, rank, world, dev)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:  # the host-core baseline, N = 1 only

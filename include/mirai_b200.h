@@ -435,6 +435,13 @@ int mirai_nf4_quantize(const void* weight_bf16, int32_t num_experts, int64_t out
  * q = clamp(round_half_even(x / scale), -127, 127).  weight_dtype is
  * MIRAI_DTYPE_F32 or MIRAI_DTYPE_BF16.  The block-Hadamard format
  * (group_size > 0) quantises rows rotated first by mirai_rotate_rows. */
+/* NF4 buffers of one key -> bf16 [E, out, in] (nf4_dequantize_stack, quant.py:380-434; the
+ * chunked_dequant runner's per-chunk dequantisation, experts.py:2148-2240), bit-identical to
+ * the grouped GEMMs' in-loop decode.  packed and out 16-byte aligned. */
+int mirai_nf4_dequantize(const uint8_t* packed, const uint8_t* absmax, const float* nested_absmax,
+                         const float* offset, const float* code, const float* nested_code, int32_t num_experts,
+                         int64_t out_features, int64_t in_features, int32_t blocksize, int32_t nested_blocksize,
+                         void* out_bf16, mirai_stream_t stream);
 int mirai_int8_quantize_rows(const void* weight, int32_t weight_dtype, int64_t rows, int64_t in_features,
                              int8_t* q, float* scale, mirai_stream_t stream);
 

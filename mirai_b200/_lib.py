@@ -126,6 +126,8 @@ SIGNATURES = {
     "mirai_moe_down_dx_lora_int8": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i64, c_i32, c_i32,
                                                    ctypes.POINTER(Int8Weight), c_vp, c_vp, c_vp, c_vp, c_vp]),
     "mirai_nf4_quantize_workspace_bytes": (c_size, [c_i32, c_i64, c_i64]),
+    "mirai_nf4_dequantize": (ctypes.c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_i64, c_i64, c_i32, c_i32,
+                                            c_vp, c_vp]),
     "mirai_nf4_quantize": (ctypes.c_int, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp,
                                           c_vp, c_vp, c_size, c_vp]),
     "mirai_int8_quantize_rows": (ctypes.c_int, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp]),

@@ -1112,10 +1112,13 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
         off[1] = MC::TWO_KEYS ? __ldg(p.q[1].offset + e) : off[0];
       }
       const int absq_row = PAIR ? 0 : kblk;  // absq block of this thread (K-major)
-      for (int kb = 0; kb < total_kb; ++kb, ++gk) {
-        if (gk % KG != grp) continue;
-        const int st = gk % STAGES, rst = gk % RAW_STAGES;
-        const uint32_t ph = (uint32_t)(gk / STAGES) & 1u, rph = (uint32_t)(gk / RAW_STAGES) & 1u;
+      // this group's k-blocks of the tile: positions gk0 + kb with (gk0 + kb) % KG == grp
+      const int gk0 = gk;
+      gk += total_kb;
+      for (int kb = ((grp - gk0) % KG + KG) % KG; kb < total_kb; kb += KG) {
+        const int g = gk0 + kb;
+        const int st = g % STAGES, rst = g % RAW_STAGES;
+        const uint32_t ph = (uint32_t)(g / STAGES) & 1u, rph = (uint32_t)(g / RAW_STAGES) & 1u;
         bool ok = mbar_wait(&sm.raw_full[rst], rph, 40);
         ok = ok && mbar_wait(&sm.empty[st], ph ^ 1, 41);
         if (!ok) {

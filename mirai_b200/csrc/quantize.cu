@@ -105,6 +105,44 @@ __global__ void __launch_bounds__(1024) nf4_nested_kernel(const float* __restric
   }
 }
 
+// NF4 -> bf16 [E, out, in] (nf4_dequantize_stack, quant.py:380-434): one
+// thread per 16 code bytes (32 elements, half an absmax block);
+// w = bf16(code[nibble] * (ncode[q] * nested_absmax + offset)), the same
+// rounding as the grouped GEMMs' in-loop decode.
+__global__ void __launch_bounds__(256) nf4_dequant_kernel(const uint4* __restrict__ packed,
+                                                          const uint8_t* __restrict__ absmax,
+                                                          const float* __restrict__ nested_absmax,
+                                                          const float* __restrict__ offset,
+                                                          const float* __restrict__ code,
+                                                          const float* __restrict__ ncode, int64_t per_expert,
+                                                          int64_t chunks, int nested_bs, int n_nested,
+                                                          uint4* __restrict__ out) {
+  __shared__ float s_code[16], s_ncode[256];
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) s_ncode[i] = ncode[i];
+  if (threadIdx.x < 16) s_code[threadIdx.x] = code[threadIdx.x];
+  __syncthreads();
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= chunks) return;
+  const int64_t cpe = per_expert / 32;
+  const int64_t e = c / cpe;
+  const int64_t blk = (c - e * cpe) >> 1;  // absmax block inside the expert
+  const float nabs = nested_absmax[e * n_nested + blk / nested_bs];
+  const float scale = __fadd_rn(__fmul_rn(s_ncode[absmax[e * (per_expert / 64) + blk]], nabs), offset[e]);
+  const uint4 w = packed[c];
+  const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+  uint32_t o[16];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t byte = (words[i] >> (8 * b)) & 0xFFu;  // first element in the high nibble
+      o[4 * i + b] = pack_bf16x2(__fmul_rn(s_code[byte >> 4], scale), __fmul_rn(s_code[byte & 15u], scale));
+    }
+  uint4* dst = out + c * 4;
+#pragma unroll
+  for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+}
+
 // INT8 per row: scale = max(amax / 127, 1e-30); q = clamp(rint(x / scale), +-127).
 template <typename T>
 __global__ void __launch_bounds__(256) int8_rows_kernel(const T* __restrict__ w, int64_t rows, int64_t in,
@@ -162,6 +200,27 @@ int mirai_nf4_quantize(const void* weight_bf16, int32_t num_experts, int64_t out
   qz::nf4_nested_kernel<<<num_experts, 1024, 0, s>>>(am, bpe, nested_blocksize, n_nested, nested_code, absmax,
                                                       nested_absmax, offset);
   return check_launch("nf4_quantize", 2);
+}
+
+int mirai_nf4_dequantize(const uint8_t* packed, const uint8_t* absmax, const float* nested_absmax,
+                         const float* offset, const float* code, const float* nested_code, int32_t num_experts,
+                         int64_t out_features, int64_t in_features, int32_t blocksize, int32_t nested_blocksize,
+                         void* out_bf16, mirai_stream_t stream) {
+  if (num_experts <= 0 || out_features <= 0 || in_features <= 0)
+    return set_error(MIRAI_ERR_INVALID_ARG, "nf4_dequantize: bad sizes");
+  if (blocksize != 64 || nested_blocksize <= 0)
+    return set_error(MIRAI_ERR_UNSUPPORTED, "nf4_dequantize: blocksize must be 64 (got %d)", blocksize);
+  const int64_t per = out_features * in_features;
+  if (per % 64 != 0) return set_error(MIRAI_ERR_UNSUPPORTED, "nf4_dequantize: out*in must be a multiple of 64");
+  if (!packed || !absmax || !nested_absmax || !offset || !code || !nested_code || !out_bf16 ||
+      (reinterpret_cast<uintptr_t>(packed) & 15u) || (reinterpret_cast<uintptr_t>(out_bf16) & 15u))
+    return set_error(MIRAI_ERR_INVALID_ARG, "nf4_dequantize: null or misaligned pointer");
+  const int64_t chunks = (int64_t)num_experts * (per / 32);
+  const int n_nested = (int)((per / 64 + nested_blocksize - 1) / nested_blocksize);
+  qz::nf4_dequant_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint4*>(packed), absmax, nested_absmax, offset, code, nested_code, per, chunks,
+      nested_blocksize, n_nested, static_cast<uint4*>(out_bf16));
+  return check_launch("nf4_dequantize");
 }
 
 int mirai_int8_quantize_rows(const void* weight, int32_t weight_dtype, int64_t rows, int64_t in_features, int8_t* q,

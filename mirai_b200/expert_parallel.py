@@ -125,6 +125,7 @@ class CudaStepOps:
             return self.ops.permute_rows(y, inverse), ("regrouped", order, inverse, ends, saved)
         w1, w3, w2 = weights
         g_in, g_mid = self.ops._rotations(w1, w3, w2)
+        w1, w3, w2 = self.ops.stage_nf4(weights, x_sorted.shape[0], w1.shape[0], training=save)
         x = self.ops.rotate_rows(x_sorted, g_in) if g_in else x_sorted
         res = self.ops.gateup_swiglu(x, offsets, w1, w3, inter=inter, sources=sources, save_gate_up=save)
         h, gu = res if save else (res, None)
@@ -142,6 +143,7 @@ class CudaStepOps:
         gu, h, low = saved
         w1, w3, w2 = weights
         g_in, g_mid = self.ops._rotations(w1, w3, w2)
+        w1, w3, w2 = self.ops.stage_nf4(weights, grad_y.shape[0], w1.shape[0], training=True)
         glow = None
         if lora is not None:
             glow = self.ops.lora_project(grad_y, offsets, lora, forward=False)

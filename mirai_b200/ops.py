@@ -210,6 +210,19 @@ def nf4_quantize(weight: torch.Tensor, code: torch.Tensor, nested_code: torch.Te
     return NF4Tensor(packed, absmax, nabs, offset, code, nested_code, (E, out_f, in_f), blocksize, nested_blocksize)
 
 
+def nf4_dequantize(w: NF4Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 [E, out, in] of an NF4 key (quant.py:380-434), bit-identical to the
+    values the grouped GEMMs decode in their main loops."""
+    E, out_f, in_f = w.shape
+    if out is None:
+        out = torch.empty((E, out_f, in_f), dtype=torch.bfloat16, device=w.packed.device)
+    _cuda(out, "out", torch.bfloat16)
+    _lib.call("mirai_nf4_dequantize", _ptr(w.packed), _ptr(w.absmax), _ptr(w.nested_absmax), _ptr(w.offset),
+              _ptr(w.code), _ptr(w.nested_code), E, out_f, in_f, w.blocksize, w.nested_blocksize, _ptr(out),
+              _stream())
+    return out
+
+
 def int8_quantize(weight: torch.Tensor, group_size: int = 0) -> Int8Tensor:
     """Symmetric per-output-channel INT8 of a [E, out, in] stack (quant.py:189-235).
 
@@ -669,10 +682,45 @@ class ForwardState:
     rank_a: torch.Tensor | None = None    # [S, 64] LoRA rank block of h (scaled)
 
 
+# NF4 staging: the grouped GEMMs decode NF4 inside their main loops, once per
+# 256-row tile of an expert, and that decode (table lookups on the integer
+# pipe) limits them below the bf16 kernels' rate.  A training step multiplies
+# every expert's weights four times (gate/up and down forward, both dX
+# GEMMs), so with many rows per expert it is faster to decode each key once
+# into a bf16 copy (one HBM pass, bit-identical values) and run the bf16
+# kernels; the copy lives for one pass (the backward decodes again, as the
+# reference's frozen linears do).
+NF4_STAGING_MODES = ("auto", "always", "never")
+_nf4_staging = "auto"
+STAGE_MIN_ROWS_PER_EXPERT = 1024  # "auto": stage when the rows per expert fill at least 4 tiles
+
+
+def set_nf4_staging(mode: str) -> None:
+    """"auto" (default: training passes with at least 1024 rows per expert on
+    average), "always" (every pass, forward-only ones included) or "never"
+    (always decode inside the GEMMs)."""
+    global _nf4_staging
+    if mode not in NF4_STAGING_MODES:
+        raise ValueError(f"NF4 staging mode must be one of {NF4_STAGING_MODES}, not {mode!r}")
+    _nf4_staging = mode
+
+
+def stage_nf4(weights, rows: int, num_experts: int, *, training: bool):
+    """The weights a pass over ``rows`` routed rows should multiply: NF4 keys
+    decoded to bf16 where staging pays (see ``set_nf4_staging``), others as
+    given."""
+    if _nf4_staging == "never" or not any(isinstance(w, NF4Tensor) for w in weights):
+        return tuple(weights)
+    if _nf4_staging == "auto" and not (training and rows >= STAGE_MIN_ROWS_PER_EXPERT * max(1, num_experts)):
+        return tuple(weights)
+    return tuple(nf4_dequantize(w) if isinstance(w, NF4Tensor) else w for w in weights)
+
+
 def moe_forward_train(tokens, top_indices, top_weights, w1, w3, w2, *, num_experts: int, inter: int,
                       out_dtype: torch.dtype | None = None, lora: DownLoRA | None = None):
     """Forward that also returns the state the dX pass consumes."""
     g_in, g_mid = _rotations(w1, w3, w2)
+    w1, w3, w2 = stage_nf4((w1, w3, w2), top_indices.numel(), num_experts, training=True)
     plan = dispatch_plan(top_indices, num_experts)
     xs = permute_rows(rotate_rows(tokens, g_in) if g_in else tokens, plan.sorted_token_indices)
     h, gu = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter, save_gate_up=True)
@@ -693,6 +741,7 @@ def moe_backward_dx(grad_out: torch.Tensor, state: ForwardState, w1, w3, w2, *, 
     grad_out [T, H] -> (dx [T, H], d_top_weights fp32 [T, k])."""
     plan = state.plan
     H = state.y_sorted.shape[1]
+    w1, w3, w2 = stage_nf4((w1, w3, w2), state.y_sorted.shape[0], plan.offsets.numel(), training=True)
     gy, gw = combine_backward(grad_out, state.y_sorted, plan.inverse_order, state.top_weights)
     glow = None
     if lora is not None:

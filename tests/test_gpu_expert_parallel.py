@@ -115,7 +115,8 @@ def test_expert_parallel_equals_single_gpu_layer(fmt, chunks, transport, copy_st
         pytest.skip(f"needs {world} GPUs")
     from mirai_b200.build import build
     build()
-    cfg = (3000, 256, 8, 2, 384, fmt, chunks, transport, copy_streams, regroup, layout)
+    # 1500 tokens per rank: the second ipc call outgrows the first call's 2 MiB-rounded buffers
+    cfg = (1500 * world, 256, 8, 2, 384, fmt, chunks, transport, copy_streams, regroup, layout)
     with mp.Manager() as mgr:
         results = mgr.dict()
         mp.start_processes(_rank_main, args=(world, _free_port(), cfg, results), nprocs=world, start_method="spawn")

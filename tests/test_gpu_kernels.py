@@ -303,6 +303,58 @@ def test_nf4_quantizer_matches_oracle(E, out_f, in_f):
     np.testing.assert_array_equal(got.offset.cpu().numpy(), ref["offset"])
 
 
+@pytest.mark.parametrize("E,out_f,in_f", [(2, 128, 256), (3, 1408, 256), (1, 64, 64), (5, 192, 320)])
+def test_nf4_dequantize_matches_oracle(E, out_f, in_f):
+    """The standalone NF4 decode (the staging pass) equals the reference rule
+    bf16(code[nibble] * (ncode[q] * nested_absmax + offset)) bit for bit."""
+    dev = _dev()
+    from mirai_b200 import ops
+    rng = np.random.default_rng(E * out_f + in_f)
+    g = oq.nf4_quantize_grouped((rng.standard_normal((E, out_f, in_f)) * 0.05).astype(np.float32),
+                                nested_blocksize=256 if out_f * in_f >= 64 * 256 else 16)
+    w = ops.NF4Tensor(torch.from_numpy(g["nf4"]).to(dev), torch.from_numpy(g["absmax"]).to(dev),
+                      torch.from_numpy(g["nabsmax"]).to(dev), torch.from_numpy(g["offset"]).to(dev),
+                      torch.from_numpy(g["code"]).to(dev), torch.from_numpy(g["ncode"]).to(dev), g["shape"],
+                      nested_blocksize=g["nested_blocksize"])
+    got = ops.nf4_dequantize(w)
+    _check(ops)
+    assert got.dtype == torch.bfloat16 and tuple(got.shape) == (E, out_f, in_f)
+    assert np.array_equal(_f32(got), oq.nf4_dequantize_grouped(g))
+
+
+@pytest.mark.parametrize("lora_rank", [0, 16])
+def test_nf4_staged_train_step_equals_in_loop_decode(lora_rank):
+    """A training pass on bf16 copies of the NF4 keys (decoded once) gives the
+    same bits as the GEMMs that decode inside their main loops: the decoded
+    values, the tiles and the accumulation order are the same."""
+    dev = _dev()
+    from mirai_b200 import ops
+    T, H, E, k, I = 2048, 512, 4, 2, 384
+    rng = np.random.default_rng(21)
+    _, dw = _weights("nf4", rng, E, H, I, dev)
+    x = _bf16(rng.standard_normal((T, H)).astype(np.float32)).to(dev)
+    g = _bf16(rng.standard_normal((T, H)).astype(np.float32)).to(dev)
+    idx, w = ops.route_topk(torch.from_numpy((rng.standard_normal((T, E)) * 1.5).astype(np.float32)).to(dev), k)
+    res = {}
+    for mode in ("never", "always"):
+        ops.set_nf4_staging(mode)
+        try:
+            lora = None
+            if lora_rank:
+                gen = torch.Generator(device=dev).manual_seed(3)
+                lora = ops.DownLoRA(torch.randn(E, lora_rank, I, device=dev, generator=gen) * 0.05,
+                                    torch.randn(E, H, lora_rank, device=dev, generator=gen) * 0.05, 2.0,
+                                    compute_grads=True)
+            out, st = ops.moe_forward_train(x, idx, w, *dw, num_experts=E, inter=I, lora=lora)
+            dx, dwt = ops.moe_backward_dx(g, st, *dw, inter=I, lora=lora)
+            res[mode] = (out, dx, dwt) + ((lora.grad_a, lora.grad_b) if lora else ())
+        finally:
+            ops.set_nf4_staging("auto")
+    _check(ops)
+    for a, b in zip(res["never"], res["always"]):
+        assert torch.equal(a, b)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_int8_quantizer_matches_reference_golden(golden, dtype):
     dev = _dev()
