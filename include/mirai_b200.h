@@ -380,6 +380,41 @@ int mirai_moe_down_dx_lora_int8(const void* grad_y, const int32_t* offsets, int3
                                 const void* gate_up, const void* rank_a, const void* rank_b,
                                 void* grad_gate_up, mirai_stream_t stream);
 
+/* The LoRA kernels and the fused rank-block GEMMs over source-major segments
+ * (no counterpart: the reference has no expert parallelism).  offsets holds
+ * num_sources * num_experts running ends, segment s*E + e = source s's rows of
+ * expert e (the layout an expert owner receives); num_sources = 1 is the
+ * entry point without _src.  At most 1024 segments and 64 sources.  A factor
+ * gradient sums each expert's segments in source order. */
+int mirai_moe_lora_project_src(const void* x, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                               int64_t num_rows, int32_t k_dim, const void* factor, int32_t factor_layout,
+                               int32_t rank, float scale, void* out, mirai_stream_t stream);
+int mirai_moe_lora_grad_src(const void* x, const void* g_rank, const int32_t* offsets, int32_t num_sources,
+                            int32_t num_experts, int64_t num_rows, int32_t k_dim, int32_t rank, float* grad,
+                            int64_t stride_e, int64_t stride_r, int64_t stride_k, mirai_stream_t stream);
+int mirai_moe_down_lora_src_bf16(const void* h, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                                 int64_t num_rows, int32_t inter, int32_t hidden, const void* w2,
+                                 const void* rank_a, const void* rank_b, void* y, mirai_stream_t stream);
+int mirai_moe_down_lora_src_nf4(const void* h, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                                int64_t num_rows, int32_t inter, int32_t hidden, const mirai_nf4_weight* w2,
+                                const void* rank_a, const void* rank_b, void* y, mirai_stream_t stream);
+int mirai_moe_down_lora_src_int8(const void* h, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                                 int64_t num_rows, int32_t inter, int32_t hidden, const mirai_int8_weight* w2,
+                                 const void* rank_a, const void* rank_b, void* y, mirai_stream_t stream);
+/* gate_up == NULL: dh = grad_y W2 + the rank block, [S, I], without the SwiGLU backward */
+int mirai_moe_down_dx_lora_src_bf16(const void* grad_y, const int32_t* offsets, int32_t num_sources,
+                                    int32_t num_experts, int64_t num_rows, int32_t hidden, int32_t inter,
+                                    const void* w2, const void* gate_up, const void* rank_a, const void* rank_b,
+                                    void* grad_gate_up, mirai_stream_t stream);
+int mirai_moe_down_dx_lora_src_nf4(const void* grad_y, const int32_t* offsets, int32_t num_sources,
+                                   int32_t num_experts, int64_t num_rows, int32_t hidden, int32_t inter,
+                                   const mirai_nf4_weight* w2, const void* gate_up, const void* rank_a,
+                                   const void* rank_b, void* grad_gate_up, mirai_stream_t stream);
+int mirai_moe_down_dx_lora_src_int8(const void* grad_y, const int32_t* offsets, int32_t num_sources,
+                                    int32_t num_experts, int64_t num_rows, int32_t hidden, int32_t inter,
+                                    const mirai_int8_weight* w2, const void* gate_up, const void* rank_a,
+                                    const void* rank_b, void* grad_gate_up, mirai_stream_t stream);
+
 /* ------------------------------- f4: any weight layout, activation, group count
  * The four grouped GEMMs (gate/up + activation, down, down dX with the
  * activation's backward, gate/up dX) for weights in either layout above and

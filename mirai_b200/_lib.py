@@ -132,6 +132,16 @@ SIGNATURES = {
                                           c_vp, c_vp, c_size, c_vp]),
     "mirai_int8_quantize_rows": (ctypes.c_int, [c_vp, c_i32, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "mirai_rotate_rows": (ctypes.c_int, [c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_i32, c_vp]),
+    "mirai_moe_lora_project_src": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_vp, c_i32, c_i32,
+                                                  c_f32, c_vp, c_vp]),
+    "mirai_moe_lora_grad_src": (ctypes.c_int, [c_vp, c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_i32, c_vp, c_i64,
+                                               c_i64, c_i64, c_vp]),
+    **{f"mirai_moe_down_lora_src_{f}": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_i32, t, c_vp, c_vp,
+                                                       c_vp, c_vp])
+       for f, t in (("bf16", c_vp), ("nf4", ctypes.POINTER(Nf4Weight)), ("int8", ctypes.POINTER(Int8Weight)))},
+    **{f"mirai_moe_down_dx_lora_src_{f}": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_i32, t, c_vp,
+                                                          c_vp, c_vp, c_vp, c_vp])
+       for f, t in (("bf16", c_vp), ("nf4", ctypes.POINTER(Nf4Weight)), ("int8", ctypes.POINTER(Int8Weight)))},
     **{f"mirai_moe_down_dx_src_{f}": (ctypes.c_int, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_i32, t, c_vp, c_vp,
                                                      c_vp])
        for f, t in (("bf16", c_vp), ("nf4", ctypes.POINTER(Nf4Weight)), ("int8", ctypes.POINTER(Int8Weight)))},

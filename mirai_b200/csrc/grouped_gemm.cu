@@ -1801,6 +1801,31 @@ int mirai_moe_down_dx_lora_int8(const void* grad_y, const int32_t* offsets, int3
                      const_cast<void*>(gate_up), wi(w2), wi(w2), hidden, inter, stream, &rb);
 }
 
+// ---- LoRA rank block over source-major segments (the expert-parallel train step
+// on an expert owner; num_sources = 1 equals the entry points above).
+#define MIRAI_LORA_SRC(SUF, WT, WRAP)                                                                          \
+  int mirai_moe_down_lora_src_##SUF(const void* h, const int32_t* offsets, int32_t num_sources,             \
+                                    int32_t num_experts, int64_t num_rows, int32_t inter, int32_t hidden,    \
+                                    WT w2, const void* rank_a, const void* rank_b, void* y,                 \
+                                    mirai_stream_t stream) {                                                 \
+    const RankBlock rb{rank_a, rank_b};                                                                      \
+    return run<DOWN>("down_lora_src_" #SUF, h, offsets, num_experts, num_rows, inter, hidden, y, nullptr,    \
+                     WRAP(w2), WRAP(w2), hidden, inter, stream, &rb, num_sources);                           \
+  }                                                                                                          \
+  int mirai_moe_down_dx_lora_src_##SUF(const void* grad_y, const int32_t* offsets, int32_t num_sources,     \
+                                       int32_t num_experts, int64_t num_rows, int32_t hidden, int32_t inter, \
+                                       WT w2, const void* gate_up, const void* rank_a, const void* rank_b,   \
+                                       void* grad_gate_up, mirai_stream_t stream) {                          \
+    const RankBlock rb{rank_a, rank_b};                                                                      \
+    return run<DXDOWN>("down_dx_lora_src_" #SUF, grad_y, offsets, num_experts, num_rows, hidden, inter,      \
+                       grad_gate_up, const_cast<void*>(gate_up), WRAP(w2), WRAP(w2), hidden, inter, stream,  \
+                       &rb, num_sources, gate_up == nullptr);                                                \
+  }
+MIRAI_LORA_SRC(bf16, const void*, wb)
+MIRAI_LORA_SRC(nf4, const mirai_nf4_weight*, wn)
+MIRAI_LORA_SRC(int8, const mirai_int8_weight*, wi)
+#undef MIRAI_LORA_SRC
+
 // ---- dX: down without the SwiGLU backward: dh = dy W2 [S, I] (+ the rank block).  The rotated
 // INT8 format rotates dh before the SwiGLU backward (mirai_swiglu_backward_rotated).
 int mirai_moe_down_dh_int8(const void* grad_y, const int32_t* offsets, int32_t num_experts, int64_t num_rows,

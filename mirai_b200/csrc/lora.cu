@@ -20,13 +20,19 @@
 // segment's end in its last block are zeroed in shared memory before the MMA
 // so the next expert's rows never enter the sum.  Blocks are summed in row
 // order by one accumulator, so the result is deterministic.
+//
+// Both take the rows as `nsrc` x E segments (source-major: segment s*E + e
+// holds source s's rows of expert e, the layout an expert owner receives in
+// the expert-parallel exchange; nsrc = 1 is one segment per expert).  A
+// gradient CTA walks its expert's segments in source order.
 #include "common.cuh"
 
 namespace mirai {
 namespace lr {
 
 constexpr int kMaxRank = 32;
-constexpr int kMaxExperts = 1024;
+constexpr int kMaxExperts = 1024;     // segments (sources x experts) of one launch
+constexpr int kMaxSources = 64;
 constexpr int kThreads = 128;         // 4 warps: TMA producer, MMA issuer, all four drain TMEM
 constexpr int kStages = 4;
 constexpr int kABytes = 128 * 64 * 2; // 16 KB: 128 rows x 64 k (project) / 2 x [64 rows x 64 cols] (grad)
@@ -83,21 +89,22 @@ __global__ void __launch_bounds__(kThreads) lora_grad_zero_kernel(int K, int ran
 template <int LAYOUT>
 __global__ void __launch_bounds__(kThreads) lora_project_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                                 const __grid_constant__ CUtensorMap tmap_f,
-                                                                const int32_t* __restrict__ offsets, int E, int S,
-                                                                int K, int rank, float scale,
+                                                                const int32_t* __restrict__ offsets, int E, int nsrc,
+                                                                int S, int K, int rank, float scale,
                                                                 __nv_bfloat16* __restrict__ out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = align1024(smem_raw);
   __shared__ Barriers bar;
   __shared__ int tile_prefix[kMaxExperts + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = nsrc * E;  // segments
   if (warp == 0) {
-    // tiles of 128 rows per expert segment, in expert order
+    // tiles of 128 rows per segment, in segment order
     int carry = 0;
-    for (int e0 = 0; e0 < E; e0 += 32) {
+    for (int e0 = 0; e0 < G; e0 += 32) {
       const int e = e0 + lane;
       int cnt = 0;
-      if (e < E) {
+      if (e < G) {
         const int end = offsets[e], beg = e > 0 ? offsets[e - 1] : 0;
         cnt = end > beg ? (end - beg + 127) / 128 : 0;
       }
@@ -107,7 +114,7 @@ __global__ void __launch_bounds__(kThreads) lora_project_kernel(const __grid_con
         const int v = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += v;
       }
-      if (e < E) tile_prefix[e] = carry + incl - cnt;
+      if (e < G) tile_prefix[e] = carry + incl - cnt;
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
     __syncwarp();
@@ -115,17 +122,17 @@ __global__ void __launch_bounds__(kThreads) lora_project_kernel(const __grid_con
       const int t = blockIdx.x;
       bar.tile_e = -1;
       if (t < carry) {
-        int lo = 0, hi = E;
+        int lo = 0, hi = G;
         while (hi - lo > 1) {
           const int mid = (lo + hi) >> 1;
           if (tile_prefix[mid] <= t) lo = mid;
           else hi = mid;
         }
-        // skip experts with no tiles that share the prefix value
-        while (lo + 1 < E && tile_prefix[lo + 1] <= t) ++lo;
+        // skip segments with no tiles that share the prefix value
+        while (lo + 1 < G && tile_prefix[lo + 1] <= t) ++lo;
         const int beg = lo > 0 ? offsets[lo - 1] : 0, end = offsets[lo];
         const int m = t - tile_prefix[lo];
-        bar.tile_e = lo;
+        bar.tile_e = lo % E;  // the segment's expert
         bar.tile_row0 = beg + m * 128;
         bar.tile_rows = min(128, end - (beg + m * 128));
       }
@@ -215,17 +222,25 @@ __global__ void __launch_bounds__(kThreads) lora_project_kernel(const __grid_con
 
 __global__ void __launch_bounds__(kThreads) lora_grad_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                              const __grid_constant__ CUtensorMap tmap_g,
-                                                             const int32_t* __restrict__ offsets, int K, int rank,
-                                                             float* __restrict__ grad, int64_t sE, int64_t sJ,
-                                                             int64_t sK) {
+                                                             const int32_t* __restrict__ offsets, int E, int nsrc,
+                                                             int K, int rank, float* __restrict__ grad, int64_t sE,
+                                                             int64_t sJ, int64_t sK) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles = align1024(smem_raw);
   __shared__ Barriers bar;
+  __shared__ int seg_beg[kMaxSources], seg_end[kMaxSources];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ncb = (K + 127) / 128;
   const int e = blockIdx.x / ncb, cb = blockIdx.x % ncb;
-  const int beg = e > 0 ? offsets[e - 1] : 0, end = offsets[e];
-  const int nb = end > beg ? (end - beg + 63) / 64 : 0;
+  // this expert's segments (one per source), in source order
+  for (int s = threadIdx.x; s < nsrc; s += blockDim.x) {
+    const int j = s * E + e;
+    seg_beg[s] = j > 0 ? offsets[j - 1] : 0;
+    seg_end[s] = offsets[j];
+  }
+  __syncthreads();
+  int nb = 0;
+  for (int s = 0; s < nsrc; ++s) nb += seg_end[s] > seg_beg[s] ? (seg_end[s] - seg_beg[s] + 63) / 64 : 0;
   if (nb == 0) {
     zero_grad_tile(e, cb, K, rank, grad, sE, sJ, sK);
     return;
@@ -244,28 +259,31 @@ __global__ void __launch_bounds__(kThreads) lora_grad_kernel(const __grid_consta
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_x);
     prefetch_tmap(&tmap_g);
-    int b = 0;
+    int b = 0, seg = 0, s0 = seg_beg[0];
     for (; b < nb; ++b) {
+      while (s0 >= seg_end[seg] && seg + 1 < nsrc) s0 = seg_beg[++seg];  // next non-empty segment
       const int st = b % kStages;
       if (b >= kStages && !mbar_wait(&bar.empty[st], ((b / kStages) - 1) & 1, 283)) break;
       uint8_t* a = tiles + st * kStageBytes;
-      const int s0 = beg + 64 * b;
       mbar_arrive_expect_tx(&bar.full[st], kStageBytes);
       tma_load_2d(a, &tmap_x, cb * 128, s0, &bar.full[st]);
       tma_load_2d(a + kABytes / 2, &tmap_x, cb * 128 + 64, s0, &bar.full[st]);
       tma_load_2d(a + kABytes, &tmap_g, 0, s0, &bar.full[st]);
+      s0 += 64;
     }
     if (b < nb) drain_fulls(bar, b);
   } else if (warp == 1) {
     constexpr uint32_t idesc = make_idesc_bf16(128, 64, true, true);
-    int b = 0;
+    int b = 0, seg = 0, s0 = seg_beg[0];
     for (; b < nb; ++b) {
+      while (s0 >= seg_end[seg] && seg + 1 < nsrc) s0 = seg_beg[++seg];
       const int st = b % kStages;
       if (!__all_sync(0xffffffffu, mbar_wait(&bar.full[st], (b / kStages) & 1, 284))) break;
       uint8_t* a = tiles + st * kStageBytes;
-      const int n = min(64, end - (beg + 64 * b));
+      const int n = max(0, min(64, seg_end[seg] - s0));
+      s0 += 64;
       if (n < 64) {
-        // rows n..63 of this block belong to the next expert (or lie past the
+        // rows n..63 of this block belong to the next segment (or lie past the
         // end): zero them in all three 64-row boxes (row r = bytes r*128..+128)
         const uint4 z = make_uint4(0, 0, 0, 0);
         for (int i = n * 8 + lane; i < 64 * 8; i += 32) {
@@ -316,12 +334,14 @@ using namespace mirai;
 
 extern "C" {
 
-int mirai_moe_lora_project(const void* x, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
-                           int32_t k_dim, const void* factor, int32_t factor_layout, int32_t rank, float scale,
-                           void* out, mirai_stream_t stream) {
-  if (num_experts <= 0 || num_experts > lr::kMaxExperts || num_rows < 0 || k_dim <= 0 || k_dim % 8 != 0)
-    return set_error(MIRAI_ERR_INVALID_ARG, "lora_project: bad sizes (E=%d, K=%d; K must be a multiple of 8)",
-                     num_experts, k_dim);
+int mirai_moe_lora_project_src(const void* x, const int32_t* offsets, int32_t num_sources, int32_t num_experts,
+                               int64_t num_rows, int32_t k_dim, const void* factor, int32_t factor_layout,
+                               int32_t rank, float scale, void* out, mirai_stream_t stream) {
+  if (num_experts <= 0 || num_sources <= 0 || num_sources > lr::kMaxSources ||
+      (int64_t)num_sources * num_experts > lr::kMaxExperts || num_rows < 0 || k_dim <= 0 || k_dim % 8 != 0)
+    return set_error(MIRAI_ERR_INVALID_ARG,
+                     "lora_project: bad sizes (sources=%d, E=%d, K=%d; at most %d segments, K a multiple of 8)",
+                     num_sources, num_experts, k_dim, lr::kMaxExperts);
   if (rank <= 0 || rank > lr::kMaxRank)
     return set_error(MIRAI_ERR_UNSUPPORTED, "lora_project: rank %d outside 1..%d", rank, lr::kMaxRank);
   if (factor_layout != lr::kFactorRows && factor_layout != lr::kFactorCols)
@@ -343,22 +363,32 @@ int mirai_moe_lora_project(const void* x, const int32_t* offsets, int32_t num_ex
                       64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int64_t max_tiles = (num_rows + 127) / 128 + num_experts;
+  const int64_t max_tiles = (num_rows + 127) / 128 + (int64_t)num_sources * num_experts;
   auto kern = factor_layout == lr::kFactorRows ? lr::lora_project_kernel<lr::kFactorRows>
                                                : lr::lora_project_kernel<lr::kFactorCols>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lr::kSmemBytes);
   if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "lora_project: %s", cudaGetErrorString(e));
-  kern<<<(unsigned)max_tiles, lr::kThreads, lr::kSmemBytes, s>>>(tx, tf, offsets, num_experts, (int)num_rows, k_dim,
-                                                                 rank, scale, static_cast<__nv_bfloat16*>(out));
+  kern<<<(unsigned)max_tiles, lr::kThreads, lr::kSmemBytes, s>>>(tx, tf, offsets, num_experts, num_sources,
+                                                                 (int)num_rows, k_dim, rank, scale,
+                                                                 static_cast<__nv_bfloat16*>(out));
   return check_launch("lora_project");
 }
 
-int mirai_moe_lora_grad(const void* x, const void* g_rank, const int32_t* offsets, int32_t num_experts,
-                        int64_t num_rows, int32_t k_dim, int32_t rank, float* grad, int64_t stride_e,
-                        int64_t stride_r, int64_t stride_k, mirai_stream_t stream) {
-  if (num_experts <= 0 || num_experts > lr::kMaxExperts || num_rows < 0 || k_dim <= 0 || k_dim % 8 != 0)
-    return set_error(MIRAI_ERR_INVALID_ARG, "lora_grad: bad sizes (E=%d, K=%d; K must be a multiple of 8)",
-                     num_experts, k_dim);
+int mirai_moe_lora_project(const void* x, const int32_t* offsets, int32_t num_experts, int64_t num_rows,
+                           int32_t k_dim, const void* factor, int32_t factor_layout, int32_t rank, float scale,
+                           void* out, mirai_stream_t stream) {
+  return mirai_moe_lora_project_src(x, offsets, 1, num_experts, num_rows, k_dim, factor, factor_layout, rank, scale,
+                                    out, stream);
+}
+
+int mirai_moe_lora_grad_src(const void* x, const void* g_rank, const int32_t* offsets, int32_t num_sources,
+                            int32_t num_experts, int64_t num_rows, int32_t k_dim, int32_t rank, float* grad,
+                            int64_t stride_e, int64_t stride_r, int64_t stride_k, mirai_stream_t stream) {
+  if (num_experts <= 0 || num_sources <= 0 || num_sources > lr::kMaxSources ||
+      (int64_t)num_sources * num_experts > lr::kMaxExperts || num_rows < 0 || k_dim <= 0 || k_dim % 8 != 0)
+    return set_error(MIRAI_ERR_INVALID_ARG,
+                     "lora_grad: bad sizes (sources=%d, E=%d, K=%d; at most %d segments, K a multiple of 8)",
+                     num_sources, num_experts, k_dim, lr::kMaxExperts);
   if (rank <= 0 || rank > lr::kMaxRank)
     return set_error(MIRAI_ERR_UNSUPPORTED, "lora_grad: rank %d outside 1..%d", rank, lr::kMaxRank);
   if (num_rows >= ((int64_t)1 << 31))
@@ -385,8 +415,15 @@ int mirai_moe_lora_grad(const void* x, const void* g_rank, const int32_t* offset
       cudaFuncSetAttribute(lr::lora_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lr::kSmemBytes);
   if (e != cudaSuccess) return set_error(MIRAI_ERR_CUDA, "lora_grad: %s", cudaGetErrorString(e));
   lr::lora_grad_kernel<<<(unsigned)(ncb * num_experts), lr::kThreads, lr::kSmemBytes, s>>>(
-      tx, tg, offsets, k_dim, rank, grad, stride_e, stride_r, stride_k);
+      tx, tg, offsets, num_experts, num_sources, k_dim, rank, grad, stride_e, stride_r, stride_k);
   return check_launch("lora_grad");
+}
+
+int mirai_moe_lora_grad(const void* x, const void* g_rank, const int32_t* offsets, int32_t num_experts,
+                        int64_t num_rows, int32_t k_dim, int32_t rank, float* grad, int64_t stride_e,
+                        int64_t stride_r, int64_t stride_k, mirai_stream_t stream) {
+  return mirai_moe_lora_grad_src(x, g_rank, offsets, 1, num_experts, num_rows, k_dim, rank, grad, stride_e,
+                                 stride_r, stride_k, stream);
 }
 
 }  // extern "C"

@@ -102,34 +102,23 @@ class CudaStepOps:
     def experts(self, x_sorted, offsets, weights, inter, sources=1):
         return self.experts_train(x_sorted, offsets, weights, inter, sources, save=False)[0]
 
-    @staticmethod
-    def _regroup(offsets, sources, total):
-        """Expert-major order of ``total`` source-major rows, from the segment
-        ends on the device (no host read): (order, inverse, expert-major ends)."""
-        E = offsets.numel() // sources
-        ends = offsets.to(torch.int64)
-        L = (ends - torch.cat([ends.new_zeros(1), ends[:-1]])).view(sources, E)
-        order, inverse = regroup_order(L, total)
-        return order, inverse, torch.cumsum(L.sum(0), 0).to(torch.int32)
+    def stage(self, weights, rows, training):
+        """The weights a layer's owner GEMMs multiply over ``rows`` received rows
+        (NF4 keys decoded once to bf16 where that pays: ``ops.stage_nf4``)."""
+        return self.ops.stage_nf4(tuple(weights), rows, weights[0].shape[0], training=training)
 
     def experts_train(self, x_sorted, offsets, weights, inter, sources=1, save=True, lora=None):
-        """The owner's GEMMs; the block-Hadamard INT8 format rotates the received
-        rows and h here (a row's rotation does not depend on where it runs).
-        With a LoRA adapter on w2 (this rank's experts' factors) the received
-        rows are regrouped expert-major first, so the rank-block kernels see one
-        segment per expert; the rows, and so the products, are unchanged."""
-        if lora is not None and sources > 1:
-            order, inverse, ends = self._regroup(offsets, sources, x_sorted.shape[0])
-            y, saved = self.experts_train(self.ops.permute_rows(x_sorted, order), ends, weights, inter, 1, save,
-                                          lora)
-            return self.ops.permute_rows(y, inverse), ("regrouped", order, inverse, ends, saved)
+        """The owner's GEMMs over its received (source, expert) segments; the
+        block-Hadamard INT8 format rotates the received rows and h here (a row's
+        rotation does not depend on where it runs).  A LoRA adapter on w2 (this
+        rank's experts' factors) runs on the same segments: its projections and
+        rank blocks read each segment's expert."""
         w1, w3, w2 = weights
         g_in, g_mid = self.ops._rotations(w1, w3, w2)
-        w1, w3, w2 = self.ops.stage_nf4(weights, x_sorted.shape[0], w1.shape[0], training=save)
         x = self.ops.rotate_rows(x_sorted, g_in) if g_in else x_sorted
         res = self.ops.gateup_swiglu(x, offsets, w1, w3, inter=inter, sources=sources, save_gate_up=save)
         h, gu = res if save else (res, None)
-        low = self.ops.lora_project(h, offsets, lora, forward=True) if lora is not None else None
+        low = self.ops.lora_project(h, offsets, lora, forward=True, sources=sources) if lora is not None else None
         y = self.ops.down(self.ops.rotate_rows(h, g_mid) if g_mid else h, offsets, w2, hidden=x_sorted.shape[1],
                           sources=sources, lora=lora, rank_a=low)
         keep = lora is not None and lora.compute_grads
@@ -143,22 +132,23 @@ class CudaStepOps:
         gu, h, low = saved
         w1, w3, w2 = weights
         g_in, g_mid = self.ops._rotations(w1, w3, w2)
-        w1, w3, w2 = self.ops.stage_nf4(weights, grad_y.shape[0], w1.shape[0], training=True)
         glow = None
         if lora is not None:
-            glow = self.ops.lora_project(grad_y, offsets, lora, forward=False)
+            glow = self.ops.lora_project(grad_y, offsets, lora, forward=False, sources=sources)
             if lora.compute_grads:  # this chunk's share of the factor gradients, added up over chunks
                 E, Hb, r = lora.b.shape
                 Ia = lora.a.shape[2]
                 ga = self.ops.lora_grad(h, glow, offsets, r, torch.empty((E, r, Ia), dtype=torch.float32,
-                                                                         device=grad_y.device), (r * Ia, Ia, 1))
+                                                                         device=grad_y.device), (r * Ia, Ia, 1),
+                                        sources=sources)
                 gb = self.ops.lora_grad(grad_y, low, offsets, r, torch.empty((E, Hb, r), dtype=torch.float32,
-                                                                             device=grad_y.device), (Hb * r, 1, r))
+                                                                             device=grad_y.device), (Hb * r, 1, r),
+                                        sources=sources)
                 lora.grad_a = ga if lora.grad_a is None else lora.grad_a + ga
                 lora.grad_b = gb if lora.grad_b is None else lora.grad_b + gb
         if g_mid:
-            dh = (self.ops.down_dx(grad_y, offsets, w2, None, inter=inter, sources=sources) if sources > 1
-                  else self.ops.down_dh(grad_y, offsets, w2, inter=inter, lora=lora, rank_a=glow))
+            dh = (self.ops.down_dx(grad_y, offsets, w2, None, inter=inter, sources=sources, lora=lora, rank_a=glow)
+                  if sources > 1 else self.ops.down_dh(grad_y, offsets, w2, inter=inter, lora=lora, rank_a=glow))
             dgu = self.ops.swiglu_backward_rotated(dh, gu, g_mid)
         else:
             dgu = self.ops.down_dx(grad_y, offsets, w2, gu, inter=inter, sources=sources, lora=lora, rank_a=glow)
@@ -188,6 +178,22 @@ class EPTrainState:
     top_k: int
     hidden: int
     dtype: torch.dtype
+    staged: tuple | None = None  # (the local NF4 keys, their bf16 copies) when the forward staged them
+
+
+def _stage(ops, weights, rows: int, training: bool):
+    """(weights the owner's GEMMs multiply, (keys, copies) or None): NF4 keys
+    decoded once per layer where that pays (``CudaStepOps.stage``)."""
+    f = getattr(ops, "stage", None)
+    staged = tuple(weights) if f is None else f(weights, rows, training)
+    return staged, ((tuple(weights), staged) if staged[0] is not weights[0] else None)
+
+
+def _weights_for(staged, local_weights):
+    """The forward's bf16 copies when the backward gets the same keys."""
+    if staged is not None and all(a is b for a, b in zip(staged[0], local_weights)):
+        return staged[1]
+    return local_weights
 
 
 def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: Any, *, shard: ExpertShard,
@@ -227,10 +233,11 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
         if not train:
             y = ops.experts(xs, plan.offsets, local_weights, inter)
             return ops.combine(y, plan.inverse_order, tw, top_k, tokens.dtype)
-        y, saved = ops.experts_train(xs, plan.offsets, local_weights, inter, **({"lora": lora} if lora else {}))
+        wts, staged = _stage(ops, local_weights, xs.shape[0], True)
+        y, saved = ops.experts_train(xs, plan.offsets, wts, inter, **({"lora": lora} if lora else {}))
         out = ops.combine(y, plan.inverse_order, tw, top_k, tokens.dtype)
         return out, EPTrainState([(0, T)], [dict(tw=tw, plan=plan, y_back=y, sc=None, rc=None, offs=plan.offsets,
-                                                 saved=saved)], top_k, H, tokens.dtype)
+                                                 saved=saved)], top_k, H, tokens.dtype, staged)
     C = max(1, int(chunks))
     bounds = [((T * c) // C, (T * (c + 1)) // C) for c in range(C)]
     # ---- per chunk, on the current stream: route, plan, permute
@@ -311,10 +318,11 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
     out = torch.empty((T, H), dtype=tokens.dtype, device=dev)
     if train:
         state = []
+        wts, staged = _stage(ops, local_weights, sum(sum(r) for r in rc), True)
         for c, (b, e) in enumerate(bounds):
             x_recv = dispatch(c)
             if x_recv.shape[0]:
-                y_recv, saved = ops.experts_train(x_recv, offs_dev[c], local_weights, inter, sources=G,
+                y_recv, saved = ops.experts_train(x_recv, offs_dev[c], wts, inter, sources=G,
                                                   **({"lora": lora} if lora else {}))
             else:
                 y_recv, saved = torch.empty((0, H), dtype=x_recv.dtype, device=dev), None
@@ -323,7 +331,7 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
                 out[b:e] = ops.combine(y_back, prep[c][1].inverse_order, prep[c][0], top_k, tokens.dtype)
             state.append(dict(tw=prep[c][0], plan=prep[c][1], y_back=y_back, sc=sc[c], rc=rc[c], offs=offs_dev[c],
                               saved=saved))
-        return out, EPTrainState(bounds, state, top_k, H, tokens.dtype)
+        return out, EPTrainState(bounds, state, top_k, H, tokens.dtype, staged)
     if comm is None:
         for c, (b, e) in enumerate(bounds):
             y_back = give_back(c, compute(c, dispatch(c)))
@@ -371,6 +379,8 @@ def ep_moe_backward(grad_out: torch.Tensor, state: EPTrainState, local_weights: 
     dev = grad_out.device
     dx = torch.empty((T, H), dtype=state.dtype, device=dev)
     dw = torch.empty((T, k), dtype=torch.float32, device=dev)
+    local_weights = _weights_for(state.staged, local_weights)
+    state.staged = None
     for (b, e), st in zip(state.bounds, state.chunks):
         plan = st["plan"]
         if e > b:
@@ -832,6 +842,9 @@ class ExpertParallelMoE:
             mark(f"dispatch copies + arrival, chunk {c}", comm)
         returned, saved = [], []
         kw = {"lora": lora} if lora is not None else {}
+        staged = None
+        if train:
+            local_weights, staged = _stage(ops, local_weights, sum(plan.in_rows), True)
         for c in range(C):
             ex.wait(landed[c])
             rows_c = plan.in_rows[c]
@@ -878,7 +891,7 @@ class ExpertParallelMoE:
         return out, IPCTrainState(gen=self._gen, bounds=bounds, prep=[(p[0], p[1]) for p in prep], plan=plan,
                                   offs=offs_dev, saved=saved, y_back=y_back, x_in=x_in, dx_ret=dx_ret,
                                   ptrs=list(ptrs), data=data, ret2=[p + in_cap + ret_cap for p in data],
-                                  row_bytes=row_bytes, top_k=k, hidden=H, dtype=tokens.dtype)
+                                  row_bytes=row_bytes, top_k=k, hidden=H, dtype=tokens.dtype, staged=staged)
 
     def backward(self, grad_out: torch.Tensor, state: "IPCTrainState", local_weights: Any, *,
                  lora=None) -> tuple[torch.Tensor, torch.Tensor]:
@@ -907,6 +920,8 @@ class ExpertParallelMoE:
         ex = _Exchange(self, state.ptrs, comp)
         dx = torch.empty((T, H), dtype=state.dtype, device=dev)
         dw = torch.empty((T, k), dtype=torch.float32, device=dev)
+        local_weights = _weights_for(state.staged, local_weights)
+        state.staged = None
         sent = []
         for c, (b, e) in enumerate(state.bounds):
             tw, dplan = state.prep[c]
@@ -998,3 +1013,4 @@ class IPCTrainState:
     top_k: int
     hidden: int
     dtype: torch.dtype
+    staged: tuple | None = None  # (the local NF4 keys, their bf16 copies) when the forward staged them

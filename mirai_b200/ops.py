@@ -336,10 +336,16 @@ def down(h: torch.Tensor, offsets: torch.Tensor, w2, *, hidden: int, out: torch.
     S, I = h.shape
     y = out if out is not None else torch.empty((S, hidden), dtype=torch.bfloat16, device=h.device)
     if sources > 1:
-        if lora is not None or offsets.numel() % sources:
-            raise ValueError("source-major segments: no adapter, offsets a multiple of sources")
-        _lib.call(f"mirai_moe_down_src_{_fmt_suffix(w2)}", _ptr(h), _ptr(offsets), sources, offsets.numel() // sources,
-                  S, I, hidden, _wptr(w2), _ptr(y), _stream())
+        if offsets.numel() % sources:
+            raise ValueError("source-major segments: offsets must be a multiple of sources")
+        E = offsets.numel() // sources
+        if lora is None:
+            _lib.call(f"mirai_moe_down_src_{_fmt_suffix(w2)}", _ptr(h), _ptr(offsets), sources, E, S, I, hidden,
+                      _wptr(w2), _ptr(y), _stream())
+            return y
+        low = rank_a if rank_a is not None else lora_project(h, offsets, lora, forward=True, sources=sources)
+        _lib.call(f"mirai_moe_down_lora_src_{_fmt_suffix(w2)}", _ptr(h), _ptr(offsets), sources, E, S, I, hidden,
+                  _wptr(w2), _ptr(low), _ptr(lora.b_pad()), _ptr(y), _stream())
         return y
     E = offsets.numel()
     if lora is None:
@@ -423,16 +429,20 @@ class DownLoRA:
 LORA_FACTOR_ROWS, LORA_FACTOR_COLS = 0, 1
 
 
-def lora_project(x: torch.Tensor, offsets: torch.Tensor, lora: DownLoRA, *, forward: bool) -> torch.Tensor:
+def lora_project(x: torch.Tensor, offsets: torch.Tensor, lora: DownLoRA, *, forward: bool,
+                 sources: int = 1) -> torch.Tensor:
     """[S, 64] bf16 rank-block operand bf16(scale * x F_e^T), zero past the rank:
-    F = A ([E, r, I], x = h) when ``forward``, else B^T ([E, H, r], x = grad_y)."""
+    F = A ([E, r, I], x = h) when ``forward``, else B^T ([E, H, r], x = grad_y).
+    ``sources`` > 1: source-major segments (offsets [sources * E])."""
     x = _cuda(x, "x", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
     S, K = x.shape
     out = torch.empty((S, 64), dtype=torch.bfloat16, device=x.device)
     factor, layout = (lora.a_pad(), LORA_FACTOR_ROWS) if forward else (lora.b_pad(), LORA_FACTOR_COLS)
-    _lib.call("mirai_moe_lora_project", _ptr(x), _ptr(offsets), offsets.numel(), S, K, _ptr(factor), layout,
-              int(lora.rank), float(lora.scale), _ptr(out), _stream())
+    if offsets.numel() % sources:
+        raise ValueError("source-major segments: offsets must be a multiple of sources")
+    _lib.call("mirai_moe_lora_project_src", _ptr(x), _ptr(offsets), int(sources), offsets.numel() // sources, S, K,
+              _ptr(factor), layout, int(lora.rank), float(lora.scale), _ptr(out), _stream())
     return out
 
 
@@ -504,18 +514,27 @@ def down_dx(grad_y: torch.Tensor, offsets: torch.Tensor, w2, gate_up: torch.Tens
     (+ the LoRA path's input gradient when ``lora``).  ``sources`` > 1:
     source-major segments (an expert owner's rows); there ``gate_up=None``
     returns dh [S, I] itself."""
+    group = getattr(w2, "group_size", 0)  # block-Hadamard INT8: the rotation group of dh
     w2 = _as_weight(w2)
     gy = _cuda(grad_y, "grad_y", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
     S, H = gy.shape
     if sources > 1:
-        if lora is not None or offsets.numel() % sources:
-            raise ValueError("source-major segments: no adapter, offsets a multiple of sources")
+        if offsets.numel() % sources:
+            raise ValueError("source-major segments: offsets must be a multiple of sources")
+        E = offsets.numel() // sources
         gu = None if gate_up is None else _cuda(gate_up, "gate_up", torch.bfloat16)
         width = inter if gu is None else 2 * inter
         dgu = out if out is not None else torch.empty((S, width), dtype=torch.bfloat16, device=gy.device)
-        _lib.call(f"mirai_moe_down_dx_src_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), sources,
-                  offsets.numel() // sources, S, H, inter, _wptr(w2), _ptr(gu), _ptr(dgu), _stream())
+        if lora is None:
+            _lib.call(f"mirai_moe_down_dx_src_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), sources, E, S, H, inter,
+                      _wptr(w2), _ptr(gu), _ptr(dgu), _stream())
+            return dgu
+        glow = rank_a if rank_a is not None else lora_project(gy, offsets, lora, forward=False, sources=sources)
+        # dh alone in the block-Hadamard INT8 format is rotated afterwards: its A factor is rotated too
+        rot = group if gu is None else 0
+        _lib.call(f"mirai_moe_down_dx_lora_src_{_fmt_suffix(w2)}", _ptr(gy), _ptr(offsets), sources, E, S, H, inter,
+                  _wptr(w2), _ptr(gu), _ptr(glow), _ptr(lora.a_pad(rotation=rot)), _ptr(dgu), _stream())
         return dgu
     gu = _cuda(gate_up, "gate_up", torch.bfloat16)
     dgu = out if out is not None else torch.empty((S, 2 * inter), dtype=torch.bfloat16, device=gy.device)
@@ -551,15 +570,19 @@ def down_dh(grad_y: torch.Tensor, offsets: torch.Tensor, w2: Int8Tensor, *, inte
 
 
 def lora_grad(x: torch.Tensor, g_rank: torch.Tensor, offsets: torch.Tensor, rank: int, out: torch.Tensor,
-              strides) -> torch.Tensor:
-    """out[e][j][k] = sum over segment e of g_rank[s, j] * x[s, k] (fp32, by strides)."""
+              strides, sources: int = 1) -> torch.Tensor:
+    """out[e][j][k] = sum over the rows of expert e of g_rank[s, j] * x[s, k]
+    (fp32, by strides); ``sources`` > 1: source-major segments, summed in
+    source order."""
     x = _cuda(x, "x", torch.bfloat16)
     g = _cuda(g_rank, "g_rank", torch.bfloat16)
     offsets = _cuda(offsets, "offsets", torch.int32)
     S, K = x.shape
     se, sr, sk = (int(v) for v in strides)
-    _lib.call("mirai_moe_lora_grad", _ptr(x), _ptr(g), _ptr(offsets), offsets.numel(), S, K, int(rank), _ptr(out),
-              se, sr, sk, _stream())
+    if offsets.numel() % sources:
+        raise ValueError("source-major segments: offsets must be a multiple of sources")
+    _lib.call("mirai_moe_lora_grad_src", _ptr(x), _ptr(g), _ptr(offsets), int(sources), offsets.numel() // sources,
+              S, K, int(rank), _ptr(out), se, sr, sk, _stream())
     return out
 
 
@@ -680,6 +703,7 @@ class ForwardState:
     top_weights: torch.Tensor
     h: torch.Tensor | None = None         # [S, I] bf16, kept when LoRA factor grads are wanted
     rank_a: torch.Tensor | None = None    # [S, 64] LoRA rank block of h (scaled)
+    staged: tuple | None = None           # (the NF4 keys, their bf16 copies) when the forward staged them
 
 
 # NF4 staging: the grouped GEMMs decode NF4 inside their main loops, once per
@@ -688,8 +712,10 @@ class ForwardState:
 # every expert's weights four times (gate/up and down forward, both dX
 # GEMMs), so with many rows per expert it is faster to decode each key once
 # into a bf16 copy (one HBM pass, bit-identical values) and run the bf16
-# kernels; the copy lives for one pass (the backward decodes again, as the
-# reference's frozen linears do).
+# kernels.  The training forward keeps its copies in the state it returns and
+# the backward multiplies them again (the reference's frozen linears decode a
+# second time instead); they are freed with the state, so a layer holds
+# 2 bytes per expert weight from its forward until its backward.
 NF4_STAGING_MODES = ("auto", "always", "never")
 _nf4_staging = "auto"
 STAGE_MIN_ROWS_PER_EXPERT = 1024  # "auto": stage when the rows per expert fill at least 4 tiles
@@ -720,7 +746,9 @@ def moe_forward_train(tokens, top_indices, top_weights, w1, w3, w2, *, num_exper
                       out_dtype: torch.dtype | None = None, lora: DownLoRA | None = None):
     """Forward that also returns the state the dX pass consumes."""
     g_in, g_mid = _rotations(w1, w3, w2)
-    w1, w3, w2 = stage_nf4((w1, w3, w2), top_indices.numel(), num_experts, training=True)
+    keys = (w1, w3, w2)
+    w1, w3, w2 = stage_nf4(keys, top_indices.numel(), num_experts, training=True)
+    staged = (keys, (w1, w3, w2)) if w1 is not keys[0] else None
     plan = dispatch_plan(top_indices, num_experts)
     xs = permute_rows(rotate_rows(tokens, g_in) if g_in else tokens, plan.sorted_token_indices)
     h, gu = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter, save_gate_up=True)
@@ -731,7 +759,7 @@ def moe_forward_train(tokens, top_indices, top_weights, w1, w3, w2, *, num_exper
              rank_a=low)
     out = combine(y, plan.inverse_order, top_weights, out_dtype=out_dtype or tokens.dtype)
     keep = lora is not None and lora.compute_grads
-    return out, ForwardState(plan, y, gu, top_weights.float(), h if keep else None, low if keep else None)
+    return out, ForwardState(plan, y, gu, top_weights.float(), h if keep else None, low if keep else None, staged)
 
 
 def moe_backward_dx(grad_out: torch.Tensor, state: ForwardState, w1, w3, w2, *, inter: int,
@@ -741,7 +769,11 @@ def moe_backward_dx(grad_out: torch.Tensor, state: ForwardState, w1, w3, w2, *, 
     grad_out [T, H] -> (dx [T, H], d_top_weights fp32 [T, k])."""
     plan = state.plan
     H = state.y_sorted.shape[1]
-    w1, w3, w2 = stage_nf4((w1, w3, w2), state.y_sorted.shape[0], plan.offsets.numel(), training=True)
+    if state.staged is not None and all(a is b for a, b in zip(state.staged[0], (w1, w3, w2))):
+        w1, w3, w2 = state.staged[1]  # the forward's bf16 copies of these NF4 keys
+        state.staged = None
+    else:
+        w1, w3, w2 = stage_nf4((w1, w3, w2), state.y_sorted.shape[0], plan.offsets.numel(), training=True)
     gy, gw = combine_backward(grad_out, state.y_sorted, plan.inverse_order, state.top_weights)
     glow = None
     if lora is not None:

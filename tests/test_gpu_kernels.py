@@ -671,6 +671,53 @@ def test_source_major_segments_equal_expert_major(fmt):
     assert torch.equal(y_src[pd], y_exp)
 
 
+@pytest.mark.parametrize("fmt", ["nf4", "bf16"])
+def test_source_major_lora_equals_expert_major(fmt):
+    """The LoRA kernels and the rank-block GEMMs over source-major segments
+    (forward rank block, fused down, down dX with the SwiGLU backward, the
+    factor gradients) against the same rows grouped by expert: row products
+    exactly equal; factor gradients, which sum an expert's rows in 64-row
+    blocks that start anew at each source, to fp32 rounding."""
+    dev = _dev()
+    from mirai_b200 import ops
+    G, E, H, I, r = 3, 4, 256, 384, 16
+    rng = np.random.default_rng(5 + len(fmt))
+    counts = rng.integers(0, 260, size=(G, E))
+    counts[0, 1] = 0
+    counts[2, 3] = 300
+    R = int(counts.sum())
+    _, dw = _weights(fmt, rng, E, H, I, dev)
+    x = torch.randn(R, H, device=dev).to(torch.bfloat16)
+    gy = torch.randn(R, H, device=dev).to(torch.bfloat16)
+    gen = torch.Generator(device=dev).manual_seed(9)
+    lora = ops.DownLoRA(torch.randn(E, r, I, device=dev, generator=gen) * 0.05,
+                        torch.randn(E, H, r, device=dev, generator=gen) * 0.05, 2.0)
+    ends = np.cumsum(counts.reshape(-1)).astype(np.int32)
+    starts = np.concatenate([[0], ends[:-1]])
+    perm = torch.from_numpy(np.concatenate([np.arange(starts[s * E + e], ends[s * E + e])
+                                            for e in range(E) for s in range(G)])).to(dev)
+    off_src = torch.from_numpy(ends).to(dev)
+    off_exp = torch.from_numpy(np.cumsum(counts.sum(0)).astype(np.int32)).to(dev)
+
+    def run(xx, gg, offs, sources):
+        h, gu = ops.gateup_swiglu(xx, offs, dw[0], dw[1], inter=I, sources=sources, save_gate_up=True)
+        low = ops.lora_project(h, offs, lora, forward=True, sources=sources)
+        y = ops.down(h, offs, dw[2], hidden=H, lora=lora, rank_a=low, sources=sources)
+        glow = ops.lora_project(gg, offs, lora, forward=False, sources=sources)
+        dgu = ops.down_dx(gg, offs, dw[2], gu, inter=I, lora=lora, rank_a=glow, sources=sources)
+        ga = ops.lora_grad(h, glow, offs, r, torch.empty((E, r, I), device=dev), (r * I, I, 1), sources=sources)
+        gb = ops.lora_grad(gg, low, offs, r, torch.empty((E, H, r), device=dev), (H * r, 1, r), sources=sources)
+        return low, y, glow, dgu, ga, gb
+
+    src = run(x, gy, off_src, G)
+    exp = run(x[perm], gy[perm], off_exp, 1)
+    _check(ops)
+    for a, b in zip(src[:4], exp[:4]):
+        assert torch.equal(a[perm], b)
+    for a, b in zip(src[4:], exp[4:]):
+        assert float((a - b).abs().max() / b.abs().max()) < 1e-5
+
+
 def test_exchange_wait_gives_up_and_reports_a_timeout():
     """A peer that never signals (a flag nothing sets): the exchange's arrival
     wait gives up after its 2 s limit, records MIRAI_ERR_DEVICE_TIMEOUT with the
