@@ -115,21 +115,22 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(const uint32_t* __rest
                                                           const float* __restrict__ nested_absmax,
                                                           const float* __restrict__ offset,
                                                           const float* __restrict__ code,
-                                                          const float* __restrict__ ncode, int64_t per_expert,
-                                                          int64_t chunks, int nested_bs, int n_nested,
-                                                          uint4* __restrict__ out) {
+                                                          const float* __restrict__ ncode, int per_expert,
+                                                          int nested_bs, int n_nested, uint4* __restrict__ out) {
   __shared__ float s_code[16], s_ncode[256];
   for (int i = threadIdx.x; i < 256; i += blockDim.x) s_ncode[i] = ncode[i];
   if (threadIdx.x < 16) s_code[threadIdx.x] = code[threadIdx.x];
   __syncthreads();
-  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // 8-element chunk
-  if (c >= chunks) return;
-  const int64_t cpe = per_expert / 8;
-  const int64_t e = c / cpe;
-  const int64_t blk = (c - e * cpe) >> 3;  // absmax block inside the expert
-  const float nabs = __ldg(nested_absmax + e * n_nested + blk / nested_bs);
+  // grid: x = 256-chunk blocks of one expert, y = expert (no 64-bit division per thread)
+  const int e = blockIdx.y;
+  const int cl = blockIdx.x * blockDim.x + threadIdx.x;  // 8-element chunk inside the expert
+  if (cl >= per_expert / 8) return;
+  const int blk = cl >> 3;  // absmax block inside the expert
+  const int nb = (nested_bs & (nested_bs - 1)) == 0 ? blk >> (31 - __clz(nested_bs)) : blk / nested_bs;
+  const float nabs = __ldg(nested_absmax + (int64_t)e * n_nested + nb);
   const float scale =
-      __fadd_rn(__fmul_rn(s_ncode[__ldg(absmax + e * (per_expert / 64) + blk)], nabs), __ldg(offset + e));
+      __fadd_rn(__fmul_rn(s_ncode[__ldg(absmax + (int64_t)e * (per_expert / 64) + blk)], nabs), __ldg(offset + e));
+  const int64_t c = (int64_t)e * (per_expert / 8) + cl;
   const uint32_t w = packed[c];
   uint32_t o[4];
 #pragma unroll
@@ -209,13 +210,15 @@ int mirai_nf4_dequantize(const uint8_t* packed, const uint8_t* absmax, const flo
     return set_error(MIRAI_ERR_UNSUPPORTED, "nf4_dequantize: blocksize must be 64 (got %d)", blocksize);
   const int64_t per = out_features * in_features;
   if (per % 64 != 0) return set_error(MIRAI_ERR_UNSUPPORTED, "nf4_dequantize: out*in must be a multiple of 64");
+  if (per >= ((int64_t)1 << 31) || num_experts > 65535)
+    return set_error(MIRAI_ERR_UNSUPPORTED, "nf4_dequantize: at most 2^31 elements per expert and 65535 experts");
   if (!packed || !absmax || !nested_absmax || !offset || !code || !nested_code || !out_bf16 ||
       (reinterpret_cast<uintptr_t>(packed) & 15u) || (reinterpret_cast<uintptr_t>(out_bf16) & 15u))
     return set_error(MIRAI_ERR_INVALID_ARG, "nf4_dequantize: null or misaligned pointer");
-  const int64_t chunks = (int64_t)num_experts * (per / 8);
   const int n_nested = (int)((per / 64 + nested_blocksize - 1) / nested_blocksize);
-  qz::nf4_dequant_kernel<<<(unsigned)((chunks + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const uint32_t*>(packed), absmax, nested_absmax, offset, code, nested_code, per, chunks,
+  const dim3 grid((unsigned)((per / 8 + 255) / 256), (unsigned)num_experts);
+  qz::nf4_dequant_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint32_t*>(packed), absmax, nested_absmax, offset, code, nested_code, (int)per,
       nested_blocksize, n_nested, static_cast<uint4*>(out_bf16));
   return check_launch("nf4_dequantize");
 }

@@ -10,7 +10,6 @@ experts without rows must not break the collective.
 """
 
 import os
-import socket
 import types
 
 import numpy as np
@@ -109,9 +108,8 @@ def _problem(T, H, E, k, I, seed):
     return x, logits, ws
 
 
-def _rank_main(rank, world, port, cfg, results):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+def _rank_main(rank, world, rdv, cfg, results):
+    dist.init_process_group("gloo", init_method=f"file://{rdv}", rank=rank, world_size=world)
     try:
         from mirai_b200.expert_parallel import ExpertShard, ep_moe_forward, shard_tokens
         T, H, E, k, I, seed, token_split, chunks = cfg
@@ -127,16 +125,19 @@ def _rank_main(rank, world, port, cfg, results):
         dist.destroy_process_group()
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous():
+    """A fresh rendezvous file for one process group (file:// init: no TCP port
+    to collide with another test's group)."""
+    import tempfile
+    fd, path = tempfile.mkstemp(prefix="mirai_pg_")
+    os.close(fd)
+    return path
 
 
 def _run(world, cfg):
     with mp.get_context("spawn").Manager() as mgr:
         results = mgr.dict()
-        mp.start_processes(_rank_main, args=(world, _free_port(), cfg, results), nprocs=world, start_method="spawn")
+        mp.start_processes(_rank_main, args=(world, _rendezvous(), cfg, results), nprocs=world, start_method="spawn")
         return dict(results)
 
 
@@ -270,11 +271,11 @@ class CorruptCountsOps(OracleStepOps):
         return p
 
 
-def _fault_rank_main(rank, world, port, mode, results):
+def _fault_rank_main(rank, world, rdv, mode, results):
     import time
     from datetime import timedelta
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    dist.init_process_group("gloo", init_method=f"file://{rdv}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=5))
     try:
         from mirai_b200.expert_parallel import ExpertShard, ep_moe_forward, shard_tokens
         T, H, E, k, I = 64, 32, 4, 2, 64
@@ -306,7 +307,7 @@ def _fault_rank_main(rank, world, port, mode, results):
 def _run_fault(mode):
     with mp.get_context("spawn").Manager() as mgr:
         results = mgr.dict()
-        mp.start_processes(_fault_rank_main, args=(2, _free_port(), mode, results), nprocs=2, start_method="spawn")
+        mp.start_processes(_fault_rank_main, args=(2, _rendezvous(), mode, results), nprocs=2, start_method="spawn")
         return dict(results)
 
 
@@ -344,9 +345,8 @@ def test_check_counts():
         check_counts(M, 1, [8, 8, 7])
 
 
-def _bwd_rank_main(rank, world, port, cfg, results):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+def _bwd_rank_main(rank, world, rdv, cfg, results):
+    dist.init_process_group("gloo", init_method=f"file://{rdv}", rank=rank, world_size=world)
     try:
         from mirai_b200.expert_parallel import ExpertShard, ep_moe_backward, ep_moe_forward, shard_tokens
         T, H, E, k, I, seed, token_split, chunks = cfg
@@ -367,7 +367,7 @@ def _bwd_rank_main(rank, world, port, cfg, results):
 def _run_bwd(world, cfg):
     with mp.get_context("spawn").Manager() as mgr:
         results = mgr.dict()
-        mp.start_processes(_bwd_rank_main, args=(world, _free_port(), cfg, results), nprocs=world,
+        mp.start_processes(_bwd_rank_main, args=(world, _rendezvous(), cfg, results), nprocs=world,
                            start_method="spawn")
         return dict(results)
 

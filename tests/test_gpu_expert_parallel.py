@@ -8,7 +8,6 @@ Skipped with fewer than two GPUs.
 """
 
 import os
-import socket
 
 import pytest
 import torch
@@ -33,13 +32,14 @@ def _quant(fmt, w, dev):
     return w.contiguous()
 
 
-def _rank_main(rank, world, port, cfg, results):
+def _rank_main(rank, world, rdv, cfg, results):
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     from datetime import timedelta
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    dist.init_process_group("nccl", init_method=f"file://{rdv}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
     try:
         from mirai_b200 import ops
         from mirai_b200.expert_parallel import ExpertShard, ep_moe_forward, shard_tokens
@@ -88,10 +88,13 @@ def _rank_main(rank, world, port, cfg, results):
         dist.destroy_process_group()
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rendezvous():
+    """A fresh rendezvous file for one process group (file:// init: no TCP port
+    to collide with another test's group)."""
+    import tempfile
+    fd, path = tempfile.mkstemp(prefix="mirai_pg_")
+    os.close(fd)
+    return path
 
 
 @pytest.mark.parametrize("fmt,chunks,transport,copy_streams,world,regroup,layout", [
@@ -119,7 +122,7 @@ def test_expert_parallel_equals_single_gpu_layer(fmt, chunks, transport, copy_st
     cfg = (1500 * world, 256, 8, 2, 384, fmt, chunks, transport, copy_streams, regroup, layout)
     with mp.Manager() as mgr:
         results = mgr.dict()
-        mp.start_processes(_rank_main, args=(world, _free_port(), cfg, results), nprocs=world, start_method="spawn")
+        mp.start_processes(_rank_main, args=(world, _rendezvous(), cfg, results), nprocs=world, start_method="spawn")
         res = dict(results)
     for r in range(world):
         code, equal, maxdiff = res[r]
@@ -127,13 +130,14 @@ def test_expert_parallel_equals_single_gpu_layer(fmt, chunks, transport, copy_st
         assert equal, f"rank {r}: max |diff| {maxdiff}"
 
 
-def _train_rank_main(rank, world, port, cfg, results):
+def _train_rank_main(rank, world, rdv, cfg, results):
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     from datetime import timedelta
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    dist.init_process_group("nccl", init_method=f"file://{rdv}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
     try:
         from mirai_b200 import ops
         from mirai_b200.expert_parallel import (ExpertParallelMoE, ExpertShard, ep_moe_backward, ep_moe_forward,
@@ -225,7 +229,7 @@ def test_expert_parallel_backward_equals_single_gpu(fmt, chunks, world, rotated,
     cfg = (2000, 256, 8, 2, 384, fmt, chunks, rotated, lora_rank, transport, regroup)
     with mp.Manager() as mgr:
         results = mgr.dict()
-        mp.start_processes(_train_rank_main, args=(world, _free_port(), cfg, results), nprocs=world,
+        mp.start_processes(_train_rank_main, args=(world, _rendezvous(), cfg, results), nprocs=world,
                            start_method="spawn")
         res = dict(results)
     for r in range(world):
