@@ -111,7 +111,8 @@ template <int WF, bool PAIR> struct Cfg {
   // threads take the k-blocks in turn (group g: k-blocks g, g+KG, ...).
   static constexpr int KG = QUANT ? DEQ_THREADS / B_ROWS : 1;
   static constexpr int GROUP_WARPS = QUANT ? B_ROWS / 32 : 0;            // dequant warps per group
-  static constexpr int STAGES = WF == W_BF16 ? (PAIR ? 6 : 4) : (PAIR ? 4 : 3);
+  // (bf16 pairs: 5 operand stages, leaving room for the staged epilogue's boxes)
+  static constexpr int STAGES = WF == W_BF16 ? (PAIR ? 5 : 4) : (PAIR ? 4 : 3);
   // raw-code ring: its own producer warp runs ahead of the operand ring
   static constexpr int RAW_STAGES = WF == W_BF16 ? 1 : (PAIR ? (WF == W_NF4 ? 8 : 4) : (WF == W_NF4 ? 4 : 2));
   static constexpr int EPI_WARPS = epi_warps(WF);
@@ -193,15 +194,15 @@ struct alignas(16) DeqSmem {
   float code[2][16];
 };
 
-// Staged epilogue (NF4 / INT8): each epilogue warp writes 32 rows x 32 bf16
+// Staged epilogue (CTA pairs): each epilogue warp writes 32 rows x 32 bf16
 // columns of an output into one of STG_BUFS shared-memory boxes (64-byte TMA
 // swizzle) and a TMA store writes the box to global memory, instead of every
 // lane storing its own row (32 cache lines per warp store, whose wavefronts
-// share the shared-memory port with the dequantisers).
+// share the shared-memory port with the operand traffic).
 constexpr int STG_BUFS = 3;
 constexpr uint32_t STG_BOX = 32 * 64;  // bytes: 32 rows x 32 bf16
 // (CTA pairs only: the single-CTA variants, kept for A/B measurement, have no room left)
-template <int WF, bool PAIR> __host__ __device__ constexpr bool staged_epilogue() { return WF != W_BF16 && PAIR; }
+template <int WF, bool PAIR> __host__ __device__ constexpr bool staged_epilogue() { return PAIR; }
 
 template <int WF, bool PAIR>
 constexpr size_t smem_bytes() {
@@ -1497,7 +1498,7 @@ int run_groups(const char* name, const void* a, const int32_t* offsets, int E, i
   // output maps of the staged epilogue (32 x 32 bf16 boxes, 64-byte swizzle); a map that
   // a mode does not store through is a copy of another (never used)
   CUtensorMap to[3];
-  if (w0.fmt != W_BF16) {
+  {
     const bool dgu = MODE == DXDOWN && p.gate_up != nullptr;  // [S, 2N]: gate half, then up half
     const uint64_t ld = dgu ? 2 * (uint64_t)N : (uint64_t)N;
     char* o = static_cast<char*>(out);
@@ -1516,8 +1517,6 @@ int run_groups(const char* name, const void* a, const int32_t* offsets, int E, i
                               (uint64_t)N, (uint64_t)S, 4 * (uint64_t)N, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
                : (to[2] = to[0], MIRAI_OK);
     if (rc) return rc;
-  } else {
-    to[0] = to[1] = to[2] = ta;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   constexpr bool NAT = MCfg<MODE>::MN_NATIVE;
