@@ -105,11 +105,14 @@ __global__ void __launch_bounds__(1024) nf4_nested_kernel(const float* __restric
   }
 }
 
-// NF4 -> bf16 [E, out, in] (nf4_dequantize_stack, quant.py:380-434): one
-// thread per 4 code bytes (8 elements), so that a warp reads 128 contiguous
-// bytes and writes 512 (HBM-bound: 2.25 bytes moved per element);
+// NF4 -> bf16 [E, out, in] (nf4_dequantize_stack, quant.py:380-434): a
+// thread decodes 4 code bytes (8 elements) per step, kDequantItems steps a
+// block-width apart, so that a warp reads 128 contiguous bytes and writes 512
+// per step (HBM-bound: 2.25 bytes moved per element);
 // w = bf16(code[nibble] * (ncode[q] * nested_absmax + offset)), the same
 // rounding as the grouped GEMMs' in-loop decode.
+constexpr int kDequantItems = 8;  // 8-element chunks per thread
+
 __global__ void __launch_bounds__(256) nf4_dequant_kernel(const uint32_t* __restrict__ packed,
                                                           const uint8_t* __restrict__ absmax,
                                                           const float* __restrict__ nested_absmax,
@@ -121,24 +124,44 @@ __global__ void __launch_bounds__(256) nf4_dequant_kernel(const uint32_t* __rest
   for (int i = threadIdx.x; i < 256; i += blockDim.x) s_ncode[i] = ncode[i];
   if (threadIdx.x < 16) s_code[threadIdx.x] = code[threadIdx.x];
   __syncthreads();
-  // grid: x = 256-chunk blocks of one expert, y = expert (no 64-bit division per thread)
+  // grid: x = blocks of kDequantItems x 256 chunks of one expert, y = expert (no 64-bit
+  // division per thread); each thread issues all its loads before decoding
   const int e = blockIdx.y;
-  const int cl = blockIdx.x * blockDim.x + threadIdx.x;  // 8-element chunk inside the expert
-  if (cl >= per_expert / 8) return;
-  const int blk = cl >> 3;  // absmax block inside the expert
-  const int nb = (nested_bs & (nested_bs - 1)) == 0 ? blk >> (31 - __clz(nested_bs)) : blk / nested_bs;
-  const float nabs = __ldg(nested_absmax + (int64_t)e * n_nested + nb);
-  const float scale =
-      __fadd_rn(__fmul_rn(s_ncode[__ldg(absmax + (int64_t)e * (per_expert / 64) + blk)], nabs), __ldg(offset + e));
-  const int64_t c = (int64_t)e * (per_expert / 8) + cl;
-  const uint32_t w = packed[c];
-  uint32_t o[4];
+  const int cpe = per_expert / 8;  // 8-element chunks per expert
+  const int base = blockIdx.x * (blockDim.x * kDequantItems) + threadIdx.x;
+  const float off = __ldg(offset + e);
+  const uint32_t* pk = packed + (int64_t)e * cpe;
+  const uint8_t* am = absmax + (int64_t)e * (per_expert / 64);
+  const float* na = nested_absmax + (int64_t)e * n_nested;
+  const bool pow2 = (nested_bs & (nested_bs - 1)) == 0;
+  const int nshift = 31 - __clz(nested_bs);
+  uint32_t w[kDequantItems];
+  uint8_t q[kDequantItems];
+  float nabs[kDequantItems];
 #pragma unroll
-  for (int b = 0; b < 4; ++b) {
-    const uint32_t byte = (w >> (8 * b)) & 0xFFu;  // first element in the high nibble
-    o[b] = pack_bf16x2(__fmul_rn(s_code[byte >> 4], scale), __fmul_rn(s_code[byte & 15u], scale));
+  for (int i = 0; i < kDequantItems; ++i) {
+    const int cl = base + i * blockDim.x;
+    if (cl < cpe) {
+      const int blk = cl >> 3;  // absmax block inside the expert
+      w[i] = __ldg(pk + cl);
+      q[i] = __ldg(am + blk);
+      nabs[i] = __ldg(na + (pow2 ? blk >> nshift : blk / nested_bs));
+    }
   }
-  out[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  uint4* dst = out + (int64_t)e * cpe;
+#pragma unroll
+  for (int i = 0; i < kDequantItems; ++i) {
+    const int cl = base + i * blockDim.x;
+    if (cl >= cpe) break;
+    const float scale = __fadd_rn(__fmul_rn(s_ncode[q[i]], nabs[i]), off);
+    uint32_t o[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t byte = (w[i] >> (8 * b)) & 0xFFu;  // first element in the high nibble
+      o[b] = pack_bf16x2(__fmul_rn(s_code[byte >> 4], scale), __fmul_rn(s_code[byte & 15u], scale));
+    }
+    dst[cl] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 // INT8 per row: scale = max(amax / 127, 1e-30); q = clamp(rint(x / scale), +-127).
@@ -216,7 +239,8 @@ int mirai_nf4_dequantize(const uint8_t* packed, const uint8_t* absmax, const flo
       (reinterpret_cast<uintptr_t>(packed) & 15u) || (reinterpret_cast<uintptr_t>(out_bf16) & 15u))
     return set_error(MIRAI_ERR_INVALID_ARG, "nf4_dequantize: null or misaligned pointer");
   const int n_nested = (int)((per / 64 + nested_blocksize - 1) / nested_blocksize);
-  const dim3 grid((unsigned)((per / 8 + 255) / 256), (unsigned)num_experts);
+  const dim3 grid((unsigned)((per / 8 + 256 * qz::kDequantItems - 1) / (256 * qz::kDequantItems)),
+                  (unsigned)num_experts);
   qz::nf4_dequant_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint32_t*>(packed), absmax, nested_absmax, offset, code, nested_code, (int)per,
       nested_blocksize, n_nested, static_cast<uint4*>(out_bf16));
