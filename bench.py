@@ -842,15 +842,16 @@ def cpu_baseline(cfg, args):
 
 
 # ----------------------------------------------------------------------------- probes (--probe)
-# Measurements of the expert-parallel exchange behind the profiles/ summaries,
-# run as `bench.py --probe ...` (one process per GPU under torchrun, except
-# gemms):
+# Measurements behind the profiles/ summaries, run as `bench.py --probe ...`
+# (one process per GPU under torchrun, except gemms and epilogue):
 #   bandwidth  bytes crossing NVLink per rank per second: NCCL all_to_all_single
 #              vs copy-engine transfers into peer-mapped buffers (the ipc transport)
 #   blocks     that copy-engine exchange (128 MB per rank) split into 1-128 copies
 #              per peer on one or two streams: the cost of a copy
 #   gemms      (one GPU) the owner's GEMMs on source-major rows vs the same rows
 #              contiguous per expert
+#   epilogue   (one GPU) c2's down dX with and without its SwiGLU-backward epilogue,
+#              and the NF4 decode of one key
 #   phases     CUDA-event times between the phases of one ExpertParallelMoE layer
 #              (1 chunk) on rank 0, over 10 layers after 3 warm-up layers
 #              (--config, --ep-layout, --ep-copy-streams, --ep-regroup)
@@ -1062,12 +1063,44 @@ def probe_gemms(dev):
 
 
 
+def probe_epilogue(dev):
+    """c2's down dX on bf16 copies of NF4 weights with its full epilogue (saved
+    gate/up read, SwiGLU backward, two outputs) against the same GEMM writing dh
+    alone (``gate_up`` NULL), and the NF4 decode of one key (ms, CUDA events,
+    mean of 30 launches after 3)."""
+    import torch
+    from mirai_b200 import _lib, ops, tables
+    cfg = CONFIGS["c2"]
+    T, H, E, k, I = cfg["T"], cfg["H"], cfg["E"], cfg["k"], cfg["I"]
+    S = T * k
+    g = torch.Generator(device=dev).manual_seed(0)
+    w2q = ops.nf4_quantize((torch.randn(E, H, I, device=dev, generator=g) * 0.02).to(torch.bfloat16),
+                           tables.nf4_code(dev), tables.dynamic_map(dev))
+    w2 = ops.nf4_dequantize(w2q)
+    offs = torch.tensor([(S * (j + 1)) // E for j in range(E)], dtype=torch.int32, device=dev)
+    gy = torch.randn(S, H, device=dev, generator=g).to(torch.bfloat16)
+    gu = torch.randn(S, 2 * I, device=dev, generator=g).to(torch.bfloat16)
+    dgu = torch.empty(S, 2 * I, dtype=torch.bfloat16, device=dev)
+    dh = torch.empty(S, I, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    res = {
+        "down_dx_full_ms": time_kernel(lambda: ops.down_dx(gy, offs, w2, gu, inter=I, out=dgu), 30),
+        "down_dx_dh_only_ms": time_kernel(lambda: _lib.call("mirai_moe_down_dx_src_bf16", gy.data_ptr(),
+                                                            offs.data_ptr(), 1, E, S, H, I, w2.data_ptr(), None,
+                                                            dh.data_ptr(), stream), 30),
+        "nf4_dequantize_one_key_ms": time_kernel(lambda: ops.nf4_dequantize(w2q, out=w2), 30),
+    }
+    ops.check_device()
+    return res
+
+
 def run_probe(args):
     import torch
     import torch.distributed as dist
     from datetime import timedelta
-    if args.probe == "gemms":  # one GPU, no process group
-        print(json.dumps(probe_gemms(torch.device("cuda", 0))), flush=True)
+    if args.probe in ("gemms", "epilogue"):  # one GPU, no process group
+        dev = torch.device("cuda", 0)
+        print(json.dumps(probe_gemms(dev) if args.probe == "gemms" else probe_epilogue(dev)), flush=True)
         return
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -1123,7 +1156,7 @@ def main():
                     help="N > 1: copy-engine transfers into peer-mapped buffers, or NCCL all_to_all_single")
     ap.add_argument("--tokens", type=int, default=None,
                     help="override the workload's token count (small cases for profiler captures)")
-    ap.add_argument("--probe", default=None, choices=["bandwidth", "blocks", "phases", "gemms"],
+    ap.add_argument("--probe", default=None, choices=["bandwidth", "blocks", "phases", "gemms", "epilogue"],
                     help="run one expert-parallel measurement instead of the benchmark (see the probes section)")
     args = ap.parse_args()
     if args.warmup < 3:
