@@ -59,7 +59,9 @@ LORA_RANK = 16
 # summary and its command are under profiles/).  A kernel changed since its
 # capture, or not captured, reports null.
 NCU_TRAFFIC = {
-    "c2-gateup_swiglu_nf4": (363_831_552 + 166_611_712, "profiles/grouped_gemm_nf4_c2.md"),
+    "c2-gateup_dx_bf16 (NF4 staged)": (739_500_000 + 247_990_000, "profiles/grouped_gemm_traffic_c2.md"),
+    "c2-down_dx_bf16 (NF4 staged)": (865_320_000 + 337_760_000, "profiles/grouped_gemm_traffic_c2.md"),
+    "c2-gateup_swiglu_bf16 (NF4 staged)": (639_560_000 + 516_470_000, "profiles/grouped_gemm_traffic_c2.md"),
 }
 
 

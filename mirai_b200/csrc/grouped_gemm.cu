@@ -835,26 +835,44 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
           tmem_ld_wait();
           if (valid && col < p.N) {
             uint32_t dg[16], du[16];
+            // (the register budget of the NF4 / INT8 epilogue warps keeps them on the per-element form)
+            if (WF != W_BF16 || p.act == ACT_SWIGLU7) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float dgo[2], duo[2];
+              for (int j = 0; j < 16; ++j) {
+                float dgo[2], duo[2];
 #pragma unroll
-              for (int hh = 0; hh < 2; ++hh) {
-                const float dh = bf16r(__uint_as_float(v32[2 * j + hh]));
-                const float gv = hh ? bf16_hi(gw[j]) : bf16_lo(gw[j]);
-                const float uv = hh ? bf16_hi(uw[j]) : bf16_lo(uw[j]);
-                if (p.act == ACT_SWIGLU7) {
-                  swiglu7_backward(dh, gv, uv, dgo[hh], duo[hh]);
-                  continue;
+                for (int hh = 0; hh < 2; ++hh) {
+                  const float dh = bf16r(__uint_as_float(v32[2 * j + hh]));
+                  const float gv = hh ? bf16_hi(gw[j]) : bf16_lo(gw[j]);
+                  const float uv = hh ? bf16_hi(uw[j]) : bf16_lo(uw[j]);
+                  if (p.act == ACT_SWIGLU7) {
+                    swiglu7_backward(dh, gv, uv, dgo[hh], duo[hh]);
+                    continue;
+                  }
+                  const float sg = __fdividef(1.f, 1.f + __expf(-gv));
+                  const float act = bf16r(gv * sg);
+                  const float dact = bf16r(dh * uv);
+                  duo[hh] = dh * act;
+                  dgo[hh] = dact * sg * (1.f + gv * (1.f - sg));
                 }
-                const float sg = __fdividef(1.f, 1.f + __expf(-gv));
-                const float act = bf16r(gv * sg);
-                const float dact = bf16r(dh * uv);
-                duo[hh] = dh * act;
-                dgo[hh] = dact * sg * (1.f + gv * (1.f - sg));
+                dg[j] = pack_bf16x2(dgo[0], dgo[1]);
+                du[j] = pack_bf16x2(duo[0], duo[1]);
               }
-              dg[j] = pack_bf16x2(dgo[0], dgo[1]);
-              du[j] = pack_bf16x2(duo[0], duo[1]);
+            } else {
+              // Column pairs as bf16x2: dh, silu(g) and the products dh*up, dh*act are the
+              // reference's bf16 tensors; a product of two bf16 values is exact in fp32, so the
+              // packed multiply rounds it exactly as an fp32 multiply and a bf16 rounding would.
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const uint32_t dh2 = pack_bf16x2(__uint_as_float(v32[2 * j]), __uint_as_float(v32[2 * j + 1]));
+                const float g0 = bf16_lo(gw[j]), g1 = bf16_hi(gw[j]);
+                const float s0 = __fdividef(1.f, 1.f + __expf(-g0));
+                const float s1 = __fdividef(1.f, 1.f + __expf(-g1));
+                const uint32_t dact2 = bf16x2_mul(dh2, uw[j]);
+                du[j] = bf16x2_mul(dh2, pack_bf16x2(g0 * s0, g1 * s1));
+                const float d0 = bf16_lo(dact2), d1 = bf16_hi(dact2);
+                dg[j] = pack_bf16x2(d0 * s0 * (1.f + g0 * (1.f - s0)), d1 * s1 * (1.f + g1 * (1.f - s1)));
+              }
             }
             if (boxed) {
               stage_store(&tmap_o0, col, row0, dg);  // the gate half of dgu
