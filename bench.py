@@ -982,9 +982,11 @@ def probe_blocks(dev, world, rank):
     return res
 
 
-def probe_phases(dev, world, rank, config, layout="source", copy_streams=1, regroup="auto"):
+def probe_phases(dev, world, rank, config, layout="source", copy_streams=1, regroup="auto", train=False,
+                 chunks=1):
     import torch
     import torch.distributed as dist
+    from mirai_b200 import ops
     from mirai_b200.expert_parallel import ExpertParallelMoE, ExpertShard, shard_tokens
     cfg = dict(CONFIGS[config], layers=1)
     strong = CONFIGS[config].get("ep") == "strong"
@@ -992,8 +994,22 @@ def probe_phases(dev, world, rank, config, layout="source", copy_streams=1, regr
     b, e = shard_tokens(T_total, world, rank)
     shard = ExpertShard(cfg["E"], world, rank)
     x, logits, stack = make_ep_workload(cfg, dev, rank, shard, e - b)
-    layer = ExpertParallelMoE(shard, top_k=cfg["k"], inter=cfg["I"], chunks=1, layout=layout,
+    layer = ExpertParallelMoE(shard, top_k=cfg["k"], inter=cfg["I"], chunks=chunks, layout=layout,
                               copy_streams=copy_streams, regroup=regroup)
+    lora = g_out = None
+    if train:
+        gen = torch.Generator(device=dev).manual_seed(99 + rank)
+        g_out = torch.randn(e - b, cfg["H"], device=dev, generator=gen).to(torch.bfloat16)
+        lora = ops.DownLoRA(torch.randn(shard.local, LORA_RANK, cfg["I"], device=dev, generator=gen) * 0.03,
+                            torch.randn(shard.local, cfg["H"], LORA_RANK, device=dev, generator=gen) * 0.02,
+                            16.0 / LORA_RANK, compute_grads=True)
+
+    def step():
+        if not train:
+            return layer.forward(x, logits, stack[0][1])
+        _, st = layer.forward(x, logits, stack[0][1], train=True, lora=lora)
+        return layer.backward(g_out, st, stack[0][1], lora=lora)
+
     events = []
 
     def hook(name, stream):  # records at its point in the stream
@@ -1004,21 +1020,27 @@ def probe_phases(dev, world, rank, config, layout="source", copy_streams=1, regr
     layer.on_phase = hook
     for _ in range(3):
         events.clear()
-        layer.forward(x, logits, stack[0][1])
+        step()
     torch.cuda.synchronize()
     dist.barrier()
     acc: dict[str, float] = {}
+    step_ms = 0.0
     for _ in range(10):
         events.clear()
-        layer.forward(x, logits, stack[0][1])
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        step()
+        t1.record()
         torch.cuda.synchronize()
+        step_ms += t0.elapsed_time(t1) / 10
         for i in range(1, len(events)):
             name = events[i][0]
             acc[name] = acc.get(name, 0.0) + events[i - 1][1].elapsed_time(events[i][1]) / 10
     layer.close()
     return {"config": config, "world": world, "tokens_rank0": e - b, "layout": layout, "copy_streams": copy_streams,
-            "regroup": regroup,
-            "phases_ms": {k: round(v, 3) for k, v in acc.items()}, "layer_ms": round(sum(acc.values()), 3)}
+            "regroup": regroup, "train": train, "chunks": chunks,
+            "phases_ms": {k: round(v, 3) for k, v in acc.items()}, "layer_ms": round(sum(acc.values()), 3),
+            "step_ms": round(step_ms, 3)}
 
 
 def probe_gemms(dev):
@@ -1115,7 +1137,8 @@ def run_probe(args):
         elif args.probe == "blocks":
             res = probe_blocks(dev, world, rank)
         else:
-            res = probe_phases(dev, world, rank, args.config, args.ep_layout, args.ep_copy_streams, args.ep_regroup)
+            res = probe_phases(dev, world, rank, args.config, args.ep_layout, args.ep_copy_streams, args.ep_regroup,
+                               train=args.mode == "train", chunks=args.ep_chunks)
         if rank == 0:
             print(json.dumps(res), flush=True)
     finally:
