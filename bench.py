@@ -78,10 +78,17 @@ def load_peaks():
 # ----------------------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """Polls NVML (read-only) for SM clock and clock-event reasons."""
+    """Polls NVML (read-only) for SM clock and clock-event reasons.
 
-    def __init__(self, index: int, period_s: float = 0.005):
-        self.index, self.period = index, period_s
+    Every rank samples its own GPU; with several ranks the period grows with
+    their number (5 ms x ranks), so that the processes' NVML queries stay few
+    beside the driver calls of the copy-engine exchange (an 8-GPU train step
+    timed 11.8 ms under eight 5 ms samplers and 5.1 ms in the phases probe,
+    which samples nothing)."""
+
+    def __init__(self, index: int, period_s: float | None = None):
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.index, self.period = index, period_s if period_s is not None else 0.005 * max(1, world)
         self.samples = []
         self.reasons = set()
         self.max_mhz = None
