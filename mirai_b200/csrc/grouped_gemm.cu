@@ -766,17 +766,18 @@ __global__ void __launch_bounds__(Cfg<WF, PAIR>::THREADS, 1)
               // Round where the reference's bf16 tensors round: gate and up (the
               // GEMM outputs), then SwiGLU's silu(gate) and product (experts.py:301-317)
               // or swiglu7 in fp32 on the bf16 gate/up (grouped_moe.py:287-306).
-              const float g0 = bf16r(__uint_as_float(g[2 * j])), g1 = bf16r(__uint_as_float(g[2 * j + 1]));
-              const float u0 = bf16r(__uint_as_float(u[2 * j])), u1 = bf16r(__uint_as_float(u[2 * j + 1]));
+              // (column pairs as bf16x2: the product of two bf16 values is exact in fp32, so
+              // mul.rn.bf16x2 rounds it as an fp32 multiply and a bf16 rounding would)
+              gp[j] = pack_bf16x2(__uint_as_float(g[2 * j]), __uint_as_float(g[2 * j + 1]));
+              up[j] = pack_bf16x2(__uint_as_float(u[2 * j]), __uint_as_float(u[2 * j + 1]));
+              const float g0 = bf16_lo(gp[j]), g1 = bf16_hi(gp[j]);
               if (p.act == ACT_SWIGLU7) {
-                hp[j] = pack_bf16x2(swiglu7(g0, u0), swiglu7(g1, u1));
+                hp[j] = pack_bf16x2(swiglu7(g0, bf16_lo(up[j])), swiglu7(g1, bf16_hi(up[j])));
               } else {
-                const float a0 = bf16r(__fdividef(g0, 1.f + __expf(-g0)));
-                const float a1 = bf16r(__fdividef(g1, 1.f + __expf(-g1)));
-                hp[j] = pack_bf16x2(a0 * u0, a1 * u1);
+                const float a0 = __fdividef(g0, 1.f + __expf(-g0));
+                const float a1 = __fdividef(g1, 1.f + __expf(-g1));
+                hp[j] = bf16x2_mul(pack_bf16x2(a0, a1), up[j]);
               }
-              gp[j] = pack_bf16x2(g0, g1);
-              up[j] = pack_bf16x2(u0, u1);
             }
             if (boxed) {
               stage_store(&tmap_o0, col0 + c * 32, row0, hp);
