@@ -55,13 +55,14 @@ CONFIGS = {
 METRIC = "MoE-FFN tokens/s (NF4 experts) + % TC/HBM roofline at 1/2/4/8 B200"
 LORA_RANK = 16
 # DRAM bytes (read + write) per launch of a grouped GEMM from an ncu capture of
-# the same kernel on the same workload, with the capture it came from (the
-# summary and its command are under profiles/).  A kernel changed since its
-# capture, or not captured, reports null.
+# the same kernel on the same workload and mode (keyed config-mode-kernel), with
+# the capture it came from (the summary and its command are under profiles/).
+# A kernel changed since its capture, or not captured, reports null.
 NCU_TRAFFIC = {
-    "c2-gateup_dx_bf16 (NF4 staged)": (739_500_000 + 247_990_000, "profiles/grouped_gemm_traffic_c2.md"),
-    "c2-down_dx_bf16 (NF4 staged)": (865_320_000 + 337_760_000, "profiles/grouped_gemm_traffic_c2.md"),
-    "c2-gateup_swiglu_bf16 (NF4 staged)": (639_560_000 + 516_470_000, "profiles/grouped_gemm_traffic_c2.md"),
+    "c2-train-gateup_dx_bf16 (NF4 staged)": (739_500_000 + 247_990_000, "profiles/grouped_gemm_traffic_c2.md"),
+    "c2-train-down_dx_bf16 (NF4 staged)": (865_320_000 + 337_760_000, "profiles/grouped_gemm_traffic_c2.md"),
+    "c2-train-gateup_swiglu_bf16 (NF4 staged)": (639_560_000 + 516_470_000,
+                                                 "profiles/grouped_gemm_traffic_c2.md"),
 }
 
 
@@ -389,7 +390,7 @@ def run_ours(args, cfg, rank, world, dev):
     achieved = top_flops / (kernel_ms[top] * 1e-3) / 1e12
     fmt = make_weights_fmt(cfg, args)
     kname = f"{top}_{'bf16 (NF4 staged)' if staged else cfg['fmt']}"
-    traffic = NCU_TRAFFIC.get(f"{args.config}-{kname}") if not args.int8_rotation else None
+    traffic = NCU_TRAFFIC.get(f"{args.config}-{args.mode}-{kname}") if not args.int8_rotation else None
     lora_flops = 6.0 * S * LORA_RANK * (H + I)  # rank projection + rank block, fwd and dX, and the factor grads
     step_flops = (12.0 * S * H * I + lora_flops) if train else 6.0 * S * H * I
     line = {
