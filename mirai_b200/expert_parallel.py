@@ -790,15 +790,14 @@ class ExpertParallelMoE:
         mark("start", comp)
         C = self.chunks
         bounds = [((T * c) // C, (T * (c + 1)) // C) for c in range(C)]
-        prep = []
+        routed = []
         for b, e in bounds:
             idx, tw = ops.route(logits[b:e], k)
-            plan = ops.plan(idx, E)
-            prep.append((tw, plan, ops.permute(tokens[b:e], plan.sorted_token_indices)))
-        mark("route+plan+permute", comp)
+            routed.append((tw, ops.plan(idx, E), idx.numel()))
+        mark("route+plan", comp)
         # every rank's rows per (destination, chunk, local expert): one gather, one host read
-        mine = torch.stack([p[1].counts.view(G, El) for p in prep], dim=1).contiguous()  # [dest, chunk, expert]
-        allm = torch.empty((G,) + tuple(mine.shape), dtype=mine.dtype, device=dev)      # [source, dest, chunk, expert]
+        mine = torch.stack([p[1].counts.view(G, El) for p in routed], dim=1).contiguous()  # [dest, chunk, expert]
+        allm = torch.empty((G,) + tuple(mine.shape), dtype=mine.dtype, device=dev)        # [source, dest, chunk, expert]
         dist.all_gather_into_tensor(allm, mine, group=self.group)
         row_bytes = H * tokens.element_size()
         counts = allm.cpu().numpy()
@@ -807,7 +806,10 @@ class ExpertParallelMoE:
             # that gave up (a peer more than 2 s late) or a failed kernel check is reported here,
             # before this call moves any row.  The last call's status is read by check().
             self.check()
-        check_counts(counts, me, [p[2].shape[0] for p in prep])
+        # the permutes run on the GPU while this host plans the exchange
+        prep = [(tw, plan, ops.permute(tokens[b:e], plan.sorted_token_indices))
+                for (tw, plan, _), (b, e) in zip(routed, bounds)]
+        check_counts(counts, me, [n for _, _, n in routed])
         plan = exchange_blocks(counts, me, self.layout, regroup=self.regroup, hidden=H,
                                inter=self.inter, row_bytes=row_bytes)
         in_cap = (plan.in_cap * row_bytes + 255) // 256 * 256
