@@ -167,8 +167,8 @@ def make_workload(cfg, dev, seed, rotation=False):
             w = ops.nf4_quantize(w, tables.nf4_code(dev), tables.dynamic_map(dev))
         elif cfg["fmt"] == "int8":
             # the reference's default format rotates groups of best_group_size(in) (quant.py:87-91)
-            g = (256 if shape[2] % 256 == 0 else 64 if shape[2] % 64 == 0 else 16) if rotation else 0
-            w = ops.int8_quantize(w.float(), group_size=g)
+            grp = (256 if shape[2] % 256 == 0 else 64 if shape[2] % 64 == 0 else 16) if rotation else 0
+            w = ops.int8_quantize(w.float(), group_size=grp)
         ws.append(w)
     torch.cuda.synchronize()
     return x, logits, ws
