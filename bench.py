@@ -590,7 +590,9 @@ def run_ep(args, cfg, rank, world, dev):
     offs = torch.tensor([(R * (j + 1)) // shard.local for j in range(shard.local)], dtype=torch.int32, device=dev)
     xl = torch.randn(R, H, device=dev).to(torch.bfloat16)
     hl = torch.empty((R, I), dtype=torch.bfloat16, device=dev)
-    w1, w3, _ = stack[0][1]
+    # the weights the layer's GEMMs multiply (NF4 staged to bf16 copies where that pays)
+    w1, w3, _ = ops.stage_nf4(stack[0][1], R, shard.local, training=train)
+    staged = w1 is not stack[0][1][0]
     kclocks = ClockSampler(torch.cuda.current_device()).start()
     for _ in range(3):
         ops.gateup_swiglu(xl, offs, w1, w3, inter=I, out=hl)
@@ -643,6 +645,10 @@ def run_ep(args, cfg, rank, world, dev):
                         f"({T_r} on rank 0), H={H} E={E} ({shard.local} per GPU) k={k} I={I} {cfg['fmt']} experts",
             "tokens_total": T_total, "hidden": H, "experts": E, "experts_per_gpu": shard.local, "top_k": k,
             "intermediate": I, "layers": layers, "weights": cfg["fmt"],
+            **({"nf4_decode": "once per layer into bf16 copies of the rank's experts, then the bf16 GEMMs "
+                              f"(staging {args.nf4_staging})" if staged else
+                              f"inside the GEMMs' main loops (staging {args.nf4_staging})"}
+               if cfg["fmt"] == "nf4" else {}),
             "parallelism": f"ep{world}: experts sharded by contiguous blocks, tokens sharded by rank, " + (
                 f"copy-engine transfers into {args.ep_layout}-major peer-mapped receive buffers (CUDA IPC over "
                 f"NVLink, {args.ep_copy_streams} copy stream(s), regroup {args.ep_regroup}), arrival marked by "
@@ -658,7 +664,7 @@ def run_ep(args, cfg, rank, world, dev):
         },
         "tflops": (12.0 if train else 6.0) * S_total * H * I * layers / (ms * 1e-3) / 1e12,
         "roofline": {
-            "kernel": f"gateup_swiglu_{cfg['fmt']}",
+            "kernel": f"gateup_swiglu_{'bf16 (NF4 staged)' if staged else cfg['fmt']}",
             "bound": "tensor",
             "achieved": achieved,
             "peak": peaks["bf16_tflops"],

@@ -231,7 +231,7 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
         plan = ops.plan(idx, E)
         xs = ops.permute(tokens, plan.sorted_token_indices)
         if not train:
-            y = ops.experts(xs, plan.offsets, local_weights, inter)
+            y = ops.experts(xs, plan.offsets, _stage(ops, local_weights, xs.shape[0], False)[0], inter)
             return ops.combine(y, plan.inverse_order, tw, top_k, tokens.dtype)
         wts, staged = _stage(ops, local_weights, xs.shape[0], True)
         y, saved = ops.experts_train(xs, plan.offsets, wts, inter, **({"lora": lora} if lora else {}))
@@ -304,10 +304,15 @@ def ep_moe_forward(tokens: torch.Tensor, logits: torch.Tensor, local_weights: An
         _a2a(x_recv, xs, rc[c], sc[c], group)
         return x_recv
 
+    fwd_weights = None
+
     def compute(c, x_recv):
+        nonlocal fwd_weights
         if x_recv.shape[0] == 0:
             return torch.empty((0, H), dtype=x_recv.dtype, device=dev)
-        return ops.experts(x_recv, offs_dev[c], local_weights, inter, sources=G)
+        if fwd_weights is None:  # NF4 keys decoded once for the layer where that pays
+            fwd_weights = _stage(ops, local_weights, sum(sum(r) for r in rc), False)[0]
+        return ops.experts(x_recv, offs_dev[c], fwd_weights, inter, sources=G)
 
     def give_back(c, y_recv):
         keep(y_recv, comm)
@@ -844,9 +849,10 @@ class ExpertParallelMoE:
             mark(f"dispatch copies + arrival, chunk {c}", comm)
         returned, saved = [], []
         kw = {"lora": lora} if lora is not None else {}
-        staged = None
-        if train:
-            local_weights, staged = _stage(ops, local_weights, sum(plan.in_rows), True)
+        # NF4 keys decoded once for this layer where that pays (kept for the backward when training)
+        local_weights, staged = _stage(ops, local_weights, sum(plan.in_rows), train)
+        if not train:
+            staged = None
         for c in range(C):
             ex.wait(landed[c])
             rows_c = plan.in_rows[c]
