@@ -360,13 +360,13 @@ def test_nf4_staged_forward_equals_in_loop_decode_at_c4_width():
     per expert) gives the in-loop decode's bits at c4's H=4096, I=1536."""
     dev = _dev()
     from mirai_b200 import ops
-    T, H, E, k, I = 2048, 4096, 4, 8, 1536
+    T, H, E, k, I = 4096, 4096, 4, 4, 1536
     rng = np.random.default_rng(31)
     _, dw = _weights("nf4", rng, E, H, I, dev, std=0.02)
     x = _bf16(rng.standard_normal((T, H)).astype(np.float32)).to(dev)
     idx, w = ops.route_topk(torch.from_numpy(rng.standard_normal((T, E)).astype(np.float32)).to(dev), k)
     res = {}
-    for mode in ("never", "auto"):  # 2048 * 8 / 4 = 4096 rows per expert: "auto" stages
+    for mode in ("never", "auto"):  # 4096 * 4 / 4 = 4096 rows per expert: "auto" stages
         ops.set_nf4_staging(mode)
         try:
             res[mode] = ops.moe_forward(x, idx, w, *dw, num_experts=E, inter=I)
