@@ -7,14 +7,18 @@ Default workload: BASELINE config 2 as it is defined -- 32768 tokens, hidden
 with double-quantised absmax, forward plus the dX backward through the frozen
 experts with a rank-16 LoRA on w2 (its factor gradients included).  One step
 = one pass of the path over the batch: fp32 router top-k on precomputed gate
-logits -> dispatch plan -> permute -> gate/up grouped GEMM + SwiGLU (fused
-NF4 dequant) -> LoRA rank projection -> down grouped GEMM with the rank block
--> weighted combine; then combine backward -> down dX (SwiGLU backward fused)
--> gate/up dX -> un-permute sum, and the LoRA factor gradients.
+logits -> NF4 decode of the three keys into bf16 copies (with 2048 rows per
+expert a training pass stages them; --nf4-staging never keeps the decode
+inside the GEMMs) -> dispatch plan -> permute -> gate/up grouped GEMM + SwiGLU
+-> LoRA rank projection -> down grouped GEMM with the rank block -> weighted
+combine; then combine backward -> down dX (SwiGLU backward fused) -> gate/up
+dX -> un-permute sum, and the LoRA factor gradients.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c0..c4] [--mode train|fwd]
-                    [--int8-rotation] [--impl ours|reference] [--ep-transport ipc|nccl] [--ep-chunks C]
+                    [--int8-rotation] [--nf4-staging auto|always|never] [--tokens T]
+                    [--impl ours|reference] [--ep-transport ipc|nccl] [--ep-chunks C]
                     [--ep-layout source|expert] [--ep-regroup never|auto|always] [--ep-copy-streams S]
+                    [--probe bandwidth|blocks|phases|gemms|epilogue]
 
 ``--mode fwd`` times the forward layer alone (the line also carries the
 forward rate of a train run under ``forward``).  ``--int8-rotation`` runs
