@@ -239,3 +239,32 @@ def test_lora_factor_pads_are_kept_until_the_factor_changes():
     ops._factor_pads(p)["b"] = "rebuilt"
     p.data = torch.zeros(2, 4, 8)  # new storage
     assert "b" not in ops._factor_pads(p)
+
+
+def test_nf4_staging_policy(monkeypatch):
+    """Which passes decode NF4 keys once into bf16 copies: training passes from
+    1024 rows per expert, forward-only ones from 4096, every pass with
+    "always", none with "never"; other formats are passed through."""
+    from mirai_b200 import ops
+
+    key = object.__new__(ops.NF4Tensor)  # a stand-in key: the policy only looks at its type
+    decoded = []
+    monkeypatch.setattr(ops, "nf4_dequantize", lambda w: decoded.append(w) or "bf16 copy")
+    keys = (key, key, key)
+    E = 8
+    try:
+        assert ops.stage_nf4(keys, 1024 * E, E, training=True) == ("bf16 copy",) * 3
+        assert ops.stage_nf4(keys, 1024 * E - 1, E, training=True) == keys
+        assert ops.stage_nf4(keys, 4096 * E - 1, E, training=False) == keys
+        assert ops.stage_nf4(keys, 4096 * E, E, training=False) == ("bf16 copy",) * 3
+        ops.set_nf4_staging("never")
+        assert ops.stage_nf4(keys, 10 ** 9, E, training=True) == keys
+        ops.set_nf4_staging("always")
+        assert ops.stage_nf4(keys, 1, E, training=False) == ("bf16 copy",) * 3
+        dense = (torch.zeros(1), torch.zeros(1), torch.zeros(1))
+        assert ops.stage_nf4(dense, 10 ** 9, E, training=True) == dense
+        with pytest.raises(ValueError, match="staging mode"):
+            ops.set_nf4_staging("sometimes")
+    finally:
+        ops.set_nf4_staging("auto")
+    assert len(decoded) == 9
