@@ -193,46 +193,63 @@ def weight_bytes(cfg):
 def measure_e2e(dev, host_in, n_out, out_shape, compute, args, barrier):
     """ms per step through the public API with host buffers.  Every step copies
     its inputs host -> device from pinned memory and its results device -> host.
-    Two buffer slots and two copy streams let step j's upload and step j-1's
-    download overlap the neighbouring steps' compute, as a serving loop would."""
+    Two buffer slots and their own copy streams let step j's upload and step
+    j-1's download overlap the neighbouring steps' compute, as a serving loop
+    would; each direction's bytes are split by rows over ``--e2e-copy-streams``
+    streams (copy engines)."""
     import torch
 
     comp = torch.cuda.current_stream()
-    up, down_s = torch.cuda.Stream(), torch.cuda.Stream()
+    lanes = max(1, int(getattr(args, "e2e_copy_streams", 1)))
+    ups = [torch.cuda.Stream() for _ in range(lanes)]
+    downs = [torch.cuda.Stream() for _ in range(lanes)]
+
+    def parts(t):  # the row blocks each lane copies
+        return torch.tensor_split(t, lanes, dim=0) if t.dim() else (t,)
+
     slots = []
     for _ in range(2):
         slots.append({
             "din": [torch.empty_like(t, device=dev) for t in host_in],
             "dout": [torch.empty(out_shape, dtype=torch.bfloat16, device=dev) for _ in range(n_out)],
             "hout": [torch.empty(out_shape, dtype=torch.bfloat16).pin_memory() for _ in range(n_out)],
-            "loaded": torch.cuda.Event(), "computed": torch.cuda.Event(), "saved": torch.cuda.Event(),
-            "used": False,
+            "loaded": [torch.cuda.Event() for _ in range(lanes)], "computed": torch.cuda.Event(),
+            "saved": [torch.cuda.Event() for _ in range(lanes)], "used": False,
         })
 
     def e2e_step(j):
         sl = slots[j % 2]
-        with torch.cuda.stream(up):
-            if sl["used"]:
-                up.wait_event(sl["computed"])  # the slot's previous step has read its inputs
-            for d, h in zip(sl["din"], host_in):
-                d.copy_(h, non_blocking=True)
-            sl["loaded"].record(up)
-        comp.wait_event(sl["loaded"])
+        for i, s in enumerate(ups):
+            with torch.cuda.stream(s):
+                if sl["used"]:
+                    s.wait_event(sl["computed"])  # the slot's previous step has read its inputs
+                for d, h in zip(sl["din"], host_in):
+                    dp, hp = parts(d), parts(h)
+                    if i < len(dp):
+                        dp[i].copy_(hp[i], non_blocking=True)
+                sl["loaded"][i].record(s)
+        for ev in sl["loaded"]:
+            comp.wait_event(ev)
         if sl["used"]:
-            comp.wait_event(sl["saved"])  # the slot's previous result has been downloaded
+            for ev in sl["saved"]:
+                comp.wait_event(ev)  # the slot's previous result has been downloaded
         compute(sl["din"], sl["dout"])
         sl["computed"].record(comp)
-        with torch.cuda.stream(down_s):
-            down_s.wait_event(sl["computed"])
-            for h, d in zip(sl["hout"], sl["dout"]):
-                h.copy_(d, non_blocking=True)
-            sl["saved"].record(down_s)
+        for i, s in enumerate(downs):
+            with torch.cuda.stream(s):
+                s.wait_event(sl["computed"])
+                for h, d in zip(sl["hout"], sl["dout"]):
+                    hp, dp = parts(h), parts(d)
+                    if i < len(hp):
+                        hp[i].copy_(dp[i], non_blocking=True)
+                sl["saved"][i].record(s)
         sl["used"] = True
 
     def drain():
         for sl in slots:
             if sl["used"]:
-                comp.wait_event(sl["saved"])
+                for ev in sl["saved"]:
+                    comp.wait_event(ev)
 
     for j in range(max(1, min(3, args.warmup))):
         e2e_step(j)
@@ -241,8 +258,8 @@ def measure_e2e(dev, host_in, n_out, out_shape, compute, args, barrier):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(comp)
-    up.wait_event(e0)
-    down_s.wait_event(e0)
+    for s in ups + downs:
+        s.wait_event(e0)
     for j in range(args.steps):
         e2e_step(j)
     drain()
@@ -446,7 +463,8 @@ def run_ours(args, cfg, rank, world, dev):
             "unit": "tokens/s",
             "h2d_bytes_per_step": T * H * 2 * (2 if train else 1) + T * E * 4,
             "d2h_bytes_per_step": T * H * 2 * (2 if train else 1),
-            "copies": "pinned host buffers; 2 slots, uploads and downloads on their own streams overlap compute",
+            "copies": f"pinned host buffers; 2 slots, uploads and downloads on their own streams overlap compute, "
+                      f"each direction split over {args.e2e_copy_streams} stream(s)",
         },
         "gpu_launches": launches,
         "gpu_launches_source": "libmirai_b200's own count of the kernels its entry points enqueued in the timed "
@@ -684,7 +702,8 @@ def run_ep(args, cfg, rank, world, dev):
             "unit": "tokens/s",
             "h2d_bytes_per_step": T_r * H * 2 * (2 if train else 1) + T_r * E * 4,
             "d2h_bytes_per_step": T_r * H * 2 * (2 if train else 1),
-            "copies": "per rank: pinned host buffers; 2 slots, uploads and downloads on their own streams",
+            "copies": "per rank: pinned host buffers; 2 slots, uploads and downloads on their own streams, "
+                      f"each direction split over {args.e2e_copy_streams} stream(s)",
         },
         "gpu_launches": launches,
         "gpu_launches_scope": "rank 0 (every rank launches its own)",
@@ -1178,6 +1197,8 @@ def main():
     ap.add_argument("--int8-rotation", action="store_true",
                     help="c3: INT8 in the reference's default block-Hadamard format (groups of 256)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-copy-streams", type=int, default=1,
+                    help="end-to-end timing: streams (copy engines) each direction's host copies are split over")
     ap.add_argument("--nf4-staging", default="auto", choices=["auto", "always", "never"],
                     help="NF4 experts: decode each key once per pass into bf16 copies for the bf16 GEMMs "
                          "(always), decode inside the GEMMs (never), or stage training passes with many rows "
