@@ -684,9 +684,10 @@ def moe_forward(tokens: torch.Tensor, top_indices: torch.Tensor, top_weights: to
     not S) and h before the down GEMM; the LoRA rank block is projected from
     the unrotated h."""
     g_in, g_mid = _rotations(w1, w3, w2)
-    w1, w3, w2 = stage_nf4((w1, w3, w2), top_indices.numel(), num_experts, training=False)
+    (w1, w3, w2), join = _stage_beside((w1, w3, w2), top_indices.numel(), num_experts, training=False)
     plan = dispatch_plan(top_indices, num_experts)
     xs = permute_rows(rotate_rows(tokens, g_in) if g_in else tokens, plan.sorted_token_indices)
+    join()
     h = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter)
     low = lora_project(h, plan.offsets, lora, forward=True) if lora is not None else None
     y = down(rotate_rows(h, g_mid) if g_mid else h, plan.offsets, w2, hidden=tokens.shape[1], lora=lora,
@@ -736,16 +737,50 @@ def set_nf4_staging(mode: str) -> None:
     _nf4_staging = mode
 
 
+def _staging_pays(weights, rows: int, num_experts: int, training: bool) -> bool:
+    if _nf4_staging == "never" or not any(isinstance(w, NF4Tensor) for w in weights):
+        return False
+    least = STAGE_MIN_ROWS_PER_EXPERT if training else STAGE_MIN_ROWS_PER_EXPERT_FORWARD
+    return _nf4_staging == "always" or rows >= least * max(1, num_experts)
+
+
 def stage_nf4(weights, rows: int, num_experts: int, *, training: bool):
     """The weights a pass over ``rows`` routed rows should multiply: NF4 keys
     decoded to bf16 where staging pays (see ``set_nf4_staging``), others as
     given."""
-    if _nf4_staging == "never" or not any(isinstance(w, NF4Tensor) for w in weights):
-        return tuple(weights)
-    least = STAGE_MIN_ROWS_PER_EXPERT if training else STAGE_MIN_ROWS_PER_EXPERT_FORWARD
-    if _nf4_staging == "auto" and rows < least * max(1, num_experts):
+    if not _staging_pays(weights, rows, num_experts, training):
         return tuple(weights)
     return tuple(nf4_dequantize(w) if isinstance(w, NF4Tensor) else w for w in weights)
+
+
+_side_streams: dict = {}
+
+
+def _stage_beside(weights, rows: int, num_experts: int, *, training: bool):
+    """``stage_nf4`` with the decode on a side stream, so that it runs beside the
+    dispatch plan and the permute the caller issues next (both HBM traffic, the
+    plan kernels mostly latency).  Returns (weights, join): ``join()`` makes the
+    current stream wait for the copies; call it before the first GEMM."""
+    if not _staging_pays(weights, rows, num_experts, training):
+        return tuple(weights), (lambda: None)
+    main = torch.cuda.current_stream()
+    dev = next(w for w in weights if isinstance(w, NF4Tensor)).packed.device
+    side = _side_streams.get(dev.index)
+    if side is None:
+        side = _side_streams.setdefault(dev.index, torch.cuda.Stream(device=dev))
+    outs = [torch.empty(w.shape, dtype=torch.bfloat16, device=dev) if isinstance(w, NF4Tensor) else None
+            for w in weights]  # allocated on the caller's stream, written on the side stream
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        for w, o in zip(weights, outs):
+            if o is not None:
+                nf4_dequantize(w, out=o)
+        done = torch.cuda.Event()
+        done.record(side)
+    for o in outs:
+        if o is not None:
+            o.record_stream(side)
+    return tuple(w if o is None else o for w, o in zip(weights, outs)), (lambda: main.wait_event(done))
 
 
 def moe_forward_train(tokens, top_indices, top_weights, w1, w3, w2, *, num_experts: int, inter: int,
@@ -753,10 +788,11 @@ def moe_forward_train(tokens, top_indices, top_weights, w1, w3, w2, *, num_exper
     """Forward that also returns the state the dX pass consumes."""
     g_in, g_mid = _rotations(w1, w3, w2)
     keys = (w1, w3, w2)
-    w1, w3, w2 = stage_nf4(keys, top_indices.numel(), num_experts, training=True)
+    (w1, w3, w2), join = _stage_beside(keys, top_indices.numel(), num_experts, training=True)
     staged = (keys, (w1, w3, w2)) if w1 is not keys[0] else None
     plan = dispatch_plan(top_indices, num_experts)
     xs = permute_rows(rotate_rows(tokens, g_in) if g_in else tokens, plan.sorted_token_indices)
+    join()
     h, gu = gateup_swiglu(xs, plan.offsets, w1, w3, inter=inter, save_gate_up=True)
     low = None
     if lora is not None:
