@@ -402,3 +402,25 @@ def test_expert_parallel_backward_equals_one_rank(world, cfg):
     rdx, rdw = om.moe_backward_dx(x, ridx, rw, *ws, g, bf16=True)
     assert om.rel_max_err(dx, rdx) < 2e-2
     assert om.rel_max_err(dw, rdw) < 1e-5
+
+
+def test_owner_staging_helpers():
+    """An owner's layer stages its keys through its step ops when they offer
+    ``stage`` (the CUDA ops), keeps them as given otherwise (the oracle), and
+    its backward reuses the forward's copies only for the same keys."""
+    from mirai_b200.expert_parallel import _stage, _weights_for
+
+    keys = (object(), object(), object())
+    assert _stage(OracleStepOps(), keys, 10 ** 6, True) == (keys, None)
+
+    class Staging:
+        def stage(self, weights, rows, training):
+            return tuple(("copy", w) for w in weights) if training else tuple(weights)
+
+    copies, staged = _stage(Staging(), keys, 10 ** 6, True)
+    assert copies == tuple(("copy", w) for w in keys) and staged == (keys, copies)
+    assert _stage(Staging(), keys, 10 ** 6, False) == (keys, None)
+    assert _weights_for(staged, keys) == copies
+    other = (object(), keys[1], keys[2])
+    assert _weights_for(staged, other) == other
+    assert _weights_for(None, keys) == keys
